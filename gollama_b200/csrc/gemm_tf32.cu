@@ -1,0 +1,374 @@
+// TF32 tensor-core GEMM for sm_100a: TMA -> shared memory (128B swizzle) ->
+// tcgen05.mma (kind::tf32, fp32 accumulate in TMEM) -> tcgen05.ld epilogue.
+//
+// C[M,N] = A[M,K] . B[N,K]^T  (+ C if accumulate) (+ R if residual)
+//
+// The reference computes every linear layer through MatMulGrad
+// (pkg/tensor/grad.go:81-155): the forward C = A.B^T via MatMulTransposeB
+// (pkg/tensor/matmul.go:145-234), dA += dC.B (grad.go:102-116) and
+// dB += dC^T.A (grad.go:118-152).  All three are this one kernel with
+// different operand majors:
+//   forward  Y  = X . W^T   A = X  (K-major)  B = W (K-major)
+//   dX      dX += dY . W    A = dY (K-major)  B = W (MN-major: W is [N_out, K_in])
+//   dW      dW += dY^T . X  A = dY (MN-major) B = X (MN-major)
+//
+// Structure: one persistent CTA per SM, 192 threads:
+//   warp 0      TMA producer (one thread), STAGES-deep smem ring
+//   warp 1      TMEM allocator + UMMA issuer (one thread)
+//   warps 2..5  epilogue: TMEM -> registers -> global (fp32), 1 row per thread
+// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
+// the main loop of tile i+1.
+#include "glc_internal.h"
+#include "sm100.cuh"
+
+namespace glc {
+
+namespace {
+
+constexpr int BM = 128;         // UMMA M (one CTA, cta_group::1)
+constexpr int BN = 256;         // UMMA N
+constexpr int BK = 32;          // fp32 elements per k-block = 128 bytes = one swizzle row
+constexpr int UMMA_K = 8;       // K per tcgen05.mma for tf32
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 4;            // 16 KB
+constexpr int B_BYTES = BN * BK * 4;            // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
+constexpr int TMEM_COLS = 2 * BN;               // two accumulators
+constexpr int NUM_THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+
+struct GemmArgs {
+  float* C;
+  const float* R;
+  int M, N, K;
+  int ldc, ldr;
+  int accumulate;  // C += acc
+  int round_out;   // round stored values to TF32 (RN)
+  int m_tiles, n_tiles, num_tiles, k_blocks;
+  int* err;
+};
+
+// UMMA descriptor of the operand for k-step kk inside one stage's tile.
+//   K-major : rows of 128 B (16-byte-chunk swizzle), 8-row groups 1 KB apart;
+//             a k-step advances 32 B inside the swizzle row.
+//   MN-major: 4 KB chunks of 32 K-rows x 32 MN-elements (32-byte-chunk
+//             swizzle), 4-row K groups 512 B apart, chunks 4 KB apart (LBO);
+//             a k-step (8 K-rows) advances 1 KB.
+template <bool MN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t tile_saddr, int kk) {
+  if constexpr (MN) {
+    return umma_sdesc(tile_saddr + kk * 1024, /*LBO: MN chunk stride*/ BK * 128, /*SBO: 4-row K group*/ 512,
+                      UMMA_LAYOUT_SW128_BASE32B);
+  } else {
+    return umma_sdesc(tile_saddr + kk * 32, /*LBO unused*/ 16, /*SBO: 8 rows*/ 1024, UMMA_LAYOUT_SW128);
+  }
+}
+
+template <bool MN, int ROWS>
+__device__ __forceinline__ void load_operand(void* sdst, const CUtensorMap* tm, uint64_t* bar, int mn0, int k0) {
+  if constexpr (MN) {
+    // tensor map dims {MN, K}, box {32, BK}: one 4 KB chunk per 32 MN-elements
+#pragma unroll
+    for (int c = 0; c < ROWS / 32; ++c)
+      tma_load_2d(static_cast<uint8_t*>(sdst) + c * (BK * 128), tm, bar, mn0 + 32 * c, k0);
+  } else {
+    // tensor map dims {K, MN}, box {BK, ROWS}
+    tma_load_2d(sdst, tm, bar, k0, mn0);
+  }
+}
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;       // [2]
+  uint64_t* drain_bar = tempty_bar + 2;       // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 4 * 32);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int in_flight = 0;  // stages issued whose full barrier we have not seen consumed
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % args.m_tiles) * BM;
+        const int n0 = (tile / args.m_tiles) * BN;
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, args.err, GLC_DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + stage * STAGE_BYTES;
+          uint8_t* sB = sA + A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
+          load_operand<A_MN, BM>(sA, &tmA, &full_bar[stage], m0, kb * BK);
+          load_operand<B_MN, BN>(sB, &tmB, &full_bar[stage], n0, kb * BK);
+          in_flight = in_flight < STAGES ? in_flight + 1 : STAGES;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Abort path: wait (bounded) for the copies this thread issued to land
+        // before the CTA releases its shared memory.
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < in_flight; ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          }
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full_bar[s], ph)) {
+            if (globaltimer_ns() - t0 > 1000000000ull) {
+              atomicCAS(args.err, 0, GLC_DEV_TIMEOUT_DRAIN);
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_tf32(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t use = static_cast<uint32_t>(local >> 1);
+        if (!mbar_wait(&tempty_bar[buf], (use & 1) ^ 1, abort_flag, args.err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + buf * BN;
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, args.err, GLC_DEV_TIMEOUT_MMA_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sA = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sB = sA + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            umma_tf32(tmem_d, operand_desc<A_MN>(sA, kk), operand_desc<B_MN>(sB, kk), idesc,
+                      (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty_bar[stage]);  // frees the smem stage when these MMAs finish
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[buf]);  // accumulator ready for the epilogue
+      }
+      if (!ok && issued_any) {
+        // Abort path: make sure no MMA is still writing TMEM before dealloc.
+        umma_commit(drain_bar);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain_bar, 0)) {
+          if (globaltimer_ns() - t0 > 1000000000ull) {
+            atomicCAS(args.err, 0, GLC_DEV_TIMEOUT_DRAIN);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    const bool vec_ok = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15) == 0) &&
+                        (args.R == nullptr ||
+                         (((args.ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.R) & 15) == 0)));
+    int local = 0;
+    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&tfull_bar[buf], use & 1, abort_flag, args.err, GLC_DEV_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      const int m0 = (tile % args.m_tiles) * BM;
+      const int n0 = (tile / args.m_tiles) * BN;
+      const int row = m0 + row_in_tile;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + chunk * 32, r);
+        tmem_ld_wait();
+        if (chunk == BN / 32 - 1) {
+          // all TMEM reads of this accumulator are done: hand it back
+          tc_fence_before();
+          mbar_arrive(&tempty_bar[buf]);
+        }
+        const int col0 = n0 + chunk * 32;
+        if (row >= args.M || col0 >= args.N) continue;
+        float* crow = args.C + static_cast<size_t>(row) * args.ldc + col0;
+        const float* rrow = args.R ? args.R + static_cast<size_t>(row) * args.ldr + col0 : nullptr;
+        if (vec_ok && col0 + 32 <= args.N) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4 v = make_float4(__uint_as_float(r[4 * j + 0]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            if (args.accumulate) {
+              const float4 c = reinterpret_cast<const float4*>(crow)[j];
+              v.x += c.x; v.y += c.y; v.z += c.z; v.w += c.w;
+            }
+            if (rrow) {
+              const float4 c = reinterpret_cast<const float4*>(rrow)[j];
+              v.x += c.x; v.y += c.y; v.z += c.z; v.w += c.w;
+            }
+            if (args.round_out) {
+              v.x = round_tf32(v.x); v.y = round_tf32(v.y); v.z = round_tf32(v.z); v.w = round_tf32(v.w);
+            }
+            reinterpret_cast<float4*>(crow)[j] = v;
+          }
+        } else {
+          const int lim = min(32, args.N - col0);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (j < lim) {
+              float v = __uint_as_float(r[j]);
+              if (args.accumulate) v += crow[j];
+              if (rrow) v += rrow[j];
+              if (args.round_out) v = round_tf32(v);
+              crow[j] = v;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+int encode_operand(Context* ctx, CUtensorMap* tm, const float* ptr, int ld, bool mn, int rows_mn, int k, int box_mn) {
+  // Global tensor: K-major operand is [rows_mn][k] with row stride ld;
+  // MN-major operand is [k][rows_mn] with row stride ld.
+  cuuint64_t dims[2];
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+  cuuint32_t box[2];
+  cuuint32_t estr[2] = {1, 1};
+  if (mn) {
+    dims[0] = static_cast<cuuint64_t>(rows_mn);
+    dims[1] = static_cast<cuuint64_t>(k);
+    box[0] = 32;
+    box[1] = BK;
+  } else {
+    dims[0] = static_cast<cuuint64_t>(k);
+    dims[1] = static_cast<cuuint64_t>(rows_mn);
+    box[0] = BK;
+    box[1] = static_cast<cuuint32_t>(box_mn);
+  }
+  return ctx->encode_tiled(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box,
+                           estr, mn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+}
+
+template <bool A_MN, bool B_MN>
+int launch(Context* ctx, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t s) {
+  static bool attr_set[8] = {false};
+  const int dev = ctx->device;
+  auto kern = gemm_tf32_kernel<A_MN, B_MN>;
+  if (!attr_set[dev & 7]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return ctx->fail_cuda(e, "cudaFuncSetAttribute(gemm_tf32)");
+    attr_set[dev & 7] = true;
+  }
+  const int grid = a.num_tiles < ctx->num_sms ? a.num_tiles : ctx->num_sms;
+  kern<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(ta, tb, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return ctx->fail_cuda(e, "launch gemm_tf32");
+  ctx->count_launch();
+  return 0;
+}
+
+}  // namespace
+
+int gemm_tf32(Context* ctx, const GemmOperand& A, const GemmOperand& B, float* C, int ldc, int M, int N, int K,
+              bool accumulate, const float* R, int ldr, bool round_out, cudaStream_t stream) {
+  if (M < 0 || N < 0 || K < 0) return ctx->fail(GLC_ERR_INVALID, "gemm: negative size");
+  if (M == 0 || N == 0) return 0;
+  if (!A.ptr || !B.ptr || !C) return ctx->fail(GLC_ERR_INVALID, "gemm: null pointer");
+  if ((A.ld & 3) || (B.ld & 3) || (reinterpret_cast<uintptr_t>(A.ptr) & 15) || (reinterpret_cast<uintptr_t>(B.ptr) & 15))
+    return ctx->fail(GLC_ERR_INVALID, "gemm: operand leading dimensions must be multiples of 4 floats and 16-byte aligned");
+  if (K == 0) {
+    // empty reduction: C = (accumulate ? C : 0) + R
+    return gemm_empty_k(ctx, C, ldc, M, N, accumulate, R, ldr, stream);
+  }
+  CUtensorMap ta, tb;
+  if (encode_operand(ctx, &ta, A.ptr, A.ld, A.mn_major, M, K, BM) != 0)
+    return ctx->fail(GLC_ERR_INVALID, "gemm: cuTensorMapEncodeTiled failed for A");
+  if (encode_operand(ctx, &tb, B.ptr, B.ld, B.mn_major, N, K, BN) != 0)
+    return ctx->fail(GLC_ERR_INVALID, "gemm: cuTensorMapEncodeTiled failed for B");
+  GemmArgs a;
+  a.C = C;
+  a.R = R;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.ldc = ldc;
+  a.ldr = ldr;
+  a.accumulate = accumulate ? 1 : 0;
+  a.round_out = round_out ? 1 : 0;
+  a.m_tiles = (M + BM - 1) / BM;
+  a.n_tiles = (N + BN - 1) / BN;
+  a.num_tiles = a.m_tiles * a.n_tiles;
+  a.k_blocks = (K + BK - 1) / BK;
+  a.err = ctx->d_err;
+  if (!A.mn_major && !B.mn_major) return launch<false, false>(ctx, ta, tb, a, stream);
+  if (!A.mn_major && B.mn_major) return launch<false, true>(ctx, ta, tb, a, stream);
+  if (A.mn_major && B.mn_major) return launch<true, true>(ctx, ta, tb, a, stream);
+  return launch<true, false>(ctx, ta, tb, a, stream);
+}
+
+}  // namespace glc

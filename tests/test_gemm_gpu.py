@@ -1,0 +1,118 @@
+"""tcgen05 TF32 GEMM (the three linear-layer products of MatMulGrad,
+pkg/tensor/grad.go:81-152) against an fp64 numpy reference of the same fp32
+inputs.  Tolerance: relative Frobenius error 2e-3 (TF32 operands, fp32
+accumulation)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+def rel_fro(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+SHAPES = [
+    (128, 32, 256),
+    (256, 64, 512),
+    (200, 72, 100),      # ragged in every dimension
+    (64, 128, 344),      # tiny-config FFN width
+    (512, 344, 128),     # K not a multiple of 32
+    (1024, 512, 1376),
+    (4096, 2048, 256),   # TinyLlama K/V projection (GQA)
+]
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+def test_linear_fwd(ctx, M, K, N):
+    rng = np.random.default_rng(M * 7 + K * 3 + N)
+    X = rng.standard_normal((M, K), dtype=np.float32)
+    W = rng.standard_normal((N, K), dtype=np.float32)
+    dX, dW, dY = ctx.from_numpy(X), ctx.from_numpy(W), ctx.empty((M, N))
+    ctx.call("glc_linear_fwd", dX.ptr, dW.ptr, dY.ptr, M, K, N, None)
+    ctx.sync()
+    ref = X.astype(np.float64) @ W.astype(np.float64).T
+    assert rel_fro(dY.numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+def test_linear_fwd_residual(ctx, M, K, N):
+    rng = np.random.default_rng(11 + M)
+    X = rng.standard_normal((M, K), dtype=np.float32)
+    W = rng.standard_normal((N, K), dtype=np.float32)
+    R = rng.standard_normal((M, N), dtype=np.float32) * 10
+    dX, dW, dR, dY = ctx.from_numpy(X), ctx.from_numpy(W), ctx.from_numpy(R), ctx.empty((M, N))
+    ctx.call("glc_linear_fwd", dX.ptr, dW.ptr, dY.ptr, M, K, N, dR.ptr)
+    ctx.sync()
+    ref = X.astype(np.float64) @ W.astype(np.float64).T + R
+    assert rel_fro(dY.numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+@pytest.mark.parametrize("accumulate", [0, 1])
+def test_linear_bwd_dx(ctx, M, K, N, accumulate):
+    rng = np.random.default_rng(5 + M + N)
+    G = rng.standard_normal((M, N), dtype=np.float32)
+    W = rng.standard_normal((N, K), dtype=np.float32)
+    D0 = rng.standard_normal((M, K), dtype=np.float32)
+    dG, dW, dD = ctx.from_numpy(G), ctx.from_numpy(W), ctx.from_numpy(D0)
+    ctx.call("glc_linear_bwd_dx", dG.ptr, dW.ptr, dD.ptr, M, K, N, accumulate)
+    ctx.sync()
+    ref = G.astype(np.float64) @ W.astype(np.float64) + (D0 if accumulate else 0)
+    assert rel_fro(dD.numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+@pytest.mark.parametrize("accumulate", [0, 1])
+def test_linear_bwd_dw(ctx, M, K, N, accumulate):
+    rng = np.random.default_rng(9 + K)
+    G = rng.standard_normal((M, N), dtype=np.float32)
+    X = rng.standard_normal((M, K), dtype=np.float32)
+    D0 = rng.standard_normal((N, K), dtype=np.float32)
+    dG, dX, dD = ctx.from_numpy(G), ctx.from_numpy(X), ctx.from_numpy(D0)
+    ctx.call("glc_linear_bwd_dw", dG.ptr, dX.ptr, dD.ptr, M, K, N, accumulate)
+    ctx.sync()
+    ref = G.astype(np.float64).T @ X.astype(np.float64) + (D0 if accumulate else 0)
+    assert rel_fro(dD.numpy(), ref) < TOL
+
+
+def test_gemm_mn_major_a_k_major_b(ctx):
+    """The fourth operand-major combination (A MN-major, B K-major)."""
+    M, N, K = 300, 260, 96
+    rng = np.random.default_rng(3)
+    At = rng.standard_normal((K, M), dtype=np.float32)  # A stored [K][M]
+    B = rng.standard_normal((N, K), dtype=np.float32)
+    dA, dB, dC = ctx.from_numpy(At), ctx.from_numpy(B), ctx.empty((M, N))
+    ctx.call("glc_gemm_tf32", dA.ptr, M, 1, dB.ptr, K, 0, dC.ptr, N, M, N, K, 0, None, 0, 0)
+    ctx.sync()
+    ref = At.T.astype(np.float64) @ B.astype(np.float64).T
+    assert rel_fro(dC.numpy(), ref) < TOL
+
+
+def test_tf32_operand_rounding_probe(ctx):
+    """Records how the tensor core treats fp32 bits below the TF32 mantissa:
+    A = 1 + 0.75 ulp(tf32) is seen as 1 (truncation) or 1 + 2^-10 (rounding)."""
+    M, N, K = 128, 256, 32
+    a = np.float32(1.0 + 3 * 2.0**-12)
+    A = np.full((M, K), a, np.float32)
+    B = np.ones((N, K), np.float32)
+    dA, dB, dC = ctx.from_numpy(A), ctx.from_numpy(B), ctx.empty((M, N))
+    ctx.call("glc_linear_fwd", dA.ptr, dB.ptr, dC.ptr, M, K, N, None)
+    ctx.sync()
+    v = float(dC.numpy()[0, 0])
+    assert v in (32.0, 32.0 * (1 + 2.0**-10)), v
+    print(f"\nTF32 operand handling: {'truncation' if v == 32.0 else 'round-to-nearest'} (C = {v!r})")
+
+
+def test_gemm_rejects_misaligned(ctx):
+    from gollama_b200.device import GlcError
+
+    X = ctx.empty((4, 6))
+    W = ctx.empty((4, 6))
+    Y = ctx.empty((4, 4))
+    with pytest.raises(GlcError):
+        ctx.call("glc_linear_fwd", X.ptr, W.ptr, Y.ptr, 4, 6, 4, None)
