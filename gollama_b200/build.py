@@ -4,7 +4,7 @@ Every .cu/.cpp file under gollama_b200/csrc is compiled to an object under
 gollama_b200/_build (incrementally: a source is rebuilt when it or any header
 in csrc/ or include/ is newer than its object) and linked into
 gollama_b200/libgollama_cuda.so.  The CUDA runtime is linked statically; NCCL
-is linked dynamically.
+is resolved at run time with dlopen.
 """
 from __future__ import annotations
 
@@ -82,7 +82,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
                 f.result()
     if jobs or not LIB.exists():
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lnccl", "-ldl", "-lpthread"]
+        cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-ldl", "-lpthread"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -1,0 +1,152 @@
+// Fused softmax cross-entropy forward + backward (SoftmaxCrossEntropyGrad,
+// pkg/tensor/grad.go:210-280).
+//
+// One CTA of up to 512 threads per row; the row lives in registers (V <= 65536).  Per row:
+//   max (grad.go:220-225), e_v = exp32(l_v - max) and their float32 sum
+//   (:228-232), p_v = e_v / sum (:235-237), the target's log32(p_t + 1e-10)
+//   (:240-243; targets outside [0, V) contribute nothing), and, when the
+//   gradient is wanted, dlogits_v = p_v*scale - [v == t]*scale (:266-276),
+//   written in place over the logits (the row is fully in registers first).
+// The loss (:246) is summed by a second, single-thread kernel in row order,
+// exactly as the reference's running float32 total.
+#include <cfloat>
+
+#include "glc_internal.h"
+#include "go_math.cuh"
+#include "sm100.cuh"
+
+namespace glc {
+namespace {
+
+template <bool IS_MAX>
+__device__ __forceinline__ float block_reduce(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = IS_MAX ? fmaxf(v, w) : v + w;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < nw ? red[lane] : (IS_MAX ? -FLT_MAX : 0.f);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float w = __shfl_xor_sync(0xffffffffu, t, o);
+      t = IS_MAX ? fmaxf(t, w) : t + w;
+    }
+    if (lane == 0) red[32] = t;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(512) ce_kernel(float* __restrict__ logits, const int64_t* __restrict__ targets,
+                                                  int rows, int V, float scale, float* __restrict__ row_logp,
+                                                  int write_grad, int round_out) {
+  __shared__ float red[33];
+  const int nc = V >> 2;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    float4* lr = reinterpret_cast<float4*>(logits + static_cast<size_t>(row) * V);
+    float4 v[VPT];
+    float m = -FLT_MAX;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nc) {
+        v[i] = lr[c];
+        m = fmaxf(m, fmaxf(fmaxf(v[i].x, v[i].y), fmaxf(v[i].z, v[i].w)));
+      }
+    }
+    m = block_reduce<true>(m, red);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nc) {
+        v[i].x = go_exp32(__fsub_rn(v[i].x, m));
+        v[i].y = go_exp32(__fsub_rn(v[i].y, m));
+        v[i].z = go_exp32(__fsub_rn(v[i].z, m));
+        v[i].w = go_exp32(__fsub_rn(v[i].w, m));
+        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+      }
+    }
+    s = block_reduce<false>(s, red);
+    const int64_t t = targets[row];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nc) {
+        float p[4] = {__fdiv_rn(v[i].x, s), __fdiv_rn(v[i].y, s), __fdiv_rn(v[i].z, s), __fdiv_rn(v[i].w, s)};
+        if (t >= 4 * c && t < 4 * c + 4) {
+          const int j = static_cast<int>(t - 4 * c);
+          const float pt = j == 0 ? p[0] : j == 1 ? p[1] : j == 2 ? p[2] : p[3];
+          row_logp[row] = go_log32(__fadd_rn(pt, 1e-10f));
+        }
+        if (write_grad) {
+          float g[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            g[j] = __fmul_rn(p[j], scale);
+            if (4 * c + j == t) g[j] = __fsub_rn(g[j], scale);
+            if (round_out) g[j] = round_tf32(g[j]);
+          }
+          lr[c] = make_float4(g[0], g[1], g[2], g[3]);
+        }
+      }
+    }
+    if ((t < 0 || t >= V) && threadIdx.x == 0) row_logp[row] = 0.f;
+    __syncthreads();
+  }
+}
+
+// loss = (0 - logp_0 - logp_1 - ...) / rows over valid targets (grad.go:239-246)
+__global__ void ce_loss_sum_kernel(const float* __restrict__ row_logp, const int64_t* __restrict__ targets, int rows,
+                                   int V, float* __restrict__ loss) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  float total = 0.f;
+  for (int b = 0; b < rows; ++b) {
+    const int64_t t = targets[b];
+    if (t >= 0 && t < V) total = __fsub_rn(total, row_logp[b]);
+  }
+  *loss = __fdiv_rn(total, static_cast<float>(rows));
+}
+
+}  // namespace
+
+int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, int V, float scale, float* row_logp,
+               float* loss, bool write_grad, bool round_out, cudaStream_t s) {
+  if (rows <= 0 || V <= 0) return ctx->fail(GLC_ERR_INVALID, "softmax_ce: empty logits");
+  if ((V & 3) || (reinterpret_cast<uintptr_t>(logits) & 15))
+    return ctx->fail(GLC_ERR_INVALID, "softmax_ce: vocab must be a multiple of 4, logits 16-byte aligned");
+  if (!targets || !row_logp || !loss) return ctx->fail(GLC_ERR_INVALID, "softmax_ce: null pointer");
+  const int nc = V / 4;
+  int threads = ((nc + 31) / 32) * 32;
+  if (threads > 512) threads = 512;
+  const int vpt = (nc + threads - 1) / threads;
+  const unsigned grid = static_cast<unsigned>(rows);
+  const int wg = write_grad ? 1 : 0, ro = round_out ? 1 : 0;
+  ProfScope prof(ctx, PROF_CE, 4.0 * static_cast<double>(rows) * V * (write_grad ? 2 : 1), s);
+  if (vpt <= 1)
+    ce_kernel<1><<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+  else if (vpt <= 2)
+    ce_kernel<2><<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+  else if (vpt <= 4)
+    ce_kernel<4><<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+  else if (vpt <= 8)
+    ce_kernel<8><<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+  else if (vpt <= 16)
+    ce_kernel<16><<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+  else if (vpt <= 32)
+    ce_kernel<32><<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+  else
+    return ctx->fail(GLC_ERR_UNSUPPORTED, "softmax_ce: vocab above 65536 is not supported");
+  GLC_LAUNCH_CHECK(ctx, "softmax_ce");
+  ce_loss_sum_kernel<<<1, 32, 0, s>>>(row_logp, targets, rows, V, loss);
+  GLC_LAUNCH_CHECK(ctx, "softmax_ce loss");
+  return 0;
+}
+
+}  // namespace glc

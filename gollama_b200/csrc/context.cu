@@ -97,6 +97,11 @@ int glc_destroy(glc_ctx* ctx) {
   if (c->d_err) cudaFree(c->d_err);
   if (c->timer_start) cudaEventDestroy(c->timer_start);
   if (c->timer_stop) cudaEventDestroy(c->timer_stop);
+  for (auto& r : c->prof) {
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  for (auto e : c->event_pool) cudaEventDestroy(e);
   cudaStreamDestroy(c->stream);
   cudaStreamDestroy(c->comm_stream);
   delete c;
@@ -226,6 +231,38 @@ int glc_timer_stop(glc_ctx* ctx, float* ms) {
   if (e == cudaSuccess) e = cudaEventSynchronize(c->timer_stop);
   if (e == cudaSuccess) e = cudaEventElapsedTime(ms, c->timer_start, c->timer_stop);
   return e == cudaSuccess ? GLC_OK : c->fail_cuda(e, "timer stop");
+}
+
+int glc_profile_begin(glc_ctx* ctx) {
+  if (!ctx) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  c->profiling = true;
+  return GLC_OK;
+}
+
+int glc_profile_end(glc_ctx* ctx, int n_classes, uint64_t* counts, double* total_ms, double* total_work) {
+  if (!ctx || n_classes <= 0 || !counts || !total_ms || !total_work) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  c->profiling = false;
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return c->fail_cuda(e, "glc_profile_end");
+  for (int i = 0; i < n_classes; ++i) {
+    counts[i] = 0;
+    total_ms[i] = 0.0;
+    total_work[i] = 0.0;
+  }
+  for (auto& r : c->prof) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess && r.cls >= 0 && r.cls < n_classes) {
+      counts[r.cls] += 1;
+      total_ms[r.cls] += ms;
+      total_work[r.cls] += r.work;
+    }
+    c->event_pool.push_back(r.a);
+    c->event_pool.push_back(r.b);
+  }
+  c->prof.clear();
+  return GLC_OK;
 }
 
 int glc_gemm_tf32(glc_ctx* ctx, const float* A, int lda, int a_mn, const float* B, int ldb, int b_mn, float* C,

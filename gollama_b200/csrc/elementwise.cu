@@ -1,0 +1,247 @@
+// Bandwidth-bound elementwise kernels: SwiGLU forward/backward, RoPE,
+// embedding gather / gradient scatter, fills and TF32 rounding copies.
+#include "glc_internal.h"
+#include "go_math.cuh"
+#include "sm100.cuh"
+
+namespace glc {
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// ---------------------------------------------------------------- SwiGLU
+// Forward of forwardFFN's SiLU and product nodes (trainer.go:397-407 with
+// SiLUGrad, grad.go:424-428): s = 1/(1+exp32(-g)), h = (g*s)*u.
+__device__ __forceinline__ float swiglu_f(float g, float u) {
+  const float s = go_sigmoid(g);
+  return __fmul_rn(__fmul_rn(g, s), u);
+}
+
+__global__ void swiglu_fwd_kernel(const float4* __restrict__ g, const float4* __restrict__ u, float4* __restrict__ h,
+                                  size_t n4, int round_out) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n4; i += size_t(gridDim.x) * blockDim.x) {
+    const float4 a = g[i], b = u[i];
+    float4 o = make_float4(swiglu_f(a.x, b.x), swiglu_f(a.y, b.y), swiglu_f(a.z, b.z), swiglu_f(a.w, b.w));
+    if (round_out) o = make_float4(round_tf32(o.x), round_tf32(o.y), round_tf32(o.z), round_tf32(o.w));
+    h[i] = o;
+  }
+}
+
+// Backward of the product node (trainer.go:418-421) then SiLU (grad.go:441-445):
+//   dgs = dh*u, du = dh*(g*s), dg = dgs * (s*(1 + g*(1-s)))
+__device__ __forceinline__ void swiglu_b(float g, float u, float dh, float& dg, float& du) {
+  const float s = go_sigmoid(g);
+  const float gs = __fmul_rn(g, s);
+  const float dgs = __fmul_rn(dh, u);
+  du = __fmul_rn(dh, gs);
+  const float grad = __fmul_rn(s, __fadd_rn(1.0f, __fmul_rn(g, __fsub_rn(1.0f, s))));
+  dg = __fmul_rn(dgs, grad);
+}
+
+__global__ void swiglu_bwd_kernel(const float4* __restrict__ g, const float4* __restrict__ u,
+                                  const float4* __restrict__ dh, float4* __restrict__ dg, float4* __restrict__ du,
+                                  size_t n4, int accumulate, int round_out) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n4; i += size_t(gridDim.x) * blockDim.x) {
+    const float4 a = g[i], b = u[i], d = dh[i];
+    float4 rg, ru;
+    swiglu_b(a.x, b.x, d.x, rg.x, ru.x);
+    swiglu_b(a.y, b.y, d.y, rg.y, ru.y);
+    swiglu_b(a.z, b.z, d.z, rg.z, ru.z);
+    swiglu_b(a.w, b.w, d.w, rg.w, ru.w);
+    if (accumulate) {
+      const float4 og = dg[i], ou = du[i];
+      rg = make_float4(__fadd_rn(og.x, rg.x), __fadd_rn(og.y, rg.y), __fadd_rn(og.z, rg.z), __fadd_rn(og.w, rg.w));
+      ru = make_float4(__fadd_rn(ou.x, ru.x), __fadd_rn(ou.y, ru.y), __fadd_rn(ou.z, ru.z), __fadd_rn(ou.w, ru.w));
+    }
+    if (round_out) {
+      rg = make_float4(round_tf32(rg.x), round_tf32(rg.y), round_tf32(rg.z), round_tf32(rg.w));
+      ru = make_float4(round_tf32(ru.x), round_tf32(ru.y), round_tf32(ru.z), round_tf32(ru.w));
+    }
+    dg[i] = rg;
+    du[i] = ru;
+  }
+}
+
+// ---------------------------------------------------------------- fills / copies
+__global__ void fill_kernel(float* __restrict__ p, float v, size_t n) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) p[i] = v;
+}
+
+__global__ void add_inplace_kernel(float* __restrict__ dst, const float* __restrict__ src, size_t n) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+    dst[i] = __fadd_rn(dst[i], src[i]);
+}
+
+__global__ void round_copy_kernel(const float* __restrict__ src, float* __restrict__ dst, size_t n) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+    dst[i] = round_tf32(src[i]);
+}
+
+// ---------------------------------------------------------------- RoPE
+// apply3D (pkg/model/rope.go:96-126) on rows of nh heads x hd, consecutive
+// pairs, position t % S; inverse = 1 applies the transposed rotation (the
+// backward).  In place; optional TF32 rounding of the result.
+__global__ void rope_kernel(float* __restrict__ x, int T, int S, int nh, int hd, const float* __restrict__ cos_t,
+                            const float* __restrict__ sin_t, int inverse, int round_out) {
+  const int half = hd >> 1;
+  const size_t pairs = static_cast<size_t>(T) * nh * half;
+  for (size_t p = blockIdx.x * size_t(blockDim.x) + threadIdx.x; p < pairs; p += size_t(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(p % half);
+    const size_t th = p / half;  // t*nh + h
+    const int t = static_cast<int>(th / nh);
+    const int pos = t % S;
+    const float c = cos_t[pos * half + i], s = sin_t[pos * half + i];
+    float2* xp = reinterpret_cast<float2*>(x + th * hd) + i;
+    const float2 v = *xp;
+    float2 o;
+    if (!inverse) {
+      o.x = __fsub_rn(__fmul_rn(v.x, c), __fmul_rn(v.y, s));
+      o.y = __fadd_rn(__fmul_rn(v.x, s), __fmul_rn(v.y, c));
+    } else {
+      o.x = __fadd_rn(__fmul_rn(v.x, c), __fmul_rn(v.y, s));
+      o.y = __fadd_rn(__fmul_rn(-v.x, s), __fmul_rn(v.y, c));
+    }
+    if (round_out) {
+      o.x = round_tf32(o.x);
+      o.y = round_tf32(o.y);
+    }
+    *xp = o;
+  }
+}
+
+// ---------------------------------------------------------------- embedding
+// Forward (trainer.go:276-289): h[t] = E[tok] (+ P[t % S]); ids outside
+// [0, V) read row 0.
+__global__ void embed_fwd_kernel(const int64_t* __restrict__ tok, const float* __restrict__ E,
+                                 const float* __restrict__ P, float* __restrict__ out, int T, int S, int d, int V) {
+  const int nc = d >> 2;
+  const size_t total = static_cast<size_t>(T) * nc;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(i / nc), c = static_cast<int>(i % nc);
+    int64_t id = tok[t];
+    if (id < 0 || id >= V) id = 0;
+    float4 v = reinterpret_cast<const float4*>(E + id * d)[c];
+    if (P) {
+      const float4 p = reinterpret_cast<const float4*>(P + static_cast<size_t>(t % S) * d)[c];
+      v = make_float4(__fadd_rn(v.x, p.x), __fadd_rn(v.y, p.y), __fadd_rn(v.z, p.z), __fadd_rn(v.w, p.w));
+    }
+    reinterpret_cast<float4*>(out + static_cast<size_t>(t) * d)[c] = v;
+  }
+}
+
+// Gradient scatter dE[tok] += dh[t], t ascending, as one sequential sum per
+// distinct id (deterministic; no atomics).  seg_tok[u] is the u-th distinct
+// (clamped) id, rows order[seg_start[u] .. seg_start[u+1]) are its tokens in
+// ascending t.
+__global__ void embed_bwd_kernel(const int* __restrict__ seg_tok, const int* __restrict__ seg_start,
+                                 const int* __restrict__ order, const float* __restrict__ dh, float* __restrict__ dE,
+                                 int nseg, int d) {
+  const int nc = d >> 2;
+  for (int u = blockIdx.x; u < nseg; u += gridDim.x) {
+    float4* row = reinterpret_cast<float4*>(dE + static_cast<size_t>(seg_tok[u]) * d);
+    const int b = seg_start[u], e = seg_start[u + 1];
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+      float4 acc = row[c];
+      for (int k = b; k < e; ++k) {
+        const float4 g = reinterpret_cast<const float4*>(dh + static_cast<size_t>(order[k]) * d)[c];
+        acc = make_float4(__fadd_rn(acc.x, g.x), __fadd_rn(acc.y, g.y), __fadd_rn(acc.z, g.z), __fadd_rn(acc.w, g.w));
+      }
+      row[c] = acc;
+    }
+  }
+}
+
+}  // namespace
+
+int swiglu_fwd(Context* ctx, const float* g, const float* u, float* h, size_t n, bool round_out, cudaStream_t s) {
+  if (n == 0) return 0;
+  if ((n & 3) || !aligned16(g) || !aligned16(u) || !aligned16(h))
+    return ctx->fail(GLC_ERR_INVALID, "swiglu_fwd: size must be a multiple of 4 and pointers 16-byte aligned");
+  ProfScope prof(ctx, PROF_SWIGLU, 12.0 * n, s);
+  swiglu_fwd_kernel<<<grid_for(n / 4, 256, ctx->num_sms), 256, 0, s>>>(
+      reinterpret_cast<const float4*>(g), reinterpret_cast<const float4*>(u), reinterpret_cast<float4*>(h), n / 4,
+      round_out ? 1 : 0);
+  GLC_LAUNCH_CHECK(ctx, "swiglu_fwd");
+  return 0;
+}
+
+int swiglu_bwd(Context* ctx, const float* g, const float* u, const float* dh, float* dg, float* du, size_t n,
+               bool accumulate, bool round_out, cudaStream_t s) {
+  if (n == 0) return 0;
+  if ((n & 3) || !aligned16(g) || !aligned16(u) || !aligned16(dh) || !aligned16(dg) || !aligned16(du))
+    return ctx->fail(GLC_ERR_INVALID, "swiglu_bwd: size must be a multiple of 4 and pointers 16-byte aligned");
+  ProfScope prof(ctx, PROF_SWIGLU, (accumulate ? 28.0 : 20.0) * n, s);
+  swiglu_bwd_kernel<<<grid_for(n / 4, 256, ctx->num_sms), 256, 0, s>>>(
+      reinterpret_cast<const float4*>(g), reinterpret_cast<const float4*>(u), reinterpret_cast<const float4*>(dh),
+      reinterpret_cast<float4*>(dg), reinterpret_cast<float4*>(du), n / 4, accumulate ? 1 : 0, round_out ? 1 : 0);
+  GLC_LAUNCH_CHECK(ctx, "swiglu_bwd");
+  return 0;
+}
+
+int fill(Context* ctx, float* p, float v, size_t n, cudaStream_t s) {
+  if (n == 0) return 0;
+  if (!p) return ctx->fail(GLC_ERR_INVALID, "fill: null pointer");
+  ProfScope prof(ctx, PROF_OTHER, 4.0 * n, s);
+  fill_kernel<<<grid_for(n, 256, ctx->num_sms), 256, 0, s>>>(p, v, n);
+  GLC_LAUNCH_CHECK(ctx, "fill");
+  return 0;
+}
+
+int add_inplace(Context* ctx, float* dst, const float* src, size_t n, cudaStream_t s) {
+  if (n == 0) return 0;
+  if (!dst || !src) return ctx->fail(GLC_ERR_INVALID, "add_inplace: null pointer");
+  ProfScope prof(ctx, PROF_OTHER, 12.0 * n, s);
+  add_inplace_kernel<<<grid_for(n, 256, ctx->num_sms), 256, 0, s>>>(dst, src, n);
+  GLC_LAUNCH_CHECK(ctx, "add_inplace");
+  return 0;
+}
+
+int round_copy(Context* ctx, const float* src, float* dst, size_t n, cudaStream_t s) {
+  if (n == 0) return 0;
+  if (!src || !dst) return ctx->fail(GLC_ERR_INVALID, "round_copy: null pointer");
+  ProfScope prof(ctx, PROF_OTHER, 8.0 * n, s);
+  round_copy_kernel<<<grid_for(n, 256, ctx->num_sms), 256, 0, s>>>(src, dst, n);
+  GLC_LAUNCH_CHECK(ctx, "round_copy");
+  return 0;
+}
+
+int rope(Context* ctx, float* x, int T, int S, int nh, int hd, const float* cos_t, const float* sin_t, bool inverse,
+         bool round_out, cudaStream_t s) {
+  if (T == 0) return 0;
+  if (T < 0 || S <= 0 || nh <= 0 || hd <= 0 || (hd & 1) || !x || !cos_t || !sin_t ||
+      (reinterpret_cast<uintptr_t>(x) & 7))
+    return ctx->fail(GLC_ERR_INVALID, "rope: bad arguments");
+  const size_t pairs = static_cast<size_t>(T) * nh * (hd / 2);
+  ProfScope prof(ctx, PROF_OTHER, 16.0 * pairs, s);
+  rope_kernel<<<grid_for(pairs, 256, ctx->num_sms), 256, 0, s>>>(x, T, S, nh, hd, cos_t, sin_t, inverse ? 1 : 0,
+                                                                  round_out ? 1 : 0);
+  GLC_LAUNCH_CHECK(ctx, "rope");
+  return 0;
+}
+
+int embed_fwd(Context* ctx, const int64_t* tok, const float* E, const float* P, float* out, int T, int S, int d, int V,
+              cudaStream_t s) {
+  if (T == 0) return 0;
+  if (T < 0 || S <= 0 || d <= 0 || (d & 3) || V <= 0 || !tok || !E || !out || !aligned16(E) || !aligned16(out) ||
+      (P && !aligned16(P)))
+    return ctx->fail(GLC_ERR_INVALID, "embed_fwd: bad arguments (hidden size must be a multiple of 4)");
+  const size_t total = static_cast<size_t>(T) * (d / 4);
+  ProfScope prof(ctx, PROF_OTHER, (P ? 12.0 : 8.0) * T * d, s);
+  embed_fwd_kernel<<<grid_for(total, 256, ctx->num_sms), 256, 0, s>>>(tok, E, P, out, T, S, d, V);
+  GLC_LAUNCH_CHECK(ctx, "embed_fwd");
+  return 0;
+}
+
+int embed_bwd(Context* ctx, const int* seg_tok, const int* seg_start, const int* order, int nseg, const float* dh,
+              float* dE, int d, cudaStream_t s) {
+  if (nseg == 0) return 0;
+  if (nseg < 0 || d <= 0 || (d & 3) || !seg_tok || !seg_start || !order || !dh || !dE)
+    return ctx->fail(GLC_ERR_INVALID, "embed_bwd: bad arguments");
+  unsigned grid = static_cast<unsigned>(nseg < 8 * ctx->num_sms ? nseg : 8 * ctx->num_sms);
+  ProfScope prof(ctx, PROF_OTHER, 8.0 * 0, s);
+  embed_bwd_kernel<<<grid, 128, 0, s>>>(seg_tok, seg_start, order, dh, dE, nseg, d);
+  GLC_LAUNCH_CHECK(ctx, "embed_bwd");
+  return 0;
+}
+
+}  // namespace glc

@@ -325,6 +325,7 @@ int launch(Context* ctx, const CUtensorMap& ta, const CUtensorMap& tb, const Gem
     attr_set[dev & 7] = true;
   }
   const int grid = a.num_tiles < ctx->num_sms ? a.num_tiles : ctx->num_sms;
+  ProfScope prof(ctx, PROF_GEMM, 2.0 * a.M * a.N * static_cast<double>(a.K), s);
   kern<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(ta, tb, a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return ctx->fail_cuda(e, "launch gemm_tf32");

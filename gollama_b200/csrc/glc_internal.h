@@ -34,6 +34,26 @@ struct Context {
   int rank = 0;
   int world = 1;
   cudaEvent_t timer_start = nullptr, timer_stop = nullptr;
+  // per-kernel-class timing (glc_profile_begin/end): event pairs recorded on
+  // the launching stream around each launch
+  struct ProfRecord {
+    cudaEvent_t a, b;
+    int cls;
+    double work;
+  };
+  bool profiling = false;
+  std::vector<ProfRecord> prof;
+  std::vector<cudaEvent_t> event_pool;
+  cudaEvent_t get_event() {
+    if (!event_pool.empty()) {
+      cudaEvent_t e = event_pool.back();
+      event_pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
 
   int fail(int code, const std::string& msg) {
     last_error = msg;
@@ -56,6 +76,41 @@ struct Context {
   int workspace(size_t bytes, void** out);
 };
 
+// Kernel classes of the profiler; work is FLOPs (GEMM, attention) or bytes.
+enum ProfClass : int {
+  PROF_GEMM = 0,      // tcgen05 TF32 GEMM, 2*M*N*K FLOPs
+  PROF_ATTN_FWD = 1,  // 2 matmuls over the causal half, FLOPs
+  PROF_ATTN_BWD = 2,  // dV, dP, dQ, dK matmuls over the causal half, FLOPs
+  PROF_RMSNORM = 3,   // bytes
+  PROF_SWIGLU = 4,    // bytes
+  PROF_CE = 5,        // bytes
+  PROF_ADAMW = 6,     // bytes (grad norm + AdamW)
+  PROF_OTHER = 7,     // bytes (embedding, RoPE, fills, copies)
+  PROF_CLASSES = 8
+};
+
+// Records an event pair around the launches in its scope when profiling.
+struct ProfScope {
+  Context* c;
+  int cls;
+  double work;
+  cudaStream_t s;
+  cudaEvent_t a = nullptr;
+  ProfScope(Context* ctx, int k, double w, cudaStream_t st) : c(ctx), cls(k), work(w), s(st) {
+    if (c->profiling) {
+      a = c->get_event();
+      cudaEventRecord(a, s);
+    }
+  }
+  ~ProfScope() {
+    if (a) {
+      cudaEvent_t b = c->get_event();
+      cudaEventRecord(b, s);
+      c->prof.push_back({a, b, cls, work});
+    }
+  }
+};
+
 // A GEMM operand.  K-major: element (i, k) at ptr[i*ld + k].
 // MN-major: element (i, k) at ptr[k*ld + i].
 struct GemmOperand {
@@ -68,6 +123,49 @@ int gemm_tf32(Context* ctx, const GemmOperand& A, const GemmOperand& B, float* C
               bool accumulate, const float* R, int ldr, bool round_out, cudaStream_t stream);
 int gemm_empty_k(Context* ctx, float* C, int ldc, int M, int N, bool accumulate, const float* R, int ldr,
                  cudaStream_t stream);
+
+// ---- kernels (each enqueues on stream `s`; returns 0 or a GLC_ERR_* code)
+int rmsnorm_fwd(Context* ctx, const float* x, const float* w, float* y, float* rms, int rows, int cols, float eps,
+                bool round_out, cudaStream_t s);
+// scratch == nullptr: per-block dw partials go to the context workspace.
+int rmsnorm_bwd(Context* ctx, const float* x, const float* w, const float* rms, const float* dy, float* dx,
+                float* dx_round, float* dw, int rows, int cols, bool full, bool dx_accumulate, bool dw_accumulate,
+                float* scratch, size_t scratch_bytes, cudaStream_t s);
+int swiglu_fwd(Context* ctx, const float* g, const float* u, float* h, size_t n, bool round_out, cudaStream_t s);
+int swiglu_bwd(Context* ctx, const float* g, const float* u, const float* dh, float* dg, float* du, size_t n,
+               bool accumulate, bool round_out, cudaStream_t s);
+int fill(Context* ctx, float* p, float v, size_t n, cudaStream_t s);
+int round_copy(Context* ctx, const float* src, float* dst, size_t n, cudaStream_t s);
+int add_inplace(Context* ctx, float* dst, const float* src, size_t n, cudaStream_t s);
+int rope(Context* ctx, float* x, int T, int S, int nh, int hd, const float* cos_t, const float* sin_t, bool inverse,
+         bool round_out, cudaStream_t s);
+int embed_fwd(Context* ctx, const int64_t* tok, const float* E, const float* P, float* out, int T, int S, int d, int V,
+              cudaStream_t s);
+int embed_bwd(Context* ctx, const int* seg_tok, const int* seg_start, const int* order, int nseg, const float* dh,
+              float* dE, int d, cudaStream_t s);
+int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, int V, float scale, float* row_logp,
+               float* loss, bool write_grad, bool round_out, cudaStream_t s);
+int attention_fwd(Context* ctx, const float* q, const float* k, const float* v, float* o, float* lse, int B, int S,
+                  int H, int Hkv, int hd, bool round_out, cudaStream_t s);
+int attention_bwd(Context* ctx, const float* q, const float* k, const float* v, const float* o, const float* lse,
+                  const float* dO, float* dq, float* dk, float* dv, float* D, int B, int S, int H, int Hkv, int hd,
+                  bool round_dv, cudaStream_t s);
+// segs: device array of nseg {start, len} int64 pairs into the flat arenas.
+// elems: number of gradient elements the segments cover (for the profiler).
+int grad_norm(Context* ctx, const float* grads, const int64_t* segs, int nseg, float max_norm, double* norm_out,
+              float* scale_out, double* scratch, int scratch_count, double elems, cudaStream_t s);
+int adamw(Context* ctx, float* p, float* g, float* m, float* v, float* shadow, const int64_t* segs, int nseg,
+          const float* clip_scale, float lr, float beta1, float beta2, float eps, float wd, int step, double elems,
+          cudaStream_t s);
+
+// RoPE tables (pkg/model/rope.go:33-48) computed on the host in float64 and
+// rounded to float32: cos_t/sin_t are [max_seq][dim/2].
+void rope_table_host(int dim, int max_seq, float theta, float* cos_t, float* sin_t);
+
+// Deterministic embedding-gradient segments from host token ids (clamped to
+// [0, V)): distinct ids ascending, their tokens in ascending position.
+void embed_segments_host(const int64_t* tok, int T, int V, std::vector<int>& seg_tok, std::vector<int>& seg_start,
+                         std::vector<int>& order);
 
 inline unsigned grid_for(size_t n, int block, int num_sms, int per_sm = 8) {
   size_t g = (n + block - 1) / block;

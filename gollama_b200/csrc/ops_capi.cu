@@ -1,0 +1,114 @@
+// C ABI of the individual ops: what a GradFn of the reference tape
+// (pkg/tensor/grad.go, pkg/train/trainer.go) calls through the cgo package.
+#include <vector>
+
+#include "glc_internal.h"
+
+using glc::Context;
+
+static inline Context* C_(glc_ctx* c) { return reinterpret_cast<Context*>(c); }
+
+extern "C" {
+
+int glc_rmsnorm_fwd(glc_ctx* ctx, const float* x, const float* w, float* y, float* rms, int rows, int cols, float eps,
+                    int round_out) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::rmsnorm_fwd(C_(ctx), x, w, y, rms, rows, cols, eps, round_out != 0, C_(ctx)->stream);
+}
+
+int glc_rmsnorm_bwd(glc_ctx* ctx, const float* x, const float* w, const float* rms, const float* dy, float* dx,
+                    float* dx_round, float* dw, int rows, int cols, int full, int dx_accumulate, int dw_accumulate) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::rmsnorm_bwd(C_(ctx), x, w, rms, dy, dx, dx_round, dw, rows, cols, full != 0, dx_accumulate != 0,
+                          dw_accumulate != 0, nullptr, 0, C_(ctx)->stream);
+}
+
+int glc_swiglu_fwd(glc_ctx* ctx, const float* gate, const float* up, float* h, size_t n, int round_out) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::swiglu_fwd(C_(ctx), gate, up, h, n, round_out != 0, C_(ctx)->stream);
+}
+
+int glc_swiglu_bwd(glc_ctx* ctx, const float* gate, const float* up, const float* dh, float* dgate, float* dup,
+                   size_t n, int accumulate, int round_out) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::swiglu_bwd(C_(ctx), gate, up, dh, dgate, dup, n, accumulate != 0, round_out != 0, C_(ctx)->stream);
+}
+
+int glc_rope(glc_ctx* ctx, float* x, int T, int S, int nh, int hd, const float* cos_t, const float* sin_t, int inverse,
+             int round_out) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::rope(C_(ctx), x, T, S, nh, hd, cos_t, sin_t, inverse != 0, round_out != 0, C_(ctx)->stream);
+}
+
+int glc_rope_table(int hd, int max_seq, float theta, float* cos_host, float* sin_host) {
+  if (hd <= 0 || (hd & 1) || max_seq <= 0 || !cos_host || !sin_host) return GLC_ERR_INVALID;
+  glc::rope_table_host(hd, max_seq, theta, cos_host, sin_host);
+  return GLC_OK;
+}
+
+int glc_attention_fwd(glc_ctx* ctx, const float* q, const float* k, const float* v, float* o, float* lse, int B,
+                      int S, int H, int Hkv, int hd, int round_out) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::attention_fwd(C_(ctx), q, k, v, o, lse, B, S, H, Hkv, hd, round_out != 0, C_(ctx)->stream);
+}
+
+int glc_attention_bwd(glc_ctx* ctx, const float* q, const float* k, const float* v, const float* o, const float* lse,
+                      const float* dO, float* dq, float* dk, float* dv, int B, int S, int H, int Hkv, int hd,
+                      int round_dv) {
+  if (!ctx || B <= 0 || S <= 0 || H <= 0) return GLC_ERR_INVALID;
+  void* ws = nullptr;
+  int rc = C_(ctx)->workspace(sizeof(float) * static_cast<size_t>(B) * H * S, &ws);
+  if (rc) return rc;
+  return glc::attention_bwd(C_(ctx), q, k, v, o, lse, dO, dq, dk, dv, static_cast<float*>(ws), B, S, H, Hkv, hd,
+                            round_dv != 0, C_(ctx)->stream);
+}
+
+int glc_softmax_ce(glc_ctx* ctx, float* logits, const int64_t* targets, int rows, int V, float scale, float* row_logp,
+                   float* loss, int write_grad, int round_out) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::softmax_ce(C_(ctx), logits, targets, rows, V, scale, row_logp, loss, write_grad != 0, round_out != 0,
+                         C_(ctx)->stream);
+}
+
+int glc_embed_fwd(glc_ctx* ctx, const int64_t* tokens, const float* E, const float* P, float* out, int T, int S, int d,
+                  int V) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::embed_fwd(C_(ctx), tokens, E, P, out, T, S, d, V, C_(ctx)->stream);
+}
+
+int glc_embed_bwd(glc_ctx* ctx, const int64_t* tokens_host, int T, const float* dh, float* dE, int d, int V) {
+  if (!ctx || T < 0 || (T && !tokens_host)) return GLC_ERR_INVALID;
+  if (T == 0) return GLC_OK;
+  Context* c = C_(ctx);
+  std::vector<int> seg_tok, seg_start, order;
+  glc::embed_segments_host(tokens_host, T, V, seg_tok, seg_start, order);
+  const int nseg = static_cast<int>(seg_tok.size());
+  std::vector<int> packed(seg_tok);
+  packed.insert(packed.end(), seg_start.begin(), seg_start.end());
+  packed.insert(packed.end(), order.begin(), order.end());
+  void* ws = nullptr;
+  int rc = c->workspace(packed.size() * sizeof(int), &ws);
+  if (rc) return rc;
+  int* dev = static_cast<int*>(ws);
+  cudaError_t e = cudaMemcpyAsync(dev, packed.data(), packed.size() * sizeof(int), cudaMemcpyHostToDevice, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return c->fail_cuda(e, "embed_bwd: segment upload");
+  return glc::embed_bwd(c, dev, dev + nseg, dev + 2 * nseg + 1, nseg, dh, dE, d, c->stream);
+}
+
+int glc_fill(glc_ctx* ctx, float* p, float value, size_t n) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::fill(C_(ctx), p, value, n, C_(ctx)->stream);
+}
+
+int glc_round_tf32(glc_ctx* ctx, const float* src, float* dst, size_t n) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::round_copy(C_(ctx), src, dst, n, C_(ctx)->stream);
+}
+
+int glc_add_inplace(glc_ctx* ctx, float* dst, const float* src, size_t n) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::add_inplace(C_(ctx), dst, src, n, C_(ctx)->stream);
+}
+
+}  // extern "C"

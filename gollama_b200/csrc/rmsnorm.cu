@@ -1,0 +1,225 @@
+// RMSNorm forward and backward (RMSNormTrainable, pkg/train/trainer.go:141-203).
+//
+// Forward: rms = float32(sqrt(float64(sum x^2)/cols + float64(eps))) per row
+// (trainer.go:158-163), y = (x / rms) * w.  One warp per row, float4 loads.
+// The per-row rms is saved for the backward.
+//
+// Backward, two variants:
+//   simplified (the reference, trainer.go:182-199): dx += dy*w/rms, dw += dy*x/rms
+//   full (Llama mode): dx += dy*w/rms - x * sum_j(dy_j w_j x_j) / (cols*rms^3)
+// One block per contiguous chunk of rows; each thread owns a fixed set of
+// float4 column chunks so its share of dw accumulates in registers.  Per-block
+// dw partials go to scratch memory and a second kernel adds them up in block
+// order (deterministic).  The residual-stream gradient dx may also be written
+// rounded to TF32 for the tensor-core GEMMs that consume it.
+#include "glc_internal.h"
+#include "sm100.cuh"
+
+namespace glc {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
+                                   float* __restrict__ rms, int rows, int cols, float eps, int round_out) {
+  const int wpb = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nc = cols >> 2;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  for (int row = blockIdx.x * wpb + (threadIdx.x >> 5); row < rows; row += gridDim.x * wpb) {
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * cols);
+    float ss = 0.f;
+    for (int j = lane; j < nc; j += 32) {
+      const float4 v = xr[j];
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    ss = warp_sum(ss);
+    const float r = __double2float_rn(sqrt(static_cast<double>(ss) / static_cast<double>(cols) +
+                                           static_cast<double>(eps)));
+    if (lane == 0) rms[row] = r;
+    float4* yr = reinterpret_cast<float4*>(y + static_cast<size_t>(row) * cols);
+    for (int j = lane; j < nc; j += 32) {
+      const float4 v = xr[j], g = w4[j];
+      float4 o;
+      o.x = __fmul_rn(__fdiv_rn(v.x, r), g.x);
+      o.y = __fmul_rn(__fdiv_rn(v.y, r), g.y);
+      o.z = __fmul_rn(__fdiv_rn(v.z, r), g.z);
+      o.w = __fmul_rn(__fdiv_rn(v.w, r), g.w);
+      if (round_out) {
+        o.x = round_tf32(o.x); o.y = round_tf32(o.y); o.z = round_tf32(o.z); o.w = round_tf32(o.w);
+      }
+      yr[j] = o;
+    }
+  }
+}
+
+template <int MAXC>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                          const float* __restrict__ rms, const float* __restrict__ dy,
+                                                          float* __restrict__ dx, float* __restrict__ dx_round,
+                                                          float* __restrict__ dw_partial, int rows, int cols,
+                                                          int rows_per_block, int full, int dx_accumulate) {
+  __shared__ float red[32];
+  const int nc = cols >> 2;
+  const int tid = threadIdx.x;
+  const int row0 = blockIdx.x * rows_per_block;
+  const int row1 = min(rows, row0 + rows_per_block);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4 wv[MAXC], acc[MAXC];
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * 256;
+    wv[i] = c < nc ? w4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int row = row0; row < row1; ++row) {
+    const float r = rms[row];
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * cols);
+    const float4* dyr = reinterpret_cast<const float4*>(dy + static_cast<size_t>(row) * cols);
+    float4 xv[MAXC], dv[MAXC];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * 256;
+      if (c < nc) {
+        xv[i] = xr[c];
+        dv[i] = dyr[c];
+        if (full)
+          s += dv[i].x * wv[i].x * xv[i].x + dv[i].y * wv[i].y * xv[i].y + dv[i].z * wv[i].z * xv[i].z +
+               dv[i].w * wv[i].w * xv[i].w;
+      }
+    }
+    float coef = 0.f;
+    if (full) {
+      s = warp_sum(s);
+      if ((tid & 31) == 0) red[tid >> 5] = s;
+      __syncthreads();
+      if (tid < 32) {
+        float t = tid < (blockDim.x >> 5) ? red[tid] : 0.f;
+        t = warp_sum(t);
+        if (tid == 0) red[0] = t;
+      }
+      __syncthreads();
+      const float tot = red[0];
+      __syncthreads();
+      coef = tot / (static_cast<float>(cols) * r * r * r);
+    }
+    float4* dxr = reinterpret_cast<float4*>(dx + static_cast<size_t>(row) * cols);
+    float4* dxq = dx_round ? reinterpret_cast<float4*>(dx_round + static_cast<size_t>(row) * cols) : nullptr;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * 256;
+      if (c < nc) {
+        float4 g;
+        g.x = __fdiv_rn(__fmul_rn(dv[i].x, wv[i].x), r);
+        g.y = __fdiv_rn(__fmul_rn(dv[i].y, wv[i].y), r);
+        g.z = __fdiv_rn(__fmul_rn(dv[i].z, wv[i].z), r);
+        g.w = __fdiv_rn(__fmul_rn(dv[i].w, wv[i].w), r);
+        if (full) {
+          g.x = __fsub_rn(g.x, __fmul_rn(xv[i].x, coef));
+          g.y = __fsub_rn(g.y, __fmul_rn(xv[i].y, coef));
+          g.z = __fsub_rn(g.z, __fmul_rn(xv[i].z, coef));
+          g.w = __fsub_rn(g.w, __fmul_rn(xv[i].w, coef));
+        }
+        if (dx_accumulate) {
+          const float4 o = dxr[c];
+          g.x = __fadd_rn(o.x, g.x); g.y = __fadd_rn(o.y, g.y); g.z = __fadd_rn(o.z, g.z); g.w = __fadd_rn(o.w, g.w);
+        }
+        dxr[c] = g;
+        if (dxq) dxq[c] = make_float4(round_tf32(g.x), round_tf32(g.y), round_tf32(g.z), round_tf32(g.w));
+        acc[i].x += __fdiv_rn(__fmul_rn(dv[i].x, xv[i].x), r);
+        acc[i].y += __fdiv_rn(__fmul_rn(dv[i].y, xv[i].y), r);
+        acc[i].z += __fdiv_rn(__fmul_rn(dv[i].z, xv[i].z), r);
+        acc[i].w += __fdiv_rn(__fmul_rn(dv[i].w, xv[i].w), r);
+      }
+    }
+  }
+  float4* part = reinterpret_cast<float4*>(dw_partial + static_cast<size_t>(blockIdx.x) * cols);
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * 256;
+    if (c < nc) part[c] = acc[i];
+  }
+}
+
+// dw[j] (+)= sum over blocks b (ascending) of partial[b][j]
+__global__ void column_sum_kernel(const float* __restrict__ partial, int nblocks, int cols, float* __restrict__ out,
+                                  int accumulate) {
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < cols; j += gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int b = 0; b < nblocks; ++b) s += partial[static_cast<size_t>(b) * cols + j];
+    out[j] = accumulate ? __fadd_rn(out[j], s) : s;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+int rmsnorm_fwd(Context* ctx, const float* x, const float* w, float* y, float* rms, int rows, int cols, float eps,
+                bool round_out, cudaStream_t s) {
+  if (rows < 0 || cols <= 0 || (cols & 3)) return ctx->fail(GLC_ERR_INVALID, "rmsnorm_fwd: cols must be a positive multiple of 4");
+  if (rows == 0) return 0;
+  if (!x || !w || !y || !rms || !aligned16(x) || !aligned16(w) || !aligned16(y))
+    return ctx->fail(GLC_ERR_INVALID, "rmsnorm_fwd: null or misaligned pointer");
+  const int wpb = 8;
+  unsigned grid = static_cast<unsigned>((rows + wpb - 1) / wpb);
+  ProfScope prof(ctx, PROF_RMSNORM, 4.0 * (2.0 * rows * cols + rows + cols), s);
+  rmsnorm_fwd_kernel<<<grid, wpb * 32, 0, s>>>(x, w, y, rms, rows, cols, eps, round_out ? 1 : 0);
+  GLC_LAUNCH_CHECK(ctx, "rmsnorm_fwd");
+  return 0;
+}
+
+int rmsnorm_bwd(Context* ctx, const float* x, const float* w, const float* rms, const float* dy, float* dx,
+                float* dx_round, float* dw, int rows, int cols, bool full, bool dx_accumulate, bool dw_accumulate,
+                float* scratch, size_t scratch_bytes, cudaStream_t s) {
+  if (rows < 0 || cols <= 0 || (cols & 3)) return ctx->fail(GLC_ERR_INVALID, "rmsnorm_bwd: cols must be a positive multiple of 4");
+  const int nc = cols / 4;
+  if (nc > 8 * 256) return ctx->fail(GLC_ERR_INVALID, "rmsnorm_bwd: cols above 8192 are not supported");
+  if (rows == 0) {
+    if (dw && !dw_accumulate) {
+      cudaError_t e = cudaMemsetAsync(dw, 0, sizeof(float) * cols, s);
+      if (e != cudaSuccess) return ctx->fail_cuda(e, "rmsnorm_bwd: memset");
+    }
+    return 0;
+  }
+  if (!x || !w || !rms || !dy || !dx || !dw || !aligned16(x) || !aligned16(w) || !aligned16(dy) || !aligned16(dx) ||
+      (dx_round && !aligned16(dx_round)))
+    return ctx->fail(GLC_ERR_INVALID, "rmsnorm_bwd: null or misaligned pointer");
+  int nblocks = 4 * ctx->num_sms;
+  if (nblocks > rows) nblocks = rows;
+  const int rpb = (rows + nblocks - 1) / nblocks;
+  nblocks = (rows + rpb - 1) / rpb;
+  const size_t need = static_cast<size_t>(nblocks) * cols * sizeof(float);
+  float* partial = scratch;
+  if (partial == nullptr) {
+    void* ws = nullptr;
+    int rc = ctx->workspace(need, &ws);
+    if (rc) return rc;
+    partial = static_cast<float*>(ws);
+  } else if (scratch_bytes < need) {
+    return ctx->fail(GLC_ERR_INVALID, "rmsnorm_bwd: scratch buffer too small");
+  }
+  const int fl = full ? 1 : 0, acc = dx_accumulate ? 1 : 0;
+  ProfScope prof(ctx, PROF_RMSNORM,
+                 4.0 * static_cast<double>(rows) * cols * (3 + (dx_accumulate ? 1 : 0) + (dx_round ? 1 : 0)) + 4.0 * rows,
+                 s);
+  if (nc <= 256)
+    rmsnorm_bwd_kernel<1><<<nblocks, 256, 0, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
+  else if (nc <= 512)
+    rmsnorm_bwd_kernel<2><<<nblocks, 256, 0, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
+  else if (nc <= 1024)
+    rmsnorm_bwd_kernel<4><<<nblocks, 256, 0, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
+  else
+    rmsnorm_bwd_kernel<8><<<nblocks, 256, 0, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
+  GLC_LAUNCH_CHECK(ctx, "rmsnorm_bwd");
+  column_sum_kernel<<<(cols + 255) / 256, 256, 0, s>>>(partial, nblocks, cols, dw, dw_accumulate ? 1 : 0);
+  GLC_LAUNCH_CHECK(ctx, "rmsnorm_bwd column sum");
+  return 0;
+}
+
+}  // namespace glc

@@ -79,6 +79,23 @@ GLC_API int glc_memcpy_d2h_async(glc_ctx* ctx, void* dst, const void* src, size_
 GLC_API int glc_timer_start(glc_ctx* ctx);
 GLC_API int glc_timer_stop(glc_ctx* ctx, float* ms); /* synchronises on the stop event */
 
+/* ------------------------------------------------------------------ profiling
+ * While enabled, every kernel launch of this library is bracketed by a CUDA
+ * event pair on its stream.  glc_profile_end synchronises and returns, per
+ * kernel class (GLC_PROF_*), the launch count, the summed device time and the
+ * summed algorithmic work (FLOPs for GEMM and attention, bytes otherwise). */
+#define GLC_PROF_GEMM 0
+#define GLC_PROF_ATTN_FWD 1
+#define GLC_PROF_ATTN_BWD 2
+#define GLC_PROF_RMSNORM 3
+#define GLC_PROF_SWIGLU 4
+#define GLC_PROF_CE 5
+#define GLC_PROF_ADAMW 6
+#define GLC_PROF_OTHER 7
+#define GLC_PROF_CLASSES 8
+GLC_API int glc_profile_begin(glc_ctx* ctx);
+GLC_API int glc_profile_end(glc_ctx* ctx, int n_classes, uint64_t* counts, double* total_ms, double* total_work);
+
 /* ------------------------------------------------------------------ linear layers
  * All three run the tcgen05 TF32 tensor-core GEMM with fp32 accumulation.
  * X: [M,K], W: [N,K], Y/dY: [M,N].  Leading dimensions equal the row lengths;
@@ -102,6 +119,140 @@ GLC_API int glc_linear_bwd_dw(glc_ctx* ctx, const float* dY, const float* X, flo
  * K-major (ptr[i*ld+k]).  round_out rounds the stored values to TF32. */
 GLC_API int glc_gemm_tf32(glc_ctx* ctx, const float* A, int lda, int a_mn, const float* B, int ldb, int b_mn, float* C,
                   int ldc, int M, int N, int K, int accumulate, const float* R, int ldr, int round_out);
+
+/* ------------------------------------------------------------------ fused / elementwise ops
+ * Building blocks of the tape's GradFns; each mirrors one reference node.
+ * round_out != 0 writes TF32-rounded values (round to nearest) for tensors
+ * whose consumers are tensor-core GEMMs. */
+
+/* RMSNormTrainable.Forward (pkg/train/trainer.go:141-168): y = (x/rms)*w with
+ * rms = float32(sqrt(float64(sum x^2)/cols + float64(eps))); rms[rows] saved. */
+GLC_API int glc_rmsnorm_fwd(glc_ctx* ctx, const float* x, const float* w, float* y, float* rms, int rows, int cols,
+                            float eps, int round_out);
+/* Its GradFn (trainer.go:170-200).  full=0: the reference's simplified
+ * gradient; full=1: the exact RMSNorm gradient.  dx (+)= ..., dw (+)= ...;
+ * dx_round (nullable) receives dx rounded to TF32. */
+GLC_API int glc_rmsnorm_bwd(glc_ctx* ctx, const float* x, const float* w, const float* rms, const float* dy,
+                            float* dx, float* dx_round, float* dw, int rows, int cols, int full, int dx_accumulate,
+                            int dw_accumulate);
+/* SiLUGrad + product node of forwardFFN (pkg/tensor/grad.go:417-449,
+ * pkg/train/trainer.go:396-422) fused: h = silu(gate) * up, with the
+ * reference's exp32. n = number of elements (multiple of 4). */
+GLC_API int glc_swiglu_fwd(glc_ctx* ctx, const float* gate, const float* up, float* h, size_t n, int round_out);
+GLC_API int glc_swiglu_bwd(glc_ctx* ctx, const float* gate, const float* up, const float* dh, float* dgate,
+                           float* dup, size_t n, int accumulate, int round_out);
+/* RoPE (pkg/model/rope.go:96-126, consecutive pairs) in place on x[T, nh*hd],
+ * position t % S; inverse=1 is the backward rotation.  cos_t/sin_t are the
+ * [max_seq][hd/2] tables of glc_rope_table (device pointers). */
+GLC_API int glc_rope(glc_ctx* ctx, float* x, int T, int S, int nh, int hd, const float* cos_t, const float* sin_t,
+                     int inverse, int round_out);
+/* Host-side RoPE tables (precomputeFreqs, pkg/model/rope.go:33-48). */
+GLC_API int glc_rope_table(int hd, int max_seq, float theta, float* cos_host, float* sin_host);
+/* Causal attention (forwardAttention, pkg/train/trainer.go:323-389) with
+ * grouped KV heads (pkg/model/attention.go:118,149).  q,o: [B*S, H*hd];
+ * k,v: [B*S, Hkv*hd]; lse: [B, H, S]. */
+GLC_API int glc_attention_fwd(glc_ctx* ctx, const float* q, const float* k, const float* v, float* o, float* lse,
+                              int B, int S, int H, int Hkv, int hd, int round_out);
+/* Its backward (dq, dk, dv overwritten).  Uses the context workspace. */
+GLC_API int glc_attention_bwd(glc_ctx* ctx, const float* q, const float* k, const float* v, const float* o,
+                              const float* lse, const float* dO, float* dq, float* dk, float* dv, int B, int S, int H,
+                              int Hkv, int hd, int round_dv);
+/* SoftmaxCrossEntropyGrad (pkg/tensor/grad.go:210-280): loss (device float)
+ * = mean over rows of -log32(p_target + 1e-10); write_grad=1 overwrites the
+ * logits with the gradient (p - onehot) * scale. row_logp: [rows] scratch. */
+GLC_API int glc_softmax_ce(glc_ctx* ctx, float* logits, const int64_t* targets, int rows, int V, float scale,
+                           float* row_logp, float* loss, int write_grad, int round_out);
+/* Embedding lookup of TrainableModel.Forward (trainer.go:275-291):
+ * out[t] = E[tok[t]] (+ P[t % S] when P != NULL); ids outside [0,V) read row 0. */
+GLC_API int glc_embed_fwd(glc_ctx* ctx, const int64_t* tokens, const float* E, const float* P, float* out, int T,
+                          int S, int d, int V);
+/* Embedding gradient dE[tok[t]] += dh[t] (t ascending, deterministic);
+ * tokens_host are the same ids on the host. */
+GLC_API int glc_embed_bwd(glc_ctx* ctx, const int64_t* tokens_host, int T, const float* dh, float* dE, int d, int V);
+GLC_API int glc_fill(glc_ctx* ctx, float* p, float value, size_t n);
+GLC_API int glc_round_tf32(glc_ctx* ctx, const float* src, float* dst, size_t n);
+/* addInplace (pkg/tensor/grad.go:200-204): dst += src. */
+GLC_API int glc_add_inplace(glc_ctx* ctx, float* dst, const float* src, size_t n);
+
+/* ------------------------------------------------------------------ model / trainer */
+#define GLC_SEMANTICS_REFERENCE 0 /* pkg/train exactly, quirks included */
+#define GLC_SEMANTICS_LLAMA 1     /* RoPE, GQA, attention backward, full RMSNorm backward, CE-seeded backward */
+
+typedef struct glc_train_config {
+  /* TrainConfig (pkg/train/trainer.go:15-40) */
+  int vocab_size;
+  int hidden_size;
+  int num_layers;
+  int num_heads;
+  int intermediate_size;
+  int max_seq_len;
+  int batch_size;
+  int block_size;
+  float learning_rate;
+  float weight_decay;
+  int warmup_steps;
+  int max_steps;
+  float grad_clip_norm;
+  /* AdamW hyper-parameters (NewAdamW defaults, pkg/train/optimizer.go:24-34) */
+  float beta1;
+  float beta2;
+  float epsilon;
+  /* extensions */
+  int num_kv_heads; /* Llama semantics; 0 means num_heads */
+  int semantics;    /* GLC_SEMANTICS_* */
+  float norm_eps;   /* RMSNormTrainable.Eps, 1e-5 */
+  float rope_theta; /* 10000 */
+  float init_std;   /* std of the seeded normal weight init */
+  uint64_t seed;
+  int world_size;   /* data-parallel ranks (1 = single GPU) */
+} glc_train_config;
+
+typedef struct glc_model glc_model;
+typedef struct glc_trainer glc_trainer;
+
+/* DefaultTrainConfig (pkg/train/trainer.go:43-69) plus the extension defaults. */
+GLC_API int glc_default_train_config(glc_train_config* cfg);
+/* NewTrainableModel (pkg/train/trainer.go:206-256): parameters in one device
+ * arena in Params() order; matrices N(0, init_std) from `seed` (the Go
+ * math/rand Xavier init is not reproducible without Go), RMSNorm weights 1. */
+GLC_API int glc_model_create(glc_ctx* ctx, const glc_train_config* cfg, glc_model** out);
+GLC_API int glc_model_destroy(glc_model* m);
+/* Params() (trainer.go:429-431): count, and per parameter its offset/shape in
+ * the flat arena and whether it currently has a gradient (Grad != nil). */
+GLC_API int glc_model_num_params(glc_model* m, int* n, int64_t* total_floats);
+GLC_API int glc_model_param_info(glc_model* m, int idx, int64_t* offset, int64_t* rows, int64_t* cols,
+                                 int* has_grad);
+/* Host <-> device copies of the whole arena (parameters, gradients, AdamW m/v). */
+GLC_API int glc_model_set_params(glc_model* m, const float* host, int64_t n);
+GLC_API int glc_model_get_params(glc_model* m, float* host, int64_t n);
+GLC_API int glc_model_get_grads(glc_model* m, float* host, int64_t n);
+GLC_API int glc_model_get_moments(glc_model* m, float* m_host, float* v_host, int64_t n);
+/* NewTrainer (trainer.go:447-459): AdamW with the configured hyper-parameters
+ * and the warmup + cosine LRScheduler. */
+GLC_API int glc_trainer_create(glc_model* m, glc_trainer** out);
+GLC_API int glc_trainer_destroy(glc_trainer* t);
+/* Trainer.TrainStep (trainer.go:462-505): LR, ZeroGrad, forward, loss,
+ * backward, (data-parallel gradient allreduce), gradient clipping, AdamW.
+ * inputs/targets: host int64 [B*S] (row b = sequence b).  Returns the loss. */
+GLC_API int glc_train_step(glc_trainer* t, const int64_t* inputs, const int64_t* targets, int B, int S, float* loss);
+/* The same step with token ids already in device memory (no host copies). */
+GLC_API int glc_train_step_device(glc_trainer* t, const int64_t* inputs_dev, const int64_t* targets_dev,
+                                  const int64_t* inputs_host, int B, int S, float* loss);
+/* Global gradient norm before clipping and the learning rate of the last step. */
+GLC_API int glc_trainer_last_stats(glc_trainer* t, double* grad_norm, float* lr, int* step);
+/* Kernels launched by the last step (all of them this library's). */
+GLC_API int glc_trainer_last_launches(glc_trainer* t, uint64_t* n);
+
+/* ------------------------------------------------------------------ data parallel (NCCL)
+ * One process per GPU.  Rank 0 creates the id and shares it (file, store, ...);
+ * every rank then calls glc_dp_init.  Gradients are summed with ncclAllReduce
+ * (fp32) over NVLink during glc_train_step. */
+GLC_API int glc_dp_unique_id(unsigned char id[128]);
+GLC_API int glc_dp_init(glc_ctx* ctx, int rank, int world, const unsigned char id[128], int timeout_ms);
+GLC_API int glc_dp_allreduce_sum(glc_ctx* ctx, float* buf, size_t n);
+GLC_API int glc_dp_allreduce_max_host(glc_ctx* ctx, double* value);
+GLC_API int glc_dp_barrier(glc_ctx* ctx);
+GLC_API int glc_dp_destroy(glc_ctx* ctx);
 
 #ifdef __cplusplus
 }

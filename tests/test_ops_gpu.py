@@ -1,0 +1,211 @@
+"""Each CUDA op through the C ABI against the oracle's restatement of the
+reference op (oracle/oracle.c), on seeded inputs."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from oracle.oracle import Oracle
+from tests.helpers import FP32_RTOL, rel_fro, threads
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def orc():
+    return Oracle(threads=threads())
+
+
+def rng(seed):
+    return np.random.default_rng(seed)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 128), (257, 128), (1000, 512), (4096, 2048), (3, 8192)])
+def test_rmsnorm_fwd(ctx, orc, rows, cols):
+    r = rng(rows + cols)
+    x = r.standard_normal((rows, cols), dtype=np.float32)
+    w = (1 + 0.1 * r.standard_normal(cols)).astype(np.float32)
+    ref_y, ref_rms = orc.rmsnorm_fwd(x, w, 1e-5)
+    dx, dw, dy, drms = ctx.from_numpy(x), ctx.from_numpy(w), ctx.empty((rows, cols)), ctx.empty((rows,))
+    ctx.call("glc_rmsnorm_fwd", dx.ptr, dw.ptr, dy.ptr, drms.ptr, rows, cols, C.c_float(1e-5), 0)
+    ctx.sync()
+    assert rel_fro(drms.numpy(), ref_rms) < 1e-6
+    assert rel_fro(dy.numpy(), ref_y) < 1e-6
+
+
+@pytest.mark.parametrize("full", [0, 1])
+@pytest.mark.parametrize("rows,cols", [(5, 128), (300, 512), (2048, 2048)])
+def test_rmsnorm_bwd(ctx, orc, rows, cols, full):
+    r = rng(rows * 3 + full)
+    x = r.standard_normal((rows, cols), dtype=np.float32)
+    w = (1 + 0.1 * r.standard_normal(cols)).astype(np.float32)
+    g = r.standard_normal((rows, cols), dtype=np.float32)
+    dx0 = r.standard_normal((rows, cols), dtype=np.float32)
+    dw0 = r.standard_normal(cols).astype(np.float32)
+    _, rms = orc.rmsnorm_fwd(x, w, 1e-5)
+    ref_dx, ref_dw = orc.rmsnorm_bwd(x, w, rms, g, full, dx=dx0.copy(), dw=dw0.copy())
+    bx, bw, brms, bg = ctx.from_numpy(x), ctx.from_numpy(w), ctx.from_numpy(rms), ctx.from_numpy(g)
+    bdx, bdw, bdxr = ctx.from_numpy(dx0), ctx.from_numpy(dw0), ctx.empty((rows, cols))
+    ctx.call("glc_rmsnorm_bwd", bx.ptr, bw.ptr, brms.ptr, bg.ptr, bdx.ptr, bdxr.ptr, bdw.ptr, rows, cols, full, 1, 1)
+    ctx.sync()
+    out_dx = bdx.numpy()
+    assert rel_fro(out_dx, ref_dx) < FP32_RTOL
+    assert rel_fro(bdw.numpy(), ref_dw) < FP32_RTOL
+    # the rounded copy is dx rounded to TF32 (10 mantissa bits)
+    assert np.max(np.abs(bdxr.numpy() - out_dx) / (np.abs(out_dx) + 1e-30)) <= 2.0**-11
+
+
+def test_rmsnorm_simplified_matches_reference_formula(ctx):
+    """Reference-mode backward is exactly dx = dy*w/rms, dw = sum dy*x/rms (trainer.go:186-198)."""
+    rows, cols = 64, 128
+    r = rng(1)
+    x = r.standard_normal((rows, cols), dtype=np.float32)
+    w = r.standard_normal(cols).astype(np.float32)
+    g = r.standard_normal((rows, cols), dtype=np.float32)
+    rms = np.sqrt((x.astype(np.float64) ** 2).mean(1) + 1e-5).astype(np.float32)
+    bx, bw, brms, bg = ctx.from_numpy(x), ctx.from_numpy(w), ctx.from_numpy(rms), ctx.from_numpy(g)
+    bdx, bdw = ctx.zeros((rows, cols)), ctx.zeros((cols,))
+    ctx.call("glc_rmsnorm_bwd", bx.ptr, bw.ptr, brms.ptr, bg.ptr, bdx.ptr, None, bdw.ptr, rows, cols, 0, 0, 0)
+    ctx.sync()
+    ref_dx = (g * w[None, :]) / rms[:, None]
+    assert np.array_equal(bdx.numpy(), ref_dx.astype(np.float32))
+
+
+@pytest.mark.parametrize("n", [4, 4096, 1 << 20])
+def test_swiglu_fwd_bit_exact(ctx, orc, n):
+    """silu(g)*u with the reference's exp32 must be bit-identical to the oracle."""
+    r = rng(n)
+    g = (r.standard_normal(n) * 4).astype(np.float32)
+    g[:4] = [0.0, -88.5, 90.0, -20.0][: min(4, n)]
+    u = r.standard_normal(n).astype(np.float32)
+    gs, sig = orc.silu_fwd(g)
+    ref = gs * u
+    bg, bu, bh = ctx.from_numpy(g), ctx.from_numpy(u), ctx.empty((n,))
+    ctx.call("glc_swiglu_fwd", bg.ptr, bu.ptr, bh.ptr, n, 0)
+    ctx.sync()
+    assert np.array_equal(bh.numpy(), ref)
+
+
+@pytest.mark.parametrize("n", [4096, 1 << 20])
+def test_swiglu_bwd_bit_exact(ctx, orc, n):
+    r = rng(n + 1)
+    g = (r.standard_normal(n) * 4).astype(np.float32)
+    u = r.standard_normal(n).astype(np.float32)
+    dh = r.standard_normal(n).astype(np.float32)
+    gs, sig = orc.silu_fwd(g)
+    # product node then SiLU, as in the reference's reverse topological order
+    dgs = dh * u
+    dup = dh * gs
+    dgate = orc.silu_bwd(g, sig, dgs)
+    bg, bu, bdh = ctx.from_numpy(g), ctx.from_numpy(u), ctx.from_numpy(dh)
+    bdg, bdu = ctx.empty((n,)), ctx.empty((n,))
+    ctx.call("glc_swiglu_bwd", bg.ptr, bu.ptr, bdh.ptr, bdg.ptr, bdu.ptr, n, 0, 0)
+    ctx.sync()
+    assert np.array_equal(bdu.numpy(), dup)
+    assert np.array_equal(bdg.numpy(), dgate)
+
+
+@pytest.mark.parametrize("rows,V", [(7, 256), (512, 32000), (64, 1000)])
+@pytest.mark.parametrize("write_grad", [0, 1])
+def test_softmax_ce(ctx, orc, rows, V, write_grad):
+    r = rng(rows + V)
+    logits = (r.standard_normal((rows, V)) * 2).astype(np.float32)
+    tg = r.integers(0, V, rows).astype(np.int64)
+    tg[0] = -1          # ignored target: no loss, still counted in the mean
+    if rows > 1:
+        tg[1] = V + 5   # out of range: ignored too
+    ref_loss, probs = orc.softmax_ce(logits, tg, want_probs=True)
+    bl, bt = ctx.from_numpy(logits), ctx.from_numpy(tg)
+    blogp, bloss = ctx.empty((rows,)), ctx.empty((1,))
+    scale = np.float32(1.0) / np.float32(rows)
+    ctx.call("glc_softmax_ce", bl.ptr, bt.ptr, rows, V, C.c_float(scale), blogp.ptr, bloss.ptr, write_grad, 0)
+    ctx.sync()
+    loss = float(bloss.numpy()[0])
+    assert abs(loss - ref_loss) <= 1e-5 * abs(ref_loss)
+    if write_grad:
+        ref_g = orc.softmax_ce_grad(probs, tg)
+        assert rel_fro(bl.numpy(), ref_g) < 1e-5
+        # rows of the CE gradient sum to zero when the target is valid
+        assert np.abs(bl.numpy()[2:].sum(1)).max() < 1e-5
+
+
+def test_rope_matches_oracle_and_inverts(ctx, orc):
+    T, S, nh, hd = 256, 64, 4, 64
+    r = rng(2)
+    x = r.standard_normal((T, nh * hd), dtype=np.float32)
+    ct, st = orc.rope_table(hd, S, 10000.0)
+    ch, sh = np.zeros_like(ct), np.zeros_like(st)
+    assert ctx.lib.glc_rope_table(hd, S, C.c_float(10000.0), ch.ctypes.data_as(C.c_void_p),
+                                  sh.ctypes.data_as(C.c_void_p)) == 0
+    assert np.array_equal(ch, ct) and np.array_equal(sh, st)
+    bx, bc, bs = ctx.from_numpy(x), ctx.from_numpy(ct), ctx.from_numpy(st)
+    ctx.call("glc_rope", bx.ptr, T, S, nh, hd, bc.ptr, bs.ptr, 0, 0)
+    ctx.sync()
+    ref = orc.rope_apply(x, S, nh, hd, ct, st)
+    assert np.array_equal(bx.numpy(), ref)
+    ctx.call("glc_rope", bx.ptr, T, S, nh, hd, bc.ptr, bs.ptr, 1, 0)
+    ctx.sync()
+    ref_inv = orc.rope_apply(ref, S, nh, hd, ct, st, inverse=True)
+    assert np.array_equal(bx.numpy(), ref_inv)
+    assert rel_fro(bx.numpy(), x) < 1e-6
+
+
+@pytest.mark.parametrize("B,S,H,Hkv,hd", [(2, 64, 4, 4, 32), (1, 100, 4, 2, 64), (2, 256, 8, 4, 64), (1, 130, 2, 1, 32)])
+def test_attention_fwd_bwd(ctx, orc, B, S, H, Hkv, hd):
+    T = B * S
+    r = rng(T + H)
+    q = r.standard_normal((T, H * hd), dtype=np.float32)
+    k = r.standard_normal((T, Hkv * hd), dtype=np.float32)
+    v = r.standard_normal((T, Hkv * hd), dtype=np.float32)
+    dO = r.standard_normal((T, H * hd), dtype=np.float32)
+    ref_o = orc.attention_fwd(q, k, v, S, H, Hkv, hd)
+    ref_dq, ref_dk, ref_dv = orc.attention_bwd(q, k, v, dO, S, H, Hkv, hd)
+    bq, bk, bv, bdo = ctx.from_numpy(q), ctx.from_numpy(k), ctx.from_numpy(v), ctx.from_numpy(dO)
+    bo, blse = ctx.empty((T, H * hd)), ctx.empty((B, H, S))
+    ctx.call("glc_attention_fwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, B, S, H, Hkv, hd, 0)
+    bdq, bdk, bdv = ctx.empty(q.shape), ctx.empty(k.shape), ctx.empty(v.shape)
+    ctx.call("glc_attention_bwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, bdq.ptr, bdk.ptr, bdv.ptr,
+             B, S, H, Hkv, hd, 0)
+    ctx.sync()
+    assert rel_fro(bo.numpy(), ref_o) < FP32_RTOL
+    assert rel_fro(bdq.numpy(), ref_dq) < 1e-4
+    assert rel_fro(bdk.numpy(), ref_dk) < 1e-4
+    assert rel_fro(bdv.numpy(), ref_dv) < 1e-4
+
+
+def test_embedding_fwd_bwd(ctx):
+    V, d, B, S = 50, 64, 3, 20
+    T = B * S
+    r = rng(9)
+    E = r.standard_normal((V, d), dtype=np.float32)
+    P = r.standard_normal((S, d), dtype=np.float32)
+    tok = r.integers(0, V, T).astype(np.int64)
+    tok[3], tok[7] = -2, V + 1  # clamped to id 0 (trainer.go:280-282)
+    clamped = np.where((tok < 0) | (tok >= V), 0, tok)
+    bt, bE, bP, bo = ctx.from_numpy(tok), ctx.from_numpy(E), ctx.from_numpy(P), ctx.empty((T, d))
+    ctx.call("glc_embed_fwd", bt.ptr, bE.ptr, bP.ptr, bo.ptr, T, S, d, V)
+    ctx.sync()
+    ref = E[clamped] + P[np.arange(T) % S]
+    assert np.array_equal(bo.numpy(), ref)
+    dh = r.standard_normal((T, d), dtype=np.float32)
+    dE0 = r.standard_normal((V, d), dtype=np.float32)
+    bdh, bdE = ctx.from_numpy(dh), ctx.from_numpy(dE0)
+    ctx.call("glc_embed_bwd", tok.ctypes.data_as(C.c_void_p), T, bdh.ptr, bdE.ptr, d, V)
+    ctx.sync()
+    want = dE0.copy()
+    for t in range(T):  # dE[tok] += dh[t], t ascending
+        want[clamped[t]] += dh[t]
+    assert np.array_equal(bdE.numpy(), want)
+
+
+def test_round_tf32(ctx):
+    x = np.array([1.0 + 3 * 2.0**-12, 1.0 + 2.0**-12, -(1.0 + 3 * 2.0**-12), 3.0e-39, 1.0e30], np.float32)
+    x = np.concatenate([x, np.zeros(3, np.float32)])
+    bx, by = ctx.from_numpy(x), ctx.empty(x.shape)
+    ctx.call("glc_round_tf32", bx.ptr, by.ptr, x.size)
+    ctx.sync()
+    y = by.numpy()
+    assert y[0] == np.float32(1.0 + 2.0**-10)
+    assert y[2] == -np.float32(1.0 + 2.0**-10)
+    bits = y.view(np.uint32)
+    assert np.all(bits & 0x1FFF == 0)

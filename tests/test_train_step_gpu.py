@@ -1,0 +1,95 @@
+"""Trainer.TrainStep (pkg/train/trainer.go:462-505) on the GPU against the
+oracle's step on identical seeded parameters and tokens.
+
+Bars (tests/helpers.py): loss within 1e-4 relative; every parameter gradient
+(as TrainStep leaves it: after clipping) and every post-step weight within
+2e-3 relative Frobenius error; the set of parameters that have a gradient
+(Go's `Grad != nil`) identical."""
+import numpy as np
+import pytest
+
+from gollama_b200 import synthetic as syn
+from gollama_b200.train import NewTrainableModel, NewTrainer, config_for
+from oracle.oracle import Oracle, TrainState
+from tests.helpers import GRAD_RFRO, LOSS_RTOL, STEP_HPARAMS, WEIGHT_RFRO, oracle_config, oracle_optim, rel_fro, threads
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [syn.TINY, syn.TINY_LLAMA_MODE, syn.SMALL, syn.SMALL_LLAMA_MODE]
+
+
+def run_oracle(shape, params, inputs, targets, steps=1):
+    orc = Oracle(threads=threads())
+    ocfg = oracle_config(shape)
+    st = TrainState.create(params, len(orc.param_layout(ocfg)), oracle_optim())
+    losses = []
+    for s in range(steps):
+        loss, norm = orc.train_step(ocfg, st, inputs[s], targets[s])
+        losses.append(loss)
+    return losses, st, orc.param_layout(ocfg)
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: s.name)
+def test_train_step_parity(ctx, shape):
+    seed = 1234
+    params = syn.init_params(shape, seed)
+    inputs, targets = syn.batch(shape, seed)
+    (oloss,), st, layout = run_oracle(shape, params, [inputs], [targets])
+
+    model = NewTrainableModel(config_for(shape, **STEP_HPARAMS), ctx)
+    model.set_params(params)
+    tr = NewTrainer(model)
+    loss = tr.TrainStep(inputs, targets)
+    assert tr.last_launches() > 0
+
+    assert abs(loss - oloss) <= LOSS_RTOL * abs(oloss), (loss, oloss)
+    got_p = model.Params()
+    assert [p.has_grad for p in got_p] == [bool(h) for h in st.has_grad]
+    grads, weights = model.get_grads(), model.get_params()
+    worst = []
+    for p, (off, r, c) in zip(got_p, layout):
+        n = r * c
+        assert (p.offset, p.shape) == (off, (r, c))
+        if p.has_grad:
+            e = rel_fro(grads[off : off + n], st.grads[off : off + n])
+            worst.append((e, p.index))
+            assert e < GRAD_RFRO, f"grad of param {p.index} {p.shape}: rel-fro {e:.3e}"
+        e = rel_fro(weights[off : off + n], st.params[off : off + n])
+        assert e < WEIGHT_RFRO, f"weight of param {p.index}: rel-fro {e:.3e}"
+    worst.sort(reverse=True)
+    print(f"\n{shape.name}: loss {loss:.6f} (oracle {oloss:.6f}); worst grad rel-fro {worst[:3]}")
+
+
+def test_reference_mode_gradient_set(ctx):
+    """Reference semantics: attention has no GradFn (trainer.go:335-337) and
+    the embedding none either (:290-291), so WQ/WK/WV, every AttnNorm and
+    PosEmbed never get a gradient; AdamW leaves them untouched (optimizer.go:45)."""
+    shape = syn.TINY
+    params = syn.init_params(shape, 5)
+    inputs, targets = syn.batch(shape, 5)
+    model = NewTrainableModel(config_for(shape, **STEP_HPARAMS), ctx)
+    model.set_params(params)
+    NewTrainer(model).TrainStep(inputs, targets)
+    names = [n for n, _ in syn.param_shapes(shape)]
+    after = model.get_params()
+    for p, name in zip(model.Params(), names):
+        frozen = name == "PosEmbed" or name.endswith((".WQ", ".WK", ".WV", ".AttnNorm"))
+        assert p.has_grad == (not frozen), name
+        seg = slice(p.offset, p.offset + p.shape[0] * p.shape[1])
+        if frozen:
+            assert np.array_equal(after[seg], params[seg]), name
+
+
+def test_multi_step_loss_curve(ctx):
+    """Small Llama-mode decoder: 5 steps track the oracle's loss curve."""
+    shape = syn.SMALL_LLAMA_MODE.with_(layers=2)
+    params = syn.init_params(shape, 77)
+    batches = [syn.batch(shape, 100 + s) for s in range(5)]
+    olosses, st, _ = run_oracle(shape, params, [b[0] for b in batches], [b[1] for b in batches], steps=5)
+    model = NewTrainableModel(config_for(shape, **STEP_HPARAMS), ctx)
+    model.set_params(params)
+    tr = NewTrainer(model)
+    losses = [tr.TrainStep(i, t) for i, t in batches]
+    for a, b in zip(losses, olosses):
+        assert abs(a - b) <= 1e-3 * abs(b), (losses, olosses)
+    assert rel_fro(model.get_params(), st.params) < WEIGHT_RFRO
