@@ -56,7 +56,13 @@ def parse_args():
     ap.add_argument("--profile-steps", type=int, default=2)
     ap.add_argument("--sample-tokens", type=int, default=4, help="tokens per CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--light", action="store_true",
+                    help="skip the CPU baseline, the TF32 peak measurement and the profiled steps (for ncu launch lists)")
+    a = ap.parse_args()
+    if a.light:
+        a.no_cpu_baseline = True
+        a.profile_steps = 0
+    return a
 
 
 def dist_env():
@@ -254,8 +260,9 @@ def run_reference(args):
     from gollama_b200 import synthetic as syn
 
     tokens_per_step = syn.TINYLLAMA.tokens
-    warm_times, opt_s, threads = cpu_sample_rate(args.sample_tokens, steps=max(1, args.warmup), warm=False)
-    times, _, _ = cpu_sample_rate(args.sample_tokens, steps=max(1, args.steps), warm=False) if args.steps else ([], 0, 0)
+    W, K = max(0, args.warmup), max(1, args.steps)
+    all_times, opt_s, threads = cpu_sample_rate(args.sample_tokens, steps=W + K, warm=False)
+    times = all_times[W:]
     v = cpu_tokens_per_s(statistics.mean(times), args.sample_tokens, opt_s, tokens_per_step)
     base = cpu_baseline_dict(times, opt_s, threads, args.sample_tokens, tokens_per_step)
     out = {
@@ -396,7 +403,7 @@ def run_ours(args):
         return 0
 
     peaks, peak_src = measured_peaks()
-    tf32 = measure_tf32_peak(local)
+    tf32 = None if args.light else measure_tf32_peak(local)
     if tf32:
         tc_peak, tc_src = tf32, "cuBLAS TF32 8192^3 GEMM measured back to back in this run"
     else:
