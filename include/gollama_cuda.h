@@ -157,6 +157,22 @@ GLC_API int glc_attention_fwd(glc_ctx* ctx, const float* q, const float* k, cons
 GLC_API int glc_attention_bwd(glc_ctx* ctx, const float* q, const float* k, const float* v, const float* o,
                               const float* lse, const float* dO, float* dq, float* dk, float* dv, int B, int S, int H,
                               int Hkv, int hd, int round_dv);
+/* The same attention backward for callers that cannot allocate device memory
+ * during a call (no counterpart in the reference): programs whose device
+ * memory is wholly reserved by their own allocator or budget, and programs
+ * that must not let a call synchronise the device (glc_attention_bwd's
+ * workspace is cudaMalloc'ed on first use and regrown after a device sync).
+ * Its scratch is a fixed 4 MiB file-scope device array (every GPU that loads
+ * the library holds it until exit), so B*H*S may not exceed 1,048,576; larger
+ * calls fail with GLC_ERR_INVALID.  It calls no cudaMalloc, cudaFree or
+ * allocating library routine.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) and should come before any
+ * stream capture.  All calls share the array, which keeps the last call's
+ * contents (it is fully rewritten before use), so calls that overlap on the
+ * GPU — on different streams or contexts of one device — race. */
+GLC_API int glc_attention_bwd_noalloc(glc_ctx* ctx, const float* q, const float* k, const float* v, const float* o,
+                                      const float* lse, const float* dO, float* dq, float* dk, float* dv, int B,
+                                      int S, int H, int Hkv, int hd, int round_dv);
 /* SoftmaxCrossEntropyGrad (pkg/tensor/grad.go:210-280): loss (device float)
  * = mean over rows of -log32(p_target + 1e-10); write_grad=1 overwrites the
  * logits with the gradient (p - onehot) * scale. row_logp: [rows] scratch. */

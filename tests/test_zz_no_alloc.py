@@ -1,0 +1,50 @@
+"""glc_attention_bwd_noalloc: the attention backward for callers that cannot
+allocate device memory during a call (their memory is reserved by their own
+allocator, or a call must never synchronise the device, as growing the
+library's workspace does).  Its scratch is a fixed device array inside the
+library.  Checked through the C ABI against glc_attention_bwd on two calls in a
+row; this file is collected last so a failure here stops nothing else."""
+import numpy as np
+import pytest
+
+from gollama_b200.device import GlcError
+from tests.helpers import FP32_RTOL, rel_fro
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(ctx, B, S, H, Hkv, hd, seed):
+    T = B * S
+    r = np.random.default_rng(seed)
+    q = r.standard_normal((T, H * hd), dtype=np.float32)
+    k = r.standard_normal((T, Hkv * hd), dtype=np.float32)
+    v = r.standard_normal((T, Hkv * hd), dtype=np.float32)
+    dO = r.standard_normal((T, H * hd), dtype=np.float32)
+    bq, bk, bv, bdo = ctx.from_numpy(q), ctx.from_numpy(k), ctx.from_numpy(v), ctx.from_numpy(dO)
+    bo, blse = ctx.empty((T, H * hd)), ctx.empty((B, H, S))
+    ctx.call("glc_attention_fwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, B, S, H, Hkv, hd, 0)
+    outs = []
+    for name in ("glc_attention_bwd", "glc_attention_bwd_noalloc"):
+        dq, dk, dv = ctx.empty(q.shape), ctx.empty(k.shape), ctx.empty(v.shape)
+        ctx.call(name, bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, dq.ptr, dk.ptr, dv.ptr, B, S, H, Hkv, hd, 1)
+        ctx.sync()
+        outs.append((dq.numpy(), dk.numpy(), dv.numpy()))
+    return outs
+
+
+def test_noalloc_matches_allocating_entry_point_twice(ctx):
+    # two calls in a row with different shapes and data: the shared scratch
+    # keeps the first call's contents, which must not leak into the second
+    for seed, (B, S, H, Hkv, hd) in enumerate([(2, 256, 8, 4, 64), (1, 130, 4, 2, 32)]):
+        ref, got = _run(ctx, B, S, H, Hkv, hd, seed)
+        for a, b in zip(got, ref):
+            assert rel_fro(a, b) < FP32_RTOL
+
+
+def test_noalloc_rejects_sizes_beyond_its_scratch(ctx):
+    B, S, H, Hkv, hd = 1, 1 << 16, 32, 4, 64  # B*H*S = 2^21 rows > 2^20
+    with pytest.raises(GlcError) as e:
+        ctx.call("glc_attention_bwd_noalloc", None, None, None, None, None, None, None, None, None,
+                 B, S, H, Hkv, hd, 0)
+    assert e.value.code == -1
+    assert "exceeds the fixed scratch" in str(e.value)
