@@ -17,6 +17,8 @@
 // FMA contraction — and a TF32-rounded copy of p for the GEMMs.
 #include <cmath>
 
+#include <math_constants.h>
+
 #include "glc_internal.h"
 #include "sm100.cuh"
 
@@ -31,10 +33,12 @@ struct Seg {
 __global__ void sumsq_kernel(const float* __restrict__ g, const Seg* __restrict__ segs, double* __restrict__ partial) {
   const Seg sg = segs[blockIdx.y];
   double acc = 0.0;
-  const float* base = g + sg.start;
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < sg.len; i += int64_t(gridDim.x) * blockDim.x) {
-    const double v = static_cast<double>(base[i]);
-    acc = __dadd_rn(acc, __dmul_rn(v, v));
+  const float4* base = reinterpret_cast<const float4*>(g + sg.start);
+  const int64_t n4 = sg.len >> 2;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
+    const float4 v = base[i];
+    const double x = v.x, y = v.y, z = v.z, w = v.w;
+    acc = __dadd_rn(acc, __dadd_rn(__dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)), __dadd_rn(__dmul_rn(z, z), __dmul_rn(w, w))));
   }
   __shared__ double red[32];
 #pragma unroll
@@ -70,46 +74,77 @@ __global__ void norm_finish_kernel(const double* __restrict__ partial, int n, fl
 
 struct AdamArgs {
   float lr, b1, omb1, b2, omb2, wd;
-  double bc1, bc2, eps;
+  double bc1, bc2, rbc1, rbc2, eps;
 };
 
+// float32(mhat / (sqrt(vhat) + eps)) with mhat = m/bc1, vhat = v/bc2 in
+// float64 (optimizer.go:68-72).  Fast path: the two bias corrections as
+// multiplications by precomputed reciprocals, within a few float64 ulps of
+// the reference's quotient; its float32 rounding equals the reference's
+// unless the quotient lies within 32 ulps of a float32 rounding midpoint, in
+// which case the reference's exact division chain is evaluated instead.
+__device__ __forceinline__ float adam_update(float mi, float vi, const AdamArgs& a) {
+  const double mh = __dmul_rn(static_cast<double>(mi), a.rbc1);
+  const double vh = __dmul_rn(static_cast<double>(vi), a.rbc2);
+  const double q = __ddiv_rn(mh, __dadd_rn(__dsqrt_rn(vh), a.eps));
+  const float f = __double2float_rn(q);
+  const double fd = static_cast<double>(f);
+  const double mid_up = 0.5 * (fd + static_cast<double>(nextafterf(f, INFINITY)));
+  const double mid_dn = 0.5 * (fd + static_cast<double>(nextafterf(f, -INFINITY)));
+  const double tol = 32.0 * 1.1102230246251565e-16 * fabs(q);
+  if (fabs(q - mid_up) > tol && fabs(q - mid_dn) > tol) return f;
+  const double mhat = __ddiv_rn(static_cast<double>(mi), a.bc1);
+  const double vhat = __ddiv_rn(static_cast<double>(vi), a.bc2);
+  return __double2float_rn(__ddiv_rn(mhat, __dadd_rn(__dsqrt_rn(vhat), a.eps)));
+}
+
+__device__ __forceinline__ void adam_elem(float& p, float& g, float& m, float& v, float scale, bool scaled,
+                                          const AdamArgs& a) {
+  if (scaled) g = __fmul_rn(g, scale);
+  m = __fadd_rn(__fmul_rn(a.b1, m), __fmul_rn(a.omb1, g));
+  v = __fadd_rn(__fmul_rn(a.b2, v), __fmul_rn(__fmul_rn(a.omb2, g), g));
+  const float upd = adam_update(m, v, a);
+  p = __fsub_rn(p, __fmul_rn(a.lr, __fadd_rn(upd, __fmul_rn(a.wd, p))));
+}
+
+// Segments start and end on multiples of 4 floats (every parameter's size is
+// a multiple of the hidden size, itself a multiple of 4): float4 throughout.
 __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
                              float* __restrict__ shadow, const Seg* __restrict__ segs,
                              const float* __restrict__ clip_scale, AdamArgs a) {
   const Seg sg = segs[blockIdx.y];
   const float scale = clip_scale ? *clip_scale : 1.0f;
   const bool scaled = scale != 1.0f;
-  for (int64_t i = sg.start + blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < sg.start + sg.len;
-       i += int64_t(gridDim.x) * blockDim.x) {
-    float gi = g[i];
-    if (scaled) {
-      gi = __fmul_rn(gi, scale);
-      g[i] = gi;
-    }
-    const float mi = __fadd_rn(__fmul_rn(a.b1, m[i]), __fmul_rn(a.omb1, gi));
-    const float vi = __fadd_rn(__fmul_rn(a.b2, v[i]), __fmul_rn(__fmul_rn(a.omb2, gi), gi));
-    m[i] = mi;
-    v[i] = vi;
-    const double mhat = __ddiv_rn(static_cast<double>(mi), a.bc1);
-    const double vhat = __ddiv_rn(static_cast<double>(vi), a.bc2);
-    const float upd = __double2float_rn(__ddiv_rn(mhat, __dadd_rn(__dsqrt_rn(vhat), a.eps)));
-    const float pi = p[i];
-    const float np = __fsub_rn(pi, __fmul_rn(a.lr, __fadd_rn(upd, __fmul_rn(a.wd, pi))));
-    p[i] = np;
-    if (shadow) shadow[i] = round_tf32(np);
+  float4* p4 = reinterpret_cast<float4*>(p + sg.start);
+  float4* g4 = reinterpret_cast<float4*>(g + sg.start);
+  float4* m4 = reinterpret_cast<float4*>(m + sg.start);
+  float4* v4 = reinterpret_cast<float4*>(v + sg.start);
+  float4* s4 = shadow ? reinterpret_cast<float4*>(shadow + sg.start) : nullptr;
+  const int64_t n4 = sg.len >> 2;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
+    float4 P = p4[i], G = g4[i], M = m4[i], V = v4[i];
+    adam_elem(P.x, G.x, M.x, V.x, scale, scaled, a);
+    adam_elem(P.y, G.y, M.y, V.y, scale, scaled, a);
+    adam_elem(P.z, G.z, M.z, V.z, scale, scaled, a);
+    adam_elem(P.w, G.w, M.w, V.w, scale, scaled, a);
+    if (scaled) g4[i] = G;
+    m4[i] = M;
+    v4[i] = V;
+    p4[i] = P;
+    if (s4) s4[i] = make_float4(round_tf32(P.x), round_tf32(P.y), round_tf32(P.z), round_tf32(P.w));
   }
 }
 
 }  // namespace
 
-// segs: device array of {start, len} pairs (int64), nseg entries.
+// segs: device array of {start, len} pairs (int64), nseg entries; every start
+// and len a multiple of 4.
 int grad_norm(Context* ctx, const float* grads, const int64_t* segs, int nseg, float max_norm, double* norm_out,
               float* scale_out, double* scratch, int scratch_count, double elems, cudaStream_t s) {
   if (nseg <= 0 || !grads || !segs || !norm_out || !scale_out)
     return ctx->fail(GLC_ERR_INVALID, "grad_norm: bad arguments");
-  int bx = (2 * ctx->num_sms + nseg - 1) / nseg;
-  if (bx < 1) bx = 1;
-  if (bx > 64) bx = 64;
+  int bx = (8 * ctx->num_sms + nseg - 1) / nseg;
+  if (bx < 4) bx = 4;
   const int n = bx * nseg;
   double* partial = scratch;
   if (!partial) {
@@ -142,10 +177,11 @@ int adamw(Context* ctx, float* p, float* g, float* m, float* v, float* shadow, c
   a.wd = wd;
   a.bc1 = 1.0 - std::pow(static_cast<double>(beta1), static_cast<double>(step));
   a.bc2 = 1.0 - std::pow(static_cast<double>(beta2), static_cast<double>(step));
+  a.rbc1 = 1.0 / a.bc1;
+  a.rbc2 = 1.0 / a.bc2;
   a.eps = static_cast<double>(eps);
   int bx = (8 * ctx->num_sms + nseg - 1) / nseg;
-  if (bx < 1) bx = 1;
-  if (bx > 1024) bx = 1024;
+  if (bx < 4) bx = 4;
   // p, g, m, v read; p, m, v and the TF32 shadow written
   ProfScope prof(ctx, PROF_ADAMW, (shadow ? 32.0 : 28.0) * elems, s);
   adamw_kernel<<<dim3(bx, nseg), 256, 0, s>>>(p, g, m, v, shadow, reinterpret_cast<const Seg*>(segs), clip_scale, a);

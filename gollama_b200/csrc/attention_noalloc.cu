@@ -68,5 +68,7 @@ extern "C" int glc_attention_bwd_noalloc(glc_ctx* ctx, const float* q, const flo
   if (rc) return rc;
   // D is fully written by the first kernel of the backward before it is
   // read, so the previous call's contents need no clearing.
-  return glc::attention_bwd(c, q, k, v, o, lse, dO, dq, dk, dv, D, B, S, H, Hkv, hd, round_dv != 0, c->stream);
+  // No partial buffer: each CTA sums its KV head's query-head group itself.
+  return glc::attention_bwd(c, q, k, v, o, lse, dO, dq, dk, dv, D, nullptr, B, S, H, Hkv, hd, round_dv != 0,
+                            c->stream);
 }

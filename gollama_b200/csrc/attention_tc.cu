@@ -1,0 +1,850 @@
+// Causal attention forward and backward on the tcgen05 tensor cores (TF32
+// operands, fp32 accumulation in TMEM), flash-style: no S x S matrix in
+// global memory.
+//
+// Semantics follow forwardAttention (pkg/train/trainer.go:331-386): query t of
+// sequence b attends to keys j <= t of the same sequence, scores (q.k)*scale
+// with scale = float32(1/sqrt(hd)), softmax over them, weighted sum of v; heads
+// map to KV heads as in pkg/model/attention.go:118,149.  q/o rows hold H*hd
+// floats, k/v rows Hkv*hd; row t = b*S + s.  Inputs are expected TF32-rounded
+// (the producing kernels round them); P and dS are rounded when written.
+//
+// Every kernel: 192 threads — warp 0 issues TMA loads (one thread), warp 1
+// owns TMEM and issues tcgen05.mma (one thread), warps 2..5 do the softmax
+// arithmetic with one thread per TMEM lane (row).  All waits are bounded.
+//
+// forward   CTA = (128 queries, head).  S_j = Q K_j^T into one of two TMEM
+//           buffers (the next S overlaps this softmax); P_j goes to a K-major
+//           swizzled smem tile; O (TMEM) is rescaled when the row max grows;
+//           O += P_j V_j with V as an MN-major operand.
+// dK/dV     CTA = (128 keys, query head) or (128 keys, KV head) looping over
+//           the head group.  S^T = K Q^T, dP^T = V dO^T (64 queries per step),
+//           P^T = exp(S^T - lse), dS^T = P^T (dP^T - D) scale, dV += P^T dO,
+//           dK += dS^T Q.  Per-head partials are summed over the group by a
+//           separate deterministic kernel.
+// dQ        CTA = (128 queries, head): S = Q K^T, dP = dO V^T (64 keys per
+//           step), dS as above, dQ += dS K.
+#include <cfloat>
+#include <cmath>
+
+#include "glc_internal.h"
+#include "sm100.cuh"
+
+namespace glc {
+namespace {
+
+constexpr int NT = 192;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+
+struct Roles {
+  int warp, lane;
+  __device__ Roles() : warp(threadIdx.x >> 5), lane(threadIdx.x & 31) {}
+};
+
+// K-major tile of R rows x HD fp32 (HD/32 blocks of [R][128 B], 128B swizzle):
+// UMMA descriptor of k-step kk (8 elements of K per step).
+template <int R>
+__device__ __forceinline__ uint64_t kdesc(uint32_t base, int kk) {
+  return umma_sdesc(base + (kk >> 2) * (R * 128) + (kk & 3) * 32, 16, 1024, UMMA_LAYOUT_SW128);
+}
+// MN-major tile: chunks of 32 MN-elements x R K-rows ([R][128 B], 32-byte-atom
+// swizzle), chunk stride R*128 bytes; k-step kk advances 8 K-rows.
+template <int R>
+__device__ __forceinline__ uint64_t mdesc(uint32_t base, int kk) {
+  return umma_sdesc(base + kk * 1024, R * 128, 512, UMMA_LAYOUT_SW128_BASE32B);
+}
+
+// Loads R rows x HD columns (starting at column col0, row row0) as HD/32
+// boxes of {32, R}; the tensor map fixes the swizzle (K- or MN-major).
+template <int HD, int R>
+__device__ __forceinline__ void tma_tile(uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, int col0, int row0) {
+#pragma unroll
+  for (int c = 0; c < HD / 32; ++c) tma_load_2d(dst + c * R * 128, tm, bar, col0 + 32 * c, row0);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+// Bounded wait used by the math warps: every lane polls and the outcome is
+// made warp-uniform, so a warp never reaches a warp-collective tcgen05.ld/st
+// with some lanes gone.
+#define WAIT_OR_BREAK(bar, parity, code)                                                 \
+  if (!__all_sync(0xffffffffu, mbar_wait((bar), (parity), abort_flag, err, (code)))) {   \
+    ok = false;                                                                           \
+    break;                                                                                \
+  }
+
+// ===================================================================== forward
+template <int HD>
+struct FwdLayout {
+  static constexpr int Q = 128 * HD * 4, K = 128 * HD * 4, V = 128 * HD * 4, P = 128 * 128 * 4;
+  static constexpr int OFF_K = Q, OFF_V = OFF_K + 2 * K, OFF_P = OFF_V + 2 * V, OFF_BAR = OFF_P + P;
+  static constexpr int BYTES = OFF_BAR + 256 + 1024;
+  static constexpr int TMEM_COLS = 512;  // S0 [0,128) S1 [128,256) O [256, 256+HD)
+};
+
+template <int HD>
+__global__ void __launch_bounds__(NT, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, float* __restrict__ out, float* __restrict__ lse,
+                       int S, int H, int Hkv, int n_qt, float scale_log2, int round_out, int* err) {
+  using L = FwdLayout<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = bars + 3, *v_full = bars + 5, *v_empty = bars + 7,
+           *s_full = bars + 9, *s_free = bars + 11, *p_full = bars + 13, *p_empty = bars + 14, *drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const Roles ro;
+  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // longest rows first
+  const int h = blockIdx.y, b = blockIdx.z, kh = h / (H / Hkv);
+  const int q0 = qt * 128, row_base = b * S;
+  const int n_kv = qt + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(p_empty, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (ro.warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sQ = smem_u32(sm), sK = sQ + L::OFF_K, sV = sQ + L::OFF_V, sP = sQ + L::OFF_P;
+
+  if (ro.warp == 0) {
+    if (ro.lane == 0) {
+      bool ok = true;
+      int armed_k[2] = {-1, -1}, armed_v[2] = {-1, -1};
+      mbar_arrive_expect_tx(q_full, L::Q);
+      tma_tile<HD, 128>(sm, &tmQ, q_full, h * HD, row_base + q0);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx(&k_full[st], L::K);
+        tma_tile<HD, 128>(sm + L::OFF_K + st * L::K, &tmK, &k_full[st], kh * HD, row_base + j * 128);
+        armed_k[st] = static_cast<int>(ph);
+        if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx(&v_full[st], L::V);
+        tma_tile<HD, 128>(sm + L::OFF_V + st * L::V, &tmV, &v_full[st], kh * HD, row_base + j * 128);
+        armed_v[st] = static_cast<int>(ph);
+      }
+      if (!ok) {
+        mbar_drain(q_full, 0, err);
+        for (int st = 0; st < 2; ++st) {
+          if (armed_k[st] >= 0) mbar_drain(&k_full[st], static_cast<uint32_t>(armed_k[st]), err);
+          if (armed_v[st] >= 0) mbar_drain(&v_full[st], static_cast<uint32_t>(armed_v[st]), err);
+        }
+      }
+    }
+  } else if (ro.warp == 1) {
+    if (ro.lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_tf32(128, 128, false, false);
+      constexpr uint32_t idesc_o = umma_idesc_tf32(128, HD, false, true);
+      bool ok = mbar_wait(q_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
+      bool issued = false;
+      auto issue_s = [&](int j) -> bool {
+        const int sb = j & 1;
+        if (!mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) return false;
+        if (!mbar_wait(&k_full[sb], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk)
+          umma_tf32(tmem + sb * 128, kdesc<128>(sQ, kk), kdesc<128>(sK + sb * L::K, kk), idesc_s, kk > 0 ? 1u : 0u);
+        issued = true;
+        umma_commit(&k_empty[sb]);
+        umma_commit(&s_full[sb]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (j + 1 < n_kv && !issue_s(j + 1)) { ok = false; break; }
+        if (!mbar_wait(p_full, j & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk)
+          umma_tf32(tmem + 256, kdesc<128>(sP, kk), mdesc<128>(sV + (j & 1) * L::V, kk), idesc_o,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&v_empty[j & 1]);
+        umma_commit(p_empty);
+      }
+      if (!ok && issued) {
+        umma_commit(drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0))
+          if (globaltimer_ns() - t0 > 1000000000ull) { atomicCAS(err, 0, GLC_DEV_TIMEOUT_DRAIN); break; }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax
+    const int q = ro.warp & 3;
+    const int r = q * 32 + ro.lane;
+    const int row_abs = q0 + r;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int sb = j & 1;
+      WAIT_OR_BREAK(&s_full[sb], (j >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      tc_fence_after();
+      const int k0 = j * 128;
+      const bool diag = (j == qt);
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_addr + sb * 128 + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int key = k0 + c * 32 + e;
+          const bool valid = key < S && (!diag || key <= row_abs);
+          if (valid) mx = fmaxf(mx, __uint_as_float(v[e]) * scale_log2);
+        }
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = exp2f(m - m_new);
+      if (j > 0) {
+        WAIT_OR_BREAK(p_empty, (j - 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(lane_addr + 256 + c * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+            tmem_st_32x32b_x32(lane_addr + 256 + c * 32, v);
+          }
+          tmem_st_wait();
+        }
+      }
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_addr + sb * 128 + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          float pv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = k0 + c * 32 + g * 4 + e;
+            const bool valid = key < S && (!diag || key <= row_abs);
+            const float p = valid ? round_tf32(exp2f(__uint_as_float(v[g * 4 + e]) * scale_log2 - m_new)) : 0.f;
+            pv[e] = p;
+            sum += p;
+          }
+          st_shared_v4(sP + kmajor_sw128_offset(r, c * 32 + g * 4, 128 * 128), pv[0], pv[1], pv[2], pv[3]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[sb]);
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);
+      l = l * alpha + sum;
+      m = m_new;
+    }
+    if (__all_sync(0xffffffffu, ok && mbar_wait(p_empty, (n_kv - 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      float* orow = out + (static_cast<size_t>(row_base) + row_abs) * (static_cast<size_t>(H) * HD) + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_addr + 256 + c * 32, v);
+        tmem_ld_wait();
+        if (row_abs < S) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            float4 o4;
+            o4.x = __uint_as_float(v[4 * g + 0]) * inv;
+            o4.y = __uint_as_float(v[4 * g + 1]) * inv;
+            o4.z = __uint_as_float(v[4 * g + 2]) * inv;
+            o4.w = __uint_as_float(v[4 * g + 3]) * inv;
+            if (round_out) o4 = make_float4(round_tf32(o4.x), round_tf32(o4.y), round_tf32(o4.z), round_tf32(o4.w));
+            reinterpret_cast<float4*>(orow + c * 32)[g] = o4;
+          }
+        }
+      }
+      if (row_abs < S) lse[(static_cast<size_t>(b) * H + h) * S + row_abs] = (m + log2f(l)) * LN2;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (ro.warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
+// ===================================================================== dK / dV
+template <int HD>
+struct DkdvLayout {
+  static constexpr int K = 128 * HD * 4, V = 128 * HD * 4;
+  static constexpr int QT = 64 * HD * 4;  // one 64-query operand tile
+  static constexpr int PT = 128 * 64 * 4; // [128 keys][64 queries]
+  static constexpr int OFF_V = K, OFF_QK = OFF_V + V, OFF_QM = OFF_QK + QT, OFF_OK = OFF_QM + QT,
+                       OFF_OM = OFF_OK + QT, OFF_P = OFF_OM + QT, OFF_DS = OFF_P + PT, OFF_BAR = OFF_DS + PT;
+  static constexpr int BYTES = OFF_BAR + 256 + 1024;
+  static constexpr int TMEM_COLS = 256;  // S^T [0,64) dP^T [64,128) dV [128,128+HD) dK [128+HD, 128+2HD)
+};
+
+template <int HD, bool GROUP_LOOP>
+__global__ void __launch_bounds__(NT, 1)
+    attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQk, const __grid_constant__ CUtensorMap tmQm,
+                            const __grid_constant__ CUtensorMap tmOk, const __grid_constant__ CUtensorMap tmOm,
+                            const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                            const float* __restrict__ lse, const float* __restrict__ Dv, float* __restrict__ dk_out,
+                            float* __restrict__ dv_out, int out_heads, int S, int H, int Hkv, float scale,
+                            float scale_log2, int round_dv, int* err) {
+  using L = DkdvLayout<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint64_t *kv_full = bars, *qo_full = bars + 1, *qo_empty = bars + 2, *s_full = bars + 3, *s_free = bars + 4,
+           *ds_full = bars + 5, *ds_empty = bars + 6, *acc_done = bars + 7, *drain = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const Roles ro;
+  const int G = H / Hkv;
+  const int kt = blockIdx.x, b = blockIdx.z;
+  const int kh = GROUP_LOOP ? static_cast<int>(blockIdx.y) : static_cast<int>(blockIdx.y) / G;
+  const int h_first = GROUP_LOOP ? kh * G : static_cast<int>(blockIdx.y);
+  const int n_heads = GROUP_LOOP ? G : 1;
+  const int k0 = kt * 128, row_base = b * S;
+  const int qi0 = k0 / 64, n_q64 = (S + 63) / 64;
+  const int nq = n_q64 - qi0;
+  const int n_it = n_heads * nq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qo_full, 1);
+    mbar_init(qo_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 128);
+    mbar_init(ds_full, 128);
+    mbar_init(ds_empty, 1);
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (ro.warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t s0 = smem_u32(sm);
+
+  if (ro.warp == 0) {
+    if (ro.lane == 0) {
+      mbar_arrive_expect_tx(kv_full, L::K + L::V);
+      tma_tile<HD, 128>(sm, &tmK, kv_full, kh * HD, row_base + k0);
+      tma_tile<HD, 128>(sm + L::OFF_V, &tmV, kv_full, kh * HD, row_base + k0);
+      int armed = -1;
+      bool ok = true;
+      for (int it = 0; it < n_it; ++it) {
+        const int hq = h_first + it / nq, qr = row_base + (qi0 + it % nq) * 64;
+        if (!mbar_wait(qo_empty, (it & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx(qo_full, 4 * L::QT);
+        tma_tile<HD, 64>(sm + L::OFF_QK, &tmQk, qo_full, hq * HD, qr);
+        tma_tile<HD, 64>(sm + L::OFF_QM, &tmQm, qo_full, hq * HD, qr);
+        tma_tile<HD, 64>(sm + L::OFF_OK, &tmOk, qo_full, hq * HD, qr);
+        tma_tile<HD, 64>(sm + L::OFF_OM, &tmOm, qo_full, hq * HD, qr);
+        armed = it & 1;
+      }
+      if (!ok) {
+        mbar_drain(kv_full, 0, err);
+        if (armed >= 0) mbar_drain(qo_full, static_cast<uint32_t>(armed), err);
+      }
+    }
+  } else if (ro.warp == 1) {
+    if (ro.lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_tf32(128, 64, false, false);
+      constexpr uint32_t idesc_a = umma_idesc_tf32(128, HD, false, true);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
+      bool issued = false;
+      for (int it = 0; ok && it < n_it; ++it) {
+        if (!mbar_wait(qo_full, it & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        if (!mbar_wait(s_free, (it & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk) {
+          umma_tf32(tmem + 0, kdesc<128>(s0, kk), kdesc<64>(s0 + L::OFF_QK, kk), idesc_s, kk > 0 ? 1u : 0u);
+          umma_tf32(tmem + 64, kdesc<128>(s0 + L::OFF_V, kk), kdesc<64>(s0 + L::OFF_OK, kk), idesc_s, kk > 0 ? 1u : 0u);
+        }
+        issued = true;
+        umma_commit(s_full);
+        if (!mbar_wait(ds_full, it & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+          umma_tf32(tmem + 128, kdesc<128>(s0 + L::OFF_P, kk), mdesc<64>(s0 + L::OFF_OM, kk), idesc_a, acc);
+          umma_tf32(tmem + 128 + HD, kdesc<128>(s0 + L::OFF_DS, kk), mdesc<64>(s0 + L::OFF_QM, kk), idesc_a, acc);
+        }
+        umma_commit(qo_empty);
+        umma_commit(ds_empty);
+      }
+      if (ok) umma_commit(acc_done);
+      if (!ok && issued) {
+        umma_commit(drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0))
+          if (globaltimer_ns() - t0 > 1000000000ull) { atomicCAS(err, 0, GLC_DEV_TIMEOUT_DRAIN); break; }
+      }
+    }
+  } else {
+    const int q = ro.warp & 3;
+    const int c = q * 32 + ro.lane;  // key row within the tile
+    const int key = k0 + c;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int hq = h_first + it / nq, qbase = (qi0 + it % nq) * 64;
+      WAIT_OR_BREAK(s_full, it & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      WAIT_OR_BREAK(ds_empty, (it & 1) ^ 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      tc_fence_after();
+      const float* lse_row = lse + (static_cast<size_t>(b) * H + hq) * S;
+      const float* d_row = Dv + (static_cast<size_t>(b) * H + hq) * S;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sv[32], dpv[32];
+        tmem_ld_32x32b_x32(lane_addr + half * 32, sv);
+        tmem_ld_32x32b_x32(lane_addr + 64 + half * 32, dpv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          float pv[4], dsv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int qq = half * 32 + g * 4 + e, qa = qbase + qq;
+            const bool valid = qa < S && key < S && key <= qa;
+            float p = 0.f, ds = 0.f;
+            if (valid) {
+              p = exp2f(__uint_as_float(sv[g * 4 + e]) * scale_log2 - lse_row[qa] * LOG2E);
+              ds = p * (__uint_as_float(dpv[g * 4 + e]) - d_row[qa]) * scale;
+            }
+            pv[e] = round_tf32(p);
+            dsv[e] = round_tf32(ds);
+          }
+          const uint32_t off = kmajor_sw128_offset(c, half * 32 + g * 4, 128 * 128);
+          st_shared_v4(s0 + L::OFF_P + off, pv[0], pv[1], pv[2], pv[3]);
+          st_shared_v4(s0 + L::OFF_DS + off, dsv[0], dsv[1], dsv[2], dsv[3]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      fence_proxy_async_smem();
+      mbar_arrive(ds_full);
+    }
+    if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
+      tc_fence_after();
+      // out_heads = Hkv: final dk/dv; out_heads = H: per-query-head partials
+      const int oh = (out_heads == Hkv) ? kh : h_first;
+      const size_t row = (static_cast<size_t>(row_base) + key) * (static_cast<size_t>(out_heads) * HD) + oh * HD;
+#pragma unroll 1
+      for (int part = 0; part < 2; ++part) {  // 0: dV, 1: dK
+#pragma unroll 1
+        for (int cc = 0; cc < HD / 32; ++cc) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(lane_addr + 128 + part * HD + cc * 32, v);
+          tmem_ld_wait();
+          if (key < S) {
+            float* dst = (part == 0 ? dv_out : dk_out) + row + cc * 32;
+            const bool rnd = part == 0 && round_dv;
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              float4 o4 = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
+                                      __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
+              if (rnd) o4 = make_float4(round_tf32(o4.x), round_tf32(o4.y), round_tf32(o4.z), round_tf32(o4.w));
+              reinterpret_cast<float4*>(dst)[g] = o4;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (ro.warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
+// dk[t][kh] = sum over the G query heads of the group of partial[t][h]
+// (heads ascending: deterministic); dv the same, optionally TF32-rounded.
+__global__ void group_sum_kernel(const float* __restrict__ pk, const float* __restrict__ pv, float* __restrict__ dk,
+                                 float* __restrict__ dv, int T, int H, int Hkv, int hd, int round_dv) {
+  const int G = H / Hkv, n4 = hd / 4;
+  const size_t total = static_cast<size_t>(T) * Hkv * n4;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+    const int d4 = static_cast<int>(i % n4);
+    const size_t th = i / n4;
+    const int kh = static_cast<int>(th % Hkv);
+    const size_t t = th / Hkv;
+    float4 sk = make_float4(0.f, 0.f, 0.f, 0.f), sv = sk;
+    for (int g = 0; g < G; ++g) {
+      const size_t src = (t * H + kh * G + g) * hd / 4 + d4;
+      const float4 a = reinterpret_cast<const float4*>(pk)[src];
+      const float4 c = reinterpret_cast<const float4*>(pv)[src];
+      sk.x += a.x; sk.y += a.y; sk.z += a.z; sk.w += a.w;
+      sv.x += c.x; sv.y += c.y; sv.z += c.z; sv.w += c.w;
+    }
+    if (round_dv) sv = make_float4(round_tf32(sv.x), round_tf32(sv.y), round_tf32(sv.z), round_tf32(sv.w));
+    const size_t dst = (t * Hkv + kh) * hd / 4 + d4;
+    reinterpret_cast<float4*>(dk)[dst] = sk;
+    reinterpret_cast<float4*>(dv)[dst] = sv;
+  }
+}
+
+// ===================================================================== dQ
+template <int HD>
+struct DqLayout {
+  static constexpr int Q = 128 * HD * 4, O = 128 * HD * 4;
+  static constexpr int KT = 64 * HD * 4;              // one 64-key operand tile
+  static constexpr int STAGE = 3 * KT;                // K (K-major), K (MN-major), V (K-major)
+  static constexpr int DS = 128 * 64 * 4;
+  static constexpr int OFF_O = Q, OFF_KV = OFF_O + O, OFF_DS = OFF_KV + 2 * STAGE, OFF_BAR = OFF_DS + DS;
+  static constexpr int BYTES = OFF_BAR + 256 + 1024;
+  static constexpr int TMEM_COLS = 256;  // S [0,64) dP [64,128) dQ [128,128+HD)
+};
+
+template <int HD>
+__global__ void __launch_bounds__(NT, 1)
+    attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmO,
+                          const __grid_constant__ CUtensorMap tmKk, const __grid_constant__ CUtensorMap tmKm,
+                          const __grid_constant__ CUtensorMap tmVk, const float* __restrict__ lse,
+                          const float* __restrict__ Dv, float* __restrict__ dq, int S, int H, int Hkv, int n_qt,
+                          float scale, float scale_log2, int* err) {
+  using L = DqLayout<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint64_t *qo_full = bars, *kv_full = bars + 1, *kv_empty = bars + 3, *s_full = bars + 5, *s_free = bars + 6,
+           *ds_full = bars + 7, *ds_empty = bars + 8, *acc_done = bars + 9, *drain = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const Roles ro;
+  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);
+  const int h = blockIdx.y, b = blockIdx.z, kh = h / (H / Hkv);
+  const int q0 = qt * 128, row_base = b * S;
+  const int n_k64 = (S + 63) / 64;
+  const int nk = min(n_k64, (q0 + 128) / 64);
+
+  if (threadIdx.x == 0) {
+    mbar_init(qo_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 128);
+    mbar_init(ds_full, 128);
+    mbar_init(ds_empty, 1);
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (ro.warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t s0 = smem_u32(sm);
+
+  if (ro.warp == 0) {
+    if (ro.lane == 0) {
+      mbar_arrive_expect_tx(qo_full, L::Q + L::O);
+      tma_tile<HD, 128>(sm, &tmQ, qo_full, h * HD, row_base + q0);
+      tma_tile<HD, 128>(sm + L::OFF_O, &tmO, qo_full, h * HD, row_base + q0);
+      int armed[2] = {-1, -1};
+      bool ok = true;
+      for (int j = 0; j < nk; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx(&kv_full[st], L::STAGE);
+        uint8_t* base = sm + L::OFF_KV + st * L::STAGE;
+        tma_tile<HD, 64>(base, &tmKk, &kv_full[st], kh * HD, row_base + j * 64);
+        tma_tile<HD, 64>(base + L::KT, &tmKm, &kv_full[st], kh * HD, row_base + j * 64);
+        tma_tile<HD, 64>(base + 2 * L::KT, &tmVk, &kv_full[st], kh * HD, row_base + j * 64);
+        armed[st] = (j >> 1) & 1;
+      }
+      if (!ok) {
+        mbar_drain(qo_full, 0, err);
+        for (int st = 0; st < 2; ++st)
+          if (armed[st] >= 0) mbar_drain(&kv_full[st], static_cast<uint32_t>(armed[st]), err);
+      }
+    }
+  } else if (ro.warp == 1) {
+    if (ro.lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_tf32(128, 64, false, false);
+      constexpr uint32_t idesc_q = umma_idesc_tf32(128, HD, false, true);
+      bool ok = mbar_wait(qo_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
+      bool issued = false;
+      for (int j = 0; ok && j < nk; ++j) {
+        const int st = j & 1;
+        const uint32_t base = s0 + L::OFF_KV + st * L::STAGE;
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        if (!mbar_wait(s_free, (j & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk) {
+          umma_tf32(tmem + 0, kdesc<128>(s0, kk), kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
+          umma_tf32(tmem + 64, kdesc<128>(s0 + L::OFF_O, kk), kdesc<64>(base + 2 * L::KT, kk), idesc_s, kk > 0 ? 1u : 0u);
+        }
+        issued = true;
+        umma_commit(s_full);
+        if (!mbar_wait(ds_full, j & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_tf32(tmem + 128, kdesc<128>(s0 + L::OFF_DS, kk), mdesc<64>(base + L::KT, kk), idesc_q,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(ds_empty);
+        umma_commit(&kv_empty[st]);
+      }
+      if (ok) umma_commit(acc_done);
+      if (!ok && issued) {
+        umma_commit(drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0))
+          if (globaltimer_ns() - t0 > 1000000000ull) { atomicCAS(err, 0, GLC_DEV_TIMEOUT_DRAIN); break; }
+      }
+    }
+  } else {
+    const int q = ro.warp & 3;
+    const int r = q * 32 + ro.lane;
+    const int qa = q0 + r;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const size_t lrow = (static_cast<size_t>(b) * H + h) * S + (qa < S ? qa : 0);
+    const float lse2 = lse[lrow] * LOG2E, Dq = Dv[lrow];
+    bool ok = true;
+    for (int j = 0; j < nk; ++j) {
+      WAIT_OR_BREAK(s_full, j & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      WAIT_OR_BREAK(ds_empty, (j & 1) ^ 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      tc_fence_after();
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sv[32], dpv[32];
+        tmem_ld_32x32b_x32(lane_addr + half * 32, sv);
+        tmem_ld_32x32b_x32(lane_addr + 64 + half * 32, dpv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          float dsv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = j * 64 + half * 32 + g * 4 + e;
+            const bool valid = qa < S && key < S && key <= qa;
+            float ds = 0.f;
+            if (valid) {
+              const float p = exp2f(__uint_as_float(sv[g * 4 + e]) * scale_log2 - lse2);
+              ds = p * (__uint_as_float(dpv[g * 4 + e]) - Dq) * scale;
+            }
+            dsv[e] = round_tf32(ds);
+          }
+          st_shared_v4(s0 + L::OFF_DS + kmajor_sw128_offset(r, half * 32 + g * 4, 128 * 128), dsv[0], dsv[1], dsv[2],
+                       dsv[3]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      fence_proxy_async_smem();
+      mbar_arrive(ds_full);
+    }
+    if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
+      tc_fence_after();
+      float* drow = dq + (static_cast<size_t>(row_base) + qa) * (static_cast<size_t>(H) * HD) + h * HD;
+#pragma unroll 1
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_addr + 128 + cc * 32, v);
+        tmem_ld_wait();
+        if (qa < S) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            reinterpret_cast<float4*>(drow + cc * 32)[g] =
+                make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]), __uint_as_float(v[4 * g + 2]),
+                            __uint_as_float(v[4 * g + 3]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (ro.warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
+// D[b,h,s] = sum_d dO * O
+__global__ void attn_bwd_prep_tc_kernel(const float* __restrict__ o, const float* __restrict__ dO,
+                                        float* __restrict__ D, int T, int S, int H, int hd) {
+  const int lane = threadIdx.x & 31;
+  const int nrow = T * H;
+  for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < nrow; row += gridDim.x * (blockDim.x >> 5)) {
+    const int t = row / H, h = row % H;
+    const float* op = o + (static_cast<size_t>(t) * H + h) * hd;
+    const float* dp = dO + (static_cast<size_t>(t) * H + h) * hd;
+    float s = 0.f;
+    for (int d = lane; d < hd; d += 32) s += op[d] * dp[d];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) D[(static_cast<size_t>(t / S) * H + h) * S + (t % S)] = s;
+  }
+}
+
+// ---------------------------------------------------------------- host side
+int encode(Context* ctx, CUtensorMap* tm, const float* ptr, int cols, int rows, int box_rows, bool mn) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
+  cuuint32_t box[2] = {32, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  if (ctx->encode_tiled(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
+                        mn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B) != 0)
+    return ctx->fail(GLC_ERR_INVALID, "attention: cuTensorMapEncodeTiled failed");
+  return 0;
+}
+
+template <typename K>
+int set_smem(Context* ctx, K kern, int bytes, bool* done) {
+  if (done[ctx->device & 7]) return 0;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return ctx->fail_cuda(e, "attention: cudaFuncSetAttribute");
+  done[ctx->device & 7] = true;
+  return 0;
+}
+
+int check(Context* ctx, const float* q, const float* k, const float* v, int B, int S, int H, int Hkv, int hd) {
+  if (B <= 0 || S <= 0 || H <= 0 || Hkv <= 0 || H % Hkv) return ctx->fail(GLC_ERR_INVALID, "attention: bad B/S/H/Hkv");
+  if (hd != 32 && hd != 64) return ctx->fail(GLC_ERR_UNSUPPORTED, "attention: head_dim must be 32 or 64");
+  if (!q || !k || !v || ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15))
+    return ctx->fail(GLC_ERR_INVALID, "attention: null or misaligned pointer");
+  return 0;
+}
+
+template <int HD>
+int fwd_impl(Context* ctx, const float* q, const float* k, const float* v, float* o, float* lse, int B, int S, int H,
+             int Hkv, bool round_out, cudaStream_t s) {
+  using L = FwdLayout<HD>;
+  static bool done[8] = {false};
+  int rc = set_smem(ctx, attn_fwd_tc_kernel<HD>, L::BYTES, done);
+  if (rc) return rc;
+  const int T = B * S;
+  CUtensorMap tq, tk, tv;
+  if ((rc = encode(ctx, &tq, q, H * HD, T, 128, false)) || (rc = encode(ctx, &tk, k, Hkv * HD, T, 128, false)) ||
+      (rc = encode(ctx, &tv, v, Hkv * HD, T, 128, true)))
+    return rc;
+  const int n_qt = (S + 127) / 128;
+  const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
+  const double causal = 0.5 * static_cast<double>(S) * (S + 1);
+  ProfScope prof(ctx, PROF_ATTN_FWD, 2.0 * 2.0 * B * H * causal * HD, s);
+  attn_fwd_tc_kernel<HD><<<dim3(n_qt, H, B), NT, L::BYTES, s>>>(tq, tk, tv, o, lse, S, H, Hkv, n_qt, scale * LOG2E,
+                                                                   round_out ? 1 : 0, ctx->d_err);
+  GLC_LAUNCH_CHECK(ctx, "attention_fwd (tcgen05)");
+  return 0;
+}
+
+template <int HD>
+int bwd_impl(Context* ctx, const float* q, const float* k, const float* v, const float* o, const float* lse,
+             const float* dO, float* dq, float* dk, float* dv, float* D, float* partial, int B, int S, int H, int Hkv,
+             bool round_dv, cudaStream_t s) {
+  static bool done_g[8] = {false}, done_p[8] = {false}, done_q[8] = {false};
+  int rc = set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD, true>, DkdvLayout<HD>::BYTES, done_g);
+  if (!rc) rc = set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD, false>, DkdvLayout<HD>::BYTES, done_p);
+  if (!rc) rc = set_smem(ctx, attn_bwd_dq_tc_kernel<HD>, DqLayout<HD>::BYTES, done_q);
+  if (rc) return rc;
+  const int T = B * S, G = H / Hkv;
+  CUtensorMap tQk64, tQm64, tOk64, tOm64, tK128, tV128, tQ128, tO128, tKk64, tKm64, tVk64;
+  if ((rc = encode(ctx, &tQk64, q, H * HD, T, 64, false)) || (rc = encode(ctx, &tQm64, q, H * HD, T, 64, true)) ||
+      (rc = encode(ctx, &tOk64, dO, H * HD, T, 64, false)) || (rc = encode(ctx, &tOm64, dO, H * HD, T, 64, true)) ||
+      (rc = encode(ctx, &tK128, k, Hkv * HD, T, 128, false)) || (rc = encode(ctx, &tV128, v, Hkv * HD, T, 128, false)) ||
+      (rc = encode(ctx, &tQ128, q, H * HD, T, 128, false)) || (rc = encode(ctx, &tO128, dO, H * HD, T, 128, false)) ||
+      (rc = encode(ctx, &tKk64, k, Hkv * HD, T, 64, false)) || (rc = encode(ctx, &tKm64, k, Hkv * HD, T, 64, true)) ||
+      (rc = encode(ctx, &tVk64, v, Hkv * HD, T, 64, false)))
+    return rc;
+  const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
+  const double causal = 0.5 * static_cast<double>(S) * (S + 1);
+  ProfScope prof(ctx, PROF_ATTN_BWD, 4.0 * 2.0 * B * H * causal * HD, s);
+  attn_bwd_prep_tc_kernel<<<grid_for(static_cast<size_t>(T) * H, 8, ctx->num_sms, 16), 256, 0, s>>>(o, dO, D, T, S, H, HD);
+  GLC_LAUNCH_CHECK(ctx, "attention_bwd prep");
+  const int n_kt = (S + 127) / 128;
+  if (G == 1 || partial == nullptr) {
+    // one CTA per (key tile, KV head), looping over the query heads of its group
+    attn_bwd_dkdv_tc_kernel<HD, true><<<dim3(n_kt, Hkv, B), NT, DkdvLayout<HD>::BYTES, s>>>(
+        tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, dk, dv, Hkv, S, H, Hkv, scale, scale * LOG2E,
+        round_dv ? 1 : 0, ctx->d_err);
+    GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
+  } else {
+    // one CTA per (key tile, query head); partials [T, H*hd] for dK and dV
+    float* pk = partial;
+    float* pv = partial + static_cast<size_t>(T) * H * HD;
+    attn_bwd_dkdv_tc_kernel<HD, false><<<dim3(n_kt, H, B), NT, DkdvLayout<HD>::BYTES, s>>>(
+        tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, pk, pv, H, S, H, Hkv, scale, scale * LOG2E, 0, ctx->d_err);
+    GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
+    group_sum_kernel<<<grid_for(static_cast<size_t>(T) * Hkv * HD / 4, 256, ctx->num_sms), 256, 0, s>>>(
+        pk, pv, dk, dv, T, H, Hkv, HD, round_dv ? 1 : 0);
+    GLC_LAUNCH_CHECK(ctx, "attention_bwd group sum");
+  }
+  const int n_qt = (S + 127) / 128;
+  attn_bwd_dq_tc_kernel<HD><<<dim3(n_qt, H, B), NT, DqLayout<HD>::BYTES, s>>>(
+      tQ128, tO128, tKk64, tKm64, tVk64, lse, D, dq, S, H, Hkv, n_qt, scale, scale * LOG2E, ctx->d_err);
+  GLC_LAUNCH_CHECK(ctx, "attention_bwd dq (tcgen05)");
+  return 0;
+}
+
+}  // namespace
+
+size_t attention_bwd_partial_floats(int B, int S, int H, int Hkv, int hd) {
+  if (H == Hkv) return 0;
+  return 2 * static_cast<size_t>(B) * S * H * hd;
+}
+
+int attention_fwd(Context* ctx, const float* q, const float* k, const float* v, float* o, float* lse, int B, int S,
+                  int H, int Hkv, int hd, bool round_out, cudaStream_t s) {
+  int rc = check(ctx, q, k, v, B, S, H, Hkv, hd);
+  if (rc) return rc;
+  if (!o || !lse || (reinterpret_cast<uintptr_t>(o) & 15)) return ctx->fail(GLC_ERR_INVALID, "attention_fwd: bad output");
+  return hd == 64 ? fwd_impl<64>(ctx, q, k, v, o, lse, B, S, H, Hkv, round_out, s)
+                  : fwd_impl<32>(ctx, q, k, v, o, lse, B, S, H, Hkv, round_out, s);
+}
+
+int attention_bwd(Context* ctx, const float* q, const float* k, const float* v, const float* o, const float* lse,
+                  const float* dO, float* dq, float* dk, float* dv, float* D, float* partial, int B, int S, int H,
+                  int Hkv, int hd, bool round_dv, cudaStream_t s) {
+  int rc = check(ctx, q, k, v, B, S, H, Hkv, hd);
+  if (rc) return rc;
+  if (!o || !lse || !dO || !dq || !dk || !dv || !D ||
+      ((reinterpret_cast<uintptr_t>(dO) | reinterpret_cast<uintptr_t>(dq) | reinterpret_cast<uintptr_t>(dk) |
+        reinterpret_cast<uintptr_t>(dv)) & 15))
+    return ctx->fail(GLC_ERR_INVALID, "attention_bwd: null or misaligned pointer");
+  return hd == 64 ? bwd_impl<64>(ctx, q, k, v, o, lse, dO, dq, dk, dv, D, partial, B, S, H, Hkv, round_dv, s)
+                  : bwd_impl<32>(ctx, q, k, v, o, lse, dO, dq, dk, dv, D, partial, B, S, H, Hkv, round_dv, s);
+}
+
+}  // namespace glc

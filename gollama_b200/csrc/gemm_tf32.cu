@@ -226,7 +226,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t use = static_cast<uint32_t>(local >> 1);
-      if (!mbar_wait(&tfull_bar[buf], use & 1, abort_flag, args.err, GLC_DEV_TIMEOUT_EPILOGUE)) break;
+      // warp-uniform outcome: the TMEM loads below are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull_bar[buf], use & 1, abort_flag, args.err, GLC_DEV_TIMEOUT_EPILOGUE)))
+        break;
       tc_fence_after();
       const int m0 = (tile % args.m_tiles) * BM;
       const int n0 = (tile / args.m_tiles) * BN;

@@ -147,10 +147,13 @@ int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, in
                float* loss, bool write_grad, bool round_out, cudaStream_t s);
 int attention_fwd(Context* ctx, const float* q, const float* k, const float* v, float* o, float* lse, int B, int S,
                   int H, int Hkv, int hd, bool round_out, cudaStream_t s);
+// partial: 2*B*S*H*hd floats of scratch for per-query-head dK/dV partials
+// (attention_bwd_partial_floats); nullptr makes each CTA loop over its KV
+// head's query-head group instead (no scratch beyond D).
 int attention_bwd(Context* ctx, const float* q, const float* k, const float* v, const float* o, const float* lse,
-                  const float* dO, float* dq, float* dk, float* dv, float* D, int B, int S, int H, int Hkv, int hd,
-                  bool round_dv, cudaStream_t s);
-// segs: device array of nseg {start, len} int64 pairs into the flat arenas.
+                  const float* dO, float* dq, float* dk, float* dv, float* D, float* partial, int B, int S, int H,
+                  int Hkv, int hd, bool round_dv, cudaStream_t s);
+size_t attention_bwd_partial_floats(int B, int S, int H, int Hkv, int hd);
 // elems: number of gradient elements the segments cover (for the profiler).
 int grad_norm(Context* ctx, const float* grads, const int64_t* segs, int nseg, float max_norm, double* norm_out,
               float* scale_out, double* scratch, int scratch_count, double elems, cudaStream_t s);

@@ -55,12 +55,15 @@ int glc_attention_fwd(glc_ctx* ctx, const float* q, const float* k, const float*
 int glc_attention_bwd(glc_ctx* ctx, const float* q, const float* k, const float* v, const float* o, const float* lse,
                       const float* dO, float* dq, float* dk, float* dv, int B, int S, int H, int Hkv, int hd,
                       int round_dv) {
-  if (!ctx || B <= 0 || S <= 0 || H <= 0) return GLC_ERR_INVALID;
+  if (!ctx || B <= 0 || S <= 0 || H <= 0 || Hkv <= 0) return GLC_ERR_INVALID;
+  const size_t nd = static_cast<size_t>(B) * H * S, np = glc::attention_bwd_partial_floats(B, S, H, Hkv, hd);
   void* ws = nullptr;
-  int rc = C_(ctx)->workspace(sizeof(float) * static_cast<size_t>(B) * H * S, &ws);
+  int rc = C_(ctx)->workspace(sizeof(float) * (((nd + 63) & ~size_t(63)) + np), &ws);
   if (rc) return rc;
-  return glc::attention_bwd(C_(ctx), q, k, v, o, lse, dO, dq, dk, dv, static_cast<float*>(ws), B, S, H, Hkv, hd,
-                            round_dv != 0, C_(ctx)->stream);
+  float* D = static_cast<float*>(ws);
+  float* partial = np ? D + ((nd + 63) & ~size_t(63)) : nullptr;
+  return glc::attention_bwd(C_(ctx), q, k, v, o, lse, dO, dq, dk, dv, D, partial, B, S, H, Hkv, hd, round_dv != 0,
+                            C_(ctx)->stream);
 }
 
 int glc_softmax_ce(glc_ctx* ctx, float* logits, const int64_t* targets, int rows, int V, float scale, float* row_logp,
@@ -94,6 +97,56 @@ int glc_embed_bwd(glc_ctx* ctx, const int64_t* tokens_host, int T, const float* 
   if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
   if (e != cudaSuccess) return c->fail_cuda(e, "embed_bwd: segment upload");
   return glc::embed_bwd(c, dev, dev + nseg, dev + 2 * nseg + 1, nseg, dh, dE, d, c->stream);
+}
+
+// Uploads a host segment table to the workspace (after `offset` bytes).
+static int upload_segs(Context* c, const int64_t* segs, int nseg, size_t offset, int64_t** out, double* elems) {
+  if (nseg <= 0 || !segs) return c->fail(GLC_ERR_INVALID, "segment table is empty");
+  *elems = 0;
+  for (int i = 0; i < nseg; ++i) {
+    if (segs[2 * i] < 0 || segs[2 * i + 1] < 0 || (segs[2 * i] & 3) || (segs[2 * i + 1] & 3))
+      return c->fail(GLC_ERR_INVALID, "segments must start and end on multiples of 4 floats");
+    *elems += static_cast<double>(segs[2 * i + 1]);
+  }
+  void* ws = nullptr;
+  const size_t bytes = sizeof(int64_t) * 2 * nseg;
+  int rc = c->workspace(offset + bytes, &ws);
+  if (rc) return rc;
+  int64_t* dev = reinterpret_cast<int64_t*>(static_cast<char*>(ws) + offset);
+  cudaError_t e = cudaMemcpyAsync(dev, segs, bytes, cudaMemcpyHostToDevice, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return c->fail_cuda(e, "segment upload");
+  *out = dev;
+  return 0;
+}
+
+int glc_grad_clip_norm(glc_ctx* ctx, const float* grads, const int64_t* segs_host, int nseg, float max_norm,
+                       double* norm_dev, float* scale_dev) {
+  if (!ctx || !norm_dev || !scale_dev) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  const int bx_cap = 8 * c->num_sms;
+  const size_t partial_bytes = sizeof(double) * static_cast<size_t>(nseg > 0 ? nseg : 1) * (bx_cap + 4);
+  int64_t* segs = nullptr;
+  double elems = 0;
+  int rc = upload_segs(c, segs_host, nseg, partial_bytes, &segs, &elems);
+  if (rc) return rc;
+  void* ws = nullptr;
+  c->workspace(partial_bytes, &ws);
+  return glc::grad_norm(c, grads, segs, nseg, max_norm, norm_dev, scale_dev, static_cast<double*>(ws),
+                        static_cast<int>(partial_bytes / sizeof(double)), elems, c->stream);
+}
+
+int glc_adamw_step(glc_ctx* ctx, float* params, float* grads, float* m, float* v, float* shadow,
+                   const int64_t* segs_host, int nseg, const float* clip_scale_dev, float lr, float beta1, float beta2,
+                   float eps, float weight_decay, int step) {
+  if (!ctx) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  int64_t* segs = nullptr;
+  double elems = 0;
+  int rc = upload_segs(c, segs_host, nseg, 0, &segs, &elems);
+  if (rc) return rc;
+  return glc::adamw(c, params, grads, m, v, shadow, segs, nseg, clip_scale_dev, lr, beta1, beta2, eps, weight_decay,
+                    step, elems, c->stream);
 }
 
 int glc_fill(glc_ctx* ctx, float* p, float value, size_t n) {

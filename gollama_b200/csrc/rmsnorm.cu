@@ -146,13 +146,24 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
   }
 }
 
-// dw[j] (+)= sum over blocks b (ascending) of partial[b][j]
+// dw[j] (+)= sum over blocks b of partial[b][j].  One block per 32 columns:
+// warp w adds rows w, w+8, ... for column (32*blockIdx.x + lane), then warp 0
+// adds the 8 warp sums in order (deterministic).
 __global__ void column_sum_kernel(const float* __restrict__ partial, int nblocks, int cols, float* __restrict__ out,
                                   int accumulate) {
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < cols; j += gridDim.x * blockDim.x) {
-    float s = 0.f;
-    for (int b = 0; b < nblocks; ++b) s += partial[static_cast<size_t>(b) * cols + j];
-    out[j] = accumulate ? __fadd_rn(out[j], s) : s;
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int j = blockIdx.x * 32 + lane;
+  float s = 0.f;
+  if (j < cols)
+    for (int b = w; b < nblocks; b += 8) s += partial[static_cast<size_t>(b) * cols + j];
+  red[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && j < cols) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][lane];
+    out[j] = accumulate ? __fadd_rn(out[j], t) : t;
   }
 }
 
@@ -217,7 +228,7 @@ int rmsnorm_bwd(Context* ctx, const float* x, const float* w, const float* rms, 
   else
     rmsnorm_bwd_kernel<8><<<nblocks, 256, 0, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
   GLC_LAUNCH_CHECK(ctx, "rmsnorm_bwd");
-  column_sum_kernel<<<(cols + 255) / 256, 256, 0, s>>>(partial, nblocks, cols, dw, dw_accumulate ? 1 : 0);
+  column_sum_kernel<<<(cols + 31) / 32, 256, 0, s>>>(partial, nblocks, cols, dw, dw_accumulate ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "rmsnorm_bwd column sum");
   return 0;
 }

@@ -84,6 +84,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Abort path only: waits at most 1 s for the phase `parity` of `bar` (copies a
+// producer issued before aborting) so the CTA never exits with them in flight.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, int* gerr) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > 1000000000ull) {
+      if (gerr) atomicCAS(gerr, 0, GLC_DEV_TIMEOUT_DRAIN);
+      return;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -178,6 +190,35 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 bits, 32 consecutive columns, registers -> TMEM.
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Makes this thread's prior generic-proxy shared-memory writes visible to the
+// async proxy (the tensor core reading operands through smem descriptors).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Byte offset of element (row, k) inside a K-major 128-byte-swizzled operand
+// tile of 32-bit elements: blocks of 32 k-elements, each [rows][128 B] with
+// the 16-byte chunk index XORed by (row % 8); `block_bytes` is rows * 128.
+__device__ __forceinline__ uint32_t kmajor_sw128_offset(int row, int k, uint32_t block_bytes) {
+  const uint32_t kb = static_cast<uint32_t>(k) >> 5, chunk = (static_cast<uint32_t>(k) >> 2) & 7u;
+  return kb * block_bytes + static_cast<uint32_t>(row) * 128u + ((chunk ^ (static_cast<uint32_t>(row) & 7u)) << 4) +
+         (static_cast<uint32_t>(k) & 3u) * 4u;
+}
 
 // Round an fp32 value to the nearest TF32 value (ties away from zero), keeping
 // fp32 storage.  Used where a kernel writes a tensor whose consumers are the

@@ -278,16 +278,19 @@ struct Model {
   // that follows it in forwardLayer (trainer.go:312,317; grad.go:158-197) is
   // fused: out = residual + a . w^T, and its GradFn passes the gradient
   // through to `residual` before the two GEMM gradients.
-  Node* matmul(Tape& tp, Node* a, Node* w, Node* residual) {
+  // round_out: the output is a tensor-core operand (q, k, v feed attention);
+  // round_dx: the input gradient is one (the attention output's gradient).
+  Node* matmul(Tape& tp, Node* a, Node* w, Node* residual, bool round_out = false, bool round_dx = false) {
     const int M = static_cast<int>(a->rows), K = static_cast<int>(a->cols), N = static_cast<int>(w->rows);
     Node* out = tp.make(M, N);
     out->require_grad = a->require_grad || w->require_grad || (residual && residual->require_grad);
     if (residual) out->parents = {residual, a, w};
     else out->parents = {a, w};
     ck(gemm_tf32(ctx, {a->gemm_data, K, false}, {w->gemm_data, K, false}, out->data, N, M, N, K, false,
-                 residual ? residual->data : nullptr, N, false, tp.stream()));
+                 residual ? residual->data : nullptr, N, round_out, tp.stream()));
+    if (round_out) out->gemm_data = out->data;
     Tape* t = &tp;
-    out->grad_fn = [this, t, out, a, w, residual, M, K, N]() {
+    out->grad_fn = [this, t, out, a, w, residual, M, K, N, round_dx]() {
       if (!out->grad_live) return;
       if (residual && residual->require_grad) {
         if (!residual->grad_live && residual->param < 0) {
@@ -305,8 +308,9 @@ struct Model {
       const float* dY = t->gemm_grad(out);
       if (a->require_grad) {
         const bool acc = t->prepare_grad(a);
-        ck(gemm_tf32(ctx, {dY, N, false}, {w->gemm_data, K, true}, a->grad, K, M, K, N, acc, nullptr, 0, false,
-                     t->stream()));
+        ck(gemm_tf32(ctx, {dY, N, false}, {w->gemm_data, K, true}, a->grad, K, M, K, N, acc, nullptr, 0,
+                     round_dx && !acc, t->stream()));
+        if (round_dx && !acc) a->grad_round = a->grad;
       }
       if (w->require_grad) {
         const bool acc = t->prepare_grad(w);
@@ -345,8 +349,8 @@ struct Model {
   Node* attention(Tape& tp, Node* q, Node* k, Node* v, int B, int S) {
     const int H = cfg.num_heads, Hkv = kvh, T = B * S;
     if (llama) {
-      ck(rope(ctx, q->data, T, S, H, hd, cos_t, sin_t, false, false, tp.stream()));
-      ck(rope(ctx, k->data, T, S, Hkv, hd, cos_t, sin_t, false, false, tp.stream()));
+      ck(rope(ctx, q->data, T, S, H, hd, cos_t, sin_t, false, true, tp.stream()));
+      ck(rope(ctx, k->data, T, S, Hkv, hd, cos_t, sin_t, false, true, tp.stream()));
     }
     Node* out = tp.make(T, static_cast<int64_t>(H) * hd);
     out->require_grad = true;
@@ -361,8 +365,10 @@ struct Model {
       const bool aq = t->prepare_grad(q), ak = t->prepare_grad(k), av = t->prepare_grad(v);
       if (aq || ak || av) throw StepError{GLC_ERR_UNSUPPORTED};  // q/k/v have no other consumers
       float* D = t->alloc(static_cast<int64_t>(B) * H * S);
-      ck(attention_bwd(ctx, q->data, k->data, v->data, out->data, lse, out->grad, q->grad, k->grad, v->grad, D, B, S,
-                       H, Hkv, hd, true, t->stream()));
+      const size_t np = attention_bwd_partial_floats(B, S, H, Hkv, hd);
+      float* partial = np ? t->alloc(static_cast<int64_t>(np)) : nullptr;
+      ck(attention_bwd(ctx, q->data, k->data, v->data, out->data, lse, out->grad, q->grad, k->grad, v->grad, D,
+                       partial, B, S, H, Hkv, hd, true, t->stream()));
       ck(rope(ctx, q->grad, T, S, H, hd, cos_t, sin_t, true, true, t->stream()));
       ck(rope(ctx, k->grad, T, S, Hkv, hd, cos_t, sin_t, true, true, t->stream()));
       q->grad_round = q->grad;
@@ -437,11 +443,11 @@ struct Model {
     for (int l = 0; l < cfg.num_layers; ++l) {
       // forwardLayer (trainer.go:308-320)
       Node* n1 = rmsnorm(tp, x, P(lp(l, P_ATTN_NORM)));
-      Node* q = matmul(tp, n1, P(lp(l, P_WQ)), nullptr);
-      Node* k = matmul(tp, n1, P(lp(l, P_WK)), nullptr);
-      Node* v = matmul(tp, n1, P(lp(l, P_WV)), nullptr);
+      Node* q = matmul(tp, n1, P(lp(l, P_WQ)), nullptr, true);
+      Node* k = matmul(tp, n1, P(lp(l, P_WK)), nullptr, true);
+      Node* v = matmul(tp, n1, P(lp(l, P_WV)), nullptr, true);
       Node* att = attention(tp, q, k, v, B, S);
-      Node* x1 = matmul(tp, att, P(lp(l, P_WO)), x);
+      Node* x1 = matmul(tp, att, P(lp(l, P_WO)), x, false, true);
       Node* n2 = rmsnorm(tp, x1, P(lp(l, P_FFN_NORM)));
       // forwardFFN (trainer.go:392-426)
       Node* gate = matmul(tp, n2, P(lp(l, P_WGATE)), nullptr);
@@ -501,8 +507,11 @@ int Model::init(Context* c, const glc_train_config& conf) {
   llama = cfg.semantics == GLC_SEMANTICS_LLAMA;
   if (cfg.num_kv_heads <= 0 || !llama) cfg.num_kv_heads = cfg.num_heads;
   if (cfg.num_heads <= 0 || cfg.hidden_size % cfg.num_heads || cfg.num_heads % cfg.num_kv_heads || cfg.vocab_size <= 0 ||
-      cfg.num_layers < 0 || cfg.intermediate_size <= 0 || cfg.max_seq_len <= 0)
-    return c->fail(GLC_ERR_INVALID, "model: inconsistent configuration");
+      cfg.num_layers < 0 || cfg.intermediate_size <= 0 || cfg.max_seq_len <= 0 || (cfg.hidden_size & 3) ||
+      (cfg.intermediate_size & 3) || (cfg.vocab_size & 3))
+    return c->fail(GLC_ERR_INVALID,
+                  "model: inconsistent configuration (heads must divide hidden, kv heads must divide heads; hidden, "
+                  "intermediate and vocab sizes must be multiples of 4)");
   hd = cfg.hidden_size / cfg.num_heads;
   kvh = cfg.num_kv_heads;
   const int64_t d = cfg.hidden_size, F = cfg.intermediate_size, kvd = static_cast<int64_t>(kvh) * hd;

@@ -185,6 +185,22 @@ GLC_API int glc_embed_fwd(glc_ctx* ctx, const int64_t* tokens, const float* E, c
 /* Embedding gradient dE[tok[t]] += dh[t] (t ascending, deterministic);
  * tokens_host are the same ids on the host. */
 GLC_API int glc_embed_bwd(glc_ctx* ctx, const int64_t* tokens_host, int T, const float* dh, float* dE, int d, int V);
+/* GradientClipping (pkg/train/optimizer.go:169-196) over the parameters that
+ * have a gradient, given as a host table of nseg {start, len} int64 pairs
+ * into the gradient arena (multiples of 4 floats): norm_dev (double) receives
+ * the global L2 norm, scale_dev (float) the clip factor (1 when not clipped),
+ * both in device memory so AdamW can apply it without a host round trip. */
+GLC_API int glc_grad_clip_norm(glc_ctx* ctx, const float* grads, const int64_t* segs_host, int nseg, float max_norm,
+                               double* norm_dev, float* scale_dev);
+/* AdamW.Step (pkg/train/optimizer.go:37-76) over the same segments: grads are
+ * scaled by *clip_scale_dev (when given; the clipped values are written back
+ * as the reference's in-place clipping leaves them), moments in float32, the
+ * bias-corrected update in float64 rounded to float32, decoupled weight decay;
+ * `step` is the optimizer's step count after incrementing.  shadow (nullable)
+ * receives the new parameters rounded to TF32 for the GEMMs. */
+GLC_API int glc_adamw_step(glc_ctx* ctx, float* params, float* grads, float* m, float* v, float* shadow,
+                           const int64_t* segs_host, int nseg, const float* clip_scale_dev, float lr, float beta1,
+                           float beta2, float eps, float weight_decay, int step);
 GLC_API int glc_fill(glc_ctx* ctx, float* p, float value, size_t n);
 GLC_API int glc_round_tf32(glc_ctx* ctx, const float* src, float* dst, size_t n);
 /* addInplace (pkg/tensor/grad.go:200-204): dst += src. */

@@ -150,14 +150,25 @@ def test_rope_matches_oracle_and_inverts(ctx, orc):
     assert rel_fro(bx.numpy(), x) < 1e-6
 
 
-@pytest.mark.parametrize("B,S,H,Hkv,hd", [(2, 64, 4, 4, 32), (1, 100, 4, 2, 64), (2, 256, 8, 4, 64), (1, 130, 2, 1, 32)])
+def tf32(x):
+    """Round to the nearest TF32 value (ties away from zero), as the kernels
+    that produce tensor-core operands do."""
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    return ((b + np.uint32(0x1000)) & np.uint32(0xFFFFE000)).view(np.float32)
+
+
+ATTN_TOL = 2e-3  # TF32 tensor-core attention (P and dS rounded to TF32) vs the fp32 oracle
+
+
+@pytest.mark.parametrize("B,S,H,Hkv,hd", [(2, 64, 4, 4, 32), (1, 100, 4, 2, 64), (2, 256, 8, 4, 64), (1, 130, 2, 1, 32),
+                                          (1, 1024, 4, 1, 64), (3, 200, 2, 2, 64)])
 def test_attention_fwd_bwd(ctx, orc, B, S, H, Hkv, hd):
     T = B * S
     r = rng(T + H)
-    q = r.standard_normal((T, H * hd), dtype=np.float32)
-    k = r.standard_normal((T, Hkv * hd), dtype=np.float32)
-    v = r.standard_normal((T, Hkv * hd), dtype=np.float32)
-    dO = r.standard_normal((T, H * hd), dtype=np.float32)
+    q = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
+    k = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    v = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    dO = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
     ref_o = orc.attention_fwd(q, k, v, S, H, Hkv, hd)
     ref_dq, ref_dk, ref_dv = orc.attention_bwd(q, k, v, dO, S, H, Hkv, hd)
     bq, bk, bv, bdo = ctx.from_numpy(q), ctx.from_numpy(k), ctx.from_numpy(v), ctx.from_numpy(dO)
@@ -167,10 +178,9 @@ def test_attention_fwd_bwd(ctx, orc, B, S, H, Hkv, hd):
     ctx.call("glc_attention_bwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, bdq.ptr, bdk.ptr, bdv.ptr,
              B, S, H, Hkv, hd, 0)
     ctx.sync()
-    assert rel_fro(bo.numpy(), ref_o) < FP32_RTOL
-    assert rel_fro(bdq.numpy(), ref_dq) < 1e-4
-    assert rel_fro(bdk.numpy(), ref_dk) < 1e-4
-    assert rel_fro(bdv.numpy(), ref_dv) < 1e-4
+    errs = [rel_fro(bo.numpy(), ref_o), rel_fro(bdq.numpy(), ref_dq), rel_fro(bdk.numpy(), ref_dk),
+            rel_fro(bdv.numpy(), ref_dv)]
+    assert max(errs) < ATTN_TOL, errs
 
 
 def test_embedding_fwd_bwd(ctx):
@@ -209,3 +219,51 @@ def test_round_tf32(ctx):
     assert y[2] == -np.float32(1.0 + 2.0**-10)
     bits = y.view(np.uint32)
     assert np.all(bits & 0x1FFF == 0)
+
+
+def adamw_reference(p, g, m, v, lr, b1, b2, eps, wd, step, scale):
+    """AdamW.Step (pkg/train/optimizer.go:37-76) in numpy with Go's types:
+    float32 moments and parameters, float64 bias correction and update."""
+    f32 = np.float32
+    if scale != 1.0:
+        g = (g * f32(scale)).astype(f32)
+    m = f32(b1) * m + (f32(1) - f32(b1)) * g
+    v = f32(b2) * v + ((f32(1) - f32(b2)) * g) * g
+    bc1 = 1.0 - np.float64(f32(b1)) ** step
+    bc2 = 1.0 - np.float64(f32(b2)) ** step
+    upd = (m.astype(np.float64) / bc1 / (np.sqrt(v.astype(np.float64) / bc2) + np.float64(f32(eps)))).astype(f32)
+    p = p - f32(lr) * (upd + f32(wd) * p)
+    return p, g, m, v
+
+
+@pytest.mark.parametrize("step", [1, 7])
+def test_clip_and_adamw_bit_exact(ctx, step):
+    n = 1 << 22
+    r = rng(step)
+    p = (r.standard_normal(n) * 0.02).astype(np.float32)
+    g = (r.standard_normal(n) * np.exp(r.uniform(-12, 2, n))).astype(np.float32)
+    g[:16] = 0.0
+    m = (r.standard_normal(n) * 1e-3).astype(np.float32) if step > 1 else np.zeros(n, np.float32)
+    v = (np.abs(r.standard_normal(n)) * 1e-6).astype(np.float32) if step > 1 else np.zeros(n, np.float32)
+    segs = np.array([0, n // 2, n // 2 + 64, n // 2 - 64], np.int64)  # two segments, a 64-float hole
+    bp, bg, bm, bv, bs = ctx.from_numpy(p), ctx.from_numpy(g), ctx.from_numpy(m), ctx.from_numpy(v), ctx.empty((n,))
+    dnorm, dscale = ctx.empty((1,), np.float64), ctx.empty((1,))
+    ctx.call("glc_grad_clip_norm", bg.ptr, segs.ctypes.data_as(C.c_void_p), 2, C.c_float(1.0), dnorm.ptr, dscale.ptr)
+    ctx.call("glc_adamw_step", bp.ptr, bg.ptr, bm.ptr, bv.ptr, bs.ptr, segs.ctypes.data_as(C.c_void_p), 2, dscale.ptr,
+             C.c_float(3e-4), C.c_float(0.9), C.c_float(0.95), C.c_float(1e-8), C.c_float(0.1), step)
+    ctx.sync()
+    sel = np.r_[0 : n // 2, n // 2 + 64 : n]
+    norm = float(np.sqrt(np.sum(g[sel].astype(np.float64) ** 2)))
+    assert abs(dnorm.numpy()[0] - norm) <= 1e-12 * norm
+    scale = np.float32(1.0 / norm) if np.float32(norm) > 1.0 else np.float32(1.0)
+    assert dscale.numpy()[0] == scale
+    rp, rg, rm, rv = adamw_reference(p[sel], g[sel], m[sel], v[sel], 3e-4, 0.9, 0.95, 1e-8, 0.1, step, float(scale))
+    out_p, out_g, out_m, out_v = bp.numpy(), bg.numpy(), bm.numpy(), bv.numpy()
+    assert np.array_equal(out_m[sel], rm) and np.array_equal(out_v[sel], rv)
+    assert np.array_equal(out_g[sel], rg)
+    assert np.array_equal(out_p[sel], rp)
+    hole = slice(n // 2, n // 2 + 64)
+    assert np.array_equal(out_p[hole], p[hole]) and np.array_equal(out_g[hole], g[hole])
+    sh = bs.numpy()[sel]
+    assert np.all(sh.view(np.uint32) & 0x1FFF == 0)
+    assert np.max(np.abs(sh - rp) / np.maximum(np.abs(rp), 1e-30)) <= 2.0**-11
