@@ -69,6 +69,6 @@ extern "C" int glc_attention_bwd_noalloc(glc_ctx* ctx, const float* q, const flo
   // D is fully written by the first kernel of the backward before it is
   // read, so the previous call's contents need no clearing.
   // No partial buffer: each CTA sums its KV head's query-head group itself.
-  return glc::attention_bwd(c, q, k, v, o, lse, dO, dq, dk, dv, D, nullptr, B, S, H, Hkv, hd, round_dv != 0,
-                            c->stream);
+  const glc::AttnIO io{q, H * hd, k, Hkv * hd, v, Hkv * hd, dq, H * hd, dk, Hkv * hd, dv, Hkv * hd};
+  return glc::attention_bwd(c, io, o, lse, dO, D, nullptr, B, S, H, Hkv, hd, round_dv != 0, c->stream);
 }

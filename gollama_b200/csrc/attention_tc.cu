@@ -315,8 +315,8 @@ __global__ void __launch_bounds__(NT, 1)
                             const __grid_constant__ CUtensorMap tmOk, const __grid_constant__ CUtensorMap tmOm,
                             const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                             const float* __restrict__ lse, const float* __restrict__ Dv, float* __restrict__ dk_out,
-                            float* __restrict__ dv_out, int out_heads, int S, int H, int Hkv, float scale,
-                            float scale_log2, int round_dv, int* err) {
+                            float* __restrict__ dv_out, int dk_ld, int dv_ld, int per_head, int S, int H, int Hkv,
+                            float scale, float scale_log2, int round_dv, int* err) {
   using L = DkdvLayout<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -460,9 +460,9 @@ __global__ void __launch_bounds__(NT, 1)
     }
     if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
       tc_fence_after();
-      // out_heads = Hkv: final dk/dv; out_heads = H: per-query-head partials
-      const int oh = (out_heads == Hkv) ? kh : h_first;
-      const size_t row = (static_cast<size_t>(row_base) + key) * (static_cast<size_t>(out_heads) * HD) + oh * HD;
+      // final dk/dv at the KV head's columns, or per-query-head partials
+      const int oh = per_head ? h_first : kh;
+      const size_t trow = static_cast<size_t>(row_base) + key;
 #pragma unroll 1
       for (int part = 0; part < 2; ++part) {  // 0: dV, 1: dK
 #pragma unroll 1
@@ -471,7 +471,7 @@ __global__ void __launch_bounds__(NT, 1)
           tmem_ld_32x32b_x32(lane_addr + 128 + part * HD + cc * 32, v);
           tmem_ld_wait();
           if (key < S) {
-            float* dst = (part == 0 ? dv_out : dk_out) + row + cc * 32;
+            float* dst = (part == 0 ? dv_out + trow * dv_ld : dk_out + trow * dk_ld) + oh * HD + cc * 32;
             const bool rnd = part == 0 && round_dv;
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
@@ -496,7 +496,8 @@ __global__ void __launch_bounds__(NT, 1)
 // dk[t][kh] = sum over the G query heads of the group of partial[t][h]
 // (heads ascending: deterministic); dv the same, optionally TF32-rounded.
 __global__ void group_sum_kernel(const float* __restrict__ pk, const float* __restrict__ pv, float* __restrict__ dk,
-                                 float* __restrict__ dv, int T, int H, int Hkv, int hd, int round_dv) {
+                                 float* __restrict__ dv, int dk_ld, int dv_ld, int T, int H, int Hkv, int hd,
+                                 int round_dv) {
   const int G = H / Hkv, n4 = hd / 4;
   const size_t total = static_cast<size_t>(T) * Hkv * n4;
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
@@ -513,9 +514,8 @@ __global__ void group_sum_kernel(const float* __restrict__ pk, const float* __re
       sv.x += c.x; sv.y += c.y; sv.z += c.z; sv.w += c.w;
     }
     if (round_dv) sv = make_float4(round_tf32(sv.x), round_tf32(sv.y), round_tf32(sv.z), round_tf32(sv.w));
-    const size_t dst = (t * Hkv + kh) * hd / 4 + d4;
-    reinterpret_cast<float4*>(dk)[dst] = sk;
-    reinterpret_cast<float4*>(dv)[dst] = sv;
+    reinterpret_cast<float4*>(dk + t * dk_ld + kh * hd)[d4] = sk;
+    reinterpret_cast<float4*>(dv + t * dv_ld + kh * hd)[d4] = sv;
   }
 }
 
@@ -536,8 +536,8 @@ __global__ void __launch_bounds__(NT, 1)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmO,
                           const __grid_constant__ CUtensorMap tmKk, const __grid_constant__ CUtensorMap tmKm,
                           const __grid_constant__ CUtensorMap tmVk, const float* __restrict__ lse,
-                          const float* __restrict__ Dv, float* __restrict__ dq, int S, int H, int Hkv, int n_qt,
-                          float scale, float scale_log2, int* err) {
+                          const float* __restrict__ Dv, float* __restrict__ dq, int dq_ld, int S, int H, int Hkv,
+                          int n_qt, float scale, float scale_log2, int* err) {
   using L = DqLayout<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -677,7 +677,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
       tc_fence_after();
-      float* drow = dq + (static_cast<size_t>(row_base) + qa) * (static_cast<size_t>(H) * HD) + h * HD;
+      float* drow = dq + (static_cast<size_t>(row_base) + qa) * static_cast<size_t>(dq_ld) + h * HD;
 #pragma unroll 1
       for (int cc = 0; cc < HD / 32; ++cc) {
         uint32_t v[32];
@@ -719,9 +719,10 @@ __global__ void attn_bwd_prep_tc_kernel(const float* __restrict__ o, const float
 }
 
 // ---------------------------------------------------------------- host side
-int encode(Context* ctx, CUtensorMap* tm, const float* ptr, int cols, int rows, int box_rows, bool mn) {
+// rows x cols sub-matrix with row stride ld (elements), boxes {32, box_rows}
+int encode(Context* ctx, CUtensorMap* tm, const float* ptr, int cols, int ld, int rows, int box_rows, bool mn) {
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
   cuuint32_t box[2] = {32, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   if (ctx->encode_tiled(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
@@ -749,16 +750,16 @@ int check(Context* ctx, const float* q, const float* k, const float* v, int B, i
 }
 
 template <int HD>
-int fwd_impl(Context* ctx, const float* q, const float* k, const float* v, float* o, float* lse, int B, int S, int H,
-             int Hkv, bool round_out, cudaStream_t s) {
+int fwd_impl(Context* ctx, const float* q, int q_ld, const float* k, int k_ld, const float* v, int v_ld, float* o,
+             float* lse, int B, int S, int H, int Hkv, bool round_out, cudaStream_t s) {
   using L = FwdLayout<HD>;
   static bool done[8] = {false};
   int rc = set_smem(ctx, attn_fwd_tc_kernel<HD>, L::BYTES, done);
   if (rc) return rc;
   const int T = B * S;
   CUtensorMap tq, tk, tv;
-  if ((rc = encode(ctx, &tq, q, H * HD, T, 128, false)) || (rc = encode(ctx, &tk, k, Hkv * HD, T, 128, false)) ||
-      (rc = encode(ctx, &tv, v, Hkv * HD, T, 128, true)))
+  if ((rc = encode(ctx, &tq, q, H * HD, q_ld, T, 128, false)) || (rc = encode(ctx, &tk, k, Hkv * HD, k_ld, T, 128, false)) ||
+      (rc = encode(ctx, &tv, v, Hkv * HD, v_ld, T, 128, true)))
     return rc;
   const int n_qt = (S + 127) / 128;
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
@@ -771,9 +772,9 @@ int fwd_impl(Context* ctx, const float* q, const float* k, const float* v, float
 }
 
 template <int HD>
-int bwd_impl(Context* ctx, const float* q, const float* k, const float* v, const float* o, const float* lse,
-             const float* dO, float* dq, float* dk, float* dv, float* D, float* partial, int B, int S, int H, int Hkv,
-             bool round_dv, cudaStream_t s) {
+int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, const float* dO, float* D,
+             float* partial, int B, int S, int H, int Hkv, bool round_dv, cudaStream_t s) {
+  const float *q = io.q, *k = io.k, *v = io.v;
   static bool done_g[8] = {false}, done_p[8] = {false}, done_q[8] = {false};
   int rc = set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD, true>, DkdvLayout<HD>::BYTES, done_g);
   if (!rc) rc = set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD, false>, DkdvLayout<HD>::BYTES, done_p);
@@ -781,12 +782,13 @@ int bwd_impl(Context* ctx, const float* q, const float* k, const float* v, const
   if (rc) return rc;
   const int T = B * S, G = H / Hkv;
   CUtensorMap tQk64, tQm64, tOk64, tOm64, tK128, tV128, tQ128, tO128, tKk64, tKm64, tVk64;
-  if ((rc = encode(ctx, &tQk64, q, H * HD, T, 64, false)) || (rc = encode(ctx, &tQm64, q, H * HD, T, 64, true)) ||
-      (rc = encode(ctx, &tOk64, dO, H * HD, T, 64, false)) || (rc = encode(ctx, &tOm64, dO, H * HD, T, 64, true)) ||
-      (rc = encode(ctx, &tK128, k, Hkv * HD, T, 128, false)) || (rc = encode(ctx, &tV128, v, Hkv * HD, T, 128, false)) ||
-      (rc = encode(ctx, &tQ128, q, H * HD, T, 128, false)) || (rc = encode(ctx, &tO128, dO, H * HD, T, 128, false)) ||
-      (rc = encode(ctx, &tKk64, k, Hkv * HD, T, 64, false)) || (rc = encode(ctx, &tKm64, k, Hkv * HD, T, 64, true)) ||
-      (rc = encode(ctx, &tVk64, v, Hkv * HD, T, 64, false)))
+  const int qw = H * HD, kw = Hkv * HD;
+  if ((rc = encode(ctx, &tQk64, q, qw, io.q_ld, T, 64, false)) || (rc = encode(ctx, &tQm64, q, qw, io.q_ld, T, 64, true)) ||
+      (rc = encode(ctx, &tOk64, dO, qw, qw, T, 64, false)) || (rc = encode(ctx, &tOm64, dO, qw, qw, T, 64, true)) ||
+      (rc = encode(ctx, &tK128, k, kw, io.k_ld, T, 128, false)) || (rc = encode(ctx, &tV128, v, kw, io.v_ld, T, 128, false)) ||
+      (rc = encode(ctx, &tQ128, q, qw, io.q_ld, T, 128, false)) || (rc = encode(ctx, &tO128, dO, qw, qw, T, 128, false)) ||
+      (rc = encode(ctx, &tKk64, k, kw, io.k_ld, T, 64, false)) || (rc = encode(ctx, &tKm64, k, kw, io.k_ld, T, 64, true)) ||
+      (rc = encode(ctx, &tVk64, v, kw, io.v_ld, T, 64, false)))
     return rc;
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
   const double causal = 0.5 * static_cast<double>(S) * (S + 1);
@@ -797,23 +799,24 @@ int bwd_impl(Context* ctx, const float* q, const float* k, const float* v, const
   if (G == 1 || partial == nullptr) {
     // one CTA per (key tile, KV head), looping over the query heads of its group
     attn_bwd_dkdv_tc_kernel<HD, true><<<dim3(n_kt, Hkv, B), NT, DkdvLayout<HD>::BYTES, s>>>(
-        tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, dk, dv, Hkv, S, H, Hkv, scale, scale * LOG2E,
-        round_dv ? 1 : 0, ctx->d_err);
+        tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, io.dk, io.dv, io.dk_ld, io.dv_ld, 0, S, H, Hkv, scale,
+        scale * LOG2E, round_dv ? 1 : 0, ctx->d_err);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
   } else {
     // one CTA per (key tile, query head); partials [T, H*hd] for dK and dV
     float* pk = partial;
     float* pv = partial + static_cast<size_t>(T) * H * HD;
     attn_bwd_dkdv_tc_kernel<HD, false><<<dim3(n_kt, H, B), NT, DkdvLayout<HD>::BYTES, s>>>(
-        tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, pk, pv, H, S, H, Hkv, scale, scale * LOG2E, 0, ctx->d_err);
+        tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, pk, pv, qw, qw, 1, S, H, Hkv, scale, scale * LOG2E, 0,
+        ctx->d_err);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
     group_sum_kernel<<<grid_for(static_cast<size_t>(T) * Hkv * HD / 4, 256, ctx->num_sms), 256, 0, s>>>(
-        pk, pv, dk, dv, T, H, Hkv, HD, round_dv ? 1 : 0);
+        pk, pv, io.dk, io.dv, io.dk_ld, io.dv_ld, T, H, Hkv, HD, round_dv ? 1 : 0);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd group sum");
   }
   const int n_qt = (S + 127) / 128;
   attn_bwd_dq_tc_kernel<HD><<<dim3(n_qt, H, B), NT, DqLayout<HD>::BYTES, s>>>(
-      tQ128, tO128, tKk64, tKm64, tVk64, lse, D, dq, S, H, Hkv, n_qt, scale, scale * LOG2E, ctx->d_err);
+      tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, H, Hkv, n_qt, scale, scale * LOG2E, ctx->d_err);
   GLC_LAUNCH_CHECK(ctx, "attention_bwd dq (tcgen05)");
   return 0;
 }
@@ -825,26 +828,30 @@ size_t attention_bwd_partial_floats(int B, int S, int H, int Hkv, int hd) {
   return 2 * static_cast<size_t>(B) * S * H * hd;
 }
 
-int attention_fwd(Context* ctx, const float* q, const float* k, const float* v, float* o, float* lse, int B, int S,
-                  int H, int Hkv, int hd, bool round_out, cudaStream_t s) {
-  int rc = check(ctx, q, k, v, B, S, H, Hkv, hd);
+int attention_fwd(Context* ctx, const AttnIO& io, float* o, float* lse, int B, int S, int H, int Hkv, int hd,
+                  bool round_out, cudaStream_t s) {
+  int rc = check(ctx, io.q, io.k, io.v, B, S, H, Hkv, hd);
   if (rc) return rc;
+  if (((io.q_ld | io.k_ld | io.v_ld) & 3) || io.q_ld < H * hd || io.k_ld < Hkv * hd || io.v_ld < Hkv * hd)
+    return ctx->fail(GLC_ERR_INVALID, "attention_fwd: bad row strides");
   if (!o || !lse || (reinterpret_cast<uintptr_t>(o) & 15)) return ctx->fail(GLC_ERR_INVALID, "attention_fwd: bad output");
-  return hd == 64 ? fwd_impl<64>(ctx, q, k, v, o, lse, B, S, H, Hkv, round_out, s)
-                  : fwd_impl<32>(ctx, q, k, v, o, lse, B, S, H, Hkv, round_out, s);
+  return hd == 64 ? fwd_impl<64>(ctx, io.q, io.q_ld, io.k, io.k_ld, io.v, io.v_ld, o, lse, B, S, H, Hkv, round_out, s)
+                  : fwd_impl<32>(ctx, io.q, io.q_ld, io.k, io.k_ld, io.v, io.v_ld, o, lse, B, S, H, Hkv, round_out, s);
 }
 
-int attention_bwd(Context* ctx, const float* q, const float* k, const float* v, const float* o, const float* lse,
-                  const float* dO, float* dq, float* dk, float* dv, float* D, float* partial, int B, int S, int H,
-                  int Hkv, int hd, bool round_dv, cudaStream_t s) {
-  int rc = check(ctx, q, k, v, B, S, H, Hkv, hd);
+int attention_bwd(Context* ctx, const AttnIO& io, const float* o, const float* lse, const float* dO, float* D,
+                  float* partial, int B, int S, int H, int Hkv, int hd, bool round_dv, cudaStream_t s) {
+  int rc = check(ctx, io.q, io.k, io.v, B, S, H, Hkv, hd);
   if (rc) return rc;
-  if (!o || !lse || !dO || !dq || !dk || !dv || !D ||
-      ((reinterpret_cast<uintptr_t>(dO) | reinterpret_cast<uintptr_t>(dq) | reinterpret_cast<uintptr_t>(dk) |
-        reinterpret_cast<uintptr_t>(dv)) & 15))
+  if (!o || !lse || !dO || !io.dq || !io.dk || !io.dv || !D ||
+      ((reinterpret_cast<uintptr_t>(dO) | reinterpret_cast<uintptr_t>(io.dq) | reinterpret_cast<uintptr_t>(io.dk) |
+        reinterpret_cast<uintptr_t>(io.dv)) & 15))
     return ctx->fail(GLC_ERR_INVALID, "attention_bwd: null or misaligned pointer");
-  return hd == 64 ? bwd_impl<64>(ctx, q, k, v, o, lse, dO, dq, dk, dv, D, partial, B, S, H, Hkv, round_dv, s)
-                  : bwd_impl<32>(ctx, q, k, v, o, lse, dO, dq, dk, dv, D, partial, B, S, H, Hkv, round_dv, s);
+  if (((io.q_ld | io.k_ld | io.v_ld | io.dq_ld | io.dk_ld | io.dv_ld) & 3) || io.q_ld < H * hd || io.dq_ld < H * hd ||
+      io.k_ld < Hkv * hd || io.v_ld < Hkv * hd || io.dk_ld < Hkv * hd || io.dv_ld < Hkv * hd)
+    return ctx->fail(GLC_ERR_INVALID, "attention_bwd: bad row strides");
+  return hd == 64 ? bwd_impl<64>(ctx, io, o, lse, dO, D, partial, B, S, H, Hkv, round_dv, s)
+                  : bwd_impl<32>(ctx, io, o, lse, dO, D, partial, B, S, H, Hkv, round_dv, s);
 }
 
 }  // namespace glc

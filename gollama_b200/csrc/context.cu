@@ -289,6 +289,18 @@ int glc_linear_bwd_dx(glc_ctx* ctx, const float* dY, const float* W, float* dX, 
                         c->stream);
 }
 
+int glc_linear_bwd(glc_ctx* ctx, const float* dY, const float* X, const float* W, float* dX, float* dW, int M, int K,
+                   int N, int accumulate_dx, int accumulate_dw) {
+  if (!ctx) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  glc::GemmSpec g[2];
+  int n = 0;
+  if (dX) g[n++] = glc::GemmSpec{{dY, N, false}, {W, K, true}, dX, K, M, K, N, accumulate_dx != 0, nullptr, 0, false};
+  if (dW) g[n++] = glc::GemmSpec{{dY, N, true}, {X, K, true}, dW, K, N, K, M, accumulate_dw != 0, nullptr, 0, false};
+  if (n == 0) return GLC_OK;
+  return glc::gemm_tf32_group(c, g, n, c->stream);
+}
+
 int glc_linear_bwd_dw(glc_ctx* ctx, const float* dY, const float* X, float* dW, int M, int K, int N,
                       int accumulate) {
   if (!ctx) return GLC_ERR_INVALID;

@@ -17,13 +17,16 @@ __device__ __forceinline__ float swiglu_f(float g, float u) {
   return __fmul_rn(__fmul_rn(g, s), u);
 }
 
-__global__ void swiglu_fwd_kernel(const float4* __restrict__ g, const float4* __restrict__ u, float4* __restrict__ h,
-                                  size_t n4, int round_out) {
+__global__ void swiglu_fwd_kernel(const float* __restrict__ g, const float* __restrict__ u, size_t ld_in,
+                                  float* __restrict__ h, size_t ld_h, size_t rows, size_t cols4, int round_out) {
+  const size_t n4 = rows * cols4;
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n4; i += size_t(gridDim.x) * blockDim.x) {
-    const float4 a = g[i], b = u[i];
+    const size_t r = i / cols4, c = i % cols4;
+    const float4 a = reinterpret_cast<const float4*>(g + r * ld_in)[c];
+    const float4 b = reinterpret_cast<const float4*>(u + r * ld_in)[c];
     float4 o = make_float4(swiglu_f(a.x, b.x), swiglu_f(a.y, b.y), swiglu_f(a.z, b.z), swiglu_f(a.w, b.w));
     if (round_out) o = make_float4(round_tf32(o.x), round_tf32(o.y), round_tf32(o.z), round_tf32(o.w));
-    h[i] = o;
+    reinterpret_cast<float4*>(h + r * ld_h)[c] = o;
   }
 }
 
@@ -38,18 +41,25 @@ __device__ __forceinline__ void swiglu_b(float g, float u, float dh, float& dg, 
   dg = __fmul_rn(dgs, grad);
 }
 
-__global__ void swiglu_bwd_kernel(const float4* __restrict__ g, const float4* __restrict__ u,
-                                  const float4* __restrict__ dh, float4* __restrict__ dg, float4* __restrict__ du,
-                                  size_t n4, int accumulate, int round_out) {
+__global__ void swiglu_bwd_kernel(const float* __restrict__ g, const float* __restrict__ u, size_t ld_in,
+                                  const float* __restrict__ dh, size_t ld_dh, float* __restrict__ dg,
+                                  float* __restrict__ du, size_t ld_out, size_t rows, size_t cols4, int accumulate,
+                                  int round_out) {
+  const size_t n4 = rows * cols4;
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n4; i += size_t(gridDim.x) * blockDim.x) {
-    const float4 a = g[i], b = u[i], d = dh[i];
+    const size_t r = i / cols4, c = i % cols4;
+    const float4 a = reinterpret_cast<const float4*>(g + r * ld_in)[c];
+    const float4 b = reinterpret_cast<const float4*>(u + r * ld_in)[c];
+    const float4 d = reinterpret_cast<const float4*>(dh + r * ld_dh)[c];
     float4 rg, ru;
     swiglu_b(a.x, b.x, d.x, rg.x, ru.x);
     swiglu_b(a.y, b.y, d.y, rg.y, ru.y);
     swiglu_b(a.z, b.z, d.z, rg.z, ru.z);
     swiglu_b(a.w, b.w, d.w, rg.w, ru.w);
+    float4* pg = reinterpret_cast<float4*>(dg + r * ld_out) + c;
+    float4* pu = reinterpret_cast<float4*>(du + r * ld_out) + c;
     if (accumulate) {
-      const float4 og = dg[i], ou = du[i];
+      const float4 og = *pg, ou = *pu;
       rg = make_float4(__fadd_rn(og.x, rg.x), __fadd_rn(og.y, rg.y), __fadd_rn(og.z, rg.z), __fadd_rn(og.w, rg.w));
       ru = make_float4(__fadd_rn(ou.x, ru.x), __fadd_rn(ou.y, ru.y), __fadd_rn(ou.z, ru.z), __fadd_rn(ou.w, ru.w));
     }
@@ -57,8 +67,8 @@ __global__ void swiglu_bwd_kernel(const float4* __restrict__ g, const float4* __
       rg = make_float4(round_tf32(rg.x), round_tf32(rg.y), round_tf32(rg.z), round_tf32(rg.w));
       ru = make_float4(round_tf32(ru.x), round_tf32(ru.y), round_tf32(ru.z), round_tf32(ru.w));
     }
-    dg[i] = rg;
-    du[i] = ru;
+    *pg = rg;
+    *pu = ru;
   }
 }
 
@@ -81,17 +91,18 @@ __global__ void round_copy_kernel(const float* __restrict__ src, float* __restri
 // apply3D (pkg/model/rope.go:96-126) on rows of nh heads x hd, consecutive
 // pairs, position t % S; inverse = 1 applies the transposed rotation (the
 // backward).  In place; optional TF32 rounding of the result.
-__global__ void rope_kernel(float* __restrict__ x, int T, int S, int nh, int hd, const float* __restrict__ cos_t,
-                            const float* __restrict__ sin_t, int inverse, int round_out) {
+__global__ void rope_kernel(float* __restrict__ x, size_t ld, int T, int S, int nh, int hd,
+                            const float* __restrict__ cos_t, const float* __restrict__ sin_t, int inverse,
+                            int round_out) {
   const int half = hd >> 1;
   const size_t pairs = static_cast<size_t>(T) * nh * half;
   for (size_t p = blockIdx.x * size_t(blockDim.x) + threadIdx.x; p < pairs; p += size_t(gridDim.x) * blockDim.x) {
     const int i = static_cast<int>(p % half);
     const size_t th = p / half;  // t*nh + h
-    const int t = static_cast<int>(th / nh);
+    const int t = static_cast<int>(th / nh), hh = static_cast<int>(th % nh);
     const int pos = t % S;
     const float c = cos_t[pos * half + i], s = sin_t[pos * half + i];
-    float2* xp = reinterpret_cast<float2*>(x + th * hd) + i;
+    float2* xp = reinterpret_cast<float2*>(x + static_cast<size_t>(t) * ld + static_cast<size_t>(hh) * hd) + i;
     const float2 v = *xp;
     float2 o;
     if (!inverse) {
@@ -153,27 +164,30 @@ __global__ void embed_bwd_kernel(const int* __restrict__ seg_tok, const int* __r
 
 }  // namespace
 
-int swiglu_fwd(Context* ctx, const float* g, const float* u, float* h, size_t n, bool round_out, cudaStream_t s) {
-  if (n == 0) return 0;
-  if ((n & 3) || !aligned16(g) || !aligned16(u) || !aligned16(h))
-    return ctx->fail(GLC_ERR_INVALID, "swiglu_fwd: size must be a multiple of 4 and pointers 16-byte aligned");
+int swiglu_fwd(Context* ctx, const float* g, const float* u, size_t ld_in, float* h, size_t ld_h, size_t rows,
+               size_t cols, bool round_out, cudaStream_t s) {
+  if (rows == 0 || cols == 0) return 0;
+  if ((cols & 3) || (ld_in & 3) || (ld_h & 3) || !aligned16(g) || !aligned16(u) || !aligned16(h))
+    return ctx->fail(GLC_ERR_INVALID, "swiglu_fwd: sizes and strides must be multiples of 4, pointers 16-byte aligned");
+  const size_t n = rows * cols;
   ProfScope prof(ctx, PROF_SWIGLU, 12.0 * n, s);
-  swiglu_fwd_kernel<<<grid_for(n / 4, 256, ctx->num_sms), 256, 0, s>>>(
-      reinterpret_cast<const float4*>(g), reinterpret_cast<const float4*>(u), reinterpret_cast<float4*>(h), n / 4,
-      round_out ? 1 : 0);
+  swiglu_fwd_kernel<<<grid_for(n / 4, 256, ctx->num_sms), 256, 0, s>>>(g, u, ld_in, h, ld_h, rows, cols / 4,
+                                                                       round_out ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "swiglu_fwd");
   return 0;
 }
 
-int swiglu_bwd(Context* ctx, const float* g, const float* u, const float* dh, float* dg, float* du, size_t n,
-               bool accumulate, bool round_out, cudaStream_t s) {
-  if (n == 0) return 0;
-  if ((n & 3) || !aligned16(g) || !aligned16(u) || !aligned16(dh) || !aligned16(dg) || !aligned16(du))
-    return ctx->fail(GLC_ERR_INVALID, "swiglu_bwd: size must be a multiple of 4 and pointers 16-byte aligned");
+int swiglu_bwd(Context* ctx, const float* g, const float* u, size_t ld_in, const float* dh, size_t ld_dh, float* dg,
+               float* du, size_t ld_out, size_t rows, size_t cols, bool accumulate, bool round_out, cudaStream_t s) {
+  if (rows == 0 || cols == 0) return 0;
+  if ((cols & 3) || (ld_in & 3) || (ld_dh & 3) || (ld_out & 3) || !aligned16(g) || !aligned16(u) || !aligned16(dh) ||
+      !aligned16(dg) || !aligned16(du))
+    return ctx->fail(GLC_ERR_INVALID, "swiglu_bwd: sizes and strides must be multiples of 4, pointers 16-byte aligned");
+  const size_t n = rows * cols;
   ProfScope prof(ctx, PROF_SWIGLU, (accumulate ? 28.0 : 20.0) * n, s);
-  swiglu_bwd_kernel<<<grid_for(n / 4, 256, ctx->num_sms), 256, 0, s>>>(
-      reinterpret_cast<const float4*>(g), reinterpret_cast<const float4*>(u), reinterpret_cast<const float4*>(dh),
-      reinterpret_cast<float4*>(dg), reinterpret_cast<float4*>(du), n / 4, accumulate ? 1 : 0, round_out ? 1 : 0);
+  swiglu_bwd_kernel<<<grid_for(n / 4, 256, ctx->num_sms), 256, 0, s>>>(g, u, ld_in, dh, ld_dh, dg, du, ld_out, rows,
+                                                                       cols / 4, accumulate ? 1 : 0,
+                                                                       round_out ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "swiglu_bwd");
   return 0;
 }
@@ -205,16 +219,16 @@ int round_copy(Context* ctx, const float* src, float* dst, size_t n, cudaStream_
   return 0;
 }
 
-int rope(Context* ctx, float* x, int T, int S, int nh, int hd, const float* cos_t, const float* sin_t, bool inverse,
-         bool round_out, cudaStream_t s) {
+int rope(Context* ctx, float* x, int ld, int T, int S, int nh, int hd, const float* cos_t, const float* sin_t,
+         bool inverse, bool round_out, cudaStream_t s) {
   if (T == 0) return 0;
-  if (T < 0 || S <= 0 || nh <= 0 || hd <= 0 || (hd & 1) || !x || !cos_t || !sin_t ||
+  if (T < 0 || S <= 0 || nh <= 0 || hd <= 0 || (hd & 1) || (ld & 1) || ld < nh * hd || !x || !cos_t || !sin_t ||
       (reinterpret_cast<uintptr_t>(x) & 7))
     return ctx->fail(GLC_ERR_INVALID, "rope: bad arguments");
   const size_t pairs = static_cast<size_t>(T) * nh * (hd / 2);
   ProfScope prof(ctx, PROF_OTHER, 16.0 * pairs, s);
-  rope_kernel<<<grid_for(pairs, 256, ctx->num_sms), 256, 0, s>>>(x, T, S, nh, hd, cos_t, sin_t, inverse ? 1 : 0,
-                                                                  round_out ? 1 : 0);
+  rope_kernel<<<grid_for(pairs, 256, ctx->num_sms), 256, 0, s>>>(x, static_cast<size_t>(ld), T, S, nh, hd, cos_t,
+                                                                  sin_t, inverse ? 1 : 0, round_out ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "rope");
   return 0;
 }

@@ -18,6 +18,8 @@
 //   warps 2..5  epilogue: TMEM -> registers -> global (fp32), 1 row per thread
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
 // the main loop of tile i+1.
+#include <utility>
+
 #include "glc_internal.h"
 #include "sm100.cuh"
 
@@ -37,14 +39,26 @@ constexpr int TMEM_COLS = 2 * BN;               // two accumulators
 constexpr int NUM_THREADS = 192;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
 
-struct GemmArgs {
+// One GEMM problem of a (possibly grouped) launch.
+struct Problem {
   float* C;
   const float* R;
   int M, N, K;
   int ldc, ldr;
   int accumulate;  // C += acc
   int round_out;   // round stored values to TF32 (RN)
-  int m_tiles, n_tiles, num_tiles, k_blocks;
+  int a_mn, b_mn;  // operand majors
+  int m_tiles, n_tiles, k_blocks, tiles;
+};
+
+// Up to two independent problems share one persistent launch: their tiles
+// form one index space (problem 0 first), so the two GEMMs of a MatMulGrad
+// GradFn (dA and dB) fill the machine together instead of each leaving a
+// partial last wave.
+struct GroupArgs {
+  Problem p[2];
+  int nprob;
+  int total_tiles;
   int* err;
 };
 
@@ -54,33 +68,41 @@ struct GemmArgs {
 //   MN-major: 4 KB chunks of 32 K-rows x 32 MN-elements (32-byte-chunk
 //             swizzle), 4-row K groups 512 B apart, chunks 4 KB apart (LBO);
 //             a k-step (8 K-rows) advances 1 KB.
-template <bool MN>
-__device__ __forceinline__ uint64_t operand_desc(uint32_t tile_saddr, int kk) {
-  if constexpr (MN) {
-    return umma_sdesc(tile_saddr + kk * 1024, /*LBO: MN chunk stride*/ BK * 128, /*SBO: 4-row K group*/ 512,
-                      UMMA_LAYOUT_SW128_BASE32B);
-  } else {
-    return umma_sdesc(tile_saddr + kk * 32, /*LBO unused*/ 16, /*SBO: 8 rows*/ 1024, UMMA_LAYOUT_SW128);
-  }
+__device__ __forceinline__ uint64_t operand_desc(bool mn, uint32_t tile_saddr, int kk) {
+  return mn ? umma_sdesc(tile_saddr + kk * 1024, /*LBO: MN chunk stride*/ BK * 128, /*SBO*/ 512,
+                         UMMA_LAYOUT_SW128_BASE32B)
+            : umma_sdesc(tile_saddr + kk * 32, /*LBO unused*/ 16, /*SBO: 8 rows*/ 1024, UMMA_LAYOUT_SW128);
 }
 
-template <bool MN, int ROWS>
-__device__ __forceinline__ void load_operand(void* sdst, const CUtensorMap* tm, uint64_t* bar, int mn0, int k0) {
-  if constexpr (MN) {
+__device__ __forceinline__ void load_operand(bool mn, int rows, void* sdst, const CUtensorMap* tm, uint64_t* bar,
+                                             int mn0, int k0) {
+  if (mn) {
     // tensor map dims {MN, K}, box {32, BK}: one 4 KB chunk per 32 MN-elements
-#pragma unroll
-    for (int c = 0; c < ROWS / 32; ++c)
+    for (int c = 0; c < rows / 32; ++c)
       tma_load_2d(static_cast<uint8_t*>(sdst) + c * (BK * 128), tm, bar, mn0 + 32 * c, k0);
   } else {
-    // tensor map dims {K, MN}, box {BK, ROWS}
+    // tensor map dims {K, MN}, box {BK, rows}
     tma_load_2d(sdst, tm, bar, k0, mn0);
   }
 }
 
-template <bool A_MN, bool B_MN>
+struct TileRef {
+  int prob, m0, n0;
+};
+__device__ __forceinline__ TileRef locate(const GroupArgs& a, int tile) {
+  TileRef t;
+  t.prob = (tile < a.p[0].tiles) ? 0 : 1;
+  const int lt = t.prob ? tile - a.p[0].tiles : tile;
+  const Problem& p = a.p[t.prob];
+  t.m0 = (lt % p.m_tiles) * BM;
+  t.n0 = (lt / p.m_tiles) * BN;
+  return t;
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmArgs args) {
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
+                     const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
+                     const GroupArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -106,8 +128,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmA0);
+    tma_prefetch_desc(&tmB0);
+    if (args.nprob > 1) {
+      tma_prefetch_desc(&tmA1);
+      tma_prefetch_desc(&tmB1);
+    }
   }
   if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
   tc_fence_before();
@@ -120,12 +146,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int in_flight = 0;  // stages issued whose full barrier we have not seen consumed
+      int in_flight = 0;  // stages issued (capped at STAGES) for the abort drain
       bool ok = true;
-      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % args.m_tiles) * BM;
-        const int n0 = (tile / args.m_tiles) * BN;
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+      for (int tile = blockIdx.x; tile < args.total_tiles && ok; tile += gridDim.x) {
+        const TileRef t = locate(args, tile);
+        const Problem& p = args.p[t.prob];
+        const CUtensorMap* tmA = t.prob ? &tmA1 : &tmA0;
+        const CUtensorMap* tmB = t.prob ? &tmB1 : &tmB0;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, args.err, GLC_DEV_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
@@ -133,8 +161,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* sA = smem + stage * STAGE_BYTES;
           uint8_t* sB = sA + A_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
-          load_operand<A_MN, BM>(sA, &tmA, &full_bar[stage], m0, kb * BK);
-          load_operand<B_MN, BN>(sB, &tmB, &full_bar[stage], n0, kb * BK);
+          load_operand(p.a_mn, BM, sA, tmA, &full_bar[stage], t.m0, kb * BK);
+          load_operand(p.b_mn, BN, sB, tmB, &full_bar[stage], t.n0, kb * BK);
           in_flight = in_flight < STAGES ? in_flight + 1 : STAGES;
           if (++stage == STAGES) {
             stage = 0;
@@ -152,26 +180,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             s = STAGES - 1;
             ph ^= 1;
           }
-          const uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(&full_bar[s], ph)) {
-            if (globaltimer_ns() - t0 > 1000000000ull) {
-              atomicCAS(args.err, 0, GLC_DEV_TIMEOUT_DRAIN);
-              break;
-            }
-          }
+          mbar_drain(&full_bar[s], ph, args.err);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_tf32(BM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
       bool issued_any = false;
-      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int tile = blockIdx.x; tile < args.total_tiles && ok; tile += gridDim.x, ++local) {
+        const TileRef t = locate(args, tile);
+        const Problem& p = args.p[t.prob];
+        const uint32_t idesc = umma_idesc_tf32(BM, BN, p.a_mn != 0, p.b_mn != 0);
         const int buf = local & 1;
         const uint32_t use = static_cast<uint32_t>(local >> 1);
         if (!mbar_wait(&tempty_bar[buf], (use & 1) ^ 1, abort_flag, args.err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
@@ -180,7 +204,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + buf * BN;
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag, args.err, GLC_DEV_TIMEOUT_MMA_FULL)) {
             ok = false;
             break;
@@ -190,7 +214,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t sB = sA + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-            umma_tf32(tmem_d, operand_desc<A_MN>(sA, kk), operand_desc<B_MN>(sB, kk), idesc,
+            umma_tf32(tmem_d, operand_desc(p.a_mn, sA, kk), operand_desc(p.b_mn, sB, kk), idesc,
                       (kb > 0 || kk > 0) ? 1u : 0u);
           }
           issued_any = true;
@@ -206,33 +230,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!ok && issued_any) {
         // Abort path: make sure no MMA is still writing TMEM before dealloc.
         umma_commit(drain_bar);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(drain_bar, 0)) {
-          if (globaltimer_ns() - t0 > 1000000000ull) {
-            atomicCAS(args.err, 0, GLC_DEV_TIMEOUT_DRAIN);
-            break;
-          }
-        }
+        mbar_drain(drain_bar, 0, args.err);
       }
     }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
-    const bool vec_ok = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15) == 0) &&
-                        (args.R == nullptr ||
-                         (((args.ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.R) & 15) == 0)));
     int local = 0;
-    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++local) {
+    for (int tile = blockIdx.x; tile < args.total_tiles; tile += gridDim.x, ++local) {
+      const TileRef t = locate(args, tile);
+      const Problem& p = args.p[t.prob];
+      const bool vec_ok = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                          (p.R == nullptr || (((p.ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.R) & 15) == 0)));
       const int buf = local & 1;
       const uint32_t use = static_cast<uint32_t>(local >> 1);
       // warp-uniform outcome: the TMEM loads below are warp-collective
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull_bar[buf], use & 1, abort_flag, args.err, GLC_DEV_TIMEOUT_EPILOGUE)))
         break;
       tc_fence_after();
-      const int m0 = (tile % args.m_tiles) * BM;
-      const int n0 = (tile / args.m_tiles) * BN;
-      const int row = m0 + row_in_tile;
+      const int row = t.m0 + row_in_tile;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
 #pragma unroll 1
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
@@ -244,16 +261,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_fence_before();
           mbar_arrive(&tempty_bar[buf]);
         }
-        const int col0 = n0 + chunk * 32;
-        if (row >= args.M || col0 >= args.N) continue;
-        float* crow = args.C + static_cast<size_t>(row) * args.ldc + col0;
-        const float* rrow = args.R ? args.R + static_cast<size_t>(row) * args.ldr + col0 : nullptr;
-        if (vec_ok && col0 + 32 <= args.N) {
+        const int col0 = t.n0 + chunk * 32;
+        if (row >= p.M || col0 >= p.N) continue;
+        float* crow = p.C + static_cast<size_t>(row) * p.ldc + col0;
+        const float* rrow = p.R ? p.R + static_cast<size_t>(row) * p.ldr + col0 : nullptr;
+        if (vec_ok && col0 + 32 <= p.N) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             float4 v = make_float4(__uint_as_float(r[4 * j + 0]), __uint_as_float(r[4 * j + 1]),
                                    __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-            if (args.accumulate) {
+            if (p.accumulate) {
               const float4 c = reinterpret_cast<const float4*>(crow)[j];
               v.x += c.x; v.y += c.y; v.z += c.z; v.w += c.w;
             }
@@ -261,20 +278,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               const float4 c = reinterpret_cast<const float4*>(rrow)[j];
               v.x += c.x; v.y += c.y; v.z += c.z; v.w += c.w;
             }
-            if (args.round_out) {
+            if (p.round_out) {
               v.x = round_tf32(v.x); v.y = round_tf32(v.y); v.z = round_tf32(v.z); v.w = round_tf32(v.w);
             }
             reinterpret_cast<float4*>(crow)[j] = v;
           }
         } else {
-          const int lim = min(32, args.N - col0);
+          const int lim = min(32, p.N - col0);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             if (j < lim) {
               float v = __uint_as_float(r[j]);
-              if (args.accumulate) v += crow[j];
+              if (p.accumulate) v += crow[j];
               if (rrow) v += rrow[j];
-              if (args.round_out) v = round_tf32(v);
+              if (p.round_out) v = round_tf32(v);
               crow[j] = v;
             }
           }
@@ -316,62 +333,92 @@ int encode_operand(Context* ctx, CUtensorMap* tm, const float* ptr, int ld, bool
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 }
 
-template <bool A_MN, bool B_MN>
-int launch(Context* ctx, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t s) {
-  static bool attr_set[8] = {false};
-  const int dev = ctx->device;
-  auto kern = gemm_tf32_kernel<A_MN, B_MN>;
-  if (!attr_set[dev & 7]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return ctx->fail_cuda(e, "cudaFuncSetAttribute(gemm_tf32)");
-    attr_set[dev & 7] = true;
+int prepare(Context* ctx, const GemmSpec& g, Problem* p, CUtensorMap* ta, CUtensorMap* tb) {
+  if (g.M < 0 || g.N < 0 || g.K <= 0) return ctx->fail(GLC_ERR_INVALID, "gemm: bad size");
+  if (!g.A.ptr || !g.B.ptr || !g.C) return ctx->fail(GLC_ERR_INVALID, "gemm: null pointer");
+  if ((g.A.ld & 3) || (g.B.ld & 3) || (reinterpret_cast<uintptr_t>(g.A.ptr) & 15) ||
+      (reinterpret_cast<uintptr_t>(g.B.ptr) & 15))
+    return ctx->fail(GLC_ERR_INVALID, "gemm: operand leading dimensions must be multiples of 4 floats and 16-byte aligned");
+  if (encode_operand(ctx, ta, g.A.ptr, g.A.ld, g.A.mn_major, g.M, g.K, BM) != 0)
+    return ctx->fail(GLC_ERR_INVALID, "gemm: cuTensorMapEncodeTiled failed for A");
+  if (encode_operand(ctx, tb, g.B.ptr, g.B.ld, g.B.mn_major, g.N, g.K, BN) != 0)
+    return ctx->fail(GLC_ERR_INVALID, "gemm: cuTensorMapEncodeTiled failed for B");
+  p->C = g.C;
+  p->R = g.R;
+  p->M = g.M;
+  p->N = g.N;
+  p->K = g.K;
+  p->ldc = g.ldc;
+  p->ldr = g.ldr;
+  p->accumulate = g.accumulate ? 1 : 0;
+  p->round_out = g.round_out ? 1 : 0;
+  p->a_mn = g.A.mn_major ? 1 : 0;
+  p->b_mn = g.B.mn_major ? 1 : 0;
+  p->m_tiles = (g.M + BM - 1) / BM;
+  p->n_tiles = (g.N + BN - 1) / BN;
+  p->k_blocks = (g.K + BK - 1) / BK;
+  p->tiles = p->m_tiles * p->n_tiles;
+  return 0;
+}
+
+}  // namespace
+
+int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t stream) {
+  if (n < 1 || n > 2) return ctx->fail(GLC_ERR_INVALID, "gemm: 1 or 2 problems per launch");
+  // empty problems are finished here; K == 0 needs no tensor core
+  GemmSpec live[2];
+  int nl = 0;
+  for (int i = 0; i < n; ++i) {
+    const GemmSpec& g = specs[i];
+    if (g.M < 0 || g.N < 0 || g.K < 0) return ctx->fail(GLC_ERR_INVALID, "gemm: negative size");
+    if (g.M == 0 || g.N == 0) continue;
+    if (!g.C) return ctx->fail(GLC_ERR_INVALID, "gemm: null pointer");
+    if (g.K == 0) {
+      int rc = gemm_empty_k(ctx, g.C, g.ldc, g.M, g.N, g.accumulate, g.R, g.ldr, stream);
+      if (rc) return rc;
+      continue;
+    }
+    live[nl++] = g;
   }
-  const int grid = a.num_tiles < ctx->num_sms ? a.num_tiles : ctx->num_sms;
-  ProfScope prof(ctx, PROF_GEMM, 2.0 * a.M * a.N * static_cast<double>(a.K), s);
-  kern<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(ta, tb, a);
+  if (nl == 0) return 0;
+  // longer reductions first: their tiles take longest, so they start first
+  if (nl == 2 && live[1].K > live[0].K) std::swap(live[0], live[1]);
+  GroupArgs a{};
+  CUtensorMap tm[4];
+  for (int i = 0; i < nl; ++i) {
+    int rc = prepare(ctx, live[i], &a.p[i], &tm[2 * i], &tm[2 * i + 1]);
+    if (rc) return rc;
+  }
+  if (nl == 1) {
+    tm[2] = tm[0];
+    tm[3] = tm[1];
+    a.p[1] = a.p[0];
+    a.p[1].tiles = 0;
+  }
+  a.nprob = nl;
+  a.total_tiles = a.p[0].tiles + (nl > 1 ? a.p[1].tiles : 0);
+  a.err = ctx->d_err;
+  static bool attr_set[8] = {false};
+  if (!attr_set[ctx->device & 7]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return ctx->fail_cuda(e, "cudaFuncSetAttribute(gemm_tf32)");
+    attr_set[ctx->device & 7] = true;
+  }
+  const int grid = a.total_tiles < ctx->num_sms ? a.total_tiles : ctx->num_sms;
+  double flops = 0;
+  for (int i = 0; i < nl; ++i) flops += 2.0 * a.p[i].M * a.p[i].N * static_cast<double>(a.p[i].K);
+  ProfScope prof(ctx, PROF_GEMM, flops, stream);
+  gemm_tf32_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3], a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return ctx->fail_cuda(e, "launch gemm_tf32");
   ctx->count_launch();
   return 0;
 }
 
-}  // namespace
-
 int gemm_tf32(Context* ctx, const GemmOperand& A, const GemmOperand& B, float* C, int ldc, int M, int N, int K,
               bool accumulate, const float* R, int ldr, bool round_out, cudaStream_t stream) {
-  if (M < 0 || N < 0 || K < 0) return ctx->fail(GLC_ERR_INVALID, "gemm: negative size");
-  if (M == 0 || N == 0) return 0;
-  if (!A.ptr || !B.ptr || !C) return ctx->fail(GLC_ERR_INVALID, "gemm: null pointer");
-  if ((A.ld & 3) || (B.ld & 3) || (reinterpret_cast<uintptr_t>(A.ptr) & 15) || (reinterpret_cast<uintptr_t>(B.ptr) & 15))
-    return ctx->fail(GLC_ERR_INVALID, "gemm: operand leading dimensions must be multiples of 4 floats and 16-byte aligned");
-  if (K == 0) {
-    // empty reduction: C = (accumulate ? C : 0) + R
-    return gemm_empty_k(ctx, C, ldc, M, N, accumulate, R, ldr, stream);
-  }
-  CUtensorMap ta, tb;
-  if (encode_operand(ctx, &ta, A.ptr, A.ld, A.mn_major, M, K, BM) != 0)
-    return ctx->fail(GLC_ERR_INVALID, "gemm: cuTensorMapEncodeTiled failed for A");
-  if (encode_operand(ctx, &tb, B.ptr, B.ld, B.mn_major, N, K, BN) != 0)
-    return ctx->fail(GLC_ERR_INVALID, "gemm: cuTensorMapEncodeTiled failed for B");
-  GemmArgs a;
-  a.C = C;
-  a.R = R;
-  a.M = M;
-  a.N = N;
-  a.K = K;
-  a.ldc = ldc;
-  a.ldr = ldr;
-  a.accumulate = accumulate ? 1 : 0;
-  a.round_out = round_out ? 1 : 0;
-  a.m_tiles = (M + BM - 1) / BM;
-  a.n_tiles = (N + BN - 1) / BN;
-  a.num_tiles = a.m_tiles * a.n_tiles;
-  a.k_blocks = (K + BK - 1) / BK;
-  a.err = ctx->d_err;
-  if (!A.mn_major && !B.mn_major) return launch<false, false>(ctx, ta, tb, a, stream);
-  if (!A.mn_major && B.mn_major) return launch<false, true>(ctx, ta, tb, a, stream);
-  if (A.mn_major && B.mn_major) return launch<true, true>(ctx, ta, tb, a, stream);
-  return launch<true, false>(ctx, ta, tb, a, stream);
+  GemmSpec g{A, B, C, ldc, M, N, K, accumulate, R, ldr, round_out};
+  return gemm_tf32_group(ctx, &g, 1, stream);
 }
 
 }  // namespace glc

@@ -121,6 +121,18 @@ struct GemmOperand {
 
 int gemm_tf32(Context* ctx, const GemmOperand& A, const GemmOperand& B, float* C, int ldc, int M, int N, int K,
               bool accumulate, const float* R, int ldr, bool round_out, cudaStream_t stream);
+// One GEMM C[M,N] (+)= A . B^T (+ R) of a grouped launch.
+struct GemmSpec {
+  GemmOperand A, B;
+  float* C;
+  int ldc, M, N, K;
+  bool accumulate;
+  const float* R;
+  int ldr;
+  bool round_out;
+};
+// Runs up to two independent GEMMs in one persistent launch (shared tile queue).
+int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t stream);
 int gemm_empty_k(Context* ctx, float* C, int ldc, int M, int N, bool accumulate, const float* R, int ldr,
                  cudaStream_t stream);
 
@@ -131,28 +143,47 @@ int rmsnorm_fwd(Context* ctx, const float* x, const float* w, float* y, float* r
 int rmsnorm_bwd(Context* ctx, const float* x, const float* w, const float* rms, const float* dy, float* dx,
                 float* dx_round, float* dw, int rows, int cols, bool full, bool dx_accumulate, bool dw_accumulate,
                 float* scratch, size_t scratch_bytes, cudaStream_t s);
-int swiglu_fwd(Context* ctx, const float* g, const float* u, float* h, size_t n, bool round_out, cudaStream_t s);
-int swiglu_bwd(Context* ctx, const float* g, const float* u, const float* dh, float* dg, float* du, size_t n,
-               bool accumulate, bool round_out, cudaStream_t s);
+// rows x cols, each operand with its own row stride (elements; multiples of 4).
+int swiglu_fwd(Context* ctx, const float* g, const float* u, size_t ld_in, float* h, size_t ld_h, size_t rows,
+               size_t cols, bool round_out, cudaStream_t s);
+int swiglu_bwd(Context* ctx, const float* g, const float* u, size_t ld_in, const float* dh, size_t ld_dh, float* dg,
+               float* du, size_t ld_out, size_t rows, size_t cols, bool accumulate, bool round_out, cudaStream_t s);
 int fill(Context* ctx, float* p, float v, size_t n, cudaStream_t s);
 int round_copy(Context* ctx, const float* src, float* dst, size_t n, cudaStream_t s);
 int add_inplace(Context* ctx, float* dst, const float* src, size_t n, cudaStream_t s);
-int rope(Context* ctx, float* x, int T, int S, int nh, int hd, const float* cos_t, const float* sin_t, bool inverse,
-         bool round_out, cudaStream_t s);
+// x: T rows of row stride ld (elements); the first nh*hd columns are rotated.
+int rope(Context* ctx, float* x, int ld, int T, int S, int nh, int hd, const float* cos_t, const float* sin_t,
+         bool inverse, bool round_out, cudaStream_t s);
 int embed_fwd(Context* ctx, const int64_t* tok, const float* E, const float* P, float* out, int T, int S, int d, int V,
               cudaStream_t s);
 int embed_bwd(Context* ctx, const int* seg_tok, const int* seg_start, const int* order, int nseg, const float* dh,
               float* dE, int d, cudaStream_t s);
 int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, int V, float scale, float* row_logp,
                float* loss, bool write_grad, bool round_out, cudaStream_t s);
-int attention_fwd(Context* ctx, const float* q, const float* k, const float* v, float* o, float* lse, int B, int S,
-                  int H, int Hkv, int hd, bool round_out, cudaStream_t s);
+// q/k/v (and their gradients) may be column slices of one fused projection
+// output: each has its own row stride in elements.
+struct AttnIO {
+  const float* q;
+  int q_ld;
+  const float* k;
+  int k_ld;
+  const float* v;
+  int v_ld;
+  float* dq;
+  int dq_ld;
+  float* dk;
+  int dk_ld;
+  float* dv;
+  int dv_ld;
+};
+// o: [B*S, H*hd] contiguous; lse: [B, H, S].
+int attention_fwd(Context* ctx, const AttnIO& io, float* o, float* lse, int B, int S, int H, int Hkv, int hd,
+                  bool round_out, cudaStream_t s);
 // partial: 2*B*S*H*hd floats of scratch for per-query-head dK/dV partials
 // (attention_bwd_partial_floats); nullptr makes each CTA loop over its KV
-// head's query-head group instead (no scratch beyond D).
-int attention_bwd(Context* ctx, const float* q, const float* k, const float* v, const float* o, const float* lse,
-                  const float* dO, float* dq, float* dk, float* dv, float* D, float* partial, int B, int S, int H,
-                  int Hkv, int hd, bool round_dv, cudaStream_t s);
+// head's query-head group instead (no scratch beyond D).  dO: contiguous.
+int attention_bwd(Context* ctx, const AttnIO& io, const float* o, const float* lse, const float* dO, float* D,
+                  float* partial, int B, int S, int H, int Hkv, int hd, bool round_dv, cudaStream_t s);
 size_t attention_bwd_partial_floats(int B, int S, int H, int Hkv, int hd);
 // elems: number of gradient elements the segments cover (for the profiler).
 int grad_norm(Context* ctx, const float* grads, const int64_t* segs, int nseg, float max_norm, double* norm_out,

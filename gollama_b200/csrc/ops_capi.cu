@@ -25,19 +25,20 @@ int glc_rmsnorm_bwd(glc_ctx* ctx, const float* x, const float* w, const float* r
 
 int glc_swiglu_fwd(glc_ctx* ctx, const float* gate, const float* up, float* h, size_t n, int round_out) {
   if (!ctx) return GLC_ERR_INVALID;
-  return glc::swiglu_fwd(C_(ctx), gate, up, h, n, round_out != 0, C_(ctx)->stream);
+  return glc::swiglu_fwd(C_(ctx), gate, up, n, h, n, 1, n, round_out != 0, C_(ctx)->stream);
 }
 
 int glc_swiglu_bwd(glc_ctx* ctx, const float* gate, const float* up, const float* dh, float* dgate, float* dup,
                    size_t n, int accumulate, int round_out) {
   if (!ctx) return GLC_ERR_INVALID;
-  return glc::swiglu_bwd(C_(ctx), gate, up, dh, dgate, dup, n, accumulate != 0, round_out != 0, C_(ctx)->stream);
+  return glc::swiglu_bwd(C_(ctx), gate, up, n, dh, n, dgate, dup, n, 1, n, accumulate != 0, round_out != 0,
+                         C_(ctx)->stream);
 }
 
 int glc_rope(glc_ctx* ctx, float* x, int T, int S, int nh, int hd, const float* cos_t, const float* sin_t, int inverse,
              int round_out) {
   if (!ctx) return GLC_ERR_INVALID;
-  return glc::rope(C_(ctx), x, T, S, nh, hd, cos_t, sin_t, inverse != 0, round_out != 0, C_(ctx)->stream);
+  return glc::rope(C_(ctx), x, nh * hd, T, S, nh, hd, cos_t, sin_t, inverse != 0, round_out != 0, C_(ctx)->stream);
 }
 
 int glc_rope_table(int hd, int max_seq, float theta, float* cos_host, float* sin_host) {
@@ -49,7 +50,8 @@ int glc_rope_table(int hd, int max_seq, float theta, float* cos_host, float* sin
 int glc_attention_fwd(glc_ctx* ctx, const float* q, const float* k, const float* v, float* o, float* lse, int B,
                       int S, int H, int Hkv, int hd, int round_out) {
   if (!ctx) return GLC_ERR_INVALID;
-  return glc::attention_fwd(C_(ctx), q, k, v, o, lse, B, S, H, Hkv, hd, round_out != 0, C_(ctx)->stream);
+  const glc::AttnIO io{q, H * hd, k, Hkv * hd, v, Hkv * hd, nullptr, 0, nullptr, 0, nullptr, 0};
+  return glc::attention_fwd(C_(ctx), io, o, lse, B, S, H, Hkv, hd, round_out != 0, C_(ctx)->stream);
 }
 
 int glc_attention_bwd(glc_ctx* ctx, const float* q, const float* k, const float* v, const float* o, const float* lse,
@@ -62,8 +64,8 @@ int glc_attention_bwd(glc_ctx* ctx, const float* q, const float* k, const float*
   if (rc) return rc;
   float* D = static_cast<float*>(ws);
   float* partial = np ? D + ((nd + 63) & ~size_t(63)) : nullptr;
-  return glc::attention_bwd(C_(ctx), q, k, v, o, lse, dO, dq, dk, dv, D, partial, B, S, H, Hkv, hd, round_dv != 0,
-                            C_(ctx)->stream);
+  const glc::AttnIO io{q, H * hd, k, Hkv * hd, v, Hkv * hd, dq, H * hd, dk, Hkv * hd, dv, Hkv * hd};
+  return glc::attention_bwd(C_(ctx), io, o, lse, dO, D, partial, B, S, H, Hkv, hd, round_dv != 0, C_(ctx)->stream);
 }
 
 int glc_softmax_ce(glc_ctx* ctx, float* logits, const int64_t* targets, int rows, int V, float scale, float* row_logp,

@@ -146,6 +146,9 @@ struct Node {
   std::function<void()> grad_fn;
   std::vector<Node*> parents;
   int param = -1;
+  // A view over several adjacent parameters (WQ|WK|WV, WGate|WUp): one GEMM
+  // operand whose gradient is the gradients of all of them.
+  std::vector<int> group;
   int64_t numel() const { return rows * cols; }
 };
 
@@ -241,6 +244,7 @@ struct Model {
   std::vector<char> grad_allocated, grad_live;
   float *cos_t = nullptr, *sin_t = nullptr;  // RoPE tables [max_seq][hd/2]
   std::vector<Node> param_nodes;
+  std::vector<Node> qkv_view, gu_view;  // per layer: WQ|WK|WV and WGate|WUp
 
   int num_params() const { return static_cast<int>(offset.size()); }
   int front() const { return llama ? 1 : 2; }
@@ -272,6 +276,27 @@ struct Model {
     }
   }
   Node* P(int i) { return &param_nodes[i]; }
+  void bind_views() {
+    auto view = [&](int first, int count) {
+      Node n;
+      n.data = params + offset[first];
+      n.grad = grads + offset[first];
+      n.gemm_data = shadow + offset[first];
+      n.cols = cols[first];
+      for (int i = 0; i < count; ++i) {
+        n.rows += rows[first + i];
+        n.group.push_back(first + i);
+      }
+      n.require_grad = true;
+      return n;
+    };
+    qkv_view.clear();
+    gu_view.clear();
+    for (int l = 0; l < cfg.num_layers; ++l) {
+      qkv_view.push_back(view(lp(l, P_WQ), 3));
+      gu_view.push_back(view(lp(l, P_WGATE), 2));
+    }
+  }
 
   // ------------------------------------------------------------ tape ops
   // MatMulGrad (grad.go:81-155): out = a . w^T; with `residual`, the AddGrad
@@ -306,17 +331,20 @@ struct Model {
         }
       }
       const float* dY = t->gemm_grad(out);
+      // dA = dC . B and dB = dC^T . A (grad.go:102-152) in one grouped launch
+      GemmSpec g[2];
+      int n = 0;
       if (a->require_grad) {
         const bool acc = t->prepare_grad(a);
-        ck(gemm_tf32(ctx, {dY, N, false}, {w->gemm_data, K, true}, a->grad, K, M, K, N, acc, nullptr, 0,
-                     round_dx && !acc, t->stream()));
-        if (round_dx && !acc) a->grad_round = a->grad;
+        const bool rnd = round_dx && !acc;
+        g[n++] = GemmSpec{{dY, N, false}, {w->gemm_data, K, true}, a->grad, K, M, K, N, acc, nullptr, 0, rnd};
+        if (rnd) a->grad_round = a->grad;
       }
       if (w->require_grad) {
         const bool acc = t->prepare_grad(w);
-        ck(gemm_tf32(ctx, {dY, N, true}, {a->gemm_data, K, true}, w->grad, K, N, K, M, acc, nullptr, 0, false,
-                     t->stream()));
+        g[n++] = GemmSpec{{dY, N, true}, {a->gemm_data, K, true}, w->grad, K, N, K, M, acc, nullptr, 0, false};
       }
+      if (n) ck(gemm_tf32_group(ctx, g, n, t->stream()));
     };
     return out;
   }
@@ -344,56 +372,59 @@ struct Model {
     return out;
   }
 
-  // forwardAttention (trainer.go:323-389) without its projections; Llama
+  // forwardAttention (trainer.go:323-389) without its projections, on the
+  // fused projection output qkv = [q | k | v] ([T, H*hd + 2*Hkv*hd]); Llama
   // semantics add RoPE on q and k (in place) and a GradFn.
-  Node* attention(Tape& tp, Node* q, Node* k, Node* v, int B, int S) {
+  Node* attention(Tape& tp, Node* qkv, int B, int S) {
     const int H = cfg.num_heads, Hkv = kvh, T = B * S;
+    const int ld = static_cast<int>(qkv->cols), qw = H * hd, kw = Hkv * hd;
     if (llama) {
-      ck(rope(ctx, q->data, T, S, H, hd, cos_t, sin_t, false, true, tp.stream()));
-      ck(rope(ctx, k->data, T, S, Hkv, hd, cos_t, sin_t, false, true, tp.stream()));
+      ck(rope(ctx, qkv->data, ld, T, S, H, hd, cos_t, sin_t, false, true, tp.stream()));
+      ck(rope(ctx, qkv->data + qw, ld, T, S, Hkv, hd, cos_t, sin_t, false, true, tp.stream()));
     }
-    Node* out = tp.make(T, static_cast<int64_t>(H) * hd);
+    Node* out = tp.make(T, qw);
     out->require_grad = true;
-    out->parents = {q, k, v};
+    out->parents = {qkv};
     float* lse = tp.alloc(static_cast<int64_t>(B) * H * S);
-    ck(attention_fwd(ctx, q->data, k->data, v->data, out->data, lse, B, S, H, Hkv, hd, true, tp.stream()));
+    const AttnIO fio{qkv->data, ld, qkv->data + qw, ld, qkv->data + qw + kw, ld, nullptr, 0, nullptr, 0, nullptr, 0};
+    ck(attention_fwd(ctx, fio, out->data, lse, B, S, H, Hkv, hd, true, tp.stream()));
     out->gemm_data = out->data;
     if (!llama) return out;  // the reference attaches no GradFn (trainer.go:335-337)
     Tape* t = &tp;
-    out->grad_fn = [this, t, out, q, k, v, lse, B, S, H, Hkv, T]() {
+    out->grad_fn = [this, t, out, qkv, lse, B, S, H, Hkv, T, ld, qw, kw]() {
       if (!out->grad_live) return;
-      const bool aq = t->prepare_grad(q), ak = t->prepare_grad(k), av = t->prepare_grad(v);
-      if (aq || ak || av) throw StepError{GLC_ERR_UNSUPPORTED};  // q/k/v have no other consumers
+      if (t->prepare_grad(qkv)) throw StepError{GLC_ERR_UNSUPPORTED};  // q/k/v have no other consumers
       float* D = t->alloc(static_cast<int64_t>(B) * H * S);
       const size_t np = attention_bwd_partial_floats(B, S, H, Hkv, hd);
       float* partial = np ? t->alloc(static_cast<int64_t>(np)) : nullptr;
-      ck(attention_bwd(ctx, q->data, k->data, v->data, out->data, lse, out->grad, q->grad, k->grad, v->grad, D,
-                       partial, B, S, H, Hkv, hd, true, t->stream()));
-      ck(rope(ctx, q->grad, T, S, H, hd, cos_t, sin_t, true, true, t->stream()));
-      ck(rope(ctx, k->grad, T, S, Hkv, hd, cos_t, sin_t, true, true, t->stream()));
-      q->grad_round = q->grad;
-      k->grad_round = k->grad;
-      v->grad_round = v->grad;
+      float* g = qkv->grad;
+      const AttnIO io{qkv->data, ld, qkv->data + qw, ld, qkv->data + qw + kw, ld, g, ld, g + qw, ld, g + qw + kw, ld};
+      ck(attention_bwd(ctx, io, out->data, lse, out->grad, D, partial, B, S, H, Hkv, hd, true, t->stream()));
+      ck(rope(ctx, g, ld, T, S, H, hd, cos_t, sin_t, true, true, t->stream()));
+      ck(rope(ctx, g + qw, ld, T, S, Hkv, hd, cos_t, sin_t, true, true, t->stream()));
+      qkv->grad_round = qkv->grad;
     };
     return out;
   }
 
-  // SiLUGrad (grad.go:417-449) and the product node (trainer.go:400-422) as one node.
-  Node* swiglu(Tape& tp, Node* g, Node* u) {
-    Node* out = tp.make(g->rows, g->cols);
+  // SiLUGrad (grad.go:417-449) and the product node (trainer.go:400-422) as
+  // one node over the fused projection output gu = [gate | up] ([T, 2F]).
+  Node* swiglu(Tape& tp, Node* gu) {
+    const int64_t T = gu->rows, F = gu->cols / 2;
+    Node* out = tp.make(T, F);
     out->require_grad = true;
-    out->parents = {g, u};
-    ck(swiglu_fwd(ctx, g->data, u->data, out->data, static_cast<size_t>(g->numel()), true, tp.stream()));
+    out->parents = {gu};
+    ck(swiglu_fwd(ctx, gu->data, gu->data + F, static_cast<size_t>(2 * F), out->data, static_cast<size_t>(F),
+                  static_cast<size_t>(T), static_cast<size_t>(F), true, tp.stream()));
     out->gemm_data = out->data;
     Tape* t = &tp;
-    out->grad_fn = [this, t, out, g, u]() {
+    out->grad_fn = [this, t, out, gu, T, F]() {
       if (!out->grad_live) return;
-      const bool ag = t->prepare_grad(g), au = t->prepare_grad(u);
-      if (ag != au) throw StepError{GLC_ERR_UNSUPPORTED};
-      ck(swiglu_bwd(ctx, g->data, u->data, out->grad, g->grad, u->grad, static_cast<size_t>(g->numel()), ag, true,
-                    t->stream()));
-      g->grad_round = g->grad;
-      u->grad_round = u->grad;
+      const bool acc = t->prepare_grad(gu);
+      ck(swiglu_bwd(ctx, gu->data, gu->data + F, static_cast<size_t>(2 * F), out->grad, static_cast<size_t>(F),
+                    gu->grad, gu->grad + F, static_cast<size_t>(2 * F), static_cast<size_t>(T), static_cast<size_t>(F),
+                    acc, true, t->stream()));
+      gu->grad_round = gu->grad;
     };
     return out;
   }
@@ -443,16 +474,14 @@ struct Model {
     for (int l = 0; l < cfg.num_layers; ++l) {
       // forwardLayer (trainer.go:308-320)
       Node* n1 = rmsnorm(tp, x, P(lp(l, P_ATTN_NORM)));
-      Node* q = matmul(tp, n1, P(lp(l, P_WQ)), nullptr, true);
-      Node* k = matmul(tp, n1, P(lp(l, P_WK)), nullptr, true);
-      Node* v = matmul(tp, n1, P(lp(l, P_WV)), nullptr, true);
-      Node* att = attention(tp, q, k, v, B, S);
+      // the q, k and v projections (trainer.go:325-327) as one GEMM over WQ|WK|WV
+      Node* qkv = matmul(tp, n1, &qkv_view[l], nullptr, true);
+      Node* att = attention(tp, qkv, B, S);
       Node* x1 = matmul(tp, att, P(lp(l, P_WO)), x, false, true);
       Node* n2 = rmsnorm(tp, x1, P(lp(l, P_FFN_NORM)));
-      // forwardFFN (trainer.go:392-426)
-      Node* gate = matmul(tp, n2, P(lp(l, P_WGATE)), nullptr);
-      Node* up = matmul(tp, n2, P(lp(l, P_WUP)), nullptr);
-      Node* h = swiglu(tp, gate, up);
+      // forwardFFN (trainer.go:392-426): gate and up projections as one GEMM over WGate|WUp
+      Node* gu = matmul(tp, n2, &gu_view[l], nullptr);
+      Node* h = swiglu(tp, gu);
       x = matmul(tp, h, P(lp(l, P_WDOWN)), x1);
     }
     Node* hf = rmsnorm(tp, x, P(out_norm()));
@@ -461,6 +490,17 @@ struct Model {
 };
 
 bool Tape::prepare_grad(Node* n) {
+  if (!n->group.empty()) {
+    const bool acc = model_->grad_live[n->group[0]] != 0;
+    for (int p : n->group) {
+      if ((model_->grad_live[p] != 0) != acc) throw StepError{GLC_ERR_UNSUPPORTED};
+      model_->grad_allocated[p] = 1;
+      model_->grad_live[p] = 1;
+      model_->param_nodes[p].grad_live = true;
+    }
+    n->grad_live = true;
+    return acc;
+  }
   if (n->param >= 0) {
     model_->grad_allocated[n->param] = 1;
     const bool acc = model_->grad_live[n->param] != 0;
@@ -570,6 +610,7 @@ int Model::init(Context* c, const glc_train_config& conf) {
     cudaMemcpy(sin_t, st.data(), st.size() * sizeof(float), cudaMemcpyHostToDevice);
   }
   bind_param_nodes();
+  bind_views();
   cudaError_t e = cudaStreamSynchronize(c->stream);
   return e == cudaSuccess ? 0 : c->fail_cuda(e, "model init");
 }

@@ -114,6 +114,11 @@ GLC_API int glc_linear_bwd_dx(glc_ctx* ctx, const float* dY, const float* W, flo
 /* dW (+)= dY^T . X.  Replaces the dB loop of MatMulGrad (pkg/tensor/grad.go:118-152). */
 GLC_API int glc_linear_bwd_dw(glc_ctx* ctx, const float* dY, const float* X, float* dW, int M, int K, int N,
                       int accumulate);
+/* The whole GradFn of MatMulGrad (pkg/tensor/grad.go:94-152) in one launch:
+ * dX (+)= dY . W and dW (+)= dY^T . X share one persistent tile queue.
+ * dX or dW may be NULL when that gradient is not required. */
+GLC_API int glc_linear_bwd(glc_ctx* ctx, const float* dY, const float* X, const float* W, float* dX, float* dW, int M,
+                           int K, int N, int accumulate_dx, int accumulate_dw);
 /* General strided form of the three above: C[M,N] (+)= A . B^T (+ R) where
  * a_mn/b_mn select MN-major storage (element (i,k) at ptr[k*ld+i]) instead of
  * K-major (ptr[i*ld+k]).  round_out rounds the stored values to TF32. */

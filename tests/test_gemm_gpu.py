@@ -116,3 +116,20 @@ def test_gemm_rejects_misaligned(ctx):
     Y = ctx.empty((4, 4))
     with pytest.raises(GlcError):
         ctx.call("glc_linear_fwd", X.ptr, W.ptr, Y.ptr, 4, 6, 4, None)
+
+
+@pytest.mark.parametrize("M,K,N", [(4096, 2048, 256), (200, 72, 100), (1024, 512, 1376)])
+def test_linear_bwd_grouped(ctx, M, K, N):
+    """dX and dW of one MatMulGrad GradFn in one grouped launch."""
+    rng = np.random.default_rng(M + K)
+    G = rng.standard_normal((M, N), dtype=np.float32)
+    X = rng.standard_normal((M, K), dtype=np.float32)
+    W = rng.standard_normal((N, K), dtype=np.float32)
+    dX0 = rng.standard_normal((M, K), dtype=np.float32)
+    dG, dXa, dWa = ctx.from_numpy(G), ctx.from_numpy(X), ctx.from_numpy(W)
+    ddx, ddw = ctx.from_numpy(dX0), ctx.empty((N, K))
+    ctx.call("glc_linear_bwd", dG.ptr, dXa.ptr, dWa.ptr, ddx.ptr, ddw.ptr, M, K, N, 1, 0)
+    ctx.sync()
+    G64 = G.astype(np.float64)
+    assert rel_fro(ddx.numpy(), G64 @ W.astype(np.float64) + dX0) < TOL
+    assert rel_fro(ddw.numpy(), G64.T @ X.astype(np.float64)) < TOL
