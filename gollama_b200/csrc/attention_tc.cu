@@ -14,9 +14,9 @@
 // arithmetic with one thread per TMEM lane (row).  All waits are bounded.
 //
 // forward   CTA = (128 queries, head).  S_j = Q K_j^T into one of two TMEM
-//           buffers (the next S overlaps this softmax); P_j goes to a K-major
-//           swizzled smem tile; O (TMEM) is rescaled when the row max grows;
-//           O += P_j V_j with V as an MN-major operand.
+//           buffers (the next S overlaps this softmax); P_j replaces S_j in
+//           TMEM; O (TMEM) is rescaled when the row max grows; O += P_j V_j
+//           with V as an MN-major operand.
 // dK/dV     CTA = (128 keys, query head) or (128 keys, KV head) looping over
 //           the head group.  S^T = K Q^T, dP^T = V dO^T (64 queries per step),
 //           P^T = exp(S^T - lse), dS^T = P^T (dP^T - D) scale, dV += P^T dO,
@@ -24,6 +24,9 @@
 //           separate deterministic kernel.
 // dQ        CTA = (128 queries, head): S = Q K^T, dP = dO V^T (64 keys per
 //           step), dS as above, dQ += dS K.
+// P, P^T, dS^T and dS never touch shared memory: the math warps write them
+// back into TMEM over S (tcgen05.st) and the next MMA reads its A operand from
+// TMEM.
 #include <cfloat>
 #include <cmath>
 
@@ -63,6 +66,17 @@ __device__ __forceinline__ void tma_tile(uint8_t* dst, const CUtensorMap* tm, ui
   for (int c = 0; c < HD / 32; ++c) tma_load_2d(dst + c * R * 128, tm, bar, col0 + 32 * c, row0);
 }
 
+// 2^x by the MUFU approximation (relative error ~2^-22): P and dS are rounded
+// to TF32 (2^-11) right after, so the approximation is invisible.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Round-to-nearest TF32 (ties away from zero) of a finite value with integer
+// ops on the full-rate ALU; equal to cvt.rna.tf32.f32 for finite inputs.
+__device__ __forceinline__ uint32_t tf32_bits(float x) { return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u; }
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, float c, float d) {
   asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
@@ -77,12 +91,17 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, fl
   }
 
 // ===================================================================== forward
+// TMEM: three S/P buffers (cols 0, 128, 256) and O (cols 384..384+HD).  The
+// softmax threads overwrite S_j with P_j in place; O += P_j V_j reads P as an
+// A operand straight from TMEM.  With three buffers, S_{j+2} is computed while
+// the softmax works on S_{j+1} and PV_j runs.
 template <int HD>
 struct FwdLayout {
-  static constexpr int Q = 128 * HD * 4, K = 128 * HD * 4, V = 128 * HD * 4, P = 128 * 128 * 4;
-  static constexpr int OFF_K = Q, OFF_V = OFF_K + 2 * K, OFF_P = OFF_V + 2 * V, OFF_BAR = OFF_P + P;
+  static constexpr int Q = 128 * HD * 4, K = 128 * HD * 4, V = 128 * HD * 4;
+  static constexpr int OFF_K = Q, OFF_V = OFF_K + 2 * K, OFF_BAR = OFF_V + 2 * V;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;
-  static constexpr int TMEM_COLS = 512;  // S0 [0,128) S1 [128,256) O [256, 256+HD)
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int O_COL = 384;
 };
 
 template <int HD>
@@ -95,8 +114,8 @@ __global__ void __launch_bounds__(NT, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
   uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = bars + 3, *v_full = bars + 5, *v_empty = bars + 7,
-           *s_full = bars + 9, *s_free = bars + 11, *p_full = bars + 13, *p_empty = bars + 14, *drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+           *s_full = bars + 9, *p_full = bars + 12, *pv_done = bars + 15, *drain = bars + 18;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const Roles ro;
   const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // longest rows first
@@ -111,11 +130,12 @@ __global__ void __launch_bounds__(NT, 1)
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(p_empty, 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -125,7 +145,7 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t sQ = smem_u32(sm), sK = sQ + L::OFF_K, sV = sQ + L::OFF_V, sP = sQ + L::OFF_P;
+  const uint32_t sQ = smem_u32(sm), sK = sQ + L::OFF_K, sV = sQ + L::OFF_V;
 
   if (ro.warp == 0) {
     if (ro.lane == 0) {
@@ -159,37 +179,39 @@ __global__ void __launch_bounds__(NT, 1)
       constexpr uint32_t idesc_o = umma_idesc_tf32(128, HD, false, true);
       bool ok = mbar_wait(q_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
       bool issued = false;
+      // S_j = Q K_j^T into buffer j % 3, whose previous P (tile j-3) must be consumed
       auto issue_s = [&](int j) -> bool {
-        const int sb = j & 1;
-        if (!mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) return false;
-        if (!mbar_wait(&k_full[sb], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) return false;
+        const int sb = j % 3, st = j & 1;
+        if (j >= 3 && !mbar_wait(&pv_done[sb], ((j - 3) / 3) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM))
+          return false;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk)
-          umma_tf32(tmem + sb * 128, kdesc<128>(sQ, kk), kdesc<128>(sK + sb * L::K, kk), idesc_s, kk > 0 ? 1u : 0u);
+          umma_tf32(tmem + sb * 128, kdesc<128>(sQ, kk), kdesc<128>(sK + st * L::K, kk), idesc_s, kk > 0 ? 1u : 0u);
         issued = true;
-        umma_commit(&k_empty[sb]);
+        umma_commit(&k_empty[st]);
         umma_commit(&s_full[sb]);
         return true;
       };
       if (ok) ok = issue_s(0);
+      if (ok && n_kv > 1) ok = issue_s(1);
       for (int j = 0; ok && j < n_kv; ++j) {
-        if (j + 1 < n_kv && !issue_s(j + 1)) { ok = false; break; }
-        if (!mbar_wait(p_full, j & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        const int sb = j % 3, st = j & 1;
+        if (!mbar_wait(&p_full[sb], (j / 3) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        if (!mbar_wait(&v_full[st], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk)
-          umma_tf32(tmem + 256, kdesc<128>(sP, kk), mdesc<128>(sV + (j & 1) * L::V, kk), idesc_o,
-                    (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&v_empty[j & 1]);
-        umma_commit(p_empty);
+          umma_tf32_ts(tmem + L::O_COL, tmem + sb * 128 + kk * 8, mdesc<128>(sV + st * L::V, kk), idesc_o,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&v_empty[st]);
+        umma_commit(&pv_done[sb]);
+        if (j + 2 < n_kv && !issue_s(j + 2)) { ok = false; break; }
       }
       if (!ok && issued) {
         umma_commit(drain);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(drain, 0))
-          if (globaltimer_ns() - t0 > 1000000000ull) { atomicCAS(err, 0, GLC_DEV_TIMEOUT_DRAIN); break; }
+        mbar_drain(drain, 0, err);
       }
     }
   } else {
@@ -198,80 +220,83 @@ __global__ void __launch_bounds__(NT, 1)
     const int r = q * 32 + ro.lane;
     const int row_abs = q0 + r;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    float m = -INFINITY, l = 0.f;
+    // Lazy running max (log2 domain): P_j = 2^(s - m_used) with m_used raised
+    // only when the tile max exceeds it by more than 8, so P <= 256 and O is
+    // rescaled on few tiles; the final O / l is unchanged.
+    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1;
-      WAIT_OR_BREAK(&s_full[sb], (j >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      const int sb = j % 3;
+      WAIT_OR_BREAK(&s_full[sb], (j / 3) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
       tc_fence_after();
       const int k0 = j * 128;
       const bool diag = (j == qt);
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_addr + sb * 128 + c * 32, v);
-        tmem_ld_wait();
+      const uint32_t sa = lane_addr + sb * 128;
+      uint32_t v[128];
+      tmem_ld_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(v + 0));
+      tmem_ld_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      tmem_ld_32x32b_x32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(v + 64));
+      tmem_ld_32x32b_x32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(v + 96));
+      tmem_ld_wait();
+      float mx[8];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = k0 + c * 32 + e;
-          const bool valid = key < S && (!diag || key <= row_abs);
-          if (valid) mx = fmaxf(mx, __uint_as_float(v[e]) * scale_log2);
-        }
+      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < 128; ++e) {
+        const int key = k0 + e;
+        const bool valid = key < S && (!diag || key <= row_abs);
+        const float t = valid ? __uint_as_float(v[e]) * scale_log2 : -INFINITY;
+        v[e] = __float_as_uint(t);
+        mx[e & 7] = fmaxf(mx[e & 7], t);
       }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = exp2f(m - m_new);
-      if (j > 0) {
-        WAIT_OR_BREAK(p_empty, (j - 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      const float m_tile = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float m_new = (m_tile > m_used + 8.0f) ? m_tile : m_used;
+      const float alpha = exp2f(m_used - m_new);  // 1 unless the max was raised; 0 on the first tile
+      float sum[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum[i] = 0.f;
+#pragma unroll
+      for (int e = 0; e < 128; ++e) {
+        const uint32_t pb = tf32_bits(fast_exp2(__uint_as_float(v[e]) - m_new));
+        sum[e & 7] += __uint_as_float(pb);
+        v[e] = pb;
+      }
+      tmem_st_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(v + 0));
+      tmem_st_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      tmem_st_32x32b_x32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(v + 64));
+      tmem_st_32x32b_x32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(v + 96));
+      tmem_st_wait();
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        // O may only be rescaled once PV_{j-1} has finished accumulating into it
+        WAIT_OR_BREAK(&pv_done[(j - 1) % 3], ((j - 1) / 3) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(lane_addr + 256 + c * 32, v);
-            tmem_ld_wait();
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(lane_addr + L::O_COL + c * 32, o);
+          tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-            tmem_st_32x32b_x32(lane_addr + 256 + c * 32, v);
-          }
-          tmem_st_wait();
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st_32x32b_x32(lane_addr + L::O_COL + c * 32, o);
         }
-      }
-      float sum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_addr + sb * 128 + c * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          float pv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int key = k0 + c * 32 + g * 4 + e;
-            const bool valid = key < S && (!diag || key <= row_abs);
-            const float p = valid ? round_tf32(exp2f(__uint_as_float(v[g * 4 + e]) * scale_log2 - m_new)) : 0.f;
-            pv[e] = p;
-            sum += p;
-          }
-          st_shared_v4(sP + kmajor_sw128_offset(r, c * 32 + g * 4, 128 * 128), pv[0], pv[1], pv[2], pv[3]);
-        }
+        tmem_st_wait();
       }
       tc_fence_before();
-      mbar_arrive(&s_free[sb]);
-      fence_proxy_async_smem();
-      mbar_arrive(p_full);
-      l = l * alpha + sum;
-      m = m_new;
+      mbar_arrive(&p_full[sb]);
+      l = l * alpha + (((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7])));
+      m_used = m_new;
     }
-    if (__all_sync(0xffffffffu, ok && mbar_wait(p_empty, (n_kv - 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
+    const int last = n_kv - 1;
+    if (__all_sync(0xffffffffu, ok && mbar_wait(&pv_done[last % 3], (last / 3) & 1, abort_flag, err,
+                                                   GLC_DEV_TIMEOUT_EPILOGUE))) {
       tc_fence_after();
       const float inv = 1.0f / l;
       float* orow = out + (static_cast<size_t>(row_base) + row_abs) * (static_cast<size_t>(H) * HD) + h * HD;
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_addr + 256 + c * 32, v);
+        tmem_ld_32x32b_x32(lane_addr + L::O_COL + c * 32, v);
         tmem_ld_wait();
         if (row_abs < S) {
 #pragma unroll
@@ -286,7 +311,7 @@ __global__ void __launch_bounds__(NT, 1)
           }
         }
       }
-      if (row_abs < S) lse[(static_cast<size_t>(b) * H + h) * S + row_abs] = (m + log2f(l)) * LN2;
+      if (row_abs < S) lse[(static_cast<size_t>(b) * H + h) * S + row_abs] = (m_used + log2f(l)) * LN2;
     }
   }
   tc_fence_before();
@@ -298,15 +323,20 @@ __global__ void __launch_bounds__(NT, 1)
 }
 
 // ===================================================================== dK / dV
+// TMEM: two sets of {S^T [0,64), dP^T [64,128)} at cols 0 and 128, dV at 256,
+// dK at 256+HD.  The math warps overwrite S^T with P^T and dP^T with dS^T in
+// place; dV += P^T dO and dK += dS^T Q read them as A operands from TMEM.
+// The MMA thread issues S^T/dP^T of step i before dV/dK of step i-1, and
+// the 64-query Q/dO tiles are double-buffered.
 template <int HD>
 struct DkdvLayout {
   static constexpr int K = 128 * HD * 4, V = 128 * HD * 4;
-  static constexpr int QT = 64 * HD * 4;  // one 64-query operand tile
-  static constexpr int PT = 128 * 64 * 4; // [128 keys][64 queries]
-  static constexpr int OFF_V = K, OFF_QK = OFF_V + V, OFF_QM = OFF_QK + QT, OFF_OK = OFF_QM + QT,
-                       OFF_OM = OFF_OK + QT, OFF_P = OFF_OM + QT, OFF_DS = OFF_P + PT, OFF_BAR = OFF_DS + PT;
+  static constexpr int QT = 64 * HD * 4;    // one 64-query operand tile
+  static constexpr int STAGE = 4 * QT;      // Q (K-major), Q (MN-major), dO (K-major), dO (MN-major)
+  static constexpr int OFF_V = K, OFF_ST = OFF_V + V, OFF_LD = OFF_ST + 2 * STAGE, OFF_BAR = OFF_LD + 1024;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;
-  static constexpr int TMEM_COLS = 256;  // S^T [0,64) dP^T [64,128) dV [128,128+HD) dK [128+HD, 128+2HD)
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int DV_COL = 256, DK_COL = 256 + HD;
 };
 
 template <int HD, bool GROUP_LOOP>
@@ -321,10 +351,11 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
-  uint64_t *kv_full = bars, *qo_full = bars + 1, *qo_empty = bars + 2, *s_full = bars + 3, *s_free = bars + 4,
-           *ds_full = bars + 5, *ds_empty = bars + 6, *acc_done = bars + 7, *drain = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t *kv_full = bars, *qo_full = bars + 1, *qo_empty = bars + 3, *s_full = bars + 5, *p_full = bars + 7,
+           *set_free = bars + 9, *acc_done = bars + 11, *drain = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* stage_ld = reinterpret_cast<float*>(sm + L::OFF_LD);  // [2][lse 64 | D 64]
   const Roles ro;
   const int G = H / Hkv;
   const int kt = blockIdx.x, b = blockIdx.z;
@@ -338,12 +369,13 @@ __global__ void __launch_bounds__(NT, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(qo_full, 1);
-    mbar_init(qo_empty, 1);
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 128);
-    mbar_init(ds_full, 128);
-    mbar_init(ds_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qo_full[i], 1);
+      mbar_init(&qo_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&set_free[i], 1);
+    }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -361,21 +393,24 @@ __global__ void __launch_bounds__(NT, 1)
       mbar_arrive_expect_tx(kv_full, L::K + L::V);
       tma_tile<HD, 128>(sm, &tmK, kv_full, kh * HD, row_base + k0);
       tma_tile<HD, 128>(sm + L::OFF_V, &tmV, kv_full, kh * HD, row_base + k0);
-      int armed = -1;
+      int armed[2] = {-1, -1};
       bool ok = true;
       for (int it = 0; it < n_it; ++it) {
+        const int st = it & 1;
         const int hq = h_first + it / nq, qr = row_base + (qi0 + it % nq) * 64;
-        if (!mbar_wait(qo_empty, (it & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
-        mbar_arrive_expect_tx(qo_full, 4 * L::QT);
-        tma_tile<HD, 64>(sm + L::OFF_QK, &tmQk, qo_full, hq * HD, qr);
-        tma_tile<HD, 64>(sm + L::OFF_QM, &tmQm, qo_full, hq * HD, qr);
-        tma_tile<HD, 64>(sm + L::OFF_OK, &tmOk, qo_full, hq * HD, qr);
-        tma_tile<HD, 64>(sm + L::OFF_OM, &tmOm, qo_full, hq * HD, qr);
-        armed = it & 1;
+        if (!mbar_wait(&qo_empty[st], ((it >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx(&qo_full[st], L::STAGE);
+        uint8_t* base = sm + L::OFF_ST + st * L::STAGE;
+        tma_tile<HD, 64>(base, &tmQk, &qo_full[st], hq * HD, qr);
+        tma_tile<HD, 64>(base + L::QT, &tmQm, &qo_full[st], hq * HD, qr);
+        tma_tile<HD, 64>(base + 2 * L::QT, &tmOk, &qo_full[st], hq * HD, qr);
+        tma_tile<HD, 64>(base + 3 * L::QT, &tmOm, &qo_full[st], hq * HD, qr);
+        armed[st] = (it >> 1) & 1;
       }
       if (!ok) {
         mbar_drain(kv_full, 0, err);
-        if (armed >= 0) mbar_drain(qo_full, static_cast<uint32_t>(armed), err);
+        for (int st = 0; st < 2; ++st)
+          if (armed[st] >= 0) mbar_drain(&qo_full[st], static_cast<uint32_t>(armed[st]), err);
       }
     }
   } else if (ro.warp == 1) {
@@ -384,79 +419,88 @@ __global__ void __launch_bounds__(NT, 1)
       constexpr uint32_t idesc_a = umma_idesc_tf32(128, HD, false, true);
       bool ok = mbar_wait(kv_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
       bool issued = false;
-      for (int it = 0; ok && it < n_it; ++it) {
-        if (!mbar_wait(qo_full, it & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-        if (!mbar_wait(s_free, (it & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
-        tc_fence_after();
+      for (int it = 0; ok && it <= n_it; ++it) {
+        if (it < n_it) {
+          const int st = it & 1;
+          const uint32_t base = s0 + L::OFF_ST + st * L::STAGE;
+          if (!mbar_wait(&qo_full[st], (it >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          if (!mbar_wait(&set_free[st], ((it >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < HD / 8; ++kk) {
-          umma_tf32(tmem + 0, kdesc<128>(s0, kk), kdesc<64>(s0 + L::OFF_QK, kk), idesc_s, kk > 0 ? 1u : 0u);
-          umma_tf32(tmem + 64, kdesc<128>(s0 + L::OFF_V, kk), kdesc<64>(s0 + L::OFF_OK, kk), idesc_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < HD / 8; ++kk) {
+            umma_tf32(tmem + st * 128, kdesc<128>(s0, kk), kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
+            umma_tf32(tmem + st * 128 + 64, kdesc<128>(s0 + L::OFF_V, kk), kdesc<64>(base + 2 * L::QT, kk), idesc_s,
+                      kk > 0 ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit(&s_full[st]);
         }
-        issued = true;
-        umma_commit(s_full);
-        if (!mbar_wait(ds_full, it & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-        tc_fence_after();
+        if (it >= 1) {
+          const int pit = it - 1, ps = pit & 1;
+          const uint32_t base = s0 + L::OFF_ST + ps * L::STAGE;
+          if (!mbar_wait(&p_full[ps], (pit >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          umma_tf32(tmem + 128, kdesc<128>(s0 + L::OFF_P, kk), mdesc<64>(s0 + L::OFF_OM, kk), idesc_a, acc);
-          umma_tf32(tmem + 128 + HD, kdesc<128>(s0 + L::OFF_DS, kk), mdesc<64>(s0 + L::OFF_QM, kk), idesc_a, acc);
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t acc = (pit > 0 || kk > 0) ? 1u : 0u;
+            umma_tf32_ts(tmem + L::DV_COL, tmem + ps * 128 + kk * 8, mdesc<64>(base + 3 * L::QT, kk), idesc_a, acc);
+            umma_tf32_ts(tmem + L::DK_COL, tmem + ps * 128 + 64 + kk * 8, mdesc<64>(base + L::QT, kk), idesc_a, acc);
+          }
+          umma_commit(&set_free[ps]);
+          umma_commit(&qo_empty[ps]);
         }
-        umma_commit(qo_empty);
-        umma_commit(ds_empty);
       }
       if (ok) umma_commit(acc_done);
       if (!ok && issued) {
         umma_commit(drain);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(drain, 0))
-          if (globaltimer_ns() - t0 > 1000000000ull) { atomicCAS(err, 0, GLC_DEV_TIMEOUT_DRAIN); break; }
+        mbar_drain(drain, 0, err);
       }
     }
   } else {
     const int q = ro.warp & 3;
     const int c = q * 32 + ro.lane;  // key row within the tile
+    const int t = threadIdx.x - 64;  // 0..127 among the math threads
     const int key = k0 + c;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
+      const int st = it & 1;
       const int hq = h_first + it / nq, qbase = (qi0 + it % nq) * 64;
-      WAIT_OR_BREAK(s_full, it & 1, GLC_DEV_TIMEOUT_EPILOGUE);
-      WAIT_OR_BREAK(ds_empty, (it & 1) ^ 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      WAIT_OR_BREAK(&s_full[st], (it >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
       tc_fence_after();
-      const float* lse_row = lse + (static_cast<size_t>(b) * H + hq) * S;
-      const float* d_row = Dv + (static_cast<size_t>(b) * H + hq) * S;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sv[32], dpv[32];
-        tmem_ld_32x32b_x32(lane_addr + half * 32, sv);
-        tmem_ld_32x32b_x32(lane_addr + 64 + half * 32, dpv);
-        tmem_ld_wait();
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          float pv[4], dsv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int qq = half * 32 + g * 4 + e, qa = qbase + qq;
-            const bool valid = qa < S && key < S && key <= qa;
-            float p = 0.f, ds = 0.f;
-            if (valid) {
-              p = exp2f(__uint_as_float(sv[g * 4 + e]) * scale_log2 - lse_row[qa] * LOG2E);
-              ds = p * (__uint_as_float(dpv[g * 4 + e]) - d_row[qa]) * scale;
-            }
-            pv[e] = round_tf32(p);
-            dsv[e] = round_tf32(ds);
-          }
-          const uint32_t off = kmajor_sw128_offset(c, half * 32 + g * 4, 128 * 128);
-          st_shared_v4(s0 + L::OFF_P + off, pv[0], pv[1], pv[2], pv[3]);
-          st_shared_v4(s0 + L::OFF_DS + off, dsv[0], dsv[1], dsv[2], dsv[3]);
-        }
+      // stage lse and D of this step's 64 queries (double-buffered by step parity)
+      {
+        float* slot = stage_ld + st * 128;
+        const int qq = t & 63, qa = qbase + qq;
+        const size_t ix = (static_cast<size_t>(b) * H + hq) * S + qa;
+        slot[t] = qa < S ? (t < 64 ? lse[ix] * LOG2E : Dv[ix]) : 0.f;
       }
+      named_bar_sync(1, 128);
+      const float* lse2 = stage_ld + st * 128;
+      const float* dq = lse2 + 64;
+      const uint32_t sa = lane_addr + st * 128;
+      uint32_t sv[64], dpv[64];
+      tmem_ld_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
+      tmem_ld_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+      tmem_ld_32x32b_x32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(dpv + 0));
+      tmem_ld_32x32b_x32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(dpv + 32));
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 64; ++e) {
+        const int qa = qbase + e;
+        const bool valid = qa < S && key < S && key <= qa;
+        const float p = valid ? fast_exp2(__uint_as_float(sv[e]) * scale_log2 - lse2[e]) : 0.f;
+        const float ds = p * (__uint_as_float(dpv[e]) - dq[e]) * scale;
+        sv[e] = tf32_bits(p);
+        dpv[e] = tf32_bits(ds);
+      }
+      tmem_st_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
+      tmem_st_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+      tmem_st_32x32b_x32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(dpv + 0));
+      tmem_st_32x32b_x32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(dpv + 32));
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(s_free);
-      fence_proxy_async_smem();
-      mbar_arrive(ds_full);
+      mbar_arrive(&p_full[st]);
     }
     if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
       tc_fence_after();
@@ -468,7 +512,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll 1
         for (int cc = 0; cc < HD / 32; ++cc) {
           uint32_t v[32];
-          tmem_ld_32x32b_x32(lane_addr + 128 + part * HD + cc * 32, v);
+          tmem_ld_32x32b_x32(lane_addr + (part == 0 ? L::DV_COL : L::DK_COL) + cc * 32, v);
           tmem_ld_wait();
           if (key < S) {
             float* dst = (part == 0 ? dv_out + trow * dv_ld : dk_out + trow * dk_ld) + oh * HD + cc * 32;
@@ -520,15 +564,19 @@ __global__ void group_sum_kernel(const float* __restrict__ pk, const float* __re
 }
 
 // ===================================================================== dQ
+// TMEM: two sets of {S [0,64), dP [64,128)} at cols 0 and 128, dQ at 256.  The
+// math warps overwrite S with dS in place; dQ += dS K reads it from TMEM.  The
+// 64-key K/V tiles are double-buffered and the MMA thread issues S/dP of step
+// j before dQ of step j-1.
 template <int HD>
 struct DqLayout {
   static constexpr int Q = 128 * HD * 4, O = 128 * HD * 4;
   static constexpr int KT = 64 * HD * 4;              // one 64-key operand tile
   static constexpr int STAGE = 3 * KT;                // K (K-major), K (MN-major), V (K-major)
-  static constexpr int DS = 128 * 64 * 4;
-  static constexpr int OFF_O = Q, OFF_KV = OFF_O + O, OFF_DS = OFF_KV + 2 * STAGE, OFF_BAR = OFF_DS + DS;
+  static constexpr int OFF_O = Q, OFF_KV = OFF_O + O, OFF_BAR = OFF_KV + 2 * STAGE;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;
-  static constexpr int TMEM_COLS = 256;  // S [0,64) dP [64,128) dQ [128,128+HD)
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int DQ_COL = 256;
 };
 
 template <int HD>
@@ -542,9 +590,9 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
-  uint64_t *qo_full = bars, *kv_full = bars + 1, *kv_empty = bars + 3, *s_full = bars + 5, *s_free = bars + 6,
-           *ds_full = bars + 7, *ds_empty = bars + 8, *acc_done = bars + 9, *drain = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t *qo_full = bars, *kv_full = bars + 1, *kv_empty = bars + 3, *s_full = bars + 5, *p_full = bars + 7,
+           *set_free = bars + 9, *acc_done = bars + 11, *drain = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const Roles ro;
   const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);
@@ -558,11 +606,10 @@ __global__ void __launch_bounds__(NT, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&set_free[i], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 128);
-    mbar_init(ds_full, 128);
-    mbar_init(ds_empty, 1);
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -604,34 +651,39 @@ __global__ void __launch_bounds__(NT, 1)
       constexpr uint32_t idesc_q = umma_idesc_tf32(128, HD, false, true);
       bool ok = mbar_wait(qo_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
       bool issued = false;
-      for (int j = 0; ok && j < nk; ++j) {
-        const int st = j & 1;
-        const uint32_t base = s0 + L::OFF_KV + st * L::STAGE;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-        if (!mbar_wait(s_free, (j & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
-        tc_fence_after();
+      for (int j = 0; ok && j <= nk; ++j) {
+        if (j < nk) {
+          const int st = j & 1;
+          const uint32_t base = s0 + L::OFF_KV + st * L::STAGE;
+          if (!mbar_wait(&kv_full[st], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          if (!mbar_wait(&set_free[st], ((j >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < HD / 8; ++kk) {
-          umma_tf32(tmem + 0, kdesc<128>(s0, kk), kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
-          umma_tf32(tmem + 64, kdesc<128>(s0 + L::OFF_O, kk), kdesc<64>(base + 2 * L::KT, kk), idesc_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < HD / 8; ++kk) {
+            umma_tf32(tmem + st * 128, kdesc<128>(s0, kk), kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
+            umma_tf32(tmem + st * 128 + 64, kdesc<128>(s0 + L::OFF_O, kk), kdesc<64>(base + 2 * L::KT, kk), idesc_s,
+                      kk > 0 ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit(&s_full[st]);
         }
-        issued = true;
-        umma_commit(s_full);
-        if (!mbar_wait(ds_full, j & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-        tc_fence_after();
+        if (j >= 1) {
+          const int pj = j - 1, ps = pj & 1;
+          const uint32_t base = s0 + L::OFF_KV + ps * L::STAGE;
+          if (!mbar_wait(&p_full[ps], (pj >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_tf32(tmem + 128, kdesc<128>(s0 + L::OFF_DS, kk), mdesc<64>(base + L::KT, kk), idesc_q,
-                    (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(ds_empty);
-        umma_commit(&kv_empty[st]);
+          for (int kk = 0; kk < 8; ++kk)
+            umma_tf32_ts(tmem + L::DQ_COL, tmem + ps * 128 + kk * 8, mdesc<64>(base + L::KT, kk), idesc_q,
+                         (pj > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&set_free[ps]);
+          umma_commit(&kv_empty[ps]);
+        }
       }
       if (ok) umma_commit(acc_done);
       if (!ok && issued) {
         umma_commit(drain);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(drain, 0))
-          if (globaltimer_ns() - t0 > 1000000000ull) { atomicCAS(err, 0, GLC_DEV_TIMEOUT_DRAIN); break; }
+        mbar_drain(drain, 0, err);
       }
     }
   } else {
@@ -643,37 +695,28 @@ __global__ void __launch_bounds__(NT, 1)
     const float lse2 = lse[lrow] * LOG2E, Dq = Dv[lrow];
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
-      WAIT_OR_BREAK(s_full, j & 1, GLC_DEV_TIMEOUT_EPILOGUE);
-      WAIT_OR_BREAK(ds_empty, (j & 1) ^ 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      const int st = j & 1;
+      WAIT_OR_BREAK(&s_full[st], (j >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
       tc_fence_after();
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sv[32], dpv[32];
-        tmem_ld_32x32b_x32(lane_addr + half * 32, sv);
-        tmem_ld_32x32b_x32(lane_addr + 64 + half * 32, dpv);
-        tmem_ld_wait();
+      const uint32_t sa = lane_addr + st * 128;
+      uint32_t sv[64], dpv[64];
+      tmem_ld_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
+      tmem_ld_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+      tmem_ld_32x32b_x32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(dpv + 0));
+      tmem_ld_32x32b_x32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(dpv + 32));
+      tmem_ld_wait();
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          float dsv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int key = j * 64 + half * 32 + g * 4 + e;
-            const bool valid = qa < S && key < S && key <= qa;
-            float ds = 0.f;
-            if (valid) {
-              const float p = exp2f(__uint_as_float(sv[g * 4 + e]) * scale_log2 - lse2);
-              ds = p * (__uint_as_float(dpv[g * 4 + e]) - Dq) * scale;
-            }
-            dsv[e] = round_tf32(ds);
-          }
-          st_shared_v4(s0 + L::OFF_DS + kmajor_sw128_offset(r, half * 32 + g * 4, 128 * 128), dsv[0], dsv[1], dsv[2],
-                       dsv[3]);
-        }
+      for (int e = 0; e < 64; ++e) {
+        const int key = j * 64 + e;
+        const bool valid = qa < S && key < S && key <= qa;
+        const float p = valid ? fast_exp2(__uint_as_float(sv[e]) * scale_log2 - lse2) : 0.f;
+        sv[e] = tf32_bits(p * (__uint_as_float(dpv[e]) - Dq) * scale);
       }
+      tmem_st_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
+      tmem_st_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(s_free);
-      fence_proxy_async_smem();
-      mbar_arrive(ds_full);
+      mbar_arrive(&p_full[st]);
     }
     if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
       tc_fence_after();
@@ -681,7 +724,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll 1
       for (int cc = 0; cc < HD / 32; ++cc) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_addr + 128 + cc * 32, v);
+        tmem_ld_32x32b_x32(lane_addr + L::DQ_COL + cc * 32, v);
         tmem_ld_wait();
         if (qa < S) {
 #pragma unroll

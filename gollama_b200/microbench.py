@@ -1,0 +1,140 @@
+"""Microbenchmarks of single kernels at the TinyLlama training shapes.
+
+    python -m gollama_b200.microbench CASE [--iters N] [--warmup W]
+
+Each case allocates its operands once (seeded normal values, rounded to TF32
+where the training step feeds the tensor cores rounded operands), runs the
+kernel W times untimed and N times timed with CUDA events on the library's
+compute stream, and prints one line: case, shape, ms per launch, and TFLOP/s
+(tensor-core kernels) or GB/s (bandwidth kernels) of algorithmic work.  Used
+for ncu captures of one kernel on a bounded case.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+
+import numpy as np
+
+from .device import Context
+
+T, D, F, H, HKV, HD, S, V = 4096, 2048, 5632, 32, 4, 64, 1024, 32000
+
+
+def _tf32(x: np.ndarray) -> np.ndarray:
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    return ((b + np.uint32(0x1000)) & np.uint32(0xFFFFE000)).view(np.float32)
+
+
+def _rand(ctx, shape, seed, scale=1.0, tf32=True):
+    x = (np.random.default_rng(seed).standard_normal(shape, dtype=np.float32) * np.float32(scale))
+    return ctx.from_numpy(_tf32(x) if tf32 else x)
+
+
+def _time(ctx, fn, iters, warmup):
+    for _ in range(warmup):
+        fn()
+    ctx.sync()
+    ms = C.c_float()
+    ctx.call("glc_timer_start")
+    for _ in range(iters):
+        fn()
+    ctx.call("glc_timer_stop", C.byref(ms))
+    ctx.sync()
+    return ms.value / max(iters, 1)
+
+
+def case_gemm(ctx, kind, M, K, N, iters, warmup):
+    """kind: fwd Y=X.W^T, dx dX=dY.W, dw dW=dY^T.X, bwd (dx and dw grouped)."""
+    X, W, G = _rand(ctx, (M, K), 1), _rand(ctx, (N, K), 2), _rand(ctx, (M, N), 3)
+    Y, dX, dW = ctx.empty((M, N)), ctx.empty((M, K)), ctx.empty((N, K))
+    calls = {
+        "fwd": lambda: ctx.call("glc_linear_fwd", X.ptr, W.ptr, Y.ptr, M, K, N, None),
+        "dx": lambda: ctx.call("glc_linear_bwd_dx", G.ptr, W.ptr, dX.ptr, M, K, N, 0),
+        "dw": lambda: ctx.call("glc_linear_bwd_dw", G.ptr, X.ptr, dW.ptr, M, K, N, 0),
+        "bwd": lambda: ctx.call("glc_linear_bwd", G.ptr, X.ptr, W.ptr, dX.ptr, dW.ptr, M, K, N, 0, 0),
+    }
+    ms = _time(ctx, calls[kind], iters, warmup)
+    flops = 2.0 * M * N * K * (2 if kind == "bwd" else 1)
+    return f"gemm_{kind} M={M} K={K} N={N}", ms, flops / (ms * 1e-3) / 1e12, "TFLOP/s"
+
+
+def case_attention(ctx, kind, iters, warmup, B=4):
+    Tq = B * S
+    q, k, v = _rand(ctx, (Tq, H * HD), 4), _rand(ctx, (Tq, HKV * HD), 5), _rand(ctx, (Tq, HKV * HD), 6)
+    dO = _rand(ctx, (Tq, H * HD), 7)
+    o, lse = ctx.empty((Tq, H * HD)), ctx.empty((B, H, S))
+    dq, dk, dv = ctx.empty((Tq, H * HD)), ctx.empty((Tq, HKV * HD)), ctx.empty((Tq, HKV * HD))
+    fwd = lambda: ctx.call("glc_attention_fwd", q.ptr, k.ptr, v.ptr, o.ptr, lse.ptr, B, S, H, HKV, HD, 1)
+    fwd()
+    ctx.sync()
+    bwd = lambda: ctx.call("glc_attention_bwd", q.ptr, k.ptr, v.ptr, o.ptr, lse.ptr, dO.ptr, dq.ptr, dk.ptr, dv.ptr,
+                           B, S, H, HKV, HD, 1)
+    causal = 0.5 * S * (S + 1)
+    if kind == "fwd":
+        ms, flops = _time(ctx, fwd, iters, warmup), 4.0 * B * H * causal * HD
+    else:
+        ms, flops = _time(ctx, bwd, iters, warmup), 8.0 * B * H * causal * HD
+    return f"attention_{kind} B={B} S={S} H={H}/{HKV} hd={HD}", ms, flops / (ms * 1e-3) / 1e12, "TFLOP/s"
+
+
+def case_swiglu(ctx, iters, warmup):
+    gu = _rand(ctx, (T, 2 * F), 8, tf32=False)
+    dh = _rand(ctx, (T, F), 9, tf32=False)
+    dgu = ctx.empty((T, 2 * F))
+    n = T * F
+    ms = _time(ctx, lambda: ctx.call("glc_swiglu_bwd", gu.ptr, C.c_void_p(gu.addr + 4 * n), dh.ptr, dgu.ptr,
+                                     C.c_void_p(dgu.addr + 4 * n), n, 0, 1), iters, warmup)
+    return f"swiglu_bwd n={n}", ms, 20.0 * n / (ms * 1e-3) / 1e9, "GB/s"
+
+
+def case_rmsnorm(ctx, iters, warmup):
+    x, w, dy = _rand(ctx, (T, D), 10, tf32=False), _rand(ctx, (D,), 11, tf32=False), _rand(ctx, (T, D), 12, tf32=False)
+    y, rms = ctx.empty((T, D)), ctx.empty((T,))
+    ctx.call("glc_rmsnorm_fwd", x.ptr, w.ptr, y.ptr, rms.ptr, T, D, C.c_float(1e-5), 1)
+    dx, dxr, dw = ctx.zeros((T, D)), ctx.empty((T, D)), ctx.zeros((D,))
+    ms = _time(ctx, lambda: ctx.call("glc_rmsnorm_bwd", x.ptr, w.ptr, rms.ptr, dy.ptr, dx.ptr, dxr.ptr, dw.ptr, T, D,
+                                     1, 1, 1), iters, warmup)
+    return f"rmsnorm_bwd {T}x{D}", ms, 5.0 * 4 * T * D / (ms * 1e-3) / 1e9, "GB/s"
+
+
+def case_ce(ctx, iters, warmup):
+    logits = _rand(ctx, (T, V), 13, 2.0, tf32=False)
+    tg = ctx.from_numpy(np.random.default_rng(14).integers(0, V, T).astype(np.int64))
+    logp, loss = ctx.empty((T,)), ctx.empty((1,))
+    ms = _time(ctx, lambda: ctx.call("glc_softmax_ce", logits.ptr, tg.ptr, T, V, C.c_float(1.0 / T), logp.ptr,
+                                     loss.ptr, 0, 0), iters, warmup)
+    return f"softmax_ce {T}x{V}", ms, 4.0 * T * V / (ms * 1e-3) / 1e9, "GB/s"
+
+
+CASES = {
+    "gemm_fwd": lambda c, i, w: case_gemm(c, "fwd", T, D, D, i, w),
+    "gemm_dx": lambda c, i, w: case_gemm(c, "dx", T, D, D, i, w),
+    "gemm_dw": lambda c, i, w: case_gemm(c, "dw", T, D, D, i, w),
+    "gemm_bwd": lambda c, i, w: case_gemm(c, "bwd", T, D, D, i, w),
+    "gemm_fwd_gateup": lambda c, i, w: case_gemm(c, "fwd", T, D, 2 * F, i, w),
+    "gemm_fwd_lmhead": lambda c, i, w: case_gemm(c, "fwd", T, D, V, i, w),
+    "gemm_fwd_8192": lambda c, i, w: case_gemm(c, "fwd", 8192, 8192, 8192, i, w),
+    "attention_fwd": lambda c, i, w: case_attention(c, "fwd", i, w),
+    "attention_bwd": lambda c, i, w: case_attention(c, "bwd", i, w),
+    "swiglu_bwd": case_swiglu,
+    "rmsnorm_bwd": case_rmsnorm,
+    "softmax_ce": case_ce,
+}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("cases", nargs="+", choices=sorted(CASES) + ["all"])
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    a = ap.parse_args(argv)
+    names = sorted(CASES) if "all" in a.cases else a.cases
+    with Context(0) as ctx:
+        for n in names:
+            desc, ms, rate, unit = CASES[n](ctx, a.iters, a.warmup)
+            print(f"{n:18s} {desc:44s} {ms:9.4f} ms  {rate:9.1f} {unit}", flush=True)
+
+
+if __name__ == "__main__":
+    main()
