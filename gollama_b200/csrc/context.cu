@@ -273,6 +273,14 @@ int glc_gemm_tf32(glc_ctx* ctx, const float* A, int lda, int a_mn, const float* 
                         round_out != 0, c->stream);
 }
 
+int glc_set_gemm_variant(glc_ctx* ctx, int variant) {
+  if (!ctx) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  if (variant < 0 || variant > 2) return c->fail(GLC_ERR_INVALID, "set_gemm_variant: variant must be 0, 1 or 2");
+  c->gemm_variant = variant;
+  return GLC_OK;
+}
+
 int glc_linear_fwd(glc_ctx* ctx, const float* X, const float* W, float* Y, int M, int K, int N,
                    const float* residual) {
   if (!ctx) return GLC_ERR_INVALID;

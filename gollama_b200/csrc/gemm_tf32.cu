@@ -18,6 +18,18 @@
 //   warps 2..5  epilogue: TMEM -> registers -> global (fp32), 1 row per thread
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
 // the main loop of tile i+1.
+//
+// Two kernels share this structure:
+//   gemm_tf32_kernel       one CTA per 128x256 tile (tcgen05.mma.cta_group::1)
+//   gemm_tf32_pair_kernel  a (2,1,1) cluster per 256x256 tile
+//                          (tcgen05.mma.cta_group::2): each CTA loads 128 rows
+//                          of A and 128 rows of B, so an SM streams 32 KB of
+//                          operands per 32-deep k-block instead of 48 KB for
+//                          the same MMA work.  At full tensor rate the
+//                          single-CTA tile needs ~96 B/clk/SM from L2, near the
+//                          L2->SM limit; the pair tile needs ~64.
+// The pair kernel serves problems with M > 128; tiny ones keep the
+// single-CTA tile.
 #include <utility>
 
 #include "glc_internal.h"
@@ -89,12 +101,13 @@ __device__ __forceinline__ void load_operand(bool mn, int rows, void* sdst, cons
 struct TileRef {
   int prob, m0, n0;
 };
+template <int TILE_M>
 __device__ __forceinline__ TileRef locate(const GroupArgs& a, int tile) {
   TileRef t;
   t.prob = (tile < a.p[0].tiles) ? 0 : 1;
   const int lt = t.prob ? tile - a.p[0].tiles : tile;
   const Problem& p = a.p[t.prob];
-  t.m0 = (lt % p.m_tiles) * BM;
+  t.m0 = (lt % p.m_tiles) * TILE_M;
   t.n0 = (lt / p.m_tiles) * BN;
   return t;
 }
@@ -149,7 +162,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int in_flight = 0;  // stages issued (capped at STAGES) for the abort drain
       bool ok = true;
       for (int tile = blockIdx.x; tile < args.total_tiles && ok; tile += gridDim.x) {
-        const TileRef t = locate(args, tile);
+        const TileRef t = locate<BM>(args, tile);
         const Problem& p = args.p[t.prob];
         const CUtensorMap* tmA = t.prob ? &tmA1 : &tmA0;
         const CUtensorMap* tmB = t.prob ? &tmB1 : &tmB0;
@@ -193,7 +206,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       bool issued_any = false;
       for (int tile = blockIdx.x; tile < args.total_tiles && ok; tile += gridDim.x, ++local) {
-        const TileRef t = locate(args, tile);
+        const TileRef t = locate<BM>(args, tile);
         const Problem& p = args.p[t.prob];
         const uint32_t idesc = umma_idesc_tf32(BM, BN, p.a_mn != 0, p.b_mn != 0);
         const int buf = local & 1;
@@ -239,7 +252,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int row_in_tile = q * 32 + lane;
     int local = 0;
     for (int tile = blockIdx.x; tile < args.total_tiles; tile += gridDim.x, ++local) {
-      const TileRef t = locate(args, tile);
+      const TileRef t = locate<BM>(args, tile);
       const Problem& p = args.p[t.prob];
       const bool vec_ok = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
                           (p.R == nullptr || (((p.ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.R) & 15) == 0)));
@@ -308,6 +321,261 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------ CTA-pair kernel
+constexpr int PAIR_BM = 256;                         // cluster tile rows (128 per CTA)
+constexpr int HALF_ROWS = 128;                       // rows of A and of B each CTA loads
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = HALF_ROWS * BK * 4;        // 16 KB
+constexpr int P_B_BYTES = HALF_ROWS * BK * 4;        // 16 KB
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES; // 32 KB per CTA, 64 KB per pair
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+
+__device__ __forceinline__ void load_operand_pair(bool mn, void* sdst, const CUtensorMap* tm, uint32_t bar_cluster,
+                                                  int mn0, int k0) {
+  if (mn) {
+#pragma unroll
+    for (int c = 0; c < HALF_ROWS / 32; ++c)
+      tma_load_2d_pair(static_cast<uint8_t*>(sdst) + c * (BK * 128), tm, bar_cluster, mn0 + 32 * c, k0);
+  } else {
+    tma_load_2d_pair(sdst, tm, bar_cluster, k0, mn0);
+  }
+}
+
+// Barriers (same offsets in both CTAs):
+//   full[s]    leader only: the leader's producer arrives with expect_tx of
+//              the pair's 64 KB; both CTAs' copies complete_tx on it.  The
+//              peer's copies may land before that arrival (the transaction
+//              count goes negative meanwhile), never into an earlier phase:
+//              the peer refills stage s only after the MMA consumed it.
+//   empty[s]   both CTAs: the leader's MMA commit frees stage s in each CTA
+//   tfull[b]   both CTAs: accumulator b finished (leader's commit to each)
+//   tempty[b]  leader only: the 4 epilogue warps of each CTA released b
+//   drain      leader only: abort path, all issued MMAs finished
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_tf32_pair_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
+                          const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
+                          const GroupArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + P_STAGES;
+  uint64_t* tfull_bar = empty_bar + P_STAGES;  // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;        // [2]
+  uint64_t* drain_bar = tempty_bar + 2;        // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = static_cast<int>(blockIdx.x >> 1);
+  const int nclusters = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 2 * 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA0);
+    tma_prefetch_desc(&tmB0);
+    if (args.nprob > 1) {
+      tma_prefetch_desc(&tmA1);
+      tma_prefetch_desc(&tmB1);
+    }
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  // both CTAs' barriers exist before either CTA arrives on the other's
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producers (both CTAs)
+    if (lane == 0) {
+      const uint32_t full_leader = mapa_cluster(full_bar, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < args.total_tiles && ok; tile += nclusters) {
+        const TileRef t = locate<PAIR_BM>(args, tile);
+        const Problem& p = args.p[t.prob];
+        const CUtensorMap* tmA = t.prob ? &tmA1 : &tmA0;
+        const CUtensorMap* tmB = t.prob ? &tmB1 : &tmB0;
+        const int a_row = t.m0 + static_cast<int>(rank) * HALF_ROWS;
+        const int b_row = t.n0 + static_cast<int>(rank) * HALF_ROWS;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, args.err, GLC_DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + stage * P_STAGE_BYTES;
+          uint8_t* sB = sA + P_A_BYTES;
+          const uint32_t fb = full_leader + stage * 8;
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * P_STAGE_BYTES);
+          load_operand_pair(p.a_mn, sA, tmA, fb, a_row, kb * BK);
+          load_operand_pair(p.b_mn, sB, tmB, fb, b_row, kb * BK);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Copies signal the leader's barriers; on abort the leader waits for
+      // the stages in flight before the pair leaves (see the MMA issuer).
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (rank == 0 && lane == 0) {
+      const uint32_t empty_own = mapa_cluster(empty_bar, 0), empty_peer = mapa_cluster(empty_bar, 1);
+      const uint32_t tfull_own = mapa_cluster(tfull_bar, 0), tfull_peer = mapa_cluster(tfull_bar, 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int tile = cluster; tile < args.total_tiles && ok; tile += nclusters, ++local) {
+        const TileRef t = locate<PAIR_BM>(args, tile);
+        const Problem& p = args.p[t.prob];
+        const uint32_t idesc = umma_idesc_tf32(PAIR_BM, BN, p.a_mn != 0, p.b_mn != 0);
+        const int buf = local & 1;
+        const uint32_t use = static_cast<uint32_t>(local >> 1);
+        if (!mbar_wait(&tempty_bar[buf], (use & 1) ^ 1, abort_flag, args.err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, args.err, GLC_DEV_TIMEOUT_MMA_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sA = smem_u32(smem + stage * P_STAGE_BYTES);
+          const uint32_t sB = sA + P_A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            umma_tf32_pair(tmem_d, operand_desc(p.a_mn, sA, kk), operand_desc(p.b_mn, sB, kk), idesc,
+                           (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          // stage s is free in both CTAs once these MMAs have read it
+          umma_commit_pair(empty_own + stage * 8);
+          umma_commit_pair(empty_peer + stage * 8);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull_own + buf * 8);
+        umma_commit_pair(tfull_peer + buf * 8);
+      }
+      if (!ok) {
+        // Abort path.  (1) No MMA may still read shared memory or write TMEM
+        // of either CTA when the pair leaves.  (2) Copies the producers issued
+        // for stages not yet consumed signal this CTA's full barriers: wait
+        // for them (each wait bounded) so none lands after exit.
+        if (issued_any) {
+          umma_commit_pair(mapa_cluster(drain_bar, 0));
+          mbar_drain(drain_bar, 0, args.err);
+        }
+        for (int i = 0; i < P_STAGES; ++i) {
+          mbar_drain(&full_bar[stage], phase, args.err);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int row_in_half = q * 32 + lane;
+    const uint32_t tempty_leader = mapa_cluster(tempty_bar, 0);
+    int local = 0;
+    for (int tile = cluster; tile < args.total_tiles; tile += nclusters, ++local) {
+      const TileRef t = locate<PAIR_BM>(args, tile);
+      const Problem& p = args.p[t.prob];
+      const bool vec_ok = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                          (p.R == nullptr || (((p.ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.R) & 15) == 0)));
+      const int buf = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull_bar[buf], use & 1, abort_flag, args.err, GLC_DEV_TIMEOUT_EPILOGUE)))
+        break;
+      tc_fence_after();
+      const int row = t.m0 + static_cast<int>(rank) * HALF_ROWS + row_in_half;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + chunk * 32, r);
+        tmem_ld_wait();
+        if (chunk == BN / 32 - 1) {
+          // this warp's reads of accumulator buf are done: one arrival per warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty_leader + buf * 8);
+        }
+        const int col0 = t.n0 + chunk * 32;
+        if (row >= p.M || col0 >= p.N) continue;
+        float* crow = p.C + static_cast<size_t>(row) * p.ldc + col0;
+        const float* rrow = p.R ? p.R + static_cast<size_t>(row) * p.ldr + col0 : nullptr;
+        if (vec_ok && col0 + 32 <= p.N) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4 v = make_float4(__uint_as_float(r[4 * j + 0]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            if (p.accumulate) {
+              const float4 c = reinterpret_cast<const float4*>(crow)[j];
+              v.x += c.x; v.y += c.y; v.z += c.z; v.w += c.w;
+            }
+            if (rrow) {
+              const float4 c = reinterpret_cast<const float4*>(rrow)[j];
+              v.x += c.x; v.y += c.y; v.z += c.z; v.w += c.w;
+            }
+            if (p.round_out) {
+              v.x = round_tf32(v.x); v.y = round_tf32(v.y); v.z = round_tf32(v.z); v.w = round_tf32(v.w);
+            }
+            reinterpret_cast<float4*>(crow)[j] = v;
+          }
+        } else {
+          const int lim = min(32, p.N - col0);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (j < lim) {
+              float v = __uint_as_float(r[j]);
+              if (p.accumulate) v += crow[j];
+              if (rrow) v += rrow[j];
+              if (p.round_out) v = round_tf32(v);
+              crow[j] = v;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  // neither CTA leaves (or frees TMEM) while the other may still touch its
+  // shared memory, barriers or TMEM
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 
 int encode_operand(Context* ctx, CUtensorMap* tm, const float* ptr, int ld, bool mn, int rows_mn, int k, int box_mn) {
@@ -333,15 +601,18 @@ int encode_operand(Context* ctx, CUtensorMap* tm, const float* ptr, int ld, bool
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 }
 
-int prepare(Context* ctx, const GemmSpec& g, Problem* p, CUtensorMap* ta, CUtensorMap* tb) {
+// tile_m: rows of C per tile (BM, or PAIR_BM for the CTA pair); box_a/box_b:
+// rows of A/B one CTA loads per k-block.
+int prepare(Context* ctx, const GemmSpec& g, Problem* p, CUtensorMap* ta, CUtensorMap* tb, int tile_m, int box_a,
+            int box_b) {
   if (g.M < 0 || g.N < 0 || g.K <= 0) return ctx->fail(GLC_ERR_INVALID, "gemm: bad size");
   if (!g.A.ptr || !g.B.ptr || !g.C) return ctx->fail(GLC_ERR_INVALID, "gemm: null pointer");
   if ((g.A.ld & 3) || (g.B.ld & 3) || (reinterpret_cast<uintptr_t>(g.A.ptr) & 15) ||
       (reinterpret_cast<uintptr_t>(g.B.ptr) & 15))
     return ctx->fail(GLC_ERR_INVALID, "gemm: operand leading dimensions must be multiples of 4 floats and 16-byte aligned");
-  if (encode_operand(ctx, ta, g.A.ptr, g.A.ld, g.A.mn_major, g.M, g.K, BM) != 0)
+  if (encode_operand(ctx, ta, g.A.ptr, g.A.ld, g.A.mn_major, g.M, g.K, box_a) != 0)
     return ctx->fail(GLC_ERR_INVALID, "gemm: cuTensorMapEncodeTiled failed for A");
-  if (encode_operand(ctx, tb, g.B.ptr, g.B.ld, g.B.mn_major, g.N, g.K, BN) != 0)
+  if (encode_operand(ctx, tb, g.B.ptr, g.B.ld, g.B.mn_major, g.N, g.K, box_b) != 0)
     return ctx->fail(GLC_ERR_INVALID, "gemm: cuTensorMapEncodeTiled failed for B");
   p->C = g.C;
   p->R = g.R;
@@ -354,7 +625,7 @@ int prepare(Context* ctx, const GemmSpec& g, Problem* p, CUtensorMap* ta, CUtens
   p->round_out = g.round_out ? 1 : 0;
   p->a_mn = g.A.mn_major ? 1 : 0;
   p->b_mn = g.B.mn_major ? 1 : 0;
-  p->m_tiles = (g.M + BM - 1) / BM;
+  p->m_tiles = (g.M + tile_m - 1) / tile_m;
   p->n_tiles = (g.N + BN - 1) / BN;
   p->k_blocks = (g.K + BK - 1) / BK;
   p->tiles = p->m_tiles * p->n_tiles;
@@ -383,10 +654,17 @@ int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t str
   if (nl == 0) return 0;
   // longer reductions first: their tiles take longest, so they start first
   if (nl == 2 && live[1].K > live[0].K) std::swap(live[0], live[1]);
+  // CTA pairs unless a problem has at most 128 rows (a pair tile would be
+  // half empty) or the context pins a variant.
+  bool pair = true;
+  for (int i = 0; i < nl; ++i) pair = pair && live[i].M > BM;
+  if (ctx->gemm_variant == 1) pair = false;
+  if (ctx->gemm_variant == 2) pair = true;
   GroupArgs a{};
   CUtensorMap tm[4];
   for (int i = 0; i < nl; ++i) {
-    int rc = prepare(ctx, live[i], &a.p[i], &tm[2 * i], &tm[2 * i + 1]);
+    int rc = pair ? prepare(ctx, live[i], &a.p[i], &tm[2 * i], &tm[2 * i + 1], PAIR_BM, HALF_ROWS, HALF_ROWS)
+                  : prepare(ctx, live[i], &a.p[i], &tm[2 * i], &tm[2 * i + 1], BM, BM, BN);
     if (rc) return rc;
   }
   if (nl == 1) {
@@ -398,17 +676,28 @@ int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t str
   a.nprob = nl;
   a.total_tiles = a.p[0].tiles + (nl > 1 ? a.p[1].tiles : 0);
   a.err = ctx->d_err;
-  static bool attr_set[8] = {false};
-  if (!attr_set[ctx->device & 7]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  static bool attr_set[2][8] = {{false}};
+  const int dev = ctx->device & 7;
+  if (!attr_set[pair][dev]) {
+    cudaError_t e = pair ? cudaFuncSetAttribute(gemm_tf32_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                P_SMEM_BYTES)
+                         : cudaFuncSetAttribute(gemm_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                SMEM_BYTES);
     if (e != cudaSuccess) return ctx->fail_cuda(e, "cudaFuncSetAttribute(gemm_tf32)");
-    attr_set[ctx->device & 7] = true;
+    attr_set[pair][dev] = true;
   }
-  const int grid = a.total_tiles < ctx->num_sms ? a.total_tiles : ctx->num_sms;
   double flops = 0;
   for (int i = 0; i < nl; ++i) flops += 2.0 * a.p[i].M * a.p[i].N * static_cast<double>(a.p[i].K);
   ProfScope prof(ctx, PROF_GEMM, flops, stream);
-  gemm_tf32_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3], a);
+  if (pair) {
+    // one cluster per SM pair; clusters loop over the tiles
+    const int pairs = ctx->num_sms / 2;
+    const int clusters = a.total_tiles < pairs ? a.total_tiles : pairs;
+    gemm_tf32_pair_kernel<<<2 * clusters, NUM_THREADS, P_SMEM_BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3], a);
+  } else {
+    const int grid = a.total_tiles < ctx->num_sms ? a.total_tiles : ctx->num_sms;
+    gemm_tf32_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3], a);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return ctx->fail_cuda(e, "launch gemm_tf32");
   ctx->count_launch();

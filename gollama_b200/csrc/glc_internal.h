@@ -25,6 +25,7 @@ struct Context {
   int* d_err = nullptr;                // device error word written by bounded waits
   std::string last_error;
   uint64_t launches = 0;               // kernels this library launched
+  int gemm_variant = 0;                // 0 automatic, 1 single-CTA tiles, 2 CTA-pair tiles
   EncodeTiledFn encode_fn = nullptr;
   // scratch workspace owned by the context (grown on demand, never shrunk)
   void* ws = nullptr;

@@ -128,9 +128,12 @@ def main(argv=None):
     ap.add_argument("cases", nargs="+", choices=sorted(CASES) + ["all"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--variant", type=int, default=0, choices=[0, 1, 2],
+                    help="GEMM tiles: 0 automatic, 1 single-CTA 128x256, 2 CTA-pair 256x256")
     a = ap.parse_args(argv)
     names = sorted(CASES) if "all" in a.cases else a.cases
     with Context(0) as ctx:
+        ctx.call("glc_set_gemm_variant", a.variant)
         for n in names:
             desc, ms, rate, unit = CASES[n](ctx, a.iters, a.warmup)
             print(f"{n:18s} {desc:44s} {ms:9.4f} ms  {rate:9.1f} {unit}", flush=True)

@@ -124,6 +124,12 @@ GLC_API int glc_linear_bwd(glc_ctx* ctx, const float* dY, const float* X, const 
  * K-major (ptr[i*ld+k]).  round_out rounds the stored values to TF32. */
 GLC_API int glc_gemm_tf32(glc_ctx* ctx, const float* A, int lda, int a_mn, const float* B, int ldb, int b_mn, float* C,
                   int ldc, int M, int N, int K, int accumulate, const float* R, int ldr, int round_out);
+/* Selects the GEMM tile shape for later calls on this context (tuning and
+ * diagnostics; no reference counterpart): 0 automatic (CTA-pair 256x256 tiles
+ * on tcgen05.mma.cta_group::2 unless a problem has at most 128 rows),
+ * 1 single-CTA 128x256 tiles, 2 CTA-pair tiles always.  Results agree to fp32
+ * rounding across variants. */
+GLC_API int glc_set_gemm_variant(glc_ctx* ctx, int variant);
 
 /* ------------------------------------------------------------------ fused / elementwise ops
  * Building blocks of the tape's GradFns; each mirrors one reference node.

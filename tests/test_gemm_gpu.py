@@ -133,3 +133,36 @@ def test_linear_bwd_grouped(ctx, M, K, N):
     G64 = G.astype(np.float64)
     assert rel_fro(ddx.numpy(), G64 @ W.astype(np.float64) + dX0) < TOL
     assert rel_fro(ddw.numpy(), G64.T @ X.astype(np.float64)) < TOL
+
+
+@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("M,K,N", [(64, 96, 200), (200, 72, 100), (384, 256, 640), (1024, 512, 1376)])
+def test_gemm_variants_all_majors(ctx, variant, M, K, N):
+    """Single-CTA (1) and CTA-pair (2) tiles on the forward, dX and dW
+    products, with ragged edges and with row counts that leave the second CTA
+    of a pair without rows."""
+    rng = np.random.default_rng(variant * 1000 + M + K + N)
+    X = rng.standard_normal((M, K), dtype=np.float32)
+    W = rng.standard_normal((N, K), dtype=np.float32)
+    G = rng.standard_normal((M, N), dtype=np.float32)
+    D0 = rng.standard_normal((M, K), dtype=np.float32)
+    dX, dW, dG = ctx.from_numpy(X), ctx.from_numpy(W), ctx.from_numpy(G)
+    Y, gX, gW = ctx.empty((M, N)), ctx.from_numpy(D0), ctx.empty((N, K))
+    ctx.call("glc_set_gemm_variant", variant)
+    try:
+        ctx.call("glc_linear_fwd", dX.ptr, dW.ptr, Y.ptr, M, K, N, None)
+        ctx.call("glc_linear_bwd", dG.ptr, dX.ptr, dW.ptr, gX.ptr, gW.ptr, M, K, N, 1, 0)
+        ctx.sync()
+    finally:
+        ctx.call("glc_set_gemm_variant", 0)
+    X64, W64, G64 = X.astype(np.float64), W.astype(np.float64), G.astype(np.float64)
+    assert rel_fro(Y.numpy(), X64 @ W64.T) < TOL
+    assert rel_fro(gX.numpy(), G64 @ W64 + D0) < TOL
+    assert rel_fro(gW.numpy(), G64.T @ X64) < TOL
+
+
+def test_gemm_variant_rejects_unknown(ctx):
+    from gollama_b200.device import GlcError
+
+    with pytest.raises(GlcError):
+        ctx.call("glc_set_gemm_variant", 3)
