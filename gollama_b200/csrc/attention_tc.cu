@@ -542,13 +542,13 @@ __global__ void __launch_bounds__(NT, 1)
 __global__ void group_sum_kernel(const float* __restrict__ pk, const float* __restrict__ pv, float* __restrict__ dk,
                                  float* __restrict__ dv, int dk_ld, int dv_ld, int T, int H, int Hkv, int hd,
                                  int round_dv) {
-  const int G = H / Hkv, n4 = hd / 4;
-  const size_t total = static_cast<size_t>(T) * Hkv * n4;
-  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
-    const int d4 = static_cast<int>(i % n4);
-    const size_t th = i / n4;
-    const int kh = static_cast<int>(th % Hkv);
-    const size_t t = th / Hkv;
+  // 32-bit index math: the host checks T * Hkv * hd / 4 < 2^31
+  const int G = H / Hkv, n4 = hd / 4, per_t = Hkv * n4;
+  const int total = T * per_t;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const size_t t = static_cast<unsigned>(i) / static_cast<unsigned>(per_t);
+    const int rem = i - static_cast<int>(t) * per_t;
+    const int kh = rem / n4, d4 = rem - kh * n4;
     float4 sk = make_float4(0.f, 0.f, 0.f, 0.f), sv = sk;
     for (int g = 0; g < G; ++g) {
       const size_t src = (t * H + kh * G + g) * hd / 4 + d4;
@@ -853,6 +853,8 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
         tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, pk, pv, qw, qw, 1, S, H, Hkv, scale, scale * LOG2E, 0,
         ctx->d_err);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
+    if (static_cast<long long>(T) * Hkv * HD / 4 >= (1LL << 31))
+      return ctx->fail(GLC_ERR_INVALID, "attention_bwd: B*S*Hkv*hd too large");
     group_sum_kernel<<<grid_for(static_cast<size_t>(T) * Hkv * HD / 4, 256, ctx->num_sms), 256, 0, s>>>(
         pk, pv, io.dk, io.dv, io.dk_ld, io.dv_ld, T, H, Hkv, HD, round_dv ? 1 : 0);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd group sum");

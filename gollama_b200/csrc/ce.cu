@@ -102,19 +102,43 @@ __global__ void __launch_bounds__(512) ce_kernel(float* __restrict__ logits, con
   }
 }
 
-// loss = (0 - logp_0 - logp_1 - ...) / rows over valid targets (grad.go:239-246)
+// loss = (0 - logp_0 - logp_1 - ...) / rows over valid targets (grad.go:239-246).
+// One block: the threads stage chunks of row_logp in shared memory, thread 0
+// subtracts them in row order (the reference's running float32 total).
 __global__ void ce_loss_sum_kernel(const float* __restrict__ row_logp, const int64_t* __restrict__ targets, int rows,
                                    int V, float* __restrict__ loss) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  constexpr int CHUNK = 2048;
+  __shared__ float buf[CHUNK];
   float total = 0.f;
-  for (int b = 0; b < rows; ++b) {
-    const int64_t t = targets[b];
-    if (t >= 0 && t < V) total = __fsub_rn(total, row_logp[b]);
+  for (int base = 0; base < rows; base += CHUNK) {
+    const int n = min(CHUNK, rows - base);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const int64_t t = targets[base + i];
+      buf[i] = (t >= 0 && t < V) ? row_logp[base + i] : 0.f;  // x - 0 == x: invalid rows add nothing
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+      for (int i = 0; i < n; ++i) total = __fsub_rn(total, buf[i]);
+    __syncthreads();
   }
-  *loss = __fdiv_rn(total, static_cast<float>(rows));
+  if (threadIdx.x == 0) *loss = __fdiv_rn(total, static_cast<float>(rows));
+}
+
+__global__ void exp32_kernel(const float* __restrict__ x, float* __restrict__ y, size_t n) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+    y[i] = go_exp32(x[i]);
 }
 
 }  // namespace
+
+int exp32(Context* ctx, const float* x, float* y, size_t n, cudaStream_t s) {
+  if (n == 0) return 0;
+  if (!x || !y) return ctx->fail(GLC_ERR_INVALID, "exp32: null pointer");
+  ProfScope prof(ctx, PROF_OTHER, 8.0 * n, s);
+  exp32_kernel<<<grid_for(n, 256, ctx->num_sms), 256, 0, s>>>(x, y, n);
+  GLC_LAUNCH_CHECK(ctx, "exp32");
+  return 0;
+}
 
 int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, int V, float scale, float* row_logp,
                float* loss, bool write_grad, bool round_out, cudaStream_t s) {
@@ -144,7 +168,7 @@ int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, in
   else
     return ctx->fail(GLC_ERR_UNSUPPORTED, "softmax_ce: vocab above 65536 is not supported");
   GLC_LAUNCH_CHECK(ctx, "softmax_ce");
-  ce_loss_sum_kernel<<<1, 32, 0, s>>>(row_logp, targets, rows, V, loss);
+  ce_loss_sum_kernel<<<1, 256, 0, s>>>(row_logp, targets, rows, V, loss);
   GLC_LAUNCH_CHECK(ctx, "softmax_ce loss");
   return 0;
 }

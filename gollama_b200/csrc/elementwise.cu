@@ -17,11 +17,13 @@ __device__ __forceinline__ float swiglu_f(float g, float u) {
   return __fmul_rn(__fmul_rn(g, s), u);
 }
 
+// 2-D launch: blockIdx.x/threadIdx.x pick a float4 column, blockIdx.y strides
+// over rows (32-bit index arithmetic, no per-element division).
 __global__ void swiglu_fwd_kernel(const float* __restrict__ g, const float* __restrict__ u, size_t ld_in,
-                                  float* __restrict__ h, size_t ld_h, size_t rows, size_t cols4, int round_out) {
-  const size_t n4 = rows * cols4;
-  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n4; i += size_t(gridDim.x) * blockDim.x) {
-    const size_t r = i / cols4, c = i % cols4;
+                                  float* __restrict__ h, size_t ld_h, unsigned rows, unsigned cols4, int round_out) {
+  const unsigned c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols4) return;
+  for (unsigned r = blockIdx.y; r < rows; r += gridDim.y) {
     const float4 a = reinterpret_cast<const float4*>(g + r * ld_in)[c];
     const float4 b = reinterpret_cast<const float4*>(u + r * ld_in)[c];
     float4 o = make_float4(swiglu_f(a.x, b.x), swiglu_f(a.y, b.y), swiglu_f(a.z, b.z), swiglu_f(a.w, b.w));
@@ -43,11 +45,11 @@ __device__ __forceinline__ void swiglu_b(float g, float u, float dh, float& dg, 
 
 __global__ void swiglu_bwd_kernel(const float* __restrict__ g, const float* __restrict__ u, size_t ld_in,
                                   const float* __restrict__ dh, size_t ld_dh, float* __restrict__ dg,
-                                  float* __restrict__ du, size_t ld_out, size_t rows, size_t cols4, int accumulate,
+                                  float* __restrict__ du, size_t ld_out, unsigned rows, unsigned cols4, int accumulate,
                                   int round_out) {
-  const size_t n4 = rows * cols4;
-  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n4; i += size_t(gridDim.x) * blockDim.x) {
-    const size_t r = i / cols4, c = i % cols4;
+  const unsigned c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols4) return;
+  for (unsigned r = blockIdx.y; r < rows; r += gridDim.y) {
     const float4 a = reinterpret_cast<const float4*>(g + r * ld_in)[c];
     const float4 b = reinterpret_cast<const float4*>(u + r * ld_in)[c];
     const float4 d = reinterpret_cast<const float4*>(dh + r * ld_dh)[c];
@@ -72,6 +74,17 @@ __global__ void swiglu_bwd_kernel(const float* __restrict__ g, const float* __re
   }
 }
 
+// Grid of a row-strided 2-D elementwise launch: enough column blocks to
+// cover cols4 float4s, rows spread so the whole launch has ~16 blocks per SM.
+inline dim3 grid_2d(size_t rows, size_t cols4, int block, int num_sms) {
+  const unsigned bx = static_cast<unsigned>((cols4 + block - 1) / block);
+  size_t by = (static_cast<size_t>(num_sms) * 16 + bx - 1) / bx;
+  if (by > rows) by = rows;
+  if (by > 65535) by = 65535;
+  if (by < 1) by = 1;
+  return dim3(bx, static_cast<unsigned>(by));
+}
+
 // ---------------------------------------------------------------- fills / copies
 __global__ void fill_kernel(float* __restrict__ p, float v, size_t n) {
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) p[i] = v;
@@ -91,15 +104,16 @@ __global__ void round_copy_kernel(const float* __restrict__ src, float* __restri
 // apply3D (pkg/model/rope.go:96-126) on rows of nh heads x hd, consecutive
 // pairs, position t % S; inverse = 1 applies the transposed rotation (the
 // backward).  In place; optional TF32 rounding of the result.
+// Launch: blockIdx.y strides over tokens; the threads of a block cover the
+// row's nh*hd/2 pairs (blockDim.x * gridDim.x >= pairs per row).
 __global__ void rope_kernel(float* __restrict__ x, size_t ld, int T, int S, int nh, int hd,
                             const float* __restrict__ cos_t, const float* __restrict__ sin_t, int inverse,
                             int round_out) {
   const int half = hd >> 1;
-  const size_t pairs = static_cast<size_t>(T) * nh * half;
-  for (size_t p = blockIdx.x * size_t(blockDim.x) + threadIdx.x; p < pairs; p += size_t(gridDim.x) * blockDim.x) {
-    const int i = static_cast<int>(p % half);
-    const size_t th = p / half;  // t*nh + h
-    const int t = static_cast<int>(th / nh), hh = static_cast<int>(th % nh);
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;  // pair index inside the row: head * half + i
+  if (q >= nh * half) return;
+  const int hh = q / half, i = q - hh * half;
+  for (int t = blockIdx.y; t < T; t += gridDim.y) {
     const int pos = t % S;
     const float c = cos_t[pos * half + i], s = sin_t[pos * half + i];
     float2* xp = reinterpret_cast<float2*>(x + static_cast<size_t>(t) * ld + static_cast<size_t>(hh) * hd) + i;
@@ -171,8 +185,9 @@ int swiglu_fwd(Context* ctx, const float* g, const float* u, size_t ld_in, float
     return ctx->fail(GLC_ERR_INVALID, "swiglu_fwd: sizes and strides must be multiples of 4, pointers 16-byte aligned");
   const size_t n = rows * cols;
   ProfScope prof(ctx, PROF_SWIGLU, 12.0 * n, s);
-  swiglu_fwd_kernel<<<grid_for(n / 4, 256, ctx->num_sms), 256, 0, s>>>(g, u, ld_in, h, ld_h, rows, cols / 4,
-                                                                       round_out ? 1 : 0);
+  if (rows > 0xFFFFFFFFu || cols / 4 > 0xFFFFFFFFu) return ctx->fail(GLC_ERR_INVALID, "swiglu_fwd: too large");
+  swiglu_fwd_kernel<<<grid_2d(rows, cols / 4, 256, ctx->num_sms), 256, 0, s>>>(
+      g, u, ld_in, h, ld_h, static_cast<unsigned>(rows), static_cast<unsigned>(cols / 4), round_out ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "swiglu_fwd");
   return 0;
 }
@@ -185,9 +200,10 @@ int swiglu_bwd(Context* ctx, const float* g, const float* u, size_t ld_in, const
     return ctx->fail(GLC_ERR_INVALID, "swiglu_bwd: sizes and strides must be multiples of 4, pointers 16-byte aligned");
   const size_t n = rows * cols;
   ProfScope prof(ctx, PROF_SWIGLU, (accumulate ? 28.0 : 20.0) * n, s);
-  swiglu_bwd_kernel<<<grid_for(n / 4, 256, ctx->num_sms), 256, 0, s>>>(g, u, ld_in, dh, ld_dh, dg, du, ld_out, rows,
-                                                                       cols / 4, accumulate ? 1 : 0,
-                                                                       round_out ? 1 : 0);
+  if (rows > 0xFFFFFFFFu || cols / 4 > 0xFFFFFFFFu) return ctx->fail(GLC_ERR_INVALID, "swiglu_bwd: too large");
+  swiglu_bwd_kernel<<<grid_2d(rows, cols / 4, 256, ctx->num_sms), 256, 0, s>>>(
+      g, u, ld_in, dh, ld_dh, dg, du, ld_out, static_cast<unsigned>(rows), static_cast<unsigned>(cols / 4),
+      accumulate ? 1 : 0, round_out ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "swiglu_bwd");
   return 0;
 }
@@ -227,8 +243,13 @@ int rope(Context* ctx, float* x, int ld, int T, int S, int nh, int hd, const flo
     return ctx->fail(GLC_ERR_INVALID, "rope: bad arguments");
   const size_t pairs = static_cast<size_t>(T) * nh * (hd / 2);
   ProfScope prof(ctx, PROF_OTHER, 16.0 * pairs, s);
-  rope_kernel<<<grid_for(pairs, 256, ctx->num_sms), 256, 0, s>>>(x, static_cast<size_t>(ld), T, S, nh, hd, cos_t,
-                                                                  sin_t, inverse ? 1 : 0, round_out ? 1 : 0);
+  const int row_pairs = nh * (hd / 2);
+  const int bx = (row_pairs + 255) / 256;
+  int by = (ctx->num_sms * 16 + bx - 1) / bx;
+  if (by > T) by = T;
+  if (by > 65535) by = 65535;
+  rope_kernel<<<dim3(bx, by), 256, 0, s>>>(x, static_cast<size_t>(ld), T, S, nh, hd, cos_t, sin_t, inverse ? 1 : 0,
+                                           round_out ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "rope");
   return 0;
 }

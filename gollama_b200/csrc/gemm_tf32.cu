@@ -61,6 +61,11 @@ struct Problem {
   int round_out;   // round stored values to TF32 (RN)
   int a_mn, b_mn;  // operand majors
   int m_tiles, n_tiles, k_blocks, tiles;
+  // Tile order.  Concurrent tiles share the operand of the slow-moving index
+  // through L2 and stream the other; the operand of the fast-moving index is
+  // re-read once per sweep unless it stays in L2.  n_fast walks N fastest
+  // (A tiles stay hot), chosen when A is the larger operand.
+  int n_fast;
 };
 
 // Up to two independent problems share one persistent launch: their tiles
@@ -107,8 +112,13 @@ __device__ __forceinline__ TileRef locate(const GroupArgs& a, int tile) {
   t.prob = (tile < a.p[0].tiles) ? 0 : 1;
   const int lt = t.prob ? tile - a.p[0].tiles : tile;
   const Problem& p = a.p[t.prob];
-  t.m0 = (lt % p.m_tiles) * TILE_M;
-  t.n0 = (lt / p.m_tiles) * BN;
+  if (p.n_fast) {
+    t.n0 = (lt % p.n_tiles) * BN;
+    t.m0 = (lt / p.n_tiles) * TILE_M;
+  } else {
+    t.m0 = (lt % p.m_tiles) * TILE_M;
+    t.n0 = (lt / p.m_tiles) * BN;
+  }
   return t;
 }
 
@@ -629,6 +639,7 @@ int prepare(Context* ctx, const GemmSpec& g, Problem* p, CUtensorMap* ta, CUtens
   p->n_tiles = (g.N + BN - 1) / BN;
   p->k_blocks = (g.K + BK - 1) / BK;
   p->tiles = p->m_tiles * p->n_tiles;
+  p->n_fast = static_cast<double>(g.M) > static_cast<double>(g.N) ? 1 : 0;  // A (M x K) larger than B (N x K)
   return 0;
 }
 

@@ -151,6 +151,7 @@ int swiglu_bwd(Context* ctx, const float* g, const float* u, size_t ld_in, const
                float* du, size_t ld_out, size_t rows, size_t cols, bool accumulate, bool round_out, cudaStream_t s);
 int fill(Context* ctx, float* p, float v, size_t n, cudaStream_t s);
 int round_copy(Context* ctx, const float* src, float* dst, size_t n, cudaStream_t s);
+int exp32(Context* ctx, const float* x, float* y, size_t n, cudaStream_t s);
 int add_inplace(Context* ctx, float* dst, const float* src, size_t n, cudaStream_t s);
 // x: T rows of row stride ld (elements); the first nh*hd columns are rotated.
 int rope(Context* ctx, float* x, int ld, int T, int S, int nh, int hd, const float* cos_t, const float* sin_t,

@@ -161,6 +161,11 @@ int glc_round_tf32(glc_ctx* ctx, const float* src, float* dst, size_t n) {
   return glc::round_copy(C_(ctx), src, dst, n, C_(ctx)->stream);
 }
 
+int glc_exp32(glc_ctx* ctx, const float* x, float* y, size_t n) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::exp32(C_(ctx), x, y, n, C_(ctx)->stream);
+}
+
 int glc_add_inplace(glc_ctx* ctx, float* dst, const float* src, size_t n) {
   if (!ctx) return GLC_ERR_INVALID;
   return glc::add_inplace(C_(ctx), dst, src, n, C_(ctx)->stream);

@@ -59,6 +59,17 @@ def case_gemm(ctx, kind, M, K, N, iters, warmup):
     return f"gemm_{kind} M={M} K={K} N={N}", ms, flops / (ms * 1e-3) / 1e12, "TFLOP/s"
 
 
+def case_linear_sweep(ctx, iters, warmup):
+    """Linear-layer sweep: M in {4096, 16384, 32768} x (K, N) in {(2048, 2048),
+    (2048, 5632), (5632, 2048)}, forward, dX and dW separately."""
+    out = []
+    for M in (4096, 16384, 32768):
+        for K, N in ((2048, 2048), (2048, 5632), (5632, 2048)):
+            for kind in ("fwd", "dx", "dw"):
+                out.append(case_gemm(ctx, kind, M, K, N, iters, warmup))
+    return out
+
+
 def case_attention(ctx, kind, iters, warmup, B=4):
     Tq = B * S
     q, k, v = _rand(ctx, (Tq, H * HD), 4), _rand(ctx, (Tq, HKV * HD), 5), _rand(ctx, (Tq, HKV * HD), 6)
@@ -115,6 +126,12 @@ CASES = {
     "gemm_fwd_gateup": lambda c, i, w: case_gemm(c, "fwd", T, D, 2 * F, i, w),
     "gemm_fwd_lmhead": lambda c, i, w: case_gemm(c, "fwd", T, D, V, i, w),
     "gemm_fwd_8192": lambda c, i, w: case_gemm(c, "fwd", 8192, 8192, 8192, i, w),
+    "gemm_dx_lmhead": lambda c, i, w: case_gemm(c, "dx", T, D, V, i, w),
+    "gemm_dw_lmhead": lambda c, i, w: case_gemm(c, "dw", T, D, V, i, w),
+    "gemm_bwd_lmhead": lambda c, i, w: case_gemm(c, "bwd", T, D, V, i, w),
+    "gemm_bwd_down": lambda c, i, w: case_gemm(c, "bwd", T, F, D, i, w),
+    "gemm_bwd_gateup": lambda c, i, w: case_gemm(c, "bwd", T, D, 2 * F, i, w),
+    "linear_sweep": case_linear_sweep,
     "attention_fwd": lambda c, i, w: case_attention(c, "fwd", i, w),
     "attention_bwd": lambda c, i, w: case_attention(c, "bwd", i, w),
     "swiglu_bwd": case_swiglu,
@@ -135,8 +152,9 @@ def main(argv=None):
     with Context(0) as ctx:
         ctx.call("glc_set_gemm_variant", a.variant)
         for n in names:
-            desc, ms, rate, unit = CASES[n](ctx, a.iters, a.warmup)
-            print(f"{n:18s} {desc:44s} {ms:9.4f} ms  {rate:9.1f} {unit}", flush=True)
+            res = CASES[n](ctx, a.iters, a.warmup)
+            for desc, ms, rate, unit in (res if isinstance(res, list) else [res]):
+                print(f"{n:18s} {desc:44s} {ms:9.4f} ms  {rate:9.1f} {unit}", flush=True)
 
 
 if __name__ == "__main__":

@@ -214,6 +214,10 @@ GLC_API int glc_adamw_step(glc_ctx* ctx, float* params, float* grads, float* m, 
                            float beta2, float eps, float weight_decay, int step);
 GLC_API int glc_fill(glc_ctx* ctx, float* p, float value, size_t n);
 GLC_API int glc_round_tf32(glc_ctx* ctx, const float* src, float* dst, size_t n);
+/* exp32 (pkg/tensor/grad.go:283-293) elementwise: y[i] = float32(_exp(x[i])),
+ * the exact value the reference's softmax cross-entropy and SiLU use, through
+ * the same device function those kernels call. */
+GLC_API int glc_exp32(glc_ctx* ctx, const float* x, float* y, size_t n);
 /* addInplace (pkg/tensor/grad.go:200-204): dst += src. */
 GLC_API int glc_add_inplace(glc_ctx* ctx, float* dst, const float* src, size_t n);
 

@@ -363,6 +363,10 @@ float FN(exp32)(float x) { /* grad.go:283-293 */
   return (float)FN(go_exp)((double)x);
 }
 
+void FN(exp32_array)(const float* x, float* y, int64_t n) { /* exp32 over an array (test vectors) */
+  for (int64_t i = 0; i < n; ++i) y[i] = FN(exp32)(x[i]);
+}
+
 float FN(log32)(float x) { return (float)FN(go_log)((double)x); } /* grad.go:296-298 */
 
 /* ------------------------------------------------------------------ SiLU (SiLUGrad, grad.go:417-449) */

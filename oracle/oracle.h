@@ -73,6 +73,7 @@ typedef struct {
   void P##rmsnorm_bwd(const real* x, const real* w, const real* rms, const real* dout, real* dx, real* dw,     \
                       int rows, int cols, int full);                                                          \
   float P##exp32(float x);                                                                                    \
+  void P##exp32_array(const float* x, float* y, int64_t n);                                                   \
   float P##log32(float x);                                                                                    \
   double P##go_exp(double x);                                                                                 \
   double P##go_log(double x);                                                                                 \

@@ -267,3 +267,31 @@ def test_clip_and_adamw_bit_exact(ctx, step):
     sh = bs.numpy()[sel]
     assert np.all(sh.view(np.uint32) & 0x1FFF == 0)
     assert np.max(np.abs(sh - rp) / np.maximum(np.abs(rp), 1e-30)) <= 2.0**-11
+
+
+def test_exp32_bit_exact_against_oracle(ctx):
+    """The device exp32 equals the oracle's restatement of the reference's
+    exp32 bit for bit: a strided sweep over every float bit pattern in
+    [-88.5, 88.5], random arguments, and the edges (subnormal results,
+    saturation, infinities, zeros).  The reference's _exp keeps only two
+    polynomial terms (exp32(1) = 2.718261, not e), so a more accurate
+    exponential would fail here."""
+    from oracle.oracle import lib
+
+    top = np.float32(88.5).view(np.uint32)
+    pos = np.arange(0, int(top), 97, dtype=np.uint32)
+    sweep = np.concatenate([pos, pos | np.uint32(0x80000000)]).view(np.float32)
+    rnd = np.random.default_rng(7).uniform(-90.0, 90.0, 1 << 22).astype(np.float32)
+    edges = np.array([0.0, -0.0, -87.0, np.nextafter(np.float32(-87.0), np.float32(-100)), 88.0,
+                      np.nextafter(np.float32(88.0), np.float32(100)), -88.0,
+                      np.nextafter(np.float32(-88.0), np.float32(-100)), -100.0, 100.0, 1e-30, -1e-30, 1e-45,
+                      -1e-45, np.inf, -np.inf, 0.6931472, -0.6931472, 1.0, -1.0], dtype=np.float32)
+    x = np.ascontiguousarray(np.concatenate([sweep, rnd, edges]))
+    want = np.empty_like(x)
+    lib().orc_exp32_array(x.ctypes.data_as(C.c_void_p), want.ctypes.data_as(C.c_void_p), C.c_int64(x.size))
+    dx, dy = ctx.from_numpy(x), ctx.empty(x.shape)
+    ctx.call("glc_exp32", dx.ptr, dy.ptr, x.size)
+    ctx.sync()
+    got = dy.numpy()
+    bad = np.nonzero(got.view(np.uint32) != want.view(np.uint32))[0]
+    assert bad.size == 0, f"{bad.size} mismatches, first x={x[bad[:5]]} got={got[bad[:5]]} want={want[bad[:5]]}"
