@@ -9,9 +9,12 @@
 // floats, k/v rows Hkv*hd; row t = b*S + s.  Inputs are expected TF32-rounded
 // (the producing kernels round them); P and dS are rounded when written.
 //
-// Every kernel: 192 threads — warp 0 issues TMA loads (one thread), warp 1
-// owns TMEM and issues tcgen05.mma (one thread), warps 2..5 do the softmax
-// arithmetic with one thread per TMEM lane (row).  All waits are bounded.
+// Every kernel: 320 threads — warp 0 issues TMA loads (one thread), warp 1
+// owns TMEM and issues tcgen05.mma (one thread), warps 2..9 do the softmax
+// arithmetic: warp w reads TMEM lane quarter w % 4 (one thread per row) and
+// column half (w - 2) / 4 of each tile, so two warps share every row.  Values
+// the two halves of a row must agree on pass through shared memory behind an
+// mbarrier.  All waits are bounded.
 //
 // forward   CTA = (128 queries, head).  S_j = Q K_j^T into one of two TMEM
 //           buffers (the next S overlaps this softmax); P_j replaces S_j in
@@ -36,13 +39,16 @@
 namespace glc {
 namespace {
 
-constexpr int NT = 192;
+constexpr int NT = 320;
+constexpr int MATH_THREADS = 256;  // warps 2..9
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 
 struct Roles {
   int warp, lane;
   __device__ Roles() : warp(threadIdx.x >> 5), lane(threadIdx.x & 31) {}
+  __device__ int quarter() const { return warp & 3; }       // TMEM lanes this warp may access
+  __device__ int half() const { return (warp - 2) >> 2; }   // column half of a tile (math warps)
 };
 
 // K-major tile of R rows x HD fp32 (HD/32 blocks of [R][128 B], 128B swizzle):
@@ -98,7 +104,8 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, fl
 template <int HD>
 struct FwdLayout {
   static constexpr int Q = 128 * HD * 4, K = 128 * HD * 4, V = 128 * HD * 4;
-  static constexpr int OFF_K = Q, OFF_V = OFF_K + 2 * K, OFF_BAR = OFF_V + 2 * V;
+  static constexpr int OFF_K = Q, OFF_V = OFF_K + 2 * K, OFF_X = OFF_V + 2 * V;
+  static constexpr int OFF_BAR = OFF_X + 2 * 2 * 128 * 4;  // [parity][half][row] row maxima
   static constexpr int BYTES = OFF_BAR + 256 + 1024;
   static constexpr int TMEM_COLS = 512;
   static constexpr int O_COL = 384;
@@ -114,8 +121,8 @@ __global__ void __launch_bounds__(NT, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
   uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = bars + 3, *v_full = bars + 5, *v_empty = bars + 7,
-           *s_full = bars + 9, *p_full = bars + 12, *pv_done = bars + 15, *drain = bars + 18;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+           *s_full = bars + 9, *p_full = bars + 12, *pv_done = bars + 15, *drain = bars + 18, *xchg = bars + 19;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const Roles ro;
   const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // longest rows first
@@ -133,9 +140,11 @@ __global__ void __launch_bounds__(NT, 1)
     }
     for (int i = 0; i < 3; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], MATH_THREADS);
       mbar_init(&pv_done[i], 1);
     }
+    mbar_init(&xchg[0], MATH_THREADS);
+    mbar_init(&xchg[1], MATH_THREADS);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -216,63 +225,75 @@ __global__ void __launch_bounds__(NT, 1)
     }
   } else {
     // ---------------------------------------------------------------- softmax
-    const int q = ro.warp & 3;
+    const int q = ro.quarter(), hf = ro.half();
     const int r = q * 32 + ro.lane;
     const int row_abs = q0 + r;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    float* xmax = reinterpret_cast<float*>(sm + L::OFF_X);
     // Lazy running max (log2 domain): P_j = 2^(s - m_used) with m_used raised
     // only when the tile max exceeds it by more than 8, so P <= 256 and O is
-    // rescaled on few tiles; the final O / l is unchanged.
+    // rescaled on few tiles; the final O / l is unchanged.  Both warps of a
+    // row take the same decisions (they exchange their half-row maxima), and
+    // each keeps the partial sum l of its own columns.
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       const int sb = j % 3;
       WAIT_OR_BREAK(&s_full[sb], (j / 3) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
       tc_fence_after();
-      const int k0 = j * 128;
-      const bool diag = (j == qt);
-      const uint32_t sa = lane_addr + sb * 128;
-      uint32_t v[128];
+      const int k0 = j * 128 + hf * 64;
+      const uint32_t sa = lane_addr + sb * 128 + hf * 64;
+      uint32_t v[64];
       tmem_ld_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(v + 0));
       tmem_ld_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-      tmem_ld_32x32b_x32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(v + 64));
-      tmem_ld_32x32b_x32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(v + 96));
       tmem_ld_wait();
+      // Masking is needed only on the diagonal tile and past the sequence end
+      // (warp-uniform); elsewhere every score is live.
+      if (j == qt || k0 + 64 > S) {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+          const int key = k0 + e;
+          if (!(key < S && key <= row_abs)) v[e] = __float_as_uint(-INFINITY);
+        }
+      }
+      // max over raw scores (scale > 0); scores enter the exponent scaled by
+      // scale*log2(e) in one FMA below
       float mx[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < 128; ++e) {
-        const int key = k0 + e;
-        const bool valid = key < S && (!diag || key <= row_abs);
-        const float t = valid ? __uint_as_float(v[e]) * scale_log2 : -INFINITY;
-        v[e] = __float_as_uint(t);
-        mx[e & 7] = fmaxf(mx[e & 7], t);
-      }
-      const float m_tile = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      for (int e = 0; e < 64; ++e) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(v[e]));
+      const float m_half = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * scale_log2;
+      float* xs = xmax + (j & 1) * 256;
+      xs[hf * 128 + r] = m_half;
+      mbar_arrive(&xchg[j & 1]);
+      WAIT_OR_BREAK(&xchg[j & 1], (j >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      const float m_tile = fmaxf(m_half, xs[(hf ^ 1) * 128 + r]);
       const float m_new = (m_tile > m_used + 8.0f) ? m_tile : m_used;
       const float alpha = exp2f(m_used - m_new);  // 1 unless the max was raised; 0 on the first tile
       float sum[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) sum[i] = 0.f;
+      // a fully masked row half has m_new = -inf until a live key arrives:
+      // its scores are -inf too, and 2^(-inf) = 0 must not become NaN
+      const float m_sub = m_new == -INFINITY ? 0.f : m_new;
 #pragma unroll
-      for (int e = 0; e < 128; ++e) {
-        const uint32_t pb = tf32_bits(fast_exp2(__uint_as_float(v[e]) - m_new));
+      for (int e = 0; e < 64; ++e) {
+        const uint32_t pb = tf32_bits(fast_exp2(fmaf(__uint_as_float(v[e]), scale_log2, -m_sub)));
         sum[e & 7] += __uint_as_float(pb);
         v[e] = pb;
       }
       tmem_st_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(v + 0));
       tmem_st_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-      tmem_st_32x32b_x32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(v + 64));
-      tmem_st_32x32b_x32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(v + 96));
       tmem_st_wait();
+      // both warps of a row see the same alphas, so they agree on this branch
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
         // O may only be rescaled once PV_{j-1} has finished accumulating into it
         WAIT_OR_BREAK(&pv_done[(j - 1) % 3], ((j - 1) / 3) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
+        for (int c = hf; c < HD / 32; c += 2) {
           uint32_t o[32];
           tmem_ld_32x32b_x32(lane_addr + L::O_COL + c * 32, o);
           tmem_ld_wait();
@@ -287,6 +308,20 @@ __global__ void __launch_bounds__(NT, 1)
       l = l * alpha + (((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7])));
       m_used = m_new;
     }
+    // total l of the row = sum of the two halves' partial sums (exchange slot
+    // and barrier of the next tile parity)
+    {
+      const int j = n_kv;
+      float* xs = xmax + (j & 1) * 256;
+      if (ok) {
+        xs[hf * 128 + r] = l;
+        mbar_arrive(&xchg[j & 1]);
+      }
+      if (__all_sync(0xffffffffu, ok && mbar_wait(&xchg[j & 1], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE)))
+        l = hf == 0 ? l + xs[128 + r] : xs[r] + l;
+      else
+        ok = false;
+    }
     const int last = n_kv - 1;
     if (__all_sync(0xffffffffu, ok && mbar_wait(&pv_done[last % 3], (last / 3) & 1, abort_flag, err,
                                                    GLC_DEV_TIMEOUT_EPILOGUE))) {
@@ -294,7 +329,7 @@ __global__ void __launch_bounds__(NT, 1)
       const float inv = 1.0f / l;
       float* orow = out + (static_cast<size_t>(row_base) + row_abs) * (static_cast<size_t>(H) * HD) + h * HD;
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = hf; c < HD / 32; c += 2) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(lane_addr + L::O_COL + c * 32, v);
         tmem_ld_wait();
@@ -311,7 +346,7 @@ __global__ void __launch_bounds__(NT, 1)
           }
         }
       }
-      if (row_abs < S) lse[(static_cast<size_t>(b) * H + h) * S + row_abs] = (m_used + log2f(l)) * LN2;
+      if (hf == 0 && row_abs < S) lse[(static_cast<size_t>(b) * H + h) * S + row_abs] = (m_used + log2f(l)) * LN2;
     }
   }
   tc_fence_before();
@@ -323,21 +358,49 @@ __global__ void __launch_bounds__(NT, 1)
 }
 
 // ===================================================================== dK / dV
-// TMEM: two sets of {S^T [0,64), dP^T [64,128)} at cols 0 and 128, dV at 256,
-// dK at 256+HD.  The math warps overwrite S^T with P^T and dP^T with dS^T in
-// place; dV += P^T dO and dK += dS^T Q read them as A operands from TMEM.
-// The MMA thread issues S^T/dP^T of step i before dV/dK of step i-1, and
-// the 64-query Q/dO tiles are double-buffered.
+// TMEM: two sets of {S^T [0,64), dP^T [64,128)} at cols 0 and 128, then K, V
+// (the A operands of S^T = K Q^T and dP^T = V dO^T), dV and dK, HD columns
+// each.  The math warps overwrite S^T with P^T and dP^T with dS^T in place;
+// dV += P^T dO and dK += dS^T Q read them as A operands from TMEM.  With K
+// and V out of shared memory, three 64-query Q/dO stages fit: K and V are
+// first loaded into the third stage's space, copied row by row into TMEM by
+// the math warps, and the space is then released to the producer.
 template <int HD>
 struct DkdvLayout {
   static constexpr int K = 128 * HD * 4, V = 128 * HD * 4;
   static constexpr int QT = 64 * HD * 4;    // one 64-query operand tile
   static constexpr int STAGE = 4 * QT;      // Q (K-major), Q (MN-major), dO (K-major), dO (MN-major)
-  static constexpr int OFF_V = K, OFF_ST = OFF_V + V, OFF_LD = OFF_ST + 2 * STAGE, OFF_BAR = OFF_LD + 1024;
+  static constexpr int NST = 3, NSET = 2;
+  static constexpr int OFF_KV = 2 * STAGE;  // K and V land in stage 2 (K + V == STAGE)
+  static constexpr int OFF_LD = NST * STAGE, OFF_BAR = OFF_LD + 1024;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;
   static constexpr int TMEM_COLS = 512;
-  static constexpr int DV_COL = 256, DK_COL = 256 + HD;
+  static constexpr int K_COL = 256, V_COL = 256 + HD, DV_COL = 256 + 2 * HD, DK_COL = 256 + 3 * HD;
+  static_assert(K + V == STAGE, "K and V fill exactly one stage");
 };
+
+// Copies row `row` of a K-major SW128 tile of 128 rows x HD fp32 (HD/32 blocks
+// of [128][128 B]) into TMEM columns [col, col + HD) of the thread's lane: the
+// column blocks are shared between the two warps of the lane quarter.
+template <int HD>
+__device__ __forceinline__ void tile_rows_to_tmem(const uint8_t* tile, int row, uint32_t lane_addr, int col,
+                                                  int first_block, int hf) {
+#pragma unroll
+  for (int cb = 0; cb < HD / 32; ++cb) {
+    if (((first_block + cb) & 1) != hf) continue;
+    const uint8_t* rp = tile + cb * (128 * 128) + row * 128;
+    uint32_t v[32];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const float4 f = *reinterpret_cast<const float4*>(rp + ((c ^ (row & 7)) << 4));
+      v[4 * c] = __float_as_uint(f.x);
+      v[4 * c + 1] = __float_as_uint(f.y);
+      v[4 * c + 2] = __float_as_uint(f.z);
+      v[4 * c + 3] = __float_as_uint(f.w);
+    }
+    tmem_st_32x32b_x32(lane_addr + col + cb * 32, v);
+  }
+}
 
 template <int HD, bool GROUP_LOOP>
 __global__ void __launch_bounds__(NT, 1)
@@ -351,9 +414,10 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
-  uint64_t *kv_full = bars, *qo_full = bars + 1, *qo_empty = bars + 3, *s_full = bars + 5, *p_full = bars + 7,
-           *set_free = bars + 9, *acc_done = bars + 11, *drain = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t *kv_full = bars, *qo_full = bars + 1, *qo_empty = bars + 4, *s_full = bars + 7, *p_full = bars + 9,
+           *set_free = bars + 11, *acc_done = bars + 13, *drain = bars + 14, *ld_ready = bars + 15,
+           *kv_moved = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* stage_ld = reinterpret_cast<float*>(sm + L::OFF_LD);  // [2][lse 64 | D 64]
   const Roles ro;
@@ -369,12 +433,16 @@ __global__ void __launch_bounds__(NT, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    mbar_init(kv_moved, MATH_THREADS);
+    for (int i = 0; i < L::NST; ++i) {
       mbar_init(&qo_full[i], 1);
       mbar_init(&qo_empty[i], 1);
+    }
+    for (int i = 0; i < L::NSET; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], MATH_THREADS);
       mbar_init(&set_free[i], 1);
+      mbar_init(&ld_ready[i], MATH_THREADS);
     }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
@@ -391,25 +459,28 @@ __global__ void __launch_bounds__(NT, 1)
   if (ro.warp == 0) {
     if (ro.lane == 0) {
       mbar_arrive_expect_tx(kv_full, L::K + L::V);
-      tma_tile<HD, 128>(sm, &tmK, kv_full, kh * HD, row_base + k0);
-      tma_tile<HD, 128>(sm + L::OFF_V, &tmV, kv_full, kh * HD, row_base + k0);
-      int armed[2] = {-1, -1};
+      tma_tile<HD, 128>(sm + L::OFF_KV, &tmK, kv_full, kh * HD, row_base + k0);
+      tma_tile<HD, 128>(sm + L::OFF_KV + L::K, &tmV, kv_full, kh * HD, row_base + k0);
+      int armed[L::NST] = {-1, -1, -1};
       bool ok = true;
       for (int it = 0; it < n_it; ++it) {
-        const int st = it & 1;
+        const int st = it % L::NST;
+        const uint32_t ph = (it / L::NST) & 1;
         const int hq = h_first + it / nq, qr = row_base + (qi0 + it % nq) * 64;
-        if (!mbar_wait(&qo_empty[st], ((it >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        // stage 2 holds K and V until the math warps have moved them to TMEM
+        if (it == 2 && !mbar_wait(kv_moved, 0, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        if (!mbar_wait(&qo_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
         mbar_arrive_expect_tx(&qo_full[st], L::STAGE);
-        uint8_t* base = sm + L::OFF_ST + st * L::STAGE;
+        uint8_t* base = sm + st * L::STAGE;
         tma_tile<HD, 64>(base, &tmQk, &qo_full[st], hq * HD, qr);
         tma_tile<HD, 64>(base + L::QT, &tmQm, &qo_full[st], hq * HD, qr);
         tma_tile<HD, 64>(base + 2 * L::QT, &tmOk, &qo_full[st], hq * HD, qr);
         tma_tile<HD, 64>(base + 3 * L::QT, &tmOm, &qo_full[st], hq * HD, qr);
-        armed[st] = (it >> 1) & 1;
+        armed[st] = static_cast<int>(ph);
       }
       if (!ok) {
         mbar_drain(kv_full, 0, err);
-        for (int st = 0; st < 2; ++st)
+        for (int st = 0; st < L::NST; ++st)
           if (armed[st] >= 0) mbar_drain(&qo_full[st], static_cast<uint32_t>(armed[st]), err);
       }
     }
@@ -417,36 +488,38 @@ __global__ void __launch_bounds__(NT, 1)
     if (ro.lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_tf32(128, 64, false, false);
       constexpr uint32_t idesc_a = umma_idesc_tf32(128, HD, false, true);
-      bool ok = mbar_wait(kv_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
+      // K and V are A operands in TMEM once the math warps have copied them
+      bool ok = mbar_wait(kv_moved, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
       bool issued = false;
+      tc_fence_after();
       for (int it = 0; ok && it <= n_it; ++it) {
         if (it < n_it) {
-          const int st = it & 1;
-          const uint32_t base = s0 + L::OFF_ST + st * L::STAGE;
-          if (!mbar_wait(&qo_full[st], (it >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-          if (!mbar_wait(&set_free[st], ((it >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
+          const int st = it % L::NST, ts = it % L::NSET;
+          const uint32_t base = s0 + st * L::STAGE;
+          if (!mbar_wait(&qo_full[st], (it / L::NST) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          if (!mbar_wait(&set_free[ts], ((it / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < HD / 8; ++kk) {
-            umma_tf32(tmem + st * 128, kdesc<128>(s0, kk), kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
-            umma_tf32(tmem + st * 128 + 64, kdesc<128>(s0 + L::OFF_V, kk), kdesc<64>(base + 2 * L::QT, kk), idesc_s,
-                      kk > 0 ? 1u : 0u);
+            umma_tf32_ts(tmem + ts * 128, tmem + L::K_COL + kk * 8, kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
+            umma_tf32_ts(tmem + ts * 128 + 64, tmem + L::V_COL + kk * 8, kdesc<64>(base + 2 * L::QT, kk), idesc_s,
+                         kk > 0 ? 1u : 0u);
           }
           issued = true;
-          umma_commit(&s_full[st]);
+          umma_commit(&s_full[ts]);
         }
         if (it >= 1) {
-          const int pit = it - 1, ps = pit & 1;
-          const uint32_t base = s0 + L::OFF_ST + ps * L::STAGE;
-          if (!mbar_wait(&p_full[ps], (pit >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          const int pit = it - 1, ps = pit % L::NST, pts = pit % L::NSET;
+          const uint32_t base = s0 + ps * L::STAGE;
+          if (!mbar_wait(&p_full[pts], (pit / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t acc = (pit > 0 || kk > 0) ? 1u : 0u;
-            umma_tf32_ts(tmem + L::DV_COL, tmem + ps * 128 + kk * 8, mdesc<64>(base + 3 * L::QT, kk), idesc_a, acc);
-            umma_tf32_ts(tmem + L::DK_COL, tmem + ps * 128 + 64 + kk * 8, mdesc<64>(base + L::QT, kk), idesc_a, acc);
+            umma_tf32_ts(tmem + L::DV_COL, tmem + pts * 128 + kk * 8, mdesc<64>(base + 3 * L::QT, kk), idesc_a, acc);
+            umma_tf32_ts(tmem + L::DK_COL, tmem + pts * 128 + 64 + kk * 8, mdesc<64>(base + L::QT, kk), idesc_a, acc);
           }
-          umma_commit(&set_free[ps]);
+          umma_commit(&set_free[pts]);
           umma_commit(&qo_empty[ps]);
         }
       }
@@ -457,73 +530,109 @@ __global__ void __launch_bounds__(NT, 1)
       }
     }
   } else {
-    const int q = ro.warp & 3;
-    const int c = q * 32 + ro.lane;  // key row within the tile
-    const int t = threadIdx.x - 64;  // 0..127 among the math threads
+    const int q = ro.quarter(), hf = ro.half();
+    const int c = q * 32 + ro.lane;         // key row within the tile
+    const int t = threadIdx.x - 64;         // 0..255 among the math threads
     const int key = k0 + c;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
     bool ok = true;
-    for (int it = 0; it < n_it; ++it) {
-      const int st = it & 1;
-      const int hq = h_first + it / nq, qbase = (qi0 + it % nq) * 64;
-      WAIT_OR_BREAK(&s_full[st], (it >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
-      tc_fence_after();
-      // stage lse and D of this step's 64 queries (double-buffered by step parity)
-      {
-        float* slot = stage_ld + st * 128;
-        const int qq = t & 63, qa = qbase + qq;
-        const size_t ix = (static_cast<size_t>(b) * H + hq) * S + qa;
-        slot[t] = qa < S ? (t < 64 ? lse[ix] * LOG2E : Dv[ix]) : 0.f;
-      }
-      named_bar_sync(1, 128);
-      const float* lse2 = stage_ld + st * 128;
-      const float* dq = lse2 + 64;
-      const uint32_t sa = lane_addr + st * 128;
-      uint32_t sv[64], dpv[64];
-      tmem_ld_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
-      tmem_ld_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-      tmem_ld_32x32b_x32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(dpv + 0));
-      tmem_ld_32x32b_x32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(dpv + 32));
-      tmem_ld_wait();
-#pragma unroll
-      for (int e = 0; e < 64; ++e) {
-        const int qa = qbase + e;
-        const bool valid = qa < S && key < S && key <= qa;
-        const float p = valid ? fast_exp2(__uint_as_float(sv[e]) * scale_log2 - lse2[e]) : 0.f;
-        const float ds = p * (__uint_as_float(dpv[e]) - dq[e]) * scale;
-        sv[e] = tf32_bits(p);
-        dpv[e] = tf32_bits(ds);
-      }
-      tmem_st_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
-      tmem_st_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-      tmem_st_32x32b_x32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(dpv + 0));
-      tmem_st_32x32b_x32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(dpv + 32));
+    // K and V rows -> TMEM, then release stage 2 and start the MMA thread
+    if (__all_sync(0xffffffffu, mbar_wait(kv_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
+      tile_rows_to_tmem<HD>(sm + L::OFF_KV, c, lane_addr, L::K_COL, 0, hf);
+      tile_rows_to_tmem<HD>(sm + L::OFF_KV + L::K, c, lane_addr, L::V_COL, HD / 32, hf);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[st]);
+      mbar_arrive(kv_moved);
+    } else {
+      ok = false;
+    }
+    // lse (scaled to log2) or D of one of the step's 64 queries: thread t < 128
+    // fetches entry t of the step's [lse 64 | D 64] staging slot
+    auto fetch = [&](int i) -> float {
+      const int hq = h_first + i / nq, qa = (qi0 + i % nq) * 64 + (t & 63);
+      const size_t ix = (static_cast<size_t>(b) * H + hq) * S + qa;
+      return qa < S ? (t < 64 ? lse[ix] * LOG2E : Dv[ix]) : 0.f;
+    };
+    float pre = (t < 128 && n_it > 0) ? fetch(0) : 0.f;
+    for (int it = 0; ok && it < n_it; ++it) {
+      const int st = it & 1, ts = it % L::NSET;
+      const int qbase = (qi0 + it % nq) * 64;
+      // stage this step's lse and D (double-buffered by step parity; slot st is
+      // rewritten two steps later, after every reader has arrived on the other
+      // slot's barrier), then fetch the next step's while this one computes
+      float* slot = stage_ld + st * 128;
+      if (t < 128) slot[t] = pre;
+      mbar_arrive(&ld_ready[st]);
+      if (t < 128 && it + 1 < n_it) pre = fetch(it + 1);
+      WAIT_OR_BREAK(&ld_ready[st], (it >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      WAIT_OR_BREAK(&s_full[ts], (it / L::NSET) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      tc_fence_after();
+      // this warp's 32 queries: S^T columns [hf*32, +32), dP^T columns 64 + [hf*32, +32)
+      float lse2[32], dqs[32];
+      {
+        const float4* l4 = reinterpret_cast<const float4*>(slot + hf * 32);
+        const float4* d4 = reinterpret_cast<const float4*>(slot + 64 + hf * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 a = l4[i], d = d4[i];
+          lse2[4 * i] = a.x; lse2[4 * i + 1] = a.y; lse2[4 * i + 2] = a.z; lse2[4 * i + 3] = a.w;
+          dqs[4 * i] = d.x * scale; dqs[4 * i + 1] = d.y * scale; dqs[4 * i + 2] = d.z * scale; dqs[4 * i + 3] = d.w * scale;
+        }
+      }
+      const uint32_t sa = lane_addr + ts * 128 + hf * 32;
+      uint32_t sv[32], dpv[32];
+      tmem_ld_32x32b_x32(sa, sv);
+      tmem_ld_32x32b_x32(sa + 64, dpv);
+      tmem_ld_wait();
+      // every query of this half is past every key of the tile and inside
+      // the sequence: no mask (warp-uniform test)
+      const int q_lo = qbase + hf * 32;
+      if (q_lo >= k0 + 127 && q_lo + 32 <= S && k0 + 128 <= S) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float p = fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2[e]));
+          const float ds = p * fmaf(__uint_as_float(dpv[e]), scale, -dqs[e]);
+          sv[e] = tf32_bits(p);
+          dpv[e] = tf32_bits(ds);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int qa = q_lo + e;
+          const bool valid = qa < S && key < S && key <= qa;
+          const float p = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2[e])) : 0.f;
+          const float ds = p * fmaf(__uint_as_float(dpv[e]), scale, -dqs[e]);
+          sv[e] = tf32_bits(p);
+          dpv[e] = tf32_bits(ds);
+        }
+      }
+      tmem_st_32x32b_x32(sa, sv);
+      tmem_st_32x32b_x32(sa + 64, dpv);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[ts]);
     }
     if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
       tc_fence_after();
-      // final dk/dv at the KV head's columns, or per-query-head partials
+      // final dk/dv at the KV head's columns, or per-query-head partials;
+      // column half 0 writes dV, half 1 writes dK
       const int oh = per_head ? h_first : kh;
       const size_t trow = static_cast<size_t>(row_base) + key;
+      const int part = hf;
 #pragma unroll 1
-      for (int part = 0; part < 2; ++part) {  // 0: dV, 1: dK
-#pragma unroll 1
-        for (int cc = 0; cc < HD / 32; ++cc) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(lane_addr + (part == 0 ? L::DV_COL : L::DK_COL) + cc * 32, v);
-          tmem_ld_wait();
-          if (key < S) {
-            float* dst = (part == 0 ? dv_out + trow * dv_ld : dk_out + trow * dk_ld) + oh * HD + cc * 32;
-            const bool rnd = part == 0 && round_dv;
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_addr + (part == 0 ? L::DV_COL : L::DK_COL) + cc * 32, v);
+        tmem_ld_wait();
+        if (key < S) {
+          float* dst = (part == 0 ? dv_out + trow * dv_ld : dk_out + trow * dk_ld) + oh * HD + cc * 32;
+          const bool rnd = part == 0 && round_dv;
 #pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              float4 o4 = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
-                                      __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
-              if (rnd) o4 = make_float4(round_tf32(o4.x), round_tf32(o4.y), round_tf32(o4.z), round_tf32(o4.w));
-              reinterpret_cast<float4*>(dst)[g] = o4;
-            }
+          for (int g = 0; g < 8; ++g) {
+            float4 o4 = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
+                                    __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
+            if (rnd) o4 = make_float4(round_tf32(o4.x), round_tf32(o4.y), round_tf32(o4.z), round_tf32(o4.w));
+            reinterpret_cast<float4*>(dst)[g] = o4;
           }
         }
       }
@@ -564,19 +673,25 @@ __global__ void group_sum_kernel(const float* __restrict__ pk, const float* __re
 }
 
 // ===================================================================== dQ
-// TMEM: two sets of {S [0,64), dP [64,128)} at cols 0 and 128, dQ at 256.  The
-// math warps overwrite S with dS in place; dQ += dS K reads it from TMEM.  The
-// 64-key K/V tiles are double-buffered and the MMA thread issues S/dP of step
-// j before dQ of step j-1.
+// TMEM: two sets of {S [0,64), dP [64,128)} at cols 0 and 128, then Q and dO
+// (the A operands of S = Q K^T and dP = dO V^T) and dQ, HD columns each.  The
+// math warps overwrite S with dS in place; dQ += dS K reads it from TMEM.
+// With Q and dO out of shared memory, four 64-key K/V stages fit: Q and dO
+// first land in the space of stages 2 and 3, are copied row by row into TMEM
+// by the math warps, and the space is then released to the producer.  The
+// MMA thread issues S/dP of step j before dQ of step j-1.
 template <int HD>
 struct DqLayout {
   static constexpr int Q = 128 * HD * 4, O = 128 * HD * 4;
   static constexpr int KT = 64 * HD * 4;              // one 64-key operand tile
   static constexpr int STAGE = 3 * KT;                // K (K-major), K (MN-major), V (K-major)
-  static constexpr int OFF_O = Q, OFF_KV = OFF_O + O, OFF_BAR = OFF_KV + 2 * STAGE;
+  static constexpr int NST = 4, NSET = 2;             // smem K/V stages, TMEM S/dP sets
+  static constexpr int OFF_QO = 2 * STAGE;            // Q and dO land in stages 2..3
+  static constexpr int OFF_BAR = NST * STAGE;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;
   static constexpr int TMEM_COLS = 512;
-  static constexpr int DQ_COL = 256;
+  static constexpr int Q_COL = 256, O_COL = 256 + HD, DQ_COL = 256 + 2 * HD;
+  static_assert(Q + O <= 2 * STAGE, "Q and dO fit in two stages");
 };
 
 template <int HD>
@@ -590,9 +705,9 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
-  uint64_t *qo_full = bars, *kv_full = bars + 1, *kv_empty = bars + 3, *s_full = bars + 5, *p_full = bars + 7,
-           *set_free = bars + 9, *acc_done = bars + 11, *drain = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t *qo_full = bars, *kv_full = bars + 1, *kv_empty = bars + 5, *s_full = bars + 9, *p_full = bars + 11,
+           *set_free = bars + 13, *acc_done = bars + 15, *drain = bars + 16, *qo_moved = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const Roles ro;
   const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);
@@ -603,11 +718,14 @@ __global__ void __launch_bounds__(NT, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(qo_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    mbar_init(qo_moved, MATH_THREADS);
+    for (int i = 0; i < L::NST; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < L::NSET; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], MATH_THREADS);
       mbar_init(&set_free[i], 1);
     }
     mbar_init(acc_done, 1);
@@ -625,23 +743,26 @@ __global__ void __launch_bounds__(NT, 1)
   if (ro.warp == 0) {
     if (ro.lane == 0) {
       mbar_arrive_expect_tx(qo_full, L::Q + L::O);
-      tma_tile<HD, 128>(sm, &tmQ, qo_full, h * HD, row_base + q0);
-      tma_tile<HD, 128>(sm + L::OFF_O, &tmO, qo_full, h * HD, row_base + q0);
-      int armed[2] = {-1, -1};
+      tma_tile<HD, 128>(sm + L::OFF_QO, &tmQ, qo_full, h * HD, row_base + q0);
+      tma_tile<HD, 128>(sm + L::OFF_QO + L::Q, &tmO, qo_full, h * HD, row_base + q0);
+      int armed[L::NST] = {-1, -1, -1, -1};
       bool ok = true;
       for (int j = 0; j < nk; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        const int st = j % L::NST;
+        const uint32_t ph = (j / L::NST) & 1;
+        // stages 2 and 3 hold Q and dO until the math warps have moved them to TMEM
+        if (j == 2 && !mbar_wait(qo_moved, 0, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        if (!mbar_wait(&kv_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
         mbar_arrive_expect_tx(&kv_full[st], L::STAGE);
-        uint8_t* base = sm + L::OFF_KV + st * L::STAGE;
+        uint8_t* base = sm + st * L::STAGE;
         tma_tile<HD, 64>(base, &tmKk, &kv_full[st], kh * HD, row_base + j * 64);
         tma_tile<HD, 64>(base + L::KT, &tmKm, &kv_full[st], kh * HD, row_base + j * 64);
         tma_tile<HD, 64>(base + 2 * L::KT, &tmVk, &kv_full[st], kh * HD, row_base + j * 64);
-        armed[st] = (j >> 1) & 1;
+        armed[st] = static_cast<int>(ph);
       }
       if (!ok) {
         mbar_drain(qo_full, 0, err);
-        for (int st = 0; st < 2; ++st)
+        for (int st = 0; st < L::NST; ++st)
           if (armed[st] >= 0) mbar_drain(&kv_full[st], static_cast<uint32_t>(armed[st]), err);
       }
     }
@@ -649,34 +770,36 @@ __global__ void __launch_bounds__(NT, 1)
     if (ro.lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_tf32(128, 64, false, false);
       constexpr uint32_t idesc_q = umma_idesc_tf32(128, HD, false, true);
-      bool ok = mbar_wait(qo_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
+      // Q and dO are A operands in TMEM once the math warps have copied them
+      bool ok = mbar_wait(qo_moved, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
       bool issued = false;
+      tc_fence_after();
       for (int j = 0; ok && j <= nk; ++j) {
         if (j < nk) {
-          const int st = j & 1;
-          const uint32_t base = s0 + L::OFF_KV + st * L::STAGE;
-          if (!mbar_wait(&kv_full[st], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-          if (!mbar_wait(&set_free[st], ((j >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
+          const int st = j % L::NST, ts = j % L::NSET;
+          const uint32_t base = s0 + st * L::STAGE;
+          if (!mbar_wait(&kv_full[st], (j / L::NST) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          if (!mbar_wait(&set_free[ts], ((j / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < HD / 8; ++kk) {
-            umma_tf32(tmem + st * 128, kdesc<128>(s0, kk), kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
-            umma_tf32(tmem + st * 128 + 64, kdesc<128>(s0 + L::OFF_O, kk), kdesc<64>(base + 2 * L::KT, kk), idesc_s,
-                      kk > 0 ? 1u : 0u);
+            umma_tf32_ts(tmem + ts * 128, tmem + L::Q_COL + kk * 8, kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
+            umma_tf32_ts(tmem + ts * 128 + 64, tmem + L::O_COL + kk * 8, kdesc<64>(base + 2 * L::KT, kk), idesc_s,
+                         kk > 0 ? 1u : 0u);
           }
           issued = true;
-          umma_commit(&s_full[st]);
+          umma_commit(&s_full[ts]);
         }
         if (j >= 1) {
-          const int pj = j - 1, ps = pj & 1;
-          const uint32_t base = s0 + L::OFF_KV + ps * L::STAGE;
-          if (!mbar_wait(&p_full[ps], (pj >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          const int pj = j - 1, ps = pj % L::NST, pts = pj % L::NSET;
+          const uint32_t base = s0 + ps * L::STAGE;
+          if (!mbar_wait(&p_full[pts], (pj / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_tf32_ts(tmem + L::DQ_COL, tmem + ps * 128 + kk * 8, mdesc<64>(base + L::KT, kk), idesc_q,
+            umma_tf32_ts(tmem + L::DQ_COL, tmem + pts * 128 + kk * 8, mdesc<64>(base + L::KT, kk), idesc_q,
                          (pj > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&set_free[ps]);
+          umma_commit(&set_free[pts]);
           umma_commit(&kv_empty[ps]);
         }
       }
@@ -687,42 +810,62 @@ __global__ void __launch_bounds__(NT, 1)
       }
     }
   } else {
-    const int q = ro.warp & 3;
+    const int q = ro.quarter(), hf = ro.half();
     const int r = q * 32 + ro.lane;
     const int qa = q0 + r;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const size_t lrow = (static_cast<size_t>(b) * H + h) * S + (qa < S ? qa : 0);
     const float lse2 = lse[lrow] * LOG2E, Dq = Dv[lrow];
     bool ok = true;
-    for (int j = 0; j < nk; ++j) {
-      const int st = j & 1;
-      WAIT_OR_BREAK(&s_full[st], (j >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
-      tc_fence_after();
-      const uint32_t sa = lane_addr + st * 128;
-      uint32_t sv[64], dpv[64];
-      tmem_ld_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
-      tmem_ld_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-      tmem_ld_32x32b_x32(sa + 64, *reinterpret_cast<uint32_t(*)[32]>(dpv + 0));
-      tmem_ld_32x32b_x32(sa + 96, *reinterpret_cast<uint32_t(*)[32]>(dpv + 32));
-      tmem_ld_wait();
-#pragma unroll
-      for (int e = 0; e < 64; ++e) {
-        const int key = j * 64 + e;
-        const bool valid = qa < S && key < S && key <= qa;
-        const float p = valid ? fast_exp2(__uint_as_float(sv[e]) * scale_log2 - lse2) : 0.f;
-        sv[e] = tf32_bits(p * (__uint_as_float(dpv[e]) - Dq) * scale);
-      }
-      tmem_st_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
-      tmem_st_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+    // Q and dO rows -> TMEM, then release stages 2..3 and start the MMA thread
+    if (__all_sync(0xffffffffu, mbar_wait(qo_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
+      tile_rows_to_tmem<HD>(sm + L::OFF_QO, r, lane_addr, L::Q_COL, 0, hf);
+      tile_rows_to_tmem<HD>(sm + L::OFF_QO + L::Q, r, lane_addr, L::O_COL, HD / 32, hf);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[st]);
+      mbar_arrive(qo_moved);
+    } else {
+      ok = false;
+    }
+    for (int j = 0; ok && j < nk; ++j) {
+      const int ts = j % L::NSET;
+      WAIT_OR_BREAK(&s_full[ts], (j / L::NSET) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      tc_fence_after();
+      // this warp's 32 keys: S columns [hf*32, +32), dP columns 64 + [hf*32, +32)
+      const uint32_t sa = lane_addr + ts * 128 + hf * 32;
+      uint32_t sv[32], dpv[32];
+      tmem_ld_32x32b_x32(sa, sv);
+      tmem_ld_32x32b_x32(sa + 64, dpv);
+      tmem_ld_wait();
+      const int k_lo = j * 64 + hf * 32;
+      const float nDs = -Dq * scale;
+      // every key of this half precedes every row of the tile: no mask
+      // (warp-uniform test)
+      if (k_lo + 32 <= q0 + 1 && q0 + 128 <= S) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float p = fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2));
+          sv[e] = tf32_bits(p * fmaf(__uint_as_float(dpv[e]), scale, nDs));
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int key = k_lo + e;
+          const bool valid = qa < S && key < S && key <= qa;
+          const float p = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2)) : 0.f;
+          sv[e] = tf32_bits(p * fmaf(__uint_as_float(dpv[e]), scale, nDs));
+        }
+      }
+      tmem_st_32x32b_x32(sa, sv);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[ts]);
     }
     if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
       tc_fence_after();
       float* drow = dq + (static_cast<size_t>(row_base) + qa) * static_cast<size_t>(dq_ld) + h * HD;
 #pragma unroll 1
-      for (int cc = 0; cc < HD / 32; ++cc) {
+      for (int cc = hf; cc < HD / 32; cc += 2) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(lane_addr + L::DQ_COL + cc * 32, v);
         tmem_ld_wait();

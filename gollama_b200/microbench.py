@@ -70,7 +70,7 @@ def case_linear_sweep(ctx, iters, warmup):
     return out
 
 
-def case_attention(ctx, kind, iters, warmup, B=4):
+def case_attention(ctx, kind, iters, warmup, B=4, S=S):
     Tq = B * S
     q, k, v = _rand(ctx, (Tq, H * HD), 4), _rand(ctx, (Tq, HKV * HD), 5), _rand(ctx, (Tq, HKV * HD), 6)
     dO = _rand(ctx, (Tq, H * HD), 7)
@@ -134,6 +134,10 @@ CASES = {
     "linear_sweep": case_linear_sweep,
     "attention_fwd": lambda c, i, w: case_attention(c, "fwd", i, w),
     "attention_bwd": lambda c, i, w: case_attention(c, "bwd", i, w),
+    "attention_fwd_s2048": lambda c, i, w: case_attention(c, "fwd", i, w, S=2048),
+    "attention_bwd_s2048": lambda c, i, w: case_attention(c, "bwd", i, w, S=2048),
+    "attention_fwd_s256": lambda c, i, w: case_attention(c, "fwd", i, w, B=16, S=256),
+    "attention_bwd_s256": lambda c, i, w: case_attention(c, "bwd", i, w, B=16, S=256),
     "swiglu_bwd": case_swiglu,
     "rmsnorm_bwd": case_rmsnorm,
     "softmax_ce": case_ce,
