@@ -101,10 +101,15 @@ int nccl_wait(Context* c, ncclResult_t r, const char* what) {
 
 }  // namespace
 
-int dp_allreduce_grads(Context* c, float* buf, size_t n) {
+int dp_allreduce_grads(Context* c, float* buf, size_t n) { return dp_allreduce_on(c, buf, n, c->stream); }
+
+// Enqueues an in-place fp32 sum over the ranks on `stream` and returns once
+// NCCL has accepted it (the reduction itself runs asynchronously).
+int dp_allreduce_on(Context* c, float* buf, size_t n, cudaStream_t stream) {
   Comm* cm = comm_of(c);
   if (!cm || !cm->comm) return c->fail(GLC_ERR_NCCL, "allreduce: data parallelism not initialised (glc_dp_init)");
-  ncclResult_t r = nccl().AllReduce(buf, buf, n, ncclFloat, ncclSum, cm->comm, c->stream);
+  if (n == 0) return 0;
+  ncclResult_t r = nccl().AllReduce(buf, buf, n, ncclFloat, ncclSum, cm->comm, stream);
   return nccl_wait(c, r, "ncclAllReduce");
 }
 

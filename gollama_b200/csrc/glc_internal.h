@@ -151,6 +151,9 @@ int swiglu_bwd(Context* ctx, const float* g, const float* u, size_t ld_in, const
                float* du, size_t ld_out, size_t rows, size_t cols, bool accumulate, bool round_out, cudaStream_t s);
 int fill(Context* ctx, float* p, float v, size_t n, cudaStream_t s);
 int round_copy(Context* ctx, const float* src, float* dst, size_t n, cudaStream_t s);
+// data parallel (dp.cu): in-place fp32 sum over the ranks
+int dp_allreduce_grads(Context* c, float* buf, size_t n);
+int dp_allreduce_on(Context* c, float* buf, size_t n, cudaStream_t stream);
 int exp32(Context* ctx, const float* x, float* y, size_t n, cudaStream_t s);
 int add_inplace(Context* ctx, float* dst, const float* src, size_t n, cudaStream_t s);
 // x: T rows of row stride ld (elements); the first nh*hd columns are rotated.

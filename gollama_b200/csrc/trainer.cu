@@ -198,7 +198,11 @@ class Tape {
   // gradient, DFS topological order over Parents, GradFns in reverse.
   // seed_in_place reuses the root's data buffer for the ones (the caller
   // guarantees nothing reads it afterwards).
-  void backward(Node* root, bool seed_in_place) {
+  // `before` sees the GradFn order before any runs; `after` is called once
+  // each GradFn has been enqueued (its gradients are final on the stream).
+  using OrderHook = std::function<void(const std::vector<Node*>&)>;
+  using NodeHook = std::function<void(Node*)>;
+  void backward(Node* root, bool seed_in_place, const OrderHook& before = nullptr, const NodeHook& after = nullptr) {
     if (!root->grad_live) {
       if (!root->grad) root->grad = seed_in_place ? root->data : alloc(root->numel());
       ck(fill(ctx_, root->grad, 1.0f, static_cast<size_t>(root->numel()), stream()));
@@ -208,8 +212,14 @@ class Tape {
     std::vector<Node*> order;
     seen_.clear();
     topo(root, order);
+    std::vector<Node*> run;
     for (auto it = order.rbegin(); it != order.rend(); ++it)
-      if ((*it)->grad_fn) (*it)->grad_fn();
+      if ((*it)->grad_fn) run.push_back(*it);
+    if (before) before(run);
+    for (Node* n : run) {
+      n->grad_fn();
+      if (after) after(n);
+    }
   }
 
  private:
@@ -247,20 +257,34 @@ struct Model {
   std::vector<Node> qkv_view, gu_view;  // per layer: WQ|WK|WV and WGate|WUp
 
   int num_params() const { return static_cast<int>(offset.size()); }
+  // Gradient buckets for the data-parallel sum, contiguous in the arena: the
+  // front parameters (embedding, and positions in reference mode), one per
+  // layer, and the output norm.  bucket_of[i] is parameter i's bucket.
+  std::vector<int64_t> bucket_begin, bucket_end;
+  std::vector<int> bucket_of;
+  void plan_buckets() {
+    bucket_begin.clear();
+    bucket_end.clear();
+    bucket_of.assign(num_params(), -1);
+    auto add = [&](int first, int last) {  // parameters [first, last]
+      for (int i = first; i <= last; ++i) bucket_of[i] = static_cast<int>(bucket_begin.size());
+      bucket_begin.push_back(offset[first]);
+      bucket_end.push_back(offset[last] + rows[last] * cols[last]);
+    };
+    add(0, front() - 1);
+    for (int l = 0; l < cfg.num_layers; ++l) add(lp(l, 0), lp(l, P_PER_LAYER - 1));
+    add(out_norm(), out_norm());
+  }
   int front() const { return llama ? 1 : 2; }
   int lp(int layer, int which) const { return front() + layer * P_PER_LAYER + which; }
   int out_norm() const { return num_params() - 1; }
 
   ~Model() {
-    cudaFree(params);
-    cudaFree(grads);
-    cudaFree(m);
-    cudaFree(v);
-    cudaFree(shadow);
-    cudaFree(cos_t);
-    cudaFree(sin_t);
+    for (float* p : {params, grads, m, v, shadow, cos_t, sin_t})
+      if (p) cudaFree(p);
   }
 
+  bool layout(const glc_train_config& conf);
   int init(Context* c, const glc_train_config& conf);
   void bind_param_nodes() {
     param_nodes.assign(num_params(), Node());
@@ -541,17 +565,15 @@ __global__ void init_normal_kernel(float* p, int64_t n, uint64_t seed, float std
 
 }  // namespace
 
-int Model::init(Context* c, const glc_train_config& conf) {
-  ctx = c;
+// Parameter layout in Params() order (host only; no device work).
+bool Model::layout(const glc_train_config& conf) {
   cfg = conf;
   llama = cfg.semantics == GLC_SEMANTICS_LLAMA;
   if (cfg.num_kv_heads <= 0 || !llama) cfg.num_kv_heads = cfg.num_heads;
   if (cfg.num_heads <= 0 || cfg.hidden_size % cfg.num_heads || cfg.num_heads % cfg.num_kv_heads || cfg.vocab_size <= 0 ||
       cfg.num_layers < 0 || cfg.intermediate_size <= 0 || cfg.max_seq_len <= 0 || (cfg.hidden_size & 3) ||
       (cfg.intermediate_size & 3) || (cfg.vocab_size & 3))
-    return c->fail(GLC_ERR_INVALID,
-                  "model: inconsistent configuration (heads must divide hidden, kv heads must divide heads; hidden, "
-                  "intermediate and vocab sizes must be multiples of 4)");
+    return false;
   hd = cfg.hidden_size / cfg.num_heads;
   kvh = cfg.num_kv_heads;
   const int64_t d = cfg.hidden_size, F = cfg.intermediate_size, kvd = static_cast<int64_t>(kvh) * hd;
@@ -575,6 +597,16 @@ int Model::init(Context* c, const glc_train_config& conf) {
     add(d, F);
   }
   add(1, d);
+  plan_buckets();
+  return true;
+}
+
+int Model::init(Context* c, const glc_train_config& conf) {
+  ctx = c;
+  if (!layout(conf))
+    return c->fail(GLC_ERR_INVALID,
+                  "model: inconsistent configuration (heads must divide hidden, kv heads must divide heads; hidden, "
+                  "intermediate and vocab sizes must be multiples of 4)");
   const size_t bytes = sizeof(float) * static_cast<size_t>(total);
   for (float** p : {&params, &grads, &m, &v, &shadow}) {
     if (cudaMalloc(p, bytes) != cudaSuccess) return c->fail(GLC_ERR_NOMEM, "model: cannot allocate parameter arenas");
@@ -637,8 +669,15 @@ struct Trainer {
   int nseg = 0;
   int64_t seg_elems = 0;
   std::vector<char> segs_for;
+  // data-parallel gradient buckets (Model::plan_buckets): per-step state
+  std::vector<cudaEvent_t> bucket_ev;
+  cudaEvent_t comm_done = nullptr;
+  std::vector<int> consumers, bucket_pending;
+  std::vector<char> bucket_launched;
 
   ~Trainer() {
+    for (cudaEvent_t e : bucket_ev) cudaEventDestroy(e);
+    if (comm_done) cudaEventDestroy(comm_done);
     cudaFree(scalars);
     cudaFreeHost(loss_host);
     cudaFree(tok_dev);
@@ -683,8 +722,6 @@ struct Trainer {
   int train_step(const int64_t* in_dev, const int64_t* tg_dev, const int64_t* in_host, int B, int S, float* loss_out);
 };
 
-int dp_allreduce_grads(Context* ctx, float* buf, size_t n);  // dp.cpp
-
 int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int64_t* in_host, int B, int S,
                         float* loss_out) {
   const auto& c = model->cfg;
@@ -714,6 +751,62 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
     float* d_scale = d_loss + 1;
     double* d_norm = reinterpret_cast<double*>(static_cast<char*>(scalars) + 8);
     const int W = c.world_size > 0 ? c.world_size : 1;
+    // Gradient hooks.  Before the GradFns run, count each parameter's
+    // consumers in the run order (the tied embedding has two; the fused
+    // q/k/v and gate/up views count for each member) and zero the allocated
+    // gradients nothing will write.  With W > 1, each GradFn's completion
+    // lowers its parameters' counts; a bucket whose parameters are all final
+    // is summed over the ranks on the communication stream while the
+    // backward continues on the compute stream.
+    const bool dp = W > 1;
+    const int np = model->num_params(), nb = static_cast<int>(model->bucket_begin.size());
+    if (dp && static_cast<int>(bucket_ev.size()) != nb) {
+      for (int b = static_cast<int>(bucket_ev.size()); b < nb; ++b) {
+        cudaEvent_t e;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) throw StepError{GLC_ERR_CUDA};
+        bucket_ev.push_back(e);
+      }
+      if (!comm_done && cudaEventCreateWithFlags(&comm_done, cudaEventDisableTiming) != cudaSuccess)
+        throw StepError{GLC_ERR_CUDA};
+    }
+    auto for_params = [](Node* p, const std::function<void(int)>& f) {
+      if (p->param >= 0) f(p->param);
+      for (int i : p->group) f(i);
+    };
+    auto launch_bucket = [&](int b) {
+      if (bucket_launched[b]) return;
+      bucket_launched[b] = 1;
+      if (cudaEventRecord(bucket_ev[b], ctx->stream) != cudaSuccess ||
+          cudaStreamWaitEvent(ctx->comm_stream, bucket_ev[b], 0) != cudaSuccess)
+        throw StepError{GLC_ERR_CUDA};
+      ck(dp_allreduce_on(ctx, model->grads + model->bucket_begin[b],
+                         static_cast<size_t>(model->bucket_end[b] - model->bucket_begin[b]), ctx->comm_stream));
+    };
+    const Tape::OrderHook before = [&](const std::vector<Node*>& run) {
+      consumers.assign(np, 0);
+      for (Node* n : run)
+        for (Node* p : n->parents) for_params(p, [&](int i) { ++consumers[i]; });
+      for (int i = 0; i < np; ++i)
+        if (consumers[i] == 0 && model->grad_allocated[i] && !model->grad_live[i]) {
+          if (cudaMemsetAsync(model->grads + model->offset[i], 0, sizeof(float) * model->rows[i] * model->cols[i],
+                              ctx->stream) != cudaSuccess)
+            throw StepError{GLC_ERR_CUDA};
+          model->grad_live[i] = 1;
+        }
+      if (dp) {
+        bucket_pending.assign(nb, 0);
+        bucket_launched.assign(nb, 0);
+        for (int i = 0; i < np; ++i)
+          if (consumers[i] > 0) ++bucket_pending[model->bucket_of[i]];
+      }
+    };
+    const Tape::NodeHook after = [&](Node* n) {
+      if (!dp) return;
+      for (Node* p : n->parents)
+        for_params(p, [&](int i) {
+          if (--consumers[i] == 0 && --bucket_pending[model->bucket_of[i]] == 0) launch_bucket(model->bucket_of[i]);
+        });
+    };
     if (model->llama) {
       // loss node with the CE GradFn; the kernel writes (p - onehot)/N over
       // the logits, which nothing reads afterwards.  With W data-parallel
@@ -728,11 +821,11 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
         logits->grad_live = true;
         logits->grad_round = logits->data;
       };
-      tape->backward(lossn, false);
+      tape->backward(lossn, false, before, after);
     } else {
       ck(softmax_ce(ctx, logits->data, tg_dev, T, c.vocab_size, 1.0f, row_logp, d_loss, false, false, ctx->stream));
       // logits.Backward(): Grad is nil, so it is seeded with ones (grad.go:45-50)
-      tape->backward(logits, true);
+      tape->backward(logits, true, before, after);
     }
     // a parameter whose gradient exists but received nothing this step is zero
     for (int i = 0; i < model->num_params(); ++i)
@@ -743,7 +836,14 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
         model->grad_live[i] = 1;
       }
     refresh_segments();
-    if (W > 1) ck(dp_allreduce_grads(ctx, model->grads, static_cast<size_t>(model->total)));
+    if (dp) {
+      // buckets no GradFn completed (no consumer this step), then clipping
+      // waits for every sum
+      for (int b = 0; b < nb; ++b) launch_bucket(b);
+      if (cudaEventRecord(comm_done, ctx->comm_stream) != cudaSuccess ||
+          cudaStreamWaitEvent(ctx->stream, comm_done, 0) != cudaSuccess)
+        throw StepError{GLC_ERR_CUDA};
+    }
     if (nseg > 0) {
       // GradientClipping (optimizer.go:169-196) then AdamW.Step (:37-76)
       ck(grad_norm(ctx, model->grads, segs_dev, nseg, c.grad_clip_norm, d_norm, d_scale, nullptr, 0,
@@ -842,6 +942,19 @@ int glc_model_num_params(glc_model* m, int* n, int64_t* total) {
   if (!m) return GLC_ERR_INVALID;
   if (n) *n = m->impl.num_params();
   if (total) *total = m->impl.total;
+  return GLC_OK;
+}
+
+int glc_dp_bucket_plan(const glc_train_config* cfg, int64_t* begin, int64_t* end, int capacity, int* count) {
+  if (!cfg || !count || capacity < 0 || (capacity > 0 && (!begin || !end))) return GLC_ERR_INVALID;
+  glc::Model model;  // layout only: no device memory
+  if (!model.layout(*cfg)) return GLC_ERR_INVALID;
+  const int n = static_cast<int>(model.bucket_begin.size());
+  *count = n;
+  for (int i = 0; i < n && i < capacity; ++i) {
+    begin[i] = model.bucket_begin[i];
+    end[i] = model.bucket_end[i];
+  }
   return GLC_OK;
 }
 

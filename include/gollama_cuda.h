@@ -300,6 +300,16 @@ GLC_API int glc_dp_allreduce_sum(glc_ctx* ctx, float* buf, size_t n);
 GLC_API int glc_dp_allreduce_max_host(glc_ctx* ctx, double* value);
 GLC_API int glc_dp_barrier(glc_ctx* ctx);
 GLC_API int glc_dp_destroy(glc_ctx* ctx);
+/* Gradient buckets of the data-parallel sum for a configuration (host only,
+ * no device needed; no reference counterpart): [begin[i], end[i]) in floats
+ * of the gradient arena, contiguous and covering it: the front parameters
+ * (embedding, plus positions in reference mode), one bucket per layer, and
+ * the output norm.  During glc_train_step with world_size > 1, a bucket is
+ * summed over the ranks on the context's communication stream as soon as the
+ * last GradFn writing it has been enqueued, overlapping the rest of the
+ * backward.  *count receives the number of buckets; at most `capacity` are
+ * written. */
+GLC_API int glc_dp_bucket_plan(const glc_train_config* cfg, int64_t* begin, int64_t* end, int capacity, int* count);
 
 #ifdef __cplusplus
 }
