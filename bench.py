@@ -94,17 +94,24 @@ class ClockSampler:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self):
+    def __init__(self, n_gpus: int = 1):
         self.proc = None
         self.path = None
+        # only this job's GPUs: polling every GPU of a shared box takes driver
+        # locks on all of them, and with data parallelism a stall on any rank
+        # holds up every rank's next gradient sum
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").strip()
+        ids = [x.strip() for x in vis.split(",") if x.strip()] if vis else [str(i) for i in range(n_gpus)]
+        self.ids = ",".join(ids[:n_gpus])
 
     def start(self):
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.ids, f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
@@ -362,11 +369,13 @@ def run_ours(args):
     for i in range(W):
         step_device(i)
     ctx.sync()
-    barrier()
-    sampler = ClockSampler() if rank == 0 else None
+    # the sampler starts (and settles) before the barrier, so every rank's
+    # timer starts together
+    sampler = ClockSampler(world) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
+    barrier()
     l0 = ctx.launches()
     ms = C.c_float()
     ctx.call("glc_timer_start")
@@ -479,6 +488,9 @@ def run_ours(args):
 
 def main():
     args = parse_args()
+    # rank 0's stdout must be exactly one JSON line; NCCL prints a version
+    # banner to stdout at communicator creation below level WARN
+    os.environ["NCCL_DEBUG"] = "WARN"
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
