@@ -89,6 +89,20 @@ def case_attention(ctx, kind, iters, warmup, B=4, S=S):
     return f"attention_{kind} B={B} S={S} H={H}/{HKV} hd={HD}", ms, flops / (ms * 1e-3) / 1e12, "TFLOP/s"
 
 
+def case_quant_dx(ctx, qtype, iters, warmup, M=16384, K=D, N=F):
+    """dX [M, K] = dY [M, N] . deq(W) with W [N, K] stored as Q8_0 (8) or Q4_0 (2):
+    fp16 scales U(0.005, 0.02), random codes."""
+    r = np.random.default_rng(qtype)
+    nb = N * K // 32
+    scale = r.uniform(0.005, 0.02, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    codes = r.integers(0, 256, (nb, 32 if qtype == 8 else 16), dtype=np.uint8)
+    w = ctx.from_numpy(np.ascontiguousarray(np.concatenate([scale, codes], axis=1)).reshape(-1))
+    dy, dx = _rand(ctx, (M, N), 15), ctx.empty((M, K))
+    ms = _time(ctx, lambda: ctx.call("glc_linear_bwd_dx_q", dy.ptr, w.ptr, qtype, dx.ptr, M, K, N, 0), iters, warmup)
+    name = "Q8_0" if qtype == 8 else "Q4_0"
+    return f"linear_bwd_dx_q {name} M={M} K={K} N={N}", ms, 2.0 * M * N * K / (ms * 1e-3) / 1e12, "TFLOP/s"
+
+
 def case_swiglu(ctx, iters, warmup):
     gu = _rand(ctx, (T, 2 * F), 8, tf32=False)
     dh = _rand(ctx, (T, F), 9, tf32=False)
@@ -139,6 +153,8 @@ CASES = {
     "attention_fwd_s256": lambda c, i, w: case_attention(c, "fwd", i, w, B=16, S=256),
     "attention_bwd_s256": lambda c, i, w: case_attention(c, "bwd", i, w, B=16, S=256),
     "swiglu_bwd": case_swiglu,
+    "quant_dx_q8_0": lambda c, i, w: case_quant_dx(c, 8, i, w),
+    "quant_dx_q4_0": lambda c, i, w: case_quant_dx(c, 2, i, w),
     "rmsnorm_bwd": case_rmsnorm,
     "softmax_ce": case_ce,
 }

@@ -119,6 +119,24 @@ GLC_API int glc_linear_bwd_dw(glc_ctx* ctx, const float* dY, const float* X, flo
  * dX or dW may be NULL when that gradient is not required. */
 GLC_API int glc_linear_bwd(glc_ctx* ctx, const float* dY, const float* X, const float* W, float* dX, float* dW, int M,
                            int K, int N, int accumulate_dx, int accumulate_dw);
+/* Frozen quantized weights (pkg/quant/dequant.go).  Type codes are GGUF's
+ * (pkg/gguf/format.go:40-46). */
+#define GLC_QTYPE_F32 0
+#define GLC_QTYPE_F16 1
+#define GLC_QTYPE_Q4_0 2
+#define GLC_QTYPE_Q8_0 8
+/* Dequantize (pkg/quant/dequant.go:367-393) of n elements on the device, exact
+ * fp32 results: F16 via fp16ToFp32 (:9-41), Q8_0 (:68-85), Q4_0 (:99-119; low
+ * nibble first).  src 2-byte aligned, dst 16-byte aligned; n a multiple of 4
+ * (of 32 for the block formats). */
+GLC_API int glc_dequantize(glc_ctx* ctx, int type, const void* src, float* dst, size_t n);
+/* dX (+)= dY . deq(W) for a linear layer whose weight W [N out][K in] is stored
+ * quantized row by row: the dA loop of MatMulGrad (pkg/tensor/grad.go:102-116)
+ * applied to the weight the reference dequantizes at load
+ * (pkg/model/transformer.go:285-303).  Uses the context workspace for one
+ * TF32-rounded fp32 copy of W. */
+GLC_API int glc_linear_bwd_dx_q(glc_ctx* ctx, const float* dY, const void* Wq, int type, float* dX, int M, int K,
+                                int N, int accumulate);
 /* General strided form of the three above: C[M,N] (+)= A . B^T (+ R) where
  * a_mn/b_mn select MN-major storage (element (i,k) at ptr[k*ld+i]) instead of
  * K-major (ptr[i*ld+k]).  round_out rounds the stored values to TF32. */

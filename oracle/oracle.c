@@ -369,6 +369,96 @@ void FN(exp32_array)(const float* x, float* y, int64_t n) { /* exp32 over an arr
 
 float FN(log32)(float x) { return (float)FN(go_log)((double)x); } /* grad.go:296-298 */
 
+/* ------------------------------------------------------------------ frozen quantized weights
+ * pkg/quant/dequant.go.  Type codes are GGUF's (pkg/gguf/format.go:40-46):
+ * 0 F32, 1 F16, 2 Q4_0, 8 Q8_0. */
+#ifndef ORC_QTYPES
+#define ORC_QTYPES
+enum { ORC_Q_F32 = 0, ORC_Q_F16 = 1, ORC_Q_Q4_0 = 2, ORC_Q_Q8_0 = 8 };
+#endif
+
+/* fp16ToFp32 (dequant.go:9-41): exact widening; a subnormal half is
+ * normalised by shifting its mantissa up until the implicit bit appears. */
+float FN(fp16_to_fp32)(uint16_t h) {
+  uint32_t sign = (uint32_t)(h >> 15) & 1u, e = (uint32_t)(h >> 10) & 0x1fu, m = (uint32_t)h & 0x3ffu, bits;
+  if (e == 0) {
+    if (m == 0) {
+      bits = sign << 31;
+    } else {
+      int32_t ex = 1;
+      while (!(m & 0x400u)) {
+        m <<= 1;
+        --ex;
+      }
+      m &= 0x3ffu;
+      bits = (sign << 31) | ((uint32_t)(ex + 127 - 15) << 23) | (m << 13);
+    }
+  } else if (e == 31) {
+    bits = (sign << 31) | 0x7f800000u | (m << 13);
+  } else {
+    bits = (sign << 31) | ((e + 127 - 15) << 23) | (m << 13);
+  }
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+static uint16_t rd_u16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); } /* little endian */
+
+/* Dequantize (dequant.go:367-393) for F32, F16 (:50-56), Q8_0 (:68-85: per
+ * 32-element block a half scale then 32 int8 codes, w = scale * q) and Q4_0
+ * (:99-119: a half scale then 16 bytes; element 2i is the low nibble - 8,
+ * element 2i+1 the high nibble - 8).  n counts output elements; block types
+ * need n % 32 == 0.  Products are float32 like the reference's. */
+int FN(dequantize)(const uint8_t* data, real* out, int64_t n, int type) {
+  if (type == ORC_Q_F32) {
+    for (int64_t i = 0; i < n; ++i) {
+      float f;
+      memcpy(&f, data + 4 * i, 4);
+      out[i] = f;
+    }
+    return 0;
+  }
+  if (type == ORC_Q_F16) {
+    for (int64_t i = 0; i < n; ++i) out[i] = FN(fp16_to_fp32)(rd_u16(data + 2 * i));
+    return 0;
+  }
+  if (n % 32) return -1;
+  if (type == ORC_Q_Q8_0) {
+    for (int64_t b = 0; b < n / 32; ++b) {
+      const uint8_t* blk = data + 34 * b;
+      const float scale = FN(fp16_to_fp32)(rd_u16(blk));
+      for (int i = 0; i < 32; ++i) out[32 * b + i] = scale * (float)(int8_t)blk[2 + i];
+    }
+    return 0;
+  }
+  if (type == ORC_Q_Q4_0) {
+    for (int64_t b = 0; b < n / 32; ++b) {
+      const uint8_t* blk = data + 18 * b;
+      const float scale = FN(fp16_to_fp32)(rd_u16(blk));
+      for (int i = 0; i < 16; ++i) {
+        const uint8_t q = blk[2 + i];
+        out[32 * b + 2 * i] = scale * (float)((int)(q & 0x0f) - 8);
+        out[32 * b + 2 * i + 1] = scale * (float)((int)(q >> 4) - 8);
+      }
+    }
+    return 0;
+  }
+  return -1;
+}
+
+/* dX[M,K] += dY[M,N] . deq(W)[N,K] with W's rows (out features) stored as
+ * quantized rows of K (in features): the reference dequantizes the weight
+ * (dequant.go) and runs MatMulGrad's dA loop (grad.go:102-116). */
+int FN(linear_bwd_dx_q)(const real* dy, const uint8_t* wq, int type, real* dx, int M, int K, int N) {
+  real* w = (real*)malloc(sizeof(real) * (size_t)N * (size_t)K);
+  if (!w) return -1;
+  int rc = FN(dequantize)(wq, w, (int64_t)N * K, type);
+  if (rc == 0) FN(matmul_grad_da)(dy, w, dx, M, K, N);
+  free(w);
+  return rc;
+}
+
 /* ------------------------------------------------------------------ SiLU (SiLUGrad, grad.go:417-449) */
 void FN(silu_fwd)(const real* x, real* out, real* sig, int64_t n) {
   for (int64_t i = 0; i < n; ++i) {

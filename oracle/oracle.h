@@ -73,6 +73,9 @@ typedef struct {
   void P##rmsnorm_bwd(const real* x, const real* w, const real* rms, const real* dout, real* dx, real* dw,     \
                       int rows, int cols, int full);                                                          \
   float P##exp32(float x);                                                                                    \
+  float P##fp16_to_fp32(uint16_t h);                                                                          \
+  int P##dequantize(const uint8_t* data, real* out, int64_t n, int type);                                     \
+  int P##linear_bwd_dx_q(const real* dy, const uint8_t* wq, int type, real* dx, int M, int K, int N);          \
   void P##exp32_array(const float* x, float* y, int64_t n);                                                   \
   float P##log32(float x);                                                                                    \
   double P##go_exp(double x);                                                                                 \
