@@ -60,6 +60,7 @@ struct Problem {
   int accumulate;  // C += acc
   int round_out;   // round stored values to TF32 (RN)
   int a_mn, b_mn;  // operand majors
+  int a_3d, b_3d;  // MN-major operand described as [MN/32 chunks][K][32]: one TMA per k-block
   int m_tiles, n_tiles, k_blocks, tiles;
   // Tile order.  Concurrent tiles share the operand of the slow-moving index
   // through L2 and stream the other; the operand of the fast-moving index is
@@ -91,9 +92,12 @@ __device__ __forceinline__ uint64_t operand_desc(bool mn, uint32_t tile_saddr, i
             : umma_sdesc(tile_saddr + kk * 32, /*LBO unused*/ 16, /*SBO: 8 rows*/ 1024, UMMA_LAYOUT_SW128);
 }
 
-__device__ __forceinline__ void load_operand(bool mn, int rows, void* sdst, const CUtensorMap* tm, uint64_t* bar,
-                                             int mn0, int k0) {
-  if (mn) {
+__device__ __forceinline__ void load_operand(bool mn, bool mn3d, int rows, void* sdst, const CUtensorMap* tm,
+                                             uint64_t* bar, int mn0, int k0) {
+  if (mn3d) {
+    // all rows/32 chunks of 32 MN-elements x BK K-rows in one copy (same smem layout)
+    tma_load_3d(sdst, tm, bar, 0, k0, mn0 / 32);
+  } else if (mn) {
     // tensor map dims {MN, K}, box {32, BK}: one 4 KB chunk per 32 MN-elements
     for (int c = 0; c < rows / 32; ++c)
       tma_load_2d(static_cast<uint8_t*>(sdst) + c * (BK * 128), tm, bar, mn0 + 32 * c, k0);
@@ -184,8 +188,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* sA = smem + stage * STAGE_BYTES;
           uint8_t* sB = sA + A_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
-          load_operand(p.a_mn, BM, sA, tmA, &full_bar[stage], t.m0, kb * BK);
-          load_operand(p.b_mn, BN, sB, tmB, &full_bar[stage], t.n0, kb * BK);
+          load_operand(p.a_mn, p.a_3d, BM, sA, tmA, &full_bar[stage], t.m0, kb * BK);
+          load_operand(p.b_mn, p.b_3d, BN, sB, tmB, &full_bar[stage], t.n0, kb * BK);
           in_flight = in_flight < STAGES ? in_flight + 1 : STAGES;
           if (++stage == STAGES) {
             stage = 0;
@@ -340,9 +344,11 @@ constexpr int P_B_BYTES = HALF_ROWS * BK * 4;        // 16 KB
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES; // 32 KB per CTA, 64 KB per pair
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
 
-__device__ __forceinline__ void load_operand_pair(bool mn, void* sdst, const CUtensorMap* tm, uint32_t bar_cluster,
-                                                  int mn0, int k0) {
-  if (mn) {
+__device__ __forceinline__ void load_operand_pair(bool mn, bool mn3d, void* sdst, const CUtensorMap* tm,
+                                                  uint32_t bar_cluster, int mn0, int k0) {
+  if (mn3d) {
+    tma_load_3d_pair(sdst, tm, bar_cluster, 0, k0, mn0 / 32);
+  } else if (mn) {
 #pragma unroll
     for (int c = 0; c < HALF_ROWS / 32; ++c)
       tma_load_2d_pair(static_cast<uint8_t*>(sdst) + c * (BK * 128), tm, bar_cluster, mn0 + 32 * c, k0);
@@ -430,8 +436,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           uint8_t* sB = sA + P_A_BYTES;
           const uint32_t fb = full_leader + stage * 8;
           if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * P_STAGE_BYTES);
-          load_operand_pair(p.a_mn, sA, tmA, fb, a_row, kb * BK);
-          load_operand_pair(p.b_mn, sB, tmB, fb, b_row, kb * BK);
+          load_operand_pair(p.a_mn, p.a_3d, sA, tmA, fb, a_row, kb * BK);
+          load_operand_pair(p.b_mn, p.b_3d, sB, tmB, fb, b_row, kb * BK);
           if (++stage == P_STAGES) {
             stage = 0;
             phase ^= 1;
@@ -588,13 +594,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 
 // ---------------------------------------------------------------- host side
 
-int encode_operand(Context* ctx, CUtensorMap* tm, const float* ptr, int ld, bool mn, int rows_mn, int k, int box_mn) {
-  // Global tensor: K-major operand is [rows_mn][k] with row stride ld;
-  // MN-major operand is [k][rows_mn] with row stride ld.
+// Global tensor: a K-major operand is [rows_mn][k] with row stride ld; an
+// MN-major one [k][rows_mn].  An MN-major operand whose MN extent is a
+// multiple of 32 is described in three dimensions, {32, k, rows_mn/32} with
+// strides {ld, 32} elements, so one box brings all of a tile's 32-element
+// chunks; otherwise 2-D boxes of 32 MN-elements (the partial chunk is
+// zero-filled).  *three_d reports which.
+int encode_operand(Context* ctx, CUtensorMap* tm, const float* ptr, int ld, bool mn, int rows_mn, int k, int box_mn,
+                   int* three_d) {
+  cuuint32_t estr[3] = {1, 1, 1};
+  *three_d = 0;
+  if (mn && rows_mn % 32 == 0 && box_mn % 32 == 0) {
+    cuuint64_t dims[3] = {32, static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows_mn / 32)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, 128};
+    cuuint32_t box[3] = {32, BK, static_cast<cuuint32_t>(box_mn / 32)};
+    *three_d = 1;
+    return ctx->encode_tiled(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(ptr), dims, strides, box,
+                             estr, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  }
   cuuint64_t dims[2];
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
   cuuint32_t box[2];
-  cuuint32_t estr[2] = {1, 1};
   if (mn) {
     dims[0] = static_cast<cuuint64_t>(rows_mn);
     dims[1] = static_cast<cuuint64_t>(k);
@@ -620,9 +640,9 @@ int prepare(Context* ctx, const GemmSpec& g, Problem* p, CUtensorMap* ta, CUtens
   if ((g.A.ld & 3) || (g.B.ld & 3) || (reinterpret_cast<uintptr_t>(g.A.ptr) & 15) ||
       (reinterpret_cast<uintptr_t>(g.B.ptr) & 15))
     return ctx->fail(GLC_ERR_INVALID, "gemm: operand leading dimensions must be multiples of 4 floats and 16-byte aligned");
-  if (encode_operand(ctx, ta, g.A.ptr, g.A.ld, g.A.mn_major, g.M, g.K, box_a) != 0)
+  if (encode_operand(ctx, ta, g.A.ptr, g.A.ld, g.A.mn_major, g.M, g.K, box_a, &p->a_3d) != 0)
     return ctx->fail(GLC_ERR_INVALID, "gemm: cuTensorMapEncodeTiled failed for A");
-  if (encode_operand(ctx, tb, g.B.ptr, g.B.ld, g.B.mn_major, g.N, g.K, box_b) != 0)
+  if (encode_operand(ctx, tb, g.B.ptr, g.B.ld, g.B.mn_major, g.N, g.K, box_b, &p->b_3d) != 0)
     return ctx->fail(GLC_ERR_INVALID, "gemm: cuTensorMapEncodeTiled failed for B");
   p->C = g.C;
   p->R = g.R;

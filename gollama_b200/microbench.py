@@ -59,6 +59,23 @@ def case_gemm(ctx, kind, M, K, N, iters, warmup):
     return f"gemm_{kind} M={M} K={K} N={N}", ms, flops / (ms * 1e-3) / 1e12, "TFLOP/s"
 
 
+def case_gemm_majors(ctx, iters, warmup, M=16384, N=2048, K=2048):
+    """C[M,N] = A . B^T through glc_gemm_tf32 with each operand K- or MN-major."""
+    out = []
+    A_k, A_m = _rand(ctx, (M, K), 21), _rand(ctx, (K, M), 22)
+    B_k, B_m = _rand(ctx, (N, K), 23), _rand(ctx, (K, N), 24)
+    Cm = ctx.empty((M, N))
+    for am in (0, 1):
+        for bm in (0, 1):
+            A, lda = (A_m, M) if am else (A_k, K)
+            B, ldb = (B_m, N) if bm else (B_k, K)
+            f = lambda: ctx.call("glc_gemm_tf32", A.ptr, lda, am, B.ptr, ldb, bm, Cm.ptr, N, M, N, K, 0, None, 0, 0)
+            ms = _time(ctx, f, iters, warmup)
+            out.append((f"gemm A{'mn' if am else 'k'} B{'mn' if bm else 'k'} M={M} N={N} K={K}", ms,
+                        2.0 * M * N * K / (ms * 1e-3) / 1e12, "TFLOP/s"))
+    return out
+
+
 def case_linear_sweep(ctx, iters, warmup):
     """Linear-layer sweep: M in {4096, 16384, 32768} x (K, N) in {(2048, 2048),
     (2048, 5632), (5632, 2048)}, forward, dX and dW separately."""
@@ -146,6 +163,7 @@ CASES = {
     "gemm_bwd_down": lambda c, i, w: case_gemm(c, "bwd", T, F, D, i, w),
     "gemm_bwd_gateup": lambda c, i, w: case_gemm(c, "bwd", T, D, 2 * F, i, w),
     "linear_sweep": case_linear_sweep,
+    "gemm_majors": case_gemm_majors,
     "attention_fwd": lambda c, i, w: case_attention(c, "fwd", i, w),
     "attention_bwd": lambda c, i, w: case_attention(c, "bwd", i, w),
     "attention_fwd_s2048": lambda c, i, w: case_attention(c, "fwd", i, w, S=2048),
