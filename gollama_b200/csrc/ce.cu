@@ -42,7 +42,7 @@ __device__ __forceinline__ float block_reduce(float v, float* red) {
   return red[32];
 }
 
-template <int VPT>
+template <int VPT, bool FAST>
 __global__ void __launch_bounds__(512) ce_kernel(float* __restrict__ logits, const int64_t* __restrict__ targets,
                                                   int rows, int V, float scale, float* __restrict__ row_logp,
                                                   int write_grad, int round_out) {
@@ -66,10 +66,10 @@ __global__ void __launch_bounds__(512) ce_kernel(float* __restrict__ logits, con
     for (int i = 0; i < VPT; ++i) {
       const int c = threadIdx.x + i * blockDim.x;
       if (c < nc) {
-        v[i].x = go_exp32(__fsub_rn(v[i].x, m));
-        v[i].y = go_exp32(__fsub_rn(v[i].y, m));
-        v[i].z = go_exp32(__fsub_rn(v[i].z, m));
-        v[i].w = go_exp32(__fsub_rn(v[i].w, m));
+        v[i].x = FAST ? expf(__fsub_rn(v[i].x, m)) : go_exp32_fast(__fsub_rn(v[i].x, m));
+        v[i].y = FAST ? expf(__fsub_rn(v[i].y, m)) : go_exp32_fast(__fsub_rn(v[i].y, m));
+        v[i].z = FAST ? expf(__fsub_rn(v[i].z, m)) : go_exp32_fast(__fsub_rn(v[i].z, m));
+        v[i].w = FAST ? expf(__fsub_rn(v[i].w, m)) : go_exp32_fast(__fsub_rn(v[i].w, m));
         s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
       }
     }
@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(512) ce_kernel(float* __restrict__ logits, con
         if (t >= 4 * c && t < 4 * c + 4) {
           const int j = static_cast<int>(t - 4 * c);
           const float pt = j == 0 ? p[0] : j == 1 ? p[1] : j == 2 ? p[2] : p[3];
-          row_logp[row] = go_log32(__fadd_rn(pt, 1e-10f));
+          row_logp[row] = FAST ? logf(__fadd_rn(pt, 1e-10f)) : go_log32(__fadd_rn(pt, 1e-10f));
         }
         if (write_grad) {
           float g[4];
@@ -126,7 +126,7 @@ __global__ void ce_loss_sum_kernel(const float* __restrict__ row_logp, const int
 
 __global__ void exp32_kernel(const float* __restrict__ x, float* __restrict__ y, size_t n) {
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
-    y[i] = go_exp32(x[i]);
+    y[i] = go_exp32_fast(x[i]);
 }
 
 }  // namespace
@@ -141,7 +141,7 @@ int exp32(Context* ctx, const float* x, float* y, size_t n, cudaStream_t s) {
 }
 
 int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, int V, float scale, float* row_logp,
-               float* loss, bool write_grad, bool round_out, cudaStream_t s) {
+               float* loss, bool write_grad, bool round_out, cudaStream_t s, bool fast_exp) {
   if (rows <= 0 || V <= 0) return ctx->fail(GLC_ERR_INVALID, "softmax_ce: empty logits");
   if ((V & 3) || (reinterpret_cast<uintptr_t>(logits) & 15))
     return ctx->fail(GLC_ERR_INVALID, "softmax_ce: vocab must be a multiple of 4, logits 16-byte aligned");
@@ -154,17 +154,17 @@ int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, in
   const int wg = write_grad ? 1 : 0, ro = round_out ? 1 : 0;
   ProfScope prof(ctx, PROF_CE, 4.0 * static_cast<double>(rows) * V * (write_grad ? 2 : 1), s);
   if (vpt <= 1)
-    ce_kernel<1><<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+    (fast_exp ? ce_kernel<1, true> : ce_kernel<1, false>)<<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
   else if (vpt <= 2)
-    ce_kernel<2><<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+    (fast_exp ? ce_kernel<2, true> : ce_kernel<2, false>)<<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
   else if (vpt <= 4)
-    ce_kernel<4><<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+    (fast_exp ? ce_kernel<4, true> : ce_kernel<4, false>)<<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
   else if (vpt <= 8)
-    ce_kernel<8><<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+    (fast_exp ? ce_kernel<8, true> : ce_kernel<8, false>)<<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
   else if (vpt <= 16)
-    ce_kernel<16><<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+    (fast_exp ? ce_kernel<16, true> : ce_kernel<16, false>)<<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
   else if (vpt <= 32)
-    ce_kernel<32><<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+    (fast_exp ? ce_kernel<32, true> : ce_kernel<32, false>)<<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
   else
     return ctx->fail(GLC_ERR_UNSUPPORTED, "softmax_ce: vocab above 65536 is not supported");
   GLC_LAUNCH_CHECK(ctx, "softmax_ce");

@@ -288,6 +288,19 @@ int glc_linear_fwd(glc_ctx* ctx, const float* X, const float* W, float* Y, int M
   return glc::gemm_tf32(c, {X, K, false}, {W, K, false}, Y, N, M, N, K, false, residual, N, false, c->stream);
 }
 
+int glc_linear_fwd_swiglu(glc_ctx* ctx, const float* X, const float* Wgu, float* GU, float* H, int M, int K, int F,
+                          int round_h) {
+  if (!ctx) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  if (F <= 0) return c->fail(GLC_ERR_INVALID, "linear_fwd_swiglu: F must be positive");
+  glc::GemmSpec g{{X, K, false}, {Wgu, K, false}, GU, 2 * F, M, 2 * F, K, false, nullptr, 0, false};
+  g.glu = F;
+  g.glu_h = H;
+  g.ld_glu = F;
+  g.glu_round = round_h != 0;
+  return glc::gemm_tf32_group(c, &g, 1, c->stream);
+}
+
 int glc_linear_bwd_dx(glc_ctx* ctx, const float* dY, const float* W, float* dX, int M, int K, int N,
                       int accumulate) {
   if (!ctx) return GLC_ERR_INVALID;

@@ -12,13 +12,20 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 // ---------------------------------------------------------------- SwiGLU
 // Forward of forwardFFN's SiLU and product nodes (trainer.go:397-407 with
 // SiLUGrad, grad.go:424-428): s = 1/(1+exp32(-g)), h = (g*s)*u.
+// FAST: llama semantics, sigmoid with the hardware-assisted expf instead of
+// the reference's float64 exp32 (the decoder's tolerance allows it).
+template <bool FAST>
+__device__ __forceinline__ float sigmoid_f(float g) {
+  return FAST ? __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))) : go_sigmoid(g);
+}
+template <bool FAST>
 __device__ __forceinline__ float swiglu_f(float g, float u) {
-  const float s = go_sigmoid(g);
-  return __fmul_rn(__fmul_rn(g, s), u);
+  return FAST ? __fmul_rn(__fmul_rn(g, sigmoid_f<true>(g)), u) : go_swiglu(g, u);
 }
 
 // 2-D launch: blockIdx.x/threadIdx.x pick a float4 column, blockIdx.y strides
 // over rows (32-bit index arithmetic, no per-element division).
+template <bool FAST>
 __global__ void swiglu_fwd_kernel(const float* __restrict__ g, const float* __restrict__ u, size_t ld_in,
                                   float* __restrict__ h, size_t ld_h, unsigned rows, unsigned cols4, int round_out) {
   const unsigned c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -26,7 +33,8 @@ __global__ void swiglu_fwd_kernel(const float* __restrict__ g, const float* __re
   for (unsigned r = blockIdx.y; r < rows; r += gridDim.y) {
     const float4 a = reinterpret_cast<const float4*>(g + r * ld_in)[c];
     const float4 b = reinterpret_cast<const float4*>(u + r * ld_in)[c];
-    float4 o = make_float4(swiglu_f(a.x, b.x), swiglu_f(a.y, b.y), swiglu_f(a.z, b.z), swiglu_f(a.w, b.w));
+    float4 o = make_float4(swiglu_f<FAST>(a.x, b.x), swiglu_f<FAST>(a.y, b.y), swiglu_f<FAST>(a.z, b.z),
+                           swiglu_f<FAST>(a.w, b.w));
     if (round_out) o = make_float4(round_tf32(o.x), round_tf32(o.y), round_tf32(o.z), round_tf32(o.w));
     reinterpret_cast<float4*>(h + r * ld_h)[c] = o;
   }
@@ -34,8 +42,9 @@ __global__ void swiglu_fwd_kernel(const float* __restrict__ g, const float* __re
 
 // Backward of the product node (trainer.go:418-421) then SiLU (grad.go:441-445):
 //   dgs = dh*u, du = dh*(g*s), dg = dgs * (s*(1 + g*(1-s)))
+template <bool FAST>
 __device__ __forceinline__ void swiglu_b(float g, float u, float dh, float& dg, float& du) {
-  const float s = go_sigmoid(g);
+  const float s = sigmoid_f<FAST>(g);
   const float gs = __fmul_rn(g, s);
   const float dgs = __fmul_rn(dh, u);
   du = __fmul_rn(dh, gs);
@@ -43,6 +52,7 @@ __device__ __forceinline__ void swiglu_b(float g, float u, float dh, float& dg, 
   dg = __fmul_rn(dgs, grad);
 }
 
+template <bool FAST>
 __global__ void swiglu_bwd_kernel(const float* __restrict__ g, const float* __restrict__ u, size_t ld_in,
                                   const float* __restrict__ dh, size_t ld_dh, float* __restrict__ dg,
                                   float* __restrict__ du, size_t ld_out, unsigned rows, unsigned cols4, int accumulate,
@@ -54,10 +64,10 @@ __global__ void swiglu_bwd_kernel(const float* __restrict__ g, const float* __re
     const float4 b = reinterpret_cast<const float4*>(u + r * ld_in)[c];
     const float4 d = reinterpret_cast<const float4*>(dh + r * ld_dh)[c];
     float4 rg, ru;
-    swiglu_b(a.x, b.x, d.x, rg.x, ru.x);
-    swiglu_b(a.y, b.y, d.y, rg.y, ru.y);
-    swiglu_b(a.z, b.z, d.z, rg.z, ru.z);
-    swiglu_b(a.w, b.w, d.w, rg.w, ru.w);
+    swiglu_b<FAST>(a.x, b.x, d.x, rg.x, ru.x);
+    swiglu_b<FAST>(a.y, b.y, d.y, rg.y, ru.y);
+    swiglu_b<FAST>(a.z, b.z, d.z, rg.z, ru.z);
+    swiglu_b<FAST>(a.w, b.w, d.w, rg.w, ru.w);
     float4* pg = reinterpret_cast<float4*>(dg + r * ld_out) + c;
     float4* pu = reinterpret_cast<float4*>(du + r * ld_out) + c;
     if (accumulate) {
@@ -179,21 +189,23 @@ __global__ void embed_bwd_kernel(const int* __restrict__ seg_tok, const int* __r
 }  // namespace
 
 int swiglu_fwd(Context* ctx, const float* g, const float* u, size_t ld_in, float* h, size_t ld_h, size_t rows,
-               size_t cols, bool round_out, cudaStream_t s) {
+               size_t cols, bool round_out, cudaStream_t s, bool fast_exp) {
   if (rows == 0 || cols == 0) return 0;
   if ((cols & 3) || (ld_in & 3) || (ld_h & 3) || !aligned16(g) || !aligned16(u) || !aligned16(h))
     return ctx->fail(GLC_ERR_INVALID, "swiglu_fwd: sizes and strides must be multiples of 4, pointers 16-byte aligned");
   const size_t n = rows * cols;
   ProfScope prof(ctx, PROF_SWIGLU, 12.0 * n, s);
   if (rows > 0xFFFFFFFFu || cols / 4 > 0xFFFFFFFFu) return ctx->fail(GLC_ERR_INVALID, "swiglu_fwd: too large");
-  swiglu_fwd_kernel<<<grid_2d(rows, cols / 4, 256, ctx->num_sms), 256, 0, s>>>(
+  auto kern = fast_exp ? swiglu_fwd_kernel<true> : swiglu_fwd_kernel<false>;
+  kern<<<grid_2d(rows, cols / 4, 256, ctx->num_sms), 256, 0, s>>>(
       g, u, ld_in, h, ld_h, static_cast<unsigned>(rows), static_cast<unsigned>(cols / 4), round_out ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "swiglu_fwd");
   return 0;
 }
 
 int swiglu_bwd(Context* ctx, const float* g, const float* u, size_t ld_in, const float* dh, size_t ld_dh, float* dg,
-               float* du, size_t ld_out, size_t rows, size_t cols, bool accumulate, bool round_out, cudaStream_t s) {
+               float* du, size_t ld_out, size_t rows, size_t cols, bool accumulate, bool round_out, cudaStream_t s,
+               bool fast_exp) {
   if (rows == 0 || cols == 0) return 0;
   if ((cols & 3) || (ld_in & 3) || (ld_dh & 3) || (ld_out & 3) || !aligned16(g) || !aligned16(u) || !aligned16(dh) ||
       !aligned16(dg) || !aligned16(du))
@@ -201,7 +213,8 @@ int swiglu_bwd(Context* ctx, const float* g, const float* u, size_t ld_in, const
   const size_t n = rows * cols;
   ProfScope prof(ctx, PROF_SWIGLU, (accumulate ? 28.0 : 20.0) * n, s);
   if (rows > 0xFFFFFFFFu || cols / 4 > 0xFFFFFFFFu) return ctx->fail(GLC_ERR_INVALID, "swiglu_bwd: too large");
-  swiglu_bwd_kernel<<<grid_2d(rows, cols / 4, 256, ctx->num_sms), 256, 0, s>>>(
+  auto kern = fast_exp ? swiglu_bwd_kernel<true> : swiglu_bwd_kernel<false>;
+  kern<<<grid_2d(rows, cols / 4, 256, ctx->num_sms), 256, 0, s>>>(
       g, u, ld_in, dh, ld_dh, dg, du, ld_out, static_cast<unsigned>(rows), static_cast<unsigned>(cols / 4),
       accumulate ? 1 : 0, round_out ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "swiglu_bwd");

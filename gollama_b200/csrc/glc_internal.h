@@ -131,6 +131,13 @@ struct GemmSpec {
   const float* R;
   int ldr;
   bool round_out;
+  // SwiGLU epilogue: glu = F > 0 means B's rows are [gate F | up F] (N = 2F);
+  // C receives both halves and glu_h [M][F] (row stride ld_glu) receives
+  // h = silu(gate) * up, TF32-rounded when glu_round.
+  int glu = 0;
+  float* glu_h = nullptr;
+  int ld_glu = 0;
+  bool glu_round = false;
 };
 // Runs up to two independent GEMMs in one persistent launch (shared tile queue).
 int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t stream);
@@ -145,10 +152,12 @@ int rmsnorm_bwd(Context* ctx, const float* x, const float* w, const float* rms, 
                 float* dx_round, float* dw, int rows, int cols, bool full, bool dx_accumulate, bool dw_accumulate,
                 float* scratch, size_t scratch_bytes, cudaStream_t s);
 // rows x cols, each operand with its own row stride (elements; multiples of 4).
+// fast_exp: llama semantics, expf/logf instead of the reference's exp32/log32
 int swiglu_fwd(Context* ctx, const float* g, const float* u, size_t ld_in, float* h, size_t ld_h, size_t rows,
-               size_t cols, bool round_out, cudaStream_t s);
+               size_t cols, bool round_out, cudaStream_t s, bool fast_exp = false);
 int swiglu_bwd(Context* ctx, const float* g, const float* u, size_t ld_in, const float* dh, size_t ld_dh, float* dg,
-               float* du, size_t ld_out, size_t rows, size_t cols, bool accumulate, bool round_out, cudaStream_t s);
+               float* du, size_t ld_out, size_t rows, size_t cols, bool accumulate, bool round_out, cudaStream_t s,
+               bool fast_exp = false);
 int fill(Context* ctx, float* p, float v, size_t n, cudaStream_t s);
 int round_copy(Context* ctx, const float* src, float* dst, size_t n, cudaStream_t s);
 // data parallel (dp.cu): in-place fp32 sum over the ranks
@@ -164,7 +173,7 @@ int embed_fwd(Context* ctx, const int64_t* tok, const float* E, const float* P, 
 int embed_bwd(Context* ctx, const int* seg_tok, const int* seg_start, const int* order, int nseg, const float* dh,
               float* dE, int d, cudaStream_t s);
 int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, int V, float scale, float* row_logp,
-               float* loss, bool write_grad, bool round_out, cudaStream_t s);
+               float* loss, bool write_grad, bool round_out, cudaStream_t s, bool fast_exp = false);
 // q/k/v (and their gradients) may be column slices of one fused projection
 // output: each has its own row stride in elements.
 struct AttnIO {

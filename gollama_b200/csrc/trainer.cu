@@ -329,14 +329,25 @@ struct Model {
   // through to `residual` before the two GEMM gradients.
   // round_out: the output is a tensor-core operand (q, k, v feed attention);
   // round_dx: the input gradient is one (the attention output's gradient).
-  Node* matmul(Tape& tp, Node* a, Node* w, Node* residual, bool round_out = false, bool round_dx = false) {
+  // swiglu_h: when set, w is a [gate F | up F] view and the same launch also
+  // writes h = silu(gate) * up (TF32-rounded) there; the SwiGLU node then
+  // adopts that buffer instead of running its own forward.
+  Node* matmul(Tape& tp, Node* a, Node* w, Node* residual, bool round_out = false, bool round_dx = false,
+               float* swiglu_h = nullptr) {
     const int M = static_cast<int>(a->rows), K = static_cast<int>(a->cols), N = static_cast<int>(w->rows);
     Node* out = tp.make(M, N);
     out->require_grad = a->require_grad || w->require_grad || (residual && residual->require_grad);
     if (residual) out->parents = {residual, a, w};
     else out->parents = {a, w};
-    ck(gemm_tf32(ctx, {a->gemm_data, K, false}, {w->gemm_data, K, false}, out->data, N, M, N, K, false,
-                 residual ? residual->data : nullptr, N, round_out, tp.stream()));
+    GemmSpec fwd{{a->gemm_data, K, false}, {w->gemm_data, K, false}, out->data, N, M, N, K, false,
+                 residual ? residual->data : nullptr, N, round_out};
+    if (swiglu_h) {
+      fwd.glu = N / 2;
+      fwd.glu_h = swiglu_h;
+      fwd.ld_glu = N / 2;
+      fwd.glu_round = true;
+    }
+    ck(gemm_tf32_group(ctx, &fwd, 1, tp.stream()));
     if (round_out) out->gemm_data = out->data;
     Tape* t = &tp;
     out->grad_fn = [this, t, out, a, w, residual, M, K, N, round_dx]() {
@@ -433,13 +444,17 @@ struct Model {
 
   // SiLUGrad (grad.go:417-449) and the product node (trainer.go:400-422) as
   // one node over the fused projection output gu = [gate | up] ([T, 2F]).
-  Node* swiglu(Tape& tp, Node* gu) {
+  // out: a node whose data the gate/up GEMM already filled with h (fused
+  // epilogue), or nullptr to compute h here.
+  Node* swiglu(Tape& tp, Node* gu, Node* out = nullptr) {
     const int64_t T = gu->rows, F = gu->cols / 2;
-    Node* out = tp.make(T, F);
+    const bool fused = out != nullptr;
+    if (!out) out = tp.make(T, F);
     out->require_grad = true;
     out->parents = {gu};
-    ck(swiglu_fwd(ctx, gu->data, gu->data + F, static_cast<size_t>(2 * F), out->data, static_cast<size_t>(F),
-                  static_cast<size_t>(T), static_cast<size_t>(F), true, tp.stream()));
+    if (!fused)
+      ck(swiglu_fwd(ctx, gu->data, gu->data + F, static_cast<size_t>(2 * F), out->data, static_cast<size_t>(F),
+                    static_cast<size_t>(T), static_cast<size_t>(F), true, tp.stream(), llama));
     out->gemm_data = out->data;
     Tape* t = &tp;
     out->grad_fn = [this, t, out, gu, T, F]() {
@@ -447,7 +462,7 @@ struct Model {
       const bool acc = t->prepare_grad(gu);
       ck(swiglu_bwd(ctx, gu->data, gu->data + F, static_cast<size_t>(2 * F), out->grad, static_cast<size_t>(F),
                     gu->grad, gu->grad + F, static_cast<size_t>(2 * F), static_cast<size_t>(T), static_cast<size_t>(F),
-                    acc, true, t->stream()));
+                    acc, true, t->stream(), llama));
       gu->grad_round = gu->grad;
     };
     return out;
@@ -504,6 +519,8 @@ struct Model {
       Node* x1 = matmul(tp, att, P(lp(l, P_WO)), x, false, true);
       Node* n2 = rmsnorm(tp, x1, P(lp(l, P_FFN_NORM)));
       // forwardFFN (trainer.go:392-426): gate and up projections as one GEMM over WGate|WUp
+      // the SwiGLU epilogue (matmul's swiglu_h) runs the float64 exp32 inside
+      // the GEMM and is slower than the two launches at these sizes
       Node* gu = matmul(tp, n2, &gu_view[l], nullptr);
       Node* h = swiglu(tp, gu);
       x = matmul(tp, h, P(lp(l, P_WDOWN)), x1);
@@ -812,7 +829,8 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
       // the logits, which nothing reads afterwards.  With W data-parallel
       // ranks the mean is over the global batch: scale 1/(W*T).
       const float scale = 1.0f / static_cast<float>(static_cast<int64_t>(W) * T);
-      ck(softmax_ce(ctx, logits->data, tg_dev, T, c.vocab_size, scale, row_logp, d_loss, true, true, ctx->stream));
+      ck(softmax_ce(ctx, logits->data, tg_dev, T, c.vocab_size, scale, row_logp, d_loss, true, true, ctx->stream,
+                    /*fast_exp=*/true));
       Node* lossn = tape->make(1, 1);
       lossn->require_grad = true;
       lossn->parents = {logits};

@@ -120,6 +120,15 @@ def case_quant_dx(ctx, qtype, iters, warmup, M=16384, K=D, N=F):
     return f"linear_bwd_dx_q {name} M={M} K={K} N={N}", ms, 2.0 * M * N * K / (ms * 1e-3) / 1e12, "TFLOP/s"
 
 
+def case_gateup_swiglu(ctx, iters, warmup, M=T, K=D, F=F):
+    """Gate/up projection with the SwiGLU epilogue (one launch) against the
+    GEMM alone."""
+    X, W = _rand(ctx, (M, K), 25), _rand(ctx, (2 * F, K), 26, 0.05)
+    GU, Hh = ctx.empty((M, 2 * F)), ctx.empty((M, F))
+    ms = _time(ctx, lambda: ctx.call("glc_linear_fwd_swiglu", X.ptr, W.ptr, GU.ptr, Hh.ptr, M, K, F, 1), iters, warmup)
+    return f"gate/up GEMM + SwiGLU M={M} K={K} F={F}", ms, 2.0 * M * 2 * F * K / (ms * 1e-3) / 1e12, "TFLOP/s"
+
+
 def case_swiglu(ctx, iters, warmup):
     gu = _rand(ctx, (T, 2 * F), 8, tf32=False)
     dh = _rand(ctx, (T, F), 9, tf32=False)
@@ -171,6 +180,7 @@ CASES = {
     "attention_fwd_s256": lambda c, i, w: case_attention(c, "fwd", i, w, B=16, S=256),
     "attention_bwd_s256": lambda c, i, w: case_attention(c, "bwd", i, w, B=16, S=256),
     "swiglu_bwd": case_swiglu,
+    "gateup_swiglu": case_gateup_swiglu,
     "quant_dx_q8_0": lambda c, i, w: case_quant_dx(c, 8, i, w),
     "quant_dx_q4_0": lambda c, i, w: case_quant_dx(c, 2, i, w),
     "rmsnorm_bwd": case_rmsnorm,

@@ -119,6 +119,18 @@ GLC_API int glc_linear_bwd_dw(glc_ctx* ctx, const float* dY, const float* X, flo
  * dX or dW may be NULL when that gradient is not required. */
 GLC_API int glc_linear_bwd(glc_ctx* ctx, const float* dY, const float* X, const float* W, float* dX, float* dW, int M,
                            int K, int N, int accumulate_dx, int accumulate_dw);
+/* Gate and up projections with the SwiGLU product in one launch:
+ * GU[M][2F] = X[M][K] . Wgu^T (Wgu = [WGate rows F | WUp rows F], each
+ * MatMulTransposeB, pkg/tensor/matmul.go:145-234) and H[M][F] = silu(gate) *
+ * up (SiLUGrad's forward, pkg/tensor/grad.go:426-427, then the product node,
+ * pkg/train/trainer.go:400-422, with the reference's exp32), H TF32-rounded
+ * when round_h.  GU and H equal glc_linear_fwd followed by glc_swiglu_fwd bit
+ * for bit.  The SwiGLU runs in the GEMM epilogue on CTA pairs; with the
+ * reference's float64 exp32 that epilogue does not hide under the MMAs at
+ * 4096 x 2048 x 2*5632 (0.47 ms against 0.30 + 0.13 ms for the two calls), so
+ * glc_train_step keeps the two launches. */
+GLC_API int glc_linear_fwd_swiglu(glc_ctx* ctx, const float* X, const float* Wgu, float* GU, float* H, int M, int K,
+                                  int F, int round_h);
 /* Frozen quantized weights (pkg/quant/dequant.go).  Type codes are GGUF's
  * (pkg/gguf/format.go:40-46). */
 #define GLC_QTYPE_F32 0

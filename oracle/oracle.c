@@ -459,6 +459,17 @@ int FN(linear_bwd_dx_q)(const real* dy, const uint8_t* wq, int type, real* dx, i
   return rc;
 }
 
+/* ------------------------------------------------------------------ exponential of the current semantics
+ * Reference semantics use the reference's exp32/log32 (grad.go:283-298).
+ * Llama semantics use the C library's expf/logf: the benchmark's decoder is
+ * not the reference trainer's model, and its tolerance (loss 1e-4, gradients
+ * 2e-3) is far above the 1.4e-5 by which exp32 differs from e^x.  The flag is
+ * set only for the duration of a whole-model forward/backward in llama mode;
+ * the single-op entry points always use exp32/log32. */
+static int g_libm_exp = 0;
+static float mode_exp32(float x) { return g_libm_exp ? expf(x) : FN(exp32)(x); }
+static float mode_log32(float x) { return g_libm_exp ? logf(x) : FN(log32)(x); }
+
 /* ------------------------------------------------------------------ SiLU (SiLUGrad, grad.go:417-449) */
 void FN(silu_fwd)(const real* x, real* out, real* sig, int64_t n) {
   for (int64_t i = 0; i < n; ++i) {
@@ -466,7 +477,7 @@ void FN(silu_fwd)(const real* x, real* out, real* sig, int64_t n) {
 #ifdef ORC_DOUBLE
     sig[i] = 1.0 / (1.0 + exp(-v));
 #else
-    sig[i] = 1.0f / (1.0f + FN(exp32)(-v));
+    sig[i] = 1.0f / (1.0f + mode_exp32(-v));
 #endif
     out[i] = v * sig[i];
   }
@@ -506,7 +517,7 @@ static void ce_rows(void* p, int s, int e) {
 #ifdef ORC_DOUBLE
       pr[v] = exp(l[v] - maxv);
 #else
-      pr[v] = FN(exp32)(l[v] - maxv);
+      pr[v] = mode_exp32(l[v] - maxv);
 #endif
       sum += pr[v];
     }
@@ -517,7 +528,7 @@ static void ce_rows(void* p, int s, int e) {
 #ifdef ORC_DOUBLE
       loss = -log(pr[t] + 1e-10);
 #else
-      loss = -FN(log32)(pr[t] + 1e-10f);
+      loss = -mode_log32(pr[t] + 1e-10f);
 #endif
     }
     g->row_loss[b] = loss;
@@ -777,6 +788,7 @@ real FN(forward_backward)(const orc_config* c, const real* params, real* grads, 
   const int T = B * S, d = c->hidden, F = c->inter, V = c->vocab, L = c->layers, H = c->heads;
   const int hd = head_dim(c), Hkv = kvh(c), kvd = Hkv * hd;
   const int llama = c->mode == ORC_MODE_LLAMA;
+  g_libm_exp = llama;
   int64_t off, r, cc;
 #define PARAM(idx) (FN(param_info)(c, (idx), &off, &r, &cc), params + off)
 #define GRAD(idx) (FN(param_info)(c, (idx), &off, &r, &cc), has_grad[(idx)] = 1, grads + off)
@@ -965,6 +977,7 @@ real FN(forward_backward)(const orc_config* c, const real* params, real* grads, 
   free(sin_t);
 #undef PARAM
 #undef GRAD
+  g_libm_exp = 0;
   return loss;
 }
 

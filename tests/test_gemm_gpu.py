@@ -166,3 +166,31 @@ def test_gemm_variant_rejects_unknown(ctx):
 
     with pytest.raises(GlcError):
         ctx.call("glc_set_gemm_variant", 3)
+
+
+@pytest.mark.parametrize("variant", [0, 1])
+@pytest.mark.parametrize("M,K,F", [(64, 64, 344), (256, 128, 344), (300, 256, 1376), (4096, 2048, 5632)])
+def test_linear_fwd_swiglu_matches_separate_ops(ctx, variant, M, K, F):
+    """glc_linear_fwd_swiglu (SwiGLU in the GEMM epilogue on CTA pairs; GEMM then
+    the SwiGLU kernel otherwise) equals glc_linear_fwd followed by
+    glc_swiglu_fwd bit for bit."""
+    rng = np.random.default_rng(M + K + F)
+    X = rng.standard_normal((M, K), dtype=np.float32)
+    W = (rng.standard_normal((2 * F, K), dtype=np.float32) * 0.1).astype(np.float32)
+    dX, dW = ctx.from_numpy(X), ctx.from_numpy(W)
+    gu, h = ctx.empty((M, 2 * F)), ctx.empty((M, F))
+    ctx.call("glc_set_gemm_variant", variant)
+    try:
+        ctx.call("glc_linear_fwd_swiglu", dX.ptr, dW.ptr, gu.ptr, h.ptr, M, K, F, 1)
+        y = ctx.empty((M, 2 * F))
+        ctx.call("glc_linear_fwd", dX.ptr, dW.ptr, y.ptr, M, K, 2 * F, None)
+        ctx.sync()
+    finally:
+        ctx.call("glc_set_gemm_variant", 0)
+    ref_gu = y.numpy()
+    assert np.array_equal(gu.numpy().view(np.uint32), ref_gu.view(np.uint32))
+    g, u = ctx.from_numpy(np.ascontiguousarray(ref_gu[:, :F])), ctx.from_numpy(np.ascontiguousarray(ref_gu[:, F:]))
+    h2 = ctx.empty((M, F))
+    ctx.call("glc_swiglu_fwd", g.ptr, u.ptr, h2.ptr, M * F, 1)
+    ctx.sync()
+    assert np.array_equal(h.numpy().view(np.uint32), h2.numpy().view(np.uint32))
