@@ -168,21 +168,33 @@ __global__ void embed_fwd_kernel(const int64_t* __restrict__ tok, const float* _
 // distinct id (deterministic; no atomics).  seg_tok[u] is the u-th distinct
 // (clamped) id, rows order[seg_start[u] .. seg_start[u+1]) are its tokens in
 // ascending t.
+// Launch: blockIdx.x strides over segments, blockIdx.y picks a chunk of
+// blockDim.x float4 columns, so a frequent id's long segment is spread over
+// several blocks; each thread owns one float4 column and fetches 8 rows ahead
+// before adding them in ascending t (the order, and so the bits, of the
+// sequential sum).
 __global__ void embed_bwd_kernel(const int* __restrict__ seg_tok, const int* __restrict__ seg_start,
                                  const int* __restrict__ order, const float* __restrict__ dh, float* __restrict__ dE,
                                  int nseg, int d) {
   const int nc = d >> 2;
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c >= nc) return;
   for (int u = blockIdx.x; u < nseg; u += gridDim.x) {
     float4* row = reinterpret_cast<float4*>(dE + static_cast<size_t>(seg_tok[u]) * d);
     const int b = seg_start[u], e = seg_start[u + 1];
-    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
-      float4 acc = row[c];
-      for (int k = b; k < e; ++k) {
-        const float4 g = reinterpret_cast<const float4*>(dh + static_cast<size_t>(order[k]) * d)[c];
-        acc = make_float4(__fadd_rn(acc.x, g.x), __fadd_rn(acc.y, g.y), __fadd_rn(acc.z, g.z), __fadd_rn(acc.w, g.w));
-      }
-      row[c] = acc;
+    float4 acc = row[c];
+    for (int k = b; k < e; k += 8) {
+      float4 g[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (k + i < e) g[i] = reinterpret_cast<const float4*>(dh + static_cast<size_t>(order[k + i]) * d)[c];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (k + i < e)
+          acc = make_float4(__fadd_rn(acc.x, g[i].x), __fadd_rn(acc.y, g[i].y), __fadd_rn(acc.z, g[i].z),
+                            __fadd_rn(acc.w, g[i].w));
     }
+    row[c] = acc;
   }
 }
 
@@ -285,9 +297,12 @@ int embed_bwd(Context* ctx, const int* seg_tok, const int* seg_start, const int*
   if (nseg == 0) return 0;
   if (nseg < 0 || d <= 0 || (d & 3) || !seg_tok || !seg_start || !order || !dh || !dE)
     return ctx->fail(GLC_ERR_INVALID, "embed_bwd: bad arguments");
-  unsigned grid = static_cast<unsigned>(nseg < 8 * ctx->num_sms ? nseg : 8 * ctx->num_sms);
+  const int nc = d / 4;
+  const unsigned gy = static_cast<unsigned>((nc + 127) / 128);
+  unsigned gx = static_cast<unsigned>((8 * ctx->num_sms + gy - 1) / gy);
+  if (gx > static_cast<unsigned>(nseg)) gx = static_cast<unsigned>(nseg);
   ProfScope prof(ctx, PROF_OTHER, 8.0 * 0, s);
-  embed_bwd_kernel<<<grid, 128, 0, s>>>(seg_tok, seg_start, order, dh, dE, nseg, d);
+  embed_bwd_kernel<<<dim3(gx, gy), 128, 0, s>>>(seg_tok, seg_start, order, dh, dE, nseg, d);
   GLC_LAUNCH_CHECK(ctx, "embed_bwd");
   return 0;
 }

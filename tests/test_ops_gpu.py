@@ -208,6 +208,27 @@ def test_embedding_fwd_bwd(ctx):
     assert np.array_equal(bdE.numpy(), want)
 
 
+@pytest.mark.parametrize("d", [2048, 2052])
+def test_embedding_bwd_hot_ids(ctx, d):
+    """Zipf-like ids: one id holds 301 rows (a ragged tail of 8-row batches),
+    rows of d/4 float4 columns spread over several column blocks; the sum per
+    id stays in ascending t, bit for bit."""
+    V, T = 4000, 1200
+    r = rng(10)
+    tok = r.integers(0, V, T).astype(np.int64)
+    tok[r.choice(T, 301, replace=False)] = 17
+    tok[r.choice(np.flatnonzero(tok != 17), 9, replace=False)] = 3
+    dh = r.standard_normal((T, d), dtype=np.float32)
+    dE0 = r.standard_normal((V, d), dtype=np.float32)
+    bdh, bdE = ctx.from_numpy(dh), ctx.from_numpy(dE0)
+    ctx.call("glc_embed_bwd", tok.ctypes.data_as(C.c_void_p), T, bdh.ptr, bdE.ptr, d, V)
+    ctx.sync()
+    want = dE0.copy()
+    for t in range(T):
+        want[tok[t]] += dh[t]
+    assert np.array_equal(bdE.numpy(), want)
+
+
 def test_round_tf32(ctx):
     x = np.array([1.0 + 3 * 2.0**-12, 1.0 + 2.0**-12, -(1.0 + 3 * 2.0**-12), 3.0e-39, 1.0e30], np.float32)
     x = np.concatenate([x, np.zeros(3, np.float32)])
