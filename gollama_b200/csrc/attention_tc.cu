@@ -402,13 +402,18 @@ __device__ __forceinline__ void tile_rows_to_tmem(const uint8_t* tile, int row, 
   }
 }
 
-template <int HD, bool GROUP_LOOP>
+// Grid (Hkv * nsplit, B, key tiles): the G query heads of a KV head are
+// split over nsplit CTAs, each looping over its G / nsplit heads with dK/dV
+// accumulated in TMEM; key tiles vary slowest, so the longest CTAs (key
+// tile 0 meets every query) are dispatched first.  nsplit == 1 writes the
+// final dk/dv; otherwise partial [T][Hkv * nsplit][hd] for the group sum.
+template <int HD>
 __global__ void __launch_bounds__(NT, 1)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQk, const __grid_constant__ CUtensorMap tmQm,
                             const __grid_constant__ CUtensorMap tmOk, const __grid_constant__ CUtensorMap tmOm,
                             const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                             const float* __restrict__ lse, const float* __restrict__ Dv, float* __restrict__ dk_out,
-                            float* __restrict__ dv_out, int dk_ld, int dv_ld, int per_head, int S, int H, int Hkv,
+                            float* __restrict__ dv_out, int dk_ld, int dv_ld, int nsplit, int S, int H, int Hkv,
                             float scale, float scale_log2, int round_dv, int* err) {
   using L = DkdvLayout<HD>;
   extern __shared__ uint8_t smem_raw[];
@@ -422,10 +427,10 @@ __global__ void __launch_bounds__(NT, 1)
   float* stage_ld = reinterpret_cast<float*>(sm + L::OFF_LD);  // [2][lse 64 | D 64]
   const Roles ro;
   const int G = H / Hkv;
-  const int kt = blockIdx.x, b = blockIdx.z;
-  const int kh = GROUP_LOOP ? static_cast<int>(blockIdx.y) : static_cast<int>(blockIdx.y) / G;
-  const int h_first = GROUP_LOOP ? kh * G : static_cast<int>(blockIdx.y);
-  const int n_heads = GROUP_LOOP ? G : 1;
+  const int kt = blockIdx.z, b = blockIdx.y;
+  const int kh = static_cast<int>(blockIdx.x) / nsplit, split = static_cast<int>(blockIdx.x) - kh * nsplit;
+  const int n_heads = G / nsplit;
+  const int h_first = kh * G + split * n_heads;
   const int k0 = kt * 128, row_base = b * S;
   const int qi0 = k0 / 64, n_q64 = (S + 63) / 64;
   const int nq = n_q64 - qi0;
@@ -614,9 +619,9 @@ __global__ void __launch_bounds__(NT, 1)
     }
     if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
       tc_fence_after();
-      // final dk/dv at the KV head's columns, or per-query-head partials;
+      // final dk/dv at the KV head's columns, or this CTA's partial;
       // column half 0 writes dV, half 1 writes dK
-      const int oh = per_head ? h_first : kh;
+      const int oh = static_cast<int>(blockIdx.x);
       const size_t trow = static_cast<size_t>(row_base) + key;
       const int part = hf;
 #pragma unroll 1
@@ -626,7 +631,7 @@ __global__ void __launch_bounds__(NT, 1)
         tmem_ld_wait();
         if (key < S) {
           float* dst = (part == 0 ? dv_out + trow * dv_ld : dk_out + trow * dk_ld) + oh * HD + cc * 32;
-          const bool rnd = part == 0 && round_dv;
+          const bool rnd = part == 0 && round_dv && nsplit == 1;
 #pragma unroll
           for (int g = 0; g < 8; ++g) {
             float4 o4 = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
@@ -646,27 +651,40 @@ __global__ void __launch_bounds__(NT, 1)
   }
 }
 
-// dk[t][kh] = sum over the G query heads of the group of partial[t][h]
-// (heads ascending: deterministic); dv the same, optionally TF32-rounded.
+// dk[t][kh] = sum over the nsplit partials of the KV head, partial[t][kh *
+// nsplit + g] (g ascending: deterministic); dv the same, optionally
+// TF32-rounded.
+// With RoPE tables, dk gets the transposed rotation at position t % S and is
+// TF32-rounded (what a separate backward RoPE pass would write).
 __global__ void group_sum_kernel(const float* __restrict__ pk, const float* __restrict__ pv, float* __restrict__ dk,
-                                 float* __restrict__ dv, int dk_ld, int dv_ld, int T, int H, int Hkv, int hd,
-                                 int round_dv) {
+                                 float* __restrict__ dv, int dk_ld, int dv_ld, int T, int S, int nsplit, int Hkv, int hd,
+                                 int round_dv, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin) {
   // 32-bit index math: the host checks T * Hkv * hd / 4 < 2^31
-  const int G = H / Hkv, n4 = hd / 4, per_t = Hkv * n4;
+  const int n4 = hd / 4, per_t = Hkv * n4;
   const int total = T * per_t;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const size_t t = static_cast<unsigned>(i) / static_cast<unsigned>(per_t);
     const int rem = i - static_cast<int>(t) * per_t;
     const int kh = rem / n4, d4 = rem - kh * n4;
     float4 sk = make_float4(0.f, 0.f, 0.f, 0.f), sv = sk;
-    for (int g = 0; g < G; ++g) {
-      const size_t src = (t * H + kh * G + g) * hd / 4 + d4;
+    for (int g = 0; g < nsplit; ++g) {
+      const size_t src = (t * Hkv * nsplit + kh * nsplit + g) * hd / 4 + d4;
       const float4 a = reinterpret_cast<const float4*>(pk)[src];
       const float4 c = reinterpret_cast<const float4*>(pv)[src];
       sk.x += a.x; sk.y += a.y; sk.z += a.z; sk.w += a.w;
       sv.x += c.x; sv.y += c.y; sv.z += c.z; sv.w += c.w;
     }
     if (round_dv) sv = make_float4(round_tf32(sv.x), round_tf32(sv.y), round_tf32(sv.z), round_tf32(sv.w));
+    if (rope_cos) {
+      // columns 4*d4 .. 4*d4+3 are the pairs 2*d4 and 2*d4+1 of head kh
+      const size_t trow = (t % static_cast<unsigned>(S)) * static_cast<size_t>(hd / 2);
+      const float2 c = reinterpret_cast<const float2*>(rope_cos + trow)[d4];
+      const float2 sn = reinterpret_cast<const float2*>(rope_sin + trow)[d4];
+      sk = make_float4(round_tf32(__fadd_rn(__fmul_rn(sk.x, c.x), __fmul_rn(sk.y, sn.x))),
+                       round_tf32(__fadd_rn(__fmul_rn(-sk.x, sn.x), __fmul_rn(sk.y, c.x))),
+                       round_tf32(__fadd_rn(__fmul_rn(sk.z, c.y), __fmul_rn(sk.w, sn.y))),
+                       round_tf32(__fadd_rn(__fmul_rn(-sk.z, sn.y), __fmul_rn(sk.w, c.y))));
+    }
     reinterpret_cast<float4*>(dk + t * dk_ld + kh * hd)[d4] = sk;
     reinterpret_cast<float4*>(dv + t * dv_ld + kh * hd)[d4] = sv;
   }
@@ -700,7 +718,8 @@ __global__ void __launch_bounds__(NT, 1)
                           const __grid_constant__ CUtensorMap tmKk, const __grid_constant__ CUtensorMap tmKm,
                           const __grid_constant__ CUtensorMap tmVk, const float* __restrict__ lse,
                           const float* __restrict__ Dv, float* __restrict__ dq, int dq_ld, int S, int H, int Hkv,
-                          int n_qt, float scale, float scale_log2, int* err) {
+                          int n_qt, float scale, float scale_log2, const float* __restrict__ rope_cos,
+                          const float* __restrict__ rope_sin, int* err) {
   using L = DqLayout<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -869,6 +888,24 @@ __global__ void __launch_bounds__(NT, 1)
         uint32_t v[32];
         tmem_ld_32x32b_x32(lane_addr + L::DQ_COL + cc * 32, v);
         tmem_ld_wait();
+        if (qa < S && rope_cos) {
+          // transposed RoPE rotation of the row's pairs cc*16 .. cc*16+15 at
+          // position qa, then TF32 rounding
+          const float4* cr = reinterpret_cast<const float4*>(rope_cos + static_cast<size_t>(qa) * (HD / 2) + cc * 16);
+          const float4* sr = reinterpret_cast<const float4*>(rope_sin + static_cast<size_t>(qa) * (HD / 2) + cc * 16);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const float4 c4 = cr[g], s4 = sr[g];
+            const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int p = 4 * g + e;
+              const float x0 = __uint_as_float(v[2 * p]), x1 = __uint_as_float(v[2 * p + 1]);
+              v[2 * p] = __float_as_uint(round_tf32(__fadd_rn(__fmul_rn(x0, cs[e]), __fmul_rn(x1, sn[e]))));
+              v[2 * p + 1] = __float_as_uint(round_tf32(__fadd_rn(__fmul_rn(-x0, sn[e]), __fmul_rn(x1, cs[e]))));
+            }
+          }
+        }
         if (qa < S) {
 #pragma unroll
           for (int g = 0; g < 8; ++g)
@@ -959,11 +996,11 @@ int fwd_impl(Context* ctx, const float* q, int q_ld, const float* k, int k_ld, c
 
 template <int HD>
 int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, const float* dO, float* D,
-             float* partial, int B, int S, int H, int Hkv, bool round_dv, cudaStream_t s) {
+             float* partial, int B, int S, int H, int Hkv, bool round_dv, const float* rope_cos,
+             const float* rope_sin, cudaStream_t s) {
   const float *q = io.q, *k = io.k, *v = io.v;
-  static bool done_g[8] = {false}, done_p[8] = {false}, done_q[8] = {false};
-  int rc = set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD, true>, DkdvLayout<HD>::BYTES, done_g);
-  if (!rc) rc = set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD, false>, DkdvLayout<HD>::BYTES, done_p);
+  static bool done_g[8] = {false}, done_q[8] = {false};
+  int rc = set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD>, DkdvLayout<HD>::BYTES, done_g);
   if (!rc) rc = set_smem(ctx, attn_bwd_dq_tc_kernel<HD>, DqLayout<HD>::BYTES, done_q);
   if (rc) return rc;
   const int T = B * S, G = H / Hkv;
@@ -982,29 +1019,45 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
   attn_bwd_prep_tc_kernel<<<grid_for(static_cast<size_t>(T) * H, 8, ctx->num_sms, 16), 256, 0, s>>>(o, dO, D, T, S, H, HD);
   GLC_LAUNCH_CHECK(ctx, "attention_bwd prep");
   const int n_kt = (S + 127) / 128;
-  if (G == 1 || partial == nullptr) {
-    // one CTA per (key tile, KV head), looping over the query heads of its group
-    attn_bwd_dkdv_tc_kernel<HD, true><<<dim3(n_kt, Hkv, B), NT, DkdvLayout<HD>::BYTES, s>>>(
-        tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, io.dk, io.dv, io.dk_ld, io.dv_ld, 0, S, H, Hkv, scale,
+  // CTAs per KV head: the fewest that still give 1.5 waves (each CTA loads
+  // its K/V tile once and pays one prologue; fewer partials to sum), or the
+  // context's override; 1 without scratch or without grouping
+  int nsplit = 1;
+  if (G > 1 && partial != nullptr) {
+    const long long per = static_cast<long long>(n_kt) * B * Hkv;
+    nsplit = G;
+    for (int d = 1; d <= G; ++d)
+      if (G % d == 0 && 2 * per * d >= 3LL * ctx->num_sms) {
+        nsplit = d;
+        break;
+      }
+    if (ctx->attn_split > 0 && G % ctx->attn_split == 0) nsplit = ctx->attn_split;
+  }
+  if (nsplit == 1) {
+    attn_bwd_dkdv_tc_kernel<HD><<<dim3(Hkv, B, n_kt), NT, DkdvLayout<HD>::BYTES, s>>>(
+        tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, io.dk, io.dv, io.dk_ld, io.dv_ld, 1, S, H, Hkv, scale,
         scale * LOG2E, round_dv ? 1 : 0, ctx->d_err);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
+    if (rope_cos && (rc = rope(ctx, io.dk, io.dk_ld, T, S, Hkv, HD, rope_cos, rope_sin, true, true, s))) return rc;
   } else {
-    // one CTA per (key tile, query head); partials [T, H*hd] for dK and dV
+    // partials [T][Hkv * nsplit][hd] for dK and dV, summed by the group sum
+    const int pw = Hkv * nsplit * HD;
     float* pk = partial;
-    float* pv = partial + static_cast<size_t>(T) * H * HD;
-    attn_bwd_dkdv_tc_kernel<HD, false><<<dim3(n_kt, H, B), NT, DkdvLayout<HD>::BYTES, s>>>(
-        tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, pk, pv, qw, qw, 1, S, H, Hkv, scale, scale * LOG2E, 0,
+    float* pv = partial + static_cast<size_t>(T) * pw;
+    attn_bwd_dkdv_tc_kernel<HD><<<dim3(Hkv * nsplit, B, n_kt), NT, DkdvLayout<HD>::BYTES, s>>>(
+        tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, pk, pv, pw, pw, nsplit, S, H, Hkv, scale, scale * LOG2E, 0,
         ctx->d_err);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
     if (static_cast<long long>(T) * Hkv * HD / 4 >= (1LL << 31))
       return ctx->fail(GLC_ERR_INVALID, "attention_bwd: B*S*Hkv*hd too large");
     group_sum_kernel<<<grid_for(static_cast<size_t>(T) * Hkv * HD / 4, 256, ctx->num_sms), 256, 0, s>>>(
-        pk, pv, io.dk, io.dv, io.dk_ld, io.dv_ld, T, H, Hkv, HD, round_dv ? 1 : 0);
+        pk, pv, io.dk, io.dv, io.dk_ld, io.dv_ld, T, S, nsplit, Hkv, HD, round_dv ? 1 : 0, rope_cos, rope_sin);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd group sum");
   }
   const int n_qt = (S + 127) / 128;
   attn_bwd_dq_tc_kernel<HD><<<dim3(n_qt, H, B), NT, DqLayout<HD>::BYTES, s>>>(
-      tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, H, Hkv, n_qt, scale, scale * LOG2E, ctx->d_err);
+      tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,
+      rope_sin, ctx->d_err);
   GLC_LAUNCH_CHECK(ctx, "attention_bwd dq (tcgen05)");
   return 0;
 }
@@ -1028,7 +1081,8 @@ int attention_fwd(Context* ctx, const AttnIO& io, float* o, float* lse, int B, i
 }
 
 int attention_bwd(Context* ctx, const AttnIO& io, const float* o, const float* lse, const float* dO, float* D,
-                  float* partial, int B, int S, int H, int Hkv, int hd, bool round_dv, cudaStream_t s) {
+                  float* partial, int B, int S, int H, int Hkv, int hd, bool round_dv, cudaStream_t s,
+                  const float* rope_cos, const float* rope_sin) {
   int rc = check(ctx, io.q, io.k, io.v, B, S, H, Hkv, hd);
   if (rc) return rc;
   if (!o || !lse || !dO || !io.dq || !io.dk || !io.dv || !D ||
@@ -1038,8 +1092,11 @@ int attention_bwd(Context* ctx, const AttnIO& io, const float* o, const float* l
   if (((io.q_ld | io.k_ld | io.v_ld | io.dq_ld | io.dk_ld | io.dv_ld) & 3) || io.q_ld < H * hd || io.dq_ld < H * hd ||
       io.k_ld < Hkv * hd || io.v_ld < Hkv * hd || io.dk_ld < Hkv * hd || io.dv_ld < Hkv * hd)
     return ctx->fail(GLC_ERR_INVALID, "attention_bwd: bad row strides");
-  return hd == 64 ? bwd_impl<64>(ctx, io, o, lse, dO, D, partial, B, S, H, Hkv, round_dv, s)
-                  : bwd_impl<32>(ctx, io, o, lse, dO, D, partial, B, S, H, Hkv, round_dv, s);
+  if ((rope_cos == nullptr) != (rope_sin == nullptr) ||
+      ((reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 15))
+    return ctx->fail(GLC_ERR_INVALID, "attention_bwd: bad RoPE tables");
+  return hd == 64 ? bwd_impl<64>(ctx, io, o, lse, dO, D, partial, B, S, H, Hkv, round_dv, rope_cos, rope_sin, s)
+                  : bwd_impl<32>(ctx, io, o, lse, dO, D, partial, B, S, H, Hkv, round_dv, rope_cos, rope_sin, s);
 }
 
 }  // namespace glc

@@ -281,6 +281,14 @@ int glc_set_gemm_variant(glc_ctx* ctx, int variant) {
   return GLC_OK;
 }
 
+int glc_set_attention_split(glc_ctx* ctx, int nsplit) {
+  if (!ctx) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  if (nsplit < 0 || nsplit > 1024) return c->fail(GLC_ERR_INVALID, "set_attention_split: nsplit must be 0..1024");
+  c->attn_split = nsplit;
+  return GLC_OK;
+}
+
 int glc_linear_fwd(glc_ctx* ctx, const float* X, const float* W, float* Y, int M, int K, int N,
                    const float* residual) {
   if (!ctx) return GLC_ERR_INVALID;

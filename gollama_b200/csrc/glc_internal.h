@@ -26,6 +26,7 @@ struct Context {
   std::string last_error;
   uint64_t launches = 0;               // kernels this library launched
   int gemm_variant = 0;                // 0 automatic, 1 single-CTA tiles, 2 CTA-pair tiles
+  int attn_split = 0;                  // dK/dV CTAs per KV head: 0 automatic, else a divisor of the group
   EncodeTiledFn encode_fn = nullptr;
   // scratch workspace owned by the context (grown on demand, never shrunk)
   void* ws = nullptr;
@@ -196,8 +197,12 @@ int attention_fwd(Context* ctx, const AttnIO& io, float* o, float* lse, int B, i
 // partial: 2*B*S*H*hd floats of scratch for per-query-head dK/dV partials
 // (attention_bwd_partial_floats); nullptr makes each CTA loop over its KV
 // head's query-head group instead (no scratch beyond D).  dO: contiguous.
+// rope_cos/rope_sin ([>= S][hd/2], 16-byte aligned): when given, dq and dk
+// leave with the transposed RoPE rotation applied and TF32-rounded, as the
+// separate backward RoPE pass would leave them.
 int attention_bwd(Context* ctx, const AttnIO& io, const float* o, const float* lse, const float* dO, float* D,
-                  float* partial, int B, int S, int H, int Hkv, int hd, bool round_dv, cudaStream_t s);
+                  float* partial, int B, int S, int H, int Hkv, int hd, bool round_dv, cudaStream_t s,
+                  const float* rope_cos = nullptr, const float* rope_sin = nullptr);
 size_t attention_bwd_partial_floats(int B, int S, int H, int Hkv, int hd);
 // elems: number of gradient elements the segments cover (for the profiler).
 int grad_norm(Context* ctx, const float* grads, const int64_t* segs, int nseg, float max_norm, double* norm_out,

@@ -414,8 +414,8 @@ struct Model {
     const int H = cfg.num_heads, Hkv = kvh, T = B * S;
     const int ld = static_cast<int>(qkv->cols), qw = H * hd, kw = Hkv * hd;
     if (llama) {
-      ck(rope(ctx, qkv->data, ld, T, S, H, hd, cos_t, sin_t, false, true, tp.stream()));
-      ck(rope(ctx, qkv->data + qw, ld, T, S, Hkv, hd, cos_t, sin_t, false, true, tp.stream()));
+      // q and k are adjacent in each row: H + Hkv heads rotated by one launch
+      ck(rope(ctx, qkv->data, ld, T, S, H + Hkv, hd, cos_t, sin_t, false, true, tp.stream()));
     }
     Node* out = tp.make(T, qw);
     out->require_grad = true;
@@ -434,9 +434,9 @@ struct Model {
       float* partial = np ? t->alloc(static_cast<int64_t>(np)) : nullptr;
       float* g = qkv->grad;
       const AttnIO io{qkv->data, ld, qkv->data + qw, ld, qkv->data + qw + kw, ld, g, ld, g + qw, ld, g + qw + kw, ld};
-      ck(attention_bwd(ctx, io, out->data, lse, out->grad, D, partial, B, S, H, Hkv, hd, true, t->stream()));
-      ck(rope(ctx, g, ld, T, S, H, hd, cos_t, sin_t, true, true, t->stream()));
-      ck(rope(ctx, g + qw, ld, T, S, Hkv, hd, cos_t, sin_t, true, true, t->stream()));
+      // the backward RoPE rotation of dq and dk happens in the kernels that write them
+      ck(attention_bwd(ctx, io, out->data, lse, out->grad, D, partial, B, S, H, Hkv, hd, true, t->stream(), cos_t,
+                       sin_t));
       qkv->grad_round = qkv->grad;
     };
     return out;

@@ -160,6 +160,12 @@ GLC_API int glc_gemm_tf32(glc_ctx* ctx, const float* A, int lda, int a_mn, const
  * 1 single-CTA 128x256 tiles, 2 CTA-pair tiles always.  Results agree to fp32
  * rounding across variants. */
 GLC_API int glc_set_gemm_variant(glc_ctx* ctx, int variant);
+/* Selects how many CTAs share one KV head's query-head group in the attention
+ * backward's dK/dV kernel (tuning and diagnostics; no reference counterpart):
+ * 0 automatic, else a divisor of H / Hkv (other values fall back to automatic).
+ * Each CTA accumulates its heads in TMEM; more than one writes partials that a
+ * deterministic group sum adds.  Results agree to fp32 rounding across splits. */
+GLC_API int glc_set_attention_split(glc_ctx* ctx, int nsplit);
 
 /* ------------------------------------------------------------------ fused / elementwise ops
  * Building blocks of the tape's GradFns; each mirrors one reference node.

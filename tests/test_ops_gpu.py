@@ -183,6 +183,40 @@ def test_attention_fwd_bwd(ctx, orc, B, S, H, Hkv, hd):
     assert max(errs) < ATTN_TOL, errs
 
 
+@pytest.mark.parametrize("nsplit", [1, 2, 4, 3])
+def test_attention_bwd_group_splits(ctx, orc, nsplit):
+    """dK/dV with the 4 query heads of each KV head over 1, 2 or 4 CTAs (3 is
+    not a divisor and falls back to the automatic choice): every split
+    against the oracle, and dq unchanged bit for bit."""
+    B, S, H, Hkv, hd = 2, 384, 8, 2, 64
+    T = B * S
+    r = rng(77)
+    q = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
+    k = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    v = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    dO = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
+    ref_dq, ref_dk, ref_dv = orc.attention_bwd(q, k, v, dO, S, H, Hkv, hd)
+    bq, bk, bv, bdo = ctx.from_numpy(q), ctx.from_numpy(k), ctx.from_numpy(v), ctx.from_numpy(dO)
+    bo, blse = ctx.empty((T, H * hd)), ctx.empty((B, H, S))
+    ctx.call("glc_attention_fwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, B, S, H, Hkv, hd, 0)
+    outs = []
+    try:
+        for split in (0, nsplit):
+            ctx.call("glc_set_attention_split", split)
+            bdq, bdk, bdv = ctx.empty(q.shape), ctx.empty(k.shape), ctx.empty(v.shape)
+            ctx.call("glc_attention_bwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, bdq.ptr, bdk.ptr,
+                     bdv.ptr, B, S, H, Hkv, hd, 0)
+            ctx.sync()
+            outs.append((bdq.numpy(), bdk.numpy(), bdv.numpy()))
+    finally:
+        ctx.call("glc_set_attention_split", 0)
+    dq, dk, dv = outs[1]
+    errs = [rel_fro(dq, ref_dq), rel_fro(dk, ref_dk), rel_fro(dv, ref_dv)]
+    assert max(errs) < ATTN_TOL, errs
+    assert np.array_equal(dq, outs[0][0])
+    assert rel_fro(dk, outs[0][1]) < 1e-5 and rel_fro(dv, outs[0][2]) < 1e-5
+
+
 def test_embedding_fwd_bwd(ctx):
     V, d, B, S = 50, 64, 3, 20
     T = B * S
