@@ -125,8 +125,10 @@ __global__ void __launch_bounds__(NT, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const Roles ro;
-  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // longest rows first
-  const int h = blockIdx.y, b = blockIdx.z, kh = h / (H / Hkv);
+  // grid (H, B, query tiles): query tiles vary slowest and the longest rows
+  // (last tile, most keys) are dispatched first
+  const int qt = n_qt - 1 - static_cast<int>(blockIdx.z);
+  const int h = blockIdx.x, b = blockIdx.y, kh = h / (H / Hkv);
   const int q0 = qt * 128, row_base = b * S;
   const int n_kv = qt + 1;
 
@@ -729,8 +731,9 @@ __global__ void __launch_bounds__(NT, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const Roles ro;
-  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);
-  const int h = blockIdx.y, b = blockIdx.z, kh = h / (H / Hkv);
+  // grid (H, B, query tiles), longest CTAs (last query tile) dispatched first
+  const int qt = n_qt - 1 - static_cast<int>(blockIdx.z);
+  const int h = blockIdx.x, b = blockIdx.y, kh = h / (H / Hkv);
   const int q0 = qt * 128, row_base = b * S;
   const int n_k64 = (S + 63) / 64;
   const int nk = min(n_k64, (q0 + 128) / 64);
@@ -988,7 +991,7 @@ int fwd_impl(Context* ctx, const float* q, int q_ld, const float* k, int k_ld, c
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
   const double causal = 0.5 * static_cast<double>(S) * (S + 1);
   ProfScope prof(ctx, PROF_ATTN_FWD, 2.0 * 2.0 * B * H * causal * HD, s);
-  attn_fwd_tc_kernel<HD><<<dim3(n_qt, H, B), NT, L::BYTES, s>>>(tq, tk, tv, o, lse, S, H, Hkv, n_qt, scale * LOG2E,
+  attn_fwd_tc_kernel<HD><<<dim3(H, B, n_qt), NT, L::BYTES, s>>>(tq, tk, tv, o, lse, S, H, Hkv, n_qt, scale * LOG2E,
                                                                    round_out ? 1 : 0, ctx->d_err);
   GLC_LAUNCH_CHECK(ctx, "attention_fwd (tcgen05)");
   return 0;
@@ -1055,7 +1058,7 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     GLC_LAUNCH_CHECK(ctx, "attention_bwd group sum");
   }
   const int n_qt = (S + 127) / 128;
-  attn_bwd_dq_tc_kernel<HD><<<dim3(n_qt, H, B), NT, DqLayout<HD>::BYTES, s>>>(
+  attn_bwd_dq_tc_kernel<HD><<<dim3(H, B, n_qt), NT, DqLayout<HD>::BYTES, s>>>(
       tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,
       rope_sin, ctx->d_err);
   GLC_LAUNCH_CHECK(ctx, "attention_bwd dq (tcgen05)");

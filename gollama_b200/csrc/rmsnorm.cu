@@ -147,16 +147,27 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
 }
 
 // dw[j] (+)= sum over blocks b of partial[b][j].  One block per 32 columns:
-// warp w adds rows w, w+8, ... for column (32*blockIdx.x + lane), then warp 0
-// adds the 8 warp sums in order (deterministic).
+// warp w keeps four running sums, of rows w + 8 * (4i + c) for c = 0..3 (four
+// independent load chains), adds them in order c = 0..3, and warp 0 adds the
+// 8 warp sums in order (deterministic).
 __global__ void column_sum_kernel(const float* __restrict__ partial, int nblocks, int cols, float* __restrict__ out,
                                   int accumulate) {
   __shared__ float red[8][33];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int j = blockIdx.x * 32 + lane;
   float s = 0.f;
-  if (j < cols)
-    for (int b = w; b < nblocks; b += 8) s += partial[static_cast<size_t>(b) * cols + j];
+  if (j < cols) {
+    float c4[4] = {0.f, 0.f, 0.f, 0.f};
+    int b = w;
+    for (; b + 24 < nblocks; b += 32) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) c4[c] += partial[static_cast<size_t>(b + 8 * c) * cols + j];
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      if (b + 8 * c < nblocks) c4[c] += partial[static_cast<size_t>(b + 8 * c) * cols + j];
+    s = ((c4[0] + c4[1]) + c4[2]) + c4[3];
+  }
   red[w][lane] = s;
   __syncthreads();
   if (w == 0 && j < cols) {

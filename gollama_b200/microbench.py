@@ -170,6 +170,9 @@ CASES = {
     "gemm_dw_lmhead": lambda c, i, w: case_gemm(c, "dw", T, D, V, i, w),
     "gemm_bwd_lmhead": lambda c, i, w: case_gemm(c, "bwd", T, D, V, i, w),
     "gemm_bwd_down": lambda c, i, w: case_gemm(c, "bwd", T, F, D, i, w),
+    "gemm_fwd_down": lambda c, i, w: case_gemm(c, "fwd", T, F, D, i, w),
+    "gemm_fwd_qkv": lambda c, i, w: case_gemm(c, "fwd", T, D, D + 2 * D // 8, i, w),
+    "gemm_bwd_qkv": lambda c, i, w: case_gemm(c, "bwd", T, D, D + 2 * D // 8, i, w),
     "gemm_bwd_gateup": lambda c, i, w: case_gemm(c, "bwd", T, D, 2 * F, i, w),
     "linear_sweep": case_linear_sweep,
     "gemm_majors": case_gemm_majors,
