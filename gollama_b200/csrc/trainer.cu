@@ -821,7 +821,16 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
       if (!dp) return;
       for (Node* p : n->parents)
         for_params(p, [&](int i) {
-          if (--consumers[i] == 0 && --bucket_pending[model->bucket_of[i]] == 0) launch_bucket(model->bucket_of[i]);
+          if (--consumers[i] != 0) return;
+          // final: an allocated gradient no GradFn wrote this step is zero
+          // before its bucket is summed over the ranks
+          if (model->grad_allocated[i] && !model->grad_live[i]) {
+            if (cudaMemsetAsync(model->grads + model->offset[i], 0,
+                                sizeof(float) * model->rows[i] * model->cols[i], ctx->stream) != cudaSuccess)
+              throw StepError{GLC_ERR_CUDA};
+            model->grad_live[i] = 1;
+          }
+          if (--bucket_pending[model->bucket_of[i]] == 0) launch_bucket(model->bucket_of[i]);
         });
     };
     if (model->llama) {

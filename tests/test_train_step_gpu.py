@@ -93,3 +93,31 @@ def test_multi_step_loss_curve(ctx):
     for a, b in zip(losses, olosses):
         assert abs(a - b) <= 1e-3 * abs(b), (losses, olosses)
     assert rel_fro(model.get_params(), st.params) < WEIGHT_RFRO
+
+
+@pytest.mark.parametrize("shape", [syn.TINY, syn.TINY_LLAMA_MODE], ids=lambda s: s.name)
+def test_second_step_norm_grads_weights(ctx, shape):
+    """Two steps (the second with every gradient already allocated, AdamW
+    moments non-zero): each step's clip norm, and the second step's clipped
+    gradients and weights, against the oracle's."""
+    params = syn.init_params(shape, 31)
+    batches = [syn.batch(shape, 40 + s) for s in range(2)]
+    orc = Oracle(threads=threads())
+    ocfg = oracle_config(shape)
+    st = TrainState.create(params, len(orc.param_layout(ocfg)), oracle_optim())
+    onorms = [orc.train_step(ocfg, st, i, t)[1] for i, t in batches]
+    model = NewTrainableModel(config_for(shape, **STEP_HPARAMS), ctx)
+    model.set_params(params)
+    tr = NewTrainer(model)
+    norms = []
+    for i, t in batches:
+        tr.TrainStep(i, t)
+        norms.append(tr.last_stats()[0])
+    for a, b in zip(norms, onorms):
+        assert abs(a - b) <= 2e-3 * abs(b), (norms, onorms)
+    grads, weights = model.get_grads(), model.get_params()
+    for p in model.Params():
+        seg = slice(p.offset, p.offset + p.shape[0] * p.shape[1])
+        if p.has_grad:
+            assert rel_fro(grads[seg], st.grads[seg]) < GRAD_RFRO, p.index
+        assert rel_fro(weights[seg], st.params[seg]) < WEIGHT_RFRO, p.index
