@@ -111,7 +111,7 @@ __device__ __forceinline__ void adam_elem(float& p, float& g, float& m, float& v
 // a multiple of the hidden size, itself a multiple of 4): float4 throughout.
 __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
                              float* __restrict__ shadow, const Seg* __restrict__ segs,
-                             const float* __restrict__ clip_scale, AdamArgs a) {
+                             const float* __restrict__ clip_scale, AdamArgs a, int write_g) {
   const Seg sg = segs[blockIdx.y];
   const float scale = clip_scale ? *clip_scale : 1.0f;
   const bool scaled = scale != 1.0f;
@@ -127,7 +127,7 @@ __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float
     adam_elem(P.y, G.y, M.y, V.y, scale, scaled, a);
     adam_elem(P.z, G.z, M.z, V.z, scale, scaled, a);
     adam_elem(P.w, G.w, M.w, V.w, scale, scaled, a);
-    if (scaled) g4[i] = G;
+    if (scaled && write_g) g4[i] = G;
     m4[i] = M;
     v4[i] = V;
     p4[i] = P;
@@ -165,7 +165,7 @@ int grad_norm(Context* ctx, const float* grads, const int64_t* segs, int nseg, f
 
 int adamw(Context* ctx, float* p, float* g, float* m, float* v, float* shadow, const int64_t* segs, int nseg,
           const float* clip_scale, float lr, float beta1, float beta2, float eps, float wd, int step, double elems,
-          cudaStream_t s) {
+          cudaStream_t s, bool write_grad) {
   if (nseg <= 0) return 0;
   if (!p || !g || !m || !v || !segs || step <= 0) return ctx->fail(GLC_ERR_INVALID, "adamw: bad arguments");
   AdamArgs a;
@@ -184,8 +184,27 @@ int adamw(Context* ctx, float* p, float* g, float* m, float* v, float* shadow, c
   if (bx < 4) bx = 4;
   // p, g, m, v read; p, m, v and the TF32 shadow written
   ProfScope prof(ctx, PROF_ADAMW, (shadow ? 32.0 : 28.0) * elems, s);
-  adamw_kernel<<<dim3(bx, nseg), 256, 0, s>>>(p, g, m, v, shadow, reinterpret_cast<const Seg*>(segs), clip_scale, a);
+  adamw_kernel<<<dim3(bx, nseg), 256, 0, s>>>(p, g, m, v, shadow, reinterpret_cast<const Seg*>(segs), clip_scale, a,
+                                               write_grad ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "adamw");
+  return 0;
+}
+
+namespace {
+// g = g * scale (float32, as the clipping in the AdamW kernel), unless scale is 1
+__global__ void scale_in_place_kernel(float* __restrict__ g, size_t n, const float* __restrict__ scale) {
+  const float sc = *scale;
+  if (sc == 1.0f) return;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+    g[i] = __fmul_rn(g[i], sc);
+}
+}  // namespace
+
+int scale_in_place(Context* ctx, float* g, size_t n, const float* scale, cudaStream_t s) {
+  if (n == 0) return 0;
+  if (!g || !scale) return ctx->fail(GLC_ERR_INVALID, "scale_in_place: null pointer");
+  scale_in_place_kernel<<<grid_for(n, 256, ctx->num_sms), 256, 0, s>>>(g, n, scale);
+  GLC_LAUNCH_CHECK(ctx, "scale_in_place");
   return 0;
 }
 

@@ -209,7 +209,11 @@ int grad_norm(Context* ctx, const float* grads, const int64_t* segs, int nseg, f
               float* scale_out, double* scratch, int scratch_count, double elems, cudaStream_t s);
 int adamw(Context* ctx, float* p, float* g, float* m, float* v, float* shadow, const int64_t* segs, int nseg,
           const float* clip_scale, float lr, float beta1, float beta2, float eps, float wd, int step, double elems,
-          cudaStream_t s);
+          cudaStream_t s, bool write_grad = true);
+// write_grad = false leaves the unclipped gradient in g (the caller applies the
+// clip scale later, scale_in_place); otherwise g receives the clipped gradient
+// as GradientClipping (optimizer.go:169-196) leaves it.
+int scale_in_place(Context* ctx, float* g, size_t n, const float* scale, cudaStream_t s);
 
 // RoPE tables (pkg/model/rope.go:33-48) computed on the host in float64 and
 // rounded to float32: cos_t/sin_t are [max_seq][dim/2].

@@ -80,7 +80,9 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
     const float r = rms[row];
     const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * cols);
     const float4* dyr = reinterpret_cast<const float4*>(dy + static_cast<size_t>(row) * cols);
-    float4 xv[MAXC], dv[MAXC];
+    float4* dxr = reinterpret_cast<float4*>(dx + static_cast<size_t>(row) * cols);
+    // the accumulated dx is loaded with x and dy, before the row reduction
+    float4 xv[MAXC], dv[MAXC], ov[MAXC];
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < MAXC; ++i) {
@@ -88,6 +90,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
       if (c < nc) {
         xv[i] = xr[c];
         dv[i] = dyr[c];
+        if (dx_accumulate) ov[i] = dxr[c];
         if (full)
           s += dv[i].x * wv[i].x * xv[i].x + dv[i].y * wv[i].y * xv[i].y + dv[i].z * wv[i].z * xv[i].z +
                dv[i].w * wv[i].w * xv[i].w;
@@ -108,7 +111,6 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
       __syncthreads();
       coef = tot / (static_cast<float>(cols) * r * r * r);
     }
-    float4* dxr = reinterpret_cast<float4*>(dx + static_cast<size_t>(row) * cols);
     float4* dxq = dx_round ? reinterpret_cast<float4*>(dx_round + static_cast<size_t>(row) * cols) : nullptr;
 #pragma unroll
     for (int i = 0; i < MAXC; ++i) {
@@ -126,7 +128,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
           g.w = __fsub_rn(g.w, __fmul_rn(xv[i].w, coef));
         }
         if (dx_accumulate) {
-          const float4 o = dxr[c];
+          const float4 o = ov[i];
           g.x = __fadd_rn(o.x, g.x); g.y = __fadd_rn(o.y, g.y); g.z = __fadd_rn(o.z, g.z); g.w = __fadd_rn(o.w, g.w);
         }
         dxr[c] = g;

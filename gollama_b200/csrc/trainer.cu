@@ -253,6 +253,11 @@ struct Model {
   // Go's `Grad != nil` per parameter, and "holds this step's value"
   std::vector<char> grad_allocated, grad_live;
   float *cos_t = nullptr, *sin_t = nullptr;  // RoPE tables [max_seq][hd/2]
+  // After a step the gradients hold the unclipped values and pending_scale
+  // (one device float) the clip scale; reading them applies it first, so the
+  // step does not write the clipped gradients back (4 bytes per parameter).
+  float* pending_scale = nullptr;
+  bool scale_pending = false;
   std::vector<Node> param_nodes;
   std::vector<Node> qkv_view, gu_view;  // per layer: WQ|WK|WV and WGate|WUp
 
@@ -280,7 +285,7 @@ struct Model {
   int out_norm() const { return num_params() - 1; }
 
   ~Model() {
-    for (float* p : {params, grads, m, v, shadow, cos_t, sin_t})
+    for (float* p : {params, grads, m, v, shadow, cos_t, sin_t, pending_scale})
       if (p) cudaFree(p);
   }
 
@@ -628,6 +633,7 @@ int Model::init(Context* c, const glc_train_config& conf) {
   for (float** p : {&params, &grads, &m, &v, &shadow}) {
     if (cudaMalloc(p, bytes) != cudaSuccess) return c->fail(GLC_ERR_NOMEM, "model: cannot allocate parameter arenas");
   }
+  if (cudaMalloc(&pending_scale, sizeof(float)) != cudaSuccess) return c->fail(GLC_ERR_NOMEM, "model: clip scale");
   if (cudaMemsetAsync(grads, 0, bytes, c->stream) != cudaSuccess || cudaMemsetAsync(m, 0, bytes, c->stream) != cudaSuccess ||
       cudaMemsetAsync(v, 0, bytes, c->stream) != cudaSuccess)
     return c->fail(GLC_ERR_CUDA, "model: memset");
@@ -747,7 +753,8 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
   const int T = B * S;
   const uint64_t l0 = ctx->launches;
   try {
-    // TrainStep (trainer.go:462-505)
+    // TrainStep (trainer.go:462-505); every gradient is rewritten below
+    model->scale_pending = false;
     ++step;
     lr = get_lr(step);
     // ZeroGrad (optimizer.go:79-83): existing gradients become zero; the
@@ -877,7 +884,12 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
                    static_cast<double>(seg_elems), ctx->stream));
       ++adam_step;
       ck(adamw(ctx, model->params, model->grads, model->m, model->v, model->shadow, segs_dev, nseg, d_scale, lr,
-               c.beta1, c.beta2, c.epsilon, c.weight_decay, adam_step, static_cast<double>(seg_elems), ctx->stream));
+               c.beta1, c.beta2, c.epsilon, c.weight_decay, adam_step, static_cast<double>(seg_elems), ctx->stream,
+               /*write_grad=*/false));
+      if (cudaMemcpyAsync(model->pending_scale, d_scale, sizeof(float), cudaMemcpyDeviceToDevice, ctx->stream) !=
+          cudaSuccess)
+        throw StepError{GLC_ERR_CUDA};
+      model->scale_pending = true;
     }
     if (cudaMemcpyAsync(loss_host, scalars, 16, cudaMemcpyDeviceToHost, ctx->stream) != cudaSuccess)
       throw StepError{GLC_ERR_CUDA};
@@ -1015,6 +1027,13 @@ int glc_model_get_params(glc_model* m, float* host, int64_t n) {
   return arena_copy(m, m ? m->impl.params : nullptr, host, nullptr, n, false);
 }
 int glc_model_get_grads(glc_model* m, float* host, int64_t n) {
+  if (m && n == m->impl.total && m->impl.scale_pending) {
+    // the gradients as GradientClipping left them (optimizer.go:169-196)
+    glc::Model& md = m->impl;
+    int rc = glc::scale_in_place(md.ctx, md.grads, static_cast<size_t>(md.total), md.pending_scale, md.ctx->stream);
+    if (rc) return rc;
+    md.scale_pending = false;
+  }
   return arena_copy(m, m ? m->impl.grads : nullptr, host, nullptr, n, false);
 }
 int glc_model_get_moments(glc_model* m, float* mh, float* vh, int64_t n) {

@@ -149,6 +149,35 @@ def case_rmsnorm(ctx, iters, warmup):
     return f"rmsnorm_bwd {T}x{D}", ms, 5.0 * 4 * T * D / (ms * 1e-3) / 1e9, "GB/s"
 
 
+def case_rmsnorm_fwd(ctx, iters, warmup):
+    x, w = _rand(ctx, (T, D), 10, tf32=False), _rand(ctx, (D,), 11, tf32=False)
+    y, rms = ctx.empty((T, D)), ctx.empty((T,))
+    ms = _time(ctx, lambda: ctx.call("glc_rmsnorm_fwd", x.ptr, w.ptr, y.ptr, rms.ptr, T, D, C.c_float(1e-5), 1),
+               iters, warmup)
+    return f"rmsnorm_fwd {T}x{D}", ms, 2.0 * 4 * T * D / (ms * 1e-3) / 1e9, "GB/s"
+
+
+def case_optimizer(ctx, iters, warmup, n=1 << 28):
+    """Clip norm and AdamW over one 2^28-parameter segment (5 fp32 arenas,
+    5.4 GB), clip scale 0.5 so the clipped gradient is written back:
+    norm 4 B/parameter, AdamW 36 B/parameter."""
+    r = np.random.default_rng(15)
+    p = ctx.from_numpy((r.standard_normal(n, dtype=np.float32) * np.float32(0.02)))
+    g = ctx.from_numpy((r.standard_normal(n, dtype=np.float32) * np.float32(1e-3)))
+    m, v, sh = ctx.zeros((n,)), ctx.zeros((n,)), ctx.empty((n,))
+    segs = np.array([0, n], np.int64)
+    sp = segs.ctypes.data_as(C.c_void_p)
+    norm, nscale = ctx.empty((2,)), ctx.empty((1,))  # a float64 and a float32
+    scale = ctx.from_numpy(np.array([0.5], np.float32))
+    ms_n = _time(ctx, lambda: ctx.call("glc_grad_clip_norm", g.ptr, sp, 1, C.c_float(1.0), norm.ptr, nscale.ptr),
+                 iters, warmup)
+    ms_a = _time(ctx, lambda: ctx.call("glc_adamw_step", p.ptr, g.ptr, m.ptr, v.ptr, sh.ptr, sp, 1, scale.ptr,
+                                       C.c_float(3e-4), C.c_float(0.9), C.c_float(0.95), C.c_float(1e-8),
+                                       C.c_float(0.1), 1), iters, warmup)
+    return [(f"grad_clip_norm n={n}", ms_n, 4.0 * n / (ms_n * 1e-3) / 1e9, "GB/s"),
+            (f"adamw n={n} (clipped)", ms_a, 36.0 * n / (ms_a * 1e-3) / 1e9, "GB/s")]
+
+
 def case_ce(ctx, iters, warmup):
     logits = _rand(ctx, (T, V), 13, 2.0, tf32=False)
     tg = ctx.from_numpy(np.random.default_rng(14).integers(0, V, T).astype(np.int64))
@@ -187,6 +216,8 @@ CASES = {
     "quant_dx_q8_0": lambda c, i, w: case_quant_dx(c, 8, i, w),
     "quant_dx_q4_0": lambda c, i, w: case_quant_dx(c, 2, i, w),
     "rmsnorm_bwd": case_rmsnorm,
+    "rmsnorm_fwd": case_rmsnorm_fwd,
+    "optimizer": case_optimizer,
     "softmax_ce": case_ce,
 }
 
