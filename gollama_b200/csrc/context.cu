@@ -102,6 +102,7 @@ int glc_destroy(glc_ctx* ctx) {
     cudaEventDestroy(r.b);
   }
   for (auto e : c->event_pool) cudaEventDestroy(e);
+  for (auto& s : c->gemm_sched) cudaFree(s.second);
   cudaStreamDestroy(c->stream);
   cudaStreamDestroy(c->comm_stream);
   delete c;

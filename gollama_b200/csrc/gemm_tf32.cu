@@ -30,6 +30,9 @@
 //                          L2->SM limit; the pair tile needs ~64.
 // The pair kernel serves problems with M > 128; tiny ones keep the
 // single-CTA tile.
+#include <algorithm>
+#include <functional>
+#include <queue>
 #include <utility>
 
 #include "glc_internal.h"
@@ -94,7 +97,27 @@ struct GroupArgs {
   int nprob;
   int total_tiles;
   int* err;
+  // Tile order of the CTA-pair kernel: nullptr walks tile = cluster,
+  // cluster + clusters, ...; otherwise sched[c] .. sched[c + 1] index into
+  // the tile list sched[clusters + 1 ..] the clusters of cluster c.
+  const int* sched;
 };
+
+// The range of list positions of cluster c and the tile at position it.
+__device__ __forceinline__ void sched_range(const GroupArgs& a, int c, int nclusters, int& it0, int& it1, int& step) {
+  if (a.sched) {
+    it0 = a.sched[c];
+    it1 = a.sched[c + 1];
+    step = 1;
+  } else {
+    it0 = c;
+    it1 = a.total_tiles;
+    step = nclusters;
+  }
+}
+__device__ __forceinline__ int sched_tile(const GroupArgs& a, int nclusters, int it) {
+  return a.sched ? a.sched[nclusters + 1 + it] : it;
+}
 
 // UMMA descriptor of the operand for k-step kk inside one stage's tile.
 //   K-major : rows of 128 B (16-byte-chunk swizzle), 8-row groups 1 KB apart;
@@ -437,8 +460,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = cluster; tile < args.total_tiles && ok; tile += nclusters) {
-        const TileRef t = locate<PAIR_BM>(args, tile);
+      int it0, it1, istep;
+      sched_range(args, cluster, nclusters, it0, it1, istep);
+      for (int it = it0; it < it1 && ok; it += istep) {
+        const TileRef t = locate<PAIR_BM>(args, sched_tile(args, nclusters, it));
         const Problem& p = args.p[t.prob];
         const CUtensorMap* tmA = t.prob ? &tmA1 : &tmA0;
         const CUtensorMap* tmB = t.prob ? &tmB1 : &tmB0;
@@ -474,8 +499,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
       int local = 0;
       bool ok = true;
       bool issued_any = false;
-      for (int tile = cluster; tile < args.total_tiles && ok; tile += nclusters, ++local) {
-        const TileRef t = locate<PAIR_BM>(args, tile);
+      int it0, it1, istep;
+      sched_range(args, cluster, nclusters, it0, it1, istep);
+      for (int it = it0; it < it1 && ok; it += istep, ++local) {
+        const TileRef t = locate<PAIR_BM>(args, sched_tile(args, nclusters, it));
         const Problem& p = args.p[t.prob];
         const uint32_t idesc = umma_idesc_tf32(PAIR_BM, BN, p.a_mn != 0, p.b_mn != 0);
         const int buf = local & 1;
@@ -537,8 +564,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
     const int row_in_half = q * 32 + lane;
     const uint32_t tempty_leader = mapa_cluster(tempty_bar, 0);
     int local = 0;
-    for (int tile = cluster; tile < args.total_tiles; tile += nclusters, ++local) {
-      const TileRef t = locate<PAIR_BM>(args, tile);
+    int it0, it1, istep;
+    sched_range(args, cluster, nclusters, it0, it1, istep);
+    for (int it = it0; it < it1; it += istep, ++local) {
+      const TileRef t = locate<PAIR_BM>(args, sched_tile(args, nclusters, it));
       const Problem& p = args.p[t.prob];
       const bool vec_ok = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
                           (p.R == nullptr || (((p.ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.R) & 15) == 0)));
@@ -739,6 +768,60 @@ int prepare(Context* ctx, const GemmSpec& g, Problem* p, CUtensorMap* ta, CUtens
   return 0;
 }
 
+// Tile lists for a grouped CTA-pair launch.  The two problems' tiles cost
+// different times (their k-block counts differ: dX and dW of one layer), so
+// the fixed rotation tile = cluster + i * clusters can leave some clusters a
+// long tile more than others.  Here tiles are handed out in index order to
+// the cluster that frees first, with a tile's time estimated as its k-blocks
+// plus 2 (pipeline turn-around): the order a dynamic queue would produce,
+// fixed on the host so every role of both CTAs walks the same list.  Cached
+// per shape on the device; nullptr (the rotation) when the estimate is not
+// at least 1 % shorter than the rotation's (the rotation keeps concurrent
+// tiles adjacent) or if memory is short.
+const int* pair_schedule(Context* ctx, const GroupArgs& a, int clusters) {
+  const std::array<long long, 5> key{a.p[0].tiles, a.p[0].k_blocks, a.p[1].tiles, a.p[1].k_blocks, clusters};
+  for (auto& e : ctx->gemm_sched)
+    if (e.first == key) return e.second;
+  std::vector<std::vector<int>> lists(clusters);
+  using Slot = std::pair<long long, int>;  // (estimated finish, cluster): ties go to the lower cluster
+  std::priority_queue<Slot, std::vector<Slot>, std::greater<Slot>> q;
+  for (int c = 0; c < clusters; ++c) q.push({0, c});
+  std::vector<long long> rot(clusters, 0);
+  long long greedy_end = 0;
+  for (int t = 0; t < a.total_tiles; ++t) {
+    const Slot s = q.top();
+    q.pop();
+    lists[s.second].push_back(t);
+    const int kb = t < a.p[0].tiles ? a.p[0].k_blocks : a.p[1].k_blocks;
+    q.push({s.first + kb + 2, s.second});
+    greedy_end = std::max(greedy_end, s.first + kb + 2);
+    rot[t % clusters] += kb + 2;
+  }
+  if (100 * greedy_end > 99 * *std::max_element(rot.begin(), rot.end())) {
+    ctx->gemm_sched.push_back({key, nullptr});
+    return nullptr;
+  }
+  std::vector<int> h(static_cast<size_t>(clusters) + 1 + a.total_tiles);
+  int pos = 0;
+  for (int c = 0; c < clusters; ++c) {
+    h[c] = pos;
+    for (int t : lists[c]) h[clusters + 1 + pos++] = t;
+  }
+  h[clusters] = pos;
+  int* d = nullptr;
+  if (cudaMalloc(&d, h.size() * sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (cudaMemcpy(d, h.data(), h.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(d);
+    cudaGetLastError();
+    return nullptr;
+  }
+  ctx->gemm_sched.push_back({key, d});
+  return d;
+}
+
 }  // namespace
 
 int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t stream) {
@@ -824,6 +907,7 @@ int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t str
     // one cluster per SM pair; clusters loop over the tiles
     const int pairs = ctx->num_sms / 2;
     const int clusters = a.total_tiles < pairs ? a.total_tiles : pairs;
+    if (nl == 2) a.sched = pair_schedule(ctx, a, clusters);
     gemm_tf32_pair_kernel<<<2 * clusters, P_NUM_THREADS, P_SMEM_BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3], a);
   } else {
     const int grid = a.total_tiles < ctx->num_sms ? a.total_tiles : ctx->num_sms;

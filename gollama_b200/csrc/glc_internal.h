@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <array>
 #include <cstddef>
 #include <cstdint>
 #include <mutex>
@@ -26,6 +27,9 @@ struct Context {
   std::string last_error;
   uint64_t launches = 0;               // kernels this library launched
   int gemm_variant = 0;                // 0 automatic, 1 single-CTA tiles, 2 CTA-pair tiles
+  // device tile lists of grouped CTA-pair GEMM launches, by (tiles and
+  // k-blocks of each problem, clusters); built once per shape
+  std::vector<std::pair<std::array<long long, 5>, int*>> gemm_sched;
   int attn_split = 0;                  // dK/dV CTAs per KV head: 0 automatic, else a divisor of the group
   EncodeTiledFn encode_fn = nullptr;
   // scratch workspace owned by the context (grown on demand, never shrunk)
