@@ -105,7 +105,7 @@ def test_swiglu_bwd_bit_exact(ctx, orc, n):
     assert np.array_equal(bdg.numpy(), dgate)
 
 
-@pytest.mark.parametrize("rows,V", [(7, 256), (512, 32000), (64, 1000)])
+@pytest.mark.parametrize("rows,V", [(7, 256), (512, 32000), (64, 1000), (33, 8196), (16, 40000)])
 @pytest.mark.parametrize("write_grad", [0, 1])
 def test_softmax_ce(ctx, orc, rows, V, write_grad):
     r = rng(rows + V)
