@@ -41,6 +41,12 @@ namespace {
 
 constexpr int NT = 320;
 constexpr int MATH_THREADS = 256;  // warps 2..9
+// Backward kernels: warp 10 issues the accumulating MMAs (dV/dK, dQ) while
+// warp 1 issues S and dP.  One thread issues a tcgen05.mma about every 49
+// cycles at best, and an N = 64 TF32 MMA with A in TMEM needs 32 cycles of
+// the tensor core: two issuing threads keep it busy, one cannot.
+constexpr int NT_BWD = 352;
+constexpr int ACC_WARP = 10;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 
@@ -410,7 +416,7 @@ __device__ __forceinline__ void tile_rows_to_tmem(const uint8_t* tile, int row, 
 // tile 0 meets every query) are dispatched first.  nsplit == 1 writes the
 // final dk/dv; otherwise partial [T][Hkv * nsplit][hd] for the group sum.
 template <int HD>
-__global__ void __launch_bounds__(NT, 1)
+__global__ void __launch_bounds__(NT_BWD, 1)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQk, const __grid_constant__ CUtensorMap tmQm,
                             const __grid_constant__ CUtensorMap tmOk, const __grid_constant__ CUtensorMap tmOm,
                             const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -424,7 +430,8 @@ __global__ void __launch_bounds__(NT, 1)
   uint64_t *kv_full = bars, *qo_full = bars + 1, *qo_empty = bars + 4, *s_full = bars + 7, *p_full = bars + 9,
            *set_free = bars + 11, *acc_done = bars + 13, *drain = bars + 14, *ld_ready = bars + 15,
            *kv_moved = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* drain_acc = bars + 18;  // abort path of the accumulate issuer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* stage_ld = reinterpret_cast<float*>(sm + L::OFF_LD);  // [2][lse 64 | D 64]
   const Roles ro;
@@ -453,6 +460,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
+    mbar_init(drain_acc, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -494,46 +502,56 @@ __global__ void __launch_bounds__(NT, 1)
   } else if (ro.warp == 1) {
     if (ro.lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_tf32(128, 64, false, false);
-      constexpr uint32_t idesc_a = umma_idesc_tf32(128, HD, false, true);
       // K and V are A operands in TMEM once the math warps have copied them
       bool ok = mbar_wait(kv_moved, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
       bool issued = false;
       tc_fence_after();
-      for (int it = 0; ok && it <= n_it; ++it) {
-        if (it < n_it) {
-          const int st = it % L::NST, ts = it % L::NSET;
-          const uint32_t base = s0 + st * L::STAGE;
-          if (!mbar_wait(&qo_full[st], (it / L::NST) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-          if (!mbar_wait(&set_free[ts], ((it / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
-          tc_fence_after();
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int st = it % L::NST, ts = it % L::NSET;
+        const uint32_t base = s0 + st * L::STAGE;
+        if (!mbar_wait(&qo_full[st], (it / L::NST) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        if (!mbar_wait(&set_free[ts], ((it / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
+        tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < HD / 8; ++kk) {
-            umma_tf32_ts(tmem + ts * 128, tmem + L::K_COL + kk * 8, kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
-            umma_tf32_ts(tmem + ts * 128 + 64, tmem + L::V_COL + kk * 8, kdesc<64>(base + 2 * L::QT, kk), idesc_s,
-                         kk > 0 ? 1u : 0u);
-          }
-          issued = true;
-          umma_commit(&s_full[ts]);
+        for (int kk = 0; kk < HD / 8; ++kk) {
+          umma_tf32_ts(tmem + ts * 128, tmem + L::K_COL + kk * 8, kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
+          umma_tf32_ts(tmem + ts * 128 + 64, tmem + L::V_COL + kk * 8, kdesc<64>(base + 2 * L::QT, kk), idesc_s,
+                       kk > 0 ? 1u : 0u);
         }
-        if (it >= 1) {
-          const int pit = it - 1, ps = pit % L::NST, pts = pit % L::NSET;
-          const uint32_t base = s0 + ps * L::STAGE;
-          if (!mbar_wait(&p_full[pts], (pit / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t acc = (pit > 0 || kk > 0) ? 1u : 0u;
-            umma_tf32_ts(tmem + L::DV_COL, tmem + pts * 128 + kk * 8, mdesc<64>(base + 3 * L::QT, kk), idesc_a, acc);
-            umma_tf32_ts(tmem + L::DK_COL, tmem + pts * 128 + 64 + kk * 8, mdesc<64>(base + L::QT, kk), idesc_a, acc);
-          }
-          umma_commit(&set_free[pts]);
-          umma_commit(&qo_empty[ps]);
-        }
+        issued = true;
+        umma_commit(&s_full[ts]);
       }
-      if (ok) umma_commit(acc_done);
       if (!ok && issued) {
         umma_commit(drain);
         mbar_drain(drain, 0, err);
+      }
+    }
+  } else if (ro.warp == ACC_WARP) {
+    // dV += P^T dO and dK += dS^T Q of each step once the math warps have
+    // written P and dS.  Its commits also cover the S/dP MMAs of the same
+    // step (they completed before the math warps could read S).
+    if (ro.lane == 0) {
+      constexpr uint32_t idesc_a = umma_idesc_tf32(128, HD, false, true);
+      bool ok = true, issued = false;
+      for (int pit = 0; ok && pit < n_it; ++pit) {
+        const int ps = pit % L::NST, pts = pit % L::NSET;
+        const uint32_t base = s0 + ps * L::STAGE;
+        if (!mbar_wait(&p_full[pts], (pit / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t acc = (pit > 0 || kk > 0) ? 1u : 0u;
+          umma_tf32_ts(tmem + L::DV_COL, tmem + pts * 128 + kk * 8, mdesc<64>(base + 3 * L::QT, kk), idesc_a, acc);
+          umma_tf32_ts(tmem + L::DK_COL, tmem + pts * 128 + 64 + kk * 8, mdesc<64>(base + L::QT, kk), idesc_a, acc);
+        }
+        issued = true;
+        umma_commit(&set_free[pts]);
+        umma_commit(&qo_empty[ps]);
+      }
+      if (ok) umma_commit(acc_done);
+      if (!ok && issued) {
+        umma_commit(drain_acc);
+        mbar_drain(drain_acc, 0, err);
       }
     }
   } else {
@@ -715,7 +733,7 @@ struct DqLayout {
 };
 
 template <int HD>
-__global__ void __launch_bounds__(NT, 1)
+__global__ void __launch_bounds__(NT_BWD, 1)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmO,
                           const __grid_constant__ CUtensorMap tmKk, const __grid_constant__ CUtensorMap tmKm,
                           const __grid_constant__ CUtensorMap tmVk, const float* __restrict__ lse,
@@ -728,7 +746,8 @@ __global__ void __launch_bounds__(NT, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
   uint64_t *qo_full = bars, *kv_full = bars + 1, *kv_empty = bars + 5, *s_full = bars + 9, *p_full = bars + 11,
            *set_free = bars + 13, *acc_done = bars + 15, *drain = bars + 16, *qo_moved = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* drain_acc = bars + 18;  // abort path of the accumulate issuer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const Roles ro;
   // grid (H, B, query tiles), longest CTAs (last query tile) dispatched first
@@ -752,6 +771,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
+    mbar_init(drain_acc, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -791,44 +811,53 @@ __global__ void __launch_bounds__(NT, 1)
   } else if (ro.warp == 1) {
     if (ro.lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_tf32(128, 64, false, false);
-      constexpr uint32_t idesc_q = umma_idesc_tf32(128, HD, false, true);
       // Q and dO are A operands in TMEM once the math warps have copied them
       bool ok = mbar_wait(qo_moved, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
       bool issued = false;
       tc_fence_after();
-      for (int j = 0; ok && j <= nk; ++j) {
-        if (j < nk) {
-          const int st = j % L::NST, ts = j % L::NSET;
-          const uint32_t base = s0 + st * L::STAGE;
-          if (!mbar_wait(&kv_full[st], (j / L::NST) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-          if (!mbar_wait(&set_free[ts], ((j / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
-          tc_fence_after();
+      for (int j = 0; ok && j < nk; ++j) {
+        const int st = j % L::NST, ts = j % L::NSET;
+        const uint32_t base = s0 + st * L::STAGE;
+        if (!mbar_wait(&kv_full[st], (j / L::NST) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        if (!mbar_wait(&set_free[ts], ((j / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
+        tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < HD / 8; ++kk) {
-            umma_tf32_ts(tmem + ts * 128, tmem + L::Q_COL + kk * 8, kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
-            umma_tf32_ts(tmem + ts * 128 + 64, tmem + L::O_COL + kk * 8, kdesc<64>(base + 2 * L::KT, kk), idesc_s,
-                         kk > 0 ? 1u : 0u);
-          }
-          issued = true;
-          umma_commit(&s_full[ts]);
+        for (int kk = 0; kk < HD / 8; ++kk) {
+          umma_tf32_ts(tmem + ts * 128, tmem + L::Q_COL + kk * 8, kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
+          umma_tf32_ts(tmem + ts * 128 + 64, tmem + L::O_COL + kk * 8, kdesc<64>(base + 2 * L::KT, kk), idesc_s,
+                       kk > 0 ? 1u : 0u);
         }
-        if (j >= 1) {
-          const int pj = j - 1, ps = pj % L::NST, pts = pj % L::NSET;
-          const uint32_t base = s0 + ps * L::STAGE;
-          if (!mbar_wait(&p_full[pts], (pj / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_tf32_ts(tmem + L::DQ_COL, tmem + pts * 128 + kk * 8, mdesc<64>(base + L::KT, kk), idesc_q,
-                         (pj > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&set_free[pts]);
-          umma_commit(&kv_empty[ps]);
-        }
+        issued = true;
+        umma_commit(&s_full[ts]);
       }
-      if (ok) umma_commit(acc_done);
       if (!ok && issued) {
         umma_commit(drain);
         mbar_drain(drain, 0, err);
+      }
+    }
+  } else if (ro.warp == ACC_WARP) {
+    // dQ += dS K of each step once the math warps have written dS; its
+    // commits also cover the step's S/dP MMAs (complete before dS exists)
+    if (ro.lane == 0) {
+      constexpr uint32_t idesc_q = umma_idesc_tf32(128, HD, false, true);
+      bool ok = true, issued = false;
+      for (int pj = 0; ok && pj < nk; ++pj) {
+        const int ps = pj % L::NST, pts = pj % L::NSET;
+        const uint32_t base = s0 + ps * L::STAGE;
+        if (!mbar_wait(&p_full[pts], (pj / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_tf32_ts(tmem + L::DQ_COL, tmem + pts * 128 + kk * 8, mdesc<64>(base + L::KT, kk), idesc_q,
+                       (pj > 0 || kk > 0) ? 1u : 0u);
+        issued = true;
+        umma_commit(&set_free[pts]);
+        umma_commit(&kv_empty[ps]);
+      }
+      if (ok) umma_commit(acc_done);
+      if (!ok && issued) {
+        umma_commit(drain_acc);
+        mbar_drain(drain_acc, 0, err);
       }
     }
   } else {
@@ -1037,7 +1066,7 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     if (ctx->attn_split > 0 && G % ctx->attn_split == 0) nsplit = ctx->attn_split;
   }
   if (nsplit == 1) {
-    attn_bwd_dkdv_tc_kernel<HD><<<dim3(Hkv, B, n_kt), NT, DkdvLayout<HD>::BYTES, s>>>(
+    attn_bwd_dkdv_tc_kernel<HD><<<dim3(Hkv, B, n_kt), NT_BWD, DkdvLayout<HD>::BYTES, s>>>(
         tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, io.dk, io.dv, io.dk_ld, io.dv_ld, 1, S, H, Hkv, scale,
         scale * LOG2E, round_dv ? 1 : 0, ctx->d_err);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
@@ -1047,7 +1076,7 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     const int pw = Hkv * nsplit * HD;
     float* pk = partial;
     float* pv = partial + static_cast<size_t>(T) * pw;
-    attn_bwd_dkdv_tc_kernel<HD><<<dim3(Hkv * nsplit, B, n_kt), NT, DkdvLayout<HD>::BYTES, s>>>(
+    attn_bwd_dkdv_tc_kernel<HD><<<dim3(Hkv * nsplit, B, n_kt), NT_BWD, DkdvLayout<HD>::BYTES, s>>>(
         tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, pk, pv, pw, pw, nsplit, S, H, Hkv, scale, scale * LOG2E, 0,
         ctx->d_err);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
@@ -1058,7 +1087,7 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     GLC_LAUNCH_CHECK(ctx, "attention_bwd group sum");
   }
   const int n_qt = (S + 127) / 128;
-  attn_bwd_dq_tc_kernel<HD><<<dim3(H, B, n_qt), NT, DqLayout<HD>::BYTES, s>>>(
+  attn_bwd_dq_tc_kernel<HD><<<dim3(H, B, n_qt), NT_BWD, DqLayout<HD>::BYTES, s>>>(
       tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,
       rope_sin, ctx->d_err);
   GLC_LAUNCH_CHECK(ctx, "attention_bwd dq (tcgen05)");

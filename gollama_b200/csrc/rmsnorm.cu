@@ -148,36 +148,54 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
   }
 }
 
-// dw[j] (+)= sum over blocks b of partial[b][j].  One block per 32 columns:
-// warp w keeps four running sums, of rows w + 8 * (4i + c) for c = 0..3 (four
-// independent load chains), adds them in order c = 0..3, and warp 0 adds the
-// 8 warp sums in order (deterministic).
-__global__ void column_sum_kernel(const float* __restrict__ partial, int nblocks, int cols, float* __restrict__ out,
-                                  int accumulate) {
-  __shared__ float red[8][33];
+// dw[j] (+)= sum over blocks b of partial[b][j].  A cluster of CS_CL CTAs
+// per 32 columns: CTA rank r adds the partial rows of its quarter
+// [r*q, (r+1)*q), each of its 16 warps keeping four running sums (rows
+// w + 16*(4i + c), added in order c = 0..3), the warps' sums added in warp
+// order; rank 0 then adds the CS_CL quarter sums in rank order through
+// distributed shared memory (deterministic).
+constexpr int CS_CL = 4;
+constexpr int CS_WARPS = 16;
+__global__ void __cluster_dims__(CS_CL, 1, 1) __launch_bounds__(CS_WARPS * 32)
+    column_sum_kernel(const float* __restrict__ partial, int nblocks, int cols, float* __restrict__ out,
+                      int accumulate) {
+  __shared__ float red[CS_WARPS][33];
+  __shared__ float quarter[32];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int j = blockIdx.x * 32 + lane;
+  const int rank = static_cast<int>(cluster_ctarank());
+  const int j = static_cast<int>(blockIdx.x / CS_CL) * 32 + lane;
+  const int q = (nblocks + CS_CL - 1) / CS_CL;
+  const int b0 = rank * q, b1 = min(nblocks, b0 + q);
   float s = 0.f;
   if (j < cols) {
     float c4[4] = {0.f, 0.f, 0.f, 0.f};
-    int b = w;
-    for (; b + 24 < nblocks; b += 32) {
+    int b = b0 + w;
+    for (; b + 3 * CS_WARPS < b1; b += 4 * CS_WARPS) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) c4[c] += partial[static_cast<size_t>(b + 8 * c) * cols + j];
+      for (int c = 0; c < 4; ++c) c4[c] += partial[static_cast<size_t>(b + CS_WARPS * c) * cols + j];
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c)
-      if (b + 8 * c < nblocks) c4[c] += partial[static_cast<size_t>(b + 8 * c) * cols + j];
+      if (b + CS_WARPS * c < b1) c4[c] += partial[static_cast<size_t>(b + CS_WARPS * c) * cols + j];
     s = ((c4[0] + c4[1]) + c4[2]) + c4[3];
   }
   red[w][lane] = s;
   __syncthreads();
-  if (w == 0 && j < cols) {
+  if (w == 0) {
     float t = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) t += red[k][lane];
+    for (int k = 0; k < CS_WARPS; ++k) t += red[k][lane];
+    quarter[lane] = t;
+  }
+  cluster_sync_all();
+  if (rank == 0 && w == 0 && j < cols) {
+    float t = ld_shared_cluster_f32(mapa_cluster(&quarter[lane], 0));
+#pragma unroll
+    for (int r = 1; r < CS_CL; ++r) t += ld_shared_cluster_f32(mapa_cluster(&quarter[lane], r));
     out[j] = accumulate ? __fadd_rn(out[j], t) : t;
   }
+  // the peers' quarter sums stay in place until rank 0 has read them
+  cluster_sync_all();
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -241,7 +259,8 @@ int rmsnorm_bwd(Context* ctx, const float* x, const float* w, const float* rms, 
   else
     rmsnorm_bwd_kernel<8><<<nblocks, 256, 0, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
   GLC_LAUNCH_CHECK(ctx, "rmsnorm_bwd");
-  column_sum_kernel<<<(cols + 31) / 32, 256, 0, s>>>(partial, nblocks, cols, dw, dw_accumulate ? 1 : 0);
+  column_sum_kernel<<<((cols + 31) / 32) * CS_CL, CS_WARPS * 32, 0, s>>>(partial, nblocks, cols, dw,
+                                                                          dw_accumulate ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "rmsnorm_bwd column sum");
   return 0;
 }
