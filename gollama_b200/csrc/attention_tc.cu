@@ -39,13 +39,13 @@
 namespace glc {
 namespace {
 
-constexpr int NT = 320;
+// Warps: 0 TMA producer, 1 MMA issuer for the score products (S, and dP in
+// the backward), 2..9 math, 10 MMA issuer for the accumulating products
+// (O += P V; dV/dK; dQ).  One thread issues a tcgen05.mma about every 49
+// cycles at best, and an N = 64 TF32 MMA with A in TMEM needs 32 cycles of the
+// tensor core: two issuing threads keep it busy, one cannot.
+constexpr int NT = 352;
 constexpr int MATH_THREADS = 256;  // warps 2..9
-// Backward kernels: warp 10 issues the accumulating MMAs (dV/dK, dQ) while
-// warp 1 issues S and dP.  One thread issues a tcgen05.mma about every 49
-// cycles at best, and an N = 64 TF32 MMA with A in TMEM needs 32 cycles of
-// the tensor core: two issuing threads keep it busy, one cannot.
-constexpr int NT_BWD = 352;
 constexpr int ACC_WARP = 10;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
@@ -128,7 +128,8 @@ __global__ void __launch_bounds__(NT, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
   uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = bars + 3, *v_full = bars + 5, *v_empty = bars + 7,
            *s_full = bars + 9, *p_full = bars + 12, *pv_done = bars + 15, *drain = bars + 18, *xchg = bars + 19;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
+  uint64_t* drain_acc = bars + 21;  // abort path of the P V issuer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const Roles ro;
   // grid (H, B, query tiles): query tiles vary slowest and the longest rows
@@ -154,6 +155,7 @@ __global__ void __launch_bounds__(NT, 1)
     mbar_init(&xchg[0], MATH_THREADS);
     mbar_init(&xchg[1], MATH_THREADS);
     mbar_init(drain, 1);
+    mbar_init(drain_acc, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -193,15 +195,16 @@ __global__ void __launch_bounds__(NT, 1)
   } else if (ro.warp == 1) {
     if (ro.lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_tf32(128, 128, false, false);
-      constexpr uint32_t idesc_o = umma_idesc_tf32(128, HD, false, true);
       bool ok = mbar_wait(q_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
       bool issued = false;
       // S_j = Q K_j^T into buffer j % 3, whose previous P (tile j-3) must be consumed
-      auto issue_s = [&](int j) -> bool {
+      for (int j = 0; ok && j < n_kv; ++j) {
         const int sb = j % 3, st = j & 1;
-        if (j >= 3 && !mbar_wait(&pv_done[sb], ((j - 3) / 3) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM))
-          return false;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) return false;
+        if (j >= 3 && !mbar_wait(&pv_done[sb], ((j - 3) / 3) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk)
@@ -209,10 +212,18 @@ __global__ void __launch_bounds__(NT, 1)
         issued = true;
         umma_commit(&k_empty[st]);
         umma_commit(&s_full[sb]);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      if (ok && n_kv > 1) ok = issue_s(1);
+      }
+      if (!ok && issued) {
+        umma_commit(drain);
+        mbar_drain(drain, 0, err);
+      }
+    }
+  } else if (ro.warp == ACC_WARP) {
+    // O += P_j V_j once the softmax has written P_j; pv_done[j % 3] frees the
+    // S/P buffer for S_{j+3} and lets the softmax rescale O
+    if (ro.lane == 0) {
+      constexpr uint32_t idesc_o = umma_idesc_tf32(128, HD, false, true);
+      bool ok = true, issued = false;
       for (int j = 0; ok && j < n_kv; ++j) {
         const int sb = j % 3, st = j & 1;
         if (!mbar_wait(&p_full[sb], (j / 3) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
@@ -222,13 +233,13 @@ __global__ void __launch_bounds__(NT, 1)
         for (int kk = 0; kk < 16; ++kk)
           umma_tf32_ts(tmem + L::O_COL, tmem + sb * 128 + kk * 8, mdesc<128>(sV + st * L::V, kk), idesc_o,
                        (j > 0 || kk > 0) ? 1u : 0u);
+        issued = true;
         umma_commit(&v_empty[st]);
         umma_commit(&pv_done[sb]);
-        if (j + 2 < n_kv && !issue_s(j + 2)) { ok = false; break; }
       }
       if (!ok && issued) {
-        umma_commit(drain);
-        mbar_drain(drain, 0, err);
+        umma_commit(drain_acc);
+        mbar_drain(drain_acc, 0, err);
       }
     }
   } else {
@@ -416,7 +427,7 @@ __device__ __forceinline__ void tile_rows_to_tmem(const uint8_t* tile, int row, 
 // tile 0 meets every query) are dispatched first.  nsplit == 1 writes the
 // final dk/dv; otherwise partial [T][Hkv * nsplit][hd] for the group sum.
 template <int HD>
-__global__ void __launch_bounds__(NT_BWD, 1)
+__global__ void __launch_bounds__(NT, 1)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQk, const __grid_constant__ CUtensorMap tmQm,
                             const __grid_constant__ CUtensorMap tmOk, const __grid_constant__ CUtensorMap tmOm,
                             const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -733,7 +744,7 @@ struct DqLayout {
 };
 
 template <int HD>
-__global__ void __launch_bounds__(NT_BWD, 1)
+__global__ void __launch_bounds__(NT, 1)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmO,
                           const __grid_constant__ CUtensorMap tmKk, const __grid_constant__ CUtensorMap tmKm,
                           const __grid_constant__ CUtensorMap tmVk, const float* __restrict__ lse,
@@ -1066,7 +1077,7 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     if (ctx->attn_split > 0 && G % ctx->attn_split == 0) nsplit = ctx->attn_split;
   }
   if (nsplit == 1) {
-    attn_bwd_dkdv_tc_kernel<HD><<<dim3(Hkv, B, n_kt), NT_BWD, DkdvLayout<HD>::BYTES, s>>>(
+    attn_bwd_dkdv_tc_kernel<HD><<<dim3(Hkv, B, n_kt), NT, DkdvLayout<HD>::BYTES, s>>>(
         tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, io.dk, io.dv, io.dk_ld, io.dv_ld, 1, S, H, Hkv, scale,
         scale * LOG2E, round_dv ? 1 : 0, ctx->d_err);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
@@ -1076,7 +1087,7 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     const int pw = Hkv * nsplit * HD;
     float* pk = partial;
     float* pv = partial + static_cast<size_t>(T) * pw;
-    attn_bwd_dkdv_tc_kernel<HD><<<dim3(Hkv * nsplit, B, n_kt), NT_BWD, DkdvLayout<HD>::BYTES, s>>>(
+    attn_bwd_dkdv_tc_kernel<HD><<<dim3(Hkv * nsplit, B, n_kt), NT, DkdvLayout<HD>::BYTES, s>>>(
         tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, pk, pv, pw, pw, nsplit, S, H, Hkv, scale, scale * LOG2E, 0,
         ctx->d_err);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
@@ -1087,7 +1098,7 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     GLC_LAUNCH_CHECK(ctx, "attention_bwd group sum");
   }
   const int n_qt = (S + 127) / 128;
-  attn_bwd_dq_tc_kernel<HD><<<dim3(H, B, n_qt), NT_BWD, DqLayout<HD>::BYTES, s>>>(
+  attn_bwd_dq_tc_kernel<HD><<<dim3(H, B, n_qt), NT, DqLayout<HD>::BYTES, s>>>(
       tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,
       rope_sin, ctx->d_err);
   GLC_LAUNCH_CHECK(ctx, "attention_bwd dq (tcgen05)");
