@@ -2,6 +2,7 @@
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 import numpy as np
 
@@ -27,6 +28,13 @@ class Context:
             raise GlcError(rc, "glc_init", f"cannot open device {device} (sm_100a required)")
         self.h = h
         self.device = device
+        # objects holding resources of this context, closed before it (order:
+        # trainers, then models); weak, so they may also go first on their own
+        self._owned: list[tuple[int, weakref.ref]] = []
+
+    def adopt(self, obj, order: int) -> None:
+        """Close obj (obj.close()) before this context is destroyed, lower order first."""
+        self._owned.append((order, weakref.ref(obj)))
 
     def check(self, rc: int, where: str) -> None:
         if rc != 0:
@@ -52,6 +60,12 @@ class Context:
 
     def close(self) -> None:
         if getattr(self, "h", None):
+            # the library's models and trainers refer to the context: they go first
+            for _, ref in sorted(getattr(self, "_owned", []), key=lambda e: e[0]):
+                obj = ref()
+                if obj is not None:
+                    obj.close()
+            self._owned = []
             self.lib.glc_destroy(self.h)
             self.h = None
 

@@ -100,6 +100,7 @@ class TrainableModel:
         h = C.c_void_p()
         self.ctx.check(self.ctx.lib.glc_model_create(self.ctx.h, C.byref(self._c), C.byref(h)), "glc_model_create")
         self.h = h
+        self.ctx.adopt(self, 1)
         n, tot = C.c_int(), C.c_int64()
         self.ctx.check(self.ctx.lib.glc_model_num_params(self.h, C.byref(n), C.byref(tot)), "glc_model_num_params")
         self.num_params = n.value
@@ -144,9 +145,10 @@ class TrainableModel:
         return m, v
 
     def close(self) -> None:
-        if getattr(self, "h", None):
+        # a model whose context is already gone was closed with it
+        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
             self.ctx.lib.glc_model_destroy(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:
@@ -169,6 +171,7 @@ class Trainer:
         h = C.c_void_p()
         self.ctx.check(self.ctx.lib.glc_trainer_create(model.h, C.byref(h)), "glc_trainer_create")
         self.h = h
+        self.ctx.adopt(self, 0)
 
     def TrainStep(self, inputs, targets) -> float:
         inp = np.ascontiguousarray(inputs, np.int64)
@@ -196,9 +199,9 @@ class Trainer:
         return n.value
 
     def close(self) -> None:
-        if getattr(self, "h", None):
+        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
             self.ctx.lib.glc_trainer_destroy(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:

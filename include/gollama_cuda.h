@@ -49,7 +49,8 @@ typedef struct glc_ctx glc_ctx;
  * cuTensorMapEncodeTiled.  Fails with GLC_ERR_UNSUPPORTED on anything but an
  * sm_100 device. */
 GLC_API int glc_init(int device, glc_ctx** out);
-/* Replaces metal.Cleanup (pkg/metal/metal.go:193-196). */
+/* Replaces metal.Cleanup (pkg/metal/metal.go:193-196).  Trainers and models
+ * created on the context must be destroyed before it (they use its stream). */
 GLC_API int glc_destroy(glc_ctx* ctx);
 /* Copies the last error message (NUL-terminated, truncated to n). */
 GLC_API int glc_last_error(glc_ctx* ctx, char* buf, size_t n);
@@ -299,6 +300,7 @@ GLC_API int glc_default_train_config(glc_train_config* cfg);
  * arena in Params() order; matrices N(0, init_std) from `seed` (the Go
  * math/rand Xavier init is not reproducible without Go), RMSNorm weights 1. */
 GLC_API int glc_model_create(glc_ctx* ctx, const glc_train_config* cfg, glc_model** out);
+/* Before its context, and after every trainer created on it. */
 GLC_API int glc_model_destroy(glc_model* m);
 /* Params() (trainer.go:429-431): count, and per parameter its offset/shape in
  * the flat arena and whether it currently has a gradient (Grad != nil). */
@@ -308,11 +310,15 @@ GLC_API int glc_model_param_info(glc_model* m, int idx, int64_t* offset, int64_t
 /* Host <-> device copies of the whole arena (parameters, gradients, AdamW m/v). */
 GLC_API int glc_model_set_params(glc_model* m, const float* host, int64_t n);
 GLC_API int glc_model_get_params(glc_model* m, float* host, int64_t n);
+/* After a TrainStep the gradients are returned as GradientClipping leaves them
+ * (scaled by the clip factor); the step itself keeps them unscaled on the
+ * device and applies the factor here, in place, on the first read. */
 GLC_API int glc_model_get_grads(glc_model* m, float* host, int64_t n);
 GLC_API int glc_model_get_moments(glc_model* m, float* m_host, float* v_host, int64_t n);
 /* NewTrainer (trainer.go:447-459): AdamW with the configured hyper-parameters
  * and the warmup + cosine LRScheduler. */
 GLC_API int glc_trainer_create(glc_model* m, glc_trainer** out);
+/* Before its model and context. */
 GLC_API int glc_trainer_destroy(glc_trainer* t);
 /* Trainer.TrainStep (trainer.go:462-505): LR, ZeroGrad, forward, loss,
  * backward, (data-parallel gradient allreduce), gradient clipping, AdamW.

@@ -121,3 +121,18 @@ def test_second_step_norm_grads_weights(ctx, shape):
         if p.has_grad:
             assert rel_fro(grads[seg], st.grads[seg]) < GRAD_RFRO, p.index
         assert rel_fro(weights[seg], st.params[seg]) < WEIGHT_RFRO, p.index
+
+
+def test_context_closes_its_models_and_trainers():
+    """Models and trainers use their context's stream: closing the context
+    closes them first (trainers, then models), and a later close is a no-op."""
+    from gollama_b200.device import Context
+
+    with Context(0) as c:
+        model = NewTrainableModel(config_for(syn.TINY, **STEP_HPARAMS), c)
+        model.set_params(syn.init_params(syn.TINY, 3))
+        tr = NewTrainer(model)
+        tr.TrainStep(*syn.batch(syn.TINY, 3))
+    assert tr.h is None and model.h is None
+    tr.close()
+    model.close()
