@@ -282,6 +282,12 @@ int glc_set_gemm_variant(glc_ctx* ctx, int variant) {
   return GLC_OK;
 }
 
+int glc_set_fused_swiglu(glc_ctx* ctx, int on) {
+  if (!ctx) return GLC_ERR_INVALID;
+  C_(ctx)->fuse_swiglu = on != 0;
+  return GLC_OK;
+}
+
 int glc_set_attention_split(glc_ctx* ctx, int nsplit) {
   if (!ctx) return GLC_ERR_INVALID;
   Context* c = C_(ctx);

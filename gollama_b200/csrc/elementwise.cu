@@ -12,16 +12,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 // ---------------------------------------------------------------- SwiGLU
 // Forward of forwardFFN's SiLU and product nodes (trainer.go:397-407 with
 // SiLUGrad, grad.go:424-428): s = 1/(1+exp32(-g)), h = (g*s)*u.
-// FAST: llama semantics, sigmoid with the hardware-assisted expf instead of
-// the reference's float64 exp32 (the decoder's tolerance allows it).
-template <bool FAST>
-__device__ __forceinline__ float sigmoid_f(float g) {
-  return FAST ? __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))) : go_sigmoid(g);
-}
-template <bool FAST>
-__device__ __forceinline__ float swiglu_f(float g, float u) {
-  return FAST ? __fmul_rn(__fmul_rn(g, sigmoid_f<true>(g)), u) : go_swiglu(g, u);
-}
+// FAST: llama semantics (sigmoid_f / swiglu_f in go_math.cuh).
 
 // 2-D launch: blockIdx.x/threadIdx.x pick a float4 column, blockIdx.y strides
 // over rows (32-bit index arithmetic, no per-element division).

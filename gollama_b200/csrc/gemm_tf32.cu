@@ -80,6 +80,7 @@ struct Problem {
   float* h;
   int ldh;
   int round_h;
+  int glu_fast;    // h with expf (Llama semantics) instead of the reference's exp32
   int m_tiles, n_tiles, k_blocks, tiles;
   // Tile order.  Concurrent tiles share the operand of the slow-moving index
   // through L2 and stream the other; the operand of the fast-moving index is
@@ -606,8 +607,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
                                             __uint_as_float(g[4 * j + 2]), __uint_as_float(g[4 * j + 3]));
               const float4 uv = make_float4(__uint_as_float(u[4 * j]), __uint_as_float(u[4 * j + 1]),
                                             __uint_as_float(u[4 * j + 2]), __uint_as_float(u[4 * j + 3]));
-              float4 hv = make_float4(go_swiglu(gv.x, uv.x), go_swiglu(gv.y, uv.y), go_swiglu(gv.z, uv.z),
-                                      go_swiglu(gv.w, uv.w));
+              float4 hv = p.glu_fast ? make_float4(swiglu_f<true>(gv.x, uv.x), swiglu_f<true>(gv.y, uv.y),
+                                                   swiglu_f<true>(gv.z, uv.z), swiglu_f<true>(gv.w, uv.w))
+                                     : make_float4(go_swiglu(gv.x, uv.x), go_swiglu(gv.y, uv.y),
+                                                   go_swiglu(gv.z, uv.z), go_swiglu(gv.w, uv.w));
               if (p.round_h) hv = make_float4(round_tf32(hv.x), round_tf32(hv.y), round_tf32(hv.z), round_tf32(hv.w));
               reinterpret_cast<float4*>(grow)[j] = gv;
               reinterpret_cast<float4*>(urow)[j] = uv;
@@ -619,7 +622,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
             for (int j = 0; j < 32; ++j) {
               if (j < lim) {
                 const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
-                float hv = go_swiglu(gv, uv);
+                float hv = p.glu_fast ? swiglu_f<true>(gv, uv) : go_swiglu(gv, uv);
                 if (p.round_h) hv = round_tf32(hv);
                 grow[j] = gv;
                 urow[j] = uv;
@@ -763,6 +766,7 @@ int prepare(Context* ctx, const GemmSpec& g, Problem* p, CUtensorMap* ta, CUtens
   p->h = g.glu_h;
   p->ldh = g.ld_glu;
   p->round_h = g.glu_round ? 1 : 0;
+  p->glu_fast = g.glu_fast ? 1 : 0;
   if (g.glu) p->n_tiles = (g.glu + 127) / 128;
   p->tiles = p->m_tiles * p->n_tiles;
   return 0;
@@ -870,7 +874,7 @@ int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t str
       const GemmSpec& g = live[i];
       if (g.glu)
         rc = swiglu_fwd(ctx, g.C, g.C + g.glu, static_cast<size_t>(g.ldc), g.glu_h, static_cast<size_t>(g.ld_glu),
-                        static_cast<size_t>(g.M), static_cast<size_t>(g.glu), g.glu_round, stream);
+                        static_cast<size_t>(g.M), static_cast<size_t>(g.glu), g.glu_round, stream, g.glu_fast);
     }
     return rc;
   }

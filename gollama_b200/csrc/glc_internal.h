@@ -30,6 +30,7 @@ struct Context {
   // device tile lists of grouped CTA-pair GEMM launches, by (tiles and
   // k-blocks of each problem, clusters); built once per shape
   std::vector<std::pair<std::array<long long, 5>, int*>> gemm_sched;
+  bool fuse_swiglu = false;            // trainer: SwiGLU forward in the gate/up GEMM epilogue (Llama semantics)
   int attn_split = 0;                  // dK/dV CTAs per KV head: 0 automatic, else a divisor of the group
   EncodeTiledFn encode_fn = nullptr;
   // scratch workspace owned by the context (grown on demand, never shrunk)
@@ -143,6 +144,7 @@ struct GemmSpec {
   float* glu_h = nullptr;
   int ld_glu = 0;
   bool glu_round = false;
+  bool glu_fast = false;  // Llama semantics: expf in the sigmoid
 };
 // Runs up to two independent GEMMs in one persistent launch (shared tile queue).
 int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t stream);

@@ -111,4 +111,17 @@ __device__ __forceinline__ float go_swiglu(float g, float u) {
   return __fmul_rn(__fmul_rn(g, s), u);
 }
 
+// FAST: Llama semantics, the sigmoid with float expf instead of the
+// reference's float64 exp32 (the decoder package takes math.Exp); the same
+// float32 operation order otherwise.  Shared by the SwiGLU kernels and the
+// GEMM's SwiGLU epilogue, which must agree bit for bit.
+template <bool FAST>
+__device__ __forceinline__ float sigmoid_f(float g) {
+  return FAST ? __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))) : go_sigmoid(g);
+}
+template <bool FAST>
+__device__ __forceinline__ float swiglu_f(float g, float u) {
+  return FAST ? __fmul_rn(__fmul_rn(g, sigmoid_f<true>(g)), u) : go_swiglu(g, u);
+}
+
 }  // namespace glc

@@ -351,6 +351,7 @@ struct Model {
       fwd.glu_h = swiglu_h;
       fwd.ld_glu = N / 2;
       fwd.glu_round = true;
+      fwd.glu_fast = llama;
     }
     ck(gemm_tf32_group(ctx, &fwd, 1, tp.stream()));
     if (round_out) out->gemm_data = out->data;
@@ -523,11 +524,19 @@ struct Model {
       Node* att = attention(tp, qkv, B, S);
       Node* x1 = matmul(tp, att, P(lp(l, P_WO)), x, false, true);
       Node* n2 = rmsnorm(tp, x1, P(lp(l, P_FFN_NORM)));
-      // forwardFFN (trainer.go:392-426): gate and up projections as one GEMM over WGate|WUp
-      // the SwiGLU epilogue (matmul's swiglu_h) runs the float64 exp32 inside
-      // the GEMM and is slower than the two launches at these sizes
-      Node* gu = matmul(tp, n2, &gu_view[l], nullptr);
-      Node* h = swiglu(tp, gu);
+      // forwardFFN (trainer.go:392-426): gate and up projections as one GEMM over
+      // WGate|WUp.  On request (Llama semantics) its epilogue also writes
+      // h = silu(g)*u; by default the SwiGLU kernel runs after the GEMM, which
+      // is faster: the epilogue warps become the GEMM's bottleneck.
+      Node* h = nullptr;
+      if (llama && ctx->fuse_swiglu) {
+        Node* hn = tp.make(n2->rows, cfg.intermediate_size);
+        Node* gu = matmul(tp, n2, &gu_view[l], nullptr, false, false, hn->data);
+        h = swiglu(tp, gu, hn);
+      } else {
+        Node* gu = matmul(tp, n2, &gu_view[l], nullptr);
+        h = swiglu(tp, gu);
+      }
       x = matmul(tp, h, P(lp(l, P_WDOWN)), x1);
     }
     Node* hf = rmsnorm(tp, x, P(out_norm()));

@@ -167,6 +167,11 @@ GLC_API int glc_set_gemm_variant(glc_ctx* ctx, int variant);
  * Each CTA accumulates its heads in TMEM; more than one writes partials that a
  * deterministic group sum adds.  Results agree to fp32 rounding across splits. */
 GLC_API int glc_set_attention_split(glc_ctx* ctx, int nsplit);
+/* Trainer (Llama semantics): 1 computes the SwiGLU forward in the gate/up
+ * GEMM's epilogue, 0 (default, faster on B200 at the TinyLlama shape) runs it
+ * as its own kernel after the GEMM (diagnostics; no reference counterpart).
+ * Results are bit-identical. */
+GLC_API int glc_set_fused_swiglu(glc_ctx* ctx, int on);
 
 /* ------------------------------------------------------------------ fused / elementwise ops
  * Building blocks of the tape's GradFns; each mirrors one reference node.

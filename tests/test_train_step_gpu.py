@@ -136,3 +136,26 @@ def test_context_closes_its_models_and_trainers():
     assert tr.h is None and model.h is None
     tr.close()
     model.close()
+
+
+@pytest.mark.parametrize("shape", [syn.TINY_LLAMA_MODE, syn.SMALL_LLAMA_MODE.with_(layers=2)], ids=lambda s: s.name)
+def test_fused_swiglu_epilogue_bit_identical(ctx, shape):
+    """With Llama semantics the SwiGLU forward may run in the gate/up GEMM's
+    epilogue; the step is bit-identical to the default separate kernel."""
+    params = syn.init_params(shape, 21)
+    inputs, targets = syn.batch(shape, 21)
+    out = []
+    try:
+        for fused in (1, 0):
+            ctx.call("glc_set_fused_swiglu", fused)
+            model = NewTrainableModel(config_for(shape, **STEP_HPARAMS), ctx)
+            model.set_params(params)
+            loss = NewTrainer(model).TrainStep(inputs, targets)
+            out.append((loss, model.get_grads(), model.get_params()))
+            model.close()
+    finally:
+        ctx.call("glc_set_fused_swiglu", 0)
+    (l1, g1, w1), (l0, g0, w0) = out
+    assert l1 == l0
+    assert np.array_equal(g1.view(np.uint32), g0.view(np.uint32))
+    assert np.array_equal(w1.view(np.uint32), w0.view(np.uint32))
