@@ -967,20 +967,26 @@ __global__ void __launch_bounds__(NT, 1)
   }
 }
 
-// D[b,h,s] = sum_d dO * O
+// D[b,h,s] = sum_d dO * O.  HD/4 lanes per (token, head) row, one float4 of
+// each operand per lane, 32/(HD/4) rows per warp, one row group per warp.
+template <int HD>
 __global__ void attn_bwd_prep_tc_kernel(const float* __restrict__ o, const float* __restrict__ dO,
-                                        float* __restrict__ D, int T, int S, int H, int hd) {
-  const int lane = threadIdx.x & 31;
+                                        float* __restrict__ D, int T, int S, int H) {
+  constexpr int LPR = HD / 4, RPW = 32 / LPR;
+  const int lane = threadIdx.x & 31, sub = lane / LPR, li = lane % LPR;
   const int nrow = T * H;
-  for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < nrow; row += gridDim.x * (blockDim.x >> 5)) {
-    const int t = row / H, h = row % H;
-    const float* op = o + (static_cast<size_t>(t) * H + h) * hd;
-    const float* dp = dO + (static_cast<size_t>(t) * H + h) * hd;
-    float s = 0.f;
-    for (int d = lane; d < hd; d += 32) s += op[d] * dp[d];
+  const int row = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW + sub;
+  float s = 0.f;
+  if (row < nrow) {
+    const float4 a = reinterpret_cast<const float4*>(o + static_cast<size_t>(row) * HD)[li];
+    const float4 b = reinterpret_cast<const float4*>(dO + static_cast<size_t>(row) * HD)[li];
+    s = (a.x * b.x + a.y * b.y) + (a.z * b.z + a.w * b.w);
+  }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    if (lane == 0) D[(static_cast<size_t>(t / S) * H + h) * S + (t % S)] = s;
+  for (int off = LPR / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (li == 0 && row < nrow) {
+    const int t = row / H, h = row - t * H;
+    D[(static_cast<size_t>(t / S) * H + h) * S + (t % S)] = s;
   }
 }
 
@@ -1059,7 +1065,11 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
   const double causal = 0.5 * static_cast<double>(S) * (S + 1);
   ProfScope prof(ctx, PROF_ATTN_BWD, 4.0 * 2.0 * B * H * causal * HD, s);
-  attn_bwd_prep_tc_kernel<<<grid_for(static_cast<size_t>(T) * H, 8, ctx->num_sms, 16), 256, 0, s>>>(o, dO, D, T, S, H, HD);
+  {
+    const long long nrow = static_cast<long long>(T) * H;
+    const long long warps = (nrow + (32 / (HD / 4)) - 1) / (32 / (HD / 4));
+    attn_bwd_prep_tc_kernel<HD><<<static_cast<unsigned>((warps + 7) / 8), 256, 0, s>>>(o, dO, D, T, S, H);
+  }
   GLC_LAUNCH_CHECK(ctx, "attention_bwd prep");
   const int n_kt = (S + 127) / 128;
   // CTAs per KV head: the fewest that still give 1.5 waves (each CTA loads
@@ -1129,7 +1139,8 @@ int attention_bwd(Context* ctx, const AttnIO& io, const float* o, const float* l
   int rc = check(ctx, io.q, io.k, io.v, B, S, H, Hkv, hd);
   if (rc) return rc;
   if (!o || !lse || !dO || !io.dq || !io.dk || !io.dv || !D ||
-      ((reinterpret_cast<uintptr_t>(dO) | reinterpret_cast<uintptr_t>(io.dq) | reinterpret_cast<uintptr_t>(io.dk) |
+      ((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(dO) | reinterpret_cast<uintptr_t>(io.dq) |
+        reinterpret_cast<uintptr_t>(io.dk) |
         reinterpret_cast<uintptr_t>(io.dv)) & 15))
     return ctx->fail(GLC_ERR_INVALID, "attention_bwd: null or misaligned pointer");
   if (((io.q_ld | io.k_ld | io.v_ld | io.dq_ld | io.dk_ld | io.dv_ld) & 3) || io.q_ld < H * hd || io.dq_ld < H * hd ||
