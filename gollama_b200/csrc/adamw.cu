@@ -72,6 +72,26 @@ __global__ void norm_finish_kernel(const double* __restrict__ partial, int n, fl
   }
 }
 
+// First level of the finishing sum when the partials are many: block b adds
+// partial[b*chunk, min(n, (b+1)*chunk)) in a fixed order into out[b].
+__global__ void slot_sum_kernel(const double* __restrict__ partial, long long n, long long chunk,
+                                double* __restrict__ out) {
+  __shared__ double red[32];
+  const long long b0 = static_cast<long long>(blockIdx.x) * chunk;
+  const long long b1 = min(n, b0 + chunk);
+  double acc = 0.0;
+  for (long long i = b0 + threadIdx.x; i < b1; i += blockDim.x) acc += partial[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < (blockDim.x >> 5); ++w) t += red[w];
+    out[blockIdx.x] = t;
+  }
+}
+
 struct AdamArgs {
   float lr, b1, omb1, b2, omb2, wd;
   double bc1, bc2, rbc1, rbc2, eps;
@@ -139,12 +159,46 @@ __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float
 
 // segs: device array of {start, len} pairs (int64), nseg entries; every start
 // and len a multiple of 4.
+int grad_norm_blocks(const Context* ctx, int nseg) {
+  if (nseg <= 0) return 0;
+  const int bx = (8 * ctx->num_sms + nseg - 1) / nseg;
+  return bx < 4 ? 4 : bx;
+}
+
+int grad_sumsq(Context* ctx, const float* grads, const int64_t* segs, int nseg, int bx, double* partial, double elems,
+               cudaStream_t s) {
+  if (nseg <= 0) return 0;
+  if (!grads || !segs || !partial || bx <= 0) return ctx->fail(GLC_ERR_INVALID, "grad_sumsq: bad arguments");
+  ProfScope prof(ctx, PROF_ADAMW, 4.0 * elems, s);
+  sumsq_kernel<<<dim3(bx, nseg), 256, 0, s>>>(grads, reinterpret_cast<const Seg*>(segs), partial);
+  GLC_LAUNCH_CHECK(ctx, "grad_norm partial");
+  return 0;
+}
+
+int grad_norm_finish(Context* ctx, const double* partial, long long n, float max_norm, double* norm_out,
+                     float* scale_out, cudaStream_t s, double* lvl, long long lvl_cap) {
+  if (n <= 0 || n > 0x7fffffffLL || !partial || !norm_out || !scale_out)
+    return ctx->fail(GLC_ERR_INVALID, "grad_norm_finish: bad arguments");
+  ProfScope prof(ctx, PROF_ADAMW, 8.0 * static_cast<double>(n), s);
+  const long long chunk = 1024;
+  const long long nb = (n + chunk - 1) / chunk;
+  if (n > 8192 && lvl && lvl_cap >= nb) {
+    // many partials (the GEMM epilogues' slots): blocks of 1024 first
+    slot_sum_kernel<<<static_cast<unsigned>(nb), 256, 0, s>>>(partial, n, chunk, lvl);
+    GLC_LAUNCH_CHECK(ctx, "grad_norm slot sum");
+    partial = lvl;
+    n = nb;
+  }
+  norm_finish_kernel<<<1, 256, 0, s>>>(partial, static_cast<int>(n), max_norm, norm_out, scale_out);
+  GLC_LAUNCH_CHECK(ctx, "grad_norm finish");
+  return 0;
+}
+
 int grad_norm(Context* ctx, const float* grads, const int64_t* segs, int nseg, float max_norm, double* norm_out,
               float* scale_out, double* scratch, int scratch_count, double elems, cudaStream_t s) {
   if (nseg <= 0 || !grads || !segs || !norm_out || !scale_out)
     return ctx->fail(GLC_ERR_INVALID, "grad_norm: bad arguments");
-  int bx = (8 * ctx->num_sms + nseg - 1) / nseg;
-  if (bx < 4) bx = 4;
+  const int bx = grad_norm_blocks(ctx, nseg);
   const int n = bx * nseg;
   double* partial = scratch;
   if (!partial) {
@@ -155,12 +209,9 @@ int grad_norm(Context* ctx, const float* grads, const int64_t* segs, int nseg, f
   } else if (scratch_count < n) {
     return ctx->fail(GLC_ERR_INVALID, "grad_norm: scratch buffer too small");
   }
-  ProfScope prof(ctx, PROF_ADAMW, 4.0 * elems, s);
-  sumsq_kernel<<<dim3(bx, nseg), 256, 0, s>>>(grads, reinterpret_cast<const Seg*>(segs), partial);
-  GLC_LAUNCH_CHECK(ctx, "grad_norm partial");
-  norm_finish_kernel<<<1, 256, 0, s>>>(partial, n, max_norm, norm_out, scale_out);
-  GLC_LAUNCH_CHECK(ctx, "grad_norm finish");
-  return 0;
+  int rc = grad_sumsq(ctx, grads, segs, nseg, bx, partial, elems, s);
+  if (!rc) rc = grad_norm_finish(ctx, partial, n, max_norm, norm_out, scale_out, s, nullptr, 0);
+  return rc;
 }
 
 int adamw(Context* ctx, float* p, float* g, float* m, float* v, float* shadow, const int64_t* segs, int nseg,

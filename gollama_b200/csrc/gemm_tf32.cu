@@ -70,6 +70,10 @@ struct Problem {
   int ldc, ldr;
   int accumulate;  // C += acc
   int round_out;   // round stored values to TF32 (RN)
+  // Sum of squares of the stored values (a gradient's share of the clip
+  // norm): each epilogue warp writes its float64 sum of a tile to
+  // sumsq[tile * slots_per_tile + warp slot]; nullptr: none.
+  double* sumsq;
   int a_mn, b_mn;  // operand majors
   int a_3d, b_3d;  // MN-major operand described as [MN/32 chunks][K][32]: one TMA per k-block
   // SwiGLU epilogue (CTA-pair kernel only): glu = F; a tile covers 128 h
@@ -319,6 +323,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int row = t.m0 + row_in_tile;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      double sq = 0.0;
 #pragma unroll 1
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
         uint32_t r[32];
@@ -349,6 +354,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (p.round_out) {
               v.x = round_tf32(v.x); v.y = round_tf32(v.y); v.z = round_tf32(v.z); v.w = round_tf32(v.w);
             }
+            if (p.sumsq) {
+              sq = fma(static_cast<double>(v.x), static_cast<double>(v.x), sq);
+              sq = fma(static_cast<double>(v.y), static_cast<double>(v.y), sq);
+              sq = fma(static_cast<double>(v.z), static_cast<double>(v.z), sq);
+              sq = fma(static_cast<double>(v.w), static_cast<double>(v.w), sq);
+            }
             reinterpret_cast<float4*>(crow)[j] = v;
           }
         } else {
@@ -360,10 +371,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               if (p.accumulate) v += crow[j];
               if (rrow) v += rrow[j];
               if (p.round_out) v = round_tf32(v);
+              if (p.sumsq) sq = fma(static_cast<double>(v), static_cast<double>(v), sq);
               crow[j] = v;
             }
           }
         }
+      }
+      if (p.sumsq) {
+        // 4 epilogue warps per 128x256 tile, slot = warp - 2
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        const int tid = (t.m0 / BM) * p.n_tiles + t.n0 / BN;
+        if (lane == 0) p.sumsq[tid * 4 + (warp - 2)] = sq;
       }
     }
   }
@@ -633,6 +652,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
         }
         continue;
       }
+      double sq = 0.0;
 #pragma unroll 1
       for (int chunk = ch * (BN / 32 / P_SPLIT); chunk < (ch + 1) * (BN / 32 / P_SPLIT); ++chunk) {
         uint32_t r[32];
@@ -664,6 +684,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
             if (p.round_out) {
               v.x = round_tf32(v.x); v.y = round_tf32(v.y); v.z = round_tf32(v.z); v.w = round_tf32(v.w);
             }
+            if (p.sumsq) {
+              sq = fma(static_cast<double>(v.x), static_cast<double>(v.x), sq);
+              sq = fma(static_cast<double>(v.y), static_cast<double>(v.y), sq);
+              sq = fma(static_cast<double>(v.z), static_cast<double>(v.z), sq);
+              sq = fma(static_cast<double>(v.w), static_cast<double>(v.w), sq);
+            }
             reinterpret_cast<float4*>(crow)[j] = v;
           }
         } else {
@@ -675,10 +701,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
               if (p.accumulate) v += crow[j];
               if (rrow) v += rrow[j];
               if (p.round_out) v = round_tf32(v);
+              if (p.sumsq) sq = fma(static_cast<double>(v), static_cast<double>(v), sq);
               crow[j] = v;
             }
           }
         }
+      }
+      if (p.sumsq) {
+        // 2 * P_EPI_WARPS epilogue warps per 256x256 tile, slot = rank * P_EPI_WARPS + warp - 2
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        const int tid = (t.m0 / PAIR_BM) * p.n_tiles + t.n0 / BN;
+        if (lane == 0) p.sumsq[tid * (2 * P_EPI_WARPS) + static_cast<int>(rank) * P_EPI_WARPS + (warp - 2)] = sq;
       }
     }
   }
@@ -755,6 +789,7 @@ int prepare(Context* ctx, const GemmSpec& g, Problem* p, CUtensorMap* ta, CUtens
   p->ldr = g.ldr;
   p->accumulate = g.accumulate ? 1 : 0;
   p->round_out = g.round_out ? 1 : 0;
+  p->sumsq = g.sumsq;
   p->a_mn = g.A.mn_major ? 1 : 0;
   p->b_mn = g.B.mn_major ? 1 : 0;
   p->m_tiles = (g.M + tile_m - 1) / tile_m;
@@ -769,6 +804,11 @@ int prepare(Context* ctx, const GemmSpec& g, Problem* p, CUtensorMap* ta, CUtens
   p->glu_fast = g.glu_fast ? 1 : 0;
   if (g.glu) p->n_tiles = (g.glu + 127) / 128;
   p->tiles = p->m_tiles * p->n_tiles;
+  if (g.sumsq) {
+    const long long per_tile = tile_m == PAIR_BM ? 2 * P_EPI_WARPS : 4;
+    if (g.glu || static_cast<long long>(p->tiles) * per_tile > g.sumsq_cap)
+      return ctx->fail(GLC_ERR_INVALID, "gemm: sum-of-squares slots too few, or with the SwiGLU epilogue");
+  }
   return 0;
 }
 
@@ -827,6 +867,11 @@ const int* pair_schedule(Context* ctx, const GroupArgs& a, int clusters) {
 }
 
 }  // namespace
+
+long long gemm_sumsq_slots(long long M, long long N) {
+  static_assert(2 * P_EPI_WARPS <= 8, "pair tiles: at most 8 slots per 256-row tile");
+  return ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * 8;
+}
 
 int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t stream) {
   if (n < 1 || n > 2) return ctx->fail(GLC_ERR_INVALID, "gemm: 1 or 2 problems per launch");

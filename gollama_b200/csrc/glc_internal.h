@@ -145,7 +145,15 @@ struct GemmSpec {
   int ld_glu = 0;
   bool glu_round = false;
   bool glu_fast = false;  // Llama semantics: expf in the sigmoid
+  // Sum of squares of the stored C (float64 partials, one per epilogue warp
+  // and tile, at most gemm_sumsq_slots(M, N) of them, added in any fixed
+  // order by the caller); nullptr: none.  Not with the SwiGLU epilogue.
+  double* sumsq = nullptr;
+  long long sumsq_cap = 0;
 };
+// Upper bound of the partial slots a GEMM with sumsq writes (either tile
+// shape): ceil(M/128) * ceil(N/256) * 8.
+long long gemm_sumsq_slots(long long M, long long N);
 // Runs up to two independent GEMMs in one persistent launch (shared tile queue).
 int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t stream);
 int gemm_empty_k(Context* ctx, float* C, int ldc, int M, int N, bool accumulate, const float* R, int ldr,
@@ -213,6 +221,17 @@ size_t attention_bwd_partial_floats(int B, int S, int H, int Hkv, int hd);
 // elems: number of gradient elements the segments cover (for the profiler).
 int grad_norm(Context* ctx, const float* grads, const int64_t* segs, int nseg, float max_norm, double* norm_out,
               float* scale_out, double* scratch, int scratch_count, double elems, cudaStream_t s);
+// The two halves of grad_norm: grad_sumsq writes bx * nseg float64 partial
+// sums of squares (bx = grad_norm_blocks(nseg) blocks per segment);
+// grad_norm_finish adds n partials in a fixed order and derives the norm and
+// the clip scale (GradientClipping, optimizer.go:169-196); with more than
+// 8192 partials and lvl (room for ceil(n/1024) doubles) it adds them in
+// blocks of 1024 first.
+int grad_norm_blocks(const Context* ctx, int nseg);
+int grad_sumsq(Context* ctx, const float* grads, const int64_t* segs, int nseg, int bx, double* partial, double elems,
+               cudaStream_t s);
+int grad_norm_finish(Context* ctx, const double* partial, long long n, float max_norm, double* norm_out,
+                     float* scale_out, cudaStream_t s, double* lvl = nullptr, long long lvl_cap = 0);
 int adamw(Context* ctx, float* p, float* g, float* m, float* v, float* shadow, const int64_t* segs, int nseg,
           const float* clip_scale, float lr, float beta1, float beta2, float eps, float wd, int step, double elems,
           cudaStream_t s, bool write_grad = true);

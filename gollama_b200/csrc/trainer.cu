@@ -258,6 +258,20 @@ struct Model {
   // step does not write the clipped gradients back (4 bytes per parameter).
   float* pending_scale = nullptr;
   bool scale_pending = false;
+  // Clip norm from the GEMM epilogues (one GPU): a weight's gradient is final
+  // once the last GradFn reading the weight has run, and that GradFn's dW
+  // GEMM stores it, so its epilogue adds the squares of what it stores into
+  // float64 slots; a small pass covers the gradients no such GEMM stores (the
+  // tied embedding, which the scatter also writes, and the RMSNorm weights),
+  // and one kernel adds every slot in order.  norm_slots holds norm_slot_cap
+  // GEMM slots, then room for that pass's partials.
+  double* norm_slots = nullptr;
+  long long norm_slot_cap = 0, norm_slot_used = 0;
+  double* norm_lvl = nullptr;  // inside norm_slots: the finishing sum's first level
+  long long norm_lvl_cap = 0;
+  bool norm_fused = false;                 // this step
+  std::vector<const Node*> last_consumer;  // this step: the last GradFn reading each parameter
+  std::vector<char> norm_covered;          // this step: parameters a GEMM epilogue measured
   std::vector<Node> param_nodes;
   std::vector<Node> qkv_view, gu_view;  // per layer: WQ|WK|WV and WGate|WUp
 
@@ -287,6 +301,7 @@ struct Model {
   ~Model() {
     for (float* p : {params, grads, m, v, shadow, cos_t, sin_t, pending_scale})
       if (p) cudaFree(p);
+    if (norm_slots) cudaFree(norm_slots);
   }
 
   bool layout(const glc_train_config& conf);
@@ -383,11 +398,32 @@ struct Model {
       }
       if (w->require_grad) {
         const bool acc = t->prepare_grad(w);
-        g[n++] = GemmSpec{{dY, N, true}, {a->gemm_data, K, true}, w->grad, K, N, K, M, acc, nullptr, 0, false};
+        g[n] = GemmSpec{{dY, N, true}, {a->gemm_data, K, true}, w->grad, K, N, K, M, acc, nullptr, 0, false};
+        claim_norm_slots(w, out, N, K, g[n]);
+        ++n;
       }
       if (n) ck(gemm_tf32_group(ctx, g, n, t->stream()));
     };
     return out;
+  }
+
+  // When the clip norm comes from the GEMM epilogues and `consumer` is the
+  // last GradFn reading every parameter of w, the dW GEMM into w's gradient
+  // sums the squares of the final values into the next free slots.
+  void claim_norm_slots(const Node* w, const Node* consumer, int rows, int cols, GemmSpec& g) {
+    if (!norm_fused) return;
+    std::vector<int> ps;
+    if (w->param >= 0) ps.push_back(w->param);
+    for (int i : w->group) ps.push_back(i);
+    if (ps.empty()) return;
+    for (int i : ps)
+      if (last_consumer[i] != consumer) return;
+    const long long need = gemm_sumsq_slots(rows, cols);
+    if (norm_slot_used + need > norm_slot_cap) return;
+    g.sumsq = norm_slots + norm_slot_used;
+    g.sumsq_cap = need;
+    norm_slot_used += need;
+    for (int i : ps) norm_covered[i] = 1;
   }
 
   // RMSNormTrainable.Forward and its GradFn (trainer.go:141-203).
@@ -680,6 +716,10 @@ int Model::init(Context* c, const glc_train_config& conf) {
 }
 
 // ---------------------------------------------------------------- trainer
+// Floats per block of the clip-norm pass over the gradients no GEMM epilogue
+// measured (a multiple of 4: segment starts and lengths are).
+constexpr int64_t kNormChunk = 65536;
+
 struct Trainer {
   Model* model = nullptr;
   Context* ctx = nullptr;
@@ -701,6 +741,12 @@ struct Trainer {
   int nseg = 0;
   int64_t seg_elems = 0;
   std::vector<char> segs_for;
+  // segments of the allocated gradients no GEMM epilogue measured (clip norm
+  // from the epilogues), for the set they were built for
+  int64_t* rest_segs_dev = nullptr;
+  int nrest = 0;
+  double rest_elems = 0;
+  std::vector<char> rest_for;
   // data-parallel gradient buckets (Model::plan_buckets): per-step state
   std::vector<cudaEvent_t> bucket_ev;
   cudaEvent_t comm_done = nullptr;
@@ -715,6 +761,7 @@ struct Trainer {
     cudaFree(tok_dev);
     cudaFree(row_logp);
     cudaFree(segs_dev);
+    cudaFree(rest_segs_dev);
   }
 
   float get_lr(int s) const {  // LRScheduler.GetLR (optimizer.go:157-166)
@@ -749,6 +796,44 @@ struct Trainer {
         throw StepError{GLC_ERR_CUDA};
     }
     segs_for = model->grad_allocated;
+  }
+
+  void refresh_rest_segments() {
+    const int np = model->num_params();
+    std::vector<char> key(np);
+    for (int i = 0; i < np; ++i) key[i] = model->grad_allocated[i] ? (model->norm_covered[i] ? 2 : 1) : 0;
+    if (key == rest_for && (rest_segs_dev || nrest == 0) && !rest_for.empty()) return;
+    // adjacent gradients merged, then cut into chunks of at most kNormChunk
+    // floats, one block each (the tied embedding is 65.5M floats, an RMSNorm
+    // weight a few thousand)
+    std::vector<int64_t> m;
+    rest_elems = 0;
+    for (int i = 0; i < np; ++i) {
+      if (key[i] != 1) continue;
+      const int64_t st = model->offset[i], len = model->rows[i] * model->cols[i];
+      rest_elems += static_cast<double>(len);
+      if (!m.empty() && m[m.size() - 2] + m[m.size() - 1] == st) {
+        m[m.size() - 1] += len;
+      } else {
+        m.push_back(st);
+        m.push_back(len);
+      }
+    }
+    std::vector<int64_t> s;
+    for (size_t k = 0; k < m.size(); k += 2)
+      for (int64_t o = 0; o < m[k + 1]; o += kNormChunk) {
+        s.push_back(m[k] + o);
+        s.push_back(std::min<int64_t>(kNormChunk, m[k + 1] - o));
+      }
+    cudaFree(rest_segs_dev);
+    rest_segs_dev = nullptr;
+    nrest = static_cast<int>(s.size() / 2);
+    if (nrest) {
+      if (cudaMalloc(&rest_segs_dev, s.size() * sizeof(int64_t)) != cudaSuccess) throw StepError{GLC_ERR_NOMEM};
+      if (cudaMemcpy(rest_segs_dev, s.data(), s.size() * sizeof(int64_t), cudaMemcpyHostToDevice) != cudaSuccess)
+        throw StepError{GLC_ERR_CUDA};
+    }
+    rest_for = key;
   }
 
   int train_step(const int64_t* in_dev, const int64_t* tg_dev, const int64_t* in_host, int B, int S, float* loss_out);
@@ -793,6 +878,25 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
     // backward continues on the compute stream.
     const bool dp = W > 1;
     const int np = model->num_params(), nb = static_cast<int>(model->bucket_begin.size());
+    // one GPU: the clip norm's squares come from the dW GEMM epilogues (with
+    // data parallelism the norm is of the summed gradient: one pass after it)
+    if (!dp && !model->norm_slots) {
+      long long cap = 0;
+      for (int i = 0; i < np; ++i)
+        if (model->rows[i] > 1) cap += gemm_sumsq_slots(model->rows[i], model->cols[i]);
+      const long long rest = model->total / kNormChunk + 2LL * np + 64;  // chunks of the remaining pass
+      const long long lvl = (cap + rest) / 1024 + 1;
+      if (cudaMalloc(&model->norm_slots, sizeof(double) * static_cast<size_t>(cap + rest + lvl)) == cudaSuccess) {
+        model->norm_slot_cap = cap;
+        model->norm_lvl = model->norm_slots + cap + rest;
+        model->norm_lvl_cap = lvl;
+      } else {
+        model->norm_slots = nullptr;
+        cudaGetLastError();
+      }
+    }
+    model->norm_fused = !dp && model->norm_slots != nullptr;
+    model->norm_slot_used = 0;
     if (dp && static_cast<int>(bucket_ev.size()) != nb) {
       for (int b = static_cast<int>(bucket_ev.size()); b < nb; ++b) {
         cudaEvent_t e;
@@ -819,6 +923,15 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
       consumers.assign(np, 0);
       for (Node* n : run)
         for (Node* p : n->parents) for_params(p, [&](int i) { ++consumers[i]; });
+      if (model->norm_fused) {
+        model->last_consumer.assign(np, nullptr);
+        for (Node* n : run)
+          for (Node* p : n->parents) for_params(p, [&](int i) { model->last_consumer[i] = n; });
+        model->norm_covered.assign(np, 0);
+        if (cudaMemsetAsync(model->norm_slots, 0, sizeof(double) * static_cast<size_t>(model->norm_slot_cap),
+                            ctx->stream) != cudaSuccess)
+          throw StepError{GLC_ERR_CUDA};
+      }
       for (int i = 0; i < np; ++i)
         if (consumers[i] == 0 && model->grad_allocated[i] && !model->grad_live[i]) {
           if (cudaMemsetAsync(model->grads + model->offset[i], 0, sizeof(float) * model->rows[i] * model->cols[i],
@@ -889,8 +1002,19 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
     }
     if (nseg > 0) {
       // GradientClipping (optimizer.go:169-196) then AdamW.Step (:37-76)
-      ck(grad_norm(ctx, model->grads, segs_dev, nseg, c.grad_clip_norm, d_norm, d_scale, nullptr, 0,
-                   static_cast<double>(seg_elems), ctx->stream));
+      if (model->norm_fused) {
+        // the GEMM epilogues' slots, then the gradients they did not reach
+        refresh_rest_segments();
+        const int bx = 1;  // one block per chunk
+        if (nrest > 0)
+          ck(grad_sumsq(ctx, model->grads, rest_segs_dev, nrest, bx, model->norm_slots + model->norm_slot_used,
+                        rest_elems, ctx->stream));
+        ck(grad_norm_finish(ctx, model->norm_slots, model->norm_slot_used + static_cast<long long>(bx) * nrest,
+                            c.grad_clip_norm, d_norm, d_scale, ctx->stream, model->norm_lvl, model->norm_lvl_cap));
+      } else {
+        ck(grad_norm(ctx, model->grads, segs_dev, nseg, c.grad_clip_norm, d_norm, d_scale, nullptr, 0,
+                     static_cast<double>(seg_elems), ctx->stream));
+      }
       ++adam_step;
       ck(adamw(ctx, model->params, model->grads, model->m, model->v, model->shadow, segs_dev, nseg, d_scale, lr,
                c.beta1, c.beta2, c.epsilon, c.weight_decay, adam_step, static_cast<double>(seg_elems), ctx->stream,

@@ -159,3 +159,28 @@ def test_fused_swiglu_epilogue_bit_identical(ctx, shape):
     assert l1 == l0
     assert np.array_equal(g1.view(np.uint32), g0.view(np.uint32))
     assert np.array_equal(w1.view(np.uint32), w0.view(np.uint32))
+
+
+@pytest.mark.parametrize("shape", [syn.TINY, syn.TINY_LLAMA_MODE, syn.SMALL_LLAMA_MODE.with_(layers=2)],
+                         ids=lambda s: s.name)
+def test_clip_norm_covers_every_gradient_once(ctx, shape):
+    """On one GPU the clip norm's squares come from the dW GEMM epilogues plus
+    a pass over the gradients no GEMM stores.  With a threshold that never
+    clips, the reported norm equals the float64 norm of the returned
+    gradients: a gradient counted twice or missed would show far above
+    float64 rounding."""
+    hp = dict(STEP_HPARAMS, GradClipNorm=1e30)
+    params = syn.init_params(shape, 8)
+    model = NewTrainableModel(config_for(shape, **hp), ctx)
+    model.set_params(params)
+    tr = NewTrainer(model)
+    for s in range(2):  # the first step allocates the gradients, the second reuses them
+        tr.TrainStep(*syn.batch(shape, 50 + s))
+        norm = tr.last_stats()[0]
+        g = model.get_grads().astype(np.float64)
+        has = np.zeros(g.size, bool)
+        for p in model.Params():
+            if p.has_grad:
+                has[p.offset : p.offset + p.shape[0] * p.shape[1]] = True
+        ref = float(np.sqrt(np.sum(g[has] ** 2)))
+        assert abs(norm - ref) <= 1e-10 * ref, (s, norm, ref)
