@@ -135,6 +135,43 @@ __global__ void rope_kernel(float* __restrict__ x, size_t ld, int T, int S, int 
   }
 }
 
+// The same two pairs at a time (float4 of x, float2 of the tables) when the
+// head size and row stride are multiples of 4 floats and x is 16-byte
+// aligned; identical operations per pair.
+__device__ __forceinline__ float2 rope_pair(float a, float b, float c, float s, int inverse, int round_out) {
+  float2 o;
+  if (!inverse) {
+    o.x = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    o.y = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+  } else {
+    o.x = __fadd_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    o.y = __fadd_rn(__fmul_rn(-a, s), __fmul_rn(b, c));
+  }
+  if (round_out) {
+    o.x = round_tf32(o.x);
+    o.y = round_tf32(o.y);
+  }
+  return o;
+}
+__global__ void rope4_kernel(float* __restrict__ x, size_t ld, int T, int S, int nh, int hd,
+                             const float* __restrict__ cos_t, const float* __restrict__ sin_t, int inverse,
+                             int round_out) {
+  const int half = hd >> 1, quads = hd >> 2;
+  const int qq = blockIdx.x * blockDim.x + threadIdx.x;  // head * quads + j: pairs 2j and 2j+1 of the head
+  if (qq >= nh * quads) return;
+  const int hh = qq / quads, j = qq - hh * quads;
+  for (int t = blockIdx.y; t < T; t += gridDim.y) {
+    const int pos = t % S;
+    const float2 c = reinterpret_cast<const float2*>(cos_t + pos * half)[j];
+    const float2 s = reinterpret_cast<const float2*>(sin_t + pos * half)[j];
+    float4* xp = reinterpret_cast<float4*>(x + static_cast<size_t>(t) * ld + static_cast<size_t>(hh) * hd) + j;
+    const float4 v = *xp;
+    const float2 o0 = rope_pair(v.x, v.y, c.x, s.x, inverse, round_out);
+    const float2 o1 = rope_pair(v.z, v.w, c.y, s.y, inverse, round_out);
+    *xp = make_float4(o0.x, o0.y, o1.x, o1.y);
+  }
+}
+
 // ---------------------------------------------------------------- embedding
 // Forward (trainer.go:276-289): h[t] = E[tok] (+ P[t % S]); ids outside
 // [0, V) read row 0.
@@ -259,6 +296,18 @@ int rope(Context* ctx, float* x, int ld, int T, int S, int nh, int hd, const flo
     return ctx->fail(GLC_ERR_INVALID, "rope: bad arguments");
   const size_t pairs = static_cast<size_t>(T) * nh * (hd / 2);
   ProfScope prof(ctx, PROF_OTHER, 16.0 * pairs, s);
+  if ((hd & 3) == 0 && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      ((reinterpret_cast<uintptr_t>(cos_t) | reinterpret_cast<uintptr_t>(sin_t)) & 7) == 0) {
+    const int row_quads = nh * (hd / 4);
+    const int bx = (row_quads + 255) / 256;
+    int by = (ctx->num_sms * 16 + bx - 1) / bx;
+    if (by > T) by = T;
+    if (by > 65535) by = 65535;
+    rope4_kernel<<<dim3(bx, by), 256, 0, s>>>(x, static_cast<size_t>(ld), T, S, nh, hd, cos_t, sin_t,
+                                              inverse ? 1 : 0, round_out ? 1 : 0);
+    GLC_LAUNCH_CHECK(ctx, "rope");
+    return 0;
+  }
   const int row_pairs = nh * (hd / 2);
   const int bx = (row_pairs + 255) / 256;
   int by = (ctx->num_sms * 16 + bx - 1) / bx;
