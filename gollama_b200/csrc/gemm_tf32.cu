@@ -826,32 +826,11 @@ const int* pair_schedule(Context* ctx, const GroupArgs& a, int clusters) {
   const std::array<long long, 5> key{a.p[0].tiles, a.p[0].k_blocks, a.p[1].tiles, a.p[1].k_blocks, clusters};
   for (auto& e : ctx->gemm_sched)
     if (e.first == key) return e.second;
-  std::vector<std::vector<int>> lists(clusters);
-  using Slot = std::pair<long long, int>;  // (estimated finish, cluster): ties go to the lower cluster
-  std::priority_queue<Slot, std::vector<Slot>, std::greater<Slot>> q;
-  for (int c = 0; c < clusters; ++c) q.push({0, c});
-  std::vector<long long> rot(clusters, 0);
-  long long greedy_end = 0;
-  for (int t = 0; t < a.total_tiles; ++t) {
-    const Slot s = q.top();
-    q.pop();
-    lists[s.second].push_back(t);
-    const int kb = t < a.p[0].tiles ? a.p[0].k_blocks : a.p[1].k_blocks;
-    q.push({s.first + kb + 2, s.second});
-    greedy_end = std::max(greedy_end, s.first + kb + 2);
-    rot[t % clusters] += kb + 2;
-  }
-  if (100 * greedy_end > 99 * *std::max_element(rot.begin(), rot.end())) {
+  std::vector<int> h;
+  if (!gemm_tile_lists(a.p[0].tiles, a.p[0].k_blocks, a.p[1].tiles, a.p[1].k_blocks, clusters, &h)) {
     ctx->gemm_sched.push_back({key, nullptr});
     return nullptr;
   }
-  std::vector<int> h(static_cast<size_t>(clusters) + 1 + a.total_tiles);
-  int pos = 0;
-  for (int c = 0; c < clusters; ++c) {
-    h[c] = pos;
-    for (int t : lists[c]) h[clusters + 1 + pos++] = t;
-  }
-  h[clusters] = pos;
   int* d = nullptr;
   if (cudaMalloc(&d, h.size() * sizeof(int)) != cudaSuccess) {
     cudaGetLastError();
@@ -867,6 +846,35 @@ const int* pair_schedule(Context* ctx, const GroupArgs& a, int clusters) {
 }
 
 }  // namespace
+
+bool gemm_tile_lists(int tiles0, int kb0, int tiles1, int kb1, int clusters, std::vector<int>* out) {
+  const int total = tiles0 + tiles1;
+  if (clusters <= 0 || total <= 0) return false;
+  std::vector<std::vector<int>> lists(clusters);
+  using Slot = std::pair<long long, int>;  // (estimated finish, cluster): ties go to the lower cluster
+  std::priority_queue<Slot, std::vector<Slot>, std::greater<Slot>> q;
+  for (int c = 0; c < clusters; ++c) q.push({0, c});
+  std::vector<long long> rot(clusters, 0);
+  long long greedy_end = 0;
+  for (int t = 0; t < total; ++t) {
+    const Slot s = q.top();
+    q.pop();
+    lists[s.second].push_back(t);
+    const int kb = t < tiles0 ? kb0 : kb1;
+    q.push({s.first + kb + 2, s.second});
+    greedy_end = std::max(greedy_end, s.first + kb + 2);
+    rot[t % clusters] += kb + 2;
+  }
+  if (100 * greedy_end > 99 * *std::max_element(rot.begin(), rot.end())) return false;
+  out->assign(static_cast<size_t>(clusters) + 1 + total, 0);
+  int pos = 0;
+  for (int c = 0; c < clusters; ++c) {
+    (*out)[c] = pos;
+    for (int t : lists[c]) (*out)[clusters + 1 + pos++] = t;
+  }
+  (*out)[clusters] = pos;
+  return true;
+}
 
 long long gemm_sumsq_slots(long long M, long long N) {
   static_assert(2 * P_EPI_WARPS <= 8, "pair tiles: at most 8 slots per 256-row tile");

@@ -154,6 +154,12 @@ struct GemmSpec {
 // Upper bound of the partial slots a GEMM with sumsq writes (either tile
 // shape): ceil(M/128) * ceil(N/256) * 8.
 long long gemm_sumsq_slots(long long M, long long N);
+// Tile lists of a grouped CTA-pair launch: tiles 0..tiles0-1 of problem 0
+// (kb0 k-blocks each) then tiles1 of problem 1, handed out in order to the
+// cluster that frees first (cost k-blocks + 2).  Writes [clusters + 1 offsets
+// | tile ids] and returns true when that estimate beats the rotation
+// tile = cluster + i * clusters by at least 1 %; false: keep the rotation.
+bool gemm_tile_lists(int tiles0, int kb0, int tiles1, int kb1, int clusters, std::vector<int>* out);
 // Runs up to two independent GEMMs in one persistent launch (shared tile queue).
 int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t stream);
 int gemm_empty_k(Context* ctx, float* C, int ldc, int M, int N, bool accumulate, const float* R, int ldr,

@@ -1,5 +1,6 @@
 // C ABI of the individual ops: what a GradFn of the reference tape
 // (pkg/tensor/grad.go, pkg/train/trainer.go) calls through the cgo package.
+#include <algorithm>
 #include <vector>
 
 #include "glc_internal.h"
@@ -169,6 +170,18 @@ int glc_exp32(glc_ctx* ctx, const float* x, float* y, size_t n) {
 int glc_add_inplace(glc_ctx* ctx, float* dst, const float* src, size_t n) {
   if (!ctx) return GLC_ERR_INVALID;
   return glc::add_inplace(C_(ctx), dst, src, n, C_(ctx)->stream);
+}
+
+int glc_gemm_tile_lists(int tiles0, int kb0, int tiles1, int kb1, int clusters, int* out, int capacity, int* used) {
+  if (!used || tiles0 < 0 || tiles1 < 0 || kb0 < 0 || kb1 < 0 || clusters <= 0 || tiles0 + tiles1 <= 0)
+    return GLC_ERR_INVALID;
+  std::vector<int> h;
+  *used = 0;
+  if (!glc::gemm_tile_lists(tiles0, kb0, tiles1, kb1, clusters, &h)) return GLC_OK;
+  if (!out || capacity < static_cast<int>(h.size())) return GLC_ERR_INVALID;
+  std::copy(h.begin(), h.end(), out);
+  *used = 1;
+  return GLC_OK;
 }
 
 }  // extern "C"

@@ -357,6 +357,14 @@ GLC_API int glc_dp_destroy(glc_ctx* ctx);
  * backward.  *count receives the number of buckets; at most `capacity` are
  * written. */
 GLC_API int glc_dp_bucket_plan(const glc_train_config* cfg, int64_t* begin, int64_t* end, int capacity, int* count);
+/* Host only (no device; diagnostics, no reference counterpart): the tile
+ * lists a grouped CTA-pair GEMM launch of two problems (tiles0 tiles of kb0
+ * k-blocks, then tiles1 of kb1) walks on `clusters` SM pairs.  On return
+ * *used is 1 and out (capacity >= clusters + 1 + tiles0 + tiles1) holds
+ * clusters + 1 list offsets followed by the tile ids, or *used is 0 when the
+ * fixed rotation tile = cluster + i * clusters is kept. */
+GLC_API int glc_gemm_tile_lists(int tiles0, int kb0, int tiles1, int kb1, int clusters, int* out, int capacity,
+                                int* used);
 
 #ifdef __cplusplus
 }
