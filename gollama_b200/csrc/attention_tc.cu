@@ -1016,6 +1016,10 @@ int set_smem(Context* ctx, K kern, int bytes, bool* done) {
 int check(Context* ctx, const float* q, const float* k, const float* v, int B, int S, int H, int Hkv, int hd) {
   if (B <= 0 || S <= 0 || H <= 0 || Hkv <= 0 || H % Hkv) return ctx->fail(GLC_ERR_INVALID, "attention: bad B/S/H/Hkv");
   if (hd != 32 && hd != 64) return ctx->fail(GLC_ERR_UNSUPPORTED, "attention: head_dim must be 32 or 64");
+  // the kernels index rows (B*S*H) and elements of a head slice in 32 bits and
+  // put B and the 128-row tiles in grid dimensions (at most 65535 each)
+  if (static_cast<long long>(B) * S * H * hd >= (1LL << 31) || B > 65535 || (S + 127) / 128 > 65535)
+    return ctx->fail(GLC_ERR_INVALID, "attention: B*S*H*hd must stay below 2^31 and B at most 65535");
   if (!q || !k || !v || ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15))
     return ctx->fail(GLC_ERR_INVALID, "attention: null or misaligned pointer");
   return 0;
