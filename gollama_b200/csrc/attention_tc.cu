@@ -9,21 +9,23 @@
 // floats, k/v rows Hkv*hd; row t = b*S + s.  Inputs are expected TF32-rounded
 // (the producing kernels round them); P and dS are rounded when written.
 //
-// Every kernel: 320 threads — warp 0 issues TMA loads (one thread), warp 1
-// owns TMEM and issues tcgen05.mma (one thread), warps 2..9 do the softmax
+// Every kernel: 352 threads — warp 0 issues TMA loads (one thread), warp 1
+// owns TMEM and issues the score MMAs (S, dP), warp 10 issues the
+// accumulating MMAs (O += P V, dV/dK, dQ), warps 2..9 do the softmax
 // arithmetic: warp w reads TMEM lane quarter w % 4 (one thread per row) and
 // column half (w - 2) / 4 of each tile, so two warps share every row.  Values
 // the two halves of a row must agree on pass through shared memory behind an
 // mbarrier.  All waits are bounded.
 //
-// forward   CTA = (128 queries, head).  S_j = Q K_j^T into one of two TMEM
+// forward   CTA = (128 queries, head).  S_j = Q K_j^T into one of three TMEM
 //           buffers (the next S overlaps this softmax); P_j replaces S_j in
 //           TMEM; O (TMEM) is rescaled when the row max grows; O += P_j V_j
 //           with V as an MN-major operand.
-// dK/dV     CTA = (128 keys, query head) or (128 keys, KV head) looping over
-//           the head group.  S^T = K Q^T, dP^T = V dO^T (64 queries per step),
-//           P^T = exp(S^T - lse), dS^T = P^T (dP^T - D) scale, dV += P^T dO,
-//           dK += dS^T Q.  Per-head partials are summed over the group by a
+// dK/dV     CTA = (128 keys, KV head, share of its query-head group): loops
+//           over its query heads.  S^T = K Q^T, dP^T = V dO^T (64 queries per
+//           step), P^T = exp(S^T - lse), dS^T = P^T (dP^T - D) scale,
+//           dV += P^T dO, dK += dS^T Q accumulated in TMEM over the heads.
+//           With more than one CTA per KV head their partials are summed by a
 //           separate deterministic kernel.
 // dQ        CTA = (128 queries, head): S = Q K^T, dP = dO V^T (64 keys per
 //           step), dS as above, dQ += dS K.
