@@ -30,6 +30,12 @@
 //                          L2->SM limit; the pair tile needs ~64.
 // The pair kernel serves problems with M > 128; tiny ones keep the
 // single-CTA tile.
+//
+// Up to two problems (the dA and dB of one MatMulGrad) share a launch; on CTA
+// pairs they walk host-built tile lists when those balance the pairs better
+// than the fixed rotation (pair_schedule).  The epilogue can also add the
+// squares of the values it stores into float64 slots (a gradient's share of
+// the clip norm, Problem::sumsq).
 #include <algorithm>
 #include <functional>
 #include <queue>
