@@ -1,0 +1,119 @@
+"""Golden vectors for the reference's float32 exponential and logarithm.
+
+The reference (pkg/tensor/grad.go:283-381) computes exp32/log32 with its own
+float64 polynomials instead of the standard library: `_exp` reduces x to
+r = x - k*ln2 with k truncated toward zero from x*log2(e) +- 0.5, evaluates a
+truncated rational polynomial and scales by 2^k with repeated doubling or
+halving; `_log` halves or doubles x into [1, 2) and evaluates a polynomial in
+s = f/(2+f).  exp32 clamps at -88 / 88 before that.
+
+This script restates both in plain Python: Python floats are IEEE float64
+and every operation below maps to one float64 operation in the same order
+(Go on amd64 does not fuse multiply-add), and numpy.float32 rounds to nearest
+like Go's float32() conversion.  It is independent of the C oracle
+(oracle/oracle.c) and of the device code, which restate the same functions
+separately; tests/test_golden.py checks the oracle against these vectors bit
+for bit, and the GPU tests check the device code against the oracle.
+
+    python tests/golden/make_golden.py     # rewrites go_exp32_log32.json
+"""
+import json
+from pathlib import Path
+
+import numpy as np
+
+OUT = Path(__file__).with_name("go_exp32_log32.json")
+
+LN2_HI = 6.93147180369123816490e-01
+LN2_LO = 1.90821492927058770002e-10
+LOG2E = 1.44269504088896338700e00
+EXP_OVERFLOW = 7.09782712893383973096e02
+EXP_UNDERFLOW = -7.45133219101941108420e02
+
+
+def go_exp(x: float) -> float:
+    """grad.go:310-352."""
+    if x > EXP_OVERFLOW:
+        return 1.7976931348623157e308
+    if x < EXP_UNDERFLOW:
+        return 0.0
+    k = int(x * LOG2E + 0.5) if x >= 0 else int(x * LOG2E - 0.5)  # int() truncates toward zero, as Go's
+    r = x - float(k) * LN2_HI - float(k) * LN2_LO
+    r2 = r * r
+    p = r - r2 * (0.16666666666666602 + r2 * (0.0027777777777015593 + r2 * 6.613756321437934e-05))
+    result = 1 - (r * p / (p - 2) - r)
+    if k > 0:
+        for _ in range(k):
+            result *= 2
+    else:
+        for _ in range(-k):
+            result /= 2
+    return result
+
+
+def go_log(x: float) -> float:
+    """grad.go:354-381."""
+    if x <= 0:
+        return -1e100
+    k = 0
+    while x >= 2:
+        x /= 2
+        k += 1
+    while x < 1:
+        x *= 2
+        k -= 1
+    f = x - 1
+    s = f / (2 + f)
+    s2 = s * s
+    s4 = s2 * s2
+    t1 = s2 * (0.6666666666666735 + s4 * (0.2857142874366239 + s4 * 0.1818357216161805))
+    t2 = s4 * (0.3999999999940942 + s4 * 0.22222198432149784)
+    big_r = t1 + t2
+    return float(k) * 0.6931471805599453 + f - s * (f - big_r)
+
+
+def exp32(x32: np.float32) -> np.float32:
+    """grad.go:283-293."""
+    if x32 < np.float32(-88):
+        return np.float32(0)
+    if x32 > np.float32(88):
+        return np.float32(3.4e38)
+    return np.float32(go_exp(float(x32)))
+
+
+def log32(x32: np.float32) -> np.float32:
+    """grad.go:295-298 (float32(-1e100), the result for x <= 0, is -Inf)."""
+    with np.errstate(over="ignore"):
+        return np.float32(go_log(float(x32)))
+
+
+def bits(v: np.float32) -> int:
+    return int(np.array([v], np.float32).view(np.uint32)[0])
+
+
+def main() -> None:
+    r = np.random.default_rng(20251201)
+    xs = np.concatenate([
+        np.array([0.0, -0.0, 1.0, -1.0, 0.5, -0.5, 88.0, -88.0, 87.99, -87.99, 88.5, -88.5, 1e-30, -1e-30,
+                  0.693147, -0.693147, 20.0, -20.0], np.float32),
+        np.linspace(-90, 90, 721, dtype=np.float32),
+        r.uniform(-88, 88, 2000).astype(np.float32),
+        (r.standard_normal(1000) * 4).astype(np.float32),
+    ])
+    ls = np.concatenate([
+        np.array([1.0, 2.0, 0.5, 1e-10, 1e-10 + 1e-16, 3.0, 1.5, 1e30, 1e-38, 0.0, -1.0], np.float32),
+        np.geomspace(1e-12, 1e4, 1500).astype(np.float32),
+        r.uniform(0, 1, 1000).astype(np.float32),
+    ])
+    data = {
+        "source": "pkg/tensor/grad.go:283-381 restated in plain Python (tests/golden/make_golden.py)",
+        "exp32": [[bits(x), bits(exp32(x))] for x in xs],
+        "log32": [[bits(x), bits(log32(x))] for x in ls],
+        "go_exp": [[float(x), go_exp(float(x))] for x in np.linspace(-30, 30, 241)],
+    }
+    OUT.write_text(json.dumps(data, separators=(",", ":")))
+    print(f"wrote {OUT} ({len(data['exp32'])} exp32, {len(data['log32'])} log32 pairs)")
+
+
+if __name__ == "__main__":
+    main()
