@@ -1,4 +1,5 @@
-"""Golden vectors for the reference's float32 exponential and logarithm.
+"""Golden vectors of the reference's own arithmetic: its float32 exponential
+and logarithm, and AdamW's cast sequence.
 
 The reference (pkg/tensor/grad.go:283-381) computes exp32/log32 with its own
 float64 polynomials instead of the standard library: `_exp` reduces x to
@@ -15,14 +16,18 @@ like Go's float32() conversion.  It is independent of the C oracle
 separately; tests/test_golden.py checks the oracle against these vectors bit
 for bit, and the GPU tests check the device code against the oracle.
 
-    python tests/golden/make_golden.py     # rewrites go_exp32_log32.json
+AdamW.Step (pkg/train/optimizer.go:37-76) is restated the same way
+(adamw_steps).
+
+    python tests/golden/make_golden.py     # rewrites go_arith.json
 """
 import json
+import math
 from pathlib import Path
 
 import numpy as np
 
-OUT = Path(__file__).with_name("go_exp32_log32.json")
+OUT = Path(__file__).with_name("go_arith.json")
 
 LN2_HI = 6.93147180369123816490e-01
 LN2_LO = 1.90821492927058770002e-10
@@ -87,8 +92,36 @@ def log32(x32: np.float32) -> np.float32:
         return np.float32(go_log(float(x32)))
 
 
+def adamw_steps(p, grads, lr, b1, b2, eps, wd):
+    """AdamW.Step (pkg/train/optimizer.go:37-76) over a float32 vector for each
+    gradient in turn: float32 moments in Go's evaluation order, float64 bias
+    corrections, estimates and update, float32 casts.  1 - beta^t uses C's
+    pow (the oracle's), not Go's math.Pow, which squares repeatedly and can
+    differ in the last place.  Returns (p, m, v) after every step."""
+    f32 = np.float32
+    lr, b1, b2, eps, wd = f32(lr), f32(b1), f32(b2), f32(eps), f32(wd)
+    m = np.zeros_like(p)
+    v = np.zeros_like(p)
+    out = []
+    for step, g in enumerate(grads, start=1):
+        bc1 = 1.0 - math.pow(float(b1), float(step))
+        bc2 = 1.0 - math.pow(float(b2), float(step))
+        m = b1 * m + (f32(1) - b1) * g
+        v = b2 * v + (f32(1) - b2) * g * g
+        mhat = m.astype(np.float64) / bc1
+        vhat = v.astype(np.float64) / bc2
+        update = (mhat / (np.sqrt(vhat) + float(eps))).astype(np.float32)
+        p = p - lr * (update + wd * p)
+        out.append((p.copy(), m.copy(), v.copy()))
+    return out
+
+
 def bits(v: np.float32) -> int:
     return int(np.array([v], np.float32).view(np.uint32)[0])
+
+
+def bitlist(a: np.ndarray) -> list:
+    return np.ascontiguousarray(a, np.float32).view(np.uint32).tolist()
 
 
 def main() -> None:
@@ -111,6 +144,13 @@ def main() -> None:
         "log32": [[bits(x), bits(log32(x))] for x in ls],
         "go_exp": [[float(x), go_exp(float(x))] for x in np.linspace(-30, 30, 241)],
     }
+    # AdamW: 96 parameters, 5 steps, the trainer's defaults (lr 3e-4, betas 0.9/0.95, eps 1e-8, wd 0.1)
+    p0 = (r.standard_normal(96) * 0.02).astype(np.float32)
+    grads = [(r.standard_normal(96) * 10.0 ** r.uniform(-4, 0)).astype(np.float32) for _ in range(5)]
+    steps = adamw_steps(p0, grads, 3e-4, 0.9, 0.95, 1e-8, 0.1)
+    data["adamw"] = {"lr": 3e-4, "beta1": 0.9, "beta2": 0.95, "eps": 1e-8, "weight_decay": 0.1,
+                     "p0": bitlist(p0), "grads": [bitlist(g) for g in grads],
+                     "after": [{"p": bitlist(p), "m": bitlist(m), "v": bitlist(v)} for p, m, v in steps]}
     OUT.write_text(json.dumps(data, separators=(",", ":")))
     print(f"wrote {OUT} ({len(data['exp32'])} exp32, {len(data['log32'])} log32 pairs)")
 

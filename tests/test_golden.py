@@ -1,7 +1,8 @@
-"""The oracle against golden vectors of the reference's own float32
-exponential and logarithm (pkg/tensor/grad.go:283-381).
+"""The oracle against golden vectors of the reference's own arithmetic: the
+float32 exponential and logarithm (pkg/tensor/grad.go:283-381) and AdamW's
+cast sequence (pkg/train/optimizer.go:37-76).
 
-tests/golden/go_exp32_log32.json is written by tests/golden/make_golden.py, a
+tests/golden/go_arith.json is written by tests/golden/make_golden.py, a
 plain-Python restatement of the reference's `_exp` / `_log` made separately
 from the C oracle (oracle/oracle.c) and the device code.  The oracle must
 reproduce every vector bit for bit (the device code is checked against the
@@ -14,7 +15,7 @@ import pytest
 
 from oracle.oracle import lib
 
-GOLDEN = json.loads((Path(__file__).parent / "golden" / "go_exp32_log32.json").read_text())
+GOLDEN = json.loads((Path(__file__).parent / "golden" / "go_arith.json").read_text())
 
 
 def f32(bits: int) -> np.float32:
@@ -37,6 +38,38 @@ def test_oracle_go_exp_float64_matches_golden():
     fn = lib().orc_go_exp
     for x, y in GOLDEN["go_exp"]:
         assert fn(x) == y, (x, fn(x), y)
+
+
+def test_oracle_adamw_matches_golden_bits():
+    """Five AdamW.Step calls (optimizer.go:37-76) on 96 parameters padded into
+    a micro model's arena: p, m and v bit for bit after every step."""
+    import ctypes as C
+
+    from gollama_b200 import synthetic as syn
+    from oracle.oracle import Oracle, TrainState
+    from tests.helpers import oracle_config, oracle_optim
+
+    gd = GOLDEN["adamw"]
+    o = Oracle(threads=1)
+    shape = syn.TINY.with_(layers=1, vocab=16, hidden=8, heads=2, inter=8, seq=4, batch=1)
+    cfg = oracle_config(shape)
+    n_all = o.param_total(cfg)
+    n = len(gd["p0"])
+    assert n_all >= n
+    p0 = np.zeros(n_all, np.float32)
+    p0[:n] = np.array(gd["p0"], np.uint32).view(np.float32)
+    st = TrainState.create(p0, len(o.param_layout(cfg)), oracle_optim())
+    st.has_grad[:] = 1
+    st.opt.lr, st.opt.beta1, st.opt.beta2 = np.float32(gd["lr"]), np.float32(gd["beta1"]), np.float32(gd["beta2"])
+    st.opt.eps, st.opt.weight_decay = np.float32(gd["eps"]), np.float32(gd["weight_decay"])
+    for g_bits, want in zip(gd["grads"], gd["after"]):
+        g = np.zeros(n_all, np.float32)
+        g[:n] = np.array(g_bits, np.uint32).view(np.float32)
+        o.fn("adamw_step")(st.params.ctypes.data_as(C.c_void_p), g.ctypes.data_as(C.c_void_p),
+                           st.has_grad.ctypes.data_as(C.c_void_p), st.m.ctypes.data_as(C.c_void_p),
+                           st.v.ctypes.data_as(C.c_void_p), C.byref(cfg), C.byref(st.opt))
+        for key, arr in (("p", st.params), ("m", st.m), ("v", st.v)):
+            assert np.array_equal(arr[:n].view(np.uint32), np.array(want[key], np.uint32)), key
 
 
 def test_golden_clamps_and_known_values():
