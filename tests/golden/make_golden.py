@@ -1,5 +1,5 @@
 """Golden vectors of the reference's own arithmetic: its float32 exponential
-and logarithm, and AdamW's cast sequence.
+and logarithm, SiLU, RMSNorm, softmax cross-entropy and AdamW.
 
 The reference (pkg/tensor/grad.go:283-381) computes exp32/log32 with its own
 float64 polynomials instead of the standard library: `_exp` reduces x to
@@ -16,8 +16,10 @@ like Go's float32() conversion.  It is independent of the C oracle
 separately; tests/test_golden.py checks the oracle against these vectors bit
 for bit, and the GPU tests check the device code against the oracle.
 
-AdamW.Step (pkg/train/optimizer.go:37-76) is restated the same way
-(adamw_steps).
+SiLU (grad.go:417-449), RMSNorm with its simplified gradient
+(pkg/train/trainer.go:141-203), softmax cross-entropy (grad.go:210-280) and
+AdamW.Step (pkg/train/optimizer.go:37-76) are restated the same way, with
+float32 sums in the reference's order.
 
     python tests/golden/make_golden.py     # rewrites go_arith.json
 """
@@ -116,12 +118,90 @@ def adamw_steps(p, grads, lr, b1, b2, eps, wd):
     return out
 
 
+def silu(xs):
+    """SiLUGrad forward (grad.go:424-428): s = 1/(1+exp32(-v)), y = v*s."""
+    f32 = np.float32
+    s = [f32(1) / (f32(1) + exp32(-v)) for v in xs]
+    return np.array(s, np.float32), np.array([v * si for v, si in zip(xs, s)], np.float32)
+
+
+def silu_grad(xs, s, dy):
+    """SiLUGrad's GradFn (grad.go:440-445) onto a zero gradient: dy * s*(1 + v*(1-s))."""
+    f32 = np.float32
+    return np.array([f32(0) + d * (si * (f32(1) + v * (f32(1) - si))) for v, si, d in zip(xs, s, dy)], np.float32)
+
+
+def rmsnorm(x, w, eps):
+    """RMSNormTrainable.Forward (trainer.go:141-167): float32 sum of squares in
+    column order, float64 sqrt, (x / rms) * w."""
+    f32 = np.float32
+    rows, cols = x.shape
+    rms = np.zeros(rows, np.float32)
+    y = np.zeros_like(x)
+    for i in range(rows):
+        ss = f32(0)
+        for j in range(cols):
+            ss = ss + x[i, j] * x[i, j]
+        rms[i] = f32(math.sqrt(float(ss) / float(cols) + float(f32(eps))))
+        for j in range(cols):
+            y[i, j] = (x[i, j] / rms[i]) * w[j]
+    return y, rms
+
+
+def rmsnorm_grad(x, w, rms, dout):
+    """Its simplified GradFn (trainer.go:182-199) onto zero gradients:
+    dw[j] += dout*x/rms over the rows in order, dx = dout*w/rms."""
+    f32 = np.float32
+    rows, cols = x.shape
+    dw = np.zeros(cols, np.float32)
+    dx = np.zeros_like(x)
+    for i in range(rows):
+        for j in range(cols):
+            dw[j] = dw[j] + dout[i, j] * x[i, j] / rms[i]
+            dx[i, j] = f32(0) + dout[i, j] * w[j] / rms[i]
+    return dx, dw
+
+
+def softmax_ce(logits, targets):
+    """SoftmaxCrossEntropyGrad (grad.go:210-280): per row the max, exp32 of the
+    differences summed in order, probabilities, the loss over valid targets
+    divided by the row count, and the GradFn onto a zero gradient."""
+    f32 = np.float32
+    rows, vocab = logits.shape
+    probs = np.zeros_like(logits)
+    total = f32(0)
+    for b in range(rows):
+        mx = logits[b, 0]
+        for v in range(1, vocab):
+            if logits[b, v] > mx:
+                mx = logits[b, v]
+        se = f32(0)
+        for v in range(vocab):
+            probs[b, v] = exp32(logits[b, v] - mx)
+            se = se + probs[b, v]
+        for v in range(vocab):
+            probs[b, v] = probs[b, v] / se
+        t = targets[b]
+        if 0 <= t < vocab:
+            total = total - log32(probs[b, t] + f32(1e-10))
+    loss = total / f32(rows)
+    scale = f32(1) / f32(rows)
+    grad = np.zeros_like(logits)
+    for b in range(rows):
+        for v in range(vocab):
+            gv = probs[b, v] * scale
+            if v == targets[b]:
+                gv = gv - scale
+            grad[b, v] = f32(0) + gv
+    return loss, grad
+
+
 def bits(v: np.float32) -> int:
     return int(np.array([v], np.float32).view(np.uint32)[0])
 
 
 def bitlist(a: np.ndarray) -> list:
-    return np.ascontiguousarray(a, np.float32).view(np.uint32).tolist()
+    return np.ascontiguousarray(a, np.float32).reshape(-1).view(np.uint32).tolist()
 
 
 def main() -> None:
@@ -144,6 +224,26 @@ def main() -> None:
         "log32": [[bits(x), bits(log32(x))] for x in ls],
         "go_exp": [[float(x), go_exp(float(x))] for x in np.linspace(-30, 30, 241)],
     }
+    # SiLU: special values and a spread of magnitudes
+    xs = np.concatenate([np.array([0.0, -0.0, 1.0, -1.0, 88.0, -88.0, 89.0, -89.0, 20.0, -20.0], np.float32),
+                         (r.standard_normal(500) * 6).astype(np.float32)])
+    sg, y = silu(xs)
+    dy = r.standard_normal(xs.size).astype(np.float32)
+    data["silu"] = {"x": bitlist(xs), "y": bitlist(y), "dy": bitlist(dy), "dx": bitlist(silu_grad(xs, sg, dy))}
+    # RMSNorm: 6 rows of 64, eps 1e-5
+    x = r.standard_normal((6, 64)).astype(np.float32)
+    w = (1 + 0.1 * r.standard_normal(64)).astype(np.float32)
+    yr, rms = rmsnorm(x, w, 1e-5)
+    dout = r.standard_normal((6, 64)).astype(np.float32)
+    dxr, dwr = rmsnorm_grad(x, w, rms, dout)
+    data["rmsnorm"] = {"eps": 1e-5, "x": bitlist(x), "w": bitlist(w), "y": bitlist(yr), "rms": bitlist(rms),
+                       "dout": bitlist(dout), "dx": bitlist(dxr), "dw": bitlist(dwr)}
+    # softmax-CE: 6 rows of 100 logits N(0, 2); one ignored and one out-of-range target
+    lg = (r.standard_normal((6, 100)) * 2).astype(np.float32)
+    tg = r.integers(0, 100, 6)
+    tg[0], tg[1] = -1, 105
+    loss, gce = softmax_ce(lg, tg)
+    data["softmax_ce"] = {"logits": bitlist(lg), "targets": tg.tolist(), "loss": bits(loss), "grad": bitlist(gce)}
     # AdamW: 96 parameters, 5 steps, the trainer's defaults (lr 3e-4, betas 0.9/0.95, eps 1e-8, wd 0.1)
     p0 = (r.standard_normal(96) * 0.02).astype(np.float32)
     grads = [(r.standard_normal(96) * 10.0 ** r.uniform(-4, 0)).astype(np.float32) for _ in range(5)]

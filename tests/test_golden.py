@@ -1,6 +1,8 @@
 """The oracle against golden vectors of the reference's own arithmetic: the
-float32 exponential and logarithm (pkg/tensor/grad.go:283-381) and AdamW's
-cast sequence (pkg/train/optimizer.go:37-76).
+float32 exponential and logarithm (pkg/tensor/grad.go:283-381), SiLU
+(grad.go:417-449), RMSNorm with its simplified gradient
+(pkg/train/trainer.go:141-203), softmax cross-entropy (grad.go:210-280) and
+AdamW's cast sequence (pkg/train/optimizer.go:37-76).
 
 tests/golden/go_arith.json is written by tests/golden/make_golden.py, a
 plain-Python restatement of the reference's `_exp` / `_log` made separately
@@ -70,6 +72,46 @@ def test_oracle_adamw_matches_golden_bits():
                            st.v.ctypes.data_as(C.c_void_p), C.byref(cfg), C.byref(st.opt))
         for key, arr in (("p", st.params), ("m", st.m), ("v", st.v)):
             assert np.array_equal(arr[:n].view(np.uint32), np.array(want[key], np.uint32)), key
+
+
+def arr(key_bits, shape=None):
+    a = np.array(key_bits, np.uint32).view(np.float32)
+    return a.reshape(shape) if shape else a
+
+
+def same(a, b_bits):
+    return np.array_equal(np.ascontiguousarray(a, np.float32).reshape(-1).view(np.uint32), np.array(b_bits, np.uint32))
+
+
+def test_oracle_silu_matches_golden_bits():
+    from oracle.oracle import Oracle
+
+    o, gd = Oracle(threads=1), GOLDEN["silu"]
+    x = arr(gd["x"])
+    y, sig = o.silu_fwd(x)
+    assert same(y, gd["y"])
+    assert same(o.silu_bwd(x, sig, arr(gd["dy"])), gd["dx"])
+
+
+def test_oracle_rmsnorm_matches_golden_bits():
+    from oracle.oracle import Oracle
+
+    o, gd = Oracle(threads=1), GOLDEN["rmsnorm"]
+    x, w = arr(gd["x"], (6, 64)), arr(gd["w"])
+    y, rms = o.rmsnorm_fwd(x, w, gd["eps"])
+    assert same(y, gd["y"]) and same(rms, gd["rms"])
+    dx, dw = o.rmsnorm_bwd(x, w, rms, arr(gd["dout"], (6, 64)), 0)
+    assert same(dx, gd["dx"]) and same(dw, gd["dw"])
+
+
+def test_oracle_softmax_ce_matches_golden_bits():
+    from oracle.oracle import Oracle
+
+    o, gd = Oracle(threads=1), GOLDEN["softmax_ce"]
+    lg = arr(gd["logits"], (6, 100))
+    loss, probs = o.softmax_ce(lg, gd["targets"], want_probs=True)
+    assert b32(loss) == gd["loss"]
+    assert same(o.softmax_ce_grad(probs, gd["targets"]), gd["grad"])
 
 
 def test_golden_clamps_and_known_values():
