@@ -1,5 +1,6 @@
 """Golden vectors of the reference's own arithmetic: its float32 exponential
-and logarithm, SiLU, RMSNorm, softmax cross-entropy and AdamW.
+and logarithm, the linear layer's products, SiLU, RMSNorm, softmax
+cross-entropy and AdamW.
 
 The reference (pkg/tensor/grad.go:283-381) computes exp32/log32 with its own
 float64 polynomials instead of the standard library: `_exp` reduces x to
@@ -16,7 +17,8 @@ like Go's float32() conversion.  It is independent of the C oracle
 separately; tests/test_golden.py checks the oracle against these vectors bit
 for bit, and the GPU tests check the device code against the oracle.
 
-SiLU (grad.go:417-449), RMSNorm with its simplified gradient
+The linear layer's products (matmul.go:145-259, grad.go:81-152), SiLU
+(grad.go:417-449), RMSNorm with its simplified gradient
 (pkg/train/trainer.go:141-203), softmax cross-entropy (grad.go:210-280) and
 AdamW.Step (pkg/train/optimizer.go:37-76) are restated the same way, with
 float32 sums in the reference's order.
@@ -196,6 +198,49 @@ def softmax_ce(logits, targets):
     return loss, grad
 
 
+def dot8(a, b):
+    """dotProduct (pkg/tensor/matmul.go:237-259): eight float32 partial sums
+    over blocks of 8, added left to right, then the remainder."""
+    f32 = np.float32
+    K = a.size
+    s = [f32(0)] * 8
+    k = 0
+    while k <= K - 8:
+        for u in range(8):
+            s[u] = s[u] + a[k + u] * b[k + u]
+        k += 8
+    total = s[0] + s[1] + s[2] + s[3] + s[4] + s[5] + s[6] + s[7]
+    while k < K:
+        total = total + a[k] * b[k]
+        k += 1
+    return total
+
+
+def matmul_grads(a, b, dc, da0, db0):
+    """MatMulTransposeB (matmul.go:145-234) C = A . B^T by dotProduct, and
+    MatMulGrad's GradFn (grad.go:94-152): dA[m,k] += sum_n dC[m,n]*B[n,k] and
+    dB[n,k] += sum_m dC[m,n]*A[m,k], each sum float32 from zero in index order."""
+    f32 = np.float32
+    M, K = a.shape
+    N = b.shape[0]
+    c = np.array([[dot8(a[i], b[j]) for j in range(N)] for i in range(M)], np.float32)
+    da = da0.copy()
+    for m in range(M):
+        for k in range(K):
+            s = f32(0)
+            for n in range(N):
+                s = s + dc[m, n] * b[n, k]
+            da[m, k] = da[m, k] + s
+    db = db0.copy()
+    for n in range(N):
+        for k in range(K):
+            s = f32(0)
+            for m in range(M):
+                s = s + dc[m, n] * a[m, k]
+            db[n, k] = db[n, k] + s
+    return c, da, db
+
+
 def bits(v: np.float32) -> int:
     return int(np.array([v], np.float32).view(np.uint32)[0])
 
@@ -224,6 +269,15 @@ def main() -> None:
         "log32": [[bits(x), bits(log32(x))] for x in ls],
         "go_exp": [[float(x), go_exp(float(x))] for x in np.linspace(-30, 30, 241)],
     }
+    # linear layer: C = A . B^T and both gradients onto existing ones; K = 21 (two blocks of 8 + 5)
+    a = r.standard_normal((5, 21)).astype(np.float32)
+    b = r.standard_normal((7, 21)).astype(np.float32)
+    dc = r.standard_normal((5, 7)).astype(np.float32)
+    da0 = r.standard_normal((5, 21)).astype(np.float32)
+    db0 = r.standard_normal((7, 21)).astype(np.float32)
+    c, da, db = matmul_grads(a, b, dc, da0, db0)
+    data["matmul"] = {"a": bitlist(a), "b": bitlist(b), "dc": bitlist(dc), "da0": bitlist(da0), "db0": bitlist(db0),
+                      "c": bitlist(c), "da": bitlist(da), "db": bitlist(db)}
     # SiLU: special values and a spread of magnitudes
     xs = np.concatenate([np.array([0.0, -0.0, 1.0, -1.0, 88.0, -88.0, 89.0, -89.0, 20.0, -20.0], np.float32),
                          (r.standard_normal(500) * 6).astype(np.float32)])

@@ -1,5 +1,6 @@
 """The oracle against golden vectors of the reference's own arithmetic: the
-float32 exponential and logarithm (pkg/tensor/grad.go:283-381), SiLU
+float32 exponential and logarithm (pkg/tensor/grad.go:283-381), the linear
+layer's products (pkg/tensor/matmul.go:145-259, grad.go:81-152), SiLU
 (grad.go:417-449), RMSNorm with its simplified gradient
 (pkg/train/trainer.go:141-203), softmax cross-entropy (grad.go:210-280) and
 AdamW's cast sequence (pkg/train/optimizer.go:37-76).
@@ -81,6 +82,19 @@ def arr(key_bits, shape=None):
 
 def same(a, b_bits):
     return np.array_equal(np.ascontiguousarray(a, np.float32).reshape(-1).view(np.uint32), np.array(b_bits, np.uint32))
+
+
+@pytest.mark.parametrize("literal", [True, False])
+def test_oracle_matmul_matches_golden_bits(literal):
+    """MatMulTransposeB with dotProduct's eight partial sums and MatMulGrad's
+    dA/dB loops, in the oracle's reference-structured and fast loops."""
+    from oracle.oracle import Oracle
+
+    o, gd = Oracle(threads=3, literal=literal), GOLDEN["matmul"]
+    a, b, dc = arr(gd["a"], (5, 21)), arr(gd["b"], (7, 21)), arr(gd["dc"], (5, 7))
+    assert same(o.matmul_transpose_b(a, b), gd["c"])
+    assert same(o.matmul_grad_da(dc, b, arr(gd["da0"], (5, 21)).copy()), gd["da"])
+    assert same(o.matmul_grad_db(dc, a, arr(gd["db0"], (7, 21)).copy()), gd["db"])
 
 
 def test_oracle_silu_matches_golden_bits():
