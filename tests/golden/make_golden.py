@@ -21,7 +21,8 @@ The linear layer's products (matmul.go:145-259, grad.go:81-152), SiLU
 (grad.go:417-449), RMSNorm with its simplified gradient
 (pkg/train/trainer.go:141-203), softmax cross-entropy (grad.go:210-280) and
 AdamW.Step (pkg/train/optimizer.go:37-76) are restated the same way, with
-float32 sums in the reference's order.
+float32 sums in the reference's order; ref_step.py restates one whole
+TrainStep in reference semantics on a micro model.
 
     python tests/golden/make_golden.py     # rewrites go_arith.json
 """
@@ -241,6 +242,33 @@ def matmul_grads(a, b, dc, da0, db0):
     return c, da, db
 
 
+def ref_step_fixture(r):
+    """Parameters in Params() order (trainer.go:217-253): TokenEmbed [V, d],
+    PosEmbed [S, d], per layer AttnNorm, WQ, WK, WV, WO, FFNNorm, WGate, WUp,
+    WDown, then OutputNorm; one TrainStep on two sequences of five tokens."""
+    import ref_step
+
+    cfg = {"layers": 2, "hidden": 8, "heads": 2, "inter": 12, "vocab": 11, "seq": 5, "norm_eps": 1e-5}
+    hp = {"lr": 3e-4, "warmup": 0, "total_steps": 10000, "beta1": 0.9, "beta2": 0.95, "eps": 1e-8, "wd": 0.1,
+          "clip": 1.0}
+    d, F, V, S = cfg["hidden"], cfg["inter"], cfg["vocab"], cfg["seq"]
+    shapes = [(V, d), (S, d)]
+    for _ in range(cfg["layers"]):
+        shapes += [(1, d), (d, d), (d, d), (d, d), (d, d), (1, d), (F, d), (F, d), (d, F)]
+    shapes.append((1, d))
+    params = [(1 + 0.1 * r.standard_normal(sh)).astype(np.float32) if sh[0] == 1
+              else (r.standard_normal(sh) * 0.3).astype(np.float32) for sh in shapes]
+    inputs = r.integers(0, V, (2, S))
+    inputs[0, 1], inputs[1, 3] = -1, V + 2        # out-of-range ids embed token 0 (trainer.go:280-282)
+    targets = r.integers(0, V, (2, S))
+    targets[0, 0], targets[1, 4] = -1, V + 3      # ignored targets (grad.go:239-243)
+    loss, grads, after, ms, vs = ref_step.train_step(params, cfg, hp, inputs, targets)
+    return {"config": cfg, "hparams": hp, "shapes": shapes, "inputs": inputs.tolist(), "targets": targets.tolist(),
+            "params": [bitlist(p) for p in params], "loss": bits(loss),
+            "grads": [None if g is None else bitlist(g) for g in grads],
+            "after": [bitlist(p) for p in after], "m": [bitlist(m) for m in ms], "v": [bitlist(v) for v in vs]}
+
+
 def bits(v: np.float32) -> int:
     return int(np.array([v], np.float32).view(np.uint32)[0])
 
@@ -298,6 +326,8 @@ def main() -> None:
     tg[0], tg[1] = -1, 105
     loss, gce = softmax_ce(lg, tg)
     data["softmax_ce"] = {"logits": bitlist(lg), "targets": tg.tolist(), "loss": bits(loss), "grad": bitlist(gce)}
+    # TrainStep in reference semantics on a micro model (ref_step.py)
+    data["ref_step"] = ref_step_fixture(r)
     # AdamW: 96 parameters, 5 steps, the trainer's defaults (lr 3e-4, betas 0.9/0.95, eps 1e-8, wd 0.1)
     p0 = (r.standard_normal(96) * 0.02).astype(np.float32)
     grads = [(r.standard_normal(96) * 10.0 ** r.uniform(-4, 0)).astype(np.float32) for _ in range(5)]

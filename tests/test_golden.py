@@ -2,8 +2,9 @@
 float32 exponential and logarithm (pkg/tensor/grad.go:283-381), the linear
 layer's products (pkg/tensor/matmul.go:145-259, grad.go:81-152), SiLU
 (grad.go:417-449), RMSNorm with its simplified gradient
-(pkg/train/trainer.go:141-203), softmax cross-entropy (grad.go:210-280) and
-AdamW's cast sequence (pkg/train/optimizer.go:37-76).
+(pkg/train/trainer.go:141-203), softmax cross-entropy (grad.go:210-280),
+AdamW's cast sequence (pkg/train/optimizer.go:37-76) and one whole TrainStep
+in reference semantics (pkg/train/trainer.go:462-505) on a micro model.
 
 tests/golden/go_arith.json is written by tests/golden/make_golden.py, a
 plain-Python restatement of the reference's `_exp` / `_log` made separately
@@ -126,6 +127,37 @@ def test_oracle_softmax_ce_matches_golden_bits():
     loss, probs = o.softmax_ce(lg, gd["targets"], want_probs=True)
     assert b32(loss) == gd["loss"]
     assert same(o.softmax_ce_grad(probs, gd["targets"]), gd["grad"])
+
+
+def test_oracle_reference_train_step_matches_golden_bits():
+    """TrainStep in reference semantics on a micro model (2 layers, d 8, 2
+    heads, FFN 12, vocab 11, two sequences of 5 with out-of-range ids and
+    ignored targets): the loss, which parameters have a gradient, every
+    clipped gradient, every weight and AdamW moment after the step, bit for
+    bit against the separate restatement (tests/golden/ref_step.py)."""
+    from oracle.oracle import Config, Oracle, OptimState, TrainState
+
+    gd = GOLDEN["ref_step"]
+    c, hp = gd["config"], gd["hparams"]
+    cfg = Config(vocab=c["vocab"], hidden=c["hidden"], layers=c["layers"], heads=c["heads"], kv_heads=c["heads"],
+                 inter=c["inter"], max_seq=c["seq"], norm_eps=c["norm_eps"], rope_theta=10000.0, mode=0)
+    o = Oracle(threads=2)
+    layout = o.param_layout(cfg)
+    assert [(r_, c_) for _, r_, c_ in layout] == [tuple(s) for s in gd["shapes"]]
+    params = np.concatenate([arr(p) for p in gd["params"]])
+    opt = OptimState(lr=0.0, beta1=hp["beta1"], beta2=hp["beta2"], eps=hp["eps"], weight_decay=hp["wd"], adam_step=0,
+                     initial_lr=hp["lr"], warmup_steps=hp["warmup"], total_steps=hp["total_steps"],
+                     grad_clip=hp["clip"], trainer_step=0)
+    st = TrainState.create(params, len(layout), opt)
+    loss, _ = o.train_step(cfg, st, np.array(gd["inputs"]), np.array(gd["targets"]))
+    assert b32(loss) == gd["loss"]
+    for i, (off, r_, c_) in enumerate(layout):
+        sl = slice(off, off + r_ * c_)
+        assert bool(st.has_grad[i]) == (gd["grads"][i] is not None), i
+        if gd["grads"][i] is not None:
+            assert same(st.grads[sl], gd["grads"][i]), ("grad", i)
+        assert same(st.params[sl], gd["after"][i]), ("param", i)
+        assert same(st.m[sl], gd["m"][i]) and same(st.v[sl], gd["v"][i]), ("moments", i)
 
 
 def test_golden_clamps_and_known_values():
