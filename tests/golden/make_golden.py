@@ -269,6 +269,33 @@ def ref_step_fixture(r):
             "after": [bitlist(p) for p in after], "m": [bitlist(m) for m in ms], "v": [bitlist(v) for v in vs]}
 
 
+def rope(dim, max_seq, theta, x, seq_len, heads):
+    """RoPE (pkg/model/rope.go): the tables (precomputeFreqs, :33-48) in
+    float64 cast to float32 — with C's pow/cos/sin, the oracle's; Go's may
+    differ in a float64's last place — and apply3D (:96-126) with consecutive
+    pairs on rows of `heads` heads, position = row % seq_len."""
+    half = dim // 2
+    cos_t = np.zeros((max_seq, half), np.float32)
+    sin_t = np.zeros((max_seq, half), np.float32)
+    for pos in range(max_seq):
+        for i in range(half):
+            freq = 1.0 / math.pow(float(np.float32(theta)), float(2 * i) / float(dim))
+            angle = float(pos) * freq
+            cos_t[pos, i] = np.float32(math.cos(angle))
+            sin_t[pos, i] = np.float32(math.sin(angle))
+    y = x.copy()
+    for t in range(x.shape[0]):
+        pos = t % seq_len
+        for h in range(heads):
+            base = h * dim
+            for i in range(half):
+                c, s = cos_t[pos, i], sin_t[pos, i]
+                x0, x1 = x[t, base + 2 * i], x[t, base + 2 * i + 1]
+                y[t, base + 2 * i] = x0 * c - x1 * s
+                y[t, base + 2 * i + 1] = x0 * s + x1 * c
+    return cos_t, sin_t, y
+
+
 def bits(v: np.float32) -> int:
     return int(np.array([v], np.float32).view(np.uint32)[0])
 
@@ -326,6 +353,11 @@ def main() -> None:
     tg[0], tg[1] = -1, 105
     loss, gce = softmax_ce(lg, tg)
     data["softmax_ce"] = {"logits": bitlist(lg), "targets": tg.tolist(), "loss": bits(loss), "grad": bitlist(gce)}
+    # RoPE: head dim 8, 3 heads, rows of 2 sequences x 6 positions, theta 10000
+    xr = r.standard_normal((12, 24)).astype(np.float32)
+    ct, stb, yr_ = rope(8, 6, 10000.0, xr, 6, 3)
+    data["rope"] = {"dim": 8, "max_seq": 6, "theta": 10000.0, "heads": 3, "x": bitlist(xr), "cos": bitlist(ct),
+                    "sin": bitlist(stb), "y": bitlist(yr_)}
     # TrainStep in reference semantics on a micro model (ref_step.py)
     data["ref_step"] = ref_step_fixture(r)
     # AdamW: 96 parameters, 5 steps, the trainer's defaults (lr 3e-4, betas 0.9/0.95, eps 1e-8, wd 0.1)

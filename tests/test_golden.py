@@ -1,6 +1,7 @@
 """The oracle against golden vectors of the reference's own arithmetic: the
 float32 exponential and logarithm (pkg/tensor/grad.go:283-381), the linear
-layer's products (pkg/tensor/matmul.go:145-259, grad.go:81-152), SiLU
+layer's products (pkg/tensor/matmul.go:145-259, grad.go:81-152), RoPE
+(pkg/model/rope.go), SiLU
 (grad.go:417-449), RMSNorm with its simplified gradient
 (pkg/train/trainer.go:141-203), softmax cross-entropy (grad.go:210-280),
 AdamW's cast sequence (pkg/train/optimizer.go:37-76) and one whole TrainStep
@@ -96,6 +97,17 @@ def test_oracle_matmul_matches_golden_bits(literal):
     assert same(o.matmul_transpose_b(a, b), gd["c"])
     assert same(o.matmul_grad_da(dc, b, arr(gd["da0"], (5, 21)).copy()), gd["da"])
     assert same(o.matmul_grad_db(dc, a, arr(gd["db0"], (7, 21)).copy()), gd["db"])
+
+
+def test_oracle_rope_matches_golden_bits():
+    """RoPE tables and the consecutive-pair rotation (pkg/model/rope.go)."""
+    from oracle.oracle import Oracle
+
+    o, gd = Oracle(threads=1), GOLDEN["rope"]
+    ct, st = o.rope_table(gd["dim"], gd["max_seq"], gd["theta"])
+    assert same(ct, gd["cos"]) and same(st, gd["sin"])
+    y = o.rope_apply(arr(gd["x"], (12, 24)), gd["max_seq"], gd["heads"], gd["dim"], ct, st)
+    assert same(y, gd["y"])
 
 
 def test_oracle_silu_matches_golden_bits():
