@@ -358,6 +358,15 @@ def main() -> None:
     ct, stb, yr_ = rope(8, 6, 10000.0, xr, 6, 3)
     data["rope"] = {"dim": 8, "max_seq": 6, "theta": 10000.0, "heads": 3, "x": bitlist(xr), "cos": bitlist(ct),
                     "sin": bitlist(stb), "y": bitlist(yr_)}
+    # grouped-query attention forward: 4 query heads over 2 KV heads, head dim 4, 2 sequences of 6
+    import ref_step
+
+    qa = r.standard_normal((12, 16)).astype(np.float32)
+    ka = r.standard_normal((12, 8)).astype(np.float32)
+    va = r.standard_normal((12, 8)).astype(np.float32)
+    oa = ref_step.attention(ref_step.Node(qa), ref_step.Node(ka), ref_step.Node(va), 6, 4, 2).data
+    data["attention_gqa"] = {"S": 6, "H": 4, "Hkv": 2, "hd": 4, "q": bitlist(qa), "k": bitlist(ka), "v": bitlist(va),
+                             "o": bitlist(oa)}
     # TrainStep in reference semantics on a micro model (ref_step.py)
     data["ref_step"] = ref_step_fixture(r)
     # AdamW: 96 parameters, 5 steps, the trainer's defaults (lr 3e-4, betas 0.9/0.95, eps 1e-8, wd 0.1)

@@ -162,24 +162,29 @@ def rmsnorm(x: Node, w: Node, eps: float) -> Node:
     return out
 
 
-def attention(q: Node, k: Node, v: Node, seq_len: int, heads: int) -> Node:
-    """forwardAttention's score/softmax/sum (trainer.go:329-382): no GradFn."""
+def attention(q: Node, k: Node, v: Node, seq_len: int, heads: int, kv_heads: int = 0) -> Node:
+    """forwardAttention's score/softmax/sum (trainer.go:329-382): no GradFn.
+    With kv_heads < heads, query head h reads KV head h / (heads / kv_heads)
+    (pkg/model/attention.go:118,149) from k/v rows of kv_heads heads."""
     Q, Kd, V = q.data, k.data, v.data
     T, d = Q.shape
     hd = d // heads
+    kvh = kv_heads or heads
+    group = heads // kvh
     scale = f32(1.0 / math.sqrt(float(hd)))
     att = np.zeros_like(Q)
     for i in range(T):
         pos, b = i % seq_len, i // seq_len
         for h in range(heads):
             o = h * hd
+            ko = (h // group) * hd
             scores = []
             mx = f32(-1e10)
             for j in range(pos + 1):
                 jj = b * seq_len + j
                 dot = f32(0)
                 for e in range(hd):
-                    dot = dot + Q[i, o + e] * Kd[jj, o + e]
+                    dot = dot + Q[i, o + e] * Kd[jj, ko + e]
                 sc = dot * scale
                 scores.append(sc)
                 if sc > mx:
@@ -193,7 +198,7 @@ def attention(q: Node, k: Node, v: Node, seq_len: int, heads: int) -> Node:
             for e in range(hd):
                 s = f32(0)
                 for j in range(pos + 1):
-                    s = s + scores[j] * V[b * seq_len + j, o + e]
+                    s = s + scores[j] * V[b * seq_len + j, ko + e]
                 att[i, o + e] = s
     return Node(att, True, [q, k, v])
 

@@ -110,6 +110,16 @@ def test_oracle_rope_matches_golden_bits():
     assert same(y, gd["y"])
 
 
+def test_oracle_gqa_attention_forward_matches_golden_bits():
+    """The trainer's attention arithmetic (trainer.go:329-382) with the KV-head
+    map of pkg/model/attention.go:118,149."""
+    from oracle.oracle import Oracle
+
+    o, gd = Oracle(threads=2), GOLDEN["attention_gqa"]
+    q, k, v = arr(gd["q"], (12, 16)), arr(gd["k"], (12, 8)), arr(gd["v"], (12, 8))
+    assert same(o.attention_fwd(q, k, v, gd["S"], gd["H"], gd["Hkv"], gd["hd"]), gd["o"])
+
+
 def test_oracle_silu_matches_golden_bits():
     from oracle.oracle import Oracle
 
