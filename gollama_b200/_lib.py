@@ -22,6 +22,7 @@ ERRORS = {
     -4: "GLC_ERR_NOMEM",
     -5: "GLC_ERR_NCCL",
     -6: "GLC_ERR_UNSUPPORTED",
+    -7: "GLC_ERR_IO",
 }
 
 _SCALARS = {

@@ -110,8 +110,8 @@ int glc_destroy(glc_ctx* ctx) {
 }
 
 int glc_last_error(glc_ctx* ctx, char* buf, size_t n) {
-  if (!ctx || !buf || n == 0) return GLC_ERR_INVALID;
-  const std::string& s = C_(ctx)->last_error;
+  if (!buf || n == 0) return GLC_ERR_INVALID;
+  const std::string& s = ctx ? C_(ctx)->last_error : glc::host_error();
   size_t k = s.size() < n - 1 ? s.size() : n - 1;
   std::memcpy(buf, s.data(), k);
   buf[k] = 0;

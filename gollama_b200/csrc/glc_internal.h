@@ -6,6 +6,7 @@
 #include <array>
 #include <cstddef>
 #include <cstdint>
+#include <functional>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -254,6 +255,33 @@ void rope_table_host(int dim, int max_seq, float theta, float* cos_t, float* sin
 // [0, V)): distinct ids ascending, their tokens in ascending position.
 void embed_segments_host(const int64_t* tok, int T, int V, std::vector<int>& seg_tok, std::vector<int>& seg_start,
                          std::vector<int>& order);
+
+// ---------------------------------------------------------------- checkpoints (checkpoint.cpp)
+// Message of the calling thread's last failed host-only call (no context).
+std::string& host_error();
+// Element counts of the parameters in Params() order (trainer.cu; host only).
+bool param_sizes(const glc_train_config& cfg, std::vector<int64_t>* sizes);
+// Go's fmt %v of a float32 into out (at most 16 bytes); returns the length.
+int format_go_float32(float v, char* out);
+bool parse_go_float32(const char* s, const char* e, float* v);
+// Callbacks that move floats [off, off + n) of the parameter arena (text) or
+// of arena a = 0 parameters, 1 m, 2 v (state) between the model and a host
+// chunk; they return false on a failed copy.
+using CkptFetch = std::function<bool(int64_t off, int64_t n, float* dst)>;
+using CkptStore = std::function<bool(int64_t off, int64_t n, const float* src)>;
+using StateFetch = std::function<bool(int a, int64_t off, int64_t n, float* dst)>;
+using StateStore = std::function<bool(int a, int64_t off, int64_t n, const float* src)>;
+struct StateInfo {
+  int step;       // LRScheduler step (Trainer.step)
+  int adam_step;  // AdamW.t
+};
+int ckpt_text_write(const char* path, int step, const glc_train_config& cfg, const std::vector<int64_t>& sizes,
+                    const CkptFetch& fetch);
+int ckpt_text_read(const char* path, const glc_train_config& cfg, const std::vector<int64_t>& sizes, int* step,
+                   const CkptStore& store);
+int state_write(const char* path, const StateInfo& info, const glc_train_config& cfg, int64_t n,
+                const StateFetch& fetch);
+int state_read(const char* path, const glc_train_config& cfg, int64_t n, StateInfo* info, const StateStore& store);
 
 inline unsigned grid_for(size_t n, int block, int num_sms, int per_sm = 8) {
   size_t g = (n + block - 1) / block;

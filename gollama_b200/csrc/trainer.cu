@@ -1057,6 +1057,16 @@ struct glc_trainer {
 
 using glc::Context;
 
+namespace glc {
+bool param_sizes(const glc_train_config& cfg, std::vector<int64_t>* sizes) {
+  Model model;  // layout only: no device memory
+  if (!model.layout(cfg)) return false;
+  sizes->clear();
+  for (int i = 0; i < model.num_params(); ++i) sizes->push_back(model.rows[i] * model.cols[i]);
+  return true;
+}
+}  // namespace glc
+
 extern "C" {
 
 int glc_default_train_config(glc_train_config* c) {
@@ -1231,6 +1241,80 @@ int glc_trainer_last_stats(glc_trainer* t, double* grad_norm, float* lr, int* st
 int glc_trainer_last_launches(glc_trainer* t, uint64_t* n) {
   if (!t || !n) return GLC_ERR_INVALID;
   *n = t->impl.last_launches;
+  return GLC_OK;
+}
+
+// ---------------------------------------------------------------- checkpoints
+// The files are written and read on the host in chunks (checkpoint.cpp); these
+// move each chunk between a device arena and host memory on the context's
+// stream, one synchronous copy at a time.
+static bool chunk_d2h(Context* c, const float* dev, int64_t off, int64_t n, float* dst) {
+  return cudaMemcpyAsync(dst, dev + off, sizeof(float) * n, cudaMemcpyDeviceToHost, c->stream) == cudaSuccess &&
+         cudaStreamSynchronize(c->stream) == cudaSuccess;
+}
+static bool chunk_h2d(Context* c, float* dev, int64_t off, int64_t n, const float* src) {
+  return cudaMemcpyAsync(dev + off, src, sizeof(float) * n, cudaMemcpyHostToDevice, c->stream) == cudaSuccess &&
+         cudaStreamSynchronize(c->stream) == cudaSuccess;
+}
+static int ckpt_status(Context* c, int rc) {
+  if (rc) c->last_error = glc::host_error();
+  return rc;
+}
+
+int glc_trainer_save_checkpoint(glc_trainer* t, const char* dir, char* path_out, size_t path_cap) {
+  if (!t || !dir) return GLC_ERR_INVALID;
+  glc::Trainer& tr = t->impl;
+  glc::Model& md = *tr.model;
+  Context* c = tr.ctx;
+  // fmt.Sprintf("%s/checkpoint_%d.bin", SavePath, step) (trainer.go:555)
+  const std::string path = std::string(dir) + "/checkpoint_" + std::to_string(tr.step) + ".bin";
+  if (path_out) {
+    if (path_cap <= path.size()) return c->fail(GLC_ERR_INVALID, "save_checkpoint: path buffer too small");
+    std::memcpy(path_out, path.c_str(), path.size() + 1);
+  }
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess) return c->fail(GLC_ERR_CUDA, "save_checkpoint: sync");
+  std::vector<int64_t> sizes;
+  for (int i = 0; i < md.num_params(); ++i) sizes.push_back(md.rows[i] * md.cols[i]);
+  return ckpt_status(c, glc::ckpt_text_write(path.c_str(), tr.step, md.cfg, sizes,
+                                             [&](int64_t off, int64_t n, float* dst) {
+                                               return chunk_d2h(c, md.params, off, n, dst);
+                                             }));
+}
+
+int glc_trainer_save_state(glc_trainer* t, const char* path) {
+  if (!t || !path) return GLC_ERR_INVALID;
+  glc::Trainer& tr = t->impl;
+  glc::Model& md = *tr.model;
+  Context* c = tr.ctx;
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess) return c->fail(GLC_ERR_CUDA, "save_state: sync");
+  const float* arenas[3] = {md.params, md.m, md.v};
+  return ckpt_status(c, glc::state_write(path, glc::StateInfo{tr.step, tr.adam_step}, md.cfg, md.total,
+                                         [&](int a, int64_t off, int64_t n, float* dst) {
+                                           return chunk_d2h(c, arenas[a], off, n, dst);
+                                         }));
+}
+
+int glc_trainer_load_state(glc_trainer* t, const char* path) {
+  if (!t || !path) return GLC_ERR_INVALID;
+  glc::Trainer& tr = t->impl;
+  glc::Model& md = *tr.model;
+  Context* c = tr.ctx;
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess) return c->fail(GLC_ERR_CUDA, "load_state: sync");
+  float* arenas[3] = {md.params, md.m, md.v};
+  glc::StateInfo info{};
+  int rc = ckpt_status(c, glc::state_read(path, md.cfg, md.total, &info,
+                                          [&](int a, int64_t off, int64_t n, const float* src) {
+                                            return chunk_h2d(c, arenas[a], off, n, src);
+                                          }));
+  if (rc) return rc;
+  // the GEMM operand copy of the weights follows the parameters
+  rc = glc::round_copy(c, md.params, md.shadow, static_cast<size_t>(md.total), c->stream);
+  if (rc) return rc;
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess) return c->fail(GLC_ERR_CUDA, "load_state: sync");
+  tr.step = info.step;
+  tr.adam_step = info.adam_step;
+  tr.lr = info.step > 0 ? tr.get_lr(info.step) : 0.f;
+  md.scale_pending = false;
   return GLC_OK;
 }
 

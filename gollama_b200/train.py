@@ -47,11 +47,13 @@ class TrainConfig:
     InitStd: float = 0.02
     Seed: int = 42
     WorldSize: int = 1
+    # host-only fields (not in glc_train_config): SaveCheckpoint's directory (trainer.go:36,65)
+    SavePath: str = "./checkpoints"
 
     def to_c(self) -> _lib.TrainConfigC:
         c = _lib.TrainConfigC()
         names = [f[0] for f in _lib.TrainConfigC._fields_]
-        vals = [getattr(self, f.name) for f in fields(self)]
+        vals = [getattr(self, f.name) for f in fields(self)][: len(names)]
         for n, v in zip(names, vals):
             setattr(c, n, v)
         return c
@@ -144,6 +146,15 @@ class TrainableModel:
         )
         return m, v
 
+    def LoadCheckpoint(self, path) -> int:
+        """Loads the parameters of a SaveCheckpoint text file (trainer.go:554-584)
+        and returns its step.  The file's dimensions must match this model."""
+        from .checkpoint import read_checkpoint
+
+        step, flat = read_checkpoint(path, self.Config)
+        self.set_params(flat)
+        return step
+
     def close(self) -> None:
         # a model whose context is already gone was closed with it
         if getattr(self, "h", None) and getattr(self.ctx, "h", None):
@@ -197,6 +208,24 @@ class Trainer:
         n = C.c_uint64()
         self.ctx.check(self.ctx.lib.glc_trainer_last_launches(self.h, C.byref(n)), "glc_trainer_last_launches")
         return n.value
+
+    def SaveCheckpoint(self) -> str:
+        """Trainer.SaveCheckpoint (trainer.go:554-584): writes
+        <Config.SavePath>/checkpoint_<step>.bin in the reference's text format
+        and returns the path."""
+        buf = C.create_string_buffer(4096)
+        self.ctx.check(self.ctx.lib.glc_trainer_save_checkpoint(self.h, str(self.Config.SavePath).encode(), buf, 4096),
+                       "glc_trainer_save_checkpoint")
+        return buf.value.decode()
+
+    def SaveState(self, path) -> None:
+        """Binary resume file: parameters, AdamW m/v and step, scheduler step."""
+        self.ctx.check(self.ctx.lib.glc_trainer_save_state(self.h, str(path).encode()), "glc_trainer_save_state")
+
+    def LoadState(self, path) -> None:
+        """Restores a SaveState file into this trainer and its model; the next
+        TrainStep continues as the saved trainer's next step would."""
+        self.ctx.check(self.ctx.lib.glc_trainer_load_state(self.h, str(path).encode()), "glc_trainer_load_state")
 
     def close(self) -> None:
         if getattr(self, "h", None) and getattr(self.ctx, "h", None):

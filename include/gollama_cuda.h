@@ -40,6 +40,7 @@ extern "C" {
 #define GLC_ERR_NOMEM (-4)       /* device allocation failed */
 #define GLC_ERR_NCCL (-5)        /* NCCL error or timeout */
 #define GLC_ERR_UNSUPPORTED (-6) /* not available in this build / device */
+#define GLC_ERR_IO (-7)          /* a file cannot be opened, read or written, or is malformed or corrupt */
 
 typedef struct glc_ctx glc_ctx;
 
@@ -52,7 +53,9 @@ GLC_API int glc_init(int device, glc_ctx** out);
 /* Replaces metal.Cleanup (pkg/metal/metal.go:193-196).  Trainers and models
  * created on the context must be destroyed before it (they use its stream). */
 GLC_API int glc_destroy(glc_ctx* ctx);
-/* Copies the last error message (NUL-terminated, truncated to n). */
+/* Copies the last error message (NUL-terminated, truncated to n).  With
+ * ctx == NULL: the message of the calling thread's last failed call that takes
+ * no context (the checkpoint file functions). */
 GLC_API int glc_last_error(glc_ctx* ctx, char* buf, size_t n);
 /* Replaces metal.DeviceName (pkg/metal/metal.go:204-206). */
 GLC_API int glc_device_name(glc_ctx* ctx, char* buf, size_t n);
@@ -336,6 +339,38 @@ GLC_API int glc_train_step_device(glc_trainer* t, const int64_t* inputs_dev, con
 GLC_API int glc_trainer_last_stats(glc_trainer* t, double* grad_norm, float* lr, int* step);
 /* Kernels launched by the last step (all of them this library's). */
 GLC_API int glc_trainer_last_launches(glc_trainer* t, uint64_t* n);
+
+/* ------------------------------------------------------------------ checkpoints
+ * Trainer.SaveCheckpoint (pkg/train/trainer.go:554-584) writes a text file:
+ *   GOLLAMA_CKPT\n step=<step>\n vocab_size=..\n hidden_size=..\n
+ *   num_layers=..\n num_heads=..\n intermediate_size=..\n WEIGHTS\n
+ * then per parameter in Params() order one line of its float32 values, each
+ * printed as Go's fmt %v prints it and followed by one space.  The functions
+ * below write that format byte for byte; the reference has no reader, and
+ * glc_checkpoint_read accepts exactly that format (values read back bit for
+ * bit; dimensions and per-parameter counts are checked against cfg).
+ *
+ * The text format holds no optimizer state.  glc_state_write/read keep a
+ * binary resume file with the parameters, AdamW's m and v, AdamW's step and
+ * the LRScheduler's step, the model dimensions and a hash of the payload;
+ * reading checks all of them before anything is written to the model.
+ *
+ * Host buffers only, no context, no device (errors: glc_last_error(NULL)).
+ * n = the model's parameter count (glc_model_num_params). */
+GLC_API int glc_checkpoint_write(const char* path, int step, const glc_train_config* cfg, const float* params,
+                                 int64_t n);
+GLC_API int glc_checkpoint_read(const char* path, const glc_train_config* cfg, int* step, float* params, int64_t n);
+GLC_API int glc_state_write(const char* path, const glc_train_config* cfg, int step, int adam_step,
+                            const float* params, const float* m, const float* v, int64_t n);
+GLC_API int glc_state_read(const char* path, const glc_train_config* cfg, int* step, int* adam_step, float* params,
+                           float* m, float* v, int64_t n);
+/* Trainer.SaveCheckpoint on the device-resident parameters: writes
+ * <dir>/checkpoint_<step>.bin (trainer.go:555) in the text format, the path
+ * is copied to path_out when it is not NULL.  Waits for the queued steps. */
+GLC_API int glc_trainer_save_checkpoint(glc_trainer* t, const char* dir, char* path_out, size_t path_cap);
+/* Binary resume of a trainer: parameters, m, v and both step counters. */
+GLC_API int glc_trainer_save_state(glc_trainer* t, const char* path);
+GLC_API int glc_trainer_load_state(glc_trainer* t, const char* path);
 
 /* ------------------------------------------------------------------ data parallel (NCCL)
  * One process per GPU.  Rank 0 creates the id and shares it (file, store, ...);
