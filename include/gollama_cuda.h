@@ -136,15 +136,22 @@ GLC_API int glc_linear_bwd(glc_ctx* ctx, const float* dY, const float* X, const 
 GLC_API int glc_linear_fwd_swiglu(glc_ctx* ctx, const float* X, const float* Wgu, float* GU, float* H, int M, int K,
                                   int F, int round_h);
 /* Frozen quantized weights (pkg/quant/dequant.go).  Type codes are GGUF's
- * (pkg/gguf/format.go:40-46). */
+ * (pkg/gguf/format.go:40-58). */
 #define GLC_QTYPE_F32 0
 #define GLC_QTYPE_F16 1
 #define GLC_QTYPE_Q4_0 2
+#define GLC_QTYPE_Q4_1 3
+#define GLC_QTYPE_Q5_0 6
+#define GLC_QTYPE_Q5_1 7
 #define GLC_QTYPE_Q8_0 8
+#define GLC_QTYPE_Q4_K 12
+#define GLC_QTYPE_Q6_K 14
 /* Dequantize (pkg/quant/dequant.go:367-393) of n elements on the device, exact
- * fp32 results: F16 via fp16ToFp32 (:9-41), Q8_0 (:68-85), Q4_0 (:99-119; low
- * nibble first).  src 2-byte aligned, dst 16-byte aligned; n a multiple of 4
- * (of 32 for the block formats). */
+ * fp32 results for every type the reference's Dequantize accepts: F16 via
+ * fp16ToFp32 (:9-41), Q8_0 (:68-85), Q4_0 (:99-119; low nibble first), Q4_1
+ * (:141-163), Q5_0 (:167-199), Q5_1 (:203-233), Q4_K (:237-300) and Q6_K
+ * (:304-344), in the reference's layouts.  src 2-byte aligned, dst 16-byte
+ * aligned; n a multiple of 4 and of the block (32, or 256 for the K types). */
 GLC_API int glc_dequantize(glc_ctx* ctx, int type, const void* src, float* dst, size_t n);
 /* dX (+)= dY . deq(W) for a linear layer whose weight W [N out][K in] is stored
  * quantized row by row: the dA loop of MatMulGrad (pkg/tensor/grad.go:102-116)

@@ -370,11 +370,14 @@ void FN(exp32_array)(const float* x, float* y, int64_t n) { /* exp32 over an arr
 float FN(log32)(float x) { return (float)FN(go_log)((double)x); } /* grad.go:296-298 */
 
 /* ------------------------------------------------------------------ frozen quantized weights
- * pkg/quant/dequant.go.  Type codes are GGUF's (pkg/gguf/format.go:40-46):
- * 0 F32, 1 F16, 2 Q4_0, 8 Q8_0. */
+ * pkg/quant/dequant.go.  Type codes are GGUF's (pkg/gguf/format.go:40-58):
+ * 0 F32, 1 F16, 2 Q4_0, 3 Q4_1, 6 Q5_0, 7 Q5_1, 8 Q8_0, 12 Q4_K, 14 Q6_K. */
 #ifndef ORC_QTYPES
 #define ORC_QTYPES
-enum { ORC_Q_F32 = 0, ORC_Q_F16 = 1, ORC_Q_Q4_0 = 2, ORC_Q_Q8_0 = 8 };
+enum {
+  ORC_Q_F32 = 0, ORC_Q_F16 = 1, ORC_Q_Q4_0 = 2, ORC_Q_Q4_1 = 3, ORC_Q_Q5_0 = 6, ORC_Q_Q5_1 = 7, ORC_Q_Q8_0 = 8,
+  ORC_Q_Q4_K = 12, ORC_Q_Q6_K = 14
+};
 #endif
 
 /* fp16ToFp32 (dequant.go:9-41): exact widening; a subnormal half is
@@ -405,11 +408,116 @@ float FN(fp16_to_fp32)(uint16_t h) {
 
 static uint16_t rd_u16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); } /* little endian */
 
+static uint32_t rd_u32(const uint8_t* p) { return (uint32_t)rd_u16(p) | ((uint32_t)rd_u16(p + 2) << 16); }
+
+/* The K-quant and 5-bit formats (dequant.go:141-344), each in the
+ * reference's loop order: per block the half scales, then per byte (or per
+ * element) the codes; every product and sum is one float32 operation. */
+static int dequant_more(const uint8_t* data, real* out, int64_t n, int type) {
+  if (type == ORC_Q_Q4_1 || type == ORC_Q_Q5_0 || type == ORC_Q_Q5_1) {
+    if (n % 32) return -1;
+    const int bpb = type == ORC_Q_Q4_1 ? 20 : type == ORC_Q_Q5_0 ? 22 : 24;
+    for (int64_t b = 0; b < n / 32; ++b) {
+      const uint8_t* blk = data + (int64_t)bpb * b;
+      const float scale = FN(fp16_to_fp32)(rd_u16(blk));
+      if (type == ORC_Q_Q4_1) { /* :141-163: scale*q + min */
+        const float mn = FN(fp16_to_fp32)(rd_u16(blk + 2));
+        for (int i = 0; i < 16; ++i) {
+          const uint8_t q = blk[4 + i];
+          const float q0 = (float)(q & 0x0f), q1 = (float)(q >> 4);
+          const float p0 = scale * q0, p1 = scale * q1;
+          out[32 * b + 2 * i] = p0 + mn;
+          out[32 * b + 2 * i + 1] = p1 + mn;
+        }
+      } else if (type == ORC_Q_Q5_0) { /* :167-199: high bit k of qh for element k, then - 16 */
+        const uint32_t qh = rd_u32(blk + 2);
+        for (int i = 0; i < 16; ++i) {
+          const uint8_t q = blk[6 + i];
+          int8_t q0 = (int8_t)(q & 0x0f), q1 = (int8_t)(q >> 4);
+          if ((qh >> (i * 2)) & 1u) q0 |= 0x10;
+          if ((qh >> (i * 2 + 1)) & 1u) q1 |= 0x10;
+          out[32 * b + 2 * i] = scale * (float)(int8_t)(q0 - 16);
+          out[32 * b + 2 * i + 1] = scale * (float)(int8_t)(q1 - 16);
+        }
+      } else { /* Q5_1, :203-233: scale*q + min */
+        const float mn = FN(fp16_to_fp32)(rd_u16(blk + 2));
+        const uint32_t qh = rd_u32(blk + 4);
+        for (int i = 0; i < 16; ++i) {
+          const uint8_t q = blk[8 + i];
+          uint8_t q0 = (uint8_t)(q & 0x0f), q1 = (uint8_t)(q >> 4);
+          if ((qh >> (i * 2)) & 1u) q0 |= 0x10;
+          if ((qh >> (i * 2 + 1)) & 1u) q1 |= 0x10;
+          const float p0 = scale * (float)q0, p1 = scale * (float)q1;
+          out[32 * b + 2 * i] = p0 + mn;
+          out[32 * b + 2 * i + 1] = p1 + mn;
+        }
+      }
+    }
+    return 0;
+  }
+  if (type == ORC_Q_Q4_K) { /* :237-300 */
+    if (n % 256) return -1;
+    for (int64_t b = 0; b < n / 256; ++b) {
+      const uint8_t* blk = data + 144 * b;
+      const float d = FN(fp16_to_fp32)(rd_u16(blk)), dmin = FN(fp16_to_fp32)(rd_u16(blk + 2));
+      const uint8_t* sc6 = blk + 4;
+      const uint8_t* qs = blk + 16;
+      uint8_t sc[8], m[8];
+      for (int j = 0; j < 4; ++j) {
+        sc[j] = sc6[j] & 63;
+        m[j] = sc6[j + 4] & 63;
+      }
+      sc[4] = (uint8_t)((sc6[8] & 0xF) | ((sc6[0] >> 6) << 4));
+      sc[5] = (uint8_t)((sc6[8] >> 4) | ((sc6[1] >> 6) << 4));
+      sc[6] = (uint8_t)((sc6[9] & 0xF) | ((sc6[2] >> 6) << 4));
+      sc[7] = (uint8_t)((sc6[9] >> 4) | ((sc6[3] >> 6) << 4));
+      m[4] = (uint8_t)((sc6[10] & 0xF) | ((sc6[4] >> 6) << 4));
+      m[5] = (uint8_t)((sc6[10] >> 4) | ((sc6[5] >> 6) << 4));
+      m[6] = (uint8_t)((sc6[11] & 0xF) | ((sc6[6] >> 6) << 4));
+      m[7] = (uint8_t)((sc6[11] >> 4) | ((sc6[7] >> 6) << 4));
+      for (int j = 0; j < 8; ++j) {
+        const float scale_val = d * (float)sc[j];
+        const float min_val = dmin * (float)m[j];
+        for (int i = 0; i < 16; ++i) {
+          const uint8_t q = qs[j * 16 + i];
+          const float p0 = scale_val * (float)(q & 0x0F), p1 = scale_val * (float)(q >> 4);
+          out[256 * b + j * 32 + i * 2] = p0 - min_val;
+          out[256 * b + j * 32 + i * 2 + 1] = p1 - min_val;
+        }
+      }
+    }
+    return 0;
+  }
+  if (type == ORC_Q_Q6_K) { /* :304-344 */
+    if (n % 256) return -1;
+    for (int64_t b = 0; b < n / 256; ++b) {
+      const uint8_t* blk = data + 210 * b;
+      const uint8_t* ql = blk;
+      const uint8_t* qh = blk + 128;
+      const uint8_t* scales = blk + 192;
+      const float d = FN(fp16_to_fp32)(rd_u16(blk + 208));
+      for (int j = 0; j < 16; ++j) {
+        const float scale_val = d * (float)(int8_t)scales[j];
+        for (int i = 0; i < 16; ++i) {
+          const int idx = j * 16 + i;
+          const uint8_t q = (idx % 2 == 0) ? (uint8_t)(ql[idx / 2] & 0x0F) : (uint8_t)(ql[idx / 2] >> 4);
+          const uint8_t q_high = (uint8_t)((qh[idx / 4] >> ((idx % 4) * 2)) & 0x03);
+          const int8_t q6 = (int8_t)((int8_t)(q | (q_high << 4)) - 32);
+          out[256 * b + idx] = scale_val * (float)q6;
+        }
+      }
+    }
+    return 0;
+  }
+  return -1;
+}
+
 /* Dequantize (dequant.go:367-393) for F32, F16 (:50-56), Q8_0 (:68-85: per
- * 32-element block a half scale then 32 int8 codes, w = scale * q) and Q4_0
+ * 32-element block a half scale then 32 int8 codes, w = scale * q), Q4_0
  * (:99-119: a half scale then 16 bytes; element 2i is the low nibble - 8,
- * element 2i+1 the high nibble - 8).  n counts output elements; block types
- * need n % 32 == 0.  Products are float32 like the reference's. */
+ * element 2i+1 the high nibble - 8) and, through dequant_more, Q4_1, Q5_0,
+ * Q5_1, Q4_K and Q6_K.  n counts output elements; block types need a whole
+ * number of blocks.  Products are float32 like the reference's. */
 int FN(dequantize)(const uint8_t* data, real* out, int64_t n, int type) {
   if (type == ORC_Q_F32) {
     for (int64_t i = 0; i < n; ++i) {
@@ -444,7 +552,7 @@ int FN(dequantize)(const uint8_t* data, real* out, int64_t n, int type) {
     }
     return 0;
   }
-  return -1;
+  return dequant_more(data, out, n, type);
 }
 
 /* dX[M,K] += dY[M,N] . deq(W)[N,K] with W's rows (out features) stored as

@@ -1,5 +1,5 @@
 """Frozen quantized weights on the GPU against the oracle: glc_dequantize bit
-for bit (every fp16 code, random Q8_0/Q4_0 blocks with extreme scales), and
+for bit (every fp16 code, random blocks of every format with extreme scales), and
 glc_linear_bwd_dx_q (dX = dY . deq(W), MatMulGrad's dA on the dequantized
 weight) within the TF32 bar of the other GEMMs (relative Frobenius error
 2e-3)."""
@@ -10,7 +10,8 @@ import pytest
 
 from oracle.oracle import lib as orc_lib
 from tests.helpers import rel_fro
-from tests.test_quant import F16, Q4_0, Q8_0, orc_dequant, random_weight
+from tests.test_quant import (F16, Q4_0, Q4_1, Q4_K, Q5_0, Q5_1, Q6_K, Q8_0, orc_dequant, random_format_bytes,
+                              random_weight, sane_format_weight)
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-3
@@ -55,16 +56,29 @@ def test_dequant_rejects_ragged_blocks(ctx):
     with pytest.raises(GlcError):
         ctx.call("glc_dequantize", Q8_0, src.ptr, out.ptr, 48)
     with pytest.raises(GlcError):
-        ctx.call("glc_dequantize", 3, src.ptr, out.ptr, 32)  # Q4_1: not supported
+        ctx.call("glc_dequantize", 9, src.ptr, out.ptr, 32)  # Q8_1: not in the reference's Dequantize
+    with pytest.raises(GlcError):
+        ctx.call("glc_dequantize", Q4_K, src.ptr, out.ptr, 32)  # a partial 256-element super-block
 
 
-@pytest.mark.parametrize("qtype", [F16, Q4_0, Q8_0])
+@pytest.mark.parametrize("qtype", [Q4_1, Q5_0, Q5_1, Q4_K, Q6_K])
+def test_dequant_more_formats_bit_exact(ctx, qtype):
+    """Random bytes in every field (NaN, infinite and subnormal scales among
+    them): identical bits except NaN encodings, as above."""
+    data, n = random_format_bytes(qtype, 512 if qtype in (Q4_K, Q6_K) else 4096, 77 + qtype)
+    got, want = gpu_dequant(ctx, data, n, qtype), orc_dequant(data, n, qtype)
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32))
+
+
+@pytest.mark.parametrize("qtype", [F16, Q4_0, Q8_0, Q4_1, Q5_0, Q5_1, Q4_K, Q6_K])
 @pytest.mark.parametrize("M,K,N,acc", [(64, 256, 96, 0), (300, 512, 1376, 1), (512, 2048, 704, 0)])
 def test_linear_bwd_dx_q(ctx, qtype, M, K, N, acc):
     r = np.random.default_rng(M + K + N + qtype)
     dy = r.standard_normal((M, N)).astype(np.float32)
     dx0 = r.standard_normal((M, K)).astype(np.float32) if acc else np.zeros((M, K), np.float32)
-    data = random_weight(qtype, N, K, 31 + qtype)
+    data = sane_format_weight(qtype, N, K, 31 + qtype)
     src = np.frombuffer(data, np.uint8).copy()
     want = dx0.astype(np.float64).copy()
     rc = orc_lib().orcd_linear_bwd_dx_q(dy.astype(np.float64).ctypes.data_as(C.c_void_p), src.ctypes.data_as(C.c_void_p),
