@@ -379,6 +379,49 @@ GLC_API int glc_trainer_save_checkpoint(glc_trainer* t, const char* dir, char* p
 GLC_API int glc_trainer_save_state(glc_trainer* t, const char* path);
 GLC_API int glc_trainer_load_state(glc_trainer* t, const char* path);
 
+/* ------------------------------------------------------------------ GGUF files
+ * gguf.Reader (pkg/gguf/reader.go).  glc_gguf_open maps the file read-only and
+ * parses it like Reader.parse (:63-123): magic "GGUF", version 2 or 3, every
+ * metadata key/value, every tensor info, and the tensor data start rounded up
+ * to `general.alignment` (a uint32 key; 32 otherwise).  Every field read is
+ * bounds-checked: a truncated or inconsistent file fails with GLC_ERR_IO.
+ * Lookups by name return index -1 when absent (a later duplicate wins, like
+ * the reference's maps).  Host-only calls report errors through
+ * glc_last_error(NULL). */
+typedef struct glc_gguf glc_gguf;
+GLC_API int glc_gguf_open(const char* path, glc_gguf** out);
+GLC_API int glc_gguf_close(glc_gguf* g);
+/* Header (reader.go:299-301) and the data section's offset. */
+GLC_API int glc_gguf_header(glc_gguf* g, uint32_t* version, uint64_t* n_tensors, uint64_t* n_kv,
+                            uint64_t* data_offset);
+/* Metadata entry i (file order): key, value type (GGUF metadata type codes,
+ * pkg/gguf/format.go:20-34), element type and count of an array (-1 and 1
+ * otherwise).  Values: element `elem` of an array, or the scalar (elem 0);
+ * integers through as_int (signed types) / as_uint (unsigned and bool),
+ * floats through as_double (float32 exactly).  Nested arrays expose their
+ * type and count only. */
+GLC_API int glc_gguf_meta_find(glc_gguf* g, const char* key, int64_t* index);
+GLC_API int glc_gguf_meta_key(glc_gguf* g, int64_t i, char* buf, size_t cap, size_t* len);
+GLC_API int glc_gguf_meta_type(glc_gguf* g, int64_t i, int* type, int* elem_type, uint64_t* count);
+GLC_API int glc_gguf_meta_number(glc_gguf* g, int64_t i, uint64_t elem, int64_t* as_int, uint64_t* as_uint,
+                                 double* as_double);
+GLC_API int glc_gguf_meta_string(glc_gguf* g, int64_t i, uint64_t elem, char* buf, size_t cap, size_t* len);
+/* TensorInfo (format.go:152-186): name, GGML type, dimensions in GGUF order
+ * (innermost first; up to dims_cap written), offset inside the data section
+ * and SizeBytes (whole blocks of GetTypeInfo, format.go:117-149). */
+GLC_API int glc_gguf_tensor_find(glc_gguf* g, const char* name, int64_t* index);
+GLC_API int glc_gguf_tensor_info(glc_gguf* g, int64_t i, char* name, size_t name_cap, size_t* name_len, int* type,
+                                 int* ndims, uint64_t* dims, int dims_cap, uint64_t* offset, uint64_t* nbytes);
+/* GetTensorData (reader.go:407-424): a pointer into the mapping, valid until
+ * glc_gguf_close; GLC_ERR_IO if the data extends beyond the file. */
+GLC_API int glc_gguf_tensor_data(glc_gguf* g, int64_t i, const void** data, uint64_t* nbytes);
+/* The tensor's stored bytes (quantized blocks as they are) to device memory
+ * of at least `cap` bytes: the operand glc_linear_bwd_dx_q takes. */
+GLC_API int glc_gguf_tensor_upload(glc_ctx* ctx, glc_gguf* g, int64_t i, void* dev, uint64_t cap);
+/* loadTensor (pkg/model/transformer.go:285-303) on the device: the stored
+ * bytes to the device, then glc_dequantize into dev (n = element count). */
+GLC_API int glc_gguf_tensor_load(glc_ctx* ctx, glc_gguf* g, int64_t i, float* dev, int64_t n);
+
 /* ------------------------------------------------------------------ data parallel (NCCL)
  * One process per GPU.  Rank 0 creates the id and shares it (file, store, ...);
  * every rank then calls glc_dp_init.  Gradients are summed with ncclAllReduce
