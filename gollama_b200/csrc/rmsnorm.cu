@@ -148,6 +148,141 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
   }
 }
 
+// The same backward with the row loads pipelined: each thread copies its own
+// float4 chunks of x, dy (and the accumulated dx) for the next PIPE_STAGES - 1
+// rows into shared memory with cp.async while it computes the current row, so
+// the rows' load latency overlaps the block reduction instead of following
+// it.  A thread reads back only the chunks it copied itself, so the pipeline
+// needs no barrier beyond the per-thread cp.async.wait_group; a stage is
+// refilled only after the values read from it were used (data dependence
+// orders the reads before the copy that overwrites them).  The arithmetic and
+// its order are the kernel above's: results are bit-identical.
+// Shared layout: [stage][array x/dy/dx][MAXC][256 threads] float4, so a warp's
+// 16-byte accesses are contiguous.
+constexpr int PIPE_STAGES = 3;
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int MAXC>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_pipe_kernel(
+    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ rms,
+    const float* __restrict__ dy, float* __restrict__ dx, float* __restrict__ dx_round,
+    float* __restrict__ dw_partial, int rows, int cols, int rows_per_block, int full, int dx_accumulate) {
+  extern __shared__ float4 stage_buf[];  // PIPE_STAGES * 3 * MAXC * 256
+  __shared__ float red[32];
+  const int nc = cols >> 2;
+  const int tid = threadIdx.x;
+  const int row0 = blockIdx.x * rows_per_block;
+  const int row1 = min(rows, row0 + rows_per_block);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  auto slot = [&](int st, int arr, int i) -> float4* { return stage_buf + ((st * 3 + arr) * MAXC + i) * 256 + tid; };
+  // copies of row `row` into stage `st` (this thread's chunks only)
+  auto issue = [&](int row, int st) {
+    if (row < row1) {
+      const size_t base = static_cast<size_t>(row) * cols;
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * 256;
+        if (c < nc) {
+          cp_async16(slot(st, 0, i), x + base + 4 * c);
+          cp_async16(slot(st, 1, i), dy + base + 4 * c);
+          if (dx_accumulate) cp_async16(slot(st, 2, i), dx + base + 4 * c);
+        }
+      }
+    }
+    cp_async_commit();  // one group per row slot, empty past the block's rows
+  };
+  float4 wv[MAXC], acc[MAXC];
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * 256;
+    wv[i] = c < nc ? w4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int s = 0; s < PIPE_STAGES - 1; ++s) issue(row0 + s, s);
+  int st = 0;
+  for (int row = row0; row < row1; ++row) {
+    // refill the stage the previous row used, then wait for this row's group
+    issue(row + PIPE_STAGES - 1, (st + PIPE_STAGES - 1) % PIPE_STAGES);
+    cp_async_wait<PIPE_STAGES - 1>();
+    const float r = rms[row];
+    float4* dxr = reinterpret_cast<float4*>(dx + static_cast<size_t>(row) * cols);
+    float4 xv[MAXC], dv[MAXC], ov[MAXC];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * 256;
+      if (c < nc) {
+        xv[i] = *slot(st, 0, i);
+        dv[i] = *slot(st, 1, i);
+        if (dx_accumulate) ov[i] = *slot(st, 2, i);
+        if (full)
+          s += dv[i].x * wv[i].x * xv[i].x + dv[i].y * wv[i].y * xv[i].y + dv[i].z * wv[i].z * xv[i].z +
+               dv[i].w * wv[i].w * xv[i].w;
+      }
+    }
+    float coef = 0.f;
+    if (full) {
+      s = warp_sum(s);
+      if ((tid & 31) == 0) red[tid >> 5] = s;
+      __syncthreads();
+      if (tid < 32) {
+        float t = tid < (blockDim.x >> 5) ? red[tid] : 0.f;
+        t = warp_sum(t);
+        if (tid == 0) red[0] = t;
+      }
+      __syncthreads();
+      const float tot = red[0];
+      __syncthreads();
+      coef = tot / (static_cast<float>(cols) * r * r * r);
+    }
+    float4* dxq = dx_round ? reinterpret_cast<float4*>(dx_round + static_cast<size_t>(row) * cols) : nullptr;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * 256;
+      if (c < nc) {
+        float4 g;
+        g.x = __fdiv_rn(__fmul_rn(dv[i].x, wv[i].x), r);
+        g.y = __fdiv_rn(__fmul_rn(dv[i].y, wv[i].y), r);
+        g.z = __fdiv_rn(__fmul_rn(dv[i].z, wv[i].z), r);
+        g.w = __fdiv_rn(__fmul_rn(dv[i].w, wv[i].w), r);
+        if (full) {
+          g.x = __fsub_rn(g.x, __fmul_rn(xv[i].x, coef));
+          g.y = __fsub_rn(g.y, __fmul_rn(xv[i].y, coef));
+          g.z = __fsub_rn(g.z, __fmul_rn(xv[i].z, coef));
+          g.w = __fsub_rn(g.w, __fmul_rn(xv[i].w, coef));
+        }
+        if (dx_accumulate) {
+          const float4 o = ov[i];
+          g.x = __fadd_rn(o.x, g.x); g.y = __fadd_rn(o.y, g.y); g.z = __fadd_rn(o.z, g.z); g.w = __fadd_rn(o.w, g.w);
+        }
+        dxr[c] = g;
+        if (dxq) dxq[c] = make_float4(round_tf32(g.x), round_tf32(g.y), round_tf32(g.z), round_tf32(g.w));
+        acc[i].x += __fdiv_rn(__fmul_rn(dv[i].x, xv[i].x), r);
+        acc[i].y += __fdiv_rn(__fmul_rn(dv[i].y, xv[i].y), r);
+        acc[i].z += __fdiv_rn(__fmul_rn(dv[i].z, xv[i].z), r);
+        acc[i].w += __fdiv_rn(__fmul_rn(dv[i].w, xv[i].w), r);
+      }
+    }
+    st = st + 1 == PIPE_STAGES ? 0 : st + 1;
+  }
+  cp_async_wait<0>();  // no copy outlives the block (groups past the last row are empty)
+  float4* part = reinterpret_cast<float4*>(dw_partial + static_cast<size_t>(blockIdx.x) * cols);
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * 256;
+    if (c < nc) part[c] = acc[i];
+  }
+}
+
 // dw[j] (+)= sum over blocks b of partial[b][j].  A cluster of CS_CL CTAs
 // per 32 columns: CTA rank r adds the partial rows of its quarter
 // [r*q, (r+1)*q), each of its 16 warps keeping four running sums (rows
@@ -232,7 +367,9 @@ int rmsnorm_bwd(Context* ctx, const float* x, const float* w, const float* rms, 
   if (!x || !w || !rms || !dy || !dx || !dw || !aligned16(x) || !aligned16(w) || !aligned16(dy) || !aligned16(dx) ||
       (dx_round && !aligned16(dx_round)))
     return ctx->fail(GLC_ERR_INVALID, "rmsnorm_bwd: null or misaligned pointer");
-  int nblocks = 4 * ctx->num_sms;
+  // pipelined variant (opt-in): rows up to 2048 columns, three blocks per SM
+  const bool pipe = ctx->rmsnorm_variant == 2 && nc <= 512;
+  int nblocks = (pipe ? 3 : 4) * ctx->num_sms;
   if (nblocks > rows) nblocks = rows;
   const int rpb = (rows + nblocks - 1) / nblocks;
   nblocks = (rows + rpb - 1) / rpb;
@@ -250,7 +387,14 @@ int rmsnorm_bwd(Context* ctx, const float* x, const float* w, const float* rms, 
   ProfScope prof(ctx, PROF_RMSNORM,
                  4.0 * static_cast<double>(rows) * cols * (3 + (dx_accumulate ? 1 : 0) + (dx_round ? 1 : 0)) + 4.0 * rows,
                  s);
-  if (nc <= 256)
+  if (pipe) {
+    const int maxc = nc <= 256 ? 1 : 2;
+    const size_t smem = sizeof(float4) * PIPE_STAGES * 3 * maxc * 256;
+    auto kern = maxc == 1 ? rmsnorm_bwd_pipe_kernel<1> : rmsnorm_bwd_pipe_kernel<2>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return ctx->fail_cuda(e, "rmsnorm_bwd: shared memory attribute");
+    kern<<<nblocks, 256, smem, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
+  } else if (nc <= 256)
     rmsnorm_bwd_kernel<1><<<nblocks, 256, 0, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
   else if (nc <= 512)
     rmsnorm_bwd_kernel<2><<<nblocks, 256, 0, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);

@@ -231,11 +231,14 @@ def main(argv=None):
                     help="GEMM tiles: 0 automatic, 1 single-CTA 128x256, 2 CTA-pair 256x256")
     ap.add_argument("--attn-split", type=int, default=0,
                     help="attention backward: dK/dV CTAs per KV head (0 automatic, else a divisor of H/Hkv)")
+    ap.add_argument("--rmsnorm-variant", type=int, default=0, choices=[0, 1, 2],
+                    help="RMSNorm backward: 0 automatic, 1 row by row, 2 cp.async-pipelined rows")
     a = ap.parse_args(argv)
     names = sorted(CASES) if "all" in a.cases else a.cases
     with Context(0) as ctx:
         ctx.call("glc_set_gemm_variant", a.variant)
         ctx.call("glc_set_attention_split", a.attn_split)
+        ctx.call("glc_set_rmsnorm_variant", a.rmsnorm_variant)
         for n in names:
             res = CASES[n](ctx, a.iters, a.warmup)
             for desc, ms, rate, unit in (res if isinstance(res, list) else [res]):

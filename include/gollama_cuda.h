@@ -177,6 +177,11 @@ GLC_API int glc_set_gemm_variant(glc_ctx* ctx, int variant);
  * Each CTA accumulates its heads in TMEM; more than one writes partials that a
  * deterministic group sum adds.  Results agree to fp32 rounding across splits. */
 GLC_API int glc_set_attention_split(glc_ctx* ctx, int nsplit);
+/* RMSNorm backward kernel (tuning; no reference counterpart): 0 automatic and
+ * 1 process a block's rows one after another; 2 stages the next rows' x, dy
+ * and dx in shared memory with cp.async while the current row is reduced
+ * (rows of up to 2048 columns; wider rows use 1).  Results are bit-identical. */
+GLC_API int glc_set_rmsnorm_variant(glc_ctx* ctx, int variant);
 /* Trainer (Llama semantics): 1 computes the SwiGLU forward in the gate/up
  * GEMM's epilogue, 0 (default, faster on B200 at the TinyLlama shape) runs it
  * as its own kernel after the GEMM (diagnostics; no reference counterpart).

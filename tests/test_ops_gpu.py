@@ -55,6 +55,35 @@ def test_rmsnorm_bwd(ctx, orc, rows, cols, full):
     assert np.max(np.abs(bdxr.numpy() - out_dx) / (np.abs(out_dx) + 1e-30)) <= 2.0**-11
 
 
+@pytest.mark.unvalidated
+@pytest.mark.parametrize("full,acc", [(0, 0), (1, 1), (1, 0)])
+@pytest.mark.parametrize("rows,cols", [(5, 128), (300, 512), (4096, 2048), (1000, 2052)])
+def test_rmsnorm_bwd_pipelined_bit_identical(ctx, rows, cols, full, acc):
+    """glc_set_rmsnorm_variant(2) (cp.async-pipelined rows) returns the same
+    bits as the row-by-row kernel; 2052 columns fall back to it."""
+    r = rng(rows + cols + full)
+    x = r.standard_normal((rows, cols), dtype=np.float32)
+    w = (1 + 0.1 * r.standard_normal(cols)).astype(np.float32)
+    g = r.standard_normal((rows, cols), dtype=np.float32)
+    dx0 = r.standard_normal((rows, cols), dtype=np.float32)
+    dw0 = r.standard_normal(cols).astype(np.float32)
+    rms = np.sqrt((x.astype(np.float64) ** 2).mean(1) + 1e-5).astype(np.float32)
+    outs = []
+    try:
+        for variant in (1, 2):
+            ctx.call("glc_set_rmsnorm_variant", variant)
+            bx, bw, brms, bg = ctx.from_numpy(x), ctx.from_numpy(w), ctx.from_numpy(rms), ctx.from_numpy(g)
+            bdx, bdw, bdxr = ctx.from_numpy(dx0), ctx.from_numpy(dw0), ctx.empty((rows, cols))
+            ctx.call("glc_rmsnorm_bwd", bx.ptr, bw.ptr, brms.ptr, bg.ptr, bdx.ptr, bdxr.ptr, bdw.ptr, rows, cols, full,
+                     acc, 1)
+            ctx.sync()
+            outs.append([a.numpy().view(np.uint32) for a in (bdx, bdxr, bdw)])
+    finally:
+        ctx.call("glc_set_rmsnorm_variant", 0)
+    for a, b in zip(*outs):
+        assert np.array_equal(a, b)
+
+
 def test_rmsnorm_simplified_matches_reference_formula(ctx):
     """Reference-mode backward is exactly dx = dy*w/rms, dw = sum dy*x/rms (trainer.go:186-198)."""
     rows, cols = 64, 128
