@@ -288,6 +288,14 @@ int glc_set_fused_swiglu(glc_ctx* ctx, int on) {
   return GLC_OK;
 }
 
+int glc_set_quant_path(glc_ctx* ctx, int path) {
+  if (!ctx) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  if (path < 0 || path > 2) return c->fail(GLC_ERR_INVALID, "set_quant_path: path must be 0, 1 or 2");
+  c->quant_path = path;
+  return GLC_OK;
+}
+
 int glc_set_rmsnorm_variant(glc_ctx* ctx, int variant) {
   if (!ctx) return GLC_ERR_INVALID;
   Context* c = C_(ctx);

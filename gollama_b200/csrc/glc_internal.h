@@ -34,6 +34,7 @@ struct Context {
   bool fuse_swiglu = false;            // trainer: SwiGLU forward in the gate/up GEMM epilogue (Llama semantics)
   int attn_split = 0;                  // dK/dV CTAs per KV head: 0 automatic, else a divisor of the group
   int rmsnorm_variant = 0;             // RMSNorm backward: 0 automatic (row per iteration), 1 same, 2 pipelined loads
+  int quant_path = 0;                  // dX through a stored weight: 0 automatic (= 1), 1 dequantize + GEMM, 2 fused
   EncodeTiledFn encode_fn = nullptr;
   // scratch workspace owned by the context (grown on demand, never shrunk)
   void* ws = nullptr;
@@ -162,6 +163,11 @@ long long gemm_sumsq_slots(long long M, long long N);
 // | tile ids] and returns true when that estimate beats the rotation
 // tile = cluster + i * clusters by at least 1 %; false: keep the rotation.
 bool gemm_tile_lists(int tiles0, int kb0, int tiles1, int kb1, int clusters, std::vector<int>* out);
+// dX[M, Kin] (+)= dY[M, Nout] . deq(W) with W [Nout][Kin] stored in a GGUF
+// format, decoded inside the GEMM's operand load (gemm_quant_fused.cu).
+bool quant_fused_supported(int type, int Kin);
+int gemm_quant_fused(Context* ctx, const float* dY, int ldy, const void* Wq, int type, float* dX, int ldx, int M,
+                     int Kin, int Nout, bool accumulate, cudaStream_t s);
 // Runs up to two independent GEMMs in one persistent launch (shared tile queue).
 int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t stream);
 int gemm_empty_k(Context* ctx, float* C, int ldc, int M, int N, bool accumulate, const float* R, int ldr,

@@ -11,7 +11,8 @@
 // pkg/tensor/grad.go:102-116, on the dequantized weight): one pass writes the
 // TF32-rounded weight into the context workspace (the quantized bytes are
 // read once, 0.53 to 1.06 B per element), then the tcgen05 GEMM runs with
-// the weight as its MN-major B operand.
+// the weight as its MN-major B operand; with glc_set_quant_path(ctx, 2) the
+// GEMM decodes the stored blocks itself (gemm_quant_fused.cu).
 #include "glc_internal.h"
 #include "quant_formats.cuh"
 #include "sm100.cuh"
@@ -83,6 +84,8 @@ int glc_linear_bwd_dx_q(glc_ctx* ctx, const float* dY, const void* Wq, int type,
   if (M < 0 || K <= 0 || N < 0) return c->fail(GLC_ERR_INVALID, "linear_bwd_dx_q: bad size");
   if (M == 0 || N == 0) return glc::gemm_tf32(c, {dY, N, false}, {nullptr, K, true}, dX, K, M, K, N, accumulate != 0,
                                               nullptr, 0, false, c->stream);
+  if (c->quant_path == 2 && type != GLC_QTYPE_F32 && glc::quant_fused_supported(type, K))
+    return glc::gemm_quant_fused(c, dY, N, Wq, type, dX, K, M, K, N, accumulate != 0, c->stream);
   const size_t n = static_cast<size_t>(N) * K;
   void* ws = nullptr;
   int rc = c->workspace(n * sizeof(float), &ws);

@@ -107,16 +107,18 @@ def case_attention(ctx, kind, iters, warmup, B=4, S=S):
 
 
 def case_quant_dx(ctx, qtype, iters, warmup, M=16384, K=D, N=F):
-    """dX [M, K] = dY [M, N] . deq(W) with W [N, K] stored as Q8_0 (8) or Q4_0 (2):
-    fp16 scales U(0.005, 0.02), random codes."""
+    """dX [M, K] = dY [M, N] . deq(W) with W [N, K] stored as Q8_0 (8), Q4_0 (2),
+    Q4_K (12) or Q6_K (14): fp16 scales U(0.005, 0.02), every other byte random."""
     r = np.random.default_rng(qtype)
-    nb = N * K // 32
-    scale = r.uniform(0.005, 0.02, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
-    codes = r.integers(0, 256, (nb, 32 if qtype == 8 else 16), dtype=np.uint8)
-    w = ctx.from_numpy(np.ascontiguousarray(np.concatenate([scale, codes], axis=1)).reshape(-1))
+    be, bb, halves = {8: (32, 34, [0]), 2: (32, 18, [0]), 12: (256, 144, [0, 2]), 14: (256, 210, [208])}[qtype]
+    nb = N * K // be
+    raw = r.integers(0, 256, (nb, bb), dtype=np.uint8)
+    for off in halves:
+        raw[:, off : off + 2] = r.uniform(0.005, 0.02, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    w = ctx.from_numpy(raw.reshape(-1))
     dy, dx = _rand(ctx, (M, N), 15), ctx.empty((M, K))
     ms = _time(ctx, lambda: ctx.call("glc_linear_bwd_dx_q", dy.ptr, w.ptr, qtype, dx.ptr, M, K, N, 0), iters, warmup)
-    name = "Q8_0" if qtype == 8 else "Q4_0"
+    name = {8: "Q8_0", 2: "Q4_0", 12: "Q4_K", 14: "Q6_K"}[qtype]
     return f"linear_bwd_dx_q {name} M={M} K={K} N={N}", ms, 2.0 * M * N * K / (ms * 1e-3) / 1e12, "TFLOP/s"
 
 
@@ -215,6 +217,8 @@ CASES = {
     "gateup_swiglu": case_gateup_swiglu,
     "quant_dx_q8_0": lambda c, i, w: case_quant_dx(c, 8, i, w),
     "quant_dx_q4_0": lambda c, i, w: case_quant_dx(c, 2, i, w),
+    "quant_dx_q4_k": lambda c, i, w: case_quant_dx(c, 12, i, w),
+    "quant_dx_q6_k": lambda c, i, w: case_quant_dx(c, 14, i, w),
     "rmsnorm_bwd": case_rmsnorm,
     "rmsnorm_fwd": case_rmsnorm_fwd,
     "optimizer": case_optimizer,
@@ -233,12 +237,15 @@ def main(argv=None):
                     help="attention backward: dK/dV CTAs per KV head (0 automatic, else a divisor of H/Hkv)")
     ap.add_argument("--rmsnorm-variant", type=int, default=0, choices=[0, 1, 2],
                     help="RMSNorm backward: 0 automatic, 1 row by row, 2 cp.async-pipelined rows")
+    ap.add_argument("--quant-path", type=int, default=0, choices=[0, 1, 2],
+                    help="quantized dX: 0 automatic, 1 dequantize + GEMM, 2 decode inside the GEMM")
     a = ap.parse_args(argv)
     names = sorted(CASES) if "all" in a.cases else a.cases
     with Context(0) as ctx:
         ctx.call("glc_set_gemm_variant", a.variant)
         ctx.call("glc_set_attention_split", a.attn_split)
         ctx.call("glc_set_rmsnorm_variant", a.rmsnorm_variant)
+        ctx.call("glc_set_quant_path", a.quant_path)
         for n in names:
             res = CASES[n](ctx, a.iters, a.warmup)
             for desc, ms, rate, unit in (res if isinstance(res, list) else [res]):

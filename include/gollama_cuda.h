@@ -157,7 +157,7 @@ GLC_API int glc_dequantize(glc_ctx* ctx, int type, const void* src, float* dst, 
  * quantized row by row: the dA loop of MatMulGrad (pkg/tensor/grad.go:102-116)
  * applied to the weight the reference dequantizes at load
  * (pkg/model/transformer.go:285-303).  Uses the context workspace for one
- * TF32-rounded fp32 copy of W. */
+ * TF32-rounded fp32 copy of W, or none on the fused path (glc_set_quant_path). */
 GLC_API int glc_linear_bwd_dx_q(glc_ctx* ctx, const float* dY, const void* Wq, int type, float* dX, int M, int K,
                                 int N, int accumulate);
 /* General strided form of the three above: C[M,N] (+)= A . B^T (+ R) where
@@ -182,6 +182,12 @@ GLC_API int glc_set_attention_split(glc_ctx* ctx, int nsplit);
  * and dx in shared memory with cp.async while the current row is reduced
  * (rows of up to 2048 columns; wider rows use 1).  Results are bit-identical. */
 GLC_API int glc_set_rmsnorm_variant(glc_ctx* ctx, int variant);
+/* glc_linear_bwd_dx_q's path (tuning; no reference counterpart): 0 automatic
+ * and 1 dequantize W into the workspace, then the CTA-pair GEMM; 2 decode the
+ * stored blocks inside the GEMM's operand load (no fp32 copy of W; F16 and
+ * the block formats with K a whole number of blocks, else path 1).  Both
+ * round W to TF32 the same way. */
+GLC_API int glc_set_quant_path(glc_ctx* ctx, int path);
 /* Trainer (Llama semantics): 1 computes the SwiGLU forward in the gate/up
  * GEMM's epilogue, 0 (default, faster on B200 at the TinyLlama shape) runs it
  * as its own kernel after the GEMM (diagnostics; no reference counterpart).

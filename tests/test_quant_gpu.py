@@ -88,3 +88,33 @@ def test_linear_bwd_dx_q(ctx, qtype, M, K, N, acc):
     ctx.call("glc_linear_bwd_dx_q", d_dy.ptr, d_w.ptr, qtype, d_dx.ptr, M, K, N, acc)
     ctx.sync()
     assert rel_fro(d_dx.numpy(), want) < TOL
+
+
+@pytest.mark.unvalidated
+@pytest.mark.parametrize("qtype", [F16, Q4_0, Q8_0, Q4_1, Q5_0, Q5_1, Q4_K, Q6_K])
+@pytest.mark.parametrize("M,K,N,acc", [(64, 256, 96, 0), (300, 512, 1376, 1), (512, 2048, 704, 0), (130, 768, 36, 1)])
+def test_linear_bwd_dx_q_fused_decode(ctx, qtype, M, K, N, acc):
+    """glc_set_quant_path(2): the blocks decoded inside the GEMM's operand load
+    give the oracle's dX within the TF32 bar and agree with the dequantize +
+    GEMM path (both round W to TF32 the same way)."""
+    r = np.random.default_rng(M + K + N + qtype + 1)
+    dy = r.standard_normal((M, N)).astype(np.float32)
+    dx0 = r.standard_normal((M, K)).astype(np.float32) if acc else np.zeros((M, K), np.float32)
+    data = sane_format_weight(qtype, N, K, 61 + qtype)
+    src = np.frombuffer(data, np.uint8).copy()
+    want = dx0.astype(np.float64).copy()
+    assert orc_lib().orcd_linear_bwd_dx_q(dy.astype(np.float64).ctypes.data_as(C.c_void_p),
+                                          src.ctypes.data_as(C.c_void_p), qtype, want.ctypes.data_as(C.c_void_p), M,
+                                          K, N) == 0
+    outs = []
+    try:
+        for path in (1, 2):
+            ctx.call("glc_set_quant_path", path)
+            d_dy, d_w, d_dx = ctx.from_numpy(dy), ctx.from_numpy(src), ctx.from_numpy(dx0)
+            ctx.call("glc_linear_bwd_dx_q", d_dy.ptr, d_w.ptr, qtype, d_dx.ptr, M, K, N, acc)
+            ctx.sync()
+            outs.append(d_dx.numpy())
+    finally:
+        ctx.call("glc_set_quant_path", 0)
+    assert rel_fro(outs[1], want) < TOL
+    assert rel_fro(outs[1], outs[0].astype(np.float64)) < 1e-6
