@@ -378,6 +378,318 @@ __global__ void __launch_bounds__(NT, 1)
   }
 }
 
+// ============================================================ forward, persistent
+// The same per-row arithmetic as attn_fwd_tc_kernel, with one CTA per SM
+// walking work items (query tile, batch, head) in the grid kernel's order
+// (longest rows first), items it = blockIdx.x + k * gridDim.x.  Every role
+// counts K/V tiles, S buffers and max exchanges across items, so the
+// pipelines never drain between items: the TMA warp fetches the next item's
+// Q (two Q buffers, released by q_empty once an item's score MMAs are done)
+// and K/V while the current item finishes, the score MMAs of the next item
+// start as soon as S buffers free up, and its P V accumulates into the other
+// of two O accumulators (o_full: an item's last P V finished; o_empty: the
+// math warps read O out) while the math warps write the current item's
+// output.  TMEM: S/P buffers at 0, 128, 256 and O at 384 + {0, HD}
+// (HD <= 64).  Results are bit-identical to the grid kernel.
+template <int HD>
+struct PFwdLayout {
+  static constexpr int Q = 128 * HD * 4, K = 128 * HD * 4, V = 128 * HD * 4;
+  static constexpr int OFF_K = 2 * Q, OFF_V = OFF_K + 2 * K, OFF_X = OFF_V + 2 * V;
+  static constexpr int OFF_BAR = OFF_X + 2 * 2 * 128 * 4;
+  static constexpr int BYTES = OFF_BAR + 512 + 1024;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int O_COL = 384;
+  static_assert(O_COL + 2 * HD <= TMEM_COLS, "two O accumulators must fit beside three S buffers");
+};
+
+struct FwdItem {
+  int h, b, qt;
+};
+__device__ __forceinline__ FwdItem fwd_item(int it, int H, int B, int n_qt) {
+  const int hb = H * B;
+  const int z = it / hb, rem = it - z * hb;
+  FwdItem w;
+  w.qt = n_qt - 1 - z;
+  w.b = rem / H;
+  w.h = rem - w.b * H;
+  return w;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(NT, 1)
+    attn_fwd_persist_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                            const __grid_constant__ CUtensorMap tmV, float* __restrict__ out, float* __restrict__ lse,
+                            int S, int B, int H, int Hkv, int n_qt, float scale_log2, int round_out, int* err) {
+  using L = PFwdLayout<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint64_t *q_full = bars, *q_empty = bars + 2, *k_full = bars + 4, *k_empty = bars + 6, *v_full = bars + 8,
+           *v_empty = bars + 10, *s_full = bars + 12, *p_full = bars + 15, *pv_done = bars + 18, *o_full = bars + 21,
+           *o_empty = bars + 23, *xchg = bars + 25, *drain = bars + 27, *drain_acc = bars + 28;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 29);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const Roles ro;
+  const int n_items = H * B * n_qt;
+  const int G = H / Hkv;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], MATH_THREADS);
+      mbar_init(&xchg[i], MATH_THREADS);
+    }
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], MATH_THREADS);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    mbar_init(drain_acc, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (ro.warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sQ = smem_u32(sm), sK = sQ + L::OFF_K, sV = sQ + L::OFF_V;
+
+  if (ro.warp == 0) {
+    if (ro.lane == 0) {
+      bool ok = true;
+      int armed_q[2] = {-1, -1}, armed_k[2] = {-1, -1}, armed_v[2] = {-1, -1};
+      int kv = 0, local = 0;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
+        const FwdItem w = fwd_item(it, H, B, n_qt);
+        const int kh = w.h / G, row_base = w.b * S;
+        const int qb = local & 1;
+        const uint32_t qph = (local >> 1) & 1;
+        if (!mbar_wait(&q_empty[qb], qph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx(&q_full[qb], L::Q);
+        tma_tile<HD, 128>(sm + qb * L::Q, &tmQ, &q_full[qb], w.h * HD, row_base + w.qt * 128);
+        armed_q[qb] = static_cast<int>(qph);
+        for (int j = 0; j <= w.qt; ++j, ++kv) {
+          const int st = kv & 1;
+          const uint32_t ph = (kv >> 1) & 1;
+          if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[st], L::K);
+          tma_tile<HD, 128>(sm + L::OFF_K + st * L::K, &tmK, &k_full[st], kh * HD, row_base + j * 128);
+          armed_k[st] = static_cast<int>(ph);
+          if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[st], L::V);
+          tma_tile<HD, 128>(sm + L::OFF_V + st * L::V, &tmV, &v_full[st], kh * HD, row_base + j * 128);
+          armed_v[st] = static_cast<int>(ph);
+        }
+      }
+      if (!ok) {
+        for (int st = 0; st < 2; ++st) {
+          if (armed_q[st] >= 0) mbar_drain(&q_full[st], static_cast<uint32_t>(armed_q[st]), err);
+          if (armed_k[st] >= 0) mbar_drain(&k_full[st], static_cast<uint32_t>(armed_k[st]), err);
+          if (armed_v[st] >= 0) mbar_drain(&v_full[st], static_cast<uint32_t>(armed_v[st]), err);
+        }
+      }
+    }
+  } else if (ro.warp == 1) {
+    if (ro.lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_tf32(128, 128, false, false);
+      bool ok = true, issued = false;
+      int sq = 0, local = 0;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
+        const FwdItem w = fwd_item(it, H, B, n_qt);
+        const int qb = local & 1;
+        if (!mbar_wait(&q_full[qb], (local >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        for (int j = 0; j <= w.qt; ++j, ++sq) {
+          const int sb = sq % 3, st = sq & 1;
+          if (sq >= 3 && !mbar_wait(&pv_done[sb], ((sq - 3) / 3) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(&k_full[st], (sq >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < HD / 8; ++kk)
+            umma_tf32(tmem + sb * 128, kdesc<128>(sQ + qb * L::Q, kk), kdesc<128>(sK + st * L::K, kk), idesc_s,
+                      kk > 0 ? 1u : 0u);
+          issued = true;
+          umma_commit(&k_empty[st]);
+          umma_commit(&s_full[sb]);
+        }
+        if (!ok) break;
+        umma_commit(&q_empty[qb]);  // this item's score MMAs no longer read Q[qb]
+      }
+      if (!ok && issued) {
+        umma_commit(drain);
+        mbar_drain(drain, 0, err);
+      }
+    }
+  } else if (ro.warp == ACC_WARP) {
+    if (ro.lane == 0) {
+      constexpr uint32_t idesc_o = umma_idesc_tf32(128, HD, false, true);
+      bool ok = true, issued = false;
+      int sq = 0, local = 0;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
+        const FwdItem w = fwd_item(it, H, B, n_qt);
+        const int ob = local & 1;
+        // O[ob] was read out by the math warps for item local - 2
+        if (!mbar_wait(&o_empty[ob], ((local >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int j = 0; j <= w.qt; ++j, ++sq) {
+          const int sb = sq % 3, st = sq & 1;
+          if (!mbar_wait(&p_full[sb], (sq / 3) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          if (!mbar_wait(&v_full[st], (sq >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 16; ++kk)
+            umma_tf32_ts(tmem + L::O_COL + ob * HD, tmem + sb * 128 + kk * 8, mdesc<128>(sV + st * L::V, kk), idesc_o,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+          issued = true;
+          umma_commit(&v_empty[st]);
+          umma_commit(&pv_done[sb]);
+        }
+        if (!ok) break;
+        umma_commit(&o_full[ob]);
+      }
+      if (!ok && issued) {
+        umma_commit(drain_acc);
+        mbar_drain(drain_acc, 0, err);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax
+    const int q = ro.quarter(), hf = ro.half();
+    const int r = q * 32 + ro.lane;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    float* xmax = reinterpret_cast<float*>(sm + L::OFF_X);
+    bool ok = true;
+    int sq = 0, xc = 0, local = 0;
+    for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
+      const FwdItem w = fwd_item(it, H, B, n_qt);
+      const int ob = local & 1;
+      const uint32_t o_col = L::O_COL + ob * HD;
+      const int q0 = w.qt * 128, row_base = w.b * S, row_abs = q0 + r;
+      const int n_kv = w.qt + 1;
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < n_kv; ++j, ++sq) {
+        const int sb = sq % 3;
+        WAIT_OR_BREAK(&s_full[sb], (sq / 3) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+        tc_fence_after();
+        const int k0 = j * 128 + hf * 64;
+        const uint32_t sa = lane_addr + sb * 128 + hf * 64;
+        uint32_t v[64];
+        tmem_ld_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(v + 0));
+        tmem_ld_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+        tmem_ld_wait();
+        if (j == w.qt || k0 + 64 > S) {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) {
+            const int key = k0 + e;
+            if (!(key < S && key <= row_abs)) v[e] = __float_as_uint(-INFINITY);
+          }
+        }
+        float mx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 64; ++e) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(v[e]));
+        const float m_half = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                   fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * scale_log2;
+        float* xs = xmax + (xc & 1) * 256;
+        xs[hf * 128 + r] = m_half;
+        mbar_arrive(&xchg[xc & 1]);
+        WAIT_OR_BREAK(&xchg[xc & 1], (xc >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+        const float m_tile = fmaxf(m_half, xs[(hf ^ 1) * 128 + r]);
+        ++xc;
+        const float m_new = (m_tile > m_used + 8.0f) ? m_tile : m_used;
+        const float alpha = exp2f(m_used - m_new);
+        float sum[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum[i] = 0.f;
+        const float m_sub = m_new == -INFINITY ? 0.f : m_new;
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+          const uint32_t pb = tf32_bits(fast_exp2(fmaf(__uint_as_float(v[e]), scale_log2, -m_sub)));
+          sum[e & 7] += __uint_as_float(pb);
+          v[e] = pb;
+        }
+        tmem_st_32x32b_x32(sa + 0, *reinterpret_cast<uint32_t(*)[32]>(v + 0));
+        tmem_st_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+        tmem_st_wait();
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+          // O may only be rescaled once this item's previous P V has finished
+          WAIT_OR_BREAK(&pv_done[(sq - 1) % 3], ((sq - 1) / 3) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = hf; c < HD / 32; c += 2) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(lane_addr + o_col + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st_32x32b_x32(lane_addr + o_col + c * 32, o);
+          }
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        mbar_arrive(&p_full[sb]);
+        l = l * alpha + (((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7])));
+        m_used = m_new;
+      }
+      if (!ok) break;
+      // total l of the row: the two halves' partial sums through the exchange
+      {
+        float* xs = xmax + (xc & 1) * 256;
+        xs[hf * 128 + r] = l;
+        mbar_arrive(&xchg[xc & 1]);
+        WAIT_OR_BREAK(&xchg[xc & 1], (xc >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+        l = hf == 0 ? l + xs[128 + r] : xs[r] + l;
+        ++xc;
+      }
+      WAIT_OR_BREAK(&o_full[ob], (local >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      float* orow = out + (static_cast<size_t>(row_base) + row_abs) * (static_cast<size_t>(H) * HD) + w.h * HD;
+#pragma unroll 1
+      for (int c = hf; c < HD / 32; c += 2) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_addr + o_col + c * 32, v);
+        tmem_ld_wait();
+        if (row_abs < S) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            float4 o4;
+            o4.x = __uint_as_float(v[4 * g + 0]) * inv;
+            o4.y = __uint_as_float(v[4 * g + 1]) * inv;
+            o4.z = __uint_as_float(v[4 * g + 2]) * inv;
+            o4.w = __uint_as_float(v[4 * g + 3]) * inv;
+            if (round_out) o4 = make_float4(round_tf32(o4.x), round_tf32(o4.y), round_tf32(o4.z), round_tf32(o4.w));
+            reinterpret_cast<float4*>(orow + c * 32)[g] = o4;
+          }
+        }
+      }
+      if (hf == 0 && row_abs < S) lse[(static_cast<size_t>(w.b) * H + w.h) * S + row_abs] = (m_used + log2f(l)) * LN2;
+      tc_fence_before();
+      mbar_arrive(&o_empty[ob]);  // O[ob] read out: the item after next may accumulate into it
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (ro.warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
 // ===================================================================== dK / dV
 // TMEM: two sets of {S^T [0,64), dP^T [64,128)} at cols 0 and 128, then K, V
 // (the A operands of S^T = K Q^T and dP^T = V dO^T), dV and dK, HD columns
@@ -1031,8 +1343,10 @@ template <int HD>
 int fwd_impl(Context* ctx, const float* q, int q_ld, const float* k, int k_ld, const float* v, int v_ld, float* o,
              float* lse, int B, int S, int H, int Hkv, bool round_out, cudaStream_t s) {
   using L = FwdLayout<HD>;
-  static bool done[8] = {false};
-  int rc = set_smem(ctx, attn_fwd_tc_kernel<HD>, L::BYTES, done);
+  static bool done[8] = {false}, done_p[8] = {false};
+  const bool persist = ctx->attn_fwd_variant == 2;
+  int rc = persist ? set_smem(ctx, attn_fwd_persist_kernel<HD>, PFwdLayout<HD>::BYTES, done_p)
+                   : set_smem(ctx, attn_fwd_tc_kernel<HD>, L::BYTES, done);
   if (rc) return rc;
   const int T = B * S;
   CUtensorMap tq, tk, tv;
@@ -1043,8 +1357,16 @@ int fwd_impl(Context* ctx, const float* q, int q_ld, const float* k, int k_ld, c
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
   const double causal = 0.5 * static_cast<double>(S) * (S + 1);
   ProfScope prof(ctx, PROF_ATTN_FWD, 2.0 * 2.0 * B * H * causal * HD, s);
-  attn_fwd_tc_kernel<HD><<<dim3(H, B, n_qt), NT, L::BYTES, s>>>(tq, tk, tv, o, lse, S, H, Hkv, n_qt, scale * LOG2E,
-                                                                   round_out ? 1 : 0, ctx->d_err);
+  if (persist) {
+    const long long items = static_cast<long long>(H) * B * n_qt;
+    if (items >= (1LL << 31)) return ctx->fail(GLC_ERR_INVALID, "attention_fwd: too many work items");
+    const int grid = static_cast<int>(items < ctx->num_sms ? items : ctx->num_sms);
+    attn_fwd_persist_kernel<HD><<<grid, NT, PFwdLayout<HD>::BYTES, s>>>(tq, tk, tv, o, lse, S, B, H, Hkv, n_qt,
+                                                                         scale * LOG2E, round_out ? 1 : 0, ctx->d_err);
+  } else {
+    attn_fwd_tc_kernel<HD><<<dim3(H, B, n_qt), NT, L::BYTES, s>>>(tq, tk, tv, o, lse, S, H, Hkv, n_qt, scale * LOG2E,
+                                                                     round_out ? 1 : 0, ctx->d_err);
+  }
   GLC_LAUNCH_CHECK(ctx, "attention_fwd (tcgen05)");
   return 0;
 }

@@ -237,6 +237,8 @@ def main(argv=None):
                     help="attention backward: dK/dV CTAs per KV head (0 automatic, else a divisor of H/Hkv)")
     ap.add_argument("--rmsnorm-variant", type=int, default=0, choices=[0, 1, 2],
                     help="RMSNorm backward: 0 automatic, 1 row by row, 2 cp.async-pipelined rows")
+    ap.add_argument("--attn-fwd-variant", type=int, default=0, choices=[0, 1, 2],
+                    help="attention forward: 0 automatic, 1 a CTA per query tile, 2 persistent CTAs")
     ap.add_argument("--quant-path", type=int, default=0, choices=[0, 1, 2],
                     help="quantized dX: 0 automatic, 1 dequantize + GEMM, 2 decode inside the GEMM")
     a = ap.parse_args(argv)
@@ -246,6 +248,7 @@ def main(argv=None):
         ctx.call("glc_set_attention_split", a.attn_split)
         ctx.call("glc_set_rmsnorm_variant", a.rmsnorm_variant)
         ctx.call("glc_set_quant_path", a.quant_path)
+        ctx.call("glc_set_attention_fwd_variant", a.attn_fwd_variant)
         for n in names:
             res = CASES[n](ctx, a.iters, a.warmup)
             for desc, ms, rate, unit in (res if isinstance(res, list) else [res]):

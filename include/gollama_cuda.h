@@ -188,6 +188,12 @@ GLC_API int glc_set_rmsnorm_variant(glc_ctx* ctx, int variant);
  * the block formats with K a whole number of blocks, else path 1).  Both
  * round W to TF32 the same way. */
 GLC_API int glc_set_quant_path(glc_ctx* ctx, int path);
+/* Attention forward kernel (tuning; no reference counterpart): 0 automatic and
+ * 1 one CTA per (query tile, batch, head); 2 one persistent CTA per SM walking
+ * those items with its pipelines running across them (the next item's loads
+ * and score products overlap the current item's last tiles and output).
+ * Results are bit-identical. */
+GLC_API int glc_set_attention_fwd_variant(glc_ctx* ctx, int variant);
 /* Trainer (Llama semantics): 1 computes the SwiGLU forward in the gate/up
  * GEMM's epilogue, 0 (default, faster on B200 at the TinyLlama shape) runs it
  * as its own kernel after the GEMM (diagnostics; no reference counterpart).

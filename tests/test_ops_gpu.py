@@ -212,6 +212,32 @@ def test_attention_fwd_bwd(ctx, orc, B, S, H, Hkv, hd):
     assert max(errs) < ATTN_TOL, errs
 
 
+@pytest.mark.unvalidated
+@pytest.mark.parametrize("B,S,H,Hkv,hd", [(1, 128, 2, 1, 64), (2, 300, 4, 2, 64), (4, 1024, 32, 4, 64),
+                                          (3, 257, 3, 3, 32), (1, 2048, 8, 8, 64)])
+def test_attention_fwd_persistent_bit_identical(ctx, B, S, H, Hkv, hd):
+    """glc_set_attention_fwd_variant(2) (one persistent CTA per SM, pipelines
+    running across work items) returns the grid kernel's O and LSE bit for bit."""
+    T = B * S
+    r = rng(T + H + hd)
+    q = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
+    k = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    v = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    bq, bk, bv = ctx.from_numpy(q), ctx.from_numpy(k), ctx.from_numpy(v)
+    outs = []
+    try:
+        for variant in (1, 2):
+            ctx.call("glc_set_attention_fwd_variant", variant)
+            bo, blse = ctx.empty((T, H * hd)), ctx.empty((B, H, S))
+            ctx.call("glc_attention_fwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, B, S, H, Hkv, hd, 0)
+            ctx.sync()
+            outs.append((bo.numpy().view(np.uint32), blse.numpy().view(np.uint32)))
+    finally:
+        ctx.call("glc_set_attention_fwd_variant", 0)
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert np.array_equal(outs[0][1], outs[1][1])
+
+
 @pytest.mark.parametrize("nsplit", [1, 2, 4, 3])
 def test_attention_bwd_group_splits(ctx, orc, nsplit):
     """dK/dV with the 4 query heads of each KV head over 1, 2 or 4 CTAs (3 is
