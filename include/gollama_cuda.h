@@ -390,7 +390,9 @@ GLC_API int glc_state_read(const char* path, const glc_train_config* cfg, int* s
                            float* m, float* v, int64_t n);
 /* Trainer.SaveCheckpoint on the device-resident parameters: writes
  * <dir>/checkpoint_<step>.bin (trainer.go:555) in the text format, the path
- * is copied to path_out when it is not NULL.  Waits for the queued steps. */
+ * is copied to path_out when it is not NULL.  Waits for the queued steps.
+ * With data parallelism every rank holds the same parameters and state: call
+ * the save functions on one rank; every rank may load the same state file. */
 GLC_API int glc_trainer_save_checkpoint(glc_trainer* t, const char* dir, char* path_out, size_t path_cap);
 /* Binary resume of a trainer: parameters, m, v and both step counters. */
 GLC_API int glc_trainer_save_state(glc_trainer* t, const char* path);
