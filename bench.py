@@ -58,7 +58,14 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--light", action="store_true",
                     help="skip the CPU baseline, the TF32 peak measurement and the profiled steps (for ncu launch lists)")
+    ap.add_argument("--set", action="append", default=[], metavar="NAME=VALUE",
+                    help="kernel variant switch glc_set_NAME(ctx, VALUE) before the run, e.g. rmsnorm_variant=2, "
+                         "attention_fwd_variant=2 (repeatable; recorded in the JSON line's config)")
     a = ap.parse_args()
+    for kv in a.set:
+        name, _, val = kv.partition("=")
+        if not name.isidentifier() or not val.lstrip("-").isdigit():
+            ap.error(f"--set wants NAME=INTEGER, got {kv!r}")
     if a.light:
         a.no_cpu_baseline = True
         a.profile_steps = 0
@@ -307,6 +314,9 @@ def run_ours(args):
 
     ctx = Context(local)
     lib = ctx.lib
+    for kv in args.set:
+        name, _, val = kv.partition("=")
+        ctx.call(f"glc_set_{name}", int(val))
     pg = None
     if world > 1:
         import datetime
@@ -471,7 +481,8 @@ def run_ours(args):
         "vs_baseline": None,
         "dtype": "tf32",
         "data": "synthetic (seeded Zipf(1.1) token ids, random N(0,0.02) weights)",
-        "config": workload_config(world),
+        "config": dict(workload_config(world), **({"variants": dict(kv.split("=", 1) for kv in args.set)}
+                                                   if args.set else {})),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * T * 8, "d2h_bytes_per_step": 16,
                 "ms_per_step": t_e2e / K},
         "roofline": roofline,
