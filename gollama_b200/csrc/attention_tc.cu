@@ -1281,6 +1281,299 @@ __global__ void __launch_bounds__(NT, 1)
   }
 }
 
+// ================================================================ dQ, persistent
+// attn_bwd_dq_tc_kernel's arithmetic with one CTA per SM walking work items
+// (query tile, batch, head) in the grid kernel's order, counting K/V stages
+// and S/dP sets across items.  Q and dO get their own staging area (three
+// K/V stages instead of four), and the math warps move the next item's Q and
+// dO into TMEM as soon as they have finished the current item's last step
+// (whose S/dP products, the only readers of Q and dO in TMEM, have completed
+// by then), before writing the current item's dQ: the next item's products
+// overlap that output.  dQ alternates between two accumulators (dq_full: an
+// item's last dQ product finished; dq_empty: the math warps read it out).
+// TMEM: S/dP sets at 0 and 128, Q at 256, dO at 256 + HD, dQ at 256 + 2 HD
+// + {0, HD}.  Results are bit-identical to the grid kernel.
+template <int HD>
+struct PDqLayout {
+  static constexpr int Q = 128 * HD * 4, O = 128 * HD * 4;
+  static constexpr int KT = 64 * HD * 4;
+  static constexpr int STAGE = 3 * KT;  // K (K-major), K (MN-major), V (K-major)
+  static constexpr int NST = 3, NSET = 2;
+  static constexpr int OFF_QO = NST * STAGE;
+  static constexpr int OFF_BAR = OFF_QO + Q + O;
+  static constexpr int BYTES = OFF_BAR + 512 + 1024;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int Q_COL = 256, O_COL = 256 + HD, DQ_COL = 256 + 2 * HD;
+  static_assert(DQ_COL + 2 * HD <= TMEM_COLS, "two dQ accumulators must fit");
+};
+
+template <int HD>
+__global__ void __launch_bounds__(NT, 1)
+    attn_bwd_dq_persist_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmO,
+                               const __grid_constant__ CUtensorMap tmKk, const __grid_constant__ CUtensorMap tmKm,
+                               const __grid_constant__ CUtensorMap tmVk, const float* __restrict__ lse,
+                               const float* __restrict__ Dv, float* __restrict__ dq, int dq_ld, int S, int B, int H,
+                               int Hkv, int n_qt, float scale, float scale_log2, const float* __restrict__ rope_cos,
+                               const float* __restrict__ rope_sin, int* err) {
+  using L = PDqLayout<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint64_t *qo_full = bars, *qo_moved = bars + 1, *kv_full = bars + 2, *kv_empty = bars + 5, *s_full = bars + 8,
+           *p_full = bars + 10, *set_free = bars + 12, *dq_full = bars + 14, *dq_empty = bars + 16, *drain = bars + 18,
+           *drain_acc = bars + 19;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const Roles ro;
+  const int n_items = H * B * n_qt;
+  const int G = H / Hkv;
+  const int n_k64 = (S + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    mbar_init(qo_full, 1);
+    mbar_init(qo_moved, MATH_THREADS);
+    for (int i = 0; i < L::NST; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < L::NSET; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], MATH_THREADS);
+      mbar_init(&set_free[i], 1);
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_empty[i], MATH_THREADS);
+    }
+    mbar_init(drain, 1);
+    mbar_init(drain_acc, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (ro.warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t s0 = smem_u32(sm);
+
+  if (ro.warp == 0) {
+    if (ro.lane == 0) {
+      int armed[L::NST] = {-1, -1, -1};
+      int armed_qo = -1;
+      bool ok = true;
+      int kv = 0, local = 0;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
+        const FwdItem w = fwd_item(it, H, B, n_qt);
+        const int kh = w.h / G, q0 = w.qt * 128, row_base = w.b * S;
+        const int nk = min(n_k64, (q0 + 128) / 64);
+        // the staging area is free once the previous item's Q and dO are in TMEM
+        if (local > 0 && !mbar_wait(qo_moved, (local - 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(qo_full, L::Q + L::O);
+        tma_tile<HD, 128>(sm + L::OFF_QO, &tmQ, qo_full, w.h * HD, row_base + q0);
+        tma_tile<HD, 128>(sm + L::OFF_QO + L::Q, &tmO, qo_full, w.h * HD, row_base + q0);
+        armed_qo = local & 1;
+        for (int j = 0; j < nk; ++j, ++kv) {
+          const int st = kv % L::NST;
+          const uint32_t ph = (kv / L::NST) & 1;
+          if (!mbar_wait(&kv_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[st], L::STAGE);
+          uint8_t* base = sm + st * L::STAGE;
+          tma_tile<HD, 64>(base, &tmKk, &kv_full[st], kh * HD, row_base + j * 64);
+          tma_tile<HD, 64>(base + L::KT, &tmKm, &kv_full[st], kh * HD, row_base + j * 64);
+          tma_tile<HD, 64>(base + 2 * L::KT, &tmVk, &kv_full[st], kh * HD, row_base + j * 64);
+          armed[st] = static_cast<int>(ph);
+        }
+      }
+      if (!ok) {
+        if (armed_qo >= 0) mbar_drain(qo_full, static_cast<uint32_t>(armed_qo), err);
+        for (int st = 0; st < L::NST; ++st)
+          if (armed[st] >= 0) mbar_drain(&kv_full[st], static_cast<uint32_t>(armed[st]), err);
+      }
+    }
+  } else if (ro.warp == 1) {
+    if (ro.lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_tf32(128, 64, false, false);
+      bool ok = true, issued = false;
+      int kv = 0, local = 0;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
+        const FwdItem w = fwd_item(it, H, B, n_qt);
+        const int nk = min(n_k64, (w.qt * 128 + 128) / 64);
+        // this item's Q and dO are in TMEM
+        if (!mbar_wait(qo_moved, local & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        tc_fence_after();
+        for (int j = 0; j < nk; ++j, ++kv) {
+          const int st = kv % L::NST, ts = kv % L::NSET;
+          const uint32_t base = s0 + st * L::STAGE;
+          if (!mbar_wait(&kv_full[st], (kv / L::NST) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          if (!mbar_wait(&set_free[ts], ((kv / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < HD / 8; ++kk) {
+            umma_tf32_ts(tmem + ts * 128, tmem + L::Q_COL + kk * 8, kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
+            umma_tf32_ts(tmem + ts * 128 + 64, tmem + L::O_COL + kk * 8, kdesc<64>(base + 2 * L::KT, kk), idesc_s,
+                         kk > 0 ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit(&s_full[ts]);
+        }
+      }
+      if (!ok && issued) {
+        umma_commit(drain);
+        mbar_drain(drain, 0, err);
+      }
+    }
+  } else if (ro.warp == ACC_WARP) {
+    if (ro.lane == 0) {
+      constexpr uint32_t idesc_q = umma_idesc_tf32(128, HD, false, true);
+      bool ok = true, issued = false;
+      int kv = 0, local = 0;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
+        const FwdItem w = fwd_item(it, H, B, n_qt);
+        const int nk = min(n_k64, (w.qt * 128 + 128) / 64);
+        const int ob = local & 1;
+        // dQ[ob] was read out by the math warps for item local - 2
+        if (!mbar_wait(&dq_empty[ob], ((local >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int j = 0; j < nk; ++j, ++kv) {
+          const int ps = kv % L::NST, pts = kv % L::NSET;
+          const uint32_t base = s0 + ps * L::STAGE;
+          if (!mbar_wait(&p_full[pts], (kv / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_tf32_ts(tmem + L::DQ_COL + ob * HD, tmem + pts * 128 + kk * 8, mdesc<64>(base + L::KT, kk), idesc_q,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+          issued = true;
+          umma_commit(&set_free[pts]);
+          umma_commit(&kv_empty[ps]);
+        }
+        if (!ok) break;
+        umma_commit(&dq_full[ob]);
+      }
+      if (!ok && issued) {
+        umma_commit(drain_acc);
+        mbar_drain(drain_acc, 0, err);
+      }
+    }
+  } else {
+    const int q = ro.quarter(), hf = ro.half();
+    const int r = q * 32 + ro.lane;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    bool ok = true;
+    int kv = 0, local = 0;
+    // the first item's Q and dO rows -> TMEM
+    if (static_cast<int>(blockIdx.x) < n_items) {
+      if (__all_sync(0xffffffffu, mbar_wait(qo_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
+        tile_rows_to_tmem<HD>(sm + L::OFF_QO, r, lane_addr, L::Q_COL, 0, hf);
+        tile_rows_to_tmem<HD>(sm + L::OFF_QO + L::Q, r, lane_addr, L::O_COL, HD / 32, hf);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(qo_moved);
+      } else {
+        ok = false;
+      }
+    }
+    for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
+      const FwdItem w = fwd_item(it, H, B, n_qt);
+      const int q0 = w.qt * 128, row_base = w.b * S, qa = q0 + r;
+      const int nk = min(n_k64, (q0 + 128) / 64);
+      const size_t lrow = (static_cast<size_t>(w.b) * H + w.h) * S + (qa < S ? qa : 0);
+      const float lse2 = lse[lrow] * LOG2E, Dq = Dv[lrow];
+      for (int j = 0; j < nk; ++j, ++kv) {
+        const int ts = kv % L::NSET;
+        WAIT_OR_BREAK(&s_full[ts], (kv / L::NSET) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+        tc_fence_after();
+        const uint32_t sa = lane_addr + ts * 128 + hf * 32;
+        uint32_t sv[32], dpv[32];
+        tmem_ld_32x32b_x32(sa, sv);
+        tmem_ld_32x32b_x32(sa + 64, dpv);
+        tmem_ld_wait();
+        const int k_lo = j * 64 + hf * 32;
+        const float nDs = -Dq * scale;
+        if (k_lo + 32 <= q0 + 1 && q0 + 128 <= S) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float p = fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2));
+            sv[e] = tf32_bits(p * fmaf(__uint_as_float(dpv[e]), scale, nDs));
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int key = k_lo + e;
+            const bool valid = qa < S && key < S && key <= qa;
+            const float p = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2)) : 0.f;
+            sv[e] = tf32_bits(p * fmaf(__uint_as_float(dpv[e]), scale, nDs));
+          }
+        }
+        tmem_st_32x32b_x32(sa, sv);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[ts]);
+      }
+      if (!ok) break;
+      // the next item's Q and dO rows -> TMEM: every product of this item that
+      // reads them completed before its last s_full
+      if (it + static_cast<int>(gridDim.x) < n_items) {
+        WAIT_OR_BREAK(qo_full, (local + 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+        tile_rows_to_tmem<HD>(sm + L::OFF_QO, r, lane_addr, L::Q_COL, 0, hf);
+        tile_rows_to_tmem<HD>(sm + L::OFF_QO + L::Q, r, lane_addr, L::O_COL, HD / 32, hf);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(qo_moved);
+      }
+      const int ob = local & 1;
+      WAIT_OR_BREAK(&dq_full[ob], (local >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      tc_fence_after();
+      float* drow = dq + (static_cast<size_t>(row_base) + qa) * static_cast<size_t>(dq_ld) + w.h * HD;
+#pragma unroll 1
+      for (int cc = hf; cc < HD / 32; cc += 2) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_addr + L::DQ_COL + ob * HD + cc * 32, v);
+        tmem_ld_wait();
+        if (qa < S && rope_cos) {
+          const float4* cr = reinterpret_cast<const float4*>(rope_cos + static_cast<size_t>(qa) * (HD / 2) + cc * 16);
+          const float4* sr = reinterpret_cast<const float4*>(rope_sin + static_cast<size_t>(qa) * (HD / 2) + cc * 16);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const float4 c4 = cr[g], s4 = sr[g];
+            const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int p = 4 * g + e;
+              const float x0 = __uint_as_float(v[2 * p]), x1 = __uint_as_float(v[2 * p + 1]);
+              v[2 * p] = __float_as_uint(round_tf32(__fadd_rn(__fmul_rn(x0, cs[e]), __fmul_rn(x1, sn[e]))));
+              v[2 * p + 1] = __float_as_uint(round_tf32(__fadd_rn(__fmul_rn(-x0, sn[e]), __fmul_rn(x1, cs[e]))));
+            }
+          }
+        }
+        if (qa < S) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            reinterpret_cast<float4*>(drow + cc * 32)[g] =
+                make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]), __uint_as_float(v[4 * g + 2]),
+                            __uint_as_float(v[4 * g + 3]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&dq_empty[ob]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (ro.warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
 // D[b,h,s] = sum_d dO * O.  HD/4 lanes per (token, head) row, one float4 of
 // each operand per lane, 32/(HD/4) rows per warp, one row group per warp.
 template <int HD>
@@ -1376,9 +1669,12 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
              float* partial, int B, int S, int H, int Hkv, bool round_dv, const float* rope_cos,
              const float* rope_sin, cudaStream_t s) {
   const float *q = io.q, *k = io.k, *v = io.v;
-  static bool done_g[8] = {false}, done_q[8] = {false};
+  static bool done_g[8] = {false}, done_q[8] = {false}, done_pq[8] = {false};
+  const bool dq_persist = ctx->attn_dq_variant == 2;
   int rc = set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD>, DkdvLayout<HD>::BYTES, done_g);
-  if (!rc) rc = set_smem(ctx, attn_bwd_dq_tc_kernel<HD>, DqLayout<HD>::BYTES, done_q);
+  if (!rc)
+    rc = dq_persist ? set_smem(ctx, attn_bwd_dq_persist_kernel<HD>, PDqLayout<HD>::BYTES, done_pq)
+                    : set_smem(ctx, attn_bwd_dq_tc_kernel<HD>, DqLayout<HD>::BYTES, done_q);
   if (rc) return rc;
   const int T = B * S, G = H / Hkv;
   CUtensorMap tQk64, tQm64, tOk64, tOm64, tK128, tV128, tQ128, tO128, tKk64, tKm64, tVk64;
@@ -1436,9 +1732,18 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     GLC_LAUNCH_CHECK(ctx, "attention_bwd group sum");
   }
   const int n_qt = (S + 127) / 128;
-  attn_bwd_dq_tc_kernel<HD><<<dim3(H, B, n_qt), NT, DqLayout<HD>::BYTES, s>>>(
-      tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,
-      rope_sin, ctx->d_err);
+  if (dq_persist) {
+    const long long items = static_cast<long long>(H) * B * n_qt;
+    if (items >= (1LL << 31)) return ctx->fail(GLC_ERR_INVALID, "attention_bwd: too many work items");
+    const int grid = static_cast<int>(items < ctx->num_sms ? items : ctx->num_sms);
+    attn_bwd_dq_persist_kernel<HD><<<grid, NT, PDqLayout<HD>::BYTES, s>>>(
+        tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, B, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,
+        rope_sin, ctx->d_err);
+  } else {
+    attn_bwd_dq_tc_kernel<HD><<<dim3(H, B, n_qt), NT, DqLayout<HD>::BYTES, s>>>(
+        tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,
+        rope_sin, ctx->d_err);
+  }
   GLC_LAUNCH_CHECK(ctx, "attention_bwd dq (tcgen05)");
   return 0;
 }

@@ -34,6 +34,7 @@ struct Context {
   bool fuse_swiglu = false;            // trainer: SwiGLU forward in the gate/up GEMM epilogue (Llama semantics)
   int attn_split = 0;                  // dK/dV CTAs per KV head: 0 automatic, else a divisor of the group
   int rmsnorm_variant = 0;             // RMSNorm backward: 0 automatic (row per iteration), 1 same, 2 pipelined loads
+  int attn_dq_variant = 0;             // attention backward dQ: 0 automatic (= 1), 1 a CTA per query tile, 2 persistent
   int attn_fwd_variant = 0;            // attention forward: 0 automatic (= 1), 1 a CTA per query tile, 2 persistent
   int quant_path = 0;                  // dX through a stored weight: 0 automatic (= 1), 1 dequantize + GEMM, 2 fused
   EncodeTiledFn encode_fn = nullptr;

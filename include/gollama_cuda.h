@@ -194,6 +194,10 @@ GLC_API int glc_set_quant_path(glc_ctx* ctx, int path);
  * and score products overlap the current item's last tiles and output).
  * Results are bit-identical. */
 GLC_API int glc_set_attention_fwd_variant(glc_ctx* ctx, int variant);
+/* The same choice for the attention backward's dQ kernel: 2 walks its
+ * (query tile, batch, head) items persistently, moving the next item's Q and
+ * dO into TMEM while the current item's dQ is written.  Bit-identical. */
+GLC_API int glc_set_attention_dq_variant(glc_ctx* ctx, int variant);
 /* Trainer (Llama semantics): 1 computes the SwiGLU forward in the gate/up
  * GEMM's epilogue, 0 (default, faster on B200 at the TinyLlama shape) runs it
  * as its own kernel after the GEMM (diagnostics; no reference counterpart).

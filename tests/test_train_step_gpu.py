@@ -184,3 +184,33 @@ def test_clip_norm_covers_every_gradient_once(ctx, shape):
                 has[p.offset : p.offset + p.shape[0] * p.shape[1]] = True
         ref = float(np.sqrt(np.sum(g[has] ** 2)))
         assert abs(norm - ref) <= 1e-10 * ref, (s, norm, ref)
+
+
+VARIANTS = ["glc_set_attention_fwd_variant", "glc_set_attention_dq_variant", "glc_set_rmsnorm_variant"]
+
+
+@pytest.mark.unvalidated
+@pytest.mark.parametrize("shape", [syn.TINY_LLAMA_MODE, syn.SMALL_LLAMA_MODE.with_(layers=2)], ids=lambda s: s.name)
+def test_opt_in_variants_step_bit_identical(ctx, shape):
+    """A whole step (RoPE in the dQ epilogue included) with the persistent
+    attention kernels and the pipelined RMSNorm backward equals the default
+    step bit for bit."""
+    params = syn.init_params(shape, 23)
+    inputs, targets = syn.batch(shape, 23)
+    out = []
+    try:
+        for v in (1, 2):
+            for name in VARIANTS:
+                ctx.call(name, v)
+            model = NewTrainableModel(config_for(shape, **STEP_HPARAMS), ctx)
+            model.set_params(params)
+            loss = NewTrainer(model).TrainStep(inputs, targets)
+            out.append((loss, model.get_grads(), model.get_params()))
+            model.close()
+    finally:
+        for name in VARIANTS:
+            ctx.call(name, 0)
+    (l1, g1, w1), (l2, g2, w2) = out
+    assert l1 == l2
+    assert np.array_equal(g1.view(np.uint32), g2.view(np.uint32))
+    assert np.array_equal(w1.view(np.uint32), w2.view(np.uint32))
