@@ -1,0 +1,256 @@
+"""Randomized simulation of the barrier protocols of the persistent attention
+kernels (attn_fwd_persist_kernel, attn_bwd_dq_persist_kernel in
+gollama_b200/csrc/attention_tc.cu).
+
+Each role (TMA producer, score-MMA issuer, accumulate-MMA issuer, math warps)
+is a generator transcribing the kernel's loops, the barrier each wait uses and
+the phase parity it computes.  Barriers follow mbarrier semantics: a phase
+completes when its arrival count is reached and its transaction bytes have
+landed, and a parity wait succeeds while the barrier's current phase parity
+differs from the one waited for.  TMA copies and tcgen05.commit arrivals
+complete later, in random order.  Every wait checks that it did not wake
+early, and every buffer reuse checks that its previous reader finished."""
+import random
+
+
+class Bar:
+    def __init__(self, name, count):
+        self.name, self.count, self.pending, self.P, self.tx = name, count, count, 0, 0
+
+    def arrive(self):
+        self.pending -= 1
+        self._maybe()
+
+    def expect_tx(self, n):
+        self.tx += n
+        self.arrive()
+
+    def complete_tx(self, n):
+        self.tx -= n
+        self._maybe()
+
+    def _maybe(self):
+        assert self.pending >= 0, self.name
+        if self.pending == 0 and self.tx == 0:
+            self.P += 1
+            self.pending = self.count
+
+    def ready(self, parity):
+        return (self.P & 1) != parity
+
+
+def _wait(bar, parity, use):
+    while not bar.ready(parity):
+        yield
+    assert bar.P >= use + 1, (bar.name, bar.P, use)  # woke for the intended phase, not an earlier one
+
+
+def _drive(roles, events, rnd, cap=2_000_000):
+    live = dict(roles)
+    for _ in range(cap):
+        if not live and not events:
+            return
+        if events and (not live or rnd.random() < 0.5):
+            events.pop(rnd.randrange(len(events)))()
+        else:
+            name = rnd.choice(list(live))
+            try:
+                next(live[name])
+            except StopIteration:
+                del live[name]
+    raise AssertionError("deadlock")
+
+
+def forward(H, B, n_qt, grid, cta, seed):
+    rnd = random.Random(seed)
+    items = list(range(cta, H * B * n_qt, grid))
+    qt_of = lambda it: n_qt - 1 - it // (H * B)
+    bars = {(n, i): Bar(f"{n}{i}", 1) for n, k in [("q_full", 2), ("q_empty", 2), ("k_full", 2), ("k_empty", 2),
+                                                       ("v_full", 2), ("v_empty", 2), ("s_full", 3), ("p_full", 3),
+                                                       ("pv_done", 3), ("o_full", 2), ("o_empty", 2), ("xchg", 2)]
+            for i in range(k)}
+    b = lambda n, i: bars[(n, i)]
+    ev = []
+    st = {"S": [None] * 3, "O": [None] * 2, "pv": set(), "epi": set(), "sdone": set()}
+
+    def tma():
+        kv = 0
+        for local, it in enumerate(items):
+            qb = local & 1
+            yield from _wait(b("q_empty", qb), ((local >> 1) & 1) ^ 1, (local >> 1) - 1)
+            assert local < 2 or (local - 2) in st["sdone"]
+            b("q_full", qb).expect_tx(1)
+            ev.append(lambda qb=qb: b("q_full", qb).complete_tx(1))
+            for _ in range(qt_of(it) + 1):
+                s_, ph = kv & 1, (kv >> 1) & 1
+                yield from _wait(b("k_empty", s_), ph ^ 1, (kv >> 1) - 1)
+                b("k_full", s_).expect_tx(1)
+                ev.append(lambda s_=s_: b("k_full", s_).complete_tx(1))
+                yield from _wait(b("v_empty", s_), ph ^ 1, (kv >> 1) - 1)
+                assert kv < 2 or (kv - 2) in st["pv"]
+                b("v_full", s_).expect_tx(1)
+                ev.append(lambda s_=s_: b("v_full", s_).complete_tx(1))
+                kv += 1
+
+    def smma():
+        sq = 0
+        for local, it in enumerate(items):
+            qb = local & 1
+            yield from _wait(b("q_full", qb), (local >> 1) & 1, local >> 1)
+            for _ in range(qt_of(it) + 1):
+                sb, s_ = sq % 3, sq & 1
+                if sq >= 3:
+                    yield from _wait(b("pv_done", sb), ((sq - 3) // 3) & 1, (sq - 3) // 3)
+                    assert (sq - 3) in st["pv"]
+                yield from _wait(b("k_full", s_), (sq >> 1) & 1, sq >> 1)
+                st["S"][sb] = sq
+                ev.append(lambda s_=s_: b("k_empty", s_).arrive())
+                ev.append(lambda sb=sb: b("s_full", sb).arrive())
+                sq += 1
+
+            def qdone(qb=qb, local=local):
+                st["sdone"].add(local)
+                b("q_empty", qb).arrive()
+            ev.append(qdone)
+
+    def acc():
+        sq = 0
+        for local, it in enumerate(items):
+            ob = local & 1
+            yield from _wait(b("o_empty", ob), ((local >> 1) & 1) ^ 1, (local >> 1) - 1)
+            assert local < 2 or (local - 2) in st["epi"]
+            st["O"][ob] = local
+            for _ in range(qt_of(it) + 1):
+                sb, s_ = sq % 3, sq & 1
+                yield from _wait(b("p_full", sb), (sq // 3) & 1, sq // 3)
+                yield from _wait(b("v_full", s_), (sq >> 1) & 1, sq >> 1)
+                assert st["S"][sb] == sq
+
+                def done(s_=s_, sb=sb, sq=sq):
+                    st["pv"].add(sq)
+                    b("v_empty", s_).arrive()
+                    b("pv_done", sb).arrive()
+                ev.append(done)
+                sq += 1
+            ev.append(lambda ob=ob: b("o_full", ob).arrive())
+
+    def math():
+        sq = xc = 0
+        for local, it in enumerate(items):
+            ob = local & 1
+            for j in range(qt_of(it) + 1):
+                sb = sq % 3
+                yield from _wait(b("s_full", sb), (sq // 3) & 1, sq // 3)
+                assert st["S"][sb] == sq
+                b("xchg", xc & 1).arrive()
+                yield from _wait(b("xchg", xc & 1), (xc >> 1) & 1, xc >> 1)
+                xc += 1
+                if j > 0 and rnd.random() < 0.5:  # the row max grew: O is rescaled
+                    yield from _wait(b("pv_done", (sq - 1) % 3), ((sq - 1) // 3) & 1, (sq - 1) // 3)
+                    assert (sq - 1) in st["pv"] and st["O"][ob] == local
+                b("p_full", sb).arrive()
+                sq += 1
+            b("xchg", xc & 1).arrive()
+            yield from _wait(b("xchg", xc & 1), (xc >> 1) & 1, xc >> 1)
+            xc += 1
+            yield from _wait(b("o_full", ob), (local >> 1) & 1, local >> 1)
+            assert st["O"][ob] == local
+            st["epi"].add(local)
+            b("o_empty", ob).arrive()
+
+    _drive({"tma": tma(), "smma": smma(), "acc": acc(), "math": math()}, ev, rnd)
+
+
+def dq(H, B, n_qt, S, grid, cta, seed):
+    rnd = random.Random(seed)
+    items = list(range(cta, H * B * n_qt, grid))
+    n_k64 = (S + 63) // 64
+    nk_of = lambda it: min(n_k64, ((n_qt - 1 - it // (H * B)) * 128 + 128) // 64)
+    bars = {(n, i): Bar(f"{n}{i}", 1) for n, k in [("qo_full", 1), ("qo_moved", 1), ("kv_full", 3),
+                                                       ("kv_empty", 3), ("s_full", 2), ("p_full", 2),
+                                                       ("set_free", 2), ("dq_full", 2), ("dq_empty", 2)]
+            for i in range(k)}
+    b = lambda n, i=0: bars[(n, i)]
+    ev = []
+    st = {"tmem_qo": None, "staging": None, "s": set(), "dq": set(), "epi": set(), "buf": [None, None]}
+
+    def tma():
+        kv = 0
+        for local, it in enumerate(items):
+            if local > 0:
+                yield from _wait(b("qo_moved"), (local - 1) & 1, local - 1)
+
+            def land(local=local):
+                st["staging"] = local
+                b("qo_full").complete_tx(1)
+            b("qo_full").expect_tx(1)
+            ev.append(land)
+            for _ in range(nk_of(it)):
+                s_, ph = kv % 3, (kv // 3) & 1
+                yield from _wait(b("kv_empty", s_), ph ^ 1, kv // 3 - 1)
+                assert kv < 3 or (kv - 3) in st["dq"]
+                b("kv_full", s_).expect_tx(1)
+                ev.append(lambda s_=s_: b("kv_full", s_).complete_tx(1))
+                kv += 1
+
+    def smma():
+        kv = 0
+        for local, it in enumerate(items):
+            yield from _wait(b("qo_moved"), local & 1, local)
+            for _ in range(nk_of(it)):
+                s_, ts = kv % 3, kv % 2
+                yield from _wait(b("kv_full", s_), (kv // 3) & 1, kv // 3)
+                yield from _wait(b("set_free", ts), ((kv // 2) & 1) ^ 1, kv // 2 - 1)
+                assert (kv < 2 or (kv - 2) in st["dq"]) and st["tmem_qo"] == local
+
+                def done(ts=ts, kv=kv):
+                    st["s"].add(kv)
+                    b("s_full", ts).arrive()
+                ev.append(done)
+                kv += 1
+
+    def acc():
+        kv = 0
+        for local, it in enumerate(items):
+            ob = local & 1
+            yield from _wait(b("dq_empty", ob), ((local >> 1) & 1) ^ 1, (local >> 1) - 1)
+            assert local < 2 or (local - 2) in st["epi"]
+            st["buf"][ob] = local
+            for _ in range(nk_of(it)):
+                ps, pts = kv % 3, kv % 2
+                yield from _wait(b("p_full", pts), (kv // 2) & 1, kv // 2)
+
+                def done(pts=pts, ps=ps, kv=kv):
+                    st["dq"].add(kv)
+                    b("set_free", pts).arrive()
+                    b("kv_empty", ps).arrive()
+                ev.append(done)
+                kv += 1
+            ev.append(lambda ob=ob: b("dq_full", ob).arrive())
+
+    def math():
+        kv = 0
+        if items:
+            yield from _wait(b("qo_full"), 0, 0)
+            assert st["staging"] == 0
+            st["tmem_qo"] = 0
+            b("qo_moved").arrive()
+        for local, it in enumerate(items):
+            for _ in range(nk_of(it)):
+                ts = kv % 2
+                yield from _wait(b("s_full", ts), (kv // 2) & 1, kv // 2)
+                assert kv in st["s"]
+                b("p_full", ts).arrive()
+                kv += 1
+            if local + 1 < len(items):
+                yield from _wait(b("qo_full"), (local + 1) & 1, local + 1)
+                assert st["staging"] == local + 1 and all(k in st["s"] for k in range(kv))
+                st["tmem_qo"] = local + 1
+                b("qo_moved").arrive()
+            ob = local & 1
+            yield from _wait(b("dq_full", ob), (local >> 1) & 1, local >> 1)
+            assert st["buf"][ob] == local
+            st["epi"].add(local)
+            b("dq_empty", ob).arrive()
+
+    _drive({"tma": tma(), "smma": smma(), "acc": acc(), "math": math()}, ev, rnd)
