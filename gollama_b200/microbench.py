@@ -141,7 +141,7 @@ def case_swiglu(ctx, iters, warmup):
     return f"swiglu_bwd n={n}", ms, 20.0 * n / (ms * 1e-3) / 1e9, "GB/s"
 
 
-def case_rmsnorm(ctx, iters, warmup):
+def case_rmsnorm(ctx, iters, warmup, T=T):
     x, w, dy = _rand(ctx, (T, D), 10, tf32=False), _rand(ctx, (D,), 11, tf32=False), _rand(ctx, (T, D), 12, tf32=False)
     y, rms = ctx.empty((T, D)), ctx.empty((T,))
     ctx.call("glc_rmsnorm_fwd", x.ptr, w.ptr, y.ptr, rms.ptr, T, D, C.c_float(1e-5), 1)
@@ -180,13 +180,25 @@ def case_optimizer(ctx, iters, warmup, n=1 << 28):
             (f"adamw n={n} (clipped)", ms_a, 36.0 * n / (ms_a * 1e-3) / 1e9, "GB/s")]
 
 
-def case_ce(ctx, iters, warmup):
+def case_ce(ctx, iters, warmup, T=T):
     logits = _rand(ctx, (T, V), 13, 2.0, tf32=False)
     tg = ctx.from_numpy(np.random.default_rng(14).integers(0, V, T).astype(np.int64))
     logp, loss = ctx.empty((T,)), ctx.empty((1,))
     ms = _time(ctx, lambda: ctx.call("glc_softmax_ce", logits.ptr, tg.ptr, T, V, C.c_float(1.0 / T), logp.ptr,
                                      loss.ptr, 0, 0), iters, warmup)
     return f"softmax_ce {T}x{V}", ms, 4.0 * T * V / (ms * 1e-3) / 1e9, "GB/s"
+
+
+def case_config4_sweep(ctx, iters, warmup):
+    """The isolated backward-op sweep at its stated sizes: linear grads for M in
+    {4096, 16384, 32768} x (K, N) in {(2048, 2048), (2048, 5632), (5632, 2048)};
+    RMSNorm backward 32768 x 2048; causal attention backward B 4, 32 heads,
+    head_dim 64, seq 2048; softmax-CE backward on 32768 x 32000 logits N(0, 2)."""
+    out = list(case_linear_sweep(ctx, iters, warmup))
+    out.append(case_rmsnorm(ctx, iters, warmup, T=32768))
+    out.append(case_attention(ctx, "bwd", iters, warmup, B=4, S=2048))
+    out.append(case_ce(ctx, iters, warmup, T=32768))
+    return out
 
 
 CASES = {
@@ -220,6 +232,7 @@ CASES = {
     "quant_dx_q4_k": lambda c, i, w: case_quant_dx(c, 12, i, w),
     "quant_dx_q6_k": lambda c, i, w: case_quant_dx(c, 14, i, w),
     "rmsnorm_bwd": case_rmsnorm,
+    "config4_sweep": case_config4_sweep,
     "rmsnorm_fwd": case_rmsnorm_fwd,
     "optimizer": case_optimizer,
     "softmax_ce": case_ce,
