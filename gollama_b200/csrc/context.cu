@@ -304,6 +304,11 @@ int glc_set_attention_dq_variant(glc_ctx* ctx, int variant) {
   return GLC_OK;
 }
 
+int glc_diag_operand_swizzle(glc_ctx* ctx, const float* src, float* out) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::swizzle_probe(C_(ctx), src, out);
+}
+
 int glc_set_quant_path(glc_ctx* ctx, int path) {
   if (!ctx) return GLC_ERR_INVALID;
   Context* c = C_(ctx);

@@ -168,6 +168,9 @@ bool gemm_tile_lists(int tiles0, int kb0, int tiles1, int kb1, int clusters, std
 // dX[M, Kin] (+)= dY[M, Nout] . deq(W) with W [Nout][Kin] stored in a GGUF
 // format, decoded inside the GEMM's operand load (gemm_quant_fused.cu).
 bool quant_fused_supported(int type, int Kin);
+// Shared-memory image (1024 floats) of one MN-major 32 x 32 TMA box loaded
+// with SWIZZLE_128B_ATOM_32B from src (element (mn, k) at src[k * 32 + mn]).
+int swizzle_probe(Context* ctx, const float* src, float* out);
 int gemm_quant_fused(Context* ctx, const float* dY, int ldy, const void* Wq, int type, float* dX, int ldx, int M,
                      int Kin, int Nout, bool accumulate, cudaStream_t s);
 // Runs up to two independent GEMMs in one persistent launch (shared tile queue).

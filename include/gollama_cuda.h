@@ -188,6 +188,11 @@ GLC_API int glc_set_rmsnorm_variant(glc_ctx* ctx, int variant);
  * the block formats with K a whole number of blocks, else path 1).  Both
  * round W to TF32 the same way. */
 GLC_API int glc_set_quant_path(glc_ctx* ctx, int path);
+/* Diagnostic (no reference counterpart): out[1024] receives the shared-memory
+ * image of one 32 x 32 fp32 tile loaded by TMA as an MN-major tensor-core
+ * operand (element (mn, k) at src[k * 32 + mn], both 1024-float device
+ * buffers), the layout the fused dequantizing GEMM's producers reproduce. */
+GLC_API int glc_diag_operand_swizzle(glc_ctx* ctx, const float* src, float* out);
 /* Attention forward kernel (tuning; no reference counterpart): 0 automatic and
  * 1 one CTA per (query tile, batch, head); 2 one persistent CTA per SM walking
  * those items with its pipelines running across them (the next item's loads
