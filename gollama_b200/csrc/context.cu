@@ -304,6 +304,12 @@ int glc_set_attention_dq_variant(glc_ctx* ctx, int variant) {
   return GLC_OK;
 }
 
+int glc_set_tracing(glc_ctx* ctx, int on) {
+  if (!ctx) return GLC_ERR_INVALID;
+  C_(ctx)->tracing = on != 0;
+  return GLC_OK;
+}
+
 int glc_diag_operand_swizzle(glc_ctx* ctx, const float* src, float* out) {
   if (!ctx) return GLC_ERR_INVALID;
   return glc::swizzle_probe(C_(ctx), src, out);

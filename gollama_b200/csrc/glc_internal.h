@@ -11,6 +11,8 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "../../include/gollama_cuda.h"
 
 namespace glc {
@@ -36,7 +38,8 @@ struct Context {
   int rmsnorm_variant = 0;             // RMSNorm backward: 0 automatic (row per iteration), 1 same, 2 pipelined loads
   int attn_dq_variant = 0;             // attention backward dQ: 0 automatic (= 1), 1 a CTA per query tile, 2 persistent
   int attn_fwd_variant = 0;            // attention forward: 0 automatic (= 1), 1 a CTA per query tile, 2 persistent
-  int quant_path = 0;                  // dX through a stored weight: 0 automatic (= 1), 1 dequantize + GEMM, 2 fused
+  int quant_path = 0;
+  bool tracing = false;                // NVTX ranges around the phases of a training step                  // dX through a stored weight: 0 automatic (= 1), 1 dequantize + GEMM, 2 fused
   EncodeTiledFn encode_fn = nullptr;
   // scratch workspace owned by the context (grown on demand, never shrunk)
   void* ws = nullptr;
@@ -86,6 +89,20 @@ struct Context {
   }
   // Returns a device scratch buffer of at least `bytes` (stream-ordered use only).
   int workspace(size_t bytes, void** out);
+};
+
+// An NVTX range for the lifetime of the object when the context traces
+// (NVTX v3 is header-only: without a tool attached the calls return at once).
+struct TraceRange {
+  bool on;
+  TraceRange(const Context* c, const char* name) : on(c->tracing) {
+    if (on) nvtxRangePushA(name);
+  }
+  ~TraceRange() {
+    if (on) nvtxRangePop();
+  }
+  TraceRange(const TraceRange&) = delete;
+  TraceRange& operator=(const TraceRange&) = delete;
 };
 
 // Kernel classes of the profiler; work is FLOPs (GEMM, attention) or bytes.

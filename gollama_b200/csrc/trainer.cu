@@ -24,6 +24,7 @@
 #include <deque>
 #include <functional>
 #include <memory>
+#include <optional>
 #include <string>
 #include <unordered_set>
 #include <vector>
@@ -859,7 +860,12 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
       n.grad_round = nullptr;
     }
     tape->reset();
-    Node* logits = model->forward(*tape, in_dev, in_host, B, S);
+    TraceRange trace_step(ctx, "glc train_step");
+    Node* logits = nullptr;
+    {
+      TraceRange trace(ctx, "forward");
+      logits = model->forward(*tape, in_dev, in_host, B, S);
+    }
     if (row_cap < T) {
       cudaFree(row_logp);
       if (cudaMalloc(&row_logp, sizeof(float) * T) != cudaSuccess) throw StepError{GLC_ERR_NOMEM};
@@ -962,6 +968,8 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
           if (--bucket_pending[model->bucket_of[i]] == 0) launch_bucket(model->bucket_of[i]);
         });
     };
+    std::optional<TraceRange> trace_bwd;
+    trace_bwd.emplace(ctx, "loss + backward");
     if (model->llama) {
       // loss node with the CE GradFn; the kernel writes (p - onehot)/N over
       // the logits, which nothing reads afterwards.  With W data-parallel
@@ -992,7 +1000,9 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
         model->grad_live[i] = 1;
       }
     refresh_segments();
+    trace_bwd.reset();
     if (dp) {
+      TraceRange trace(ctx, "gradient sums (remaining buckets)");
       // buckets no GradFn completed (no consumer this step), then clipping
       // waits for every sum
       for (int b = 0; b < nb; ++b) launch_bucket(b);
@@ -1001,6 +1011,7 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
         throw StepError{GLC_ERR_CUDA};
     }
     if (nseg > 0) {
+      TraceRange trace(ctx, "clip + AdamW");
       // GradientClipping (optimizer.go:169-196) then AdamW.Step (:37-76)
       if (model->norm_fused) {
         // the GEMM epilogues' slots, then the gradients they did not reach
@@ -1024,6 +1035,7 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
         throw StepError{GLC_ERR_CUDA};
       model->scale_pending = true;
     }
+    TraceRange trace_sync(ctx, "loss readback (waits for the step)");
     if (cudaMemcpyAsync(loss_host, scalars, 16, cudaMemcpyDeviceToHost, ctx->stream) != cudaSuccess)
       throw StepError{GLC_ERR_CUDA};
     if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) throw StepError{GLC_ERR_CUDA};

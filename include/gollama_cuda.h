@@ -188,6 +188,11 @@ GLC_API int glc_set_rmsnorm_variant(glc_ctx* ctx, int variant);
  * the block formats with K a whole number of blocks, else path 1).  Both
  * round W to TF32 the same way. */
 GLC_API int glc_set_quant_path(glc_ctx* ctx, int path);
+/* Tracing (no reference counterpart): 1 marks the phases of each training
+ * step (forward, loss + backward, the remaining gradient sums, clip + AdamW,
+ * the loss readback) as NVTX ranges for a profiler's timeline; 0 (default)
+ * skips them.  Without a profiler attached the ranges cost nothing. */
+GLC_API int glc_set_tracing(glc_ctx* ctx, int on);
 /* Diagnostic (no reference counterpart): out[1024] receives the shared-memory
  * image of one 32 x 32 fp32 tile loaded by TMA as an MN-major tensor-core
  * operand (element (mn, k) at src[k * 32 + mn], both 1024-float device

@@ -186,6 +186,27 @@ def test_clip_norm_covers_every_gradient_once(ctx, shape):
         assert abs(norm - ref) <= 1e-10 * ref, (s, norm, ref)
 
 
+def test_tracing_ranges_leave_the_step_unchanged(ctx):
+    """glc_set_tracing(1) adds NVTX ranges around the step's phases (host
+    calls only): the step's results are the same bits."""
+    shape = syn.TINY_LLAMA_MODE
+    params = syn.init_params(shape, 29)
+    inputs, targets = syn.batch(shape, 29)
+    out = []
+    try:
+        for on in (0, 1):
+            ctx.call("glc_set_tracing", on)
+            model = NewTrainableModel(config_for(shape, **STEP_HPARAMS), ctx)
+            model.set_params(params)
+            loss = NewTrainer(model).TrainStep(inputs, targets)
+            out.append((loss, model.get_params()))
+            model.close()
+    finally:
+        ctx.call("glc_set_tracing", 0)
+    assert out[0][0] == out[1][0]
+    assert np.array_equal(out[0][1].view(np.uint32), out[1][1].view(np.uint32))
+
+
 VARIANTS = ["glc_set_attention_fwd_variant", "glc_set_attention_dq_variant", "glc_set_rmsnorm_variant"]
 
 
