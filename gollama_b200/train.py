@@ -47,8 +47,11 @@ class TrainConfig:
     InitStd: float = 0.02
     Seed: int = 42
     WorldSize: int = 1
-    # host-only fields (not in glc_train_config): SaveCheckpoint's directory (trainer.go:36,65)
+    # host-only fields (not in glc_train_config): logging and checkpoint cadence
+    # and SaveCheckpoint's directory (trainer.go:33-36, defaults :62-65)
     SavePath: str = "./checkpoints"
+    LogInterval: int = 10
+    SaveInterval: int = 1000
 
     def to_c(self) -> _lib.TrainConfigC:
         c = _lib.TrainConfigC()
@@ -184,6 +187,9 @@ class Trainer:
         self.h = h
         self.ctx.adopt(self, 0)
 
+    totalLoss = np.float32(0)  # loss tracking of TrainStep (trainer.go:441-442, :501-502)
+    lossCount = 0
+
     def TrainStep(self, inputs, targets) -> float:
         inp = np.ascontiguousarray(inputs, np.int64)
         tgt = np.ascontiguousarray(targets, np.int64)
@@ -196,7 +202,19 @@ class Trainer:
                                         C.byref(loss)),
             "glc_train_step",
         )
+        self.totalLoss = np.float32(self.totalLoss + np.float32(loss.value))
+        self.lossCount += 1
         return float(loss.value)
+
+    @property
+    def step(self) -> int:
+        return self.last_stats()[2]
+
+    def Train(self, dataLoader, log=print) -> None:
+        """Trainer.Train (trainer.go:508-551): TrainStep until MaxSteps, a log
+        line every LogInterval steps, SaveCheckpoint every SaveInterval steps
+        and once at the end."""
+        train_loop(self, dataLoader, log)
 
     def last_stats(self) -> tuple[float, float, int]:
         n, lr, st = C.c_double(), C.c_float(), C.c_int()
@@ -243,7 +261,86 @@ def NewTrainer(model: TrainableModel, cfg: TrainConfig | None = None) -> Trainer
     return Trainer(model, cfg)
 
 
+def train_loop(t, dataLoader, log=print) -> None:
+    """The loop of Trainer.Train (trainer.go:508-551) over any trainer with
+    TrainStep, step, last_stats, SaveCheckpoint, Config, totalLoss and
+    lossCount.  Unlike the reference, an empty batch raises instead of
+    looping forever (trainer.go:521-524 `continue`s without advancing)."""
+    import os
+    import time
+
+    cfg = t.Config
+    start = time.monotonic()
+    os.makedirs(cfg.SavePath, exist_ok=True)
+    log(f"Starting training: {cfg.MaxSteps} steps, batch_size={cfg.BatchSize}, lr={cfg.LearningRate:.2e}")
+    while t.step < cfg.MaxSteps:
+        inputs, targets = dataLoader.NextBatch()
+        if inputs is None:
+            raise ValueError("Train: the data loader returned an empty batch")
+        loss = t.TrainStep(inputs, targets)
+        step = t.step
+        if step % cfg.LogInterval == 0:
+            avg = np.float32(t.totalLoss) / np.float32(t.lossCount)
+            steps_per_sec = step / max(time.monotonic() - start, 1e-9)
+            lr = t.last_stats()[1]
+            log(f"step {step} | loss: {loss:.4f} (avg: {avg:.4f}) | lr: {lr:.2e} | {steps_per_sec:.1f} steps/sec")
+            t.totalLoss, t.lossCount = np.float32(0), 0
+        if step % cfg.SaveInterval == 0:
+            t.SaveCheckpoint()
+    log(f"Training complete! Final step: {t.step}")
+    t.SaveCheckpoint()
+
+
+class Dataset:
+    """Dataset (pkg/train/dataset.go:13-52): one token stream, training
+    examples are windows of BlockSize tokens and their shift by one."""
+
+    def __init__(self, tokens, blockSize: int):
+        self.Tokens = np.asarray(tokens, np.int64)
+        self.BlockSize = blockSize
+
+    def Len(self) -> int:
+        return 0 if len(self.Tokens) <= self.BlockSize else len(self.Tokens) - self.BlockSize
+
+    def GetBatch(self, batchSize: int, rng: np.random.Generator):
+        """Random window starts in [0, len - BlockSize - 1) (dataset.go:39-52);
+        (None, None) when the stream is too short.  Go's math/rand stream is
+        not reproduced: the starts come from numpy's generator, and a stream
+        of exactly BlockSize + 1 tokens returns (None, None) where Go's
+        rand.Intn(0) would panic."""
+        max_start = len(self.Tokens) - self.BlockSize - 1
+        if max_start <= 0:
+            return None, None
+        starts = rng.integers(0, max_start, batchSize)
+        idx = starts[:, None] + np.arange(self.BlockSize)[None, :]
+        return self.Tokens[idx], self.Tokens[idx + 1]
+
+
+def NewDataset(tokens, blockSize: int) -> Dataset:
+    return Dataset(tokens, blockSize)
+
+
+class DataLoader:
+    """DataLoader (dataset.go:55-75): batches of random windows from a seeded generator."""
+
+    def __init__(self, dataset: Dataset, batchSize: int, shuffle: bool = True, seed: int = 0):
+        self.Dataset, self.BatchSize, self.Shuffle = dataset, batchSize, shuffle
+        self.rng = np.random.default_rng(seed)
+
+    def NextBatch(self):
+        return self.Dataset.GetBatch(self.BatchSize, self.rng)
+
+
+def NewDataLoader(dataset: Dataset, batchSize: int, shuffle: bool = True, seed: int = 0) -> DataLoader:
+    return DataLoader(dataset, batchSize, shuffle, seed)
+
+
 __all__ = [
+    "Dataset",
+    "NewDataset",
+    "DataLoader",
+    "NewDataLoader",
+    "train_loop",
     "TrainConfig",
     "DefaultTrainConfig",
     "config_for",
