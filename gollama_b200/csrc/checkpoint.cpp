@@ -7,10 +7,11 @@
 //    (GOLLAMA_CKPT, step, vocab_size, hidden_size, num_layers, num_heads,
 //    intermediate_size), a `WEIGHTS` line, then one line per parameter in
 //    Params() order holding each float32 as Go's fmt `%v` prints it followed
-//    by one space.  The reference has no reader; the one here accepts exactly
-//    what the writer produces (and therefore what the reference produces), so
-//    a text checkpoint round-trips bit for bit (`%v` prints the shortest
-//    decimal that reads back as the same float32).
+//    by one space.  The reference has no reader; the one here reads what the
+//    writer (and therefore the reference) produces, so a text checkpoint
+//    round-trips bit for bit (`%v` prints the shortest decimal that reads back
+//    as the same float32).  Values may also be spelled as other plain
+//    decimals ("0.50", "1E5"), each read as the nearest float32.
 //
 //  - A binary resume file holding what the text format leaves out: AdamW's
 //    first and second moments and step counter, and the LR scheduler's step.
@@ -174,7 +175,9 @@ int format_go_float32(float v, char* out) {
   return static_cast<int>(p - out);
 }
 
-// The inverse on one token, accepting exactly the strings above.
+// The inverse on one token: the strings above, and any other plain decimal
+// (digits, at most one point, an optional exponent; a leading '-' only),
+// rounded to the nearest float32.
 bool parse_go_float32(const char* s, const char* e, float* v) {
   if (s >= e) return false;
   const size_t n = static_cast<size_t>(e - s);

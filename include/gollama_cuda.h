@@ -385,8 +385,9 @@ GLC_API int glc_trainer_last_launches(glc_trainer* t, uint64_t* n);
  * then per parameter in Params() order one line of its float32 values, each
  * printed as Go's fmt %v prints it and followed by one space.  The functions
  * below write that format byte for byte; the reference has no reader, and
- * glc_checkpoint_read accepts exactly that format (values read back bit for
- * bit; dimensions and per-parameter counts are checked against cfg).
+ * glc_checkpoint_read reads it back bit for bit (any other plain decimal
+ * spelling of a value is read as its nearest float32; dimensions and
+ * per-parameter counts are checked against cfg).
  *
  * The text format holds no optimizer state.  glc_state_write/read keep a
  * binary resume file with the parameters, AdamW's m and v, AdamW's step and

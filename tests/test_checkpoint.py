@@ -273,3 +273,45 @@ def test_text_checkpoint_across_blocks_and_threads(tmp_path):
     path.write_bytes(blob[: len(blob) - len(lines[-2]) - 1000])
     e = _err(ck.read_checkpoint, path, cfg)
     assert e.code == GLC_ERR_IO
+
+
+def test_text_reader_survives_random_mutations(tmp_path):
+    """Random byte mutations of a valid file end in an error status or, when
+    the mutated text is still a well-formed checkpoint of the model (the
+    reader takes any plain decimal spelling, not only %v's), in the values its
+    tokens spell; never a crash."""
+    n = ck.param_count(REF_CFG)
+    flat = (np.random.default_rng(12).standard_normal(n) * 0.02).astype(np.float32)
+    good = bytearray(expected_text(REF_CFG, 9, flat))
+    rng = np.random.default_rng(13)
+    path = tmp_path / "m.bin"
+    alphabet = b"0123456789.-+e \nNaInf"
+    accepted = 0
+    for _ in range(300):
+        b = bytearray(good)
+        for _ in range(int(rng.integers(1, 4))):
+            pos = int(rng.integers(0, len(b)))
+            op = rng.integers(0, 3)
+            if op == 0:
+                b[pos] = alphabet[int(rng.integers(0, len(alphabet)))]
+            elif op == 1:
+                del b[pos]
+            else:
+                b.insert(pos, alphabet[int(rng.integers(0, len(alphabet)))])
+        path.write_bytes(bytes(b))
+        try:
+            step, back = ck.read_checkpoint(path, REF_CFG)
+        except GlcError as e:
+            assert e.code in (GLC_ERR_IO, GLC_ERR_INVALID)
+            continue
+        accepted += 1
+        # every value is its token's float32 (Python parses through float64,
+        # which may round twice: within one float32 ulp)
+        toks = [t for line in bytes(b).split(b"\n")[8:] for t in line.split(b" ") if t]
+        assert len(toks) == n
+        ref = np.array([float(t.decode()) for t in toks], np.float64).astype(np.float32)
+        fin = np.isfinite(ref)
+        assert np.array_equal(np.isnan(back), np.isnan(ref))
+        diff = np.abs(back[fin].view(np.int32).astype(np.int64) - ref[fin].view(np.int32).astype(np.int64))
+        assert diff.max(initial=0) <= 1
+    assert accepted < 300  # most mutations are refused
