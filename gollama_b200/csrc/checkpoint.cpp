@@ -24,11 +24,12 @@
 //       32  i32 x 8  vocab, hidden, layers, heads, kv heads, intermediate,
 //                    max_seq_len, semantics
 //       64  i64      floats per arena (n)
-//       72  u64      hash of the payload (below)
+//       72  u64      hash of bytes 0..71 and of the payload (below)
 //       80  f32[n] parameters, f32[n] m, f32[n] v
-//    The hash runs over the payload as 64-bit words, h = (h ^ w) * P with the
-//    FNV-1a 64 offset basis and prime, so a truncated or altered file is
-//    refused before anything is written to the model.
+//    The hash runs over the header's first 72 bytes, then the payload, as
+//    64-bit words, h = (h ^ w) * P with the FNV-1a 64 offset basis and prime,
+//    so a truncated or altered file (step counters included) is refused
+//    before anything is written to the model.
 //
 // Both formats stream through fixed-size chunks, so saving or loading a model
 // never holds more than a few chunks of host memory.  Nothing here touches the
@@ -526,6 +527,7 @@ int state_write(const char* path, const StateInfo& info, const glc_train_config&
   // the hash goes in last: write a placeholder, then seek back
   bool ok = std::fwrite(head, 1, kStateHeader, f.f) == kStateHeader;
   uint64_t h = kHashBasis;
+  hash_words(h, head, 72);
   std::vector<float> chunk(static_cast<size_t>(std::min<int64_t>(kChunkFloats, std::max<int64_t>(n, 1))));
   for (int arena = 0; arena < 3 && ok; ++arena) {
     for (int64_t off = 0; off < n && ok; off += kChunkFloats) {
@@ -574,6 +576,7 @@ int state_read(const char* path, const glc_train_config& cfg, int64_t n, StateIn
   for (int pass = 0; pass < 2; ++pass) {
     if (std::fseek(f.f, kStateHeader, SEEK_SET) != 0) return host_fail(GLC_ERR_IO, where + "cannot seek");
     uint64_t h = kHashBasis;
+    hash_words(h, head, 72);
     for (int arena = 0; arena < 3; ++arena) {
       for (int64_t off = 0; off < n; off += kChunkFloats) {
         const int64_t k = std::min(kChunkFloats, n - off);
@@ -586,7 +589,7 @@ int state_read(const char* path, const glc_train_config& cfg, int64_t n, StateIn
         }
       }
     }
-    if (pass == 0 && h != get64(head + 72)) return host_fail(GLC_ERR_IO, where + "payload hash mismatch (corrupt file)");
+    if (pass == 0 && h != get64(head + 72)) return host_fail(GLC_ERR_IO, where + "hash mismatch (corrupt file)");
   }
   info->step = static_cast<int>(st);
   info->adam_step = static_cast<int>(ast);

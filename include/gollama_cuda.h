@@ -391,7 +391,7 @@ GLC_API int glc_trainer_last_launches(glc_trainer* t, uint64_t* n);
  *
  * The text format holds no optimizer state.  glc_state_write/read keep a
  * binary resume file with the parameters, AdamW's m and v, AdamW's step and
- * the LRScheduler's step, the model dimensions and a hash of the payload;
+ * the LRScheduler's step, the model dimensions and a hash of all of them;
  * reading checks all of them before anything is written to the model.
  *
  * Host buffers only, no context, no device (errors: glc_last_error(NULL)).

@@ -210,6 +210,10 @@ def test_state_refuses_corrupt_truncated_and_mismatched(tmp_path):
     flipped[80 + 4 * n + 123] ^= 0x10  # one bit of m
     e = read(flipped)
     assert e.code == GLC_ERR_IO and "hash" in str(e)
+    stepped = bytearray(blob)
+    stepped[16] ^= 1  # the trainer step: covered by the hash too
+    e = read(stepped)
+    assert e.code == GLC_ERR_IO and "hash" in str(e)
     assert read(blob[:-4]).code == GLC_ERR_IO
     assert read(blob + b"\0\0\0\0").code == GLC_ERR_IO
     assert read(b"GLCSTATX" + blob[8:]).code == GLC_ERR_IO
