@@ -265,7 +265,13 @@ int parse(glc_gguf* g) {
     if (!c.str(&t.name) || !c.u32(&nd)) return fail_io("gguf: unexpected end of file in a tensor info");
     if (!c.have(static_cast<uint64_t>(nd) * 8)) return fail_io("gguf: unexpected end of file in tensor dimensions");
     t.dims.resize(nd);
-    for (uint32_t d = 0; d < nd; ++d) c.u64(&t.dims[d]);
+    uint64_t count = 1;
+    for (uint32_t d = 0; d < nd; ++d) {
+      c.u64(&t.dims[d]);
+      if (t.dims[d] != 0 && count > UINT64_MAX / t.dims[d] / 4)
+        return fail_io("gguf: dimensions of tensor '" + t.name + "' overflow");
+      count *= t.dims[d];
+    }
     if (!c.u32(&t.type) || !c.u64(&t.offset)) return fail_io("gguf: unexpected end of file in a tensor info");
     g->tensor_index[t.name] = static_cast<size_t>(k);
   }

@@ -149,6 +149,13 @@ def test_unknown_value_type_and_huge_counts(tmp_path):
         gguf.Open(write(tmp_path, struct.pack("<IIQQ", 0x46554747, 3, 0, 2**40) + b"\0" * 64))
 
 
+def test_overflowing_dimensions_are_refused(tmp_path):
+    blob, *_ = W.gguf_bytes([], [], extra_tensor_infos=[("huge", [2**40, 2**40], 0, 0)])
+    with pytest.raises(GlcError) as e:
+        gguf.Open(write(tmp_path, blob))
+    assert e.value.code == GLC_ERR_IO and "overflow" in str(e.value)
+
+
 def test_duplicates_and_data_past_the_end(tmp_path):
     meta = [("x", W.U32, 1), ("x", W.U32, 2)]
     t1 = ("w", [4], 0, np.arange(4, dtype=np.float32).tobytes())
