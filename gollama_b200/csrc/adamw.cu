@@ -31,6 +31,7 @@ struct Seg {
 };
 
 __global__ void sumsq_kernel(const float* __restrict__ g, const Seg* __restrict__ segs, double* __restrict__ partial) {
+  GLC_PDL_ENTRY();
   const Seg sg = segs[blockIdx.y];
   double acc = 0.0;
   const float4* base = reinterpret_cast<const float4*>(g + sg.start);
@@ -54,6 +55,7 @@ __global__ void sumsq_kernel(const float* __restrict__ g, const Seg* __restrict_
 
 __global__ void norm_finish_kernel(const double* __restrict__ partial, int n, float max_norm, double* __restrict__ norm,
                                    float* __restrict__ scale) {
+  GLC_PDL_ENTRY();
   __shared__ double red[32];
   double acc = 0.0;
   for (int i = threadIdx.x; i < n; i += blockDim.x) acc += partial[i];
@@ -76,6 +78,7 @@ __global__ void norm_finish_kernel(const double* __restrict__ partial, int n, fl
 // partial[b*chunk, min(n, (b+1)*chunk)) in a fixed order into out[b].
 __global__ void slot_sum_kernel(const double* __restrict__ partial, long long n, long long chunk,
                                 double* __restrict__ out) {
+  GLC_PDL_ENTRY();
   __shared__ double red[32];
   const long long b0 = static_cast<long long>(blockIdx.x) * chunk;
   const long long b1 = min(n, b0 + chunk);
@@ -132,6 +135,7 @@ __device__ __forceinline__ void adam_elem(float& p, float& g, float& m, float& v
 __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
                              float* __restrict__ shadow, const Seg* __restrict__ segs,
                              const float* __restrict__ clip_scale, AdamArgs a, int write_g) {
+  GLC_PDL_ENTRY();
   const Seg sg = segs[blockIdx.y];
   const float scale = clip_scale ? *clip_scale : 1.0f;
   const bool scaled = scale != 1.0f;
@@ -170,7 +174,7 @@ int grad_sumsq(Context* ctx, const float* grads, const int64_t* segs, int nseg, 
   if (nseg <= 0) return 0;
   if (!grads || !segs || !partial || bx <= 0) return ctx->fail(GLC_ERR_INVALID, "grad_sumsq: bad arguments");
   ProfScope prof(ctx, PROF_ADAMW, 4.0 * elems, s);
-  sumsq_kernel<<<dim3(bx, nseg), 256, 0, s>>>(grads, reinterpret_cast<const Seg*>(segs), partial);
+  glc::launch_pdl(ctx, sumsq_kernel, dim3(bx, nseg), 256, 0, s, grads, reinterpret_cast<const Seg*>(segs), partial);
   GLC_LAUNCH_CHECK(ctx, "grad_norm partial");
   return 0;
 }
@@ -184,12 +188,12 @@ int grad_norm_finish(Context* ctx, const double* partial, long long n, float max
   const long long nb = (n + chunk - 1) / chunk;
   if (n > 8192 && lvl && lvl_cap >= nb) {
     // many partials (the GEMM epilogues' slots): blocks of 1024 first
-    slot_sum_kernel<<<static_cast<unsigned>(nb), 256, 0, s>>>(partial, n, chunk, lvl);
+    glc::launch_pdl(ctx, slot_sum_kernel, static_cast<unsigned>(nb), 256, 0, s, partial, n, chunk, lvl);
     GLC_LAUNCH_CHECK(ctx, "grad_norm slot sum");
     partial = lvl;
     n = nb;
   }
-  norm_finish_kernel<<<1, 256, 0, s>>>(partial, static_cast<int>(n), max_norm, norm_out, scale_out);
+  glc::launch_pdl(ctx, norm_finish_kernel, 1, 256, 0, s, partial, static_cast<int>(n), max_norm, norm_out, scale_out);
   GLC_LAUNCH_CHECK(ctx, "grad_norm finish");
   return 0;
 }
@@ -235,8 +239,8 @@ int adamw(Context* ctx, float* p, float* g, float* m, float* v, float* shadow, c
   if (bx < 4) bx = 4;
   // p, g, m, v read; p, m, v and the TF32 shadow written
   ProfScope prof(ctx, PROF_ADAMW, (shadow ? 32.0 : 28.0) * elems, s);
-  adamw_kernel<<<dim3(bx, nseg), 256, 0, s>>>(p, g, m, v, shadow, reinterpret_cast<const Seg*>(segs), clip_scale, a,
-                                               write_grad ? 1 : 0);
+  glc::launch_pdl(ctx, adamw_kernel, dim3(bx, nseg), 256, 0, s, p, g, m, v, shadow, reinterpret_cast<const Seg*>(segs), clip_scale, a,
+                  write_grad ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "adamw");
   return 0;
 }
@@ -244,6 +248,7 @@ int adamw(Context* ctx, float* p, float* g, float* m, float* v, float* shadow, c
 namespace {
 // g = g * scale (float32, as the clipping in the AdamW kernel), unless scale is 1
 __global__ void scale_in_place_kernel(float* __restrict__ g, size_t n, const float* __restrict__ scale) {
+  GLC_PDL_ENTRY();
   const float sc = *scale;
   if (sc == 1.0f) return;
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
@@ -254,7 +259,7 @@ __global__ void scale_in_place_kernel(float* __restrict__ g, size_t n, const flo
 int scale_in_place(Context* ctx, float* g, size_t n, const float* scale, cudaStream_t s) {
   if (n == 0) return 0;
   if (!g || !scale) return ctx->fail(GLC_ERR_INVALID, "scale_in_place: null pointer");
-  scale_in_place_kernel<<<grid_for(n, 256, ctx->num_sms), 256, 0, s>>>(g, n, scale);
+  glc::launch_pdl(ctx, scale_in_place_kernel, grid_for(n, 256, ctx->num_sms), 256, 0, s, g, n, scale);
   GLC_LAUNCH_CHECK(ctx, "scale_in_place");
   return 0;
 }

@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(NT, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, float* __restrict__ out, float* __restrict__ lse,
                        int S, int H, int Hkv, int n_qt, float scale_log2, int round_out, int* err) {
+  GLC_PDL_ENTRY();
   using L = FwdLayout<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -420,6 +421,7 @@ __global__ void __launch_bounds__(NT, 1)
     attn_fwd_persist_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, float* __restrict__ out, float* __restrict__ lse,
                             int S, int B, int H, int Hkv, int n_qt, float scale_log2, int round_out, int* err) {
+  GLC_PDL_ENTRY();
   using L = PFwdLayout<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -748,6 +750,7 @@ __global__ void __launch_bounds__(NT, 1)
                             const float* __restrict__ lse, const float* __restrict__ Dv, float* __restrict__ dk_out,
                             float* __restrict__ dv_out, int dk_ld, int dv_ld, int nsplit, int S, int H, int Hkv,
                             float scale, float scale_log2, int round_dv, int* err) {
+  GLC_PDL_ENTRY();
   using L = DkdvLayout<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1004,6 +1007,7 @@ __global__ void __launch_bounds__(NT, 1)
 __global__ void group_sum_kernel(const float* __restrict__ pk, const float* __restrict__ pv, float* __restrict__ dk,
                                  float* __restrict__ dv, int dk_ld, int dv_ld, int T, int S, int nsplit, int Hkv, int hd,
                                  int round_dv, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin) {
+  GLC_PDL_ENTRY();
   // 32-bit index math: the host checks T * Hkv * hd / 4 < 2^31
   const int n4 = hd / 4, per_t = Hkv * n4;
   const int total = T * per_t;
@@ -1065,6 +1069,7 @@ __global__ void __launch_bounds__(NT, 1)
                           const float* __restrict__ Dv, float* __restrict__ dq, int dq_ld, int S, int H, int Hkv,
                           int n_qt, float scale, float scale_log2, const float* __restrict__ rope_cos,
                           const float* __restrict__ rope_sin, int* err) {
+  GLC_PDL_ENTRY();
   using L = DqLayout<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1315,6 +1320,7 @@ __global__ void __launch_bounds__(NT, 1)
                                const float* __restrict__ Dv, float* __restrict__ dq, int dq_ld, int S, int B, int H,
                                int Hkv, int n_qt, float scale, float scale_log2, const float* __restrict__ rope_cos,
                                const float* __restrict__ rope_sin, int* err) {
+  GLC_PDL_ENTRY();
   using L = PDqLayout<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1579,6 +1585,7 @@ __global__ void __launch_bounds__(NT, 1)
 template <int HD>
 __global__ void attn_bwd_prep_tc_kernel(const float* __restrict__ o, const float* __restrict__ dO,
                                         float* __restrict__ D, int T, int S, int H) {
+  GLC_PDL_ENTRY();
   constexpr int LPR = HD / 4, RPW = 32 / LPR;
   const int lane = threadIdx.x & 31, sub = lane / LPR, li = lane % LPR;
   const int nrow = T * H;
@@ -1654,11 +1661,11 @@ int fwd_impl(Context* ctx, const float* q, int q_ld, const float* k, int k_ld, c
     const long long items = static_cast<long long>(H) * B * n_qt;
     if (items >= (1LL << 31)) return ctx->fail(GLC_ERR_INVALID, "attention_fwd: too many work items");
     const int grid = static_cast<int>(items < ctx->num_sms ? items : ctx->num_sms);
-    attn_fwd_persist_kernel<HD><<<grid, NT, PFwdLayout<HD>::BYTES, s>>>(tq, tk, tv, o, lse, S, B, H, Hkv, n_qt,
-                                                                         scale * LOG2E, round_out ? 1 : 0, ctx->d_err);
+    glc::launch_pdl(ctx, attn_fwd_persist_kernel<HD>, grid, NT, PFwdLayout<HD>::BYTES, s, tq, tk, tv, o, lse, S, B, H, Hkv, n_qt,
+                    scale * LOG2E, round_out ? 1 : 0, ctx->d_err);
   } else {
-    attn_fwd_tc_kernel<HD><<<dim3(H, B, n_qt), NT, L::BYTES, s>>>(tq, tk, tv, o, lse, S, H, Hkv, n_qt, scale * LOG2E,
-                                                                     round_out ? 1 : 0, ctx->d_err);
+    glc::launch_pdl(ctx, attn_fwd_tc_kernel<HD>, dim3(H, B, n_qt), NT, L::BYTES, s, tq, tk, tv, o, lse, S, H, Hkv, n_qt, scale * LOG2E,
+                    round_out ? 1 : 0, ctx->d_err);
   }
   GLC_LAUNCH_CHECK(ctx, "attention_fwd (tcgen05)");
   return 0;
@@ -1692,7 +1699,7 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
   {
     const long long nrow = static_cast<long long>(T) * H;
     const long long warps = (nrow + (32 / (HD / 4)) - 1) / (32 / (HD / 4));
-    attn_bwd_prep_tc_kernel<HD><<<static_cast<unsigned>((warps + 7) / 8), 256, 0, s>>>(o, dO, D, T, S, H);
+    glc::launch_pdl(ctx, attn_bwd_prep_tc_kernel<HD>, static_cast<unsigned>((warps + 7) / 8), 256, 0, s, o, dO, D, T, S, H);
   }
   GLC_LAUNCH_CHECK(ctx, "attention_bwd prep");
   const int n_kt = (S + 127) / 128;
@@ -1711,9 +1718,9 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     if (ctx->attn_split > 0 && G % ctx->attn_split == 0) nsplit = ctx->attn_split;
   }
   if (nsplit == 1) {
-    attn_bwd_dkdv_tc_kernel<HD><<<dim3(Hkv, B, n_kt), NT, DkdvLayout<HD>::BYTES, s>>>(
-        tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, io.dk, io.dv, io.dk_ld, io.dv_ld, 1, S, H, Hkv, scale,
-        scale * LOG2E, round_dv ? 1 : 0, ctx->d_err);
+    glc::launch_pdl(ctx, attn_bwd_dkdv_tc_kernel<HD>, dim3(Hkv, B, n_kt), NT, DkdvLayout<HD>::BYTES, s,
+                    tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, io.dk, io.dv, io.dk_ld, io.dv_ld, 1, S, H, Hkv, scale,
+                    scale * LOG2E, round_dv ? 1 : 0, ctx->d_err);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
     if (rope_cos && (rc = rope(ctx, io.dk, io.dk_ld, T, S, Hkv, HD, rope_cos, rope_sin, true, true, s))) return rc;
   } else {
@@ -1721,14 +1728,14 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     const int pw = Hkv * nsplit * HD;
     float* pk = partial;
     float* pv = partial + static_cast<size_t>(T) * pw;
-    attn_bwd_dkdv_tc_kernel<HD><<<dim3(Hkv * nsplit, B, n_kt), NT, DkdvLayout<HD>::BYTES, s>>>(
-        tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, pk, pv, pw, pw, nsplit, S, H, Hkv, scale, scale * LOG2E, 0,
-        ctx->d_err);
+    glc::launch_pdl(ctx, attn_bwd_dkdv_tc_kernel<HD>, dim3(Hkv * nsplit, B, n_kt), NT, DkdvLayout<HD>::BYTES, s,
+                    tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, pk, pv, pw, pw, nsplit, S, H, Hkv, scale, scale * LOG2E, 0,
+                    ctx->d_err);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd dkdv (tcgen05)");
     if (static_cast<long long>(T) * Hkv * HD / 4 >= (1LL << 31))
       return ctx->fail(GLC_ERR_INVALID, "attention_bwd: B*S*Hkv*hd too large");
-    group_sum_kernel<<<grid_for(static_cast<size_t>(T) * Hkv * HD / 4, 256, ctx->num_sms), 256, 0, s>>>(
-        pk, pv, io.dk, io.dv, io.dk_ld, io.dv_ld, T, S, nsplit, Hkv, HD, round_dv ? 1 : 0, rope_cos, rope_sin);
+    glc::launch_pdl(ctx, group_sum_kernel, grid_for(static_cast<size_t>(T) * Hkv * HD / 4, 256, ctx->num_sms), 256, 0, s,
+                    pk, pv, io.dk, io.dv, io.dk_ld, io.dv_ld, T, S, nsplit, Hkv, HD, round_dv ? 1 : 0, rope_cos, rope_sin);
     GLC_LAUNCH_CHECK(ctx, "attention_bwd group sum");
   }
   const int n_qt = (S + 127) / 128;
@@ -1736,13 +1743,13 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     const long long items = static_cast<long long>(H) * B * n_qt;
     if (items >= (1LL << 31)) return ctx->fail(GLC_ERR_INVALID, "attention_bwd: too many work items");
     const int grid = static_cast<int>(items < ctx->num_sms ? items : ctx->num_sms);
-    attn_bwd_dq_persist_kernel<HD><<<grid, NT, PDqLayout<HD>::BYTES, s>>>(
-        tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, B, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,
-        rope_sin, ctx->d_err);
+    glc::launch_pdl(ctx, attn_bwd_dq_persist_kernel<HD>, grid, NT, PDqLayout<HD>::BYTES, s,
+                    tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, B, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,
+                    rope_sin, ctx->d_err);
   } else {
-    attn_bwd_dq_tc_kernel<HD><<<dim3(H, B, n_qt), NT, DqLayout<HD>::BYTES, s>>>(
-        tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,
-        rope_sin, ctx->d_err);
+    glc::launch_pdl(ctx, attn_bwd_dq_tc_kernel<HD>, dim3(H, B, n_qt), NT, DqLayout<HD>::BYTES, s,
+                    tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,
+                    rope_sin, ctx->d_err);
   }
   GLC_LAUNCH_CHECK(ctx, "attention_bwd dq (tcgen05)");
   return 0;

@@ -54,6 +54,7 @@ template <int VPT, bool FAST>
 __global__ void __launch_bounds__(512) ce_kernel(float* __restrict__ logits, const int64_t* __restrict__ targets,
                                                   int rows, int V, float scale, float* __restrict__ row_logp,
                                                   int write_grad, int round_out) {
+  GLC_PDL_ENTRY();
   __shared__ float red[33];
   const int nc = V >> 2;
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
@@ -136,6 +137,7 @@ template <int VPT, bool FAST>
 __global__ void __cluster_dims__(CE_CL, 1, 1) __launch_bounds__(CE_CL_THREADS, VPT <= 8 ? 4 : 2)
     ce_cluster_kernel(float* __restrict__ logits, const int64_t* __restrict__ targets, int V, int chunk, float scale,
                       float* __restrict__ row_logp, int write_grad, int round_out) {
+  GLC_PDL_ENTRY();
   __shared__ float red[33];
   __shared__ float slots[2];
   const int nc = V >> 2;
@@ -200,6 +202,7 @@ __global__ void __cluster_dims__(CE_CL, 1, 1) __launch_bounds__(CE_CL_THREADS, V
 // subtracts them in row order (the reference's running float32 total).
 __global__ void ce_loss_sum_kernel(const float* __restrict__ row_logp, const int64_t* __restrict__ targets, int rows,
                                    int V, float* __restrict__ loss) {
+  GLC_PDL_ENTRY();
   constexpr int CHUNK = 2048;
   __shared__ float buf[CHUNK];
   float total = 0.f;
@@ -218,6 +221,7 @@ __global__ void ce_loss_sum_kernel(const float* __restrict__ row_logp, const int
 }
 
 __global__ void exp32_kernel(const float* __restrict__ x, float* __restrict__ y, size_t n) {
+  GLC_PDL_ENTRY();
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
     y[i] = go_exp32_fast(x[i]);
 }
@@ -228,7 +232,7 @@ int exp32(Context* ctx, const float* x, float* y, size_t n, cudaStream_t s) {
   if (n == 0) return 0;
   if (!x || !y) return ctx->fail(GLC_ERR_INVALID, "exp32: null pointer");
   ProfScope prof(ctx, PROF_OTHER, 8.0 * n, s);
-  exp32_kernel<<<grid_for(n, 256, ctx->num_sms), 256, 0, s>>>(x, y, n);
+  glc::launch_pdl(ctx, exp32_kernel, grid_for(n, 256, ctx->num_sms), 256, 0, s, x, y, n);
   GLC_LAUNCH_CHECK(ctx, "exp32");
   return 0;
 }
@@ -249,18 +253,18 @@ int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, in
     const unsigned grid = static_cast<unsigned>(rows) * CE_CL;
     ProfScope prof(ctx, PROF_CE, 4.0 * static_cast<double>(rows) * V * (write_grad ? 2 : 1), s);
     if (vpt <= 4)
-      (fast_exp ? ce_cluster_kernel<4, true> : ce_cluster_kernel<4, false>)<<<grid, CE_CL_THREADS, 0, s>>>(
-          logits, targets, V, chunk, scale, row_logp, wg, ro);
+      glc::launch_pdl(ctx, (fast_exp ? ce_cluster_kernel<4, true> : ce_cluster_kernel<4, false>), grid, CE_CL_THREADS, 0, s,
+                      logits, targets, V, chunk, scale, row_logp, wg, ro);
     else if (vpt <= 8)
-      (fast_exp ? ce_cluster_kernel<8, true> : ce_cluster_kernel<8, false>)<<<grid, CE_CL_THREADS, 0, s>>>(
-          logits, targets, V, chunk, scale, row_logp, wg, ro);
+      glc::launch_pdl(ctx, (fast_exp ? ce_cluster_kernel<8, true> : ce_cluster_kernel<8, false>), grid, CE_CL_THREADS, 0, s,
+                      logits, targets, V, chunk, scale, row_logp, wg, ro);
     else if (vpt <= 16)
-      (fast_exp ? ce_cluster_kernel<16, true> : ce_cluster_kernel<16, false>)<<<grid, CE_CL_THREADS, 0, s>>>(
-          logits, targets, V, chunk, scale, row_logp, wg, ro);
+      glc::launch_pdl(ctx, (fast_exp ? ce_cluster_kernel<16, true> : ce_cluster_kernel<16, false>), grid, CE_CL_THREADS, 0, s,
+                      logits, targets, V, chunk, scale, row_logp, wg, ro);
     else
       return ctx->fail(GLC_ERR_UNSUPPORTED, "softmax_ce: vocab above 65536 is not supported");
     GLC_LAUNCH_CHECK(ctx, "softmax_ce (cluster)");
-    ce_loss_sum_kernel<<<1, 256, 0, s>>>(row_logp, targets, rows, V, loss);
+    glc::launch_pdl(ctx, ce_loss_sum_kernel, 1, 256, 0, s, row_logp, targets, rows, V, loss);
     GLC_LAUNCH_CHECK(ctx, "softmax_ce loss");
     return 0;
   }
@@ -270,21 +274,21 @@ int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, in
   const unsigned grid = static_cast<unsigned>(rows);
   ProfScope prof(ctx, PROF_CE, 4.0 * static_cast<double>(rows) * V * (write_grad ? 2 : 1), s);
   if (vpt <= 1)
-    (fast_exp ? ce_kernel<1, true> : ce_kernel<1, false>)<<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+    glc::launch_pdl(ctx, (fast_exp ? ce_kernel<1, true> : ce_kernel<1, false>), grid, threads, 0, s, logits, targets, rows, V, scale, row_logp, wg, ro);
   else if (vpt <= 2)
-    (fast_exp ? ce_kernel<2, true> : ce_kernel<2, false>)<<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+    glc::launch_pdl(ctx, (fast_exp ? ce_kernel<2, true> : ce_kernel<2, false>), grid, threads, 0, s, logits, targets, rows, V, scale, row_logp, wg, ro);
   else if (vpt <= 4)
-    (fast_exp ? ce_kernel<4, true> : ce_kernel<4, false>)<<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+    glc::launch_pdl(ctx, (fast_exp ? ce_kernel<4, true> : ce_kernel<4, false>), grid, threads, 0, s, logits, targets, rows, V, scale, row_logp, wg, ro);
   else if (vpt <= 8)
-    (fast_exp ? ce_kernel<8, true> : ce_kernel<8, false>)<<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+    glc::launch_pdl(ctx, (fast_exp ? ce_kernel<8, true> : ce_kernel<8, false>), grid, threads, 0, s, logits, targets, rows, V, scale, row_logp, wg, ro);
   else if (vpt <= 16)
-    (fast_exp ? ce_kernel<16, true> : ce_kernel<16, false>)<<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+    glc::launch_pdl(ctx, (fast_exp ? ce_kernel<16, true> : ce_kernel<16, false>), grid, threads, 0, s, logits, targets, rows, V, scale, row_logp, wg, ro);
   else if (vpt <= 32)
-    (fast_exp ? ce_kernel<32, true> : ce_kernel<32, false>)<<<grid, threads, 0, s>>>(logits, targets, rows, V, scale, row_logp, wg, ro);
+    glc::launch_pdl(ctx, (fast_exp ? ce_kernel<32, true> : ce_kernel<32, false>), grid, threads, 0, s, logits, targets, rows, V, scale, row_logp, wg, ro);
   else
     return ctx->fail(GLC_ERR_UNSUPPORTED, "softmax_ce: vocab above 65536 is not supported");
   GLC_LAUNCH_CHECK(ctx, "softmax_ce");
-  ce_loss_sum_kernel<<<1, 256, 0, s>>>(row_logp, targets, rows, V, loss);
+  glc::launch_pdl(ctx, ce_loss_sum_kernel, 1, 256, 0, s, row_logp, targets, rows, V, loss);
   GLC_LAUNCH_CHECK(ctx, "softmax_ce loss");
   return 0;
 }

@@ -33,6 +33,7 @@ int Context::workspace(size_t bytes, void** out) {
 
 namespace {
 __global__ void empty_k_kernel(float* C, int ldc, int M, int N, int accumulate, const float* R, int ldr) {
+  GLC_PDL_ENTRY();
   const size_t total = static_cast<size_t>(M) * N;
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
     const int r = static_cast<int>(i / N), c = static_cast<int>(i % N);
@@ -46,7 +47,7 @@ __global__ void empty_k_kernel(float* C, int ldc, int M, int N, int accumulate, 
 int gemm_empty_k(Context* ctx, float* C, int ldc, int M, int N, bool accumulate, const float* R, int ldr,
                  cudaStream_t stream) {
   const size_t total = static_cast<size_t>(M) * N;
-  empty_k_kernel<<<grid_for(total, 256, ctx->num_sms), 256, 0, stream>>>(C, ldc, M, N, accumulate ? 1 : 0, R, ldr);
+  glc::launch_pdl(ctx, empty_k_kernel, grid_for(total, 256, ctx->num_sms), 256, 0, stream, C, ldc, M, N, accumulate ? 1 : 0, R, ldr);
   GLC_LAUNCH_CHECK(ctx, "gemm_empty_k");
   return 0;
 }
@@ -301,6 +302,12 @@ int glc_set_attention_dq_variant(glc_ctx* ctx, int variant) {
   Context* c = C_(ctx);
   if (variant < 0 || variant > 2) return c->fail(GLC_ERR_INVALID, "set_attention_dq_variant: variant must be 0, 1 or 2");
   c->attn_dq_variant = variant;
+  return GLC_OK;
+}
+
+int glc_set_pdl(glc_ctx* ctx, int on) {
+  if (!ctx) return GLC_ERR_INVALID;
+  C_(ctx)->pdl = on != 0;
   return GLC_OK;
 }
 

@@ -19,6 +19,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 template <bool FAST>
 __global__ void swiglu_fwd_kernel(const float* __restrict__ g, const float* __restrict__ u, size_t ld_in,
                                   float* __restrict__ h, size_t ld_h, unsigned rows, unsigned cols4, int round_out) {
+  GLC_PDL_ENTRY();
   const unsigned c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= cols4) return;
   for (unsigned r = blockIdx.y; r < rows; r += gridDim.y) {
@@ -48,6 +49,7 @@ __global__ void swiglu_bwd_kernel(const float* __restrict__ g, const float* __re
                                   const float* __restrict__ dh, size_t ld_dh, float* __restrict__ dg,
                                   float* __restrict__ du, size_t ld_out, unsigned rows, unsigned cols4, int accumulate,
                                   int round_out) {
+  GLC_PDL_ENTRY();
   const unsigned c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= cols4) return;
   for (unsigned r = blockIdx.y; r < rows; r += gridDim.y) {
@@ -88,15 +90,18 @@ inline dim3 grid_2d(size_t rows, size_t cols4, int block, int num_sms) {
 
 // ---------------------------------------------------------------- fills / copies
 __global__ void fill_kernel(float* __restrict__ p, float v, size_t n) {
+  GLC_PDL_ENTRY();
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) p[i] = v;
 }
 
 __global__ void add_inplace_kernel(float* __restrict__ dst, const float* __restrict__ src, size_t n) {
+  GLC_PDL_ENTRY();
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
     dst[i] = __fadd_rn(dst[i], src[i]);
 }
 
 __global__ void round_copy_kernel(const float* __restrict__ src, float* __restrict__ dst, size_t n) {
+  GLC_PDL_ENTRY();
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
     dst[i] = round_tf32(src[i]);
 }
@@ -110,6 +115,7 @@ __global__ void round_copy_kernel(const float* __restrict__ src, float* __restri
 __global__ void rope_kernel(float* __restrict__ x, size_t ld, int T, int S, int nh, int hd,
                             const float* __restrict__ cos_t, const float* __restrict__ sin_t, int inverse,
                             int round_out) {
+  GLC_PDL_ENTRY();
   const int half = hd >> 1;
   const int q = blockIdx.x * blockDim.x + threadIdx.x;  // pair index inside the row: head * half + i
   if (q >= nh * half) return;
@@ -156,6 +162,7 @@ __device__ __forceinline__ float2 rope_pair(float a, float b, float c, float s, 
 __global__ void rope4_kernel(float* __restrict__ x, size_t ld, int T, int S, int nh, int hd,
                              const float* __restrict__ cos_t, const float* __restrict__ sin_t, int inverse,
                              int round_out) {
+  GLC_PDL_ENTRY();
   const int half = hd >> 1, quads = hd >> 2;
   const int qq = blockIdx.x * blockDim.x + threadIdx.x;  // head * quads + j: pairs 2j and 2j+1 of the head
   if (qq >= nh * quads) return;
@@ -177,6 +184,7 @@ __global__ void rope4_kernel(float* __restrict__ x, size_t ld, int T, int S, int
 // [0, V) read row 0.
 __global__ void embed_fwd_kernel(const int64_t* __restrict__ tok, const float* __restrict__ E,
                                  const float* __restrict__ P, float* __restrict__ out, int T, int S, int d, int V) {
+  GLC_PDL_ENTRY();
   const int nc = d >> 2;
   const size_t total = static_cast<size_t>(T) * nc;
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
@@ -204,6 +212,7 @@ __global__ void embed_fwd_kernel(const int64_t* __restrict__ tok, const float* _
 __global__ void embed_bwd_kernel(const int* __restrict__ seg_tok, const int* __restrict__ seg_start,
                                  const int* __restrict__ order, const float* __restrict__ dh, float* __restrict__ dE,
                                  int nseg, int d) {
+  GLC_PDL_ENTRY();
   const int nc = d >> 2;
   const int c = blockIdx.y * blockDim.x + threadIdx.x;
   if (c >= nc) return;
@@ -237,8 +246,8 @@ int swiglu_fwd(Context* ctx, const float* g, const float* u, size_t ld_in, float
   ProfScope prof(ctx, PROF_SWIGLU, 12.0 * n, s);
   if (rows > 0xFFFFFFFFu || cols / 4 > 0xFFFFFFFFu) return ctx->fail(GLC_ERR_INVALID, "swiglu_fwd: too large");
   auto kern = fast_exp ? swiglu_fwd_kernel<true> : swiglu_fwd_kernel<false>;
-  kern<<<grid_2d(rows, cols / 4, 256, ctx->num_sms), 256, 0, s>>>(
-      g, u, ld_in, h, ld_h, static_cast<unsigned>(rows), static_cast<unsigned>(cols / 4), round_out ? 1 : 0);
+  glc::launch_pdl(ctx, kern, grid_2d(rows, cols / 4, 256, ctx->num_sms), 256, 0, s,
+                  g, u, ld_in, h, ld_h, static_cast<unsigned>(rows), static_cast<unsigned>(cols / 4), round_out ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "swiglu_fwd");
   return 0;
 }
@@ -254,9 +263,9 @@ int swiglu_bwd(Context* ctx, const float* g, const float* u, size_t ld_in, const
   ProfScope prof(ctx, PROF_SWIGLU, (accumulate ? 28.0 : 20.0) * n, s);
   if (rows > 0xFFFFFFFFu || cols / 4 > 0xFFFFFFFFu) return ctx->fail(GLC_ERR_INVALID, "swiglu_bwd: too large");
   auto kern = fast_exp ? swiglu_bwd_kernel<true> : swiglu_bwd_kernel<false>;
-  kern<<<grid_2d(rows, cols / 4, 256, ctx->num_sms), 256, 0, s>>>(
-      g, u, ld_in, dh, ld_dh, dg, du, ld_out, static_cast<unsigned>(rows), static_cast<unsigned>(cols / 4),
-      accumulate ? 1 : 0, round_out ? 1 : 0);
+  glc::launch_pdl(ctx, kern, grid_2d(rows, cols / 4, 256, ctx->num_sms), 256, 0, s,
+                  g, u, ld_in, dh, ld_dh, dg, du, ld_out, static_cast<unsigned>(rows), static_cast<unsigned>(cols / 4),
+                  accumulate ? 1 : 0, round_out ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "swiglu_bwd");
   return 0;
 }
@@ -265,7 +274,7 @@ int fill(Context* ctx, float* p, float v, size_t n, cudaStream_t s) {
   if (n == 0) return 0;
   if (!p) return ctx->fail(GLC_ERR_INVALID, "fill: null pointer");
   ProfScope prof(ctx, PROF_OTHER, 4.0 * n, s);
-  fill_kernel<<<grid_for(n, 256, ctx->num_sms), 256, 0, s>>>(p, v, n);
+  glc::launch_pdl(ctx, fill_kernel, grid_for(n, 256, ctx->num_sms), 256, 0, s, p, v, n);
   GLC_LAUNCH_CHECK(ctx, "fill");
   return 0;
 }
@@ -274,7 +283,7 @@ int add_inplace(Context* ctx, float* dst, const float* src, size_t n, cudaStream
   if (n == 0) return 0;
   if (!dst || !src) return ctx->fail(GLC_ERR_INVALID, "add_inplace: null pointer");
   ProfScope prof(ctx, PROF_OTHER, 12.0 * n, s);
-  add_inplace_kernel<<<grid_for(n, 256, ctx->num_sms), 256, 0, s>>>(dst, src, n);
+  glc::launch_pdl(ctx, add_inplace_kernel, grid_for(n, 256, ctx->num_sms), 256, 0, s, dst, src, n);
   GLC_LAUNCH_CHECK(ctx, "add_inplace");
   return 0;
 }
@@ -283,7 +292,7 @@ int round_copy(Context* ctx, const float* src, float* dst, size_t n, cudaStream_
   if (n == 0) return 0;
   if (!src || !dst) return ctx->fail(GLC_ERR_INVALID, "round_copy: null pointer");
   ProfScope prof(ctx, PROF_OTHER, 8.0 * n, s);
-  round_copy_kernel<<<grid_for(n, 256, ctx->num_sms), 256, 0, s>>>(src, dst, n);
+  glc::launch_pdl(ctx, round_copy_kernel, grid_for(n, 256, ctx->num_sms), 256, 0, s, src, dst, n);
   GLC_LAUNCH_CHECK(ctx, "round_copy");
   return 0;
 }
@@ -303,8 +312,8 @@ int rope(Context* ctx, float* x, int ld, int T, int S, int nh, int hd, const flo
     int by = (ctx->num_sms * 16 + bx - 1) / bx;
     if (by > T) by = T;
     if (by > 65535) by = 65535;
-    rope4_kernel<<<dim3(bx, by), 256, 0, s>>>(x, static_cast<size_t>(ld), T, S, nh, hd, cos_t, sin_t,
-                                              inverse ? 1 : 0, round_out ? 1 : 0);
+    glc::launch_pdl(ctx, rope4_kernel, dim3(bx, by), 256, 0, s, x, static_cast<size_t>(ld), T, S, nh, hd, cos_t, sin_t,
+                    inverse ? 1 : 0, round_out ? 1 : 0);
     GLC_LAUNCH_CHECK(ctx, "rope");
     return 0;
   }
@@ -313,8 +322,8 @@ int rope(Context* ctx, float* x, int ld, int T, int S, int nh, int hd, const flo
   int by = (ctx->num_sms * 16 + bx - 1) / bx;
   if (by > T) by = T;
   if (by > 65535) by = 65535;
-  rope_kernel<<<dim3(bx, by), 256, 0, s>>>(x, static_cast<size_t>(ld), T, S, nh, hd, cos_t, sin_t, inverse ? 1 : 0,
-                                           round_out ? 1 : 0);
+  glc::launch_pdl(ctx, rope_kernel, dim3(bx, by), 256, 0, s, x, static_cast<size_t>(ld), T, S, nh, hd, cos_t, sin_t, inverse ? 1 : 0,
+                  round_out ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "rope");
   return 0;
 }
@@ -327,7 +336,7 @@ int embed_fwd(Context* ctx, const int64_t* tok, const float* E, const float* P, 
     return ctx->fail(GLC_ERR_INVALID, "embed_fwd: bad arguments (hidden size must be a multiple of 4)");
   const size_t total = static_cast<size_t>(T) * (d / 4);
   ProfScope prof(ctx, PROF_OTHER, (P ? 12.0 : 8.0) * T * d, s);
-  embed_fwd_kernel<<<grid_for(total, 256, ctx->num_sms), 256, 0, s>>>(tok, E, P, out, T, S, d, V);
+  glc::launch_pdl(ctx, embed_fwd_kernel, grid_for(total, 256, ctx->num_sms), 256, 0, s, tok, E, P, out, T, S, d, V);
   GLC_LAUNCH_CHECK(ctx, "embed_fwd");
   return 0;
 }
@@ -342,7 +351,7 @@ int embed_bwd(Context* ctx, const int* seg_tok, const int* seg_start, const int*
   unsigned gx = static_cast<unsigned>((8 * ctx->num_sms + gy - 1) / gy);
   if (gx > static_cast<unsigned>(nseg)) gx = static_cast<unsigned>(nseg);
   ProfScope prof(ctx, PROF_OTHER, 8.0 * 0, s);
-  embed_bwd_kernel<<<dim3(gx, gy), 128, 0, s>>>(seg_tok, seg_start, order, dh, dE, nseg, d);
+  glc::launch_pdl(ctx, embed_bwd_kernel, dim3(gx, gy), 128, 0, s, seg_tok, seg_start, order, dh, dE, nseg, d);
   GLC_LAUNCH_CHECK(ctx, "embed_bwd");
   return 0;
 }

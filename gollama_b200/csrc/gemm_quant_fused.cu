@@ -71,6 +71,7 @@ __device__ __forceinline__ uint32_t b_tile_offset(int chunk, int r, int j) {
 
 __global__ void __launch_bounds__(QF_THREADS, 1)
     gemm_quant_fused_kernel(const __grid_constant__ CUtensorMap tmA, const QuantGemmArgs args) {
+  GLC_PDL_ENTRY();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // afull[s]: the dY copy of stage s landed (TMA complete_tx); bfull[s]: the
@@ -314,6 +315,7 @@ __global__ void __launch_bounds__(QF_THREADS, 1)
 // with the one the producer warps above write (b_tile_offset).
 __global__ void __launch_bounds__(128) swizzle_probe_kernel(const __grid_constant__ CUtensorMap tm, float* out,
                                                              int* err) {
+  GLC_PDL_ENTRY();
   extern __shared__ uint8_t probe_raw[];  // 4096 + 1024 bytes: the tile on a 1024-byte boundary (swizzle phase)
   uint8_t* tile = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(probe_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t bar;
@@ -348,7 +350,7 @@ int swizzle_probe(Context* ctx, const float* src, float* out) {
   if (ctx->encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(src), dims, strides, box, estr,
                         CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B) != 0)
     return ctx->fail(GLC_ERR_INVALID, "swizzle probe: cuTensorMapEncodeTiled failed");
-  swizzle_probe_kernel<<<1, 128, 4096 + 1024, ctx->stream>>>(tm, out, ctx->d_err);
+  glc::launch_pdl(ctx, swizzle_probe_kernel, 1, 128, 4096 + 1024, ctx->stream, tm, out, ctx->d_err);
   GLC_LAUNCH_CHECK(ctx, "swizzle probe");
   return 0;
 }
@@ -397,7 +399,7 @@ int gemm_quant_fused(Context* ctx, const float* dY, int ldy, const void* Wq, int
   if (e != cudaSuccess) return ctx->fail_cuda(e, "quant gemm: shared memory attribute");
   const int grid = a.tiles < ctx->num_sms ? a.tiles : ctx->num_sms;
   ProfScope prof(ctx, PROF_GEMM, 2.0 * M * static_cast<double>(Kin) * Nout, s);
-  gemm_quant_fused_kernel<<<grid, QF_THREADS, QF_SMEM_BYTES, s>>>(tm, a);
+  glc::launch_pdl(ctx, gemm_quant_fused_kernel, grid, QF_THREADS, QF_SMEM_BYTES, s, tm, a);
   GLC_LAUNCH_CHECK(ctx, "quant gemm");
   return 0;
 }

@@ -181,6 +181,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
                      const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
                      const GroupArgs args) {
+  GLC_PDL_ENTRY();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -437,6 +438,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
     gemm_tf32_pair_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
                           const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
                           const GroupArgs args) {
+  GLC_PDL_ENTRY();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
@@ -971,10 +973,10 @@ int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t str
     const int pairs = ctx->num_sms / 2;
     const int clusters = a.total_tiles < pairs ? a.total_tiles : pairs;
     if (nl == 2) a.sched = pair_schedule(ctx, a, clusters);
-    gemm_tf32_pair_kernel<<<2 * clusters, P_NUM_THREADS, P_SMEM_BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3], a);
+    glc::launch_pdl(ctx, gemm_tf32_pair_kernel, 2 * clusters, P_NUM_THREADS, P_SMEM_BYTES, stream, tm[0], tm[1], tm[2], tm[3], a);
   } else {
     const int grid = a.total_tiles < ctx->num_sms ? a.total_tiles : ctx->num_sms;
-    gemm_tf32_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3], a);
+    glc::launch_pdl(ctx, gemm_tf32_kernel, grid, NUM_THREADS, SMEM_BYTES, stream, tm[0], tm[1], tm[2], tm[3], a);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return ctx->fail_cuda(e, "launch gemm_tf32");

@@ -9,11 +9,23 @@
 #include <functional>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include <nvtx3/nvToolsExt.h>
 
 #include "../../include/gollama_cuda.h"
+
+#if defined(__CUDACC__)
+// First statement of every kernel: wait for the grid this launch depends on
+// (a no-op unless launched with programmatic serialization), then let the
+// next kernel's launch begin while this one runs.
+#define GLC_PDL_ENTRY()                                      \
+  do {                                                       \
+    asm volatile("griddepcontrol.wait;" ::: "memory");       \
+    asm volatile("griddepcontrol.launch_dependents;" :::);   \
+  } while (0)
+#endif
 
 namespace glc {
 
@@ -39,7 +51,8 @@ struct Context {
   int attn_dq_variant = 0;             // attention backward dQ: 0 automatic (= 1), 1 a CTA per query tile, 2 persistent
   int attn_fwd_variant = 0;            // attention forward: 0 automatic (= 1), 1 a CTA per query tile, 2 persistent
   int quant_path = 0;
-  bool tracing = false;                // NVTX ranges around the phases of a training step                  // dX through a stored weight: 0 automatic (= 1), 1 dequantize + GEMM, 2 fused
+  bool tracing = false;
+  bool pdl = false;                    // programmatic dependent launch between this library's kernels                // NVTX ranges around the phases of a training step                  // dX through a stored weight: 0 automatic (= 1), 1 dequantize + GEMM, 2 fused
   EncodeTiledFn encode_fn = nullptr;
   // scratch workspace owned by the context (grown on demand, never shrunk)
   void* ws = nullptr;
@@ -311,6 +324,28 @@ int ckpt_text_read(const char* path, const glc_train_config& cfg, const std::vec
 int state_write(const char* path, const StateInfo& info, const glc_train_config& cfg, int64_t n,
                 const StateFetch& fetch);
 int state_read(const char* path, const glc_train_config& cfg, int64_t n, StateInfo* info, const StateStore& store);
+
+// Kernel launch through cudaLaunchKernelEx.  With the context's pdl switch on,
+// the launch may begin while the previous kernel on the stream finishes
+// (programmatic dependent launch); every kernel launched this way starts with
+// GLC_PDL_ENTRY, which waits for that predecessor to complete and its memory
+// to be visible before touching global memory.  Off (default), it is an
+// ordinary launch.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(const Context* ctx, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = ctx->pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 inline unsigned grid_for(size_t n, int block, int num_sms, int per_sm = 8) {
   size_t g = (n + block - 1) / block;

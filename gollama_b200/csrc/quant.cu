@@ -23,6 +23,7 @@ namespace {
 // One thread per 4 consecutive outputs (n4 = n / 4 groups); round: TF32 RN.
 __global__ void dequant_kernel(const uint8_t* __restrict__ src, float* __restrict__ dst, size_t n4, int type,
                                int round) {
+  GLC_PDL_ENTRY();
   for (size_t g = blockIdx.x * size_t(blockDim.x) + threadIdx.x; g < n4; g += size_t(gridDim.x) * blockDim.x) {
     float v[4];
     qf::dequant4(src, type, g, v);
@@ -58,8 +59,8 @@ int dequant(Context* ctx, int type, const void* src, float* dst, size_t n, bool 
   if (!src || !dst || (reinterpret_cast<uintptr_t>(src) & 1) || (reinterpret_cast<uintptr_t>(dst) & 15))
     return ctx->fail(GLC_ERR_INVALID, "dequantize: source must be 2-byte and destination 16-byte aligned");
   ProfScope prof(ctx, PROF_OTHER, static_cast<double>(quant_bytes(type, n) + 4 * n), s);
-  dequant_kernel<<<grid_for(n / 4, 256, ctx->num_sms), 256, 0, s>>>(static_cast<const uint8_t*>(src), dst, n / 4,
-                                                                      type, round ? 1 : 0);
+  glc::launch_pdl(ctx, dequant_kernel, grid_for(n / 4, 256, ctx->num_sms), 256, 0, s, static_cast<const uint8_t*>(src), dst, n / 4,
+                  type, round ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "dequantize");
   return 0;
 }

@@ -26,6 +26,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
                                    float* __restrict__ rms, int rows, int cols, float eps, int round_out) {
+  GLC_PDL_ENTRY();
   const int wpb = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nc = cols >> 2;
@@ -63,6 +64,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const float* __restric
                                                           float* __restrict__ dx, float* __restrict__ dx_round,
                                                           float* __restrict__ dw_partial, int rows, int cols,
                                                           int rows_per_block, int full, int dx_accumulate) {
+  GLC_PDL_ENTRY();
   __shared__ float red[32];
   const int nc = cols >> 2;
   const int tid = threadIdx.x;
@@ -175,6 +177,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_pipe_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ rms,
     const float* __restrict__ dy, float* __restrict__ dx, float* __restrict__ dx_round,
     float* __restrict__ dw_partial, int rows, int cols, int rows_per_block, int full, int dx_accumulate) {
+  GLC_PDL_ENTRY();
   extern __shared__ float4 stage_buf[];  // PIPE_STAGES * 3 * MAXC * 256
   __shared__ float red[32];
   const int nc = cols >> 2;
@@ -294,6 +297,7 @@ constexpr int CS_WARPS = 16;
 __global__ void __cluster_dims__(CS_CL, 1, 1) __launch_bounds__(CS_WARPS * 32)
     column_sum_kernel(const float* __restrict__ partial, int nblocks, int cols, float* __restrict__ out,
                       int accumulate) {
+  GLC_PDL_ENTRY();
   __shared__ float red[CS_WARPS][33];
   __shared__ float quarter[32];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -346,7 +350,7 @@ int rmsnorm_fwd(Context* ctx, const float* x, const float* w, float* y, float* r
   const int wpb = 8;
   unsigned grid = static_cast<unsigned>((rows + wpb - 1) / wpb);
   ProfScope prof(ctx, PROF_RMSNORM, 4.0 * (2.0 * rows * cols + rows + cols), s);
-  rmsnorm_fwd_kernel<<<grid, wpb * 32, 0, s>>>(x, w, y, rms, rows, cols, eps, round_out ? 1 : 0);
+  glc::launch_pdl(ctx, rmsnorm_fwd_kernel, grid, wpb * 32, 0, s, x, w, y, rms, rows, cols, eps, round_out ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "rmsnorm_fwd");
   return 0;
 }
@@ -393,18 +397,18 @@ int rmsnorm_bwd(Context* ctx, const float* x, const float* w, const float* rms, 
     auto kern = maxc == 1 ? rmsnorm_bwd_pipe_kernel<1> : rmsnorm_bwd_pipe_kernel<2>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return ctx->fail_cuda(e, "rmsnorm_bwd: shared memory attribute");
-    kern<<<nblocks, 256, smem, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
+    glc::launch_pdl(ctx, kern, nblocks, 256, smem, s, x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
   } else if (nc <= 256)
-    rmsnorm_bwd_kernel<1><<<nblocks, 256, 0, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
+    glc::launch_pdl(ctx, rmsnorm_bwd_kernel<1>, nblocks, 256, 0, s, x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
   else if (nc <= 512)
-    rmsnorm_bwd_kernel<2><<<nblocks, 256, 0, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
+    glc::launch_pdl(ctx, rmsnorm_bwd_kernel<2>, nblocks, 256, 0, s, x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
   else if (nc <= 1024)
-    rmsnorm_bwd_kernel<4><<<nblocks, 256, 0, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
+    glc::launch_pdl(ctx, rmsnorm_bwd_kernel<4>, nblocks, 256, 0, s, x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
   else
-    rmsnorm_bwd_kernel<8><<<nblocks, 256, 0, s>>>(x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
+    glc::launch_pdl(ctx, rmsnorm_bwd_kernel<8>, nblocks, 256, 0, s, x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, fl, acc);
   GLC_LAUNCH_CHECK(ctx, "rmsnorm_bwd");
-  column_sum_kernel<<<((cols + 31) / 32) * CS_CL, CS_WARPS * 32, 0, s>>>(partial, nblocks, cols, dw,
-                                                                          dw_accumulate ? 1 : 0);
+  glc::launch_pdl(ctx, column_sum_kernel, ((cols + 31) / 32) * CS_CL, CS_WARPS * 32, 0, s, partial, nblocks, cols, dw,
+                  dw_accumulate ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "rmsnorm_bwd column sum");
   return 0;
 }

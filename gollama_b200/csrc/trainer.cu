@@ -617,6 +617,7 @@ uint64_t splitmix(uint64_t& s) {
 }
 
 __global__ void init_normal_kernel(float* p, int64_t n, uint64_t seed, float std) {
+  GLC_PDL_ENTRY();
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
     uint64_t s = seed ^ (static_cast<uint64_t>(i) * 0xD1B54A32D192ED03ull);
     auto next = [&]() {
@@ -694,8 +695,8 @@ int Model::init(Context* c, const glc_train_config& conf) {
       int rc = fill(c, params + offset[i], 1.0f, static_cast<size_t>(n), c->stream);
       if (rc) return rc;
     } else {
-      init_normal_kernel<<<grid_for(static_cast<size_t>(n), 256, c->num_sms), 256, 0, c->stream>>>(
-          params + offset[i], n, ps, cfg.init_std);
+      glc::launch_pdl(c, init_normal_kernel, grid_for(static_cast<size_t>(n), 256, c->num_sms), 256, 0, c->stream,
+                      params + offset[i], n, ps, cfg.init_std);
       GLC_LAUNCH_CHECK(c, "model init");
     }
   }

@@ -254,6 +254,8 @@ def main(argv=None):
                     help="attention forward: 0 automatic, 1 a CTA per query tile, 2 persistent CTAs")
     ap.add_argument("--attn-dq-variant", type=int, default=0, choices=[0, 1, 2],
                     help="attention backward dQ: 0 automatic, 1 a CTA per query tile, 2 persistent CTAs")
+    ap.add_argument("--pdl", type=int, default=0, choices=[0, 1],
+                    help="programmatic dependent launch between the library's kernels")
     ap.add_argument("--quant-path", type=int, default=0, choices=[0, 1, 2],
                     help="quantized dX: 0 automatic, 1 dequantize + GEMM, 2 decode inside the GEMM")
     a = ap.parse_args(argv)
@@ -263,6 +265,7 @@ def main(argv=None):
         ctx.call("glc_set_attention_split", a.attn_split)
         ctx.call("glc_set_rmsnorm_variant", a.rmsnorm_variant)
         ctx.call("glc_set_quant_path", a.quant_path)
+        ctx.call("glc_set_pdl", a.pdl)
         ctx.call("glc_set_attention_fwd_variant", a.attn_fwd_variant)
         ctx.call("glc_set_attention_dq_variant", a.attn_dq_variant)
         for n in names:

@@ -193,6 +193,12 @@ GLC_API int glc_set_quant_path(glc_ctx* ctx, int path);
  * the loss readback) as NVTX ranges for a profiler's timeline; 0 (default)
  * skips them.  Without a profiler attached the ranges cost nothing. */
 GLC_API int glc_set_tracing(glc_ctx* ctx, int on);
+/* Programmatic dependent launch (tuning; no reference counterpart): 1 lets each
+ * of this library's kernels begin launching while the previous kernel on the
+ * stream finishes; every kernel first waits for that predecessor to complete
+ * and its memory to be visible, so results are bit-identical.  0 (default):
+ * ordinary launches. */
+GLC_API int glc_set_pdl(glc_ctx* ctx, int on);
 /* Diagnostic (no reference counterpart): out[1024] receives the shared-memory
  * image of one 32 x 32 fp32 tile loaded by TMA as an MN-major tensor-core
  * operand (element (mn, k) at src[k * 32 + mn], both 1024-float device

@@ -207,6 +207,32 @@ def test_tracing_ranges_leave_the_step_unchanged(ctx):
     assert np.array_equal(out[0][1].view(np.uint32), out[1][1].view(np.uint32))
 
 
+@pytest.mark.unvalidated
+@pytest.mark.parametrize("shape", [syn.TINY_LLAMA_MODE, syn.TINY], ids=lambda s: s.name)
+def test_programmatic_dependent_launch_step_bit_identical(ctx, shape):
+    """glc_set_pdl(1): kernels launch while their predecessor finishes and wait
+    for it at entry; two steps give the same bits as ordinary launches."""
+    params = syn.init_params(shape, 37)
+    batches = [syn.batch(shape, 37 + s) for s in range(2)]
+    out = []
+    try:
+        for on in (0, 1):
+            ctx.call("glc_set_pdl", on)
+            model = NewTrainableModel(config_for(shape, **STEP_HPARAMS), ctx)
+            model.set_params(params)
+            tr = NewTrainer(model)
+            losses = [tr.TrainStep(*b) for b in batches]
+            out.append((losses, model.get_grads(), model.get_params()))
+            tr.close()
+            model.close()
+    finally:
+        ctx.call("glc_set_pdl", 0)
+    (l0, g0, w0), (l1, g1, w1) = out
+    assert l0 == l1
+    assert np.array_equal(g0.view(np.uint32), g1.view(np.uint32))
+    assert np.array_equal(w0.view(np.uint32), w1.view(np.uint32))
+
+
 VARIANTS = ["glc_set_attention_fwd_variant", "glc_set_attention_dq_variant", "glc_set_rmsnorm_variant"]
 
 
