@@ -371,9 +371,11 @@ int rmsnorm_bwd(Context* ctx, const float* x, const float* w, const float* rms, 
   if (!x || !w || !rms || !dy || !dx || !dw || !aligned16(x) || !aligned16(w) || !aligned16(dy) || !aligned16(dx) ||
       (dx_round && !aligned16(dx_round)))
     return ctx->fail(GLC_ERR_INVALID, "rmsnorm_bwd: null or misaligned pointer");
-  // pipelined variant (opt-in): rows up to 2048 columns, three blocks per SM
+  // pipelined variant (opt-in): rows up to 2048 columns.  Both variants split
+  // the rows over the same blocks, so the per-block dw partials (and their
+  // sum) are the same bits; the pipelined kernel fits three blocks per SM.
   const bool pipe = ctx->rmsnorm_variant == 2 && nc <= 512;
-  int nblocks = (pipe ? 3 : 4) * ctx->num_sms;
+  int nblocks = 4 * ctx->num_sms;
   if (nblocks > rows) nblocks = rows;
   const int rpb = (rows + nblocks - 1) / nblocks;
   nblocks = (rows + rpb - 1) / rpb;
