@@ -96,7 +96,6 @@ def b_tile_offset(chunk, r, j):
     return chunk * 4096 + r * 128 + (((j >> 1) ^ (r & 3)) << 5) + (j & 1) * 16
 
 
-@pytest.mark.unvalidated
 def test_tma_operand_swizzle_matches_producer_layout(ctx):
     """The shared-memory image of an MN-major operand box loaded by TMA
     (SWIZZLE_128B_ATOM_32B) has element (mn, k) where the fused GEMM's
