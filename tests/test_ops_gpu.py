@@ -212,7 +212,6 @@ def test_attention_fwd_bwd(ctx, orc, B, S, H, Hkv, hd):
     assert max(errs) < ATTN_TOL, errs
 
 
-@pytest.mark.unvalidated
 @pytest.mark.parametrize("B,S,H,Hkv,hd", [(1, 128, 2, 1, 64), (2, 300, 4, 2, 64), (4, 1024, 32, 4, 64),
                                           (3, 257, 3, 3, 32), (1, 2048, 8, 8, 64)])
 def test_attention_fwd_persistent_bit_identical(ctx, B, S, H, Hkv, hd):

@@ -207,7 +207,6 @@ def test_tracing_ranges_leave_the_step_unchanged(ctx):
     assert np.array_equal(out[0][1].view(np.uint32), out[1][1].view(np.uint32))
 
 
-@pytest.mark.unvalidated
 @pytest.mark.parametrize("shape", [syn.TINY_LLAMA_MODE, syn.TINY], ids=lambda s: s.name)
 def test_programmatic_dependent_launch_step_bit_identical(ctx, shape):
     """glc_set_pdl(1): kernels launch while their predecessor finishes and wait
