@@ -54,7 +54,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--profile-steps", type=int, default=2)
-    ap.add_argument("--sample-tokens", type=int, default=4, help="tokens per CPU-baseline sample")
+    ap.add_argument("--sample-tokens", type=int, default=2, help="tokens per CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--light", action="store_true",
                     help="skip the CPU baseline, the TF32 peak measurement and the profiled steps (for ncu launch lists)")
@@ -198,72 +198,143 @@ def measure_tf32_peak(device: int, seconds: float = 2.0):
 
 
 # --------------------------------------------------------------------------- CPU baseline
-def cpu_sample_rate(sample_tokens: int, steps: int = 1, warm: bool = True):
-    """Times the oracle (reference loop nests and threading: row-parallel
+class CpuSampler:
+    """The oracle with the reference's loop nests and threading (row-parallel
     forward GEMMs, single-threaded dA loop, N-parallel dB loop, everything
-    else single-threaded) on the TinyLlama shape.  Returns per-step sample
-    times of forward+backward on `sample_tokens` tokens (one sequence), the
-    clip+AdamW time per parameter, and the thread count."""
-    from gollama_b200 import synthetic as syn
-    from oracle.oracle import Config, Oracle, OptimState, TrainState
+    else single-threaded), built like Go's amd64 code (oracle/
+    liboracle_scalar.so: -O2, no vectorisation), on the host cores.
 
-    s = syn.TINYLLAMA
-    threads = os.cpu_count() or 1
-    orc = Oracle(threads=threads, literal=True)
-    cfg = Config(vocab=s.vocab, hidden=s.hidden, layers=s.layers, heads=s.heads, kv_heads=s.kv_heads, inter=s.inter,
-                 max_seq=s.seq, norm_eps=s.norm_eps, rope_theta=s.rope_theta, mode=1)
-    n = orc.param_total(cfg)
-    rng = np.random.default_rng(0)
-    params = (rng.standard_normal(n, dtype=np.float32) * np.float32(0.02))
-    for off, r, c in orc.param_layout(cfg):
-        if r == 1:
-            params[off:off + c] = 1.0
-    inp = syn.zipf_tokens(7, (1, sample_tokens), s.vocab)
-    tgt = syn.zipf_tokens(8, (1, sample_tokens), s.vocab)
-    times = []
-    for i in range(steps + (1 if warm else 0)):
+    A full TinyLlama-shape step takes the CPU hours, so one sample measures
+    (a) forward + backward of the whole 22-layer model on one sequence of
+    `sample_tokens` tokens (every GEMM, norm, SwiGLU and the 32000-wide LM head
+    scale with the token count), and (b) one query head's causal attention
+    forward + backward over a full 1024-token sequence (what (a) runs at a
+    sequence of `sample_tokens` only); clip + AdamW is timed once on a 2-layer
+    model of the same widths.  Per step (extrapolated):
+        4096 / sample_tokens * (a) + (4 sequences * 32 heads * 22 layers) * (b)
+        + clip/AdamW per parameter * 1.03e9.
+    It also measures whole reference-semantics TrainSteps of the tiny
+    configuration (2 layers, d 128, vocab 256, 4 x 64 tokens), end to end."""
+
+    def __init__(self, sample_tokens: int):
+        from gollama_b200 import synthetic as syn
+        from oracle.oracle import Config, Oracle
+
+        self.syn = syn
+        s = self.shape = syn.TINYLLAMA
+        self.sample_tokens = sample_tokens
+        self.threads = os.cpu_count() or 1
+        self.orc = Oracle(threads=self.threads, literal=True, scalar=True)
+        self.cfg = Config(vocab=s.vocab, hidden=s.hidden, layers=s.layers, heads=s.heads, kv_heads=s.kv_heads,
+                          inter=s.inter, max_seq=s.seq, norm_eps=s.norm_eps, rope_theta=s.rope_theta, mode=1)
+        n = self.n_params = self.orc.param_total(self.cfg)
+        rng = np.random.default_rng(0)
+        self.params = rng.standard_normal(n, dtype=np.float32) * np.float32(0.02)
+        for off, r, c in self.orc.param_layout(self.cfg):
+            if r == 1:
+                self.params[off:off + c] = 1.0
+        self.inp = syn.zipf_tokens(7, (1, sample_tokens), s.vocab)
+        self.tgt = syn.zipf_tokens(8, (1, sample_tokens), s.vocab)
+        hd = s.head_dim
+        self.q1 = rng.standard_normal((s.seq, hd), dtype=np.float32)
+        self.k1 = rng.standard_normal((s.seq, hd), dtype=np.float32)
+        self.v1 = rng.standard_normal((s.seq, hd), dtype=np.float32)
+        self.do1 = rng.standard_normal((s.seq, hd), dtype=np.float32)
+        # gradient buffers of the whole model, allocated and touched once (the
+        # reference allocates its gradients once and ZeroGrad clears them every
+        # step: a per-step cost, timed here as zero_s, not a per-token one)
+        self.grads = np.zeros(n, np.float32)
+        self.has = np.zeros(len(self.orc.param_layout(self.cfg)), np.uint8)
+        self.grads.fill(0.0)  # first touch
         t0 = time.perf_counter()
-        orc.forward_backward(cfg, params, inp, tgt, backward=True)
-        dt = time.perf_counter() - t0
-        if i or not warm:
-            times.append(dt)
-    del params
-    # clip + AdamW per parameter, timed on a 2-layer model of the same widths
-    small = Config(vocab=s.vocab, hidden=s.hidden, layers=2, heads=s.heads, kv_heads=s.kv_heads, inter=s.inter,
-                   max_seq=s.seq, norm_eps=s.norm_eps, rope_theta=s.rope_theta, mode=1)
-    ns = orc.param_total(small)
-    st = TrainState.create(np.full(ns, 0.01, np.float32), len(orc.param_layout(small)),
-                           OptimState(beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, lr=3e-4, grad_clip=1.0))
-    st.grads[:] = 1e-3
-    st.has_grad[:] = 1
-    t0 = time.perf_counter()
-    orc.fn("grad_clip")(st.grads.ctypes.data_as(C.c_void_p), st.has_grad.ctypes.data_as(C.c_void_p), C.byref(small),
-                        C.c_float(1.0))
-    orc.fn("adamw_step")(st.params.ctypes.data_as(C.c_void_p), st.grads.ctypes.data_as(C.c_void_p),
-                         st.has_grad.ctypes.data_as(C.c_void_p), st.m.ctypes.data_as(C.c_void_p),
-                         st.v.ctypes.data_as(C.c_void_p), C.byref(small), C.byref(st.opt))
-    opt_per_param = (time.perf_counter() - t0) / ns
-    return times, opt_per_param * n, threads
+        self.grads.fill(0.0)
+        self.zero_s = time.perf_counter() - t0
+        self.opt_s = self._optimizer_seconds()
+        self.tiny = self._tiny_step()
 
+    def _optimizer_seconds(self) -> float:
+        from oracle.oracle import Config, OptimState, TrainState
 
-def cpu_tokens_per_s(sample_s: float, sample_tokens: int, opt_s: float, tokens_per_step: int) -> float:
-    per_token = sample_s / sample_tokens
-    return tokens_per_step / (tokens_per_step * per_token + opt_s)
+        s = self.shape
+        small = Config(vocab=s.vocab, hidden=s.hidden, layers=2, heads=s.heads, kv_heads=s.kv_heads, inter=s.inter,
+                       max_seq=s.seq, norm_eps=s.norm_eps, rope_theta=s.rope_theta, mode=1)
+        orc = self.orc
+        ns = orc.param_total(small)
+        st = TrainState.create(np.full(ns, 0.01, np.float32), len(orc.param_layout(small)),
+                               OptimState(beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, lr=3e-4, grad_clip=1.0))
+        st.grads[:] = 1e-3
+        st.has_grad[:] = 1
+        t0 = time.perf_counter()
+        orc.fn("grad_clip")(st.grads.ctypes.data_as(C.c_void_p), st.has_grad.ctypes.data_as(C.c_void_p),
+                            C.byref(small), C.c_float(1.0))
+        orc.fn("adamw_step")(st.params.ctypes.data_as(C.c_void_p), st.grads.ctypes.data_as(C.c_void_p),
+                             st.has_grad.ctypes.data_as(C.c_void_p), st.m.ctypes.data_as(C.c_void_p),
+                             st.v.ctypes.data_as(C.c_void_p), C.byref(small), C.byref(st.opt))
+        return (time.perf_counter() - t0) / ns * self.n_params
 
+    def _tiny_step(self) -> dict:
+        """Whole TrainSteps (reference semantics, pkg/train/trainer.go:462-505)
+        of the tiny configuration, timed end to end."""
+        from oracle.oracle import Config, OptimState, TrainState
 
-def cpu_baseline_dict(times, opt_s, threads, sample_tokens, tokens_per_step):
-    v = cpu_tokens_per_s(statistics.mean(times), sample_tokens, opt_s, tokens_per_step)
-    return {
-        "value": v,
-        "unit": UNIT,
-        "cores": threads,
-        "kind": "port",
-        "sample": (f"oracle port with the reference's loop nests and threading on the TinyLlama shape: forward+backward "
-                   f"of 1 sequence x {sample_tokens} tokens timed ({statistics.mean(times):.2f} s), clip+AdamW over all "
-                   f"1.03e9 parameters extrapolated from a 2-layer model ({opt_s:.1f} s); per-step cost = "
-                   f"{tokens_per_step} x per-token cost + optimizer (attention at seq {sample_tokens}, not 1024, so its "
-                   f"per-token cost is underestimated)"),
-    }
+        shape = self.syn.TINY
+        params = self.syn.init_params(shape, 1)
+        inp, tgt = self.syn.batch(shape, 1)
+        ocfg = Config(vocab=shape.vocab, hidden=shape.hidden, layers=shape.layers, heads=shape.heads,
+                      kv_heads=shape.heads, inter=shape.inter, max_seq=shape.seq, norm_eps=shape.norm_eps,
+                      rope_theta=shape.rope_theta, mode=0)
+        opt = OptimState(lr=0.0, beta1=HPARAMS["Beta1"], beta2=HPARAMS["Beta2"], eps=HPARAMS["Epsilon"],
+                         weight_decay=HPARAMS["WeightDecay"], adam_step=0, initial_lr=HPARAMS["LearningRate"],
+                         warmup_steps=HPARAMS["WarmupSteps"], total_steps=HPARAMS["MaxSteps"],
+                         grad_clip=HPARAMS["GradClipNorm"], trainer_step=0)
+        st = TrainState.create(params, len(self.orc.param_layout(ocfg)), opt)
+        self.orc.train_step(ocfg, st, inp, tgt)  # warm-up
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            self.orc.train_step(ocfg, st, inp, tgt)
+            times.append(time.perf_counter() - t0)
+        sec = statistics.median(times)
+        return {"config": "tiny: 2 layers, d 128, 4 heads, FFN 344, vocab 256, batch 4 x seq 64, reference semantics",
+                "s_per_step": sec, "tokens_per_s": shape.tokens / sec, "measured": "3 whole steps, median"}
+
+    def sample(self) -> tuple[float, float]:
+        """One sample: (a) seconds, (b) seconds."""
+        t0 = time.perf_counter()
+        self.orc.fn("forward_backward")(C.byref(self.cfg), self.params.ctypes.data_as(C.c_void_p),
+                                        self.grads.ctypes.data_as(C.c_void_p), self.has.ctypes.data_as(C.c_void_p),
+                                        self.inp.ctypes.data_as(C.c_void_p), self.tgt.ctypes.data_as(C.c_void_p), 1,
+                                        self.sample_tokens, 1)
+        a = time.perf_counter() - t0
+        S, hd = self.shape.seq, self.shape.head_dim
+        t0 = time.perf_counter()
+        self.orc.attention_fwd(self.q1, self.k1, self.v1, S, 1, 1, hd)
+        self.orc.attention_bwd(self.q1, self.k1, self.v1, self.do1, S, 1, 1, hd)
+        b = time.perf_counter() - t0
+        return a, b
+
+    def step_seconds(self, a: float, b: float) -> float:
+        s = self.shape
+        return (s.tokens / self.sample_tokens) * a + (s.batch * s.heads * s.layers) * b + self.zero_s + self.opt_s
+
+    def baseline(self, samples) -> dict:
+        a = statistics.mean(x[0] for x in samples)
+        b = statistics.mean(x[1] for x in samples)
+        sec = self.step_seconds(a, b)
+        return {
+            "value": self.shape.tokens / sec,
+            "unit": UNIT,
+            "cores": self.threads,
+            "kind": "port",
+            "sample": (f"extrapolated: the oracle with the reference's loop nests and threading, built like Go's amd64 "
+                       f"code (-O2, no vectorisation), {len(samples)} sample(s): forward+backward of the 22-layer "
+                       f"TinyLlama-shape model on 1 sequence x {self.sample_tokens} tokens ({a:.2f} s) and one query "
+                       f"head's causal attention fwd+bwd over 1024 tokens ({b:.3f} s); ZeroGrad of 1.03e9 gradients "
+                       f"({self.zero_s:.1f} s) and clip+AdamW over them from a 2-layer model ({self.opt_s:.1f} s); "
+                       f"per step = {self.shape.tokens}/{self.sample_tokens} x (a) + 2816 x (b) + ZeroGrad + "
+                       f"optimizer = {sec:.0f} s"),
+            "measured_tiny_step": self.tiny,
+        }
 
 
 # --------------------------------------------------------------------------- reference arm
@@ -275,10 +346,10 @@ def run_reference(args):
 
     tokens_per_step = syn.TINYLLAMA.tokens
     W, K = max(0, args.warmup), max(1, args.steps)
-    all_times, opt_s, threads = cpu_sample_rate(args.sample_tokens, steps=W + K, warm=False)
-    times = all_times[W:]
-    v = cpu_tokens_per_s(statistics.mean(times), args.sample_tokens, opt_s, tokens_per_step)
-    base = cpu_baseline_dict(times, opt_s, threads, args.sample_tokens, tokens_per_step)
+    sampler = CpuSampler(args.sample_tokens)
+    samples = [sampler.sample() for _ in range(W + K)][W:]
+    base = sampler.baseline(samples)
+    v = base["value"]
     out = {
         "impl": "reference",
         "metric": METRIC,
@@ -343,13 +414,12 @@ def run_ours(args):
     batches = [syn.batch(shape, 1_000_003 * rank + 17 * i + 5) for i in range(nb)]
     dev_in = [ctx.from_numpy(b[0]) for b in batches]
     dev_tg = [ctx.from_numpy(b[1]) for b in batches]
-    host_in = [np.ascontiguousarray(b[0], np.int64) for b in batches]
     loss = C.c_float()
 
     def step_device(i):
         j = i % nb
-        ctx.check(lib.glc_train_step_device(tr.h, dev_in[j].ptr, dev_tg[j].ptr, host_in[j].ctypes.data_as(C.c_void_p),
-                                            B, S, C.byref(loss)), "glc_train_step_device")
+        ctx.check(lib.glc_train_step_device(tr.h, dev_in[j].ptr, dev_tg[j].ptr, B, S, C.byref(loss)),
+                  "glc_train_step_device")
 
     # pinned host staging for the end-to-end measurement
     nbytes = T * 8
@@ -495,8 +565,8 @@ def run_ours(args):
         "peaks_source": peak_src,
     }
     if world == 1 and not args.no_cpu_baseline:
-        times, opt_s, threads = cpu_sample_rate(args.sample_tokens, steps=1, warm=False)
-        out["cpu_baseline"] = cpu_baseline_dict(times, opt_s, threads, args.sample_tokens, T)
+        sampler = CpuSampler(args.sample_tokens)
+        out["cpu_baseline"] = sampler.baseline([sampler.sample()])
     print(json.dumps(out), flush=True)
     return 0
 

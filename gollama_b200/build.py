@@ -92,5 +92,23 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
     return LIB
 
 
+SELFTEST_SRC = ROOT / "tests" / "native" / "selftest.cu"
+SELFTEST_LIB = ROOT / "tests" / "native" / "_build" / "libglc_selftest.so"
+
+
+def build_selftest() -> Path:
+    """Test-only kernels (tests/native/selftest.cu) as their own shared object;
+    nothing of it is linked into libgollama_cuda.so."""
+    if SELFTEST_LIB.exists() and SELFTEST_LIB.stat().st_mtime > max(
+            SELFTEST_SRC.stat().st_mtime, (CSRC / "sm100.cuh").stat().st_mtime):
+        return SELFTEST_LIB
+    SELFTEST_LIB.parent.mkdir(parents=True, exist_ok=True)
+    cmd = [_nvcc(), *ARCH, *NVCC_FLAGS, "-shared", "-o", str(SELFTEST_LIB), str(SELFTEST_SRC)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {SELFTEST_SRC.name}:\n{r.stdout}\n{r.stderr}")
+    return SELFTEST_LIB
+
+
 if __name__ == "__main__":
     build(verbose=True, ptxas_info="--ptxas-info" in sys.argv)

@@ -9,9 +9,16 @@
 // device synchronise in the middle of its work (growing the workspace waits
 // for all queued kernels, stalling other streams such as a gradient allreduce
 // in flight).  glc_attention_bwd_noalloc serves them: the scratch is a
-// file-scope __device__ array of fixed size that every GPU loading the library
-// holds until the process exits, and the call performs no cudaMalloc, no
-// cudaFree and no allocating library call.
+// file-scope __device__ array of fixed size, and the call performs no
+// cudaMalloc, no cudaFree and no allocating library call.
+//
+// The library is built without relocatable device code, so this file is a
+// module of its own, and CUDA loads modules lazily by default: the array is
+// placed in device memory when its module is first touched on a device.  That
+// happens in glc_init (noalloc_scratch_setup below), which looks up the
+// array's device address with the device current and caches it, so a device
+// holds the array from the first context created on it until the process
+// exits, and the entry point itself only reads the cached address.
 #include <mutex>
 #include <string>
 
@@ -31,21 +38,32 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 float* g_scratch_ptr[kMaxDevices] = {nullptr};
 
+}  // namespace
+
+namespace glc {
+
+int noalloc_scratch_setup(Context* c) {
+  if (c->device < 0 || c->device >= kMaxDevices) return 0;  // the entry point reports it
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_scratch_ptr[c->device]) return 0;
+  // glc_init made c->device current; the lookup loads this file's module on
+  // that device if lazy loading has not done so yet.
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_attn_bwd_scratch);
+  if (e != cudaSuccess || !p) return c->fail_cuda(e, "attention_bwd_noalloc set-up: cudaGetSymbolAddress");
+  g_scratch_ptr[c->device] = static_cast<float*>(p);
+  return 0;
+}
+
+}  // namespace glc
+
+namespace {
+
 int scratch_for_device(glc::Context* c, float** out) {
   if (c->device < 0 || c->device >= kMaxDevices) return c->fail(GLC_ERR_UNSUPPORTED, "attention_bwd_noalloc: device index too large");
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_ptr[c->device]) {
-    int prev = -1;
-    cudaError_t e = cudaGetDevice(&prev);
-    if (e != cudaSuccess) return c->fail_cuda(e, "attention_bwd_noalloc: cudaGetDevice");
-    if (prev != c->device && (e = cudaSetDevice(c->device)) != cudaSuccess)
-      return c->fail_cuda(e, "attention_bwd_noalloc: cudaSetDevice");
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_attn_bwd_scratch);
-    if (prev != c->device) cudaSetDevice(prev);
-    if (e != cudaSuccess || !p) return c->fail_cuda(e, "attention_bwd_noalloc: cudaGetSymbolAddress");
-    g_scratch_ptr[c->device] = static_cast<float*>(p);
-  }
+  if (!g_scratch_ptr[c->device])
+    return c->fail(GLC_ERR_INVALID, "attention_bwd_noalloc: the scratch address was not set up by glc_init");
   *out = g_scratch_ptr[c->device];
   return 0;
 }

@@ -84,6 +84,10 @@ int glc_init(int device, glc_ctx** out) {
     return GLC_ERR_UNSUPPORTED;
   }
   c->encode_fn = reinterpret_cast<glc::EncodeTiledFn>(fn);
+  if (glc::noalloc_scratch_setup(c) != 0) {
+    glc_destroy(reinterpret_cast<glc_ctx*>(c));
+    return GLC_ERR_CUDA;
+  }
   *out = reinterpret_cast<glc_ctx*>(c);
   return GLC_OK;
 }
@@ -297,10 +301,18 @@ int glc_set_attention_fwd_variant(glc_ctx* ctx, int variant) {
   return GLC_OK;
 }
 
+int glc_set_attention_dkdv_variant(glc_ctx* ctx, int variant) {
+  if (!ctx) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  if (variant < 0 || variant > 2) return c->fail(GLC_ERR_INVALID, "set_attention_dkdv_variant: variant must be 0, 1 or 2");
+  c->attn_dkdv_variant = variant;
+  return GLC_OK;
+}
+
 int glc_set_attention_dq_variant(glc_ctx* ctx, int variant) {
   if (!ctx) return GLC_ERR_INVALID;
   Context* c = C_(ctx);
-  if (variant < 0 || variant > 2) return c->fail(GLC_ERR_INVALID, "set_attention_dq_variant: variant must be 0, 1 or 2");
+  if (variant < 0 || variant > 3) return c->fail(GLC_ERR_INVALID, "set_attention_dq_variant: variant must be 0 to 3");
   c->attn_dq_variant = variant;
   return GLC_OK;
 }
@@ -315,11 +327,6 @@ int glc_set_tracing(glc_ctx* ctx, int on) {
   if (!ctx) return GLC_ERR_INVALID;
   C_(ctx)->tracing = on != 0;
   return GLC_OK;
-}
-
-int glc_diag_operand_swizzle(glc_ctx* ctx, const float* src, float* out) {
-  if (!ctx) return GLC_ERR_INVALID;
-  return glc::swizzle_probe(C_(ctx), src, out);
 }
 
 int glc_set_quant_path(glc_ctx* ctx, int path) {

@@ -200,6 +200,133 @@ __global__ void embed_fwd_kernel(const int64_t* __restrict__ tok, const float* _
   }
 }
 
+// The segments of the gradient scatter, built on the device: the token
+// positions t stably sorted by their (clamped) id, the distinct ids in
+// ascending order and where each one's run starts, as the host's
+// std::stable_sort would give them.  One CTA of 1024 threads: a least-
+// significant-digit radix sort over 8-bit digits of the id (as many passes as
+// V - 1 has bytes), each pass stable (tiles of 1024 positions in order; in a
+// tile, warps in order, and lanes in order through __match_any_sync), then a
+// block-wide scan of the run heads.  Scratch: 4 * T ints (two key/position
+// buffers).  Outputs: seg_tok[nseg], seg_start[nseg + 1], order[T], *nseg_out.
+constexpr int SEG_THREADS = 1024, SEG_RADIX = 256, SEG_WARPS = SEG_THREADS / 32;
+
+__global__ void __launch_bounds__(SEG_THREADS, 1)
+    embed_segments_kernel(const int64_t* __restrict__ tok, int T, int V, int passes, int* __restrict__ scratch,
+                          int* __restrict__ seg_tok, int* __restrict__ seg_start, int* __restrict__ order,
+                          int* __restrict__ nseg_out) {
+  GLC_PDL_ENTRY();
+  __shared__ int base[SEG_RADIX], tile_total[SEG_RADIX];
+  __shared__ int warp_cnt[SEG_WARPS][SEG_RADIX + 1];  // +1: the idle lanes' digit of a partial tile
+  __shared__ int warp_heads[SEG_WARPS];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  int* keys[2] = {scratch, scratch + 2 * static_cast<size_t>(T)};
+  int* vals[2] = {scratch + T, scratch + 3 * static_cast<size_t>(T)};
+  for (int i = tid; i < T; i += SEG_THREADS) {
+    const int64_t v = tok[i];
+    keys[0][i] = (v < 0 || v >= V) ? 0 : static_cast<int>(v);
+    vals[0][i] = i;
+  }
+  __syncthreads();
+  for (int p = 0; p < passes; ++p) {
+    const int* sk = keys[p & 1];
+    const int* sv = vals[p & 1];
+    int* dk = keys[(p + 1) & 1];
+    int* dv = vals[(p + 1) & 1];
+    const int shift = 8 * p;
+    if (tid < SEG_RADIX) tile_total[tid] = 0;
+    __syncthreads();
+    for (int i = tid; i < T; i += SEG_THREADS) atomicAdd(&tile_total[(sk[i] >> shift) & 255], 1);
+    __syncthreads();
+    if (warp == 0) {
+      // exclusive scan of the 256 digit counts: 8 per lane, then across lanes
+      int c[8], run = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = run;
+        run += tile_total[8 * lane + j];
+      }
+      int incl = run;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int x = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += x;
+      }
+      const int excl = incl - run;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) base[8 * lane + j] = excl + c[j];
+    }
+    for (int t0 = 0; t0 < T; t0 += SEG_THREADS) {
+      __syncthreads();  // base is final; the previous tile's readers of warp_cnt are done
+      for (int j = lane; j <= SEG_RADIX; j += 32) warp_cnt[warp][j] = 0;
+      const int i = t0 + tid;
+      const bool active = i < T;
+      const int key = active ? sk[i] : 0;
+      const int val = active ? sv[i] : 0;
+      const int dgt = active ? ((key >> shift) & 255) : SEG_RADIX;
+      const unsigned peers = __match_any_sync(0xffffffffu, dgt);
+      const int rank = __popc(peers & lt_mask);
+      __syncwarp();
+      if (rank == 0) warp_cnt[warp][dgt] = __popc(peers);
+      __syncthreads();
+      if (tid < SEG_RADIX) {
+        int c[SEG_WARPS];
+#pragma unroll
+        for (int w = 0; w < SEG_WARPS; ++w) c[w] = warp_cnt[w][tid];
+        int run = 0;
+#pragma unroll
+        for (int w = 0; w < SEG_WARPS; ++w) {
+          warp_cnt[w][tid] = run;
+          run += c[w];
+        }
+        tile_total[tid] = run;
+      }
+      __syncthreads();
+      if (active) {
+        const int pos = base[dgt] + warp_cnt[warp][dgt] + rank;
+        dk[pos] = key;
+        dv[pos] = val;
+      }
+      __syncthreads();
+      if (tid < SEG_RADIX) base[tid] += tile_total[tid];
+    }
+    __syncthreads();  // this pass's writes are visible to the whole block
+  }
+  const int* sk = keys[passes & 1];
+  const int* sv = vals[passes & 1];
+  int nseg = 0;  // runs before the current tile (the same in every thread)
+  for (int t0 = 0; t0 < T; t0 += SEG_THREADS) {
+    const int i = t0 + tid;
+    const bool active = i < T;
+    const int key = active ? sk[i] : 0;
+    const bool head = active && (i == 0 || sk[i - 1] != key);
+    const unsigned hb = __ballot_sync(0xffffffffu, head);
+    if (lane == 0) warp_heads[warp] = __popc(hb);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int w = 0; w < SEG_WARPS; ++w) {
+      const int c = warp_heads[w];
+      before += w < warp ? c : 0;
+      total += c;
+    }
+    if (active) {
+      order[i] = sv[i];
+      if (head) {
+        const int u = nseg + before + __popc(hb & lt_mask);
+        seg_tok[u] = key;
+        seg_start[u] = i;
+      }
+    }
+    nseg += total;
+    __syncthreads();  // warp_heads is rewritten by the next tile
+  }
+  if (tid == 0) {
+    seg_start[nseg] = T;
+    *nseg_out = nseg;
+  }
+}
+
 // Gradient scatter dE[tok] += dh[t], t ascending, as one sequential sum per
 // distinct id (deterministic; no atomics).  seg_tok[u] is the u-th distinct
 // (clamped) id, rows order[seg_start[u] .. seg_start[u+1]) are its tokens in
@@ -209,13 +336,16 @@ __global__ void embed_fwd_kernel(const int64_t* __restrict__ tok, const float* _
 // several blocks; each thread owns one float4 column and fetches 8 rows ahead
 // before adding them in ascending t (the order, and so the bits, of the
 // sequential sum).
+// The segment count comes from nseg_dev when it is given (segments built on
+// the device), else from nseg.
 __global__ void embed_bwd_kernel(const int* __restrict__ seg_tok, const int* __restrict__ seg_start,
                                  const int* __restrict__ order, const float* __restrict__ dh, float* __restrict__ dE,
-                                 int nseg, int d) {
+                                 int nseg, const int* __restrict__ nseg_dev, int d) {
   GLC_PDL_ENTRY();
   const int nc = d >> 2;
   const int c = blockIdx.y * blockDim.x + threadIdx.x;
   if (c >= nc) return;
+  if (nseg_dev) nseg = *nseg_dev;
   for (int u = blockIdx.x; u < nseg; u += gridDim.x) {
     float4* row = reinterpret_cast<float4*>(dE + static_cast<size_t>(seg_tok[u]) * d);
     const int b = seg_start[u], e = seg_start[u + 1];
@@ -342,7 +472,8 @@ int embed_fwd(Context* ctx, const int64_t* tok, const float* E, const float* P, 
 }
 
 int embed_bwd(Context* ctx, const int* seg_tok, const int* seg_start, const int* order, int nseg, const float* dh,
-              float* dE, int d, cudaStream_t s) {
+              float* dE, int d, cudaStream_t s, const int* nseg_dev) {
+  // with nseg_dev, nseg is only an upper bound (the token count) for the grid
   if (nseg == 0) return 0;
   if (nseg < 0 || d <= 0 || (d & 3) || !seg_tok || !seg_start || !order || !dh || !dE)
     return ctx->fail(GLC_ERR_INVALID, "embed_bwd: bad arguments");
@@ -351,8 +482,20 @@ int embed_bwd(Context* ctx, const int* seg_tok, const int* seg_start, const int*
   unsigned gx = static_cast<unsigned>((8 * ctx->num_sms + gy - 1) / gy);
   if (gx > static_cast<unsigned>(nseg)) gx = static_cast<unsigned>(nseg);
   ProfScope prof(ctx, PROF_OTHER, 8.0 * 0, s);
-  glc::launch_pdl(ctx, embed_bwd_kernel, dim3(gx, gy), 128, 0, s, seg_tok, seg_start, order, dh, dE, nseg, d);
+  glc::launch_pdl(ctx, embed_bwd_kernel, dim3(gx, gy), 128, 0, s, seg_tok, seg_start, order, dh, dE, nseg, nseg_dev, d);
   GLC_LAUNCH_CHECK(ctx, "embed_bwd");
+  return 0;
+}
+
+int embed_segments_device(Context* ctx, const int64_t* tok, int T, int V, int* out, cudaStream_t s) {
+  if (T <= 0 || V <= 0 || !tok || !out) return ctx->fail(GLC_ERR_INVALID, "embed_segments: bad arguments");
+  int passes = 1;
+  while (passes < 4 && (static_cast<int64_t>(V) - 1) >> (8 * passes)) ++passes;
+  const EmbedSegLayout L(T);
+  ProfScope prof(ctx, PROF_OTHER, 0.0, s);
+  glc::launch_pdl(ctx, embed_segments_kernel, dim3(1), SEG_THREADS, 0, s, tok, T, V, passes, out + L.scratch,
+                  out + L.seg_tok, out + L.seg_start, out + L.order, out + L.nseg);
+  GLC_LAUNCH_CHECK(ctx, "embed_segments");
   return 0;
 }
 

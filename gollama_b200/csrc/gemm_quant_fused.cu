@@ -309,51 +309,7 @@ __global__ void __launch_bounds__(QF_THREADS, 1)
   }
 }
 
-// Diagnostic: one TMA load of a 32 x 32 fp32 MN-major box (element (mn, k)
-// at src[k * 32 + mn]) with SWIZZLE_128B_ATOM_32B, the shared-memory image
-// copied to out[1024], so a test can compare the layout the tensor core reads
-// with the one the producer warps above write (b_tile_offset).
-__global__ void __launch_bounds__(128) swizzle_probe_kernel(const __grid_constant__ CUtensorMap tm, float* out,
-                                                             int* err) {
-  GLC_PDL_ENTRY();
-  extern __shared__ uint8_t probe_raw[];  // 4096 + 1024 bytes: the tile on a 1024-byte boundary (swizzle phase)
-  uint8_t* tile = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(probe_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar;
-  __shared__ int abort_flag;
-  if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
-    abort_flag = 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(&bar, 4096);
-    tma_load_2d(tile, &tm, &bar, 0, 0);
-  }
-  const bool ok = mbar_wait(&bar, 0, &abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
-  if (threadIdx.x == 0 && !ok) mbar_drain(&bar, 0, err);
-  __syncthreads();
-  if (__syncthreads_and(ok)) {
-    for (int i = threadIdx.x; i < 1024; i += blockDim.x) out[i] = reinterpret_cast<const float*>(tile)[i];
-  }
-}
-
 }  // namespace
-
-int swizzle_probe(Context* ctx, const float* src, float* out) {
-  if (!src || !out || (reinterpret_cast<uintptr_t>(src) & 15)) return ctx->fail(GLC_ERR_INVALID, "swizzle probe: bad buffers");
-  CUtensorMap tm;
-  cuuint64_t dims[2] = {32, 32};
-  cuuint64_t strides[1] = {32 * 4};
-  cuuint32_t box[2] = {32, 32};
-  cuuint32_t estr[2] = {1, 1};
-  if (ctx->encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(src), dims, strides, box, estr,
-                        CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B) != 0)
-    return ctx->fail(GLC_ERR_INVALID, "swizzle probe: cuTensorMapEncodeTiled failed");
-  glc::launch_pdl(ctx, swizzle_probe_kernel, 1, 128, 4096 + 1024, ctx->stream, tm, out, ctx->d_err);
-  GLC_LAUNCH_CHECK(ctx, "swizzle probe");
-  return 0;
-}
 
 // Whether the fused kernel takes this weight: a decodable stored format whose
 // blocks never straddle a row or a 256-column tile.

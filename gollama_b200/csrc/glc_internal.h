@@ -48,11 +48,12 @@ struct Context {
   bool fuse_swiglu = false;            // trainer: SwiGLU forward in the gate/up GEMM epilogue (Llama semantics)
   int attn_split = 0;                  // dK/dV CTAs per KV head: 0 automatic, else a divisor of the group
   int rmsnorm_variant = 0;             // RMSNorm backward: 0 automatic (row per iteration), 1 same, 2 pipelined loads
-  int attn_dq_variant = 0;             // attention backward dQ: 0 automatic (= 1), 1 a CTA per query tile, 2 persistent
-  int attn_fwd_variant = 0;            // attention forward: 0 automatic (= 1), 1 a CTA per query tile, 2 persistent
-  int quant_path = 0;
-  bool tracing = false;
-  bool pdl = false;                    // programmatic dependent launch between this library's kernels                // NVTX ranges around the phases of a training step                  // dX through a stored weight: 0 automatic (= 1), 1 dequantize + GEMM, 2 fused
+  int attn_dq_variant = 0;             // attention backward dQ: 0 automatic (= 2), 1 a CTA per query tile, 2 persistent, 3 CTA pairs
+  int attn_fwd_variant = 0;            // attention forward: 0 automatic (= 2), 1 a CTA per query tile, 2 persistent
+  int attn_dkdv_variant = 0;           // attention backward dK/dV: 0 automatic (= 1), 1 a CTA per key tile, 2 CTA pairs
+  int quant_path = 0;                  // dX through a stored weight: 0 automatic (= 1), 1 dequantize + GEMM, 2 fused
+  bool tracing = false;                // NVTX ranges around the phases of a training step
+  bool pdl = true;                     // programmatic dependent launch between this library's kernels
   EncodeTiledFn encode_fn = nullptr;
   // scratch workspace owned by the context (grown on demand, never shrunk)
   void* ws = nullptr;
@@ -200,7 +201,6 @@ bool gemm_tile_lists(int tiles0, int kb0, int tiles1, int kb1, int clusters, std
 bool quant_fused_supported(int type, int Kin);
 // Shared-memory image (1024 floats) of one MN-major 32 x 32 TMA box loaded
 // with SWIZZLE_128B_ATOM_32B from src (element (mn, k) at src[k * 32 + mn]).
-int swizzle_probe(Context* ctx, const float* src, float* out);
 int gemm_quant_fused(Context* ctx, const float* dY, int ldy, const void* Wq, int type, float* dX, int ldx, int M,
                      int Kin, int Nout, bool accumulate, cudaStream_t s);
 // Runs up to two independent GEMMs in one persistent launch (shared tile queue).
@@ -235,7 +235,18 @@ int rope(Context* ctx, float* x, int ld, int T, int S, int nh, int hd, const flo
 int embed_fwd(Context* ctx, const int64_t* tok, const float* E, const float* P, float* out, int T, int S, int d, int V,
               cudaStream_t s);
 int embed_bwd(Context* ctx, const int* seg_tok, const int* seg_start, const int* order, int nseg, const float* dh,
-              float* dE, int d, cudaStream_t s);
+              float* dE, int d, cudaStream_t s, const int* nseg_dev = nullptr);
+// Offsets (ints) of the device-built scatter segments of T tokens in one
+// buffer of `total` ints: seg_tok[T], seg_start[T + 1], order[T], nseg[1],
+// then 4*T ints of sort scratch.
+struct EmbedSegLayout {
+  int64_t seg_tok, seg_start, order, nseg, scratch, total;
+  explicit EmbedSegLayout(int64_t T)
+      : seg_tok(0), seg_start(T), order(2 * T + 1), nseg(3 * T + 1), scratch(3 * T + 2), total(7 * T + 2) {}
+};
+// Builds the segments of embed_bwd for tok[T] (device ids) into out
+// (EmbedSegLayout(T).total ints), on the device, with no host round trip.
+int embed_segments_device(Context* ctx, const int64_t* tok, int T, int V, int* out, cudaStream_t s);
 int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, int V, float scale, float* row_logp,
                float* loss, bool write_grad, bool round_out, cudaStream_t s, bool fast_exp = false);
 // q/k/v (and their gradients) may be column slices of one fused projection
@@ -263,6 +274,10 @@ int attention_fwd(Context* ctx, const AttnIO& io, float* o, float* lse, int B, i
 // rope_cos/rope_sin ([>= S][hd/2], 16-byte aligned): when given, dq and dk
 // leave with the transposed RoPE rotation applied and TF32-rounded, as the
 // separate backward RoPE pass would leave them.
+// Looks up, with ctx->device current, the device address of the fixed scratch
+// array of glc_attention_bwd_noalloc and caches it (once per device); called
+// by glc_init.
+int noalloc_scratch_setup(Context* ctx);
 int attention_bwd(Context* ctx, const AttnIO& io, const float* o, const float* lse, const float* dO, float* D,
                   float* partial, int B, int S, int H, int Hkv, int hd, bool round_dv, cudaStream_t s,
                   const float* rope_cos = nullptr, const float* rope_sin = nullptr);

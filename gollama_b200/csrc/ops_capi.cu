@@ -102,6 +102,20 @@ int glc_embed_bwd(glc_ctx* ctx, const int64_t* tokens_host, int T, const float* 
   return glc::embed_bwd(c, dev, dev + nseg, dev + 2 * nseg + 1, nseg, dh, dE, d, c->stream);
 }
 
+int glc_embed_bwd_device(glc_ctx* ctx, const int64_t* tokens_dev, int T, const float* dh, float* dE, int d, int V) {
+  if (!ctx || T < 0 || (T && !tokens_dev)) return GLC_ERR_INVALID;
+  if (T == 0) return GLC_OK;
+  Context* c = C_(ctx);
+  const glc::EmbedSegLayout L(T);
+  void* ws = nullptr;
+  int rc = c->workspace(static_cast<size_t>(L.total) * sizeof(int), &ws);
+  if (rc) return rc;
+  int* dev = static_cast<int*>(ws);
+  rc = glc::embed_segments_device(c, tokens_dev, T, V, dev, c->stream);
+  if (rc) return rc;
+  return glc::embed_bwd(c, dev + L.seg_tok, dev + L.seg_start, dev + L.order, T, dh, dE, d, c->stream, dev + L.nseg);
+}
+
 // Uploads a host segment table to the workspace (after `offset` bytes).
 static int upload_segs(Context* c, const int64_t* segs, int nseg, size_t offset, int64_t** out, double* elems) {
   if (nseg <= 0 || !segs) return c->fail(GLC_ERR_INVALID, "segment table is empty");

@@ -518,7 +518,7 @@ struct Model {
 
   // Embedding lookup (trainer.go:275-291); Llama semantics attach the
   // gradient scatter into TokenEmbed.
-  Node* embedding(Tape& tp, const int64_t* tok_dev, const int64_t* tok_host, int B, int S) {
+  Node* embedding(Tape& tp, const int64_t* tok_dev, int B, int S) {
     const int T = B * S, d = cfg.hidden_size;
     Node* out = tp.make(T, d);
     out->require_grad = true;
@@ -526,33 +526,25 @@ struct Model {
     out->parents = llama ? std::vector<Node*>{E} : std::vector<Node*>{E, P(1)};
     ck(embed_fwd(ctx, tok_dev, E->data, llama ? nullptr : P(1)->data, out->data, T, S, d, cfg.vocab_size, tp.stream()));
     if (!llama) return out;  // no GradFn in the reference (trainer.go:290-291)
-    std::vector<int> seg_tok, seg_start, order;
-    embed_segments_host(tok_host, T, cfg.vocab_size, seg_tok, seg_start, order);
-    const int nseg = static_cast<int>(seg_tok.size());
-    std::vector<int> packed;
-    packed.reserve(seg_tok.size() + seg_start.size() + order.size());
-    packed.insert(packed.end(), seg_tok.begin(), seg_tok.end());
-    packed.insert(packed.end(), seg_start.begin(), seg_start.end());
-    packed.insert(packed.end(), order.begin(), order.end());
-    int* dev = reinterpret_cast<int*>(tp.alloc(static_cast<int64_t>(packed.size())));
-    // pageable source: the copy is staged by the driver before returning
-    if (cudaMemcpyAsync(dev, packed.data(), packed.size() * sizeof(int), cudaMemcpyHostToDevice, tp.stream()) !=
-        cudaSuccess)
-      throw StepError{GLC_ERR_CUDA};
-    if (cudaStreamSynchronize(tp.stream()) != cudaSuccess) throw StepError{GLC_ERR_CUDA};
+    // the scatter's segments (positions sorted by id) are built on the device
+    // from the resident ids: no host copy and no synchronisation
+    const EmbedSegLayout L(T);
+    int* dev = reinterpret_cast<int*>(tp.alloc(L.total));
+    ck(embed_segments_device(ctx, tok_dev, T, cfg.vocab_size, dev, tp.stream()));
     Tape* t = &tp;
-    out->grad_fn = [this, t, out, E, dev, nseg, T, d]() {
+    out->grad_fn = [this, t, out, E, dev, L, T, d]() {
       if (!out->grad_live) return;
       const bool acc = t->prepare_grad(E);
       if (!acc) ck(cudaMemsetAsync(E->grad, 0, sizeof(float) * E->numel(), t->stream()) == cudaSuccess ? 0 : GLC_ERR_CUDA);
-      ck(embed_bwd(ctx, dev, dev + nseg, dev + 2 * nseg + 1, nseg, out->grad, E->grad, d, t->stream()));
+      ck(embed_bwd(ctx, dev + L.seg_tok, dev + L.seg_start, dev + L.order, T, out->grad, E->grad, d, t->stream(),
+                   dev + L.nseg));
     };
     return out;
   }
 
   // TrainableModel.Forward (trainer.go:271-305) -> logits node.
-  Node* forward(Tape& tp, const int64_t* tok_dev, const int64_t* tok_host, int B, int S) {
-    Node* x = embedding(tp, tok_dev, tok_host, B, S);
+  Node* forward(Tape& tp, const int64_t* tok_dev, int B, int S) {
+    Node* x = embedding(tp, tok_dev, B, S);
     for (int l = 0; l < cfg.num_layers; ++l) {
       // forwardLayer (trainer.go:308-320)
       Node* n1 = rmsnorm(tp, x, P(lp(l, P_ATTN_NORM)));
@@ -838,10 +830,10 @@ struct Trainer {
     rest_for = key;
   }
 
-  int train_step(const int64_t* in_dev, const int64_t* tg_dev, const int64_t* in_host, int B, int S, float* loss_out);
+  int train_step(const int64_t* in_dev, const int64_t* tg_dev, int B, int S, float* loss_out);
 };
 
-int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int64_t* in_host, int B, int S,
+int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, int B, int S,
                         float* loss_out) {
   const auto& c = model->cfg;
   if (B <= 0 || S <= 0) return ctx->fail(GLC_ERR_INVALID, "train_step: empty batch");
@@ -865,7 +857,7 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, const int6
     Node* logits = nullptr;
     {
       TraceRange trace(ctx, "forward");
-      logits = model->forward(*tape, in_dev, in_host, B, S);
+      logits = model->forward(*tape, in_dev, B, S);
     }
     if (row_cap < T) {
       cudaFree(row_logp);
@@ -1234,13 +1226,12 @@ int glc_train_step(glc_trainer* t, const int64_t* inputs, const int64_t* targets
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(tr.tok_dev + T, targets, sizeof(int64_t) * T, cudaMemcpyHostToDevice, tr.ctx->stream);
   if (e != cudaSuccess) return tr.ctx->fail_cuda(e, "train_step: token upload");
-  return tr.train_step(tr.tok_dev, tr.tok_dev + T, inputs, B, S, loss);
+  return tr.train_step(tr.tok_dev, tr.tok_dev + T, B, S, loss);
 }
 
-int glc_train_step_device(glc_trainer* t, const int64_t* in_dev, const int64_t* tg_dev, const int64_t* in_host, int B,
-                          int S, float* loss) {
-  if (!t || !in_dev || !tg_dev || !in_host) return GLC_ERR_INVALID;
-  return t->impl.train_step(in_dev, tg_dev, in_host, B, S, loss);
+int glc_train_step_device(glc_trainer* t, const int64_t* in_dev, const int64_t* tg_dev, int B, int S, float* loss) {
+  if (!t || !in_dev || !tg_dev || B <= 0 || S <= 0) return GLC_ERR_INVALID;
+  return t->impl.train_step(in_dev, tg_dev, B, S, loss);
 }
 
 int glc_trainer_last_stats(glc_trainer* t, double* grad_norm, float* lr, int* step) {

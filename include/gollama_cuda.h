@@ -196,24 +196,27 @@ GLC_API int glc_set_tracing(glc_ctx* ctx, int on);
 /* Programmatic dependent launch (tuning; no reference counterpart): 1 lets each
  * of this library's kernels begin launching while the previous kernel on the
  * stream finishes; every kernel first waits for that predecessor to complete
- * and its memory to be visible, so results are bit-identical.  0 (default):
- * ordinary launches. */
+ * and its memory to be visible, so results are bit-identical (the default,
+ * 0.5-0.7 ms shorter TinyLlama-shape steps); 0: ordinary launches. */
 GLC_API int glc_set_pdl(glc_ctx* ctx, int on);
-/* Diagnostic (no reference counterpart): out[1024] receives the shared-memory
- * image of one 32 x 32 fp32 tile loaded by TMA as an MN-major tensor-core
- * operand (element (mn, k) at src[k * 32 + mn], both 1024-float device
- * buffers), the layout the fused dequantizing GEMM's producers reproduce. */
-GLC_API int glc_diag_operand_swizzle(glc_ctx* ctx, const float* src, float* out);
-/* Attention forward kernel (tuning; no reference counterpart): 0 automatic and
- * 1 one CTA per (query tile, batch, head); 2 one persistent CTA per SM walking
- * those items with its pipelines running across them (the next item's loads
- * and score products overlap the current item's last tiles and output).
- * Results are bit-identical. */
+/* Attention forward kernel (tuning; no reference counterpart): 1 one CTA per
+ * (query tile, batch, head); 0 automatic and 2 one persistent CTA per SM
+ * walking those items with its pipelines running across them (the next
+ * item's loads and score products overlap the current item's last tiles and
+ * output).  Results are bit-identical. */
 GLC_API int glc_set_attention_fwd_variant(glc_ctx* ctx, int variant);
-/* The same choice for the attention backward's dQ kernel: 2 walks its
- * (query tile, batch, head) items persistently, moving the next item's Q and
- * dO into TMEM while the current item's dQ is written.  Bit-identical. */
+/* The same choice for the attention backward's dQ kernel: 0 automatic and 2
+ * walk its (query tile, batch, head) items persistently, moving the next
+ * item's Q and dO into TMEM while the current item's dQ is written; 1 one CTA
+ * per item; 3 a pair of CTAs (a cluster) per 256 queries issuing M = 256
+ * tensor-core products (head_dim 64; other head sizes use 2).  Bit-identical. */
 GLC_API int glc_set_attention_dq_variant(glc_ctx* ctx, int variant);
+/* The attention backward's dK/dV kernel (tuning; no reference counterpart):
+ * 0 automatic and 1 one CTA per (128 keys, KV head, share of its query
+ * heads); 2 a pair of CTAs (a cluster) per 256 keys issuing M = 256 tensor-core
+ * products, each CTA loading half of every query-side operand (head_dim 64;
+ * other head sizes use 1).  Bit-identical. */
+GLC_API int glc_set_attention_dkdv_variant(glc_ctx* ctx, int variant);
 /* Trainer (Llama semantics): 1 computes the SwiGLU forward in the gate/up
  * GEMM's epilogue, 0 (default, faster on B200 at the TinyLlama shape) runs it
  * as its own kernel after the GEMM (diagnostics; no reference counterpart).
@@ -262,12 +265,13 @@ GLC_API int glc_attention_bwd(glc_ctx* ctx, const float* q, const float* k, cons
  * memory is wholly reserved by their own allocator or budget, and programs
  * that must not let a call synchronise the device (glc_attention_bwd's
  * workspace is cudaMalloc'ed on first use and regrown after a device sync).
- * Its scratch is a fixed 4 MiB file-scope device array (every GPU that loads
- * the library holds it until exit), so B*H*S may not exceed 1,048,576; larger
- * calls fail with GLC_ERR_INVALID.  It calls no cudaMalloc, cudaFree or
- * allocating library routine.  The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress) and should come before any
- * stream capture.  All calls share the array, which keeps the last call's
+ * Its scratch is a fixed 4 MiB file-scope device array, so B*H*S may not
+ * exceed 1,048,576; larger calls fail with GLC_ERR_INVALID.  It calls no
+ * cudaMalloc, cudaFree or allocating library routine.  glc_init places the
+ * array on its device and looks up its address (cudaGetSymbolAddress) when
+ * it creates a context, so every device with a context holds the array from
+ * then until the process exits, and this call only reads the cached address.
+ * All calls share the array, which keeps the last call's
  * contents (it is fully rewritten before use), so calls that overlap on the
  * GPU — on different streams or contexts of one device — race. */
 GLC_API int glc_attention_bwd_noalloc(glc_ctx* ctx, const float* q, const float* k, const float* v, const float* o,
@@ -285,6 +289,11 @@ GLC_API int glc_embed_fwd(glc_ctx* ctx, const int64_t* tokens, const float* E, c
 /* Embedding gradient dE[tok[t]] += dh[t] (t ascending, deterministic);
  * tokens_host are the same ids on the host. */
 GLC_API int glc_embed_bwd(glc_ctx* ctx, const int64_t* tokens_host, int T, const float* dh, float* dE, int d, int V);
+/* The same scatter with the ids in device memory: the positions are sorted
+ * by id on the device (stable, so the sums run in ascending t and the result
+ * is bit-identical to glc_embed_bwd).  Uses the context workspace. */
+GLC_API int glc_embed_bwd_device(glc_ctx* ctx, const int64_t* tokens_dev, int T, const float* dh, float* dE, int d,
+                                 int V);
 /* GradientClipping (pkg/train/optimizer.go:169-196) over the parameters that
  * have a gradient, given as a host table of nseg {start, len} int64 pairs
  * into the gradient arena (multiples of 4 floats): norm_dev (double) receives
@@ -376,9 +385,11 @@ GLC_API int glc_trainer_destroy(glc_trainer* t);
  * backward, (data-parallel gradient allreduce), gradient clipping, AdamW.
  * inputs/targets: host int64 [B*S] (row b = sequence b).  Returns the loss. */
 GLC_API int glc_train_step(glc_trainer* t, const int64_t* inputs, const int64_t* targets, int B, int S, float* loss);
-/* The same step with token ids already in device memory (no host copies). */
-GLC_API int glc_train_step_device(glc_trainer* t, const int64_t* inputs_dev, const int64_t* targets_dev,
-                                  const int64_t* inputs_host, int B, int S, float* loss);
+/* The same step with token ids already in device memory (no host copies; the
+ * embedding gradient's token order is sorted on the device).  The only host
+ * synchronisation of a step is the loss readback at its end (trainer.go:488). */
+GLC_API int glc_train_step_device(glc_trainer* t, const int64_t* inputs_dev, const int64_t* targets_dev, int B, int S,
+                                  float* loss);
 /* Global gradient norm before clipping and the learning rate of the last step. */
 GLC_API int glc_trainer_last_stats(glc_trainer* t, double* grad_norm, float* lr, int* step);
 /* Kernels launched by the last step (all of them this library's). */

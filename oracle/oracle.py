@@ -58,32 +58,36 @@ class OptimState(C.Structure):
     ]
 
 
-_lib = None
+SCALAR_LIB_PATH = HERE / "liboracle_scalar.so"
+_libs: dict = {}
 
 
-def lib() -> C.CDLL:
-    global _lib
-    if _lib is None:
-        if not LIB_PATH.exists():
+def lib(scalar: bool = False) -> C.CDLL:
+    """The oracle library: the test build, or (scalar=True) the build compiled
+    like Go's amd64 code, which the CPU baseline times."""
+    path = SCALAR_LIB_PATH if scalar else LIB_PATH
+    if path not in _libs:
+        if not path.exists():
             build()
-        _lib = C.CDLL(str(LIB_PATH))
+        L = C.CDLL(str(path))
         for pre in ("orc_", "orcd_"):
             for name in ("exp32", "log32"):
-                getattr(_lib, pre + name).restype = C.c_float
-                getattr(_lib, pre + name).argtypes = [C.c_float]
+                getattr(L, pre + name).restype = C.c_float
+                getattr(L, pre + name).argtypes = [C.c_float]
             for name in ("go_exp", "go_log"):
-                getattr(_lib, pre + name).restype = C.c_double
-                getattr(_lib, pre + name).argtypes = [C.c_double]
-            getattr(_lib, pre + "param_total").restype = C.c_int64
-            getattr(_lib, pre + "get_lr").restype = C.c_float
-            getattr(_lib, pre + "grad_clip").restype = C.c_double
-        _lib.orc_softmax_ce.restype = C.c_float
-        _lib.orcd_softmax_ce.restype = C.c_double
-        _lib.orc_forward_backward.restype = C.c_float
-        _lib.orcd_forward_backward.restype = C.c_double
-        _lib.orc_train_step.restype = C.c_float
-        _lib.orcd_train_step.restype = C.c_double
-    return _lib
+                getattr(L, pre + name).restype = C.c_double
+                getattr(L, pre + name).argtypes = [C.c_double]
+            getattr(L, pre + "param_total").restype = C.c_int64
+            getattr(L, pre + "get_lr").restype = C.c_float
+            getattr(L, pre + "grad_clip").restype = C.c_double
+        L.orc_softmax_ce.restype = C.c_float
+        L.orcd_softmax_ce.restype = C.c_double
+        L.orc_forward_backward.restype = C.c_float
+        L.orcd_forward_backward.restype = C.c_double
+        L.orc_train_step.restype = C.c_float
+        L.orcd_train_step.restype = C.c_double
+        _libs[path] = L
+    return _libs[path]
 
 
 def _p(a: np.ndarray | None):
@@ -93,8 +97,8 @@ def _p(a: np.ndarray | None):
 class Oracle:
     """Typed access to one precision of the oracle (float32: orc_, float64: orcd_)."""
 
-    def __init__(self, double: bool = False, threads: int = 1, literal: bool = False):
-        self.L = lib()
+    def __init__(self, double: bool = False, threads: int = 1, literal: bool = False, scalar: bool = False):
+        self.L = lib(scalar)
         self.pre = "orcd_" if double else "orc_"
         self.dtype = np.float64 if double else np.float32
         self.fn("set_threads")(int(threads), int(bool(literal)))

@@ -11,7 +11,7 @@ import pytest
 
 from tests.test_quant import Q4_K, sane_format_weight
 
-pytestmark = [pytest.mark.gpu, pytest.mark.unvalidated]
+pytestmark = pytest.mark.gpu
 
 GUARD = 256  # floats on each side: keeps 16-byte (and 1 KB) alignment
 SENT = np.uint32(0x7FBADBAD)

@@ -55,7 +55,6 @@ def test_rmsnorm_bwd(ctx, orc, rows, cols, full):
     assert np.max(np.abs(bdxr.numpy() - out_dx) / (np.abs(out_dx) + 1e-30)) <= 2.0**-11
 
 
-@pytest.mark.unvalidated
 @pytest.mark.parametrize("full,acc", [(0, 0), (1, 1), (1, 0)])
 @pytest.mark.parametrize("rows,cols", [(5, 128), (300, 512), (4096, 2048), (1000, 2052)])
 def test_rmsnorm_bwd_pipelined_bit_identical(ctx, rows, cols, full, acc):
@@ -237,7 +236,6 @@ def test_attention_fwd_persistent_bit_identical(ctx, B, S, H, Hkv, hd):
     assert np.array_equal(outs[0][1], outs[1][1])
 
 
-@pytest.mark.unvalidated
 @pytest.mark.parametrize("B,S,H,Hkv,hd", [(1, 128, 2, 1, 64), (2, 300, 4, 2, 64), (4, 1024, 32, 4, 64),
                                           (3, 257, 3, 3, 32)])
 def test_attention_dq_persistent_bit_identical(ctx, B, S, H, Hkv, hd):
@@ -255,6 +253,75 @@ def test_attention_dq_persistent_bit_identical(ctx, B, S, H, Hkv, hd):
     outs = []
     try:
         for variant in (1, 2):
+            ctx.call("glc_set_attention_dq_variant", variant)
+            bdq, bdk, bdv = ctx.empty(q.shape), ctx.empty(k.shape), ctx.empty(v.shape)
+            ctx.call("glc_attention_bwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, bdq.ptr, bdk.ptr, bdv.ptr,
+                     B, S, H, Hkv, hd, 0)
+            ctx.sync()
+            outs.append([a.numpy().view(np.uint32) for a in (bdq, bdk, bdv)])
+    finally:
+        ctx.call("glc_set_attention_dq_variant", 0)
+    for a, b_ in zip(*outs):
+        assert np.array_equal(a, b_)
+
+
+@pytest.mark.parametrize("B,S,H,Hkv,hd,split", [(1, 128, 2, 1, 64, 0), (2, 300, 4, 2, 64, 0), (4, 1024, 32, 4, 64, 0),
+                                                (4, 1024, 32, 4, 64, 1), (1, 2048, 8, 8, 64, 0), (3, 257, 6, 3, 64, 3),
+                                                (1, 100, 4, 2, 64, 0), (2, 640, 8, 2, 64, 2)])
+def test_attention_dkdv_pair_bit_identical(ctx, orc, B, S, H, Hkv, hd, split):
+    """glc_set_attention_dkdv_variant(2): dK/dV on CTA pairs over 256 keys
+    (ragged sequences, sequences shorter than a pair's keys, every split of
+    the query-head group) gives the bits of the one-CTA kernel; dQ unchanged."""
+    T = B * S
+    r = rng(T + 3 * H + split)
+    q = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
+    k = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    v = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    dO = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
+    bq, bk, bv, bdo = ctx.from_numpy(q), ctx.from_numpy(k), ctx.from_numpy(v), ctx.from_numpy(dO)
+    bo, blse = ctx.empty((T, H * hd)), ctx.empty((B, H, S))
+    ctx.call("glc_attention_fwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, B, S, H, Hkv, hd, 0)
+    outs = []
+    try:
+        ctx.call("glc_set_attention_split", split)
+        for variant in (1, 2):
+            ctx.call("glc_set_attention_dkdv_variant", variant)
+            for rnd in (0, 1):
+                bdq, bdk, bdv = ctx.empty(q.shape), ctx.empty(k.shape), ctx.empty(v.shape)
+                ctx.call("glc_attention_bwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, bdq.ptr, bdk.ptr,
+                         bdv.ptr, B, S, H, Hkv, hd, rnd)
+                ctx.sync()
+                outs.append([a.numpy() for a in (bdq, bdk, bdv)])
+    finally:
+        ctx.call("glc_set_attention_dkdv_variant", 0)
+        ctx.call("glc_set_attention_split", 0)
+    for a, b_ in zip(outs[:2], outs[2:]):
+        for x, y in zip(a, b_):
+            assert np.array_equal(x.view(np.uint32), y.view(np.uint32))
+    if T <= 4096:
+        ref = orc.attention_bwd(q, k, v, dO, S, H, Hkv, hd)
+        errs = [rel_fro(x, y) for x, y in zip(outs[2], ref)]
+        assert max(errs) < ATTN_TOL, errs
+
+
+@pytest.mark.parametrize("B,S,H,Hkv,hd", [(1, 128, 2, 1, 64), (2, 300, 4, 2, 64), (4, 1024, 32, 4, 64),
+                                          (1, 2048, 8, 8, 64), (3, 257, 6, 3, 64), (1, 100, 4, 2, 64)])
+def test_attention_dq_pair_bit_identical(ctx, B, S, H, Hkv, hd):
+    """glc_set_attention_dq_variant(3): dQ on CTA pairs over 256 queries
+    (ragged sequences, sequences shorter than a pair's queries) gives the
+    bits of the one-CTA kernel, with and without the RoPE epilogue."""
+    T = B * S
+    r = rng(T + 5 * H)
+    q = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
+    k = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    v = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    dO = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
+    bq, bk, bv, bdo = ctx.from_numpy(q), ctx.from_numpy(k), ctx.from_numpy(v), ctx.from_numpy(dO)
+    bo, blse = ctx.empty((T, H * hd)), ctx.empty((B, H, S))
+    ctx.call("glc_attention_fwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, B, S, H, Hkv, hd, 0)
+    outs = []
+    try:
+        for variant in (1, 3):
             ctx.call("glc_set_attention_dq_variant", variant)
             bdq, bdk, bdv = ctx.empty(q.shape), ctx.empty(k.shape), ctx.empty(v.shape)
             ctx.call("glc_attention_bwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, bdq.ptr, bdk.ptr, bdv.ptr,
@@ -345,6 +412,35 @@ def test_embedding_bwd_hot_ids(ctx, d):
     for t in range(T):
         want[tok[t]] += dh[t]
     assert np.array_equal(bdE.numpy(), want)
+
+
+@pytest.mark.parametrize("V,T,hot", [(256, 1, False), (256, 5000, True), (32000, 4096, True), (70000, 3001, False),
+                                     (40, 2049, True), (2, 1024, False)])
+def test_embedding_bwd_device_segments_bit_identical(ctx, V, T, hot):
+    """glc_embed_bwd_device sorts the positions by id on the device (one to
+    three radix passes here, partial last tiles, out-of-range ids clamped to
+    0): the scatter is bit-identical to glc_embed_bwd's host-built segments."""
+    d = 64
+    r = rng(V + T)
+    tok = r.integers(-3, V + 3, T).astype(np.int64)
+    if hot:
+        tok[r.choice(T, T // 3, replace=False)] = 7 % V
+    dh = r.standard_normal((T, d), dtype=np.float32)
+    dE0 = r.standard_normal((V, d), dtype=np.float32)
+    outs = []
+    for name in ("glc_embed_bwd", "glc_embed_bwd_device"):
+        bt, bdh, bdE = ctx.from_numpy(tok), ctx.from_numpy(dh), ctx.from_numpy(dE0)
+        src = tok.ctypes.data_as(C.c_void_p) if name == "glc_embed_bwd" else bt.ptr
+        ctx.call(name, src, T, bdh.ptr, bdE.ptr, d, V)
+        ctx.sync()
+        outs.append(bdE.numpy().view(np.uint32))
+    assert np.array_equal(outs[0], outs[1])
+    if T <= 2049:
+        clamped = np.where((tok < 0) | (tok >= V), 0, tok)
+        want = dE0.copy()
+        for t in range(T):  # dE[tok] += dh[t], t ascending
+            want[clamped[t]] += dh[t]
+        assert np.array_equal(outs[1], want.view(np.uint32))
 
 
 def test_round_tf32(ctx):

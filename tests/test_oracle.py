@@ -324,3 +324,23 @@ def test_train_step_state(o32):
     clipped = float(np.sqrt(np.sum(st.grads.astype(np.float64) ** 2)))
     assert abs(clipped - 1.0) < 1e-4
     assert math.isfinite(loss)
+
+
+@pytest.mark.parametrize("shape", [syn.TINY, syn.TINY_LLAMA_MODE], ids=lambda s: s.name)
+def test_scalar_build_bit_identical(shape):
+    """oracle/liboracle_scalar.so (built like Go's amd64 code, which the CPU
+    baseline times) computes the same bits as the test build: a whole step in
+    reference-structured (literal) threading, loss, gradients and weights."""
+    params = syn.init_params(shape, 4)
+    inputs, targets = syn.batch(shape, 4)
+    outs = []
+    for scalar in (False, True):
+        orc = Oracle(threads=2, literal=True, scalar=scalar)
+        cfg = oracle_config(shape)
+        st = TrainState.create(params, len(orc.param_layout(cfg)), oracle_optim())
+        loss, norm = orc.train_step(cfg, st, inputs, targets)
+        outs.append((loss, norm, st.grads.copy(), st.params.copy()))
+    (l0, n0, g0, p0), (l1, n1, g1, p1) = outs
+    assert l0 == l1 and n0 == n1
+    assert np.array_equal(g0.view(np.uint32), g1.view(np.uint32))
+    assert np.array_equal(p0.view(np.uint32), p1.view(np.uint32))

@@ -90,28 +90,6 @@ def test_linear_bwd_dx_q(ctx, qtype, M, K, N, acc):
     assert rel_fro(d_dx.numpy(), want) < TOL
 
 
-def b_tile_offset(chunk, r, j):
-    """gemm_quant_fused.cu's producer offset of elements 4j..4j+3 of chunk
-    `chunk`, reduction row r (bytes)."""
-    return chunk * 4096 + r * 128 + (((j >> 1) ^ (r & 3)) << 5) + (j & 1) * 16
-
-
-def test_tma_operand_swizzle_matches_producer_layout(ctx):
-    """The shared-memory image of an MN-major operand box loaded by TMA
-    (SWIZZLE_128B_ATOM_32B) has element (mn, k) where the fused GEMM's
-    producer warps store it."""
-    src = np.arange(1024, dtype=np.float32)  # element (mn, k) = k * 32 + mn
-    d_src, d_out = ctx.from_numpy(src), ctx.zeros((1024,))
-    ctx.call("glc_diag_operand_swizzle", d_src.ptr, d_out.ptr)
-    ctx.sync()
-    img = d_out.numpy()
-    for r in range(32):
-        for j in range(8):
-            for i in range(4):
-                assert img[(b_tile_offset(0, r, j) + 4 * i) // 4] == r * 32 + 4 * j + i, (r, j, i)
-
-
-@pytest.mark.unvalidated
 @pytest.mark.parametrize("qtype", [F16, Q4_0, Q8_0, Q4_1, Q5_0, Q5_1, Q4_K, Q6_K])
 @pytest.mark.parametrize("M,K,N,acc", [(64, 256, 96, 0), (300, 512, 1376, 1), (512, 2048, 704, 0), (130, 768, 36, 1)])
 def test_linear_bwd_dx_q_fused_decode(ctx, qtype, M, K, N, acc):

@@ -15,7 +15,11 @@ from tests.helpers import GRAD_RFRO, LOSS_RTOL, STEP_HPARAMS, WEIGHT_RFRO, oracl
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [syn.TINY, syn.TINY_LLAMA_MODE, syn.SMALL, syn.SMALL_LLAMA_MODE]
+# The TinyLlama-1.1B widths (d 2048, 32 query / 4 KV heads, FFN 5632, vocab
+# 32000, sequences of 1024) with 2 of its 22 layers and 2 sequences: the
+# north-star shape at a size the oracle steps through in about a minute.
+TINYLLAMA_WIDTH = syn.TINYLLAMA.with_(name="tinyllama-width-2l-b2", layers=2, batch=2)
+SHAPES = [syn.TINY, syn.TINY_LLAMA_MODE, syn.SMALL, syn.SMALL_LLAMA_MODE, TINYLLAMA_WIDTH]
 
 
 def run_oracle(shape, params, inputs, targets, steps=1):
@@ -209,8 +213,9 @@ def test_tracing_ranges_leave_the_step_unchanged(ctx):
 
 @pytest.mark.parametrize("shape", [syn.TINY_LLAMA_MODE, syn.TINY], ids=lambda s: s.name)
 def test_programmatic_dependent_launch_step_bit_identical(ctx, shape):
-    """glc_set_pdl(1): kernels launch while their predecessor finishes and wait
-    for it at entry; two steps give the same bits as ordinary launches."""
+    """glc_set_pdl(1) (the default): kernels launch while their predecessor
+    finishes and wait for it at entry; two steps give the same bits as
+    ordinary launches (glc_set_pdl(0))."""
     params = syn.init_params(shape, 37)
     batches = [syn.batch(shape, 37 + s) for s in range(2)]
     out = []
@@ -225,17 +230,17 @@ def test_programmatic_dependent_launch_step_bit_identical(ctx, shape):
             tr.close()
             model.close()
     finally:
-        ctx.call("glc_set_pdl", 0)
+        ctx.call("glc_set_pdl", 1)  # the default
     (l0, g0, w0), (l1, g1, w1) = out
     assert l0 == l1
     assert np.array_equal(g0.view(np.uint32), g1.view(np.uint32))
     assert np.array_equal(w0.view(np.uint32), w1.view(np.uint32))
 
 
-VARIANTS = ["glc_set_attention_fwd_variant", "glc_set_attention_dq_variant", "glc_set_rmsnorm_variant"]
+VARIANTS = ["glc_set_attention_fwd_variant", "glc_set_attention_dq_variant", "glc_set_attention_dkdv_variant",
+            "glc_set_rmsnorm_variant"]
 
 
-@pytest.mark.unvalidated
 @pytest.mark.parametrize("shape", [syn.TINY_LLAMA_MODE, syn.SMALL_LLAMA_MODE.with_(layers=2)], ids=lambda s: s.name)
 def test_opt_in_variants_step_bit_identical(ctx, shape):
     """A whole step (RoPE in the dQ epilogue included) with the persistent

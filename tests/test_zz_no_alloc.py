@@ -8,7 +8,9 @@ import numpy as np
 import pytest
 
 from gollama_b200.device import GlcError
-from tests.helpers import FP32_RTOL, rel_fro
+from oracle.oracle import Oracle
+from tests.helpers import FP32_RTOL, rel_fro, threads
+from tests.test_ops_gpu import ATTN_TOL, tf32
 
 pytestmark = pytest.mark.gpu
 
@@ -55,3 +57,27 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(ctx):
                  B, S, H, Hkv, hd, 0)
     assert e.value.code == -1
     assert "exceeds the fixed scratch" in str(e.value)
+
+
+def test_noalloc_matches_oracle(ctx):
+    """One causal attention backward with a KV head shared by four query heads
+    over a 1024-token sequence, against the oracle's restatement of the
+    trainer's attention (pkg/train/trainer.go:323-389, head map of
+    pkg/model/attention.go:118,149), within the bar of the other attention tests."""
+    B, S, H, Hkv, hd = 1, 1024, 4, 1, 64
+    T = B * S
+    r = np.random.default_rng(1024)
+    q = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
+    k = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    v = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    dO = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
+    bq, bk, bv, bdo = ctx.from_numpy(q), ctx.from_numpy(k), ctx.from_numpy(v), ctx.from_numpy(dO)
+    bo, blse = ctx.empty((T, H * hd)), ctx.empty((B, H, S))
+    ctx.call("glc_attention_fwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, B, S, H, Hkv, hd, 0)
+    dq, dk, dv = ctx.empty(q.shape), ctx.empty(k.shape), ctx.empty(v.shape)
+    ctx.call("glc_attention_bwd_noalloc", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, dq.ptr, dk.ptr, dv.ptr,
+             B, S, H, Hkv, hd, 0)
+    ctx.sync()
+    ref = Oracle(threads=threads()).attention_bwd(q, k, v, dO, S, H, Hkv, hd)
+    errs = [rel_fro(a.numpy(), b) for a, b in zip((dq, dk, dv), ref)]
+    assert max(errs) < ATTN_TOL, errs
