@@ -1000,645 +1000,6 @@ __global__ void __launch_bounds__(NT, 1)
   }
 }
 
-// ============================================================ dK / dV, CTA pairs
-// The dK/dV arithmetic of attn_bwd_dkdv_tc_kernel on a (2,1,1) cluster that
-// owns 256 keys (128 per CTA): every product is one tcgen05.mma.cta_group::2
-// with M = 256, issued by the even CTA ("leader"), so a pair issues as many
-// MMAs as one CTA did for 128 keys, and each CTA loads only its half of the
-// query-side operands (the B operands are split along N between the CTAs):
-//   S^T  = K Q^T    A = K (TMEM), B = Q [64 queries x hd], 32 query rows each
-//   dP^T = V dO^T   A = V (TMEM), B = dO, 32 query rows each
-//   dV  += P^T dO   A = P^T (TMEM), B = dO MN-major, 32 of the hd columns each
-//   dK  += dS^T Q   A = dS^T (TMEM), B = Q MN-major, 32 hd columns each
-// A stage is 32 KB per CTA (64 KB on the pair) instead of 64 KB per CTA.  The
-// lse and D values of a step (64 + 64 floats) are copied into the stage by
-// the producer warp, so the math warps need no block-wide staging barrier.
-// Both CTAs walk the same query steps, from the first query the leader's keys
-// see: the odd CTA's first two 64-query steps are entirely masked (zeros).
-// The per-element arithmetic and the order of every accumulation are those of
-// attn_bwd_dkdv_tc_kernel, so dK and dV are bit-identical to it.
-//
-// Barriers (same offsets in both CTAs; "leader" = used in the leader only):
-//   kv_full        each: this CTA's K and V tiles landed
-//   kv_moved       leader: every math warp of both CTAs copied K, V to TMEM
-//   qo_full[s]     leader: both CTAs' copies of stage s (expect_tx 64 KB)
-//   ld_full[s]     each: this CTA's producer wrote the lse/D of stage s
-//   qo_empty[s]    each: the step's accumulating MMAs finished reading stage s
-//   s_full[t]      each: S^T, dP^T of TMEM set t are written
-//   p_full[t]      leader: every math warp of both CTAs wrote P^T, dS^T of set t
-//   set_free[t]    leader: the MMAs reading set t finished
-//   acc_done       each: the last accumulating MMA finished
-//   drain, drain_acc  leader: abort paths of the two issuers
-template <int HD>
-struct DkdvPairLayout {
-  static constexpr int K = 128 * HD * 4, V = 128 * HD * 4;  // one CTA's key rows
-  static constexpr int QK = 32 * HD * 4;                     // 32 query rows, K-major
-  static constexpr int QM = 64 * 32 * 4;                     // 32 hd columns x 64 queries, MN-major
-  static constexpr int STAGE = 2 * QK + 2 * QM;              // Qk, dOk, Qm, dOm: 32 KB at HD = 64
-  static constexpr int NST = 4, NSET = 2;
-  static constexpr int OFF_KV = NST * STAGE;                 // K then V
-  static constexpr int OFF_LD = OFF_KV + K + V;              // [NST][lse 64 | D 64]
-  static constexpr int OFF_BAR = OFF_LD + NST * 512;
-  static constexpr int BYTES = OFF_BAR + 256 + 1024;
-  static constexpr int TMEM_COLS = 512;
-  static constexpr int K_COL = 256, V_COL = 256 + HD, DV_COL = 256 + 2 * HD, DK_COL = 256 + 3 * HD;
-  static_assert(HD == 64, "the pair kernel splits the hd columns into two 32-column MN-major chunks");
-};
-
-// Grid (2 * Hkv * nsplit, B, key-tile pairs), cluster (2, 1, 1): cluster c =
-// blockIdx.x / 2 takes KV head c / nsplit and its query heads' share c %
-// nsplit; key-tile pairs vary slowest (the longest first).
-template <int HD>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NT, 1)
-    attn_bwd_dkdv_pair_kernel(const __grid_constant__ CUtensorMap tmQk, const __grid_constant__ CUtensorMap tmQm,
-                              const __grid_constant__ CUtensorMap tmOk, const __grid_constant__ CUtensorMap tmOm,
-                              const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                              const float* __restrict__ lse, const float* __restrict__ Dv, float* __restrict__ dk_out,
-                              float* __restrict__ dv_out, int dk_ld, int dv_ld, int nsplit, int S, int H, int Hkv,
-                              float scale, float scale_log2, int round_dv, int* err) {
-  GLC_PDL_ENTRY();
-  using L = DkdvPairLayout<HD>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
-  uint64_t *kv_full = bars, *kv_moved = bars + 1, *qo_full = bars + 2, *ld_full = bars + 6, *qo_empty = bars + 10,
-           *s_full = bars + 14, *p_full = bars + 16, *set_free = bars + 18, *acc_done = bars + 20, *drain = bars + 21,
-           *drain_acc = bars + 22;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* stage_ld = reinterpret_cast<float*>(sm + L::OFF_LD);  // [NST][lse 64 | D 64]
-  const Roles ro;
-  const uint32_t rank = cluster_ctarank();
-  const int G = H / Hkv;
-  const int kp = blockIdx.z, b = blockIdx.y;
-  const int oh = static_cast<int>(blockIdx.x >> 1);  // kh * nsplit + split
-  const int kh = oh / nsplit, split = oh - kh * nsplit;
-  const int n_heads = G / nsplit;
-  const int h_first = kh * G + split * n_heads;
-  const int k0 = kp * 256 + static_cast<int>(rank) * 128, row_base = b * S;
-  const int qi0 = kp * 4, n_q64 = (S + 63) / 64;
-  const int nq = n_q64 - qi0;
-  const int n_it = n_heads * nq;
-
-  if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
-    mbar_init(kv_moved, 2 * 8);
-    for (int i = 0; i < L::NST; ++i) {
-      mbar_init(&qo_full[i], 1);
-      mbar_init(&ld_full[i], 1);
-      mbar_init(&qo_empty[i], 1);
-    }
-    for (int i = 0; i < L::NSET; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 2 * 8);
-      mbar_init(&set_free[i], 1);
-    }
-    mbar_init(acc_done, 1);
-    mbar_init(drain, 1);
-    mbar_init(drain_acc, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (ro.warp == 1) tmem_alloc_pair(tmem_slot, L::TMEM_COLS);
-  tc_fence_before();
-  // both CTAs' barriers exist before either CTA arrives on the other's
-  cluster_sync_all();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t s0 = smem_u32(sm);
-
-  if (ro.warp == 0) {
-    // K/V of this CTA's keys, then every step's query-side halves and lse/D
-    const uint32_t full_leader = mapa_cluster(qo_full, 0);
-    if (ro.lane == 0) {
-      mbar_arrive_expect_tx(kv_full, L::K + L::V);
-      tma_tile<HD, 128>(sm + L::OFF_KV, &tmK, kv_full, kh * HD, row_base + k0);
-      tma_tile<HD, 128>(sm + L::OFF_KV + L::K, &tmV, kv_full, kh * HD, row_base + k0);
-    }
-    bool ok = true;
-    for (int it = 0; it < n_it; ++it) {
-      const int st = it % L::NST;
-      const uint32_t ph = (it / L::NST) & 1;
-      const int hq = h_first + it / nq, qbase = (qi0 + it % nq) * 64, qr = row_base + qbase;
-      if (!__all_sync(0xffffffffu, mbar_wait(&qo_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER))) {
-        ok = false;
-        break;
-      }
-      if (ro.lane == 0) {
-        const uint32_t fb = full_leader + st * 8;
-        if (rank == 0) mbar_arrive_expect_tx(&qo_full[st], 2 * L::STAGE);
-        uint8_t* base = sm + st * L::STAGE;
-        const int qh = qr + static_cast<int>(rank) * 32;  // this CTA's 32 query rows of the K-major halves
-        const int ch = hq * HD + static_cast<int>(rank) * 32;  // this CTA's 32 hd columns of the MN-major halves
-#pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          tma_load_2d_pair(base + c * (32 * 128), &tmQk, fb, hq * HD + 32 * c, qh);
-          tma_load_2d_pair(base + L::QK + c * (32 * 128), &tmOk, fb, hq * HD + 32 * c, qh);
-        }
-        tma_load_2d_pair(base + 2 * L::QK, &tmQm, fb, ch, qr);
-        tma_load_2d_pair(base + 2 * L::QK + L::QM, &tmOm, fb, ch, qr);
-      }
-      // lse (scaled to log2) and D of the step's 64 queries, two of each per lane
-      float* slot = stage_ld + st * 128;
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int qa = qbase + 32 * j + ro.lane;
-        const size_t ix = (static_cast<size_t>(b) * H + hq) * S + qa;
-        slot[32 * j + ro.lane] = qa < S ? lse[ix] * LOG2E : 0.f;
-        slot[64 + 32 * j + ro.lane] = qa < S ? Dv[ix] : 0.f;
-      }
-      __syncwarp();
-      if (ro.lane == 0) mbar_arrive(&ld_full[st]);
-    }
-    if (!ok && ro.lane == 0) mbar_drain(kv_full, 0, err);
-  } else if (ro.warp == 1) {
-    if (rank == 0 && ro.lane == 0) {
-      constexpr uint32_t idesc_s = umma_idesc_tf32(256, 64, false, false);
-      const uint32_t sfull0 = mapa_cluster(s_full, 0), sfull1 = mapa_cluster(s_full, 1);
-      // K and V are A operands in TMEM once both CTAs' math warps have copied them
-      bool ok = mbar_wait(kv_moved, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
-      bool issued = false;
-      int st = 0;
-      uint32_t ph = 0;
-      tc_fence_after();
-      for (int it = 0; ok && it < n_it; ++it) {
-        const int ts = it % L::NSET;
-        const uint32_t base = s0 + st * L::STAGE;
-        if (!mbar_wait(&qo_full[st], ph, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-        if (!mbar_wait(&set_free[ts], ((it / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < HD / 8; ++kk) {
-          umma_tf32_pair_ts(tmem + ts * 128, tmem + L::K_COL + kk * 8, kdesc<32>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
-          umma_tf32_pair_ts(tmem + ts * 128 + 64, tmem + L::V_COL + kk * 8, kdesc<32>(base + L::QK, kk), idesc_s,
-                            kk > 0 ? 1u : 0u);
-        }
-        issued = true;
-        umma_commit_pair(sfull0 + ts * 8);
-        umma_commit_pair(sfull1 + ts * 8);
-        if (++st == L::NST) {
-          st = 0;
-          ph ^= 1;
-        }
-      }
-      if (!ok) {
-        // no MMA may still touch either CTA's memory when the pair leaves, and
-        // copies the producers issued for unconsumed stages signal this CTA's
-        // qo_full: wait (bounded) for them
-        if (issued) {
-          umma_commit_pair(mapa_cluster(drain, 0));
-          mbar_drain(drain, 0, err);
-        }
-        for (int i = 0; i < L::NST; ++i) {
-          mbar_drain(&qo_full[st], ph, err);
-          if (++st == L::NST) {
-            st = 0;
-            ph ^= 1;
-          }
-        }
-      }
-    }
-  } else if (ro.warp == ACC_WARP) {
-    // dV += P^T dO and dK += dS^T Q of each step once both CTAs' math warps
-    // have written P and dS; its commits also cover the step's S/dP MMAs
-    if (rank == 0 && ro.lane == 0) {
-      constexpr uint32_t idesc_a = umma_idesc_tf32(256, HD, false, true);
-      const uint32_t empty0 = mapa_cluster(qo_empty, 0), empty1 = mapa_cluster(qo_empty, 1);
-      const uint32_t free0 = mapa_cluster(set_free, 0);
-      bool ok = true, issued = false;
-      for (int pit = 0; ok && pit < n_it; ++pit) {
-        const int ps = pit % L::NST, pts = pit % L::NSET;
-        const uint32_t base = s0 + ps * L::STAGE;
-        if (!mbar_wait(&p_full[pts], (pit / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t acc = (pit > 0 || kk > 0) ? 1u : 0u;
-          umma_tf32_pair_ts(tmem + L::DV_COL, tmem + pts * 128 + kk * 8, mdesc<64>(base + 2 * L::QK + L::QM, kk),
-                            idesc_a, acc);
-          umma_tf32_pair_ts(tmem + L::DK_COL, tmem + pts * 128 + 64 + kk * 8, mdesc<64>(base + 2 * L::QK, kk),
-                            idesc_a, acc);
-        }
-        issued = true;
-        umma_commit_pair(free0 + pts * 8);
-        umma_commit_pair(empty0 + ps * 8);
-        umma_commit_pair(empty1 + ps * 8);
-      }
-      if (ok) {
-        umma_commit_pair(mapa_cluster(acc_done, 0));
-        umma_commit_pair(mapa_cluster(acc_done, 1));
-      }
-      if (!ok && issued) {
-        umma_commit_pair(mapa_cluster(drain_acc, 0));
-        mbar_drain(drain_acc, 0, err);
-      }
-    }
-  } else {
-    const int q = ro.quarter(), hf = ro.half();
-    const int c = q * 32 + ro.lane;  // key row within this CTA's tile
-    const int key = k0 + c;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    const uint32_t moved_leader = mapa_cluster(kv_moved, 0), pfull_leader = mapa_cluster(p_full, 0);
-    bool ok = true;
-    // K and V rows -> TMEM, then tell the leader's score issuer
-    if (__all_sync(0xffffffffu, mbar_wait(kv_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
-      tile_rows_to_tmem<HD>(sm + L::OFF_KV, c, lane_addr, L::K_COL, 0, hf);
-      tile_rows_to_tmem<HD>(sm + L::OFF_KV + L::K, c, lane_addr, L::V_COL, HD / 32, hf);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (ro.lane == 0) mbar_arrive_cluster(moved_leader);
-    } else {
-      ok = false;
-    }
-    for (int it = 0; ok && it < n_it; ++it) {
-      const int st = it % L::NST, ts = it % L::NSET;
-      const int qbase = (qi0 + it % nq) * 64;
-      WAIT_OR_BREAK(&ld_full[st], (it / L::NST) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
-      WAIT_OR_BREAK(&s_full[ts], (it / L::NSET) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
-      tc_fence_after();
-      // this warp's 32 queries: S^T columns [hf*32, +32), dP^T columns 64 + [hf*32, +32)
-      const float* slot = stage_ld + st * 128;
-      float lse2[32], dqs[32];
-      {
-        const float4* l4 = reinterpret_cast<const float4*>(slot + hf * 32);
-        const float4* d4 = reinterpret_cast<const float4*>(slot + 64 + hf * 32);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 a = l4[i], d = d4[i];
-          lse2[4 * i] = a.x; lse2[4 * i + 1] = a.y; lse2[4 * i + 2] = a.z; lse2[4 * i + 3] = a.w;
-          dqs[4 * i] = d.x * scale; dqs[4 * i + 1] = d.y * scale; dqs[4 * i + 2] = d.z * scale; dqs[4 * i + 3] = d.w * scale;
-        }
-      }
-      const uint32_t sa = lane_addr + ts * 128 + hf * 32;
-      uint32_t sv[32], dpv[32];
-      const int q_lo = qbase + hf * 32;
-      if (q_lo + 31 < k0) {
-        // every query of this half precedes every key of the tile: all masked
-#pragma unroll
-        for (int e = 0; e < 32; ++e) sv[e] = dpv[e] = 0u;
-      } else {
-        tmem_ld_32x32b_x32(sa, sv);
-        tmem_ld_32x32b_x32(sa + 64, dpv);
-        tmem_ld_wait();
-        // every query of this half is past every key of the tile and inside
-        // the sequence: no mask (warp-uniform test)
-        if (q_lo >= k0 + 127 && q_lo + 32 <= S && k0 + 128 <= S) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float p = fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2[e]));
-            const float ds = p * fmaf(__uint_as_float(dpv[e]), scale, -dqs[e]);
-            sv[e] = tf32_bits(p);
-            dpv[e] = tf32_bits(ds);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int qa = q_lo + e;
-            const bool valid = qa < S && key < S && key <= qa;
-            const float p = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2[e])) : 0.f;
-            const float ds = p * fmaf(__uint_as_float(dpv[e]), scale, -dqs[e]);
-            sv[e] = tf32_bits(p);
-            dpv[e] = tf32_bits(ds);
-          }
-        }
-      }
-      tmem_st_32x32b_x32(sa, sv);
-      tmem_st_32x32b_x32(sa + 64, dpv);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (ro.lane == 0) mbar_arrive_cluster(pfull_leader + ts * 8);
-    }
-    if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
-      tc_fence_after();
-      // final dk/dv at the KV head's columns, or this cluster's partial;
-      // column half 0 writes dV, half 1 writes dK
-      const size_t trow = static_cast<size_t>(row_base) + key;
-      const int part = hf;
-#pragma unroll 1
-      for (int cc = 0; cc < HD / 32; ++cc) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_addr + (part == 0 ? L::DV_COL : L::DK_COL) + cc * 32, v);
-        tmem_ld_wait();
-        if (key < S) {
-          float* dst = (part == 0 ? dv_out + trow * dv_ld : dk_out + trow * dk_ld) + oh * HD + cc * 32;
-          const bool rnd = part == 0 && round_dv && nsplit == 1;
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            float4 o4 = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
-                                    __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
-            if (rnd) o4 = make_float4(round_tf32(o4.x), round_tf32(o4.y), round_tf32(o4.z), round_tf32(o4.w));
-            reinterpret_cast<float4*>(dst)[g] = o4;
-          }
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  // neither CTA leaves (or frees TMEM) while the other may still touch its
-  // shared memory, barriers or TMEM
-  cluster_sync_all();
-  if (ro.warp == 1) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem, L::TMEM_COLS);
-  }
-}
-
-// ================================================================= dQ, CTA pairs
-// attn_bwd_dq_tc_kernel's arithmetic on a (2,1,1) cluster that owns 256
-// queries of one head (128 per CTA): S = Q K^T, dP = dO V^T and dQ += dS K are
-// tcgen05.mma.cta_group::2 products with M = 256 issued by the even CTA, the
-// key-side B operands split along N between the CTAs (32 of a step's 64 keys
-// of K and V each for S and dP, 32 of the hd columns of K for dQ), so a stage
-// is 24 KB per CTA.  Both CTAs walk the key steps up to the pair's last
-// query: the even CTA's last two 64-key steps are entirely masked (zeros).
-// lse and D are per query row, read once.  Bit-identical to the grid kernel.
-//
-// Barriers (same offsets in both CTAs; "leader" = used in the leader only):
-//   qo_full        each: this CTA's Q and dO tiles landed
-//   qo_moved       leader: every math warp of both CTAs copied Q, dO to TMEM
-//   kv_full[s]     leader: both CTAs' copies of stage s (expect_tx 48 KB)
-//   kv_empty[s]    each: the step's dQ MMAs finished reading stage s
-//   s_full[t]      each: S, dP of TMEM set t are written
-//   p_full[t]      leader: every math warp of both CTAs wrote dS of set t
-//   set_free[t]    leader: the MMAs reading set t finished
-//   acc_done       each: the last dQ MMA finished
-//   drain, drain_acc  leader: abort paths of the two issuers
-template <int HD>
-struct DqPairLayout {
-  static constexpr int Q = 128 * HD * 4, O = 128 * HD * 4;
-  static constexpr int KK = 32 * HD * 4;    // 32 key rows, K-major
-  static constexpr int KM = 64 * 32 * 4;    // 32 hd columns x 64 keys, MN-major
-  static constexpr int STAGE = 2 * KK + KM; // K (K-major), V (K-major), K (MN-major): 24 KB at HD = 64
-  static constexpr int NST = 4, NSET = 2;
-  static constexpr int OFF_QO = NST * STAGE;
-  static constexpr int OFF_BAR = OFF_QO + Q + O;
-  static constexpr int BYTES = OFF_BAR + 256 + 1024;
-  static constexpr int TMEM_COLS = 512;
-  static constexpr int Q_COL = 256, O_COL = 256 + HD, DQ_COL = 256 + 2 * HD;
-  static_assert(HD == 64, "the pair kernel splits the hd columns into two 32-column MN-major chunks");
-};
-
-// Grid (2 * H, B, query-tile pairs), cluster (2, 1, 1): head blockIdx.x / 2;
-// the last query pairs (the longest) are dispatched first.
-template <int HD>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NT, 1)
-    attn_bwd_dq_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmO,
-                            const __grid_constant__ CUtensorMap tmKk, const __grid_constant__ CUtensorMap tmKm,
-                            const __grid_constant__ CUtensorMap tmVk, const float* __restrict__ lse,
-                            const float* __restrict__ Dv, float* __restrict__ dq, int dq_ld, int S, int H, int Hkv,
-                            int n_qp, float scale, float scale_log2, const float* __restrict__ rope_cos,
-                            const float* __restrict__ rope_sin, int* err) {
-  GLC_PDL_ENTRY();
-  using L = DqPairLayout<HD>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
-  uint64_t *qo_full = bars, *qo_moved = bars + 1, *kv_full = bars + 2, *kv_empty = bars + 6, *s_full = bars + 10,
-           *p_full = bars + 12, *set_free = bars + 14, *acc_done = bars + 16, *drain = bars + 17,
-           *drain_acc = bars + 18;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  const Roles ro;
-  const uint32_t rank = cluster_ctarank();
-  const int qp = n_qp - 1 - static_cast<int>(blockIdx.z);
-  const int h = static_cast<int>(blockIdx.x >> 1), b = blockIdx.y, kh = h / (H / Hkv);
-  const int q0 = qp * 256 + static_cast<int>(rank) * 128, row_base = b * S;
-  const int n_k64 = (S + 63) / 64;
-  const int nk = min(n_k64, (qp * 256 + 256) / 64);
-
-  if (threadIdx.x == 0) {
-    mbar_init(qo_full, 1);
-    mbar_init(qo_moved, 2 * 8);
-    for (int i = 0; i < L::NST; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-    }
-    for (int i = 0; i < L::NSET; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 2 * 8);
-      mbar_init(&set_free[i], 1);
-    }
-    mbar_init(acc_done, 1);
-    mbar_init(drain, 1);
-    mbar_init(drain_acc, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (ro.warp == 1) tmem_alloc_pair(tmem_slot, L::TMEM_COLS);
-  tc_fence_before();
-  cluster_sync_all();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t s0 = smem_u32(sm);
-
-  if (ro.warp == 0) {
-    if (ro.lane == 0) {
-      mbar_arrive_expect_tx(qo_full, L::Q + L::O);
-      tma_tile<HD, 128>(sm + L::OFF_QO, &tmQ, qo_full, h * HD, row_base + q0);
-      tma_tile<HD, 128>(sm + L::OFF_QO + L::Q, &tmO, qo_full, h * HD, row_base + q0);
-      const uint32_t full_leader = mapa_cluster(kv_full, 0);
-      bool ok = true;
-      for (int j = 0; j < nk; ++j) {
-        const int st = j % L::NST;
-        const uint32_t ph = (j / L::NST) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
-        const uint32_t fb = full_leader + st * 8;
-        if (rank == 0) mbar_arrive_expect_tx(&kv_full[st], 2 * L::STAGE);
-        uint8_t* base = sm + st * L::STAGE;
-        const int kr = row_base + j * 64, kh_rows = kr + static_cast<int>(rank) * 32;
-#pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          tma_load_2d_pair(base + c * (32 * 128), &tmKk, fb, kh * HD + 32 * c, kh_rows);
-          tma_load_2d_pair(base + L::KK + c * (32 * 128), &tmVk, fb, kh * HD + 32 * c, kh_rows);
-        }
-        tma_load_2d_pair(base + 2 * L::KK, &tmKm, fb, kh * HD + static_cast<int>(rank) * 32, kr);
-      }
-      if (!ok) mbar_drain(qo_full, 0, err);
-    }
-  } else if (ro.warp == 1) {
-    if (rank == 0 && ro.lane == 0) {
-      constexpr uint32_t idesc_s = umma_idesc_tf32(256, 64, false, false);
-      const uint32_t sfull0 = mapa_cluster(s_full, 0), sfull1 = mapa_cluster(s_full, 1);
-      bool ok = mbar_wait(qo_moved, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
-      bool issued = false;
-      int st = 0;
-      uint32_t ph = 0;
-      tc_fence_after();
-      for (int j = 0; ok && j < nk; ++j) {
-        const int ts = j % L::NSET;
-        const uint32_t base = s0 + st * L::STAGE;
-        if (!mbar_wait(&kv_full[st], ph, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-        if (!mbar_wait(&set_free[ts], ((j / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < HD / 8; ++kk) {
-          umma_tf32_pair_ts(tmem + ts * 128, tmem + L::Q_COL + kk * 8, kdesc<32>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
-          umma_tf32_pair_ts(tmem + ts * 128 + 64, tmem + L::O_COL + kk * 8, kdesc<32>(base + L::KK, kk), idesc_s,
-                            kk > 0 ? 1u : 0u);
-        }
-        issued = true;
-        umma_commit_pair(sfull0 + ts * 8);
-        umma_commit_pair(sfull1 + ts * 8);
-        if (++st == L::NST) {
-          st = 0;
-          ph ^= 1;
-        }
-      }
-      if (!ok) {
-        if (issued) {
-          umma_commit_pair(mapa_cluster(drain, 0));
-          mbar_drain(drain, 0, err);
-        }
-        for (int i = 0; i < L::NST; ++i) {
-          mbar_drain(&kv_full[st], ph, err);
-          if (++st == L::NST) {
-            st = 0;
-            ph ^= 1;
-          }
-        }
-      }
-    }
-  } else if (ro.warp == ACC_WARP) {
-    // dQ += dS K once both CTAs' math warps have written dS; its commits also
-    // cover the step's S/dP MMAs
-    if (rank == 0 && ro.lane == 0) {
-      constexpr uint32_t idesc_q = umma_idesc_tf32(256, HD, false, true);
-      const uint32_t empty0 = mapa_cluster(kv_empty, 0), empty1 = mapa_cluster(kv_empty, 1);
-      const uint32_t free0 = mapa_cluster(set_free, 0);
-      bool ok = true, issued = false;
-      for (int pj = 0; ok && pj < nk; ++pj) {
-        const int ps = pj % L::NST, pts = pj % L::NSET;
-        const uint32_t base = s0 + ps * L::STAGE;
-        if (!mbar_wait(&p_full[pts], (pj / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_tf32_pair_ts(tmem + L::DQ_COL, tmem + pts * 128 + kk * 8, mdesc<64>(base + 2 * L::KK, kk), idesc_q,
-                            (pj > 0 || kk > 0) ? 1u : 0u);
-        issued = true;
-        umma_commit_pair(free0 + pts * 8);
-        umma_commit_pair(empty0 + ps * 8);
-        umma_commit_pair(empty1 + ps * 8);
-      }
-      if (ok) {
-        umma_commit_pair(mapa_cluster(acc_done, 0));
-        umma_commit_pair(mapa_cluster(acc_done, 1));
-      }
-      if (!ok && issued) {
-        umma_commit_pair(mapa_cluster(drain_acc, 0));
-        mbar_drain(drain_acc, 0, err);
-      }
-    }
-  } else {
-    const int q = ro.quarter(), hf = ro.half();
-    const int r = q * 32 + ro.lane;
-    const int qa = q0 + r;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    const uint32_t moved_leader = mapa_cluster(qo_moved, 0), pfull_leader = mapa_cluster(p_full, 0);
-    const size_t lrow = (static_cast<size_t>(b) * H + h) * S + (qa < S ? qa : 0);
-    const float lse2 = lse[lrow] * LOG2E, Dq = Dv[lrow];
-    bool ok = true;
-    // Q and dO rows -> TMEM, then tell the leader's score issuer
-    if (__all_sync(0xffffffffu, mbar_wait(qo_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
-      tile_rows_to_tmem<HD>(sm + L::OFF_QO, r, lane_addr, L::Q_COL, 0, hf);
-      tile_rows_to_tmem<HD>(sm + L::OFF_QO + L::Q, r, lane_addr, L::O_COL, HD / 32, hf);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (ro.lane == 0) mbar_arrive_cluster(moved_leader);
-    } else {
-      ok = false;
-    }
-    for (int j = 0; ok && j < nk; ++j) {
-      const int ts = j % L::NSET;
-      WAIT_OR_BREAK(&s_full[ts], (j / L::NSET) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
-      tc_fence_after();
-      // this warp's 32 keys: S columns [hf*32, +32), dP columns 64 + [hf*32, +32)
-      const uint32_t sa = lane_addr + ts * 128 + hf * 32;
-      uint32_t sv[32];
-      const int k_lo = j * 64 + hf * 32;
-      const float nDs = -Dq * scale;
-      if (k_lo > q0 + 127) {
-        // every key of this half follows every row of the tile: all masked
-#pragma unroll
-        for (int e = 0; e < 32; ++e) sv[e] = 0u;
-      } else {
-        uint32_t dpv[32];
-        tmem_ld_32x32b_x32(sa, sv);
-        tmem_ld_32x32b_x32(sa + 64, dpv);
-        tmem_ld_wait();
-        // every key of this half precedes every row of the tile: no mask
-        // (warp-uniform test)
-        if (k_lo + 32 <= q0 + 1 && q0 + 128 <= S) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float p = fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2));
-            sv[e] = tf32_bits(p * fmaf(__uint_as_float(dpv[e]), scale, nDs));
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int key = k_lo + e;
-            const bool valid = qa < S && key < S && key <= qa;
-            const float p = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2)) : 0.f;
-            sv[e] = tf32_bits(p * fmaf(__uint_as_float(dpv[e]), scale, nDs));
-          }
-        }
-      }
-      tmem_st_32x32b_x32(sa, sv);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (ro.lane == 0) mbar_arrive_cluster(pfull_leader + ts * 8);
-    }
-    if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
-      tc_fence_after();
-      float* drow = dq + (static_cast<size_t>(row_base) + qa) * static_cast<size_t>(dq_ld) + h * HD;
-#pragma unroll 1
-      for (int cc = hf; cc < HD / 32; cc += 2) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_addr + L::DQ_COL + cc * 32, v);
-        tmem_ld_wait();
-        if (qa < S && rope_cos) {
-          // transposed RoPE rotation of the row's pairs cc*16 .. cc*16+15 at
-          // position qa, then TF32 rounding
-          const float4* cr = reinterpret_cast<const float4*>(rope_cos + static_cast<size_t>(qa) * (HD / 2) + cc * 16);
-          const float4* sr = reinterpret_cast<const float4*>(rope_sin + static_cast<size_t>(qa) * (HD / 2) + cc * 16);
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const float4 c4 = cr[g], s4 = sr[g];
-            const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int p = 4 * g + e;
-              const float x0 = __uint_as_float(v[2 * p]), x1 = __uint_as_float(v[2 * p + 1]);
-              v[2 * p] = __float_as_uint(round_tf32(__fadd_rn(__fmul_rn(x0, cs[e]), __fmul_rn(x1, sn[e]))));
-              v[2 * p + 1] = __float_as_uint(round_tf32(__fadd_rn(__fmul_rn(-x0, sn[e]), __fmul_rn(x1, cs[e]))));
-            }
-          }
-        }
-        if (qa < S) {
-#pragma unroll
-          for (int g = 0; g < 8; ++g)
-            reinterpret_cast<float4*>(drow + cc * 32)[g] =
-                make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]), __uint_as_float(v[4 * g + 2]),
-                            __uint_as_float(v[4 * g + 3]));
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync_all();
-  if (ro.warp == 1) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem, L::TMEM_COLS);
-  }
-}
-
 // dk[t][kh] = sum over the nsplit partials of the KV head, partial[t][kh *
 // nsplit + g] (g ascending: deterministic); dv the same, optionally
 // TF32-rounded.
@@ -2323,21 +1684,15 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
              float* partial, int B, int S, int H, int Hkv, bool round_dv, const float* rope_cos,
              const float* rope_sin, cudaStream_t s) {
   const float *q = io.q, *k = io.k, *v = io.v;
-  static SmemFlags done_g, done_q, done_pq, done_pair, done_qpair;
-  // dQ: 1 grid kernel, 0 automatic and 2 persistent, 3 CTA pairs (head_dim 64)
-  const bool dq_pair = HD == 64 && ctx->attn_dq_variant == 3;
-  const bool dq_persist = !dq_pair && ctx->attn_dq_variant != 1;
-  // dK/dV on CTA pairs (head_dim 64 only): variant 2
-  const bool dkdv_pair = HD == 64 && ctx->attn_dkdv_variant == 2;
-  int rc = dkdv_pair ? set_smem(ctx, attn_bwd_dkdv_pair_kernel<64>, DkdvPairLayout<64>::BYTES, done_pair)
-                     : set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD>, DkdvLayout<HD>::BYTES, done_g);
+  static SmemFlags done_g, done_q, done_pq;
+  const bool dq_persist = ctx->attn_dq_variant != 1;  // automatic: persistent
+  int rc = set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD>, DkdvLayout<HD>::BYTES, done_g);
   if (!rc)
-    rc = dq_pair      ? set_smem(ctx, attn_bwd_dq_pair_kernel<64>, DqPairLayout<64>::BYTES, done_qpair)
-         : dq_persist ? set_smem(ctx, attn_bwd_dq_persist_kernel<HD>, PDqLayout<HD>::BYTES, done_pq)
-                      : set_smem(ctx, attn_bwd_dq_tc_kernel<HD>, DqLayout<HD>::BYTES, done_q);
+    rc = dq_persist ? set_smem(ctx, attn_bwd_dq_persist_kernel<HD>, PDqLayout<HD>::BYTES, done_pq)
+                    : set_smem(ctx, attn_bwd_dq_tc_kernel<HD>, DqLayout<HD>::BYTES, done_q);
   if (rc) return rc;
   const int T = B * S, G = H / Hkv;
-  CUtensorMap tQk64, tQm64, tOk64, tOm64, tK128, tV128, tQ128, tO128, tKk64, tKm64, tVk64, tQk32, tOk32, tKk32, tVk32;
+  CUtensorMap tQk64, tQm64, tOk64, tOm64, tK128, tV128, tQ128, tO128, tKk64, tKm64, tVk64;
   const int qw = H * HD, kw = Hkv * HD;
   if ((rc = encode(ctx, &tQk64, q, qw, io.q_ld, T, 64, false)) || (rc = encode(ctx, &tQm64, q, qw, io.q_ld, T, 64, true)) ||
       (rc = encode(ctx, &tOk64, dO, qw, qw, T, 64, false)) || (rc = encode(ctx, &tOm64, dO, qw, qw, T, 64, true)) ||
@@ -2345,12 +1700,6 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
       (rc = encode(ctx, &tQ128, q, qw, io.q_ld, T, 128, false)) || (rc = encode(ctx, &tO128, dO, qw, qw, T, 128, false)) ||
       (rc = encode(ctx, &tKk64, k, kw, io.k_ld, T, 64, false)) || (rc = encode(ctx, &tKm64, k, kw, io.k_ld, T, 64, true)) ||
       (rc = encode(ctx, &tVk64, v, kw, io.v_ld, T, 64, false)))
-    return rc;
-  if (dkdv_pair &&
-      ((rc = encode(ctx, &tQk32, q, qw, io.q_ld, T, 32, false)) || (rc = encode(ctx, &tOk32, dO, qw, qw, T, 32, false))))
-    return rc;
-  if (dq_pair &&
-      ((rc = encode(ctx, &tKk32, k, kw, io.k_ld, T, 32, false)) || (rc = encode(ctx, &tVk32, v, kw, io.v_ld, T, 32, false))))
     return rc;
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(HD)));
   const double causal = 0.5 * static_cast<double>(S) * (S + 1);
@@ -2376,18 +1725,10 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
       }
     if (ctx->attn_split > 0 && G % ctx->attn_split == 0) nsplit = ctx->attn_split;
   }
-  // the dK/dV kernel: grid kernel, or CTA pairs over 256 keys
   auto launch_dkdv = [&](int ns, float* dk_out, float* dv_out, int dk_ld, int dv_ld, int rnd) {
-    if (dkdv_pair) {
-      const int n_kp = (S + 255) / 256;
-      glc::launch_pdl(ctx, attn_bwd_dkdv_pair_kernel<64>, dim3(2 * Hkv * ns, B, n_kp), NT, DkdvPairLayout<64>::BYTES, s,
-                      tQk32, tQm64, tOk32, tOm64, tK128, tV128, lse, D, dk_out, dv_out, dk_ld, dv_ld, ns, S, H, Hkv,
-                      scale, scale * LOG2E, rnd, ctx->d_err);
-    } else {
-      glc::launch_pdl(ctx, attn_bwd_dkdv_tc_kernel<HD>, dim3(Hkv * ns, B, n_kt), NT, DkdvLayout<HD>::BYTES, s,
-                      tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, dk_out, dv_out, dk_ld, dv_ld, ns, S, H, Hkv,
-                      scale, scale * LOG2E, rnd, ctx->d_err);
-    }
+    glc::launch_pdl(ctx, attn_bwd_dkdv_tc_kernel<HD>, dim3(Hkv * ns, B, n_kt), NT, DkdvLayout<HD>::BYTES, s,
+                    tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, dk_out, dv_out, dk_ld, dv_ld, ns, S, H, Hkv,
+                    scale, scale * LOG2E, rnd, ctx->d_err);
   };
   if (nsplit == 1) {
     launch_dkdv(1, io.dk, io.dv, io.dk_ld, io.dv_ld, round_dv ? 1 : 0);
@@ -2407,12 +1748,7 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     GLC_LAUNCH_CHECK(ctx, "attention_bwd group sum");
   }
   const int n_qt = (S + 127) / 128;
-  if (dq_pair) {
-    const int n_qp = (S + 255) / 256;
-    glc::launch_pdl(ctx, attn_bwd_dq_pair_kernel<64>, dim3(2 * H, B, n_qp), NT, DqPairLayout<64>::BYTES, s,
-                    tQ128, tO128, tKk32, tKm64, tVk32, lse, D, io.dq, io.dq_ld, S, H, Hkv, n_qp, scale, scale * LOG2E,
-                    rope_cos, rope_sin, ctx->d_err);
-  } else if (dq_persist) {
+  if (dq_persist) {
     const long long items = static_cast<long long>(H) * B * n_qt;
     if (items >= (1LL << 31)) return ctx->fail(GLC_ERR_INVALID, "attention_bwd: too many work items");
     const int grid = static_cast<int>(items < ctx->num_sms ? items : ctx->num_sms);

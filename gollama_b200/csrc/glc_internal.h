@@ -48,9 +48,8 @@ struct Context {
   bool fuse_swiglu = false;            // trainer: SwiGLU forward in the gate/up GEMM epilogue (Llama semantics)
   int attn_split = 0;                  // dK/dV CTAs per KV head: 0 automatic, else a divisor of the group
   int rmsnorm_variant = 0;             // RMSNorm backward: 0 automatic (row per iteration), 1 same, 2 pipelined loads
-  int attn_dq_variant = 0;             // attention backward dQ: 0 automatic (= 2), 1 a CTA per query tile, 2 persistent, 3 CTA pairs
+  int attn_dq_variant = 0;             // attention backward dQ: 0 automatic (= 2), 1 a CTA per query tile, 2 persistent
   int attn_fwd_variant = 0;            // attention forward: 0 automatic (= 2), 1 a CTA per query tile, 2 persistent
-  int attn_dkdv_variant = 0;           // attention backward dK/dV: 0 automatic (= 1), 1 a CTA per key tile, 2 CTA pairs
   int quant_path = 0;                  // dX through a stored weight: 0 automatic (= 1), 1 dequantize + GEMM, 2 fused
   bool tracing = false;                // NVTX ranges around the phases of a training step
   bool pdl = true;                     // programmatic dependent launch between this library's kernels

@@ -310,17 +310,6 @@ __device__ __forceinline__ void umma_tf32_pair(uint32_t tmem_d, uint64_t adesc, 
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// Pair MMA with the A operand in tensor memory: each CTA's 128 rows of A at
-// its own TMEM lanes, column (tmem_a + k), as umma_tf32_ts does for one CTA.
-__device__ __forceinline__ void umma_tf32_pair_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
-                                                  uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 // Arrive on the barrier at `bar_cluster` (this CTA's or the peer's) once every
 // pair MMA issued so far by this thread completes.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {

@@ -208,15 +208,8 @@ GLC_API int glc_set_attention_fwd_variant(glc_ctx* ctx, int variant);
 /* The same choice for the attention backward's dQ kernel: 0 automatic and 2
  * walk its (query tile, batch, head) items persistently, moving the next
  * item's Q and dO into TMEM while the current item's dQ is written; 1 one CTA
- * per item; 3 a pair of CTAs (a cluster) per 256 queries issuing M = 256
- * tensor-core products (head_dim 64; other head sizes use 2).  Bit-identical. */
+ * per item.  Bit-identical. */
 GLC_API int glc_set_attention_dq_variant(glc_ctx* ctx, int variant);
-/* The attention backward's dK/dV kernel (tuning; no reference counterpart):
- * 0 automatic and 1 one CTA per (128 keys, KV head, share of its query
- * heads); 2 a pair of CTAs (a cluster) per 256 keys issuing M = 256 tensor-core
- * products, each CTA loading half of every query-side operand (head_dim 64;
- * other head sizes use 1).  Bit-identical. */
-GLC_API int glc_set_attention_dkdv_variant(glc_ctx* ctx, int variant);
 /* Trainer (Llama semantics): 1 computes the SwiGLU forward in the gate/up
  * GEMM's epilogue, 0 (default, faster on B200 at the TinyLlama shape) runs it
  * as its own kernel after the GEMM (diagnostics; no reference counterpart).

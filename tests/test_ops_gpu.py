@@ -265,75 +265,6 @@ def test_attention_dq_persistent_bit_identical(ctx, B, S, H, Hkv, hd):
         assert np.array_equal(a, b_)
 
 
-@pytest.mark.parametrize("B,S,H,Hkv,hd,split", [(1, 128, 2, 1, 64, 0), (2, 300, 4, 2, 64, 0), (4, 1024, 32, 4, 64, 0),
-                                                (4, 1024, 32, 4, 64, 1), (1, 2048, 8, 8, 64, 0), (3, 257, 6, 3, 64, 3),
-                                                (1, 100, 4, 2, 64, 0), (2, 640, 8, 2, 64, 2)])
-def test_attention_dkdv_pair_bit_identical(ctx, orc, B, S, H, Hkv, hd, split):
-    """glc_set_attention_dkdv_variant(2): dK/dV on CTA pairs over 256 keys
-    (ragged sequences, sequences shorter than a pair's keys, every split of
-    the query-head group) gives the bits of the one-CTA kernel; dQ unchanged."""
-    T = B * S
-    r = rng(T + 3 * H + split)
-    q = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
-    k = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
-    v = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
-    dO = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
-    bq, bk, bv, bdo = ctx.from_numpy(q), ctx.from_numpy(k), ctx.from_numpy(v), ctx.from_numpy(dO)
-    bo, blse = ctx.empty((T, H * hd)), ctx.empty((B, H, S))
-    ctx.call("glc_attention_fwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, B, S, H, Hkv, hd, 0)
-    outs = []
-    try:
-        ctx.call("glc_set_attention_split", split)
-        for variant in (1, 2):
-            ctx.call("glc_set_attention_dkdv_variant", variant)
-            for rnd in (0, 1):
-                bdq, bdk, bdv = ctx.empty(q.shape), ctx.empty(k.shape), ctx.empty(v.shape)
-                ctx.call("glc_attention_bwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, bdq.ptr, bdk.ptr,
-                         bdv.ptr, B, S, H, Hkv, hd, rnd)
-                ctx.sync()
-                outs.append([a.numpy() for a in (bdq, bdk, bdv)])
-    finally:
-        ctx.call("glc_set_attention_dkdv_variant", 0)
-        ctx.call("glc_set_attention_split", 0)
-    for a, b_ in zip(outs[:2], outs[2:]):
-        for x, y in zip(a, b_):
-            assert np.array_equal(x.view(np.uint32), y.view(np.uint32))
-    if T <= 4096:
-        ref = orc.attention_bwd(q, k, v, dO, S, H, Hkv, hd)
-        errs = [rel_fro(x, y) for x, y in zip(outs[2], ref)]
-        assert max(errs) < ATTN_TOL, errs
-
-
-@pytest.mark.parametrize("B,S,H,Hkv,hd", [(1, 128, 2, 1, 64), (2, 300, 4, 2, 64), (4, 1024, 32, 4, 64),
-                                          (1, 2048, 8, 8, 64), (3, 257, 6, 3, 64), (1, 100, 4, 2, 64)])
-def test_attention_dq_pair_bit_identical(ctx, B, S, H, Hkv, hd):
-    """glc_set_attention_dq_variant(3): dQ on CTA pairs over 256 queries
-    (ragged sequences, sequences shorter than a pair's queries) gives the
-    bits of the one-CTA kernel, with and without the RoPE epilogue."""
-    T = B * S
-    r = rng(T + 5 * H)
-    q = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
-    k = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
-    v = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
-    dO = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
-    bq, bk, bv, bdo = ctx.from_numpy(q), ctx.from_numpy(k), ctx.from_numpy(v), ctx.from_numpy(dO)
-    bo, blse = ctx.empty((T, H * hd)), ctx.empty((B, H, S))
-    ctx.call("glc_attention_fwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, B, S, H, Hkv, hd, 0)
-    outs = []
-    try:
-        for variant in (1, 3):
-            ctx.call("glc_set_attention_dq_variant", variant)
-            bdq, bdk, bdv = ctx.empty(q.shape), ctx.empty(k.shape), ctx.empty(v.shape)
-            ctx.call("glc_attention_bwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, bdq.ptr, bdk.ptr, bdv.ptr,
-                     B, S, H, Hkv, hd, 0)
-            ctx.sync()
-            outs.append([a.numpy().view(np.uint32) for a in (bdq, bdk, bdv)])
-    finally:
-        ctx.call("glc_set_attention_dq_variant", 0)
-    for a, b_ in zip(*outs):
-        assert np.array_equal(a, b_)
-
-
 @pytest.mark.parametrize("nsplit", [1, 2, 4, 3])
 def test_attention_bwd_group_splits(ctx, orc, nsplit):
     """dK/dV with the 4 query heads of each KV head over 1, 2 or 4 CTAs (3 is
