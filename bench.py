@@ -575,7 +575,7 @@ def main():
     args = parse_args()
     # rank 0's stdout must be exactly one JSON line: NCCL's log (its version
     # banner included, printed at level WARN) goes to stderr
-    os.environ["NCCL_DEBUG"] = "WARN"
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
     os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
     if args.impl == "reference":
         return run_reference(args)

@@ -83,13 +83,24 @@ __global__ void __launch_bounds__(512) ce_kernel(float* __restrict__ logits, con
       }
     }
     s = block_reduce<false>(s, red);
+    const float inv = FAST ? 1.0f / s : 0.f;
     const int64_t t = targets[row];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int c = threadIdx.x + i * blockDim.x;
       if (c < nc) {
-        float p[4] = {__fdiv_rn(v[i].x, s), __fdiv_rn(v[i].y, s), __fdiv_rn(v[i].z, s), __fdiv_rn(v[i].w, s)};
-        if (t >= 4 * c && t < 4 * c + 4) {
+        // p_v = e_v / sum: the reference's division, bit for bit, where its
+        // bits are matched (exp32 path); the Llama path (no reference bits)
+        // multiplies by the row's reciprocal.  Without the gradient only the
+        // target's p is needed.
+        const bool has_t = t >= 4 * c && t < 4 * c + 4;
+        float p[4] = {0.f, 0.f, 0.f, 0.f};
+        if (FAST) {
+          p[0] = v[i].x * inv; p[1] = v[i].y * inv; p[2] = v[i].z * inv; p[3] = v[i].w * inv;
+        } else if (write_grad || has_t) {
+          p[0] = __fdiv_rn(v[i].x, s); p[1] = __fdiv_rn(v[i].y, s); p[2] = __fdiv_rn(v[i].z, s); p[3] = __fdiv_rn(v[i].w, s);
+        }
+        if (has_t) {
           const int j = static_cast<int>(t - 4 * c);
           const float pt = j == 0 ? p[0] : j == 1 ? p[1] : j == 2 ? p[2] : p[3];
           row_logp[row] = FAST ? logf(__fadd_rn(pt, 1e-10f)) : go_log32(__fadd_rn(pt, 1e-10f));
@@ -169,13 +180,20 @@ __global__ void __cluster_dims__(CE_CL, 1, 1) __launch_bounds__(CE_CL_THREADS, V
     }
   }
   s = cluster_reduce<false>(s, red, &slots[1]);
+  const float inv = FAST ? 1.0f / s : 0.f;
   const int64_t t = targets[row];
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int c = c0 + threadIdx.x + i * CE_CL_THREADS;
     if (c < c1) {
-      float p[4] = {__fdiv_rn(v[i].x, s), __fdiv_rn(v[i].y, s), __fdiv_rn(v[i].z, s), __fdiv_rn(v[i].w, s)};
-      if (t >= 4 * c && t < 4 * c + 4) {
+      const bool has_t = t >= 4 * c && t < 4 * c + 4;
+      float p[4] = {0.f, 0.f, 0.f, 0.f};
+      if (FAST) {
+        p[0] = v[i].x * inv; p[1] = v[i].y * inv; p[2] = v[i].z * inv; p[3] = v[i].w * inv;
+      } else if (write_grad || has_t) {
+        p[0] = __fdiv_rn(v[i].x, s); p[1] = __fdiv_rn(v[i].y, s); p[2] = __fdiv_rn(v[i].z, s); p[3] = __fdiv_rn(v[i].w, s);
+      }
+      if (has_t) {
         const int j = static_cast<int>(t - 4 * c);
         const float pt = j == 0 ? p[0] : j == 1 ? p[1] : j == 2 ? p[2] : p[3];
         row_logp[row] = FAST ? logf(__fadd_rn(pt, 1e-10f)) : go_log32(__fadd_rn(pt, 1e-10f));

@@ -72,6 +72,8 @@ int glc_init(int device, glc_ctx** out) {
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess || cudaMemset(c->d_err, 0, sizeof(int)) != cudaSuccess ||
+      cudaMalloc(&c->dyn_ctr, sizeof(int) * Context::kDynCounters) != cudaSuccess ||
+      cudaMemset(c->dyn_ctr, 0, sizeof(int) * Context::kDynCounters) != cudaSuccess ||
       cudaEventCreate(&c->timer_start) != cudaSuccess || cudaEventCreate(&c->timer_stop) != cudaSuccess) {
     delete c;
     return GLC_ERR_CUDA;
@@ -100,6 +102,7 @@ int glc_destroy(glc_ctx* ctx) {
   cudaStreamSynchronize(c->comm_stream);
   if (c->ws) cudaFree(c->ws);
   if (c->d_err) cudaFree(c->d_err);
+  if (c->dyn_ctr) cudaFree(c->dyn_ctr);
   if (c->timer_start) cudaEventDestroy(c->timer_start);
   if (c->timer_stop) cudaEventDestroy(c->timer_stop);
   for (auto& r : c->prof) {
@@ -301,6 +304,14 @@ int glc_set_attention_fwd_variant(glc_ctx* ctx, int variant) {
   return GLC_OK;
 }
 
+int glc_set_gemm_schedule(glc_ctx* ctx, int mode) {
+  if (!ctx) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  if (mode < 0 || mode > 2) return c->fail(GLC_ERR_INVALID, "set_gemm_schedule: mode must be 0, 1 or 2");
+  c->gemm_order = mode;
+  return GLC_OK;
+}
+
 int glc_set_attention_dq_variant(glc_ctx* ctx, int variant) {
   if (!ctx) return GLC_ERR_INVALID;
   Context* c = C_(ctx);
@@ -332,7 +343,7 @@ int glc_set_quant_path(glc_ctx* ctx, int path) {
 int glc_set_rmsnorm_variant(glc_ctx* ctx, int variant) {
   if (!ctx) return GLC_ERR_INVALID;
   Context* c = C_(ctx);
-  if (variant < 0 || variant > 2) return c->fail(GLC_ERR_INVALID, "set_rmsnorm_variant: variant must be 0, 1 or 2");
+  if (variant < 0 || variant > 3) return c->fail(GLC_ERR_INVALID, "set_rmsnorm_variant: variant must be 0 to 3");
   c->rmsnorm_variant = variant;
   return GLC_OK;
 }

@@ -142,6 +142,10 @@ int glc_dp_init(glc_ctx* ctx, int rank, int world, const unsigned char id[128], 
   std::memcpy(&u, id, sizeof(u));
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
+  // tuning: how many CTAs NCCL's kernels may take (SMs the gradient sums
+  // hold while the backward's GEMMs run beside them); NCCL's default if unset
+  if (const char* v = std::getenv("GLC_NCCL_MAX_CTAS")) cfg.maxCTAs = std::atoi(v);
+  if (const char* v = std::getenv("GLC_NCCL_MIN_CTAS")) cfg.minCTAs = std::atoi(v);
   ncclResult_t r = glc::nccl().CommInitRankConfig(&cm->comm, world, u, rank, &cfg);
   int rc = glc::nccl_wait(c, r, "ncclCommInitRankConfig");
   if (rc) {

@@ -37,6 +37,7 @@
 // squares of the values it stores into float64 slots (a gradient's share of
 // the clip norm, Problem::sumsq).
 #include <algorithm>
+#include <atomic>
 #include <functional>
 #include <queue>
 #include <utility>
@@ -112,6 +113,11 @@ struct GroupArgs {
   // cluster + clusters, ...; otherwise sched[c] .. sched[c + 1] index into
   // the tile list sched[clusters + 1 ..] the clusters of cluster c.
   const int* sched;
+  // Dynamic order (CTA-pair kernel, when not null): a zeroed counter in
+  // device memory; each pair takes the next tile index when it is ready for
+  // one, so pairs that start late (their SMs busy with another kernel, such
+  // as a collective on the communication stream) simply take fewer tiles.
+  int* dyn;
 };
 
 // The range of list positions of cluster c and the tile at position it.
@@ -409,7 +415,9 @@ constexpr int P_STAGES = 6;
 constexpr int P_A_BYTES = HALF_ROWS * BK * 4;        // 16 KB
 constexpr int P_B_BYTES = HALF_ROWS * BK * 4;        // 16 KB
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES; // 32 KB per CTA, 64 KB per pair
-constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr int P_TILE_RING = 8;                       // dynamic order: tile indices published ahead
+constexpr int P_RING_CONSUMERS = 2 + 2 * P_EPI_WARPS; // peer producer, MMA issuer, epilogue warps of both CTAs
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 512;
 
 __device__ __forceinline__ void load_operand_pair(bool mn, bool mn3d, void* sdst, const CUtensorMap* tm,
                                                   uint32_t bar_cluster, int mn0, int k0) {
@@ -446,14 +454,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
   uint64_t* tfull_bar = empty_bar + P_STAGES;  // [2]
   uint64_t* tempty_bar = tfull_bar + 2;        // [2]
   uint64_t* drain_bar = tempty_bar + 2;        // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* ring_full = drain_bar + 1;         // [P_TILE_RING] each CTA: tile index published
+  uint64_t* ring_empty = ring_full + P_TILE_RING;  // [P_TILE_RING] leader: every consumer read it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring_empty + P_TILE_RING);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* ring = reinterpret_cast<int*>(tmem_slot + 2);  // [P_TILE_RING]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int cluster = static_cast<int>(blockIdx.x >> 1);
   const int nclusters = static_cast<int>(gridDim.x >> 1);
+  // Dynamic order: the leader's producer takes tile indices from the counter
+  // and publishes each in slot i % P_TILE_RING of both CTAs' rings; every
+  // other role of the pair reads the slots in order and releases them on the
+  // leader's ring_empty.  A -1 ends the sequence; -2 means a wait gave up.
+  auto consume = [&](int i, bool warp_wide) -> int {
+    const int slot = i % P_TILE_RING;
+    const uint32_t ph = static_cast<uint32_t>(i / P_TILE_RING) & 1u;
+    const bool got = mbar_wait_cluster(&ring_full[slot], ph, abort_flag, args.err, GLC_DEV_TIMEOUT_MMA_FULL);
+    if (warp_wide ? !__all_sync(0xffffffffu, got) : !got) return -2;
+    const int t = ring[slot];
+    if (warp_wide) __syncwarp();
+    if (!warp_wide || lane == 0) mbar_arrive_cluster(mapa_cluster(&ring_empty[slot], 0));
+    return t;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < P_STAGES; ++s) {
@@ -465,6 +490,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
       mbar_init(&tempty_bar[b], 2 * P_EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
+    for (int i = 0; i < P_TILE_RING; ++i) {
+      mbar_init(&ring_full[i], 1);
+      mbar_init(&ring_empty[i], P_RING_CONSUMERS);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA0);
@@ -490,8 +519,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
       bool ok = true;
       int it0, it1, istep;
       sched_range(args, cluster, nclusters, it0, it1, istep);
-      for (int it = it0; it < it1 && ok; it += istep) {
-        const TileRef t = locate<PAIR_BM>(args, sched_tile(args, nclusters, it));
+      for (int it = it0, i = 0; ok; it += istep, ++i) {
+        int tile;
+        if (!args.dyn) {
+          if (it >= it1) break;
+          tile = sched_tile(args, nclusters, it);
+        } else if (rank == 0) {
+          // the pair's scheduler: take the next index, publish it to both CTAs
+          const int slot = i % P_TILE_RING;
+          if (!mbar_wait(&ring_empty[slot], (static_cast<uint32_t>(i / P_TILE_RING) & 1u) ^ 1u, abort_flag, args.err,
+                         GLC_DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          tile = atomicAdd(args.dyn, 1);
+          if (tile >= args.total_tiles) tile = -1;
+          ring[slot] = tile;
+          st_shared_cluster_u32(mapa_cluster(&ring[slot], 1), tile);
+          mbar_arrive(&ring_full[slot]);
+          mbar_arrive_cluster(mapa_cluster(&ring_full[slot], 1));
+        } else {
+          tile = consume(i, false);
+          if (tile == -2) {
+            ok = false;
+            break;
+          }
+        }
+        if (tile < 0) break;
+        const TileRef t = locate<PAIR_BM>(args, tile);
         const Problem& p = args.p[t.prob];
         const CUtensorMap* tmA = t.prob ? &tmA1 : &tmA0;
         const CUtensorMap* tmB = t.prob ? &tmB1 : &tmB0;
@@ -529,8 +584,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
       bool issued_any = false;
       int it0, it1, istep;
       sched_range(args, cluster, nclusters, it0, it1, istep);
-      for (int it = it0; it < it1 && ok; it += istep, ++local) {
-        const TileRef t = locate<PAIR_BM>(args, sched_tile(args, nclusters, it));
+      for (int it = it0; ok; it += istep, ++local) {
+        int tile;
+        if (!args.dyn) {
+          if (it >= it1) break;
+          tile = sched_tile(args, nclusters, it);
+        } else {
+          tile = consume(local, false);
+          if (tile == -2) {
+            ok = false;
+            break;
+          }
+        }
+        if (tile < 0) break;
+        const TileRef t = locate<PAIR_BM>(args, tile);
         const Problem& p = args.p[t.prob];
         const uint32_t idesc = umma_idesc_tf32(PAIR_BM, BN, p.a_mn != 0, p.b_mn != 0);
         const int buf = local & 1;
@@ -594,8 +661,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
     int local = 0;
     int it0, it1, istep;
     sched_range(args, cluster, nclusters, it0, it1, istep);
-    for (int it = it0; it < it1; it += istep, ++local) {
-      const TileRef t = locate<PAIR_BM>(args, sched_tile(args, nclusters, it));
+    for (int it = it0;; it += istep, ++local) {
+      int tile;
+      if (!args.dyn) {
+        if (it >= it1) break;
+        tile = sched_tile(args, nclusters, it);
+      } else {
+        tile = consume(local, true);
+      }
+      if (tile < 0) break;
+      const TileRef t = locate<PAIR_BM>(args, tile);
       const Problem& p = args.p[t.prob];
       const bool vec_ok = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
                           (p.R == nullptr || (((p.ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.R) & 15) == 0)));
@@ -955,15 +1030,19 @@ int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t str
   a.nprob = nl;
   a.total_tiles = a.p[0].tiles + (nl > 1 ? a.p[1].tiles : 0);
   a.err = ctx->d_err;
-  static bool attr_set[2][8] = {{false}};
-  const int dev = ctx->device & 7;
-  if (!attr_set[pair][dev]) {
+  // the shared-memory limit is a per-device attribute of each kernel: set
+  // once per device (atomic flags; a repeated setting from a racing host
+  // thread is harmless)
+  constexpr int kMaxDevices = 64;
+  static std::atomic<bool> attr_set[2][kMaxDevices];
+  if (ctx->device < 0 || ctx->device >= kMaxDevices) return ctx->fail(GLC_ERR_UNSUPPORTED, "gemm: device index too large");
+  if (!attr_set[pair][ctx->device].load(std::memory_order_acquire)) {
     cudaError_t e = pair ? cudaFuncSetAttribute(gemm_tf32_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 P_SMEM_BYTES)
                          : cudaFuncSetAttribute(gemm_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 SMEM_BYTES);
     if (e != cudaSuccess) return ctx->fail_cuda(e, "cudaFuncSetAttribute(gemm_tf32)");
-    attr_set[pair][dev] = true;
+    attr_set[pair][ctx->device].store(true, std::memory_order_release);
   }
   double flops = 0;
   for (int i = 0; i < nl; ++i) flops += 2.0 * a.p[i].M * a.p[i].N * static_cast<double>(a.p[i].K);
@@ -972,7 +1051,18 @@ int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t str
     // one cluster per SM pair; clusters loop over the tiles
     const int pairs = ctx->num_sms / 2;
     const int clusters = a.total_tiles < pairs ? a.total_tiles : pairs;
-    if (nl == 2) a.sched = pair_schedule(ctx, a, clusters);
+    if (ctx->gemm_order == 2) {
+      // dynamic order: a fresh zero counter per launch from the context's
+      // ring of counters, cleared on the stream whenever the ring wraps
+      const unsigned idx = static_cast<unsigned>(ctx->dyn_next++ % Context::kDynCounters);
+      if (idx == 0 && ctx->dyn_next > 1) {
+        cudaError_t e = cudaMemsetAsync(ctx->dyn_ctr, 0, sizeof(int) * Context::kDynCounters, stream);
+        if (e != cudaSuccess) return ctx->fail_cuda(e, "gemm: clearing the tile counters");
+      }
+      a.dyn = ctx->dyn_ctr + idx;
+    } else if (nl == 2) {
+      a.sched = pair_schedule(ctx, a, clusters);
+    }
     glc::launch_pdl(ctx, gemm_tf32_pair_kernel, 2 * clusters, P_NUM_THREADS, P_SMEM_BYTES, stream, tm[0], tm[1], tm[2], tm[3], a);
   } else {
     const int grid = a.total_tiles < ctx->num_sms ? a.total_tiles : ctx->num_sms;

@@ -42,12 +42,18 @@ struct Context {
   std::string last_error;
   uint64_t launches = 0;               // kernels this library launched
   int gemm_variant = 0;                // 0 automatic, 1 single-CTA tiles, 2 CTA-pair tiles
+  int gemm_order = 0;                  // CTA-pair tile order: 0 automatic (= 1), 1 host lists / rotation, 2 dynamic
+  // dynamic tile order: one zeroed counter per launch, from a ring cleared
+  // on the stream when it wraps
+  static constexpr int kDynCounters = 1024;
+  int* dyn_ctr = nullptr;
+  unsigned long long dyn_next = 0;
   // device tile lists of grouped CTA-pair GEMM launches, by (tiles and
   // k-blocks of each problem, clusters); built once per shape
   std::vector<std::pair<std::array<long long, 5>, int*>> gemm_sched;
   bool fuse_swiglu = false;            // trainer: SwiGLU forward in the gate/up GEMM epilogue (Llama semantics)
   int attn_split = 0;                  // dK/dV CTAs per KV head: 0 automatic, else a divisor of the group
-  int rmsnorm_variant = 0;             // RMSNorm backward: 0 automatic (row per iteration), 1 same, 2 pipelined loads
+  int rmsnorm_variant = 0;             // RMSNorm backward: 0 automatic (3 for the exact gradient, else 1), 1 row per iteration, 2 cp.async rows, 3 bulk-copied rows
   int attn_dq_variant = 0;             // attention backward dQ: 0 automatic (= 2), 1 a CTA per query tile, 2 persistent
   int attn_fwd_variant = 0;            // attention forward: 0 automatic (= 2), 1 a CTA per query tile, 2 persistent
   int quant_path = 0;                  // dX through a stored weight: 0 automatic (= 1), 1 dequantize + GEMM, 2 fused

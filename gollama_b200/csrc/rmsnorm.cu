@@ -286,6 +286,139 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_pipe_kernel(
   }
 }
 
+// The exact (Llama) backward with whole rows staged by bulk copies: one
+// thread streams the rows of x, dy (and the accumulated dx) of a block's
+// chunk into a ring of TMA_STAGES shared-memory stages (cp.async.bulk, one
+// mbarrier per stage), so several rows per block are in flight while the
+// current one is reduced; two 96 KB blocks fit an SM, eight rows in flight.
+// The row's 1/rms is applied as a product (the reference-semantics kernel
+// above divides, bit for bit with the reference; the exact gradient has no
+// reference bits to match), dw partials per block as above.
+constexpr int TMA_STAGES = 4;
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+template <int MAXC>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_full_tma_kernel(
+    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ rms,
+    const float* __restrict__ dy, float* __restrict__ dx, float* __restrict__ dx_round,
+    float* __restrict__ dw_partial, int rows, int cols, int rows_per_block, int dx_accumulate, int* err) {
+  GLC_PDL_ENTRY();
+  extern __shared__ __align__(16) float stage_rows[];  // [TMA_STAGES][3][cols], then the barriers
+  __shared__ float red[32];
+  __shared__ int abort_flag;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_rows + static_cast<size_t>(TMA_STAGES) * 3 * cols);
+  const int nc = cols >> 2;
+  const int tid = threadIdx.x;
+  const int row0 = blockIdx.x * rows_per_block;
+  const int row1 = min(rows, row0 + rows_per_block);
+  const uint32_t row_bytes = static_cast<uint32_t>(cols) * 4u;
+  const uint32_t stage_bytes = (dx_accumulate ? 3u : 2u) * row_bytes;
+  auto stage = [&](int st, int arr) { return stage_rows + (static_cast<size_t>(st) * 3 + arr) * cols; };
+  auto issue = [&](int row, int st) {  // thread 0 only
+    const size_t base = static_cast<size_t>(row) * cols;
+    mbar_arrive_expect_tx(&full[st], stage_bytes);
+    bulk_load(stage(st, 0), x + base, row_bytes, &full[st]);
+    bulk_load(stage(st, 1), dy + base, row_bytes, &full[st]);
+    if (dx_accumulate) bulk_load(stage(st, 2), dx + base, row_bytes, &full[st]);
+  };
+  if (tid == 0) {
+    for (int i = 0; i < TMA_STAGES; ++i) mbar_init(&full[i], 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int issued = 0;  // rows whose copies thread 0 has issued
+  if (tid == 0)
+    for (; issued < TMA_STAGES && row0 + issued < row1; ++issued) issue(row0 + issued, issued);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4 wv[MAXC], acc[MAXC];
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * 256;
+    wv[i] = c < nc ? w4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const float inv_cols = 1.0f / static_cast<float>(cols);
+  bool ok = true;
+  for (int row = row0; row < row1; ++row) {
+    const int k = row - row0, st = k % TMA_STAGES;
+    if (!__syncthreads_and(mbar_wait(&full[st], (k / TMA_STAGES) & 1, &abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
+      ok = false;
+      break;
+    }
+    const float rinv = 1.0f / rms[row];
+    const float4* xs = reinterpret_cast<const float4*>(stage(st, 0));
+    const float4* ds = reinterpret_cast<const float4*>(stage(st, 1));
+    const float4* os = reinterpret_cast<const float4*>(stage(st, 2));
+    float4 xv[MAXC], dv[MAXC], ov[MAXC];
+    float sdot = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * 256;
+      if (c < nc) {
+        xv[i] = xs[c];
+        dv[i] = ds[c];
+        if (dx_accumulate) ov[i] = os[c];
+        sdot += dv[i].x * wv[i].x * xv[i].x + dv[i].y * wv[i].y * xv[i].y + dv[i].z * wv[i].z * xv[i].z +
+                dv[i].w * wv[i].w * xv[i].w;
+      }
+    }
+    sdot = warp_sum(sdot);
+    if ((tid & 31) == 0) red[tid >> 5] = sdot;
+    __syncthreads();  // also: every thread holds this row's values, the stage may be refilled
+    if (tid == 0 && issued < row1 - row0) {
+      issue(row0 + issued, issued % TMA_STAGES);
+      ++issued;
+    }
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    const float coef = tot * inv_cols * rinv * rinv * rinv;
+    float4* dxr = reinterpret_cast<float4*>(dx + static_cast<size_t>(row) * cols);
+    float4* dxq = dx_round ? reinterpret_cast<float4*>(dx_round + static_cast<size_t>(row) * cols) : nullptr;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * 256;
+      if (c < nc) {
+        float4 g;
+        g.x = dv[i].x * wv[i].x * rinv - xv[i].x * coef;
+        g.y = dv[i].y * wv[i].y * rinv - xv[i].y * coef;
+        g.z = dv[i].z * wv[i].z * rinv - xv[i].z * coef;
+        g.w = dv[i].w * wv[i].w * rinv - xv[i].w * coef;
+        if (dx_accumulate) {
+          g.x += ov[i].x; g.y += ov[i].y; g.z += ov[i].z; g.w += ov[i].w;
+        }
+        dxr[c] = g;
+        if (dxq) dxq[c] = make_float4(round_tf32(g.x), round_tf32(g.y), round_tf32(g.z), round_tf32(g.w));
+        acc[i].x += dv[i].x * xv[i].x * rinv;
+        acc[i].y += dv[i].y * xv[i].y * rinv;
+        acc[i].z += dv[i].z * xv[i].z * rinv;
+        acc[i].w += dv[i].w * xv[i].w * rinv;
+      }
+    }
+    __syncthreads();  // red is rewritten by the next row
+  }
+  if (!ok && tid == 0) {
+    // no copy may land after the block exits: wait (bounded) for those in flight
+    for (int row = row0; row < row0 + issued; ++row) {
+      const int k = row - row0;
+      mbar_drain(&full[k % TMA_STAGES], (k / TMA_STAGES) & 1, err);
+    }
+  }
+  float4* part = reinterpret_cast<float4*>(dw_partial + static_cast<size_t>(blockIdx.x) * cols);
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = tid + i * 256;
+    if (c < nc) part[c] = acc[i];
+  }
+}
+
 // dw[j] (+)= sum over blocks b of partial[b][j].  A cluster of CS_CL CTAs
 // per 32 columns: CTA rank r adds the partial rows of its quarter
 // [r*q, (r+1)*q), each of its 16 warps keeping four running sums (rows
@@ -375,7 +508,10 @@ int rmsnorm_bwd(Context* ctx, const float* x, const float* w, const float* rms, 
   // the rows over the same blocks, so the per-block dw partials (and their
   // sum) are the same bits; the pipelined kernel fits three blocks per SM.
   const bool pipe = ctx->rmsnorm_variant == 2 && nc <= 512;
-  int nblocks = 4 * ctx->num_sms;
+  // the exact gradient streams whole rows through bulk copies (automatic, or
+  // variant 3): rows of up to 2048 columns, two blocks per SM
+  const bool tma = full && nc <= 512 && (ctx->rmsnorm_variant == 0 || ctx->rmsnorm_variant == 3);
+  int nblocks = (tma ? 2 : 4) * ctx->num_sms;
   if (nblocks > rows) nblocks = rows;
   const int rpb = (rows + nblocks - 1) / nblocks;
   nblocks = (rows + rpb - 1) / rpb;
@@ -393,7 +529,15 @@ int rmsnorm_bwd(Context* ctx, const float* x, const float* w, const float* rms, 
   ProfScope prof(ctx, PROF_RMSNORM,
                  4.0 * static_cast<double>(rows) * cols * (3 + (dx_accumulate ? 1 : 0) + (dx_round ? 1 : 0)) + 4.0 * rows,
                  s);
-  if (pipe) {
+  if (tma) {
+    const int maxc = nc <= 256 ? 1 : 2;
+    const size_t smem = sizeof(float) * TMA_STAGES * 3 * static_cast<size_t>(cols) + 8 * TMA_STAGES;
+    auto kern = maxc == 1 ? rmsnorm_bwd_full_tma_kernel<1> : rmsnorm_bwd_full_tma_kernel<2>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return ctx->fail_cuda(e, "rmsnorm_bwd: shared memory attribute");
+    glc::launch_pdl(ctx, kern, nblocks, 256, smem, s, x, w, rms, dy, dx, dx_round, partial, rows, cols, rpb, acc,
+                    ctx->d_err);
+  } else if (pipe) {
     const int maxc = nc <= 256 ? 1 : 2;
     const size_t smem = sizeof(float4) * PIPE_STAGES * 3 * maxc * 256;
     auto kern = maxc == 1 ? rmsnorm_bwd_pipe_kernel<1> : rmsnorm_bwd_pipe_kernel<2>;

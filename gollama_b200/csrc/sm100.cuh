@@ -84,6 +84,36 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// mbar_wait with cluster-scope acquire: for a phase completed by arrivals of
+// the peer CTA (release.cluster) whose shared-memory writes this thread reads.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  int* gerr, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 31u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > GLC_WAIT_TIMEOUT_NS) {
+        *abort_flag = 1;
+        if (gerr) atomicCAS(gerr, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
 // Abort path only: waits at most 1 s for the phase `parity` of `bar` (copies a
 // producer issued before aborting) so the CTA never exits with them in flight.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, int* gerr) {
@@ -268,6 +298,10 @@ __device__ __forceinline__ uint32_t mapa_cluster(const void* p, uint32_t rank) {
 // included) are visible to the other CTA afterwards.
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 32-bit store to shared::cluster (a peer CTA's shared memory, via mapa)
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t addr, int v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 // 32-bit load from shared::cluster (a peer CTA's shared memory, via mapa)
 __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {

@@ -248,14 +248,16 @@ def main(argv=None):
                     help="GEMM tiles: 0 automatic, 1 single-CTA 128x256, 2 CTA-pair 256x256")
     ap.add_argument("--attn-split", type=int, default=0,
                     help="attention backward: dK/dV CTAs per KV head (0 automatic, else a divisor of H/Hkv)")
-    ap.add_argument("--rmsnorm-variant", type=int, default=0, choices=[0, 1, 2],
-                    help="RMSNorm backward: 0 automatic, 1 row by row, 2 cp.async-pipelined rows")
+    ap.add_argument("--rmsnorm-variant", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="RMSNorm backward: 0 automatic, 1 row by row, 2 cp.async-pipelined rows, 3 bulk-copied rows")
     ap.add_argument("--attn-fwd-variant", type=int, default=0, choices=[0, 1, 2],
                     help="attention forward: 0 automatic, 1 a CTA per query tile, 2 persistent CTAs")
     ap.add_argument("--attn-dq-variant", type=int, default=0, choices=[0, 1, 2],
                     help="attention backward dQ: 0 automatic, 1 a CTA per query tile, 2 persistent CTAs")
     ap.add_argument("--pdl", type=int, default=0, choices=[0, 1],
                     help="programmatic dependent launch between the library's kernels")
+    ap.add_argument("--gemm-schedule", type=int, default=0, choices=[0, 1, 2],
+                    help="CTA-pair GEMM tile order: 0 automatic, 1 fixed, 2 dynamic (a tile counter)")
     ap.add_argument("--quant-path", type=int, default=0, choices=[0, 1, 2],
                     help="quantized dX: 0 automatic, 1 dequantize + GEMM, 2 decode inside the GEMM")
     a = ap.parse_args(argv)
@@ -265,6 +267,7 @@ def main(argv=None):
         ctx.call("glc_set_attention_split", a.attn_split)
         ctx.call("glc_set_rmsnorm_variant", a.rmsnorm_variant)
         ctx.call("glc_set_quant_path", a.quant_path)
+        ctx.call("glc_set_gemm_schedule", a.gemm_schedule)
         ctx.call("glc_set_pdl", a.pdl)
         ctx.call("glc_set_attention_fwd_variant", a.attn_fwd_variant)
         ctx.call("glc_set_attention_dq_variant", a.attn_dq_variant)

@@ -177,10 +177,13 @@ GLC_API int glc_set_gemm_variant(glc_ctx* ctx, int variant);
  * Each CTA accumulates its heads in TMEM; more than one writes partials that a
  * deterministic group sum adds.  Results agree to fp32 rounding across splits. */
 GLC_API int glc_set_attention_split(glc_ctx* ctx, int nsplit);
-/* RMSNorm backward kernel (tuning; no reference counterpart): 0 automatic and
- * 1 process a block's rows one after another; 2 stages the next rows' x, dy
- * and dx in shared memory with cp.async while the current row is reduced
- * (rows of up to 2048 columns; wider rows use 1).  Results are bit-identical. */
+/* RMSNorm backward kernel (tuning; no reference counterpart): 1 process a
+ * block's rows one after another; 2 stage the next rows' x, dy and dx in
+ * shared memory with cp.async while the current row is reduced (bit-identical
+ * to 1); 3 (the exact gradient only) stream whole rows through a ring of four
+ * bulk-copy stages and apply 1/rms as a product (within fp32 rounding of 1);
+ * 0 automatic: 3 for the exact gradient, 1 for the reference's simplified one.
+ * Variants 2 and 3 take rows of up to 2048 columns; wider rows use 1. */
 GLC_API int glc_set_rmsnorm_variant(glc_ctx* ctx, int variant);
 /* glc_linear_bwd_dx_q's path (tuning; no reference counterpart): 0 automatic
  * and 1 dequantize W into the workspace, then the CTA-pair GEMM; 2 decode the
@@ -210,6 +213,13 @@ GLC_API int glc_set_attention_fwd_variant(glc_ctx* ctx, int variant);
  * item's Q and dO into TMEM while the current item's dQ is written; 1 one CTA
  * per item.  Bit-identical. */
 GLC_API int glc_set_attention_dq_variant(glc_ctx* ctx, int variant);
+/* Tile order of the CTA-pair GEMM (tuning; no reference counterpart): 0
+ * automatic and 1 a fixed order per pair (a rotation, or host-built lists
+ * for a grouped dX + dW launch); 2 dynamic: every pair takes the next tile
+ * from a counter when it is ready, so pairs that start late (their SMs held
+ * by another kernel, e.g. the gradient allreduce) take fewer tiles.  Each
+ * tile is computed the same way in every order: results are bit-identical. */
+GLC_API int glc_set_gemm_schedule(glc_ctx* ctx, int mode);
 /* Trainer (Llama semantics): 1 computes the SwiGLU forward in the gate/up
  * GEMM's epilogue, 0 (default, faster on B200 at the TinyLlama shape) runs it
  * as its own kernel after the GEMM (diagnostics; no reference counterpart).

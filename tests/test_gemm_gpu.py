@@ -194,3 +194,38 @@ def test_linear_fwd_swiglu_matches_separate_ops(ctx, variant, M, K, F):
     ctx.call("glc_swiglu_fwd", g.ptr, u.ptr, h2.ptr, M * F, 1)
     ctx.sync()
     assert np.array_equal(h.numpy().view(np.uint32), h2.numpy().view(np.uint32))
+
+
+@pytest.mark.parametrize("M,K,N", [(384, 256, 640), (1024, 512, 1376), (4096, 2048, 2560), (4096, 5632, 2048),
+                                   (300, 72, 100)])
+def test_gemm_dynamic_order_bit_identical(ctx, M, K, N):
+    """glc_set_gemm_schedule(2): CTA pairs take tiles from a counter; the
+    forward, the grouped dX + dW launch and a SwiGLU-epilogue launch give
+    the same bits as the fixed order, over more launches than one pass of
+    the counter ring would need to be cleared."""
+    rng = np.random.default_rng(M + 3 * K + N)
+    X = rng.standard_normal((M, K), dtype=np.float32)
+    W = rng.standard_normal((N, K), dtype=np.float32)
+    G = rng.standard_normal((M, N), dtype=np.float32)
+    D0 = rng.standard_normal((M, K), dtype=np.float32)
+    dX, dW, dG = ctx.from_numpy(X), ctx.from_numpy(W), ctx.from_numpy(G)
+    outs = []
+    try:
+        ctx.call("glc_set_gemm_variant", 2)
+        for mode in (1, 2):
+            ctx.call("glc_set_gemm_schedule", mode)
+            Y, gX, gW = ctx.empty((M, N)), ctx.from_numpy(D0), ctx.empty((N, K))
+            ctx.call("glc_linear_fwd", dX.ptr, dW.ptr, Y.ptr, M, K, N, None)
+            ctx.call("glc_linear_bwd", dG.ptr, dX.ptr, dW.ptr, gX.ptr, gW.ptr, M, K, N, 1, 0)
+            if mode == 2:
+                for _ in range(3):  # wrap the ring of tile counters (1024 launches) once
+                    for _ in range(400):
+                        ctx.call("glc_linear_fwd", dX.ptr, dW.ptr, Y.ptr, M, K, N, None)
+                    ctx.sync()
+            ctx.sync()
+            outs.append([a.numpy().view(np.uint32) for a in (Y, gX, gW)])
+    finally:
+        ctx.call("glc_set_gemm_schedule", 0)
+        ctx.call("glc_set_gemm_variant", 0)
+    for a, b in zip(*outs):
+        assert np.array_equal(a, b)

@@ -55,6 +55,35 @@ def test_rmsnorm_bwd(ctx, orc, rows, cols, full):
     assert np.max(np.abs(bdxr.numpy() - out_dx) / (np.abs(out_dx) + 1e-30)) <= 2.0**-11
 
 
+@pytest.mark.parametrize("variant", [1, 3])
+@pytest.mark.parametrize("acc", [0, 1])
+@pytest.mark.parametrize("rows,cols", [(5, 128), (300, 512), (3, 1028), (4096, 2048), (1000, 2052), (9, 2048)])
+def test_rmsnorm_bwd_exact_variants(ctx, orc, rows, cols, acc, variant):
+    """The exact backward through the row-by-row kernel (1) and the
+    bulk-copy pipeline (3, the default for the exact gradient; more rows per
+    block than its four stages, partial last blocks, rows wider than it
+    takes fall back) against the oracle."""
+    r = rng(rows * 7 + cols + acc)
+    x = r.standard_normal((rows, cols), dtype=np.float32)
+    w = (1 + 0.1 * r.standard_normal(cols)).astype(np.float32)
+    g = r.standard_normal((rows, cols), dtype=np.float32)
+    dx0 = r.standard_normal((rows, cols), dtype=np.float32) if acc else np.zeros((rows, cols), np.float32)
+    _, rms = orc.rmsnorm_fwd(x, w, 1e-5)
+    ref_dx, ref_dw = orc.rmsnorm_bwd(x, w, rms, g, 1, dx=dx0.copy())
+    try:
+        ctx.call("glc_set_rmsnorm_variant", variant)
+        bx, bw, brms, bg = ctx.from_numpy(x), ctx.from_numpy(w), ctx.from_numpy(rms), ctx.from_numpy(g)
+        bdx, bdw, bdxr = ctx.from_numpy(dx0), ctx.zeros((cols,)), ctx.empty((rows, cols))
+        ctx.call("glc_rmsnorm_bwd", bx.ptr, bw.ptr, brms.ptr, bg.ptr, bdx.ptr, bdxr.ptr, bdw.ptr, rows, cols, 1, acc, 0)
+        ctx.sync()
+    finally:
+        ctx.call("glc_set_rmsnorm_variant", 0)
+    out_dx = bdx.numpy()
+    assert rel_fro(out_dx, ref_dx) < FP32_RTOL
+    assert rel_fro(bdw.numpy(), ref_dw) < FP32_RTOL
+    assert np.max(np.abs(bdxr.numpy() - out_dx) / (np.abs(out_dx) + 1e-30)) <= 2.0**-11
+
+
 @pytest.mark.parametrize("full,acc", [(0, 0), (1, 1), (1, 0)])
 @pytest.mark.parametrize("rows,cols", [(5, 128), (300, 512), (4096, 2048), (1000, 2052)])
 def test_rmsnorm_bwd_pipelined_bit_identical(ctx, rows, cols, full, acc):
