@@ -531,7 +531,8 @@ def run_ours(args):
         "traffic": traffic,
         "peak_source": tc_src,
         "cublas_tf32_tflops": cublas_tf32,
-        "traffic_source": "profiles/gemm_tf32_traffic.txt (ncu, average over the step's GEMM launches)",
+        "traffic_source": ("profiles/gemm_tf32_traffic.txt (ncu, one bounded capture per GEMM shape of the step, "
+                           "weighted by its launches per step)"),
         "flops_per_launch_avg": gemm_flops_per_launch,
         "avg_launch_ms": gemm_avg_ms,
         "launches_per_step": counts[0] / max(P, 1),

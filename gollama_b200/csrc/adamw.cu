@@ -53,6 +53,37 @@ __global__ void sumsq_kernel(const float* __restrict__ g, const Seg* __restrict_
   }
 }
 
+// Sums of squares of `nchunks` chunks {start, len}, one block per chunk at a
+// time (blocks stride over the chunks): out[c] is chunk c's float64 sum, the
+// same bits whichever block computes it.  A small grid keeps the pass beside
+// other work (the gradient allreduce's stream) from taking the whole GPU.
+__global__ void sumsq_chunks_kernel(const float* __restrict__ g, const Seg* __restrict__ chunks, int nchunks,
+                                    double* __restrict__ out) {
+  GLC_PDL_ENTRY();
+  __shared__ double red[32];
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    const Seg sg = chunks[c];
+    double acc = 0.0;
+    const float4* base = reinterpret_cast<const float4*>(g + sg.start);
+    const int64_t n4 = sg.len >> 2;
+    for (int64_t i = threadIdx.x; i < n4; i += blockDim.x) {
+      const float4 v = base[i];
+      const double x = v.x, y = v.y, z = v.z, w = v.w;
+      acc = __dadd_rn(acc, __dadd_rn(__dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)), __dadd_rn(__dmul_rn(z, z), __dmul_rn(w, w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double t = 0.0;
+      for (int w = 0; w < (blockDim.x >> 5); ++w) t += red[w];
+      out[c] = t;
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void norm_finish_kernel(const double* __restrict__ partial, int n, float max_norm, double* __restrict__ norm,
                                    float* __restrict__ scale) {
   GLC_PDL_ENTRY();
@@ -176,6 +207,17 @@ int grad_sumsq(Context* ctx, const float* grads, const int64_t* segs, int nseg, 
   ProfScope prof(ctx, PROF_ADAMW, 4.0 * elems, s);
   glc::launch_pdl(ctx, sumsq_kernel, dim3(bx, nseg), 256, 0, s, grads, reinterpret_cast<const Seg*>(segs), partial);
   GLC_LAUNCH_CHECK(ctx, "grad_norm partial");
+  return 0;
+}
+
+int grad_sumsq_chunks(Context* ctx, const float* grads, const int64_t* chunks, int nchunks, int blocks, double* out,
+                      double elems, cudaStream_t s) {
+  if (nchunks <= 0) return 0;
+  if (!grads || !chunks || !out || blocks <= 0) return ctx->fail(GLC_ERR_INVALID, "grad_sumsq_chunks: bad arguments");
+  ProfScope prof(ctx, PROF_ADAMW, 4.0 * elems, s);
+  glc::launch_pdl(ctx, sumsq_chunks_kernel, blocks < nchunks ? blocks : nchunks, 256, 0, s, grads,
+                  reinterpret_cast<const Seg*>(chunks), nchunks, out);
+  GLC_LAUNCH_CHECK(ctx, "grad_sumsq_chunks");
   return 0;
 }
 

@@ -756,11 +756,17 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  // Each step's products are committed in two halves so the math warps and
+  // the accumulate issuer start on the first before the second is done:
+  // s_full (S^T written) / dp_full (dP^T written) from the score issuer,
+  // p_full (P^T written: dV may start) / ds_full (dS^T written: dK) from
+  // the math warps.
   uint64_t *kv_full = bars, *qo_full = bars + 1, *qo_empty = bars + 4, *s_full = bars + 7, *p_full = bars + 9,
            *set_free = bars + 11, *acc_done = bars + 13, *drain = bars + 14, *ld_ready = bars + 15,
            *kv_moved = bars + 17;
   uint64_t* drain_acc = bars + 18;  // abort path of the accumulate issuer
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  uint64_t *dp_full = bars + 19, *ds_full = bars + 21;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* stage_ld = reinterpret_cast<float*>(sm + L::OFF_LD);  // [2][lse 64 | D 64]
   const Roles ro;
@@ -783,7 +789,9 @@ __global__ void __launch_bounds__(NT, 1)
     }
     for (int i = 0; i < L::NSET; ++i) {
       mbar_init(&s_full[i], 1);
+      mbar_init(&dp_full[i], 1);
       mbar_init(&p_full[i], MATH_THREADS);
+      mbar_init(&ds_full[i], MATH_THREADS);
       mbar_init(&set_free[i], 1);
       mbar_init(&ld_ready[i], MATH_THREADS);
     }
@@ -842,13 +850,15 @@ __global__ void __launch_bounds__(NT, 1)
         if (!mbar_wait(&set_free[ts], ((it / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < HD / 8; ++kk) {
+        for (int kk = 0; kk < HD / 8; ++kk)
           umma_tf32_ts(tmem + ts * 128, tmem + L::K_COL + kk * 8, kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
-          umma_tf32_ts(tmem + ts * 128 + 64, tmem + L::V_COL + kk * 8, kdesc<64>(base + 2 * L::QT, kk), idesc_s,
-                       kk > 0 ? 1u : 0u);
-        }
         issued = true;
         umma_commit(&s_full[ts]);
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk)
+          umma_tf32_ts(tmem + ts * 128 + 64, tmem + L::V_COL + kk * 8, kdesc<64>(base + 2 * L::QT, kk), idesc_s,
+                       kk > 0 ? 1u : 0u);
+        umma_commit(&dp_full[ts]);
       }
       if (!ok && issued) {
         umma_commit(drain);
@@ -868,12 +878,16 @@ __global__ void __launch_bounds__(NT, 1)
         if (!mbar_wait(&p_full[pts], (pit / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t acc = (pit > 0 || kk > 0) ? 1u : 0u;
-          umma_tf32_ts(tmem + L::DV_COL, tmem + pts * 128 + kk * 8, mdesc<64>(base + 3 * L::QT, kk), idesc_a, acc);
-          umma_tf32_ts(tmem + L::DK_COL, tmem + pts * 128 + 64 + kk * 8, mdesc<64>(base + L::QT, kk), idesc_a, acc);
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          umma_tf32_ts(tmem + L::DV_COL, tmem + pts * 128 + kk * 8, mdesc<64>(base + 3 * L::QT, kk), idesc_a,
+                       (pit > 0 || kk > 0) ? 1u : 0u);
         issued = true;
+        if (!mbar_wait(&ds_full[pts], (pit / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_tf32_ts(tmem + L::DK_COL, tmem + pts * 128 + 64 + kk * 8, mdesc<64>(base + L::QT, kk), idesc_a,
+                       (pit > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&set_free[pts]);
         umma_commit(&qo_empty[ps]);
       }
@@ -935,36 +949,41 @@ __global__ void __launch_bounds__(NT, 1)
       }
       const uint32_t sa = lane_addr + ts * 128 + hf * 32;
       uint32_t sv[32], dpv[32];
+      float pf[32];
       tmem_ld_32x32b_x32(sa, sv);
-      tmem_ld_32x32b_x32(sa + 64, dpv);
       tmem_ld_wait();
       // every query of this half is past every key of the tile and inside
       // the sequence: no mask (warp-uniform test)
       const int q_lo = qbase + hf * 32;
-      if (q_lo >= k0 + 127 && q_lo + 32 <= S && k0 + 128 <= S) {
+      const bool nomask = q_lo >= k0 + 127 && q_lo + 32 <= S && k0 + 128 <= S;
+      if (nomask) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float p = fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2[e]));
-          const float ds = p * fmaf(__uint_as_float(dpv[e]), scale, -dqs[e]);
-          sv[e] = tf32_bits(p);
-          dpv[e] = tf32_bits(ds);
-        }
+        for (int e = 0; e < 32; ++e) pf[e] = fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2[e]));
       } else {
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int qa = q_lo + e;
           const bool valid = qa < S && key < S && key <= qa;
-          const float p = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2[e])) : 0.f;
-          const float ds = p * fmaf(__uint_as_float(dpv[e]), scale, -dqs[e]);
-          sv[e] = tf32_bits(p);
-          dpv[e] = tf32_bits(ds);
+          pf[e] = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2[e])) : 0.f;
         }
       }
+      // P^T to TMEM: dV += P^T dO may start while dS is computed
+#pragma unroll
+      for (int e = 0; e < 32; ++e) sv[e] = tf32_bits(pf[e]);
       tmem_st_32x32b_x32(sa, sv);
-      tmem_st_32x32b_x32(sa + 64, dpv);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[ts]);
+      WAIT_OR_BREAK(&dp_full[ts], (it / L::NSET) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      tc_fence_after();
+      tmem_ld_32x32b_x32(sa + 64, dpv);
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) dpv[e] = tf32_bits(pf[e] * fmaf(__uint_as_float(dpv[e]), scale, -dqs[e]));
+      tmem_st_32x32b_x32(sa + 64, dpv);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&ds_full[ts]);
     }
     if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
       tc_fence_after();
@@ -1329,7 +1348,10 @@ __global__ void __launch_bounds__(NT, 1)
   uint64_t *qo_full = bars, *qo_moved = bars + 1, *kv_full = bars + 2, *kv_empty = bars + 5, *s_full = bars + 8,
            *p_full = bars + 10, *set_free = bars + 12, *dq_full = bars + 14, *dq_empty = bars + 16, *drain = bars + 18,
            *drain_acc = bars + 19;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  // S and dP are committed separately (s_full, dp_full): the math warps
+  // compute P while the dP products run
+  uint64_t* dp_full = bars + 20;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const Roles ro;
   const int n_items = H * B * n_qt;
@@ -1345,6 +1367,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     for (int i = 0; i < L::NSET; ++i) {
       mbar_init(&s_full[i], 1);
+      mbar_init(&dp_full[i], 1);
       mbar_init(&p_full[i], MATH_THREADS);
       mbar_init(&set_free[i], 1);
       mbar_init(&dq_full[i], 1);
@@ -1420,13 +1443,15 @@ __global__ void __launch_bounds__(NT, 1)
           }
           tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < HD / 8; ++kk) {
+          for (int kk = 0; kk < HD / 8; ++kk)
             umma_tf32_ts(tmem + ts * 128, tmem + L::Q_COL + kk * 8, kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
-            umma_tf32_ts(tmem + ts * 128 + 64, tmem + L::O_COL + kk * 8, kdesc<64>(base + 2 * L::KT, kk), idesc_s,
-                         kk > 0 ? 1u : 0u);
-          }
           issued = true;
           umma_commit(&s_full[ts]);
+#pragma unroll
+          for (int kk = 0; kk < HD / 8; ++kk)
+            umma_tf32_ts(tmem + ts * 128 + 64, tmem + L::O_COL + kk * 8, kdesc<64>(base + 2 * L::KT, kk), idesc_s,
+                         kk > 0 ? 1u : 0u);
+          umma_commit(&dp_full[ts]);
         }
       }
       if (!ok && issued) {
@@ -1500,26 +1525,28 @@ __global__ void __launch_bounds__(NT, 1)
         tc_fence_after();
         const uint32_t sa = lane_addr + ts * 128 + hf * 32;
         uint32_t sv[32], dpv[32];
+        float pf[32];
         tmem_ld_32x32b_x32(sa, sv);
-        tmem_ld_32x32b_x32(sa + 64, dpv);
         tmem_ld_wait();
         const int k_lo = j * 64 + hf * 32;
         const float nDs = -Dq * scale;
         if (k_lo + 32 <= q0 + 1 && q0 + 128 <= S) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float p = fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2));
-            sv[e] = tf32_bits(p * fmaf(__uint_as_float(dpv[e]), scale, nDs));
-          }
+          for (int e = 0; e < 32; ++e) pf[e] = fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2));
         } else {
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int key = k_lo + e;
             const bool valid = qa < S && key < S && key <= qa;
-            const float p = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2)) : 0.f;
-            sv[e] = tf32_bits(p * fmaf(__uint_as_float(dpv[e]), scale, nDs));
+            pf[e] = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2)) : 0.f;
           }
         }
+        WAIT_OR_BREAK(&dp_full[ts], (kv / L::NSET) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+        tc_fence_after();
+        tmem_ld_32x32b_x32(sa + 64, dpv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) sv[e] = tf32_bits(pf[e] * fmaf(__uint_as_float(dpv[e]), scale, nDs));
         tmem_st_32x32b_x32(sa, sv);
         tmem_st_wait();
         tc_fence_before();
@@ -1527,7 +1554,8 @@ __global__ void __launch_bounds__(NT, 1)
       }
       if (!ok) break;
       // the next item's Q and dO rows -> TMEM: every product of this item that
-      // reads them completed before its last s_full
+      // reads them (S reads Q, dP reads dO) completed before its last s_full
+      // and dp_full, both waited for above
       if (it + static_cast<int>(gridDim.x) < n_items) {
         WAIT_OR_BREAK(qo_full, (local + 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
         tile_rows_to_tmem<HD>(sm + L::OFF_QO, r, lane_addr, L::Q_COL, 0, hf);

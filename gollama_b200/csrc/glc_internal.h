@@ -299,6 +299,10 @@ int grad_norm(Context* ctx, const float* grads, const int64_t* segs, int nseg, f
 int grad_norm_blocks(const Context* ctx, int nseg);
 int grad_sumsq(Context* ctx, const float* grads, const int64_t* segs, int nseg, int bx, double* partial, double elems,
                cudaStream_t s);
+// Per-chunk float64 sums of squares of chunks {start, len} (multiples of 4
+// floats) into out[nchunks], `blocks` blocks striding over the chunks.
+int grad_sumsq_chunks(Context* ctx, const float* grads, const int64_t* chunks, int nchunks, int blocks, double* out,
+                      double elems, cudaStream_t s);
 int grad_norm_finish(Context* ctx, const double* partial, long long n, float max_norm, double* norm_out,
                      float* scale_out, cudaStream_t s, double* lvl = nullptr, long long lvl_cap = 0);
 int adamw(Context* ctx, float* p, float* g, float* m, float* v, float* shadow, const int64_t* segs, int nseg,

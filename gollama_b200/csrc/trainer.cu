@@ -746,10 +746,25 @@ struct Trainer {
   cudaEvent_t comm_done = nullptr;
   std::vector<int> consumers, bucket_pending;
   std::vector<char> bucket_launched;
+  // Data parallelism: the clip norm's sums of squares are taken per bucket on
+  // the communication stream right after the bucket's sum over the ranks
+  // (chunks of at most kNormChunk floats of the allocated gradients, bucket
+  // b's at [dp_chunk_off[b], dp_chunk_off[b + 1])), so no pass over all the
+  // gradients follows the backward.  The tables are built for the set of
+  // allocated gradients at the start of a step; a step that allocates new
+  // ones (the first) takes the full pass instead.
+  int64_t* dp_chunks_dev = nullptr;
+  std::vector<int> dp_chunk_off;
+  std::vector<char> dp_chunks_for;
+  double* dp_slots = nullptr;  // [chunks] then the finishing sum's first level
+  long long dp_nchunks = 0, dp_slots_cap = 0;
+  double dp_chunk_elems = 0;
 
   ~Trainer() {
     for (cudaEvent_t e : bucket_ev) cudaEventDestroy(e);
     if (comm_done) cudaEventDestroy(comm_done);
+    cudaFree(dp_chunks_dev);
+    cudaFree(dp_slots);
     cudaFree(scalars);
     cudaFreeHost(loss_host);
     cudaFree(tok_dev);
@@ -790,6 +805,43 @@ struct Trainer {
         throw StepError{GLC_ERR_CUDA};
     }
     segs_for = model->grad_allocated;
+  }
+
+  void refresh_dp_chunks() {
+    if (dp_chunks_for == model->grad_allocated && !dp_chunk_off.empty()) return;
+    const int nb = static_cast<int>(model->bucket_begin.size());
+    std::vector<int64_t> s;
+    dp_chunk_off.assign(nb + 1, 0);
+    dp_chunk_elems = 0;
+    for (int b = 0; b < nb; ++b) {
+      dp_chunk_off[b] = static_cast<int>(s.size() / 2);
+      for (int i = 0; i < model->num_params(); ++i) {
+        if (model->bucket_of[i] != b || !model->grad_allocated[i]) continue;
+        const int64_t st = model->offset[i], len = model->rows[i] * model->cols[i];
+        for (int64_t o = 0; o < len; o += kNormChunk) {
+          s.push_back(st + o);
+          s.push_back(std::min<int64_t>(kNormChunk, len - o));
+        }
+        dp_chunk_elems += static_cast<double>(len);
+      }
+    }
+    dp_chunk_off[nb] = static_cast<int>(s.size() / 2);
+    dp_nchunks = dp_chunk_off[nb];
+    cudaFree(dp_chunks_dev);
+    dp_chunks_dev = nullptr;
+    if (!s.empty()) {
+      if (cudaMalloc(&dp_chunks_dev, s.size() * sizeof(int64_t)) != cudaSuccess) throw StepError{GLC_ERR_NOMEM};
+      if (cudaMemcpy(dp_chunks_dev, s.data(), s.size() * sizeof(int64_t), cudaMemcpyHostToDevice) != cudaSuccess)
+        throw StepError{GLC_ERR_CUDA};
+    }
+    const long long need = dp_nchunks + dp_nchunks / 1024 + 2;
+    if (need > dp_slots_cap) {
+      cudaFree(dp_slots);
+      dp_slots = nullptr;
+      if (cudaMalloc(&dp_slots, sizeof(double) * static_cast<size_t>(need)) != cudaSuccess) throw StepError{GLC_ERR_NOMEM};
+      dp_slots_cap = need;
+    }
+    dp_chunks_for = model->grad_allocated;
   }
 
   void refresh_rest_segments() {
@@ -909,6 +961,9 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, int B, int
       if (p->param >= 0) f(p->param);
       for (int i : p->group) f(i);
     };
+    // per-bucket clip-norm tables for the gradients allocated so far
+    if (dp) refresh_dp_chunks();
+    const std::vector<char> alloc_at_start = dp ? model->grad_allocated : std::vector<char>();
     auto launch_bucket = [&](int b) {
       if (bucket_launched[b]) return;
       bucket_launched[b] = 1;
@@ -917,6 +972,12 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, int B, int
         throw StepError{GLC_ERR_CUDA};
       ck(dp_allreduce_on(ctx, model->grads + model->bucket_begin[b],
                          static_cast<size_t>(model->bucket_end[b] - model->bucket_begin[b]), ctx->comm_stream));
+      // the bucket's summed gradients are final: their squares, 16 blocks
+      // beside the backward
+      const int c0 = dp_chunk_off[b], c1 = dp_chunk_off[b + 1];
+      if (c1 > c0)
+        ck(grad_sumsq_chunks(ctx, model->grads, dp_chunks_dev + 2 * static_cast<int64_t>(c0), c1 - c0, 16,
+                             dp_slots + c0, 0.0, ctx->comm_stream));
     };
     const Tape::OrderHook before = [&](const std::vector<Node*>& run) {
       consumers.assign(np, 0);
@@ -1015,6 +1076,11 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, int B, int
                         rest_elems, ctx->stream));
         ck(grad_norm_finish(ctx, model->norm_slots, model->norm_slot_used + static_cast<long long>(bx) * nrest,
                             c.grad_clip_norm, d_norm, d_scale, ctx->stream, model->norm_lvl, model->norm_lvl_cap));
+      } else if (dp && model->grad_allocated == alloc_at_start && dp_nchunks > 0) {
+        // the per-bucket sums taken after each allreduce (this step allocated
+        // no new gradient, so the tables cover every one)
+        ck(grad_norm_finish(ctx, dp_slots, dp_nchunks, c.grad_clip_norm, d_norm, d_scale, ctx->stream,
+                            dp_slots + dp_nchunks, dp_slots_cap - dp_nchunks));
       } else {
         ck(grad_norm(ctx, model->grads, segs_dev, nseg, c.grad_clip_norm, d_norm, d_scale, nullptr, 0,
                      static_cast<double>(seg_elems), ctx->stream));

@@ -167,12 +167,12 @@ def dq(H, B, n_qt, S, grid, cta, seed):
     n_k64 = (S + 63) // 64
     nk_of = lambda it: min(n_k64, ((n_qt - 1 - it // (H * B)) * 128 + 128) // 64)
     bars = {(n, i): Bar(f"{n}{i}", 1) for n, k in [("qo_full", 1), ("qo_moved", 1), ("kv_full", 3),
-                                                       ("kv_empty", 3), ("s_full", 2), ("p_full", 2),
+                                                       ("kv_empty", 3), ("s_full", 2), ("dp_full", 2), ("p_full", 2),
                                                        ("set_free", 2), ("dq_full", 2), ("dq_empty", 2)]
             for i in range(k)}
     b = lambda n, i=0: bars[(n, i)]
     ev = []
-    st = {"tmem_qo": None, "staging": None, "s": set(), "dq": set(), "epi": set(), "buf": [None, None]}
+    st = {"tmem_qo": None, "staging": None, "s": set(), "dp": set(), "dq": set(), "epi": set(), "buf": [None, None]}
 
     def tma():
         kv = 0
@@ -203,10 +203,21 @@ def dq(H, B, n_qt, S, grid, cta, seed):
                 yield from _wait(b("set_free", ts), ((kv // 2) & 1) ^ 1, kv // 2 - 1)
                 assert (kv < 2 or (kv - 2) in st["dq"]) and st["tmem_qo"] == local
 
-                def done(ts=ts, kv=kv):
+                def s_done(ts=ts, kv=kv):
                     st["s"].add(kv)
                     b("s_full", ts).arrive()
-                ev.append(done)
+
+                def make_dp_done(ts, kv):
+                    def dp_done():
+                        # a commit arrives once every earlier MMA of its thread completed
+                        if kv not in st["s"]:
+                            ev.append(dp_done)
+                            return
+                        st["dp"].add(kv)
+                        b("dp_full", ts).arrive()
+                    return dp_done
+                ev.append(s_done)
+                ev.append(make_dp_done(ts, kv))
                 kv += 1
 
     def acc():
@@ -240,11 +251,14 @@ def dq(H, B, n_qt, S, grid, cta, seed):
                 ts = kv % 2
                 yield from _wait(b("s_full", ts), (kv // 2) & 1, kv // 2)
                 assert kv in st["s"]
+                yield from _wait(b("dp_full", ts), (kv // 2) & 1, kv // 2)
+                assert kv in st["dp"]
                 b("p_full", ts).arrive()
                 kv += 1
             if local + 1 < len(items):
                 yield from _wait(b("qo_full"), (local + 1) & 1, local + 1)
-                assert st["staging"] == local + 1 and all(k in st["s"] for k in range(kv))
+                # Q and dO in TMEM are overwritten: every S and dP product of this item has completed
+                assert st["staging"] == local + 1 and all(k in st["s"] and k in st["dp"] for k in range(kv))
                 st["tmem_qo"] = local + 1
                 b("qo_moved").arrive()
             ob = local & 1
@@ -252,5 +266,106 @@ def dq(H, B, n_qt, S, grid, cta, seed):
             assert st["buf"][ob] == local
             st["epi"].add(local)
             b("dq_empty", ob).arrive()
+
+    _drive({"tma": tma(), "smma": smma(), "acc": acc(), "math": math()}, ev, rnd)
+
+
+def dkdv(n_heads, nq, seed):
+    """attn_bwd_dkdv_tc_kernel's protocol for one CTA: n_heads * nq steps of
+    64 queries, three Q/dO stages (K and V land in the third and are copied
+    to TMEM first), two TMEM sets, each step committed in halves (S^T then
+    dP^T by the score issuer; P^T then dS^T by the math warps)."""
+    rnd = random.Random(seed)
+    n_it = n_heads * nq
+    bars = {(n, i): Bar(f"{n}{i}", 1) for n, k in [("kv_full", 1), ("kv_moved", 1), ("qo_full", 3), ("qo_empty", 3),
+                                                       ("s_full", 2), ("dp_full", 2), ("p_full", 2), ("ds_full", 2),
+                                                       ("set_free", 2), ("acc_done", 1), ("ld_ready", 2)]
+            for i in range(k)}
+    b = lambda n, i=0: bars[(n, i)]
+    ev = []
+    st = {"kv_in_stage2": False, "stage": [None] * 3, "S": set(), "dP": set(), "P": set(), "dS": set(),
+          "dv": set(), "dk": set(), "acc_done": False}
+
+    def tma():
+        def land_kv():
+            st["kv_in_stage2"] = True
+            b("kv_full").complete_tx(1)
+        b("kv_full").expect_tx(1)
+        ev.append(land_kv)
+        for it in range(n_it):
+            s_, ph = it % 3, (it // 3) & 1
+            if it == 2:
+                yield from _wait(b("kv_moved"), 0, 0)
+                st["kv_in_stage2"] = False
+            yield from _wait(b("qo_empty", s_), ph ^ 1, it // 3 - 1)
+            assert it < 3 or (it - 3) in st["dk"]
+
+            def land(s_=s_, it=it):
+                st["stage"][s_] = it
+                b("qo_full", s_).complete_tx(1)
+            b("qo_full", s_).expect_tx(1)
+            ev.append(land)
+
+    def smma():
+        yield from _wait(b("kv_moved"), 0, 0)
+        for it in range(n_it):
+            s_, ts = it % 3, it % 2
+            yield from _wait(b("qo_full", s_), (it // 3) & 1, it // 3)
+            yield from _wait(b("set_free", ts), ((it // 2) & 1) ^ 1, it // 2 - 1)
+            assert st["stage"][s_] == it and (it < 2 or (it - 2) in st["dk"])
+
+            def s_done(ts=ts, it=it):
+                st["S"].add(it)
+                b("s_full", ts).arrive()
+
+            def dp_done(ts=ts, it=it):
+                st["dP"].add(it)
+                b("dp_full", ts).arrive()
+            ev.append(s_done)
+            ev.append(dp_done)
+
+    def acc():
+        for it in range(n_it):
+            s_, ts = it % 3, it % 2
+            yield from _wait(b("p_full", ts), (it // 2) & 1, it // 2)
+            assert it in st["P"] and st["stage"][s_] == it
+            ev.append(lambda it=it: st["dv"].add(it))
+            yield from _wait(b("ds_full", ts), (it // 2) & 1, it // 2)
+            assert it in st["dS"]
+
+            def done(ts=ts, s_=s_, it=it):
+                st["dk"].add(it)
+                st["dv"].add(it)
+                b("set_free", ts).arrive()
+                b("qo_empty", s_).arrive()
+            ev.append(done)
+
+        def fin():
+            # a commit arrives once every earlier MMA of its thread completed
+            if len(st["dk"]) < n_it:
+                ev.append(fin)
+                return
+            st["acc_done"] = True
+            b("acc_done").arrive()
+        ev.append(fin)
+
+    def math():
+        yield from _wait(b("kv_full"), 0, 0)
+        assert st["kv_in_stage2"]
+        b("kv_moved").arrive()
+        for it in range(n_it):
+            ts = it % 2
+            b("ld_ready", it & 1).arrive()
+            yield from _wait(b("ld_ready", it & 1), (it >> 1) & 1, it >> 1)
+            yield from _wait(b("s_full", ts), (it // 2) & 1, it // 2)
+            assert it in st["S"]
+            st["P"].add(it)
+            b("p_full", ts).arrive()
+            yield from _wait(b("dp_full", ts), (it // 2) & 1, it // 2)
+            assert it in st["dP"]
+            st["dS"].add(it)
+            b("ds_full", ts).arrive()
+        yield from _wait(b("acc_done"), 0, 0)
+        assert st["acc_done"] and len(st["dk"]) == n_it
 
     _drive({"tma": tma(), "smma": smma(), "acc": acc(), "math": math()}, ev, rnd)

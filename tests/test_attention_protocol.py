@@ -36,3 +36,9 @@ def test_simulator_catches_a_wrong_parity():
     with pytest.raises(StopIteration):
         next(sim._wait(bar, 1, 1))
     assert next(w, "blocked") is None
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_dkdv_protocol(seed):
+    r = random.Random(seed)
+    sim.dkdv(r.randint(1, 4), r.randint(1, 16), seed)

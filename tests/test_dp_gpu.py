@@ -34,7 +34,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank, port, shape_name, out_dir):
+def _rank_main(rank, port, shape_name, out_dir, steps=1):
     import torch.distributed as dist
 
     from gollama_b200.device import Context
@@ -54,13 +54,18 @@ def _rank_main(rank, port, shape_name, out_dir):
             uid = (C.c_ubyte * 128).from_buffer_copy(obj[0])
             ctx.call("glc_dp_init", rank, WORLD, uid, 120000)
             params = syn.init_params(shape, 1234)
-            inputs, targets = syn.batch(shape, 1234)
-            rows = np.array_split(np.arange(inputs.shape[0]), WORLD)[rank]
             model = NewTrainableModel(config_for(shape, WorldSize=WORLD, **STEP_HPARAMS), ctx)
             model.set_params(params)
-            loss = NewTrainer(model).TrainStep(inputs[rows], targets[rows])
+            tr = NewTrainer(model)
+            norms = []
+            for step in range(steps):
+                inputs, targets = syn.batch(shape, 1234 + step)
+                rows = np.array_split(np.arange(inputs.shape[0]), WORLD)[rank]
+                loss = tr.TrainStep(inputs[rows], targets[rows])
+                norms.append(tr.last_stats()[0])
             np.savez(os.path.join(out_dir, f"rank{rank}.npz"), loss=loss, grads=model.get_grads(),
-                     weights=model.get_params(), has=np.array([p.has_grad for p in model.Params()]))
+                     weights=model.get_params(), has=np.array([p.has_grad for p in model.Params()]),
+                     norms=np.array(norms))
             ctx.call("glc_dp_destroy")
     finally:
         dist.destroy_process_group()
@@ -97,3 +102,37 @@ def test_two_gpu_step_matches_global_batch(shape):
             assert e < GRAD_RFRO, f"grad of param {i}: rel-fro {e:.3e}"
         e = rel_fro(r[0]["weights"][off : off + n], st.params[off : off + n])
         assert e < WEIGHT_RFRO, f"weight of param {i}: rel-fro {e:.3e}"
+
+
+@pytest.mark.skipif(_gpus() < WORLD, reason="needs two GPUs")
+@pytest.mark.parametrize("shape", [syn.TINY_LLAMA_MODE, syn.TINY], ids=lambda s: s.name)
+def test_two_gpu_three_steps_match_global_batch(shape):
+    """Three data-parallel steps: from the second on, the clip norm comes from
+    the per-bucket sums taken after each allreduce.  Every step's clip norm,
+    and the third step's gradients and weights, against the oracle's steps on
+    the global batches."""
+    import torch.multiprocessing as mp
+
+    from oracle.oracle import Oracle, TrainState
+
+    steps = 3
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_rank_main, args=(_free_port(), shape.name, d, steps), nprocs=WORLD, start_method="spawn")
+        r = [np.load(os.path.join(d, f"rank{i}.npz")) for i in range(WORLD)]
+    assert np.array_equal(r[0]["weights"], r[1]["weights"])
+    assert np.array_equal(r[0]["norms"], r[1]["norms"])
+    orc = Oracle(threads=threads())
+    ocfg = oracle_config(shape)
+    layout = orc.param_layout(ocfg)
+    st = TrainState.create(syn.init_params(shape, 1234), len(layout), oracle_optim())
+    onorms = []
+    for step in range(steps):
+        inputs, targets = syn.batch(shape, 1234 + step)
+        onorms.append(orc.train_step(ocfg, st, inputs, targets)[1])
+    for a, b in zip(r[0]["norms"], onorms):
+        assert abs(a - b) <= 2e-3 * abs(b), (list(r[0]["norms"]), onorms)
+    for i, (off, rows, cols) in enumerate(layout):
+        n = rows * cols
+        if st.has_grad[i]:
+            assert rel_fro(r[0]["grads"][off : off + n], st.grads[off : off + n]) < GRAD_RFRO, i
+        assert rel_fro(r[0]["weights"][off : off + n], st.params[off : off + n]) < WEIGHT_RFRO, i
