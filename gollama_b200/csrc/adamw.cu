@@ -163,6 +163,10 @@ __device__ __forceinline__ void adam_elem(float& p, float& g, float& m, float& v
 
 // Segments start and end on multiples of 4 floats (every parameter's size is
 // a multiple of the hidden size, itself a multiple of 4): float4 throughout.
+// Each thread takes U float4 groups per iteration (U strides apart) and
+// issues all their loads before any arithmetic, so more bytes are in flight
+// per thread; the per-element arithmetic is unchanged.
+template <int U>
 __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
                              float* __restrict__ shadow, const Seg* __restrict__ segs,
                              const float* __restrict__ clip_scale, AdamArgs a, int write_g) {
@@ -176,17 +180,33 @@ __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float
   float4* v4 = reinterpret_cast<float4*>(v + sg.start);
   float4* s4 = shadow ? reinterpret_cast<float4*>(shadow + sg.start) : nullptr;
   const int64_t n4 = sg.len >> 2;
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
-    float4 P = p4[i], G = g4[i], M = m4[i], V = v4[i];
-    adam_elem(P.x, G.x, M.x, V.x, scale, scaled, a);
-    adam_elem(P.y, G.y, M.y, V.y, scale, scaled, a);
-    adam_elem(P.z, G.z, M.z, V.z, scale, scaled, a);
-    adam_elem(P.w, G.w, M.w, V.w, scale, scaled, a);
-    if (scaled && write_g) g4[i] = G;
-    m4[i] = M;
-    v4[i] = V;
-    p4[i] = P;
-    if (s4) s4[i] = make_float4(round_tf32(P.x), round_tf32(P.y), round_tf32(P.z), round_tf32(P.w));
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i0 = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i0 < n4; i0 += U * stride) {
+    float4 P[U], G[U], M[U], V[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < n4) {
+        P[u] = p4[i];
+        G[u] = g4[i];
+        M[u] = m4[i];
+        V[u] = v4[i];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= n4) continue;
+      adam_elem(P[u].x, G[u].x, M[u].x, V[u].x, scale, scaled, a);
+      adam_elem(P[u].y, G[u].y, M[u].y, V[u].y, scale, scaled, a);
+      adam_elem(P[u].z, G[u].z, M[u].z, V[u].z, scale, scaled, a);
+      adam_elem(P[u].w, G[u].w, M[u].w, V[u].w, scale, scaled, a);
+      if (scaled && write_g) g4[i] = G[u];
+      m4[i] = M[u];
+      v4[i] = V[u];
+      p4[i] = P[u];
+      if (s4) s4[i] = make_float4(round_tf32(P[u].x), round_tf32(P[u].y), round_tf32(P[u].z), round_tf32(P[u].w));
+    }
   }
 }
 
@@ -281,8 +301,8 @@ int adamw(Context* ctx, float* p, float* g, float* m, float* v, float* shadow, c
   if (bx < 4) bx = 4;
   // p, g, m, v read; p, m, v and the TF32 shadow written
   ProfScope prof(ctx, PROF_ADAMW, (shadow ? 32.0 : 28.0) * elems, s);
-  glc::launch_pdl(ctx, adamw_kernel, dim3(bx, nseg), 256, 0, s, p, g, m, v, shadow, reinterpret_cast<const Seg*>(segs), clip_scale, a,
-                  write_grad ? 1 : 0);
+  glc::launch_pdl(ctx, adamw_kernel<2>, dim3(bx, nseg), 256, 0, s, p, g, m, v, shadow, reinterpret_cast<const Seg*>(segs),
+                  clip_scale, a, write_grad ? 1 : 0);
   GLC_LAUNCH_CHECK(ctx, "adamw");
   return 0;
 }
