@@ -81,6 +81,13 @@ __device__ __forceinline__ void tma_tile(uint8_t* dst, const CUtensorMap* tm, ui
   for (int c = 0; c < HD / 32; ++c) tma_load_2d(dst + c * R * 128, tm, bar, col0 + 32 * c, row0);
 }
 
+// tma_tile issued by a whole warp (one elected lane).
+template <int HD, int R>
+__device__ __forceinline__ void tma_tile_warp(uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, int col0, int row0) {
+#pragma unroll
+  for (int c = 0; c < HD / 32; ++c) tma_load_2d_warp(dst + c * R * 128, tm, bar, col0 + 32 * c, row0);
+}
+
 // 2^x by the MUFU approximation (relative error ~2^-22): P and dS are rounded
 // to TF32 (2^-11) right after, so the approximation is invisible.
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -466,7 +473,7 @@ __global__ void __launch_bounds__(NT, 1)
   const uint32_t sQ = smem_u32(sm), sK = sQ + L::OFF_K, sV = sQ + L::OFF_V;
 
   if (ro.warp == 0) {
-    if (ro.lane == 0) {
+    {  // whole warp: elect.sync issues
       bool ok = true;
       int armed_q[2] = {-1, -1}, armed_k[2] = {-1, -1}, armed_v[2] = {-1, -1};
       int kv = 0, local = 0;
@@ -475,20 +482,20 @@ __global__ void __launch_bounds__(NT, 1)
         const int kh = w.h / G, row_base = w.b * S;
         const int qb = local & 1;
         const uint32_t qph = (local >> 1) & 1;
-        if (!mbar_wait(&q_empty[qb], qph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
-        mbar_arrive_expect_tx(&q_full[qb], L::Q);
-        tma_tile<HD, 128>(sm + qb * L::Q, &tmQ, &q_full[qb], w.h * HD, row_base + w.qt * 128);
+        if (!mbar_wait_warp(&q_empty[qb], qph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx_warp(&q_full[qb], L::Q);
+        tma_tile_warp<HD, 128>(sm + qb * L::Q, &tmQ, &q_full[qb], w.h * HD, row_base + w.qt * 128);
         armed_q[qb] = static_cast<int>(qph);
         for (int j = 0; j <= w.qt; ++j, ++kv) {
           const int st = kv & 1;
           const uint32_t ph = (kv >> 1) & 1;
-          if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
-          mbar_arrive_expect_tx(&k_full[st], L::K);
-          tma_tile<HD, 128>(sm + L::OFF_K + st * L::K, &tmK, &k_full[st], kh * HD, row_base + j * 128);
+          if (!mbar_wait_warp(&k_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+          mbar_arrive_expect_tx_warp(&k_full[st], L::K);
+          tma_tile_warp<HD, 128>(sm + L::OFF_K + st * L::K, &tmK, &k_full[st], kh * HD, row_base + j * 128);
           armed_k[st] = static_cast<int>(ph);
-          if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
-          mbar_arrive_expect_tx(&v_full[st], L::V);
-          tma_tile<HD, 128>(sm + L::OFF_V + st * L::V, &tmV, &v_full[st], kh * HD, row_base + j * 128);
+          if (!mbar_wait_warp(&v_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+          mbar_arrive_expect_tx_warp(&v_full[st], L::V);
+          tma_tile_warp<HD, 128>(sm + L::OFF_V + st * L::V, &tmV, &v_full[st], kh * HD, row_base + j * 128);
           armed_v[st] = static_cast<int>(ph);
         }
       }
@@ -501,40 +508,40 @@ __global__ void __launch_bounds__(NT, 1)
       }
     }
   } else if (ro.warp == 1) {
-    if (ro.lane == 0) {
+    {  // whole warp: elect.sync issues
       constexpr uint32_t idesc_s = umma_idesc_tf32(128, 128, false, false);
       bool ok = true, issued = false;
       int sq = 0, local = 0;
       for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
         const FwdItem w = fwd_item(it, H, B, n_qt);
         const int qb = local & 1;
-        if (!mbar_wait(&q_full[qb], (local >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        if (!mbar_wait_warp(&q_full[qb], (local >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
         for (int j = 0; j <= w.qt; ++j, ++sq) {
           const int sb = sq % 3, st = sq & 1;
-          if (sq >= 3 && !mbar_wait(&pv_done[sb], ((sq - 3) / 3) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
+          if (sq >= 3 && !mbar_wait_warp(&pv_done[sb], ((sq - 3) / 3) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
             ok = false;
             break;
           }
-          if (!mbar_wait(&k_full[st], (sq >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          if (!mbar_wait_warp(&k_full[st], (sq >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < HD / 8; ++kk)
-            umma_tf32(tmem + sb * 128, kdesc<128>(sQ + qb * L::Q, kk), kdesc<128>(sK + st * L::K, kk), idesc_s,
+            umma_tf32_warp(tmem + sb * 128, kdesc<128>(sQ + qb * L::Q, kk), kdesc<128>(sK + st * L::K, kk), idesc_s,
                       kk > 0 ? 1u : 0u);
           issued = true;
-          umma_commit(&k_empty[st]);
-          umma_commit(&s_full[sb]);
+          umma_commit_warp(&k_empty[st]);
+          umma_commit_warp(&s_full[sb]);
         }
         if (!ok) break;
-        umma_commit(&q_empty[qb]);  // this item's score MMAs no longer read Q[qb]
+        umma_commit_warp(&q_empty[qb]);  // this item's score MMAs no longer read Q[qb]
       }
       if (!ok && issued) {
-        umma_commit(drain);
+        umma_commit_warp(drain);
         mbar_drain(drain, 0, err);
       }
     }
   } else if (ro.warp == ACC_WARP) {
-    if (ro.lane == 0) {
+    {  // whole warp: elect.sync issues
       constexpr uint32_t idesc_o = umma_idesc_tf32(128, HD, false, true);
       bool ok = true, issued = false;
       int sq = 0, local = 0;
@@ -542,29 +549,29 @@ __global__ void __launch_bounds__(NT, 1)
         const FwdItem w = fwd_item(it, H, B, n_qt);
         const int ob = local & 1;
         // O[ob] was read out by the math warps for item local - 2
-        if (!mbar_wait(&o_empty[ob], ((local >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
+        if (!mbar_wait_warp(&o_empty[ob], ((local >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
           ok = false;
           break;
         }
         tc_fence_after();
         for (int j = 0; j <= w.qt; ++j, ++sq) {
           const int sb = sq % 3, st = sq & 1;
-          if (!mbar_wait(&p_full[sb], (sq / 3) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-          if (!mbar_wait(&v_full[st], (sq >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          if (!mbar_wait_warp(&p_full[sb], (sq / 3) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          if (!mbar_wait_warp(&v_full[st], (sq >> 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 16; ++kk)
-            umma_tf32_ts(tmem + L::O_COL + ob * HD, tmem + sb * 128 + kk * 8, mdesc<128>(sV + st * L::V, kk), idesc_o,
+            umma_tf32_ts_warp(tmem + L::O_COL + ob * HD, tmem + sb * 128 + kk * 8, mdesc<128>(sV + st * L::V, kk), idesc_o,
                          (j > 0 || kk > 0) ? 1u : 0u);
           issued = true;
-          umma_commit(&v_empty[st]);
-          umma_commit(&pv_done[sb]);
+          umma_commit_warp(&v_empty[st]);
+          umma_commit_warp(&pv_done[sb]);
         }
         if (!ok) break;
-        umma_commit(&o_full[ob]);
+        umma_commit_warp(&o_full[ob]);
       }
       if (!ok && issued) {
-        umma_commit(drain_acc);
+        umma_commit_warp(drain_acc);
         mbar_drain(drain_acc, 0, err);
       }
     }
@@ -718,12 +725,13 @@ struct DkdvLayout {
 // Copies row `row` of a K-major SW128 tile of 128 rows x HD fp32 (HD/32 blocks
 // of [128][128 B]) into TMEM columns [col, col + HD) of the thread's lane: the
 // column blocks are shared between the two warps of the lane quarter.
-template <int HD>
+// With NP warps per lane quarter, block b goes to the warp with (b % NP) == part.
+template <int HD, int NP = 2>
 __device__ __forceinline__ void tile_rows_to_tmem(const uint8_t* tile, int row, uint32_t lane_addr, int col,
-                                                  int first_block, int hf) {
+                                                  int first_block, int part) {
 #pragma unroll
   for (int cb = 0; cb < HD / 32; ++cb) {
-    if (((first_block + cb) & 1) != hf) continue;
+    if (((first_block + cb) % NP) != part) continue;
     const uint8_t* rp = tile + cb * (128 * 128) + row * 128;
     uint32_t v[32];
 #pragma unroll
@@ -994,6 +1002,304 @@ __global__ void __launch_bounds__(NT, 1)
       const int part = hf;
 #pragma unroll 1
       for (int cc = 0; cc < HD / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_addr + (part == 0 ? L::DV_COL : L::DK_COL) + cc * 32, v);
+        tmem_ld_wait();
+        if (key < S) {
+          float* dst = (part == 0 ? dv_out + trow * dv_ld : dk_out + trow * dk_ld) + oh * HD + cc * 32;
+          const bool rnd = part == 0 && round_dv && nsplit == 1;
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            float4 o4 = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
+                                    __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
+            if (rnd) o4 = make_float4(round_tf32(o4.x), round_tf32(o4.y), round_tf32(o4.z), round_tf32(o4.w));
+            reinterpret_cast<float4*>(dst)[g] = o4;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (ro.warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
+// ====================================================== backward, two math groups
+// 608 threads: warp 0 TMA, warp 1 score MMAs, warps 2..17 math in two groups
+// of eight, warp 18 accumulating MMAs.  Group g (warps 2 + 8g .. 9 + 8g) takes
+// the steps with step % 2 == g and owns TMEM S/dP set g, so the softmax of one
+// step overlaps the other group's: with one group of eight warps the math of
+// consecutive steps ran back to back and bounded the kernel.  Each warp
+// stages the lse / D of its own 32 queries in a private shared-memory slot
+// (no block-wide barrier per step).  Same arithmetic as the one-group
+// kernels, bit for bit.
+constexpr int NT2 = 608;
+constexpr int GROUP_THREADS = 256;
+constexpr int ACC_WARP2 = 18;
+
+struct Roles2 {
+  int warp, lane;
+  __device__ Roles2() : warp(threadIdx.x >> 5), lane(threadIdx.x & 31) {}
+  __device__ int quarter() const { return warp & 3; }               // TMEM lanes this warp may access
+  __device__ int group() const { return (warp - 2) >> 3; }          // math group (math warps)
+  __device__ int half() const { return ((warp - 2) >> 2) & 1; }     // column half of a tile within the group
+  __device__ int part() const { return (warp - 2) >> 2; }           // 0..3: the warp among the four of its quarter
+};
+
+template <int HD>
+struct Dkdv2Layout : DkdvLayout<HD> {
+  // per math warp: [lse * log2(e) of its 32 queries | D * scale of them]
+  static constexpr int OFF_STG = DkdvLayout<HD>::OFF_LD, STG_BYTES = 16 * 64 * 4;
+  static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
+  static constexpr int BYTES = OFF_BAR + 256 + 1024;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(NT2, 1)
+    attn_bwd_dkdv2_kernel(const __grid_constant__ CUtensorMap tmQk, const __grid_constant__ CUtensorMap tmQm,
+                          const __grid_constant__ CUtensorMap tmOk, const __grid_constant__ CUtensorMap tmOm,
+                          const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                          const float* __restrict__ lse, const float* __restrict__ Dv, float* __restrict__ dk_out,
+                          float* __restrict__ dv_out, int dk_ld, int dv_ld, int nsplit, int S, int H, int Hkv,
+                          float scale, float scale_log2, int round_dv, int* err) {
+  GLC_PDL_ENTRY();
+  using L = Dkdv2Layout<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint64_t *kv_full = bars, *qo_full = bars + 1, *qo_empty = bars + 4, *s_full = bars + 7, *p_full = bars + 9,
+           *set_free = bars + 11, *acc_done = bars + 13, *drain = bars + 14, *kv_moved = bars + 15,
+           *drain_acc = bars + 16, *dp_full = bars + 17, *ds_full = bars + 19;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const Roles2 ro;
+  const int G = H / Hkv;
+  const int kt = blockIdx.z, b = blockIdx.y;
+  const int kh = static_cast<int>(blockIdx.x) / nsplit, split = static_cast<int>(blockIdx.x) - kh * nsplit;
+  const int n_heads = G / nsplit;
+  const int h_first = kh * G + split * n_heads;
+  const int k0 = kt * 128, row_base = b * S;
+  const int qi0 = k0 / 64, n_q64 = (S + 63) / 64;
+  const int nq = n_q64 - qi0;
+  const int n_it = n_heads * nq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(kv_moved, 2 * GROUP_THREADS);
+    for (int i = 0; i < L::NST; ++i) {
+      mbar_init(&qo_full[i], 1);
+      mbar_init(&qo_empty[i], 1);
+    }
+    for (int i = 0; i < L::NSET; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&dp_full[i], 1);
+      mbar_init(&p_full[i], GROUP_THREADS);
+      mbar_init(&ds_full[i], GROUP_THREADS);
+      mbar_init(&set_free[i], 1);
+    }
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    mbar_init(drain_acc, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (ro.warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t s0 = smem_u32(sm);
+
+  if (ro.warp == 0) {
+    {  // whole warp: elect.sync issues
+      mbar_arrive_expect_tx_warp(kv_full, L::K + L::V);
+      tma_tile_warp<HD, 128>(sm + L::OFF_KV, &tmK, kv_full, kh * HD, row_base + k0);
+      tma_tile_warp<HD, 128>(sm + L::OFF_KV + L::K, &tmV, kv_full, kh * HD, row_base + k0);
+      int armed[L::NST] = {-1, -1, -1};
+      bool ok = true;
+      for (int it = 0; it < n_it; ++it) {
+        const int st = it % L::NST;
+        const uint32_t ph = (it / L::NST) & 1;
+        const int hq = h_first + it / nq, qr = row_base + (qi0 + it % nq) * 64;
+        // stage 2 holds K and V until the math warps have moved them to TMEM
+        if (it == 2 && !mbar_wait_warp(kv_moved, 0, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        if (!mbar_wait_warp(&qo_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx_warp(&qo_full[st], L::STAGE);
+        uint8_t* base = sm + st * L::STAGE;
+        tma_tile_warp<HD, 64>(base, &tmQk, &qo_full[st], hq * HD, qr);
+        tma_tile_warp<HD, 64>(base + L::QT, &tmQm, &qo_full[st], hq * HD, qr);
+        tma_tile_warp<HD, 64>(base + 2 * L::QT, &tmOk, &qo_full[st], hq * HD, qr);
+        tma_tile_warp<HD, 64>(base + 3 * L::QT, &tmOm, &qo_full[st], hq * HD, qr);
+        armed[st] = static_cast<int>(ph);
+      }
+      if (!ok) {
+        mbar_drain(kv_full, 0, err);
+        for (int st = 0; st < L::NST; ++st)
+          if (armed[st] >= 0) mbar_drain(&qo_full[st], static_cast<uint32_t>(armed[st]), err);
+      }
+    }
+  } else if (ro.warp == 1) {
+    {  // whole warp: elect.sync issues
+      constexpr uint32_t idesc_s = umma_idesc_tf32(128, 64, false, false);
+      bool ok = mbar_wait_warp(kv_moved, 0, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL);
+      bool issued = false;
+      tc_fence_after();
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int st = it % L::NST, ts = it % L::NSET;
+        const uint32_t base = s0 + st * L::STAGE;
+        if (!mbar_wait_warp(&qo_full[st], (it / L::NST) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        if (!mbar_wait_warp(&set_free[ts], ((it / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk)
+          umma_tf32_ts_warp(tmem + ts * 128, tmem + L::K_COL + kk * 8, kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
+        issued = true;
+        umma_commit_warp(&s_full[ts]);
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk)
+          umma_tf32_ts_warp(tmem + ts * 128 + 64, tmem + L::V_COL + kk * 8, kdesc<64>(base + 2 * L::QT, kk), idesc_s,
+                       kk > 0 ? 1u : 0u);
+        umma_commit_warp(&dp_full[ts]);
+      }
+      if (!ok && issued) {
+        umma_commit_warp(drain);
+        mbar_drain(drain, 0, err);
+      }
+    }
+  } else if (ro.warp == ACC_WARP2) {
+    {  // whole warp: elect.sync issues
+      constexpr uint32_t idesc_a = umma_idesc_tf32(128, HD, false, true);
+      bool ok = true, issued = false;
+      for (int pit = 0; ok && pit < n_it; ++pit) {
+        const int ps = pit % L::NST, pts = pit % L::NSET;
+        const uint32_t base = s0 + ps * L::STAGE;
+        if (!mbar_wait_warp(&p_full[pts], (pit / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_tf32_ts_warp(tmem + L::DV_COL, tmem + pts * 128 + kk * 8, mdesc<64>(base + 3 * L::QT, kk), idesc_a,
+                       (pit > 0 || kk > 0) ? 1u : 0u);
+        issued = true;
+        if (!mbar_wait_warp(&ds_full[pts], (pit / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_tf32_ts_warp(tmem + L::DK_COL, tmem + pts * 128 + 64 + kk * 8, mdesc<64>(base + L::QT, kk), idesc_a,
+                       (pit > 0 || kk > 0) ? 1u : 0u);
+        umma_commit_warp(&set_free[pts]);
+        umma_commit_warp(&qo_empty[ps]);
+      }
+      if (ok) umma_commit_warp(acc_done);
+      if (!ok && issued) {
+        umma_commit_warp(drain_acc);
+        mbar_drain(drain_acc, 0, err);
+      }
+    }
+  } else {
+    const int q = ro.quarter(), hf = ro.half(), grp = ro.group();
+    const int c = q * 32 + ro.lane;  // key row within the tile
+    const int key = k0 + c;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    float* stg = reinterpret_cast<float*>(sm + L::OFF_STG) + (ro.warp - 2) * 64;
+    bool ok = true;
+    // K and V rows -> TMEM (the 2 HD/32 column blocks dealt over the quarter's
+    // four warps), then release stage 2 and start the score issuer
+    if (__all_sync(0xffffffffu, mbar_wait(kv_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
+      tile_rows_to_tmem<HD, 4>(sm + L::OFF_KV, c, lane_addr, L::K_COL, 0, ro.part());
+      tile_rows_to_tmem<HD, 4>(sm + L::OFF_KV + L::K, c, lane_addr, L::V_COL, HD / 32, ro.part());
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(kv_moved);
+    } else {
+      ok = false;
+    }
+    // lse * log2(e) and D * scale of query (lane) of this warp's half of step i
+    float pre_l = 0.f, pre_d = 0.f;
+    auto fetch = [&](int i) {
+      const int hq = h_first + i / nq, qa = (qi0 + i % nq) * 64 + hf * 32 + ro.lane;
+      const size_t ix = (static_cast<size_t>(b) * H + hq) * S + qa;
+      pre_l = qa < S ? lse[ix] * LOG2E : 0.f;
+      pre_d = qa < S ? Dv[ix] * scale : 0.f;
+    };
+    if (grp < n_it) fetch(grp);
+    for (int it = grp; ok && it < n_it; it += 2) {
+      const uint32_t ph = (it >> 1) & 1;
+      const int qbase = (qi0 + it % nq) * 64;
+      __syncwarp();
+      stg[ro.lane] = pre_l;
+      stg[32 + ro.lane] = pre_d;
+      __syncwarp();
+      if (it + 2 < n_it) fetch(it + 2);
+      WAIT_OR_BREAK(&s_full[grp], ph, GLC_DEV_TIMEOUT_EPILOGUE);
+      tc_fence_after();
+      // this warp's 32 queries: S^T columns [hf*32, +32), dP^T columns 64 + [hf*32, +32)
+      const uint32_t sa = lane_addr + grp * 128 + hf * 32;
+      uint32_t sv[32];
+      float pf[32];
+      tmem_ld_32x32b_x32(sa, sv);
+      tmem_ld_wait();
+      const int q_lo = qbase + hf * 32;
+      const bool nomask = q_lo >= k0 + 127 && q_lo + 32 <= S && k0 + 128 <= S;
+      const float4* l4 = reinterpret_cast<const float4*>(stg);
+      if (nomask) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 l = l4[i];
+          pf[4 * i] = fast_exp2(fmaf(__uint_as_float(sv[4 * i]), scale_log2, -l.x));
+          pf[4 * i + 1] = fast_exp2(fmaf(__uint_as_float(sv[4 * i + 1]), scale_log2, -l.y));
+          pf[4 * i + 2] = fast_exp2(fmaf(__uint_as_float(sv[4 * i + 2]), scale_log2, -l.z));
+          pf[4 * i + 3] = fast_exp2(fmaf(__uint_as_float(sv[4 * i + 3]), scale_log2, -l.w));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 l = l4[i];
+          const float lv[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const int e = 4 * i + e4, qa = q_lo + e;
+            const bool valid = qa < S && key < S && key <= qa;
+            pf[e] = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lv[e4])) : 0.f;
+          }
+        }
+      }
+      // P^T to TMEM: dV += P^T dO may start while dS is computed
+#pragma unroll
+      for (int e = 0; e < 32; ++e) sv[e] = tf32_bits(pf[e]);
+      tmem_st_32x32b_x32(sa, sv);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[grp]);
+      WAIT_OR_BREAK(&dp_full[grp], ph, GLC_DEV_TIMEOUT_EPILOGUE);
+      tc_fence_after();
+      tmem_ld_32x32b_x32(sa + 64, sv);
+      tmem_ld_wait();
+      const float4* d4 = reinterpret_cast<const float4*>(stg + 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 d = d4[i];
+        sv[4 * i] = tf32_bits(pf[4 * i] * fmaf(__uint_as_float(sv[4 * i]), scale, -d.x));
+        sv[4 * i + 1] = tf32_bits(pf[4 * i + 1] * fmaf(__uint_as_float(sv[4 * i + 1]), scale, -d.y));
+        sv[4 * i + 2] = tf32_bits(pf[4 * i + 2] * fmaf(__uint_as_float(sv[4 * i + 2]), scale, -d.z));
+        sv[4 * i + 3] = tf32_bits(pf[4 * i + 3] * fmaf(__uint_as_float(sv[4 * i + 3]), scale, -d.w));
+      }
+      tmem_st_32x32b_x32(sa + 64, sv);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&ds_full[grp]);
+    }
+    if (__all_sync(0xffffffffu, ok && mbar_wait(acc_done, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
+      tc_fence_after();
+      // final dk/dv at the KV head's columns, or this CTA's partial: the
+      // quarter's four warps take the 2 HD/32 column blocks of dV then dK
+      const int oh = static_cast<int>(blockIdx.x);
+      const size_t trow = static_cast<size_t>(row_base) + key;
+#pragma unroll 1
+      for (int blk = ro.part(); blk < 2 * (HD / 32); blk += 4) {
+        const int part = blk / (HD / 32), cc = blk % (HD / 32);
         uint32_t v[32];
         tmem_ld_32x32b_x32(lane_addr + (part == 0 ? L::DV_COL : L::DK_COL) + cc * 32, v);
         tmem_ld_wait();
@@ -1609,6 +1915,288 @@ __global__ void __launch_bounds__(NT, 1)
   }
 }
 
+// ====================================================== dQ, persistent, two math groups
+// attn_bwd_dq_persist_kernel with the 608-thread layout of
+// attn_bwd_dkdv2_kernel: math group g takes the K/V steps with (running step
+// count) % 2 == g and owns TMEM S/dP set g.  The group that ran an item's
+// last step moves the next item's Q and dO into TMEM and writes the item's
+// dQ while the other group starts on the next item.  Bit-identical to the
+// one-group kernels.
+template <int HD>
+__global__ void __launch_bounds__(NT2, 1)
+    attn_bwd_dq2_persist_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmO,
+                                const __grid_constant__ CUtensorMap tmKk, const __grid_constant__ CUtensorMap tmKm,
+                                const __grid_constant__ CUtensorMap tmVk, const float* __restrict__ lse,
+                                const float* __restrict__ Dv, float* __restrict__ dq, int dq_ld, int S, int B, int H,
+                                int Hkv, int n_qt, float scale, float scale_log2, const float* __restrict__ rope_cos,
+                                const float* __restrict__ rope_sin, int* err) {
+  GLC_PDL_ENTRY();
+  using L = PDqLayout<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint64_t *qo_full = bars, *qo_moved = bars + 1, *kv_full = bars + 2, *kv_empty = bars + 5, *s_full = bars + 8,
+           *p_full = bars + 10, *set_free = bars + 12, *dq_full = bars + 14, *dq_empty = bars + 16, *drain = bars + 18,
+           *drain_acc = bars + 19, *dp_full = bars + 20;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const Roles2 ro;
+  const int n_items = H * B * n_qt;
+  const int G = H / Hkv;
+  const int n_k64 = (S + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    mbar_init(qo_full, 1);
+    mbar_init(qo_moved, GROUP_THREADS);
+    for (int i = 0; i < L::NST; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < L::NSET; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&dp_full[i], 1);
+      mbar_init(&p_full[i], GROUP_THREADS);
+      mbar_init(&set_free[i], 1);
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_empty[i], GROUP_THREADS);
+    }
+    mbar_init(drain, 1);
+    mbar_init(drain_acc, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (ro.warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t s0 = smem_u32(sm);
+
+  if (ro.warp == 0) {
+    {  // whole warp: elect.sync issues
+      int armed[L::NST] = {-1, -1, -1};
+      int armed_qo = -1;
+      bool ok = true;
+      int kv = 0, local = 0;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
+        const FwdItem w = fwd_item(it, H, B, n_qt);
+        const int kh = w.h / G, q0 = w.qt * 128, row_base = w.b * S;
+        const int nk = min(n_k64, (q0 + 128) / 64);
+        if (local > 0 && !mbar_wait_warp(qo_moved, (local - 1) & 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx_warp(qo_full, L::Q + L::O);
+        tma_tile_warp<HD, 128>(sm + L::OFF_QO, &tmQ, qo_full, w.h * HD, row_base + q0);
+        tma_tile_warp<HD, 128>(sm + L::OFF_QO + L::Q, &tmO, qo_full, w.h * HD, row_base + q0);
+        armed_qo = local & 1;
+        for (int j = 0; j < nk; ++j, ++kv) {
+          const int st = kv % L::NST;
+          const uint32_t ph = (kv / L::NST) & 1;
+          if (!mbar_wait_warp(&kv_empty[st], ph ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+          mbar_arrive_expect_tx_warp(&kv_full[st], L::STAGE);
+          uint8_t* base = sm + st * L::STAGE;
+          tma_tile_warp<HD, 64>(base, &tmKk, &kv_full[st], kh * HD, row_base + j * 64);
+          tma_tile_warp<HD, 64>(base + L::KT, &tmKm, &kv_full[st], kh * HD, row_base + j * 64);
+          tma_tile_warp<HD, 64>(base + 2 * L::KT, &tmVk, &kv_full[st], kh * HD, row_base + j * 64);
+          armed[st] = static_cast<int>(ph);
+        }
+      }
+      if (!ok) {
+        if (armed_qo >= 0) mbar_drain(qo_full, static_cast<uint32_t>(armed_qo), err);
+        for (int st = 0; st < L::NST; ++st)
+          if (armed[st] >= 0) mbar_drain(&kv_full[st], static_cast<uint32_t>(armed[st]), err);
+      }
+    }
+  } else if (ro.warp == 1) {
+    {  // whole warp: elect.sync issues
+      constexpr uint32_t idesc_s = umma_idesc_tf32(128, 64, false, false);
+      bool ok = true, issued = false;
+      int kv = 0, local = 0;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
+        const FwdItem w = fwd_item(it, H, B, n_qt);
+        const int nk = min(n_k64, (w.qt * 128 + 128) / 64);
+        if (!mbar_wait_warp(qo_moved, local & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+        tc_fence_after();
+        for (int j = 0; j < nk; ++j, ++kv) {
+          const int st = kv % L::NST, ts = kv % L::NSET;
+          const uint32_t base = s0 + st * L::STAGE;
+          if (!mbar_wait_warp(&kv_full[st], (kv / L::NST) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          if (!mbar_wait_warp(&set_free[ts], ((kv / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < HD / 8; ++kk)
+            umma_tf32_ts_warp(tmem + ts * 128, tmem + L::Q_COL + kk * 8, kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
+          issued = true;
+          umma_commit_warp(&s_full[ts]);
+#pragma unroll
+          for (int kk = 0; kk < HD / 8; ++kk)
+            umma_tf32_ts_warp(tmem + ts * 128 + 64, tmem + L::O_COL + kk * 8, kdesc<64>(base + 2 * L::KT, kk), idesc_s,
+                         kk > 0 ? 1u : 0u);
+          umma_commit_warp(&dp_full[ts]);
+        }
+      }
+      if (!ok && issued) {
+        umma_commit_warp(drain);
+        mbar_drain(drain, 0, err);
+      }
+    }
+  } else if (ro.warp == ACC_WARP2) {
+    {  // whole warp: elect.sync issues
+      constexpr uint32_t idesc_q = umma_idesc_tf32(128, HD, false, true);
+      bool ok = true, issued = false;
+      int kv = 0, local = 0;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
+        const FwdItem w = fwd_item(it, H, B, n_qt);
+        const int nk = min(n_k64, (w.qt * 128 + 128) / 64);
+        const int ob = local & 1;
+        if (!mbar_wait_warp(&dq_empty[ob], ((local >> 1) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int j = 0; j < nk; ++j, ++kv) {
+          const int ps = kv % L::NST, pts = kv % L::NSET;
+          const uint32_t base = s0 + ps * L::STAGE;
+          if (!mbar_wait_warp(&p_full[pts], (kv / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_tf32_ts_warp(tmem + L::DQ_COL + ob * HD, tmem + pts * 128 + kk * 8, mdesc<64>(base + L::KT, kk), idesc_q,
+                         (j > 0 || kk > 0) ? 1u : 0u);
+          issued = true;
+          umma_commit_warp(&set_free[pts]);
+          umma_commit_warp(&kv_empty[ps]);
+        }
+        if (!ok) break;
+        umma_commit_warp(&dq_full[ob]);
+      }
+      if (!ok && issued) {
+        umma_commit_warp(drain_acc);
+        mbar_drain(drain_acc, 0, err);
+      }
+    }
+  } else {
+    const int q = ro.quarter(), hf = ro.half(), grp = ro.group();
+    const int r = q * 32 + ro.lane;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    bool ok = true;
+    int kv = 0, local = 0;
+    // the first item's Q and dO rows -> TMEM (group 0)
+    if (grp == 0 && static_cast<int>(blockIdx.x) < n_items) {
+      if (__all_sync(0xffffffffu, mbar_wait(qo_full, 0, abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
+        tile_rows_to_tmem<HD>(sm + L::OFF_QO, r, lane_addr, L::Q_COL, 0, hf);
+        tile_rows_to_tmem<HD>(sm + L::OFF_QO + L::Q, r, lane_addr, L::O_COL, HD / 32, hf);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(qo_moved);
+      } else {
+        ok = false;
+      }
+    }
+    for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++local) {
+      const FwdItem w = fwd_item(it, H, B, n_qt);
+      const int q0 = w.qt * 128, row_base = w.b * S, qa = q0 + r;
+      const int nk = min(n_k64, (q0 + 128) / 64);
+      const size_t lrow = (static_cast<size_t>(w.b) * H + w.h) * S + (qa < S ? qa : 0);
+      const float lse2 = lse[lrow] * LOG2E, Dq = Dv[lrow];
+      const float nDs = -Dq * scale;
+      const int kv_first = kv;
+      kv += nk;
+      for (int j = (grp ^ (kv_first & 1)); j < nk; j += 2) {
+        const int kvj = kv_first + j;
+        const uint32_t ph = (kvj >> 1) & 1;
+        WAIT_OR_BREAK(&s_full[grp], ph, GLC_DEV_TIMEOUT_EPILOGUE);
+        tc_fence_after();
+        const uint32_t sa = lane_addr + grp * 128 + hf * 32;
+        uint32_t sv[32];
+        float pf[32];
+        tmem_ld_32x32b_x32(sa, sv);
+        tmem_ld_wait();
+        const int k_lo = j * 64 + hf * 32;
+        if (k_lo + 32 <= q0 + 1 && q0 + 128 <= S) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) pf[e] = fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int key = k_lo + e;
+            const bool valid = qa < S && key < S && key <= qa;
+            pf[e] = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2)) : 0.f;
+          }
+        }
+        WAIT_OR_BREAK(&dp_full[grp], ph, GLC_DEV_TIMEOUT_EPILOGUE);
+        tc_fence_after();
+        tmem_ld_32x32b_x32(sa + 64, sv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) sv[e] = tf32_bits(pf[e] * fmaf(__uint_as_float(sv[e]), scale, nDs));
+        tmem_st_32x32b_x32(sa, sv);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[grp]);
+      }
+      if (!ok) break;
+      // the group that ran the item's last step (so waited for its S and dP
+      // products, which complete after every earlier product of the item)
+      // moves the next item's Q and dO and writes this item's dQ
+      if (((kv - 1) & 1) != grp) continue;
+      if (it + static_cast<int>(gridDim.x) < n_items) {
+        WAIT_OR_BREAK(qo_full, (local + 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+        tile_rows_to_tmem<HD>(sm + L::OFF_QO, r, lane_addr, L::Q_COL, 0, hf);
+        tile_rows_to_tmem<HD>(sm + L::OFF_QO + L::Q, r, lane_addr, L::O_COL, HD / 32, hf);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(qo_moved);
+      }
+      const int ob = local & 1;
+      WAIT_OR_BREAK(&dq_full[ob], (local >> 1) & 1, GLC_DEV_TIMEOUT_EPILOGUE);
+      tc_fence_after();
+      float* drow = dq + (static_cast<size_t>(row_base) + qa) * static_cast<size_t>(dq_ld) + w.h * HD;
+#pragma unroll 1
+      for (int cc = hf; cc < HD / 32; cc += 2) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_addr + L::DQ_COL + ob * HD + cc * 32, v);
+        tmem_ld_wait();
+        if (qa < S && rope_cos) {
+          const float4* cr = reinterpret_cast<const float4*>(rope_cos + static_cast<size_t>(qa) * (HD / 2) + cc * 16);
+          const float4* sr = reinterpret_cast<const float4*>(rope_sin + static_cast<size_t>(qa) * (HD / 2) + cc * 16);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const float4 c4 = cr[g], s4 = sr[g];
+            const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int p = 4 * g + e;
+              const float x0 = __uint_as_float(v[2 * p]), x1 = __uint_as_float(v[2 * p + 1]);
+              v[2 * p] = __float_as_uint(round_tf32(__fadd_rn(__fmul_rn(x0, cs[e]), __fmul_rn(x1, sn[e]))));
+              v[2 * p + 1] = __float_as_uint(round_tf32(__fadd_rn(__fmul_rn(-x0, sn[e]), __fmul_rn(x1, cs[e]))));
+            }
+          }
+        }
+        if (qa < S) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            reinterpret_cast<float4*>(drow + cc * 32)[g] =
+                make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]), __uint_as_float(v[4 * g + 2]),
+                            __uint_as_float(v[4 * g + 3]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&dq_empty[ob]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (ro.warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
 // D[b,h,s] = sum_d dO * O.  HD/4 lanes per (token, head) row, one float4 of
 // each operand per lane, 32/(HD/4) rows per warp, one row group per warp.
 template <int HD>
@@ -1712,12 +2300,16 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
              float* partial, int B, int S, int H, int Hkv, bool round_dv, const float* rope_cos,
              const float* rope_sin, cudaStream_t s) {
   const float *q = io.q, *k = io.k, *v = io.v;
-  static SmemFlags done_g, done_q, done_pq;
+  static SmemFlags done_g, done_g2, done_q, done_pq, done_pq2;
   const bool dq_persist = ctx->attn_dq_variant != 1;  // automatic: persistent
-  int rc = set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD>, DkdvLayout<HD>::BYTES, done_g);
+  const bool dq2 = ctx->attn_dq_variant == 3;
+  const bool dkdv2 = ctx->attn_dkdv_variant == 2;
+  int rc = dkdv2 ? set_smem(ctx, attn_bwd_dkdv2_kernel<HD>, Dkdv2Layout<HD>::BYTES, done_g2)
+                 : set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD>, DkdvLayout<HD>::BYTES, done_g);
   if (!rc)
-    rc = dq_persist ? set_smem(ctx, attn_bwd_dq_persist_kernel<HD>, PDqLayout<HD>::BYTES, done_pq)
-                    : set_smem(ctx, attn_bwd_dq_tc_kernel<HD>, DqLayout<HD>::BYTES, done_q);
+    rc = dq2          ? set_smem(ctx, attn_bwd_dq2_persist_kernel<HD>, PDqLayout<HD>::BYTES, done_pq2)
+         : dq_persist ? set_smem(ctx, attn_bwd_dq_persist_kernel<HD>, PDqLayout<HD>::BYTES, done_pq)
+                      : set_smem(ctx, attn_bwd_dq_tc_kernel<HD>, DqLayout<HD>::BYTES, done_q);
   if (rc) return rc;
   const int T = B * S, G = H / Hkv;
   CUtensorMap tQk64, tQm64, tOk64, tOm64, tK128, tV128, tQ128, tO128, tKk64, tKm64, tVk64;
@@ -1754,9 +2346,14 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     if (ctx->attn_split > 0 && G % ctx->attn_split == 0) nsplit = ctx->attn_split;
   }
   auto launch_dkdv = [&](int ns, float* dk_out, float* dv_out, int dk_ld, int dv_ld, int rnd) {
-    glc::launch_pdl(ctx, attn_bwd_dkdv_tc_kernel<HD>, dim3(Hkv * ns, B, n_kt), NT, DkdvLayout<HD>::BYTES, s,
-                    tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, dk_out, dv_out, dk_ld, dv_ld, ns, S, H, Hkv,
-                    scale, scale * LOG2E, rnd, ctx->d_err);
+    if (dkdv2)
+      glc::launch_pdl(ctx, attn_bwd_dkdv2_kernel<HD>, dim3(Hkv * ns, B, n_kt), NT2, Dkdv2Layout<HD>::BYTES, s,
+                      tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, dk_out, dv_out, dk_ld, dv_ld, ns, S, H, Hkv,
+                      scale, scale * LOG2E, rnd, ctx->d_err);
+    else
+      glc::launch_pdl(ctx, attn_bwd_dkdv_tc_kernel<HD>, dim3(Hkv * ns, B, n_kt), NT, DkdvLayout<HD>::BYTES, s,
+                      tQk64, tQm64, tOk64, tOm64, tK128, tV128, lse, D, dk_out, dv_out, dk_ld, dv_ld, ns, S, H, Hkv,
+                      scale, scale * LOG2E, rnd, ctx->d_err);
   };
   if (nsplit == 1) {
     launch_dkdv(1, io.dk, io.dv, io.dk_ld, io.dv_ld, round_dv ? 1 : 0);
@@ -1780,9 +2377,14 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
     const long long items = static_cast<long long>(H) * B * n_qt;
     if (items >= (1LL << 31)) return ctx->fail(GLC_ERR_INVALID, "attention_bwd: too many work items");
     const int grid = static_cast<int>(items < ctx->num_sms ? items : ctx->num_sms);
-    glc::launch_pdl(ctx, attn_bwd_dq_persist_kernel<HD>, grid, NT, PDqLayout<HD>::BYTES, s,
-                    tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, B, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,
-                    rope_sin, ctx->d_err);
+    if (dq2)
+      glc::launch_pdl(ctx, attn_bwd_dq2_persist_kernel<HD>, grid, NT2, PDqLayout<HD>::BYTES, s,
+                      tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, B, H, Hkv, n_qt, scale, scale * LOG2E,
+                      rope_cos, rope_sin, ctx->d_err);
+    else
+      glc::launch_pdl(ctx, attn_bwd_dq_persist_kernel<HD>, grid, NT, PDqLayout<HD>::BYTES, s,
+                      tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, B, H, Hkv, n_qt, scale, scale * LOG2E,
+                      rope_cos, rope_sin, ctx->d_err);
   } else {
     glc::launch_pdl(ctx, attn_bwd_dq_tc_kernel<HD>, dim3(H, B, n_qt), NT, DqLayout<HD>::BYTES, s,
                     tQ128, tO128, tKk64, tKm64, tVk64, lse, D, io.dq, io.dq_ld, S, H, Hkv, n_qt, scale, scale * LOG2E, rope_cos,

@@ -315,8 +315,16 @@ int glc_set_gemm_schedule(glc_ctx* ctx, int mode) {
 int glc_set_attention_dq_variant(glc_ctx* ctx, int variant) {
   if (!ctx) return GLC_ERR_INVALID;
   Context* c = C_(ctx);
-  if (variant < 0 || variant > 2) return c->fail(GLC_ERR_INVALID, "set_attention_dq_variant: variant must be 0, 1 or 2");
+  if (variant < 0 || variant > 3) return c->fail(GLC_ERR_INVALID, "set_attention_dq_variant: variant must be 0 to 3");
   c->attn_dq_variant = variant;
+  return GLC_OK;
+}
+
+int glc_set_attention_dkdv_variant(glc_ctx* ctx, int variant) {
+  if (!ctx) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  if (variant < 0 || variant > 2) return c->fail(GLC_ERR_INVALID, "set_attention_dkdv_variant: variant must be 0, 1 or 2");
+  c->attn_dkdv_variant = variant;
   return GLC_OK;
 }
 

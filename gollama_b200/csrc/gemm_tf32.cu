@@ -574,7 +574,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
-    if (rank == 0 && lane == 0) {
+    if (rank == 0) {  // the leader's whole warp; elect.sync issues
       const uint32_t empty_own = mapa_cluster(empty_bar, 0), empty_peer = mapa_cluster(empty_bar, 1);
       const uint32_t tfull_own = mapa_cluster(tfull_bar, 0), tfull_peer = mapa_cluster(tfull_bar, 1);
       int stage = 0;
@@ -590,7 +590,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
           if (it >= it1) break;
           tile = sched_tile(args, nclusters, it);
         } else {
-          tile = consume(local, false);
+          tile = consume(local, true);
           if (tile == -2) {
             ok = false;
             break;
@@ -602,14 +602,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
         const uint32_t idesc = umma_idesc_tf32(PAIR_BM, BN, p.a_mn != 0, p.b_mn != 0);
         const int buf = local & 1;
         const uint32_t use = static_cast<uint32_t>(local >> 1);
-        if (!mbar_wait(&tempty_bar[buf], (use & 1) ^ 1, abort_flag, args.err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
+        if (!mbar_wait_warp(&tempty_bar[buf], (use & 1) ^ 1, abort_flag, args.err, GLC_DEV_TIMEOUT_MMA_TMEM)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + buf * BN;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag, args.err, GLC_DEV_TIMEOUT_MMA_FULL)) {
+          if (!mbar_wait_warp(&full_bar[stage], phase, abort_flag, args.err, GLC_DEV_TIMEOUT_MMA_FULL)) {
             ok = false;
             break;
           }
@@ -618,21 +618,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
           const uint32_t sB = sA + P_A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-            umma_tf32_pair(tmem_d, operand_desc(p.a_mn, sA, kk), operand_desc(p.b_mn, sB, kk), idesc,
+            umma_tf32_pair_warp(tmem_d, operand_desc(p.a_mn, sA, kk), operand_desc(p.b_mn, sB, kk), idesc,
                            (kb > 0 || kk > 0) ? 1u : 0u);
           }
           issued_any = true;
           // stage s is free in both CTAs once these MMAs have read it
-          umma_commit_pair(empty_own + stage * 8);
-          umma_commit_pair(empty_peer + stage * 8);
+          umma_commit_pair_warp(empty_own + stage * 8);
+          umma_commit_pair_warp(empty_peer + stage * 8);
           if (++stage == P_STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        umma_commit_pair(tfull_own + buf * 8);
-        umma_commit_pair(tfull_peer + buf * 8);
+        umma_commit_pair_warp(tfull_own + buf * 8);
+        umma_commit_pair_warp(tfull_peer + buf * 8);
       }
       if (!ok) {
         // Abort path.  (1) No MMA may still read shared memory or write TMEM
@@ -640,7 +640,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NUM_THREADS, 1)
         // for stages not yet consumed signal this CTA's full barriers: wait
         // for them (each wait bounded) so none lands after exit.
         if (issued_any) {
-          umma_commit_pair(mapa_cluster(drain_bar, 0));
+          umma_commit_pair_warp(mapa_cluster(drain_bar, 0));
           mbar_drain(drain_bar, 0, args.err);
         }
         for (int i = 0; i < P_STAGES; ++i) {

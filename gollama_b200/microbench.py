@@ -252,8 +252,11 @@ def main(argv=None):
                     help="RMSNorm backward: 0 automatic, 1 row by row, 2 cp.async-pipelined rows, 3 bulk-copied rows")
     ap.add_argument("--attn-fwd-variant", type=int, default=0, choices=[0, 1, 2],
                     help="attention forward: 0 automatic, 1 a CTA per query tile, 2 persistent CTAs")
-    ap.add_argument("--attn-dq-variant", type=int, default=0, choices=[0, 1, 2],
-                    help="attention backward dQ: 0 automatic, 1 a CTA per query tile, 2 persistent CTAs")
+    ap.add_argument("--attn-dq-variant", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="attention backward dQ: 0 automatic, 1 a CTA per query tile, 2 persistent CTAs, "
+                         "3 persistent with two groups of softmax warps")
+    ap.add_argument("--attn-dkdv-variant", type=int, default=0, choices=[0, 1, 2],
+                    help="attention backward dK/dV: 0 automatic, 1 one group of softmax warps, 2 two groups")
     ap.add_argument("--pdl", type=int, default=0, choices=[0, 1],
                     help="programmatic dependent launch between the library's kernels")
     ap.add_argument("--gemm-schedule", type=int, default=0, choices=[0, 1, 2],
@@ -271,6 +274,7 @@ def main(argv=None):
         ctx.call("glc_set_pdl", a.pdl)
         ctx.call("glc_set_attention_fwd_variant", a.attn_fwd_variant)
         ctx.call("glc_set_attention_dq_variant", a.attn_dq_variant)
+        ctx.call("glc_set_attention_dkdv_variant", a.attn_dkdv_variant)
         for n in names:
             res = CASES[n](ctx, a.iters, a.warmup)
             for desc, ms, rate, unit in (res if isinstance(res, list) else [res]):

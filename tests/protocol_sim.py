@@ -61,6 +61,22 @@ def _drive(roles, events, rnd, cap=2_000_000):
     raise AssertionError("deadlock")
 
 
+def _in_order(q, fn, ev):
+    """A tcgen05.commit of an issuing thread: it arrives once every MMA that
+    thread issued before it has completed, so one thread's commits fire in
+    issue order (an event that comes up early is put back)."""
+    seq = q["issued"]
+    q["issued"] += 1
+
+    def fire():
+        if q["fired"] != seq:
+            ev.append(fire)
+            return
+        q["fired"] += 1
+        fn()
+    return fire
+
+
 def forward(H, B, n_qt, grid, cta, seed):
     rnd = random.Random(seed)
     items = list(range(cta, H * B * n_qt, grid))
@@ -161,7 +177,10 @@ def forward(H, B, n_qt, grid, cta, seed):
     _drive({"tma": tma(), "smma": smma(), "acc": acc(), "math": math()}, ev, rnd)
 
 
-def dq(H, B, n_qt, S, grid, cta, seed):
+def dq(H, B, n_qt, S, grid, cta, seed, groups=1):
+    """attn_bwd_dq_persist_kernel (groups=1) or attn_bwd_dq2_persist_kernel
+    (groups=2: math group g takes the steps with kv % 2 == g; the group that
+    ran an item's last step moves the next item's Q/dO and reads out dQ)."""
     rnd = random.Random(seed)
     items = list(range(cta, H * B * n_qt, grid))
     n_k64 = (S + 63) // 64
@@ -172,6 +191,7 @@ def dq(H, B, n_qt, S, grid, cta, seed):
             for i in range(k)}
     b = lambda n, i=0: bars[(n, i)]
     ev = []
+    commits = {"issued": 0, "fired": 0}
     st = {"tmem_qo": None, "staging": None, "s": set(), "dp": set(), "dq": set(), "epi": set(), "buf": [None, None]}
 
     def tma():
@@ -207,17 +227,11 @@ def dq(H, B, n_qt, S, grid, cta, seed):
                     st["s"].add(kv)
                     b("s_full", ts).arrive()
 
-                def make_dp_done(ts, kv):
-                    def dp_done():
-                        # a commit arrives once every earlier MMA of its thread completed
-                        if kv not in st["s"]:
-                            ev.append(dp_done)
-                            return
-                        st["dp"].add(kv)
-                        b("dp_full", ts).arrive()
-                    return dp_done
-                ev.append(s_done)
-                ev.append(make_dp_done(ts, kv))
+                def dp_done(ts=ts, kv=kv):
+                    st["dp"].add(kv)
+                    b("dp_full", ts).arrive()
+                ev.append(_in_order(commits, s_done, ev))
+                ev.append(_in_order(commits, dp_done, ev))
                 kv += 1
 
     def acc():
@@ -239,9 +253,9 @@ def dq(H, B, n_qt, S, grid, cta, seed):
                 kv += 1
             ev.append(lambda ob=ob: b("dq_full", ob).arrive())
 
-    def math():
+    def math(g=0):
         kv = 0
-        if items:
+        if items and g == 0:
             yield from _wait(b("qo_full"), 0, 0)
             assert st["staging"] == 0
             st["tmem_qo"] = 0
@@ -249,12 +263,17 @@ def dq(H, B, n_qt, S, grid, cta, seed):
         for local, it in enumerate(items):
             for _ in range(nk_of(it)):
                 ts = kv % 2
+                if groups == 2 and ts != g:
+                    kv += 1
+                    continue
                 yield from _wait(b("s_full", ts), (kv // 2) & 1, kv // 2)
                 assert kv in st["s"]
                 yield from _wait(b("dp_full", ts), (kv // 2) & 1, kv // 2)
                 assert kv in st["dp"]
                 b("p_full", ts).arrive()
                 kv += 1
+            if groups == 2 and (kv - 1) % 2 != g:
+                continue  # the other group ran the item's last step
             if local + 1 < len(items):
                 yield from _wait(b("qo_full"), (local + 1) & 1, local + 1)
                 # Q and dO in TMEM are overwritten: every S and dP product of this item has completed
@@ -267,20 +286,24 @@ def dq(H, B, n_qt, S, grid, cta, seed):
             st["epi"].add(local)
             b("dq_empty", ob).arrive()
 
-    _drive({"tma": tma(), "smma": smma(), "acc": acc(), "math": math()}, ev, rnd)
+    maths = {f"math{g}": math(g) for g in range(groups)}
+    _drive({"tma": tma(), "smma": smma(), "acc": acc(), **maths}, ev, rnd)
 
 
-def dkdv(n_heads, nq, seed):
+def dkdv(n_heads, nq, seed, groups=1):
     """attn_bwd_dkdv_tc_kernel's protocol for one CTA: n_heads * nq steps of
     64 queries, three Q/dO stages (K and V land in the third and are copied
     to TMEM first), two TMEM sets, each step committed in halves (S^T then
-    dP^T by the score issuer; P^T then dS^T by the math warps)."""
+    dP^T by the score issuer; P^T then dS^T by the math warps).  groups=2:
+    attn_bwd_dkdv2_kernel, math group g takes the steps with it % 2 == g, both
+    groups copy K and V, no lse/D staging barrier."""
     rnd = random.Random(seed)
     n_it = n_heads * nq
-    bars = {(n, i): Bar(f"{n}{i}", 1) for n, k in [("kv_full", 1), ("kv_moved", 1), ("qo_full", 3), ("qo_empty", 3),
+    bars = {(n, i): Bar(f"{n}{i}", 1) for n, k in [("kv_full", 1), ("qo_full", 3), ("qo_empty", 3),
                                                        ("s_full", 2), ("dp_full", 2), ("p_full", 2), ("ds_full", 2),
                                                        ("set_free", 2), ("acc_done", 1), ("ld_ready", 2)]
             for i in range(k)}
+    bars[("kv_moved", 0)] = Bar("kv_moved", groups)
     b = lambda n, i=0: bars[(n, i)]
     ev = []
     st = {"kv_in_stage2": False, "stage": [None] * 3, "S": set(), "dP": set(), "P": set(), "dS": set(),
@@ -349,14 +372,15 @@ def dkdv(n_heads, nq, seed):
             b("acc_done").arrive()
         ev.append(fin)
 
-    def math():
+    def math(g=0):
         yield from _wait(b("kv_full"), 0, 0)
         assert st["kv_in_stage2"]
         b("kv_moved").arrive()
-        for it in range(n_it):
+        for it in range(g, n_it, groups):
             ts = it % 2
-            b("ld_ready", it & 1).arrive()
-            yield from _wait(b("ld_ready", it & 1), (it >> 1) & 1, it >> 1)
+            if groups == 1:
+                b("ld_ready", it & 1).arrive()
+                yield from _wait(b("ld_ready", it & 1), (it >> 1) & 1, it >> 1)
             yield from _wait(b("s_full", ts), (it // 2) & 1, it // 2)
             assert it in st["S"]
             st["P"].add(it)
@@ -368,4 +392,5 @@ def dkdv(n_heads, nq, seed):
         yield from _wait(b("acc_done"), 0, 0)
         assert st["acc_done"] and len(st["dk"]) == n_it
 
-    _drive({"tma": tma(), "smma": smma(), "acc": acc(), "math": math()}, ev, rnd)
+    maths = {f"math{g}": math(g) for g in range(groups)}
+    _drive({"tma": tma(), "smma": smma(), "acc": acc(), **maths}, ev, rnd)

@@ -17,14 +17,15 @@ def test_forward_protocol(seed):
         sim.forward(H, B, n_qt, grid, cta, seed * 131 + cta)
 
 
+@pytest.mark.parametrize("groups", [1, 2])
 @pytest.mark.parametrize("seed", range(40))
-def test_dq_protocol(seed):
+def test_dq_protocol(seed, groups):
     r = random.Random(seed)
     H, B, n_qt = r.randint(1, 4), r.randint(1, 3), r.randint(1, 5)
     S = r.randint((n_qt - 1) * 128 + 1, n_qt * 128)
     grid = r.randint(1, H * B * n_qt)
     for cta in range(grid):
-        sim.dq(H, B, n_qt, S, grid, cta, seed * 7919 + cta)
+        sim.dq(H, B, n_qt, S, grid, cta, seed * 7919 + cta, groups)
 
 
 def test_simulator_catches_a_wrong_parity():
@@ -38,7 +39,8 @@ def test_simulator_catches_a_wrong_parity():
     assert next(w, "blocked") is None
 
 
+@pytest.mark.parametrize("groups", [1, 2])
 @pytest.mark.parametrize("seed", range(40))
-def test_dkdv_protocol(seed):
+def test_dkdv_protocol(seed, groups):
     r = random.Random(seed)
-    sim.dkdv(r.randint(1, 4), r.randint(1, 16), seed)
+    sim.dkdv(r.randint(1, 4), r.randint(1, 16), seed, groups)

@@ -268,7 +268,7 @@ def test_attention_fwd_persistent_bit_identical(ctx, B, S, H, Hkv, hd):
 @pytest.mark.parametrize("B,S,H,Hkv,hd", [(1, 128, 2, 1, 64), (2, 300, 4, 2, 64), (4, 1024, 32, 4, 64),
                                           (3, 257, 3, 3, 32)])
 def test_attention_dq_persistent_bit_identical(ctx, B, S, H, Hkv, hd):
-    """glc_set_attention_dq_variant(2): dQ bit for bit as the grid kernel's
+    """glc_set_attention_dq_variant(2) and (3): dQ bit for bit as the grid kernel's
     (dK and dV come from the unchanged kernel)."""
     T = B * S
     r = rng(T + 2 * H + hd)
@@ -281,7 +281,7 @@ def test_attention_dq_persistent_bit_identical(ctx, B, S, H, Hkv, hd):
     ctx.call("glc_attention_fwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, B, S, H, Hkv, hd, 0)
     outs = []
     try:
-        for variant in (1, 2):
+        for variant in (1, 2, 3):
             ctx.call("glc_set_attention_dq_variant", variant)
             bdq, bdk, bdv = ctx.empty(q.shape), ctx.empty(k.shape), ctx.empty(v.shape)
             ctx.call("glc_attention_bwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, bdq.ptr, bdk.ptr, bdv.ptr,
@@ -290,6 +290,40 @@ def test_attention_dq_persistent_bit_identical(ctx, B, S, H, Hkv, hd):
             outs.append([a.numpy().view(np.uint32) for a in (bdq, bdk, bdv)])
     finally:
         ctx.call("glc_set_attention_dq_variant", 0)
+    for other in outs[1:]:
+        for a, b_ in zip(outs[0], other):
+            assert np.array_equal(a, b_)
+
+
+@pytest.mark.parametrize("B,S,H,Hkv,hd,split", [(1, 128, 2, 1, 64, 0), (2, 300, 4, 2, 64, 0), (4, 1024, 32, 4, 64, 0),
+                                                (4, 1024, 32, 4, 64, 1), (3, 257, 3, 3, 32, 0), (1, 64, 2, 2, 64, 0),
+                                                (2, 200, 8, 2, 32, 4)])
+def test_attention_dkdv_two_groups_bit_identical(ctx, B, S, H, Hkv, hd, split):
+    """glc_set_attention_dkdv_variant(2): dK and dV bit for bit as the
+    one-group kernel's, for every split of the query-head group (split 0:
+    automatic) and a single-step CTA (S = 64: the second group idles)."""
+    T = B * S
+    r = rng(T + 3 * H + hd + split)
+    q = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
+    k = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    v = tf32(r.standard_normal((T, Hkv * hd), dtype=np.float32))
+    dO = tf32(r.standard_normal((T, H * hd), dtype=np.float32))
+    bq, bk, bv, bdo = ctx.from_numpy(q), ctx.from_numpy(k), ctx.from_numpy(v), ctx.from_numpy(dO)
+    bo, blse = ctx.empty((T, H * hd)), ctx.empty((B, H, S))
+    ctx.call("glc_attention_fwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, B, S, H, Hkv, hd, 0)
+    outs = []
+    try:
+        ctx.call("glc_set_attention_split", split)
+        for variant in (1, 2):
+            ctx.call("glc_set_attention_dkdv_variant", variant)
+            bdq, bdk, bdv = ctx.empty(q.shape), ctx.empty(k.shape), ctx.empty(v.shape)
+            ctx.call("glc_attention_bwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, bdq.ptr, bdk.ptr, bdv.ptr,
+                     B, S, H, Hkv, hd, 0)
+            ctx.sync()
+            outs.append([a.numpy().view(np.uint32) for a in (bdq, bdk, bdv)])
+    finally:
+        ctx.call("glc_set_attention_dkdv_variant", 0)
+        ctx.call("glc_set_attention_split", 0)
     for a, b_ in zip(*outs):
         assert np.array_equal(a, b_)
 

@@ -237,7 +237,8 @@ def test_programmatic_dependent_launch_step_bit_identical(ctx, shape):
     assert np.array_equal(w0.view(np.uint32), w1.view(np.uint32))
 
 
-VARIANTS = ["glc_set_attention_fwd_variant", "glc_set_attention_dq_variant", "glc_set_rmsnorm_variant",
+VARIANTS = ["glc_set_attention_fwd_variant", "glc_set_attention_dq_variant", "glc_set_attention_dkdv_variant",
+            "glc_set_rmsnorm_variant",
             "glc_set_gemm_schedule"]
 
 
