@@ -1070,10 +1070,13 @@ __global__ void __launch_bounds__(NT2, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  // The two halves of a TMEM set are released separately: s_free once dV
+  // has read P^T (S^T of the step after next may then be written),
+  // dp_free once dK has read dS^T.
   uint64_t *kv_full = bars, *qo_full = bars + 1, *qo_empty = bars + 4, *s_full = bars + 7, *p_full = bars + 9,
-           *set_free = bars + 11, *acc_done = bars + 13, *drain = bars + 14, *kv_moved = bars + 15,
-           *drain_acc = bars + 16, *dp_full = bars + 17, *ds_full = bars + 19;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
+           *dp_free = bars + 11, *acc_done = bars + 13, *drain = bars + 14, *kv_moved = bars + 15,
+           *drain_acc = bars + 16, *dp_full = bars + 17, *ds_full = bars + 19, *s_free = bars + 21;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const Roles2 ro;
   const int G = H / Hkv;
@@ -1098,7 +1101,8 @@ __global__ void __launch_bounds__(NT2, 1)
       mbar_init(&dp_full[i], 1);
       mbar_init(&p_full[i], GROUP_THREADS);
       mbar_init(&ds_full[i], GROUP_THREADS);
-      mbar_init(&set_free[i], 1);
+      mbar_init(&s_free[i], 1);
+      mbar_init(&dp_free[i], 1);
     }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
@@ -1151,13 +1155,15 @@ __global__ void __launch_bounds__(NT2, 1)
         const int st = it % L::NST, ts = it % L::NSET;
         const uint32_t base = s0 + st * L::STAGE;
         if (!mbar_wait_warp(&qo_full[st], (it / L::NST) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
-        if (!mbar_wait_warp(&set_free[ts], ((it / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
+        if (!mbar_wait_warp(&s_free[ts], ((it / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk)
           umma_tf32_ts_warp(tmem + ts * 128, tmem + L::K_COL + kk * 8, kdesc<64>(base, kk), idesc_s, kk > 0 ? 1u : 0u);
         issued = true;
         umma_commit_warp(&s_full[ts]);
+        if (!mbar_wait_warp(&dp_free[ts], ((it / L::NSET) & 1) ^ 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_TMEM)) { ok = false; break; }
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk)
           umma_tf32_ts_warp(tmem + ts * 128 + 64, tmem + L::V_COL + kk * 8, kdesc<64>(base + 2 * L::QT, kk), idesc_s,
@@ -1183,13 +1189,14 @@ __global__ void __launch_bounds__(NT2, 1)
           umma_tf32_ts_warp(tmem + L::DV_COL, tmem + pts * 128 + kk * 8, mdesc<64>(base + 3 * L::QT, kk), idesc_a,
                        (pit > 0 || kk > 0) ? 1u : 0u);
         issued = true;
+        umma_commit_warp(&s_free[pts]);
         if (!mbar_wait_warp(&ds_full[pts], (pit / L::NSET) & 1, abort_flag, err, GLC_DEV_TIMEOUT_MMA_FULL)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           umma_tf32_ts_warp(tmem + L::DK_COL, tmem + pts * 128 + 64 + kk * 8, mdesc<64>(base + L::QT, kk), idesc_a,
                        (pit > 0 || kk > 0) ? 1u : 0u);
-        umma_commit_warp(&set_free[pts]);
+        umma_commit_warp(&dp_free[pts]);
         umma_commit_warp(&qo_empty[ps]);
       }
       if (ok) umma_commit_warp(acc_done);

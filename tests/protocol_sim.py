@@ -296,16 +296,19 @@ def dkdv(n_heads, nq, seed, groups=1):
     to TMEM first), two TMEM sets, each step committed in halves (S^T then
     dP^T by the score issuer; P^T then dS^T by the math warps).  groups=2:
     attn_bwd_dkdv2_kernel, math group g takes the steps with it % 2 == g, both
-    groups copy K and V, no lse/D staging barrier."""
+    groups copy K and V, no lse/D staging barrier, and the halves of a TMEM
+    set are released separately (s_free after dV, dp_free after dK)."""
     rnd = random.Random(seed)
     n_it = n_heads * nq
     bars = {(n, i): Bar(f"{n}{i}", 1) for n, k in [("kv_full", 1), ("qo_full", 3), ("qo_empty", 3),
                                                        ("s_full", 2), ("dp_full", 2), ("p_full", 2), ("ds_full", 2),
-                                                       ("set_free", 2), ("acc_done", 1), ("ld_ready", 2)]
+                                                       ("set_free", 2), ("s_free", 2), ("dp_free", 2),
+                                                       ("acc_done", 1), ("ld_ready", 2)]
             for i in range(k)}
     bars[("kv_moved", 0)] = Bar("kv_moved", groups)
     b = lambda n, i=0: bars[(n, i)]
     ev = []
+    smma_q, acc_q = {"issued": 0, "fired": 0}, {"issued": 0, "fired": 0}
     st = {"kv_in_stage2": False, "stage": [None] * 3, "S": set(), "dP": set(), "P": set(), "dS": set(),
           "dv": set(), "dk": set(), "acc_done": False}
 
@@ -334,8 +337,6 @@ def dkdv(n_heads, nq, seed, groups=1):
         for it in range(n_it):
             s_, ts = it % 3, it % 2
             yield from _wait(b("qo_full", s_), (it // 3) & 1, it // 3)
-            yield from _wait(b("set_free", ts), ((it // 2) & 1) ^ 1, it // 2 - 1)
-            assert st["stage"][s_] == it and (it < 2 or (it - 2) in st["dk"])
 
             def s_done(ts=ts, it=it):
                 st["S"].add(it)
@@ -344,24 +345,40 @@ def dkdv(n_heads, nq, seed, groups=1):
             def dp_done(ts=ts, it=it):
                 st["dP"].add(it)
                 b("dp_full", ts).arrive()
-            ev.append(s_done)
-            ev.append(dp_done)
+            if groups == 1:
+                yield from _wait(b("set_free", ts), ((it // 2) & 1) ^ 1, it // 2 - 1)
+                assert st["stage"][s_] == it and (it < 2 or (it - 2) in st["dk"])
+                ev.append(s_done)
+                ev.append(dp_done)
+            else:
+                # S^T overwrites P^T of step it - 2: dV must have read it
+                yield from _wait(b("s_free", ts), ((it // 2) & 1) ^ 1, it // 2 - 1)
+                assert st["stage"][s_] == it and (it < 2 or (it - 2) in st["dv"])
+                ev.append(_in_order(smma_q, s_done, ev))
+                # dP^T overwrites dS^T of step it - 2: dK must have read it
+                yield from _wait(b("dp_free", ts), ((it // 2) & 1) ^ 1, it // 2 - 1)
+                assert it < 2 or (it - 2) in st["dk"]
+                ev.append(_in_order(smma_q, dp_done, ev))
 
     def acc():
         for it in range(n_it):
             s_, ts = it % 3, it % 2
             yield from _wait(b("p_full", ts), (it // 2) & 1, it // 2)
             assert it in st["P"] and st["stage"][s_] == it
-            ev.append(lambda it=it: st["dv"].add(it))
+
+            def dv_done(ts=ts, it=it):
+                st["dv"].add(it)
+                if groups == 2:
+                    b("s_free", ts).arrive()
+            ev.append(_in_order(acc_q, dv_done, ev))
             yield from _wait(b("ds_full", ts), (it // 2) & 1, it // 2)
             assert it in st["dS"]
 
             def done(ts=ts, s_=s_, it=it):
                 st["dk"].add(it)
-                st["dv"].add(it)
-                b("set_free", ts).arrive()
+                b("set_free" if groups == 1 else "dp_free", ts).arrive()
                 b("qo_empty", s_).arrive()
-            ev.append(done)
+            ev.append(_in_order(acc_q, done, ev))
 
         def fin():
             # a commit arrives once every earlier MMA of its thread completed
