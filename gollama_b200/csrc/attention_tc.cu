@@ -98,6 +98,34 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // Round-to-nearest TF32 (ties away from zero) of a finite value with integer
 // ops on the full-rate ALU; equal to cvt.rna.tf32.f32 for finite inputs.
 __device__ __forceinline__ uint32_t tf32_bits(float x) { return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u; }
+// The same rounding for a value that only ever feeds a kind::tf32 MMA, which
+// reads the upper 19 bits of each 32-bit operand and ignores the rest: the
+// carry of the add does the rounding, the mask is not needed.
+__device__ __forceinline__ uint32_t tf32_operand_bits(float x) { return __float_as_uint(x) + 0x1000u; }
+
+// Two fp32 FMAs / products in one sm_100 f32x2 instruction (each element
+// rounded as fmaf / __fmul_rn would): halves the FP instructions of the
+// softmax and dS arithmetic.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, float c, float d) {
   asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
@@ -1210,6 +1238,8 @@ __global__ void __launch_bounds__(NT2, 1)
     const int c = q * 32 + ro.lane;  // key row within the tile
     const int key = k0 + c;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    // [-lse * log2(e) | -D * scale] of this warp's 32 queries (negated: the
+    // addends of the FMAs below)
     float* stg = reinterpret_cast<float*>(sm + L::OFF_STG) + (ro.warp - 2) * 64;
     bool ok = true;
     // K and V rows -> TMEM (the 2 HD/32 column blocks dealt over the quarter's
@@ -1223,23 +1253,38 @@ __global__ void __launch_bounds__(NT2, 1)
     } else {
       ok = false;
     }
-    // lse * log2(e) and D * scale of query (lane) of this warp's half of step i
+    // lse * log2(e) and D * scale of query (lane) of this warp's half of a
+    // step.  Step i is query tile qi0 + i % nq of head h_first + i / nq: the
+    // group walks every second step, so (head, tile) advance by two tiles per
+    // step without a division.
     float pre_l = 0.f, pre_d = 0.f;
-    auto fetch = [&](int i) {
-      const int hq = h_first + i / nq, qa = (qi0 + i % nq) * 64 + hf * 32 + ro.lane;
+    int cur_h = grp / nq, cur_t = grp % nq;  // the step being computed
+    int nxt_h = cur_h, nxt_t = cur_t;        // the step being fetched
+    auto advance = [&](int& hh, int& tt) {
+      tt += 2;
+      while (tt >= nq) {
+        tt -= nq;
+        ++hh;
+      }
+    };
+    auto fetch = [&]() {
+      const int hq = h_first + nxt_h, qa = (qi0 + nxt_t) * 64 + hf * 32 + ro.lane;
       const size_t ix = (static_cast<size_t>(b) * H + hq) * S + qa;
       pre_l = qa < S ? lse[ix] * LOG2E : 0.f;
       pre_d = qa < S ? Dv[ix] * scale : 0.f;
     };
-    if (grp < n_it) fetch(grp);
-    for (int it = grp; ok && it < n_it; it += 2) {
+    if (grp < n_it) fetch();
+    for (int it = grp; ok && it < n_it; it += 2, advance(cur_h, cur_t)) {
       const uint32_t ph = (it >> 1) & 1;
-      const int qbase = (qi0 + it % nq) * 64;
+      const int qbase = (qi0 + cur_t) * 64;
       __syncwarp();
-      stg[ro.lane] = pre_l;
-      stg[32 + ro.lane] = pre_d;
+      stg[ro.lane] = -pre_l;
+      stg[32 + ro.lane] = -pre_d;
       __syncwarp();
-      if (it + 2 < n_it) fetch(it + 2);
+      if (it + 2 < n_it) {
+        advance(nxt_h, nxt_t);
+        fetch();
+      }
       WAIT_OR_BREAK(&s_full[grp], ph, GLC_DEV_TIMEOUT_EPILOGUE);
       tc_fence_after();
       // this warp's 32 queries: S^T columns [hf*32, +32), dP^T columns 64 + [hf*32, +32)
@@ -1252,13 +1297,18 @@ __global__ void __launch_bounds__(NT2, 1)
       const bool nomask = q_lo >= k0 + 127 && q_lo + 32 <= S && k0 + 128 <= S;
       const float4* l4 = reinterpret_cast<const float4*>(stg);
       if (nomask) {
+        const float2 k2 = make_float2(scale_log2, scale_log2);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float4 l = l4[i];
-          pf[4 * i] = fast_exp2(fmaf(__uint_as_float(sv[4 * i]), scale_log2, -l.x));
-          pf[4 * i + 1] = fast_exp2(fmaf(__uint_as_float(sv[4 * i + 1]), scale_log2, -l.y));
-          pf[4 * i + 2] = fast_exp2(fmaf(__uint_as_float(sv[4 * i + 2]), scale_log2, -l.z));
-          pf[4 * i + 3] = fast_exp2(fmaf(__uint_as_float(sv[4 * i + 3]), scale_log2, -l.w));
+          const float2 x0 = fma2(make_float2(__uint_as_float(sv[4 * i]), __uint_as_float(sv[4 * i + 1])), k2,
+                                 make_float2(l.x, l.y));
+          const float2 x1 = fma2(make_float2(__uint_as_float(sv[4 * i + 2]), __uint_as_float(sv[4 * i + 3])), k2,
+                                 make_float2(l.z, l.w));
+          pf[4 * i] = fast_exp2(x0.x);
+          pf[4 * i + 1] = fast_exp2(x0.y);
+          pf[4 * i + 2] = fast_exp2(x1.x);
+          pf[4 * i + 3] = fast_exp2(x1.y);
         }
       } else {
 #pragma unroll
@@ -1269,13 +1319,13 @@ __global__ void __launch_bounds__(NT2, 1)
           for (int e4 = 0; e4 < 4; ++e4) {
             const int e = 4 * i + e4, qa = q_lo + e;
             const bool valid = qa < S && key < S && key <= qa;
-            pf[e] = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lv[e4])) : 0.f;
+            pf[e] = valid ? fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, lv[e4])) : 0.f;
           }
         }
       }
       // P^T to TMEM: dV += P^T dO may start while dS is computed
 #pragma unroll
-      for (int e = 0; e < 32; ++e) sv[e] = tf32_bits(pf[e]);
+      for (int e = 0; e < 32; ++e) sv[e] = tf32_operand_bits(pf[e]);
       tmem_st_32x32b_x32(sa, sv);
       tmem_st_wait();
       tc_fence_before();
@@ -1285,13 +1335,20 @@ __global__ void __launch_bounds__(NT2, 1)
       tmem_ld_32x32b_x32(sa + 64, sv);
       tmem_ld_wait();
       const float4* d4 = reinterpret_cast<const float4*>(stg + 32);
+      const float2 sc2 = make_float2(scale, scale);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float4 d = d4[i];
-        sv[4 * i] = tf32_bits(pf[4 * i] * fmaf(__uint_as_float(sv[4 * i]), scale, -d.x));
-        sv[4 * i + 1] = tf32_bits(pf[4 * i + 1] * fmaf(__uint_as_float(sv[4 * i + 1]), scale, -d.y));
-        sv[4 * i + 2] = tf32_bits(pf[4 * i + 2] * fmaf(__uint_as_float(sv[4 * i + 2]), scale, -d.z));
-        sv[4 * i + 3] = tf32_bits(pf[4 * i + 3] * fmaf(__uint_as_float(sv[4 * i + 3]), scale, -d.w));
+        const float2 t0 = fma2(make_float2(__uint_as_float(sv[4 * i]), __uint_as_float(sv[4 * i + 1])), sc2,
+                               make_float2(d.x, d.y));
+        const float2 t1 = fma2(make_float2(__uint_as_float(sv[4 * i + 2]), __uint_as_float(sv[4 * i + 3])), sc2,
+                               make_float2(d.z, d.w));
+        const float2 g0 = mul2(make_float2(pf[4 * i], pf[4 * i + 1]), t0);
+        const float2 g1 = mul2(make_float2(pf[4 * i + 2], pf[4 * i + 3]), t1);
+        sv[4 * i] = tf32_operand_bits(g0.x);
+        sv[4 * i + 1] = tf32_operand_bits(g0.y);
+        sv[4 * i + 2] = tf32_operand_bits(g1.x);
+        sv[4 * i + 3] = tf32_operand_bits(g1.y);
       }
       tmem_st_32x32b_x32(sa + 64, sv);
       tmem_st_wait();
@@ -2125,8 +2182,13 @@ __global__ void __launch_bounds__(NT2, 1)
         tmem_ld_wait();
         const int k_lo = j * 64 + hf * 32;
         if (k_lo + 32 <= q0 + 1 && q0 + 128 <= S) {
+          const float2 k2 = make_float2(scale_log2, scale_log2), nl2 = make_float2(-lse2, -lse2);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) pf[e] = fast_exp2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse2));
+          for (int e = 0; e < 32; e += 2) {
+            const float2 x = fma2(make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), k2, nl2);
+            pf[e] = fast_exp2(x.x);
+            pf[e + 1] = fast_exp2(x.y);
+          }
         } else {
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
@@ -2139,8 +2201,14 @@ __global__ void __launch_bounds__(NT2, 1)
         tc_fence_after();
         tmem_ld_32x32b_x32(sa + 64, sv);
         tmem_ld_wait();
+        const float2 sc2 = make_float2(scale, scale), nd2 = make_float2(nDs, nDs);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) sv[e] = tf32_bits(pf[e] * fmaf(__uint_as_float(sv[e]), scale, nDs));
+        for (int e = 0; e < 32; e += 2) {
+          const float2 t = fma2(make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sc2, nd2);
+          const float2 g = mul2(make_float2(pf[e], pf[e + 1]), t);
+          sv[e] = tf32_operand_bits(g.x);
+          sv[e + 1] = tf32_operand_bits(g.y);
+        }
         tmem_st_32x32b_x32(sa, sv);
         tmem_st_wait();
         tc_fence_before();
@@ -2308,9 +2376,11 @@ int bwd_impl(Context* ctx, const AttnIO& io, const float* o, const float* lse, c
              const float* rope_sin, cudaStream_t s) {
   const float *q = io.q, *k = io.k, *v = io.v;
   static SmemFlags done_g, done_g2, done_q, done_pq, done_pq2;
-  const bool dq_persist = ctx->attn_dq_variant != 1;  // automatic: persistent
-  const bool dq2 = ctx->attn_dq_variant == 3;
-  const bool dkdv2 = ctx->attn_dkdv_variant == 2;
+  // automatic: the persistent dQ kernel and the dK/dV kernel, both with two
+  // groups of softmax warps
+  const bool dq_persist = ctx->attn_dq_variant != 1;
+  const bool dq2 = ctx->attn_dq_variant == 0 || ctx->attn_dq_variant == 3;
+  const bool dkdv2 = ctx->attn_dkdv_variant != 1;
   int rc = dkdv2 ? set_smem(ctx, attn_bwd_dkdv2_kernel<HD>, Dkdv2Layout<HD>::BYTES, done_g2)
                  : set_smem(ctx, attn_bwd_dkdv_tc_kernel<HD>, DkdvLayout<HD>::BYTES, done_g);
   if (!rc)

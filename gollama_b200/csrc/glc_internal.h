@@ -54,9 +54,9 @@ struct Context {
   bool fuse_swiglu = false;            // trainer: SwiGLU forward in the gate/up GEMM epilogue (Llama semantics)
   int attn_split = 0;                  // dK/dV CTAs per KV head: 0 automatic, else a divisor of the group
   int rmsnorm_variant = 0;             // RMSNorm backward: 0 automatic (3 for the exact gradient, else 1), 1 row per iteration, 2 cp.async rows, 3 bulk-copied rows
-  int attn_dq_variant = 0;             // attention backward dQ: 0 automatic (= 2), 1 a CTA per query tile, 2 persistent,
+  int attn_dq_variant = 0;             // attention backward dQ: 0 automatic (= 3), 1 a CTA per query tile, 2 persistent,
                                        // 3 persistent with two math groups
-  int attn_dkdv_variant = 0;           // attention backward dK/dV: 0 automatic (= 1), 1 one math group, 2 two math groups
+  int attn_dkdv_variant = 0;           // attention backward dK/dV: 0 automatic (= 2), 1 one math group, 2 two math groups
   int attn_fwd_variant = 0;            // attention forward: 0 automatic (= 2), 1 a CTA per query tile, 2 persistent
   int quant_path = 0;                  // dX through a stored weight: 0 automatic (= 1), 1 dequantize + GEMM, 2 fused
   bool tracing = false;                // NVTX ranges around the phases of a training step

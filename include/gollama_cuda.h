@@ -208,15 +208,15 @@ GLC_API int glc_set_pdl(glc_ctx* ctx, int on);
  * item's loads and score products overlap the current item's last tiles and
  * output).  Results are bit-identical. */
 GLC_API int glc_set_attention_fwd_variant(glc_ctx* ctx, int variant);
-/* The same choice for the attention backward's dQ kernel: 0 automatic and 2
- * walk its (query tile, batch, head) items persistently, moving the next
- * item's Q and dO into TMEM while the current item's dQ is written; 1 one CTA
- * per item; 3 persistent with sixteen softmax warps in two groups taking
- * alternate steps.  Bit-identical. */
+/* The same choice for the attention backward's dQ kernel: 2 walks its
+ * (query tile, batch, head) items persistently, moving the next item's Q and
+ * dO into TMEM while the current item's dQ is written; 0 automatic and 3 the
+ * same with sixteen softmax warps in two groups taking alternate steps; 1 one
+ * CTA per item.  Bit-identical. */
 GLC_API int glc_set_attention_dq_variant(glc_ctx* ctx, int variant);
-/* The attention backward's dK/dV kernel: 0 automatic and 1 eight softmax
- * warps that take every 64-query step in turn; 2 sixteen softmax warps in
- * two groups taking alternate steps, so one group's arithmetic overlaps the
+/* The attention backward's dK/dV kernel: 1 eight softmax warps that take
+ * every 64-query step in turn; 0 automatic and 2 sixteen softmax warps in two
+ * groups taking alternate steps, so one group's arithmetic overlaps the
  * other's.  Bit-identical. */
 GLC_API int glc_set_attention_dkdv_variant(glc_ctx* ctx, int variant);
 /* Tile order of the CTA-pair GEMM (tuning; no reference counterpart): 0
