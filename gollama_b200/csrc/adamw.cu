@@ -61,16 +61,33 @@ __global__ void sumsq_chunks_kernel(const float* __restrict__ g, const Seg* __re
                                     double* __restrict__ out) {
   GLC_PDL_ENTRY();
   __shared__ double red[32];
+  // Few blocks run this beside the backward, so each thread keeps eight
+  // independent float4 loads in flight (one at a time left a block at a few
+  // GB/s, far below what one SM can pull).
+  constexpr int U = 8;
+  auto sq4 = [](const float4 v) {
+    const double x = v.x, y = v.y, z = v.z, w = v.w;
+    return __dadd_rn(__dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)), __dadd_rn(__dmul_rn(z, z), __dmul_rn(w, w)));
+  };
   for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
     const Seg sg = chunks[c];
-    double acc = 0.0;
+    double acc = 0.0, acc2 = 0.0;
     const float4* base = reinterpret_cast<const float4*>(g + sg.start);
     const int64_t n4 = sg.len >> 2;
-    for (int64_t i = threadIdx.x; i < n4; i += blockDim.x) {
-      const float4 v = base[i];
-      const double x = v.x, y = v.y, z = v.z, w = v.w;
-      acc = __dadd_rn(acc, __dadd_rn(__dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)), __dadd_rn(__dmul_rn(z, z), __dmul_rn(w, w))));
+    const int64_t step = static_cast<int64_t>(blockDim.x) * U;
+    int64_t i = threadIdx.x;
+    for (; i + (U - 1) * static_cast<int64_t>(blockDim.x) < n4; i += step) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = base[i + u * static_cast<int64_t>(blockDim.x)];
+#pragma unroll
+      for (int u = 0; u < U; u += 2) {
+        acc = __dadd_rn(acc, sq4(v[u]));
+        acc2 = __dadd_rn(acc2, sq4(v[u + 1]));
+      }
     }
+    for (; i < n4; i += blockDim.x) acc = __dadd_rn(acc, sq4(base[i]));
+    acc = __dadd_rn(acc, acc2);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;

@@ -1051,7 +1051,10 @@ int gemm_tf32_group(Context* ctx, const GemmSpec* specs, int n, cudaStream_t str
     // one cluster per SM pair; clusters loop over the tiles
     const int pairs = ctx->num_sms / 2;
     const int clusters = a.total_tiles < pairs ? a.total_tiles : pairs;
-    if (ctx->gemm_order == 2) {
+    // automatic: the dynamic order under data parallelism, where the
+    // gradient allreduce holds SMs during the backward (2 GPUs, dynamic vs
+    // fixed: 87.2 vs 90.2 ms per step), the fixed order on one GPU
+    if (ctx->gemm_order == 2 || (ctx->gemm_order == 0 && ctx->world > 1)) {
       // dynamic order: a fresh zero counter per launch from the context's
       // ring of counters, cleared on the stream whenever the ring wraps
       const unsigned idx = static_cast<unsigned>(ctx->dyn_next++ % Context::kDynCounters);

@@ -972,11 +972,11 @@ int Trainer::train_step(const int64_t* in_dev, const int64_t* tg_dev, int B, int
         throw StepError{GLC_ERR_CUDA};
       ck(dp_allreduce_on(ctx, model->grads + model->bucket_begin[b],
                          static_cast<size_t>(model->bucket_end[b] - model->bucket_begin[b]), ctx->comm_stream));
-      // the bucket's summed gradients are final: their squares, 16 blocks
+      // the bucket's summed gradients are final: their squares, 32 blocks
       // beside the backward
       const int c0 = dp_chunk_off[b], c1 = dp_chunk_off[b + 1];
       if (c1 > c0)
-        ck(grad_sumsq_chunks(ctx, model->grads, dp_chunks_dev + 2 * static_cast<int64_t>(c0), c1 - c0, 16,
+        ck(grad_sumsq_chunks(ctx, model->grads, dp_chunks_dev + 2 * static_cast<int64_t>(c0), c1 - c0, 32,
                              dp_slots + c0, 0.0, ctx->comm_stream));
     };
     const Tape::OrderHook before = [&](const std::vector<Node*>& run) {

@@ -219,12 +219,13 @@ GLC_API int glc_set_attention_dq_variant(glc_ctx* ctx, int variant);
  * groups taking alternate steps, so one group's arithmetic overlaps the
  * other's.  Bit-identical. */
 GLC_API int glc_set_attention_dkdv_variant(glc_ctx* ctx, int variant);
-/* Tile order of the CTA-pair GEMM (tuning; no reference counterpart): 0
- * automatic and 1 a fixed order per pair (a rotation, or host-built lists
- * for a grouped dX + dW launch); 2 dynamic: every pair takes the next tile
- * from a counter when it is ready, so pairs that start late (their SMs held
- * by another kernel, e.g. the gradient allreduce) take fewer tiles.  Each
- * tile is computed the same way in every order: results are bit-identical. */
+/* Tile order of the CTA-pair GEMM (tuning; no reference counterpart): 1 a
+ * fixed order per pair (a rotation, or host-built lists for a grouped dX + dW
+ * launch); 2 dynamic: every pair takes the next tile from a counter when it
+ * is ready, so pairs that start late (their SMs held by another kernel, e.g.
+ * the gradient allreduce) take fewer tiles; 0 automatic: 2 once data
+ * parallelism is initialised, 1 otherwise.  Each tile is computed the same
+ * way in every order: results are bit-identical. */
 GLC_API int glc_set_gemm_schedule(glc_ctx* ctx, int mode);
 /* Trainer (Llama semantics): 1 computes the SwiGLU forward in the gate/up
  * GEMM's epilogue, 0 (default, faster on B200 at the TinyLlama shape) runs it
