@@ -203,11 +203,11 @@ __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t i = i0 + u * stride;
-      if (i < n4) {
-        P[u] = p4[i];
-        G[u] = g4[i];
-        M[u] = m4[i];
-        V[u] = v4[i];
+      if (i < n4) {  // each value is read and written once per step: evict-first
+        P[u] = __ldcs(p4 + i);
+        G[u] = __ldcs(g4 + i);
+        M[u] = __ldcs(m4 + i);
+        V[u] = __ldcs(v4 + i);
       }
     }
 #pragma unroll
@@ -218,11 +218,11 @@ __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float
       adam_elem(P[u].y, G[u].y, M[u].y, V[u].y, scale, scaled, a);
       adam_elem(P[u].z, G[u].z, M[u].z, V[u].z, scale, scaled, a);
       adam_elem(P[u].w, G[u].w, M[u].w, V[u].w, scale, scaled, a);
-      if (scaled && write_g) g4[i] = G[u];
-      m4[i] = M[u];
-      v4[i] = V[u];
-      p4[i] = P[u];
-      if (s4) s4[i] = make_float4(round_tf32(P[u].x), round_tf32(P[u].y), round_tf32(P[u].z), round_tf32(P[u].w));
+      if (scaled && write_g) __stcs(g4 + i, G[u]);
+      __stcs(m4 + i, M[u]);
+      __stcs(v4 + i, V[u]);
+      __stcs(p4 + i, P[u]);
+      if (s4) __stcs(s4 + i, make_float4(round_tf32(P[u].x), round_tf32(P[u].y), round_tf32(P[u].z), round_tf32(P[u].w)));
     }
   }
 }
