@@ -9,13 +9,15 @@
 // floats, k/v rows Hkv*hd; row t = b*S + s.  Inputs are expected TF32-rounded
 // (the producing kernels round them); P and dS are rounded when written.
 //
-// Every kernel: 352 threads — warp 0 issues TMA loads (one thread), warp 1
-// owns TMEM and issues the score MMAs (S, dP), warp 10 issues the
-// accumulating MMAs (O += P V, dV/dK, dQ), warps 2..9 do the softmax
+// The forward and the one-group backward kernels: 352 threads — warp 0 issues
+// TMA loads, warp 1 owns TMEM and issues the score MMAs (S, dP), warp 10 issues
+// the accumulating MMAs (O += P V, dV/dK, dQ), warps 2..9 do the softmax
 // arithmetic: warp w reads TMEM lane quarter w % 4 (one thread per row) and
 // column half (w - 2) / 4 of each tile, so two warps share every row.  Values
 // the two halves of a row must agree on pass through shared memory behind an
-// mbarrier.  All waits are bounded.
+// mbarrier.  The backward kernels used by default have 608 threads: sixteen
+// softmax warps in two groups that take alternate steps (see "two math
+// groups" below).  All waits are bounded.
 //
 // forward   CTA = (128 queries, head).  S_j = Q K_j^T into one of three TMEM
 //           buffers (the next S overlaps this softmax); P_j replaces S_j in
@@ -44,9 +46,10 @@ namespace {
 
 // Warps: 0 TMA producer, 1 MMA issuer for the score products (S, and dP in
 // the backward), 2..9 math, 10 MMA issuer for the accumulating products
-// (O += P V; dV/dK; dQ).  One thread issues a tcgen05.mma about every 49
-// cycles at best, and an N = 64 TF32 MMA with A in TMEM needs 32 cycles of the
-// tensor core: two issuing threads keep it busy, one cannot.
+// (O += P V; dV/dK; dQ).  A warp issues an N = 64 TF32 MMA (A in TMEM) about
+// every 52 cycles when the whole warp runs the loop and elect.sync picks the
+// issuing lane (about every 80 from a lane-0-only branch); the tensor core
+// needs 32: two issuing warps keep it busy, one cannot.
 constexpr int NT = 352;
 constexpr int MATH_THREADS = 256;  // warps 2..9
 constexpr int ACC_WARP = 10;
