@@ -1,4 +1,4 @@
-"""Data-parallel host logic on CPU (world_size 2, gloo).
+"""Data-parallel host logic on CPU (world_size 2 and 4, gloo).
 
 The GPU path sums each gradient bucket with NCCL as soon as the backward has
 written it (glc_dp_bucket_plan gives the buckets).  What that path relies on
@@ -10,7 +10,7 @@ is checked here without a GPU:
     reference mode the loss seed is ones, so the rank gradients add; in llama
     mode the cross-entropy mean is over the global batch, so each rank's mean
     is weighted by its share of the tokens before the sum.
-Each rank runs the oracle on its half of the batch in its own process.
+Each rank runs the oracle on its share of the batch in its own process.
 """
 import ctypes as C
 import datetime
@@ -69,7 +69,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank, port, shape_name, out_path):
+def _rank_main(rank, port, shape_name, out_path, world=WORLD):
     import torch
     import torch.distributed as dist
 
@@ -77,14 +77,14 @@ def _rank_main(rank, port, shape_name, out_path):
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
     try:
         shape = syn.SHAPES[shape_name]
         orc = Oracle(threads=2)
         cfg = oracle_config(shape)
         params = syn.init_params(shape, seed=11)
         inputs, targets = syn.batch(shape, seed=12)
-        rows = np.array_split(np.arange(inputs.shape[0]), WORLD)[rank]
+        rows = np.array_split(np.arange(inputs.shape[0]), world)[rank]
         _, grads, _ = orc.forward_backward(cfg, params, inputs[rows], targets[rows])
         if shape.mode == 1:  # llama: the loss is the mean over the global batch
             grads *= np.float32(len(rows) / inputs.shape[0])
@@ -99,13 +99,15 @@ def _rank_main(rank, port, shape_name, out_path):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("shape_name", ["tiny", "tiny-llama"])
-def test_two_rank_bucket_sum_equals_global_batch(shape_name):
+def test_rank_bucket_sum_equals_global_batch(shape_name, world):
     import torch.multiprocessing as mp
 
+    assert syn.SHAPES[shape_name].batch >= world
     with tempfile.TemporaryDirectory() as d:
         out = os.path.join(d, "grads.npz")
-        mp.start_processes(_rank_main, args=(_free_port(), shape_name, out), nprocs=WORLD, start_method="spawn")
+        mp.start_processes(_rank_main, args=(_free_port(), shape_name, out, world), nprocs=world, start_method="spawn")
         r = np.load(out)
-        # the two halves add in a different fp32 order than the full batch
+        # the ranks' shares add in a different fp32 order than the full batch
         assert rel_fro(r["summed"], r["full"]) < 1e-5
