@@ -333,9 +333,12 @@ __global__ void __launch_bounds__(SEG_THREADS, 1)
 // ascending t.
 // Launch: blockIdx.x strides over segments, blockIdx.y picks a chunk of
 // blockDim.x float4 columns, so a frequent id's long segment is spread over
-// several blocks; each thread owns one float4 column and fetches 8 rows ahead
-// before adding them in ascending t (the order, and so the bits, of the
-// sequential sum).
+// several blocks; each thread owns one float4 column.  The sum itself is
+// sequential (ascending t: the order, and so the bits, of the reference's
+// accumulation), so the time of a frequent id's segment (hundreds of rows
+// with Zipf-distributed ids) is its load latency: rows come in chunks of 16,
+// the next chunk's rows loaded while the current chunk is added and the
+// token indices of the chunk after that loaded a chunk earlier still.
 // The segment count comes from nseg_dev when it is given (segments built on
 // the device), else from nseg.
 __global__ void embed_bwd_kernel(const int* __restrict__ seg_tok, const int* __restrict__ seg_start,
@@ -346,20 +349,41 @@ __global__ void embed_bwd_kernel(const int* __restrict__ seg_tok, const int* __r
   const int c = blockIdx.y * blockDim.x + threadIdx.x;
   if (c >= nc) return;
   if (nseg_dev) nseg = *nseg_dev;
+  constexpr int CH = 16;
+  const float4* col = reinterpret_cast<const float4*>(dh) + c;
+  const size_t rs = static_cast<size_t>(nc);  // float4s per row of dh
   for (int u = blockIdx.x; u < nseg; u += gridDim.x) {
     float4* row = reinterpret_cast<float4*>(dE + static_cast<size_t>(seg_tok[u]) * d);
     const int b = seg_start[u], e = seg_start[u + 1];
     float4 acc = row[c];
-    for (int k = b; k < e; k += 8) {
-      float4 g[8];
+    // token indices of chunks 0 and 1, rows of chunk 0
+    int ix[CH], ixn[CH];
+    float4 cur[CH], nxt[CH];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (k + i < e) g[i] = reinterpret_cast<const float4*>(dh + static_cast<size_t>(order[k + i]) * d)[c];
+    for (int i = 0; i < CH; ++i) {
+      ix[i] = b + i < e ? order[b + i] : 0;
+      ixn[i] = b + CH + i < e ? order[b + CH + i] : 0;
+    }
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < CH; ++i)
+      if (b + i < e) cur[i] = col[static_cast<size_t>(ix[i]) * rs];
+    for (int k = b; k < e; k += CH) {
+      // rows of the next chunk, indices of the one after
+#pragma unroll
+      for (int i = 0; i < CH; ++i) {
+        if (k + CH + i < e) nxt[i] = col[static_cast<size_t>(ixn[i]) * rs];
+        ix[i] = k + 2 * CH + i < e ? order[k + 2 * CH + i] : 0;
+      }
+#pragma unroll
+      for (int i = 0; i < CH; ++i)
         if (k + i < e)
-          acc = make_float4(__fadd_rn(acc.x, g[i].x), __fadd_rn(acc.y, g[i].y), __fadd_rn(acc.z, g[i].z),
-                            __fadd_rn(acc.w, g[i].w));
+          acc = make_float4(__fadd_rn(acc.x, cur[i].x), __fadd_rn(acc.y, cur[i].y), __fadd_rn(acc.z, cur[i].z),
+                            __fadd_rn(acc.w, cur[i].w));
+#pragma unroll
+      for (int i = 0; i < CH; ++i) {
+        cur[i] = nxt[i];
+        ixn[i] = ix[i];
+      }
     }
     row[c] = acc;
   }
