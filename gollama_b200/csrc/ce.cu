@@ -10,13 +10,13 @@
 // The loss (:246) is summed by a second, single-thread kernel in row order,
 // exactly as the reference's running float32 total.
 //
-// Large vocabularies (V > 8192) split each row over a cluster of CE_CL CTAs
-// (ce_cluster_kernel): each holds a quarter of the row in registers, and the
-// row max and sum are exchanged through distributed shared memory, added in
-// rank order so every CTA of the row derives the same values.  A quarter row
-// needs ~64 registers per thread, so several rows share an SM and one row's
-// loads overlap another's arithmetic (one CTA per row holds a whole row per
-// SM at a time and serialises them).
+// Large vocabularies in the Llama arithmetic (8192 < V <= 32768) stream their
+// rows through persistent CTAs (ce_stream_kernel, below): bulk copies fill a
+// shared-memory ring of row chunks ahead of the row in registers.  The others
+// split each row over a cluster of CE_CL CTAs (ce_cluster_kernel): each holds
+// a quarter of the row in registers, and the row max and sum are exchanged
+// through distributed shared memory, added in rank order so every CTA of the
+// row derives the same values.
 #include <cfloat>
 
 #include "glc_internal.h"
@@ -215,24 +215,268 @@ __global__ void __cluster_dims__(CE_CL, 1, 1) __launch_bounds__(CE_CL_THREADS, V
   cluster_sync_all();
 }
 
+// Streamed rows (8192 < V <= 32768): one persistent CTA of CE_ST_THREADS per
+// SM walks the rows blockIdx.x, blockIdx.x + gridDim.x, ...  A row is cut
+// into CE_ST_CHUNKS chunks of cf4 float4 (the last one shorter).  Thread 0
+// keeps a ring of `nslots` shared-memory chunk slots filled with bulk copies
+// (one mbarrier per slot), up to nslots chunks ahead of the row in hand.  The
+// threads move the current row from its slots into registers (thread t holds
+// float4 t + 512 u of every chunk); once every thread has done so the slots
+// are refilled with the next chunks, while the row's max, exponentials, sum
+// and gradient are computed from registers and the gradient is stored
+// straight to global memory.  Loads keep streaming through the reductions
+// and stores of the row before (the one-shot clusters load, reduce and store
+// in step), and a row never leaves its CTA: two block reductions, no cluster
+// barrier.  With the reference's exp32 and division the per-element
+// arithmetic is the cluster kernel's (and its float64 exponential makes the
+// kernel compute-bound on 16 warps per SM: the clusters' 32 run it faster);
+// with the Llama arithmetic e^(x - max) is ex2.approx of one FMA and the
+// gradient one product, few enough instructions for the copies to set the
+// pace.  The row sum adds each thread's partial, then warp and block partials
+// in a fixed order.
+constexpr float kLog2e = 1.4426950408889634f;
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+constexpr int CE_ST_THREADS = 512;
+constexpr int CE_ST_WARPS = CE_ST_THREADS / 32;
+constexpr int CE_ST_CHUNKS = 8;
+constexpr int CE_ST_MAX_SLOTS = 32;
+constexpr size_t CE_ST_SMEM_BYTES = 224 * 1024;  // ring; the static barriers and partials fit beside it
+
+template <int U, bool FAST>
+__global__ void __launch_bounds__(CE_ST_THREADS, 1)
+    ce_stream_kernel(float* __restrict__ logits, const int64_t* __restrict__ targets, int rows, int V, int cf4,
+                     int nslots, float scale, float* __restrict__ row_logp, int write_grad, int round_out, int* err) {
+  GLC_PDL_ENTRY();
+  extern __shared__ __align__(16) float4 ring[];  // [nslots][cf4]
+  __shared__ uint64_t full[CE_ST_MAX_SLOTS];
+  __shared__ float red_m[CE_ST_WARPS];
+  __shared__ float red_s[CE_ST_WARPS];
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nc = V >> 2;
+  const int cta = static_cast<int>(blockIdx.x), ncta = static_cast<int>(gridDim.x);
+  const int nrows = cta < rows ? (rows - 1 - cta) / ncta + 1 : 0;
+  const int nq = nrows * CE_ST_CHUNKS;  // chunks this CTA loads
+  // thread 0 only: chunk q is chunk q % CE_ST_CHUNKS of the CTA's row q / CE_ST_CHUNKS, into slot q % nslots
+  auto issue = [&](int q) {
+    const int j = q % CE_ST_CHUNKS;
+    const size_t row = static_cast<size_t>(cta) + static_cast<size_t>(q / CE_ST_CHUNKS) * ncta;
+    const uint32_t bytes = static_cast<uint32_t>(min(cf4, nc - j * cf4)) * 16u;
+    const int slot = q % nslots;
+    mbar_arrive_expect_tx(&full[slot], bytes);
+    bulk_load(ring + static_cast<size_t>(slot) * cf4, logits + row * V + static_cast<size_t>(j) * cf4 * 4, bytes,
+              &full[slot]);
+  };
+  if (tid == 0) {
+    for (int i = 0; i < nslots; ++i) mbar_init(&full[i], 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int issued = 0;  // chunks whose copies thread 0 has issued
+  if (tid == 0)
+    for (; issued < nq && issued < nslots; ++issued) issue(issued);
+  int slot = 0;       // slot of the next chunk to consume
+  uint32_t ph = 0;    // its phase parity
+  bool ok = true, aborted = false;
+  int k = 0;
+  for (; k < nrows; ++k) {
+    const int row = cta + k * ncta;
+    const int64_t t64 = targets[row];
+    const int t = t64 >= 0 && t64 < V ? static_cast<int>(t64) : -1;  // -1 (no target) matches no column
+    const int t4 = t >= 0 ? t >> 2 : -1;                               // the target's float4 column
+    float4 v[CE_ST_CHUNKS][U];
+    float m = -FLT_MAX;
+#pragma unroll
+    for (int j = 0; j < CE_ST_CHUNKS; ++j) {
+      ok = ok && mbar_wait(&full[slot], ph, &abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE);
+      const int cnt = j + 1 < CE_ST_CHUNKS ? cf4 : nc - j * cf4;
+      const float4* src = ring + static_cast<size_t>(slot) * cf4;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int e = tid + u * CE_ST_THREADS;
+        if (e < cnt) {
+          v[j][u] = src[e];
+          m = fmaxf(m, fmaxf(fmaxf(v[j][u].x, v[j][u].y), fmaxf(v[j][u].z, v[j][u].w)));
+        }
+      }
+      if (++slot == nslots) {
+        slot = 0;
+        ph ^= 1u;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red_m[warp] = m;
+    // every thread holds its part of the row (or a wait gave up): the row's slots may be refilled
+    if (!__syncthreads_and(ok)) {
+      aborted = true;
+      break;
+    }
+    if (tid == 0) {
+      const int lim = min(nq, (k + 1) * CE_ST_CHUNKS + nslots);
+      for (; issued < lim; ++issued) issue(issued);
+    }
+    float mx = red_m[0];
+#pragma unroll
+    for (int w = 1; w < CE_ST_WARPS; ++w) mx = fmaxf(mx, red_m[w]);
+    // Llama arithmetic: e^(x - max) = 2^(x log2 e - max log2 e), one FMA and
+    // ex2.approx (relative error ~1e-6 against expf, far inside the fp32
+    // tolerance of this path and the TF32 rounding its gradient gets)
+    const float mlog2 = mx * kLog2e;
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < CE_ST_CHUNKS; ++j) {
+      const int cnt = j + 1 < CE_ST_CHUNKS ? cf4 : nc - j * cf4;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (tid + u * CE_ST_THREADS < cnt) {
+          float4& x = v[j][u];
+          if (FAST) {
+            x.x = ex2_approx(fmaf(x.x, kLog2e, -mlog2));
+            x.y = ex2_approx(fmaf(x.y, kLog2e, -mlog2));
+            x.z = ex2_approx(fmaf(x.z, kLog2e, -mlog2));
+            x.w = ex2_approx(fmaf(x.w, kLog2e, -mlog2));
+          } else {
+            x.x = go_exp32_fast(__fsub_rn(x.x, mx));
+            x.y = go_exp32_fast(__fsub_rn(x.y, mx));
+            x.z = go_exp32_fast(__fsub_rn(x.z, mx));
+            x.w = go_exp32_fast(__fsub_rn(x.w, mx));
+          }
+          s += (x.x + x.y) + (x.z + x.w);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) red_s[warp] = s;
+    // red_m is rewritten only after the next row's loads, past this barrier; red_s after the next one's first
+    __syncthreads();
+    float sum = red_s[0];
+#pragma unroll
+    for (int w = 1; w < CE_ST_WARPS; ++w) sum += red_s[w];
+    float4* lr = reinterpret_cast<float4*>(logits + static_cast<size_t>(row) * V);
+    if (FAST) {
+      // p = e * (1 / sum), the gradient p * scale as one product; the target's
+      // column (one float4 of the row) takes p_t * scale - scale and its log
+      const float inv = 1.0f / sum;
+      const float ks = inv * scale;
+#pragma unroll
+      for (int j = 0; j < CE_ST_CHUNKS; ++j) {
+        const int cnt = j + 1 < CE_ST_CHUNKS ? cf4 : nc - j * cf4;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int e = tid + u * CE_ST_THREADS;
+          if (e < cnt) {
+            const int c = j * cf4 + e;
+            const float4 x = v[j][u];
+            float g[4] = {x.x * ks, x.y * ks, x.z * ks, x.w * ks};
+            if (c == t4) {
+              const int jj = t & 3;
+              const float pt = (jj == 0 ? x.x : jj == 1 ? x.y : jj == 2 ? x.z : x.w) * inv;
+              row_logp[row] = logf(__fadd_rn(pt, 1e-10f));
+              const float gt = __fsub_rn(__fmul_rn(pt, scale), scale);
+              g[0] = jj == 0 ? gt : g[0];
+              g[1] = jj == 1 ? gt : g[1];
+              g[2] = jj == 2 ? gt : g[2];
+              g[3] = jj == 3 ? gt : g[3];
+            }
+            if (write_grad) {
+              if (round_out) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) g[q] = round_tf32(g[q]);
+              }
+              lr[c] = make_float4(g[0], g[1], g[2], g[3]);
+            }
+          }
+        }
+      }
+      if (t < 0 && tid == 0) row_logp[row] = 0.f;
+      continue;
+    }
+#pragma unroll
+    for (int j = 0; j < CE_ST_CHUNKS; ++j) {
+      const int cnt = j + 1 < CE_ST_CHUNKS ? cf4 : nc - j * cf4;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int e = tid + u * CE_ST_THREADS;
+        if (e < cnt) {
+          const int c = j * cf4 + e;
+          const float4 x = v[j][u];
+          const bool has_t = static_cast<unsigned>(t - 4 * c) < 4u;
+          float p[4] = {0.f, 0.f, 0.f, 0.f};
+          if (write_grad || has_t) {
+            p[0] = __fdiv_rn(x.x, sum); p[1] = __fdiv_rn(x.y, sum); p[2] = __fdiv_rn(x.z, sum); p[3] = __fdiv_rn(x.w, sum);
+          }
+          if (has_t) {
+            const int jj = t - 4 * c;
+            const float pt = jj == 0 ? p[0] : jj == 1 ? p[1] : jj == 2 ? p[2] : p[3];
+            row_logp[row] = go_log32(__fadd_rn(pt, 1e-10f));
+          }
+          if (write_grad) {
+            float g[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              g[q] = __fmul_rn(p[q], scale);
+              if (q == t - 4 * c) g[q] = __fsub_rn(g[q], scale);
+              if (round_out) g[q] = round_tf32(g[q]);
+            }
+            lr[c] = make_float4(g[0], g[1], g[2], g[3]);
+          }
+        }
+      }
+    }
+    if (t < 0 && tid == 0) row_logp[row] = 0.f;
+  }
+  if (aborted && tid == 0) {
+    // no copy may land after the CTA exits: wait (bounded) for those in flight
+    for (int q = k * CE_ST_CHUNKS; q < issued; ++q) mbar_drain(&full[q % nslots], (q / nslots) & 1, err);
+  }
+}
+
 // loss = (0 - logp_0 - logp_1 - ...) / rows over valid targets (grad.go:239-246).
 // One block: the threads stage chunks of row_logp in shared memory, thread 0
-// subtracts them in row order (the reference's running float32 total).
+// subtracts them in row order (the reference's running float32 total).  The
+// chunk is padded with +0 (x - 0 == x exactly, -0 included), so thread 0
+// reads eight float4 ahead and only the chain of subtractions is serial.
 __global__ void ce_loss_sum_kernel(const float* __restrict__ row_logp, const int64_t* __restrict__ targets, int rows,
                                    int V, float* __restrict__ loss) {
   GLC_PDL_ENTRY();
-  constexpr int CHUNK = 2048;
-  __shared__ float buf[CHUNK];
+  constexpr int CHUNK = 4096;
+  __shared__ __align__(16) float buf[CHUNK];
   float total = 0.f;
   for (int base = 0; base < rows; base += CHUNK) {
     const int n = min(CHUNK, rows - base);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const int64_t t = targets[base + i];
-      buf[i] = (t >= 0 && t < V) ? row_logp[base + i] : 0.f;  // x - 0 == x: invalid rows add nothing
+    for (int i = threadIdx.x; i < CHUNK; i += blockDim.x) {
+      float x = 0.f;  // invalid rows and the padding add nothing
+      if (i < n) {
+        const int64_t t = targets[base + i];
+        if (t >= 0 && t < V) x = row_logp[base + i];
+      }
+      buf[i] = x;
     }
     __syncthreads();
-    if (threadIdx.x == 0)
-      for (int i = 0; i < n; ++i) total = __fsub_rn(total, buf[i]);
+    if (threadIdx.x == 0) {
+      const float4* b4 = reinterpret_cast<const float4*>(buf);
+      const int n4 = (n + 3) >> 2;
+      for (int i = 0; i < n4; i += 8) {
+        float4 q[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) q[u] = b4[i + u];  // i + 8 <= CHUNK / 4: the padding covers the tail
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          total = __fsub_rn(total, q[u].x);
+          total = __fsub_rn(total, q[u].y);
+          total = __fsub_rn(total, q[u].z);
+          total = __fsub_rn(total, q[u].w);
+        }
+      }
+    }
     __syncthreads();
   }
   if (threadIdx.x == 0) *loss = __fdiv_rn(total, static_cast<float>(rows));
@@ -263,6 +507,28 @@ int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, in
   if (!targets || !row_logp || !loss) return ctx->fail(GLC_ERR_INVALID, "softmax_ce: null pointer");
   const int nc = V / 4;
   const int wg = write_grad ? 1 : 0, ro = round_out ? 1 : 0;
+  if (nc > 2048 && nc <= CE_ST_CHUNKS * 2 * CE_ST_THREADS &&
+      (ctx->ce_variant == 2 || (ctx->ce_variant == 0 && fast_exp))) {
+    // 8192 < V <= 32768 (automatic: the Llama arithmetic only): persistent CTAs
+    // streaming their rows through bulk-copied chunks
+    const int cf4 = (nc + CE_ST_CHUNKS - 1) / CE_ST_CHUNKS;  // <= 1024 float4: a chunk is at most 16 KiB
+    const size_t slot_bytes = static_cast<size_t>(cf4) * sizeof(float4);
+    int nslots = static_cast<int>(CE_ST_SMEM_BYTES / slot_bytes);  // >= 14 >= CE_ST_CHUNKS: a whole row fits
+    if (nslots > CE_ST_MAX_SLOTS) nslots = CE_ST_MAX_SLOTS;
+    const size_t smem = static_cast<size_t>(nslots) * slot_bytes;
+    const int grid = rows < ctx->num_sms ? rows : ctx->num_sms;
+    auto kern = cf4 <= CE_ST_THREADS ? (fast_exp ? ce_stream_kernel<1, true> : ce_stream_kernel<1, false>)
+                                     : (fast_exp ? ce_stream_kernel<2, true> : ce_stream_kernel<2, false>);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return ctx->fail_cuda(e, "softmax_ce: shared memory attribute");
+    ProfScope prof(ctx, PROF_CE, 4.0 * static_cast<double>(rows) * V * (write_grad ? 2 : 1), s);
+    glc::launch_pdl(ctx, kern, grid, CE_ST_THREADS, smem, s, logits, targets, rows, V, cf4, nslots, scale, row_logp, wg,
+                    ro, ctx->d_err);
+    GLC_LAUNCH_CHECK(ctx, "softmax_ce (streamed rows)");
+    glc::launch_pdl(ctx, ce_loss_sum_kernel, 1, 256, 0, s, row_logp, targets, rows, V, loss);
+    GLC_LAUNCH_CHECK(ctx, "softmax_ce loss");
+    return 0;
+  }
   if (nc > 2048) {
     // V > 8192: a cluster of CE_CL CTAs per row
     const int chunk = (nc + CE_CL - 1) / CE_CL;

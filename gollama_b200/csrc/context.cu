@@ -356,6 +356,14 @@ int glc_set_rmsnorm_variant(glc_ctx* ctx, int variant) {
   return GLC_OK;
 }
 
+int glc_set_ce_variant(glc_ctx* ctx, int variant) {
+  if (!ctx) return GLC_ERR_INVALID;
+  Context* c = C_(ctx);
+  if (variant < 0 || variant > 2) return c->fail(GLC_ERR_INVALID, "set_ce_variant: variant must be 0, 1 or 2");
+  c->ce_variant = variant;
+  return GLC_OK;
+}
+
 int glc_set_attention_split(glc_ctx* ctx, int nsplit) {
   if (!ctx) return GLC_ERR_INVALID;
   Context* c = C_(ctx);

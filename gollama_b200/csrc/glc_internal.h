@@ -57,6 +57,7 @@ struct Context {
   int attn_dq_variant = 0;             // attention backward dQ: 0 automatic (= 3), 1 a CTA per query tile, 2 persistent,
                                        // 3 persistent with two math groups
   int attn_dkdv_variant = 0;           // attention backward dK/dV: 0 automatic (= 2), 1 one math group, 2 two math groups
+  int ce_variant = 0;                  // softmax-CE above V = 8192: 0 automatic (2 for the Llama arithmetic up to V = 32768, else 1), 1 one-shot 4-CTA clusters, 2 streamed rows
   int attn_fwd_variant = 0;            // attention forward: 0 automatic (= 2), 1 a CTA per query tile, 2 persistent
   int quant_path = 0;                  // dX through a stored weight: 0 automatic (= 1), 1 dequantize + GEMM, 2 fused
   bool tracing = false;                // NVTX ranges around the phases of a training step

@@ -76,6 +76,13 @@ int glc_softmax_ce(glc_ctx* ctx, float* logits, const int64_t* targets, int rows
                          C_(ctx)->stream);
 }
 
+int glc_softmax_ce_llama(glc_ctx* ctx, float* logits, const int64_t* targets, int rows, int V, float scale,
+                         float* row_logp, float* loss, int write_grad, int round_out) {
+  if (!ctx) return GLC_ERR_INVALID;
+  return glc::softmax_ce(C_(ctx), logits, targets, rows, V, scale, row_logp, loss, write_grad != 0, round_out != 0,
+                         C_(ctx)->stream, /*fast_exp=*/true);
+}
+
 int glc_embed_fwd(glc_ctx* ctx, const int64_t* tokens, const float* E, const float* P, float* out, int T, int S, int d,
                   int V) {
   if (!ctx) return GLC_ERR_INVALID;

@@ -296,13 +296,6 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_pipe_kernel(
 // reference bits to match), dw partials per block as above.
 constexpr int TMA_STAGES = 4;
 
-__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(smem_dst)),
-               "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-
 template <int MAXC>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_full_tma_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ rms,

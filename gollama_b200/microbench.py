@@ -189,6 +189,28 @@ def case_ce(ctx, iters, warmup, T=T):
     return f"softmax_ce {T}x{V}", ms, 4.0 * T * V / (ms * 1e-3) / 1e9, "GB/s"
 
 
+def case_ce_grad(ctx, iters, warmup, T=T):
+    """The loss and the gradient written over the logits (8 B per logit); the
+    later iterations take the earlier gradients as logits."""
+    logits = _rand(ctx, (T, V), 13, 2.0, tf32=False)
+    tg = ctx.from_numpy(np.random.default_rng(14).integers(0, V, T).astype(np.int64))
+    logp, loss = ctx.empty((T,)), ctx.empty((1,))
+    ms = _time(ctx, lambda: ctx.call("glc_softmax_ce", logits.ptr, tg.ptr, T, V, C.c_float(1.0 / T), logp.ptr,
+                                     loss.ptr, 1, 1), iters, warmup)
+    return f"softmax_ce + gradient {T}x{V}", ms, 8.0 * T * V / (ms * 1e-3) / 1e9, "GB/s"
+
+
+def case_ce_llama(ctx, iters, warmup, T=T):
+    """The Llama-mode step's call: expf, the gradient written over the logits
+    and rounded to TF32."""
+    logits = _rand(ctx, (T, V), 13, 2.0, tf32=False)
+    tg = ctx.from_numpy(np.random.default_rng(14).integers(0, V, T).astype(np.int64))
+    logp, loss = ctx.empty((T,)), ctx.empty((1,))
+    ms = _time(ctx, lambda: ctx.call("glc_softmax_ce_llama", logits.ptr, tg.ptr, T, V, C.c_float(1.0 / T), logp.ptr,
+                                     loss.ptr, 1, 1), iters, warmup)
+    return f"softmax_ce_llama + gradient {T}x{V}", ms, 8.0 * T * V / (ms * 1e-3) / 1e9, "GB/s"
+
+
 def case_config4_sweep(ctx, iters, warmup):
     """The isolated backward-op sweep at its stated sizes: linear grads for M in
     {4096, 16384, 32768} x (K, N) in {(2048, 2048), (2048, 5632), (5632, 2048)};
@@ -236,6 +258,8 @@ CASES = {
     "rmsnorm_fwd": case_rmsnorm_fwd,
     "optimizer": case_optimizer,
     "softmax_ce": case_ce,
+    "softmax_ce_grad": case_ce_grad,
+    "softmax_ce_llama": case_ce_llama,
 }
 
 
@@ -257,6 +281,8 @@ def main(argv=None):
                          "3 persistent with two groups of softmax warps")
     ap.add_argument("--attn-dkdv-variant", type=int, default=0, choices=[0, 1, 2],
                     help="attention backward dK/dV: 0 automatic, 1 one group of softmax warps, 2 two groups")
+    ap.add_argument("--ce-variant", type=int, default=0, choices=[0, 1, 2],
+                    help="softmax-CE above V = 8192: 0 automatic, 1 one-shot clusters, 2 streamed rows")
     ap.add_argument("--pdl", type=int, default=0, choices=[0, 1],
                     help="programmatic dependent launch between the library's kernels")
     ap.add_argument("--gemm-schedule", type=int, default=0, choices=[0, 1, 2],
@@ -269,6 +295,7 @@ def main(argv=None):
         ctx.call("glc_set_gemm_variant", a.variant)
         ctx.call("glc_set_attention_split", a.attn_split)
         ctx.call("glc_set_rmsnorm_variant", a.rmsnorm_variant)
+        ctx.call("glc_set_ce_variant", a.ce_variant)
         ctx.call("glc_set_quant_path", a.quant_path)
         ctx.call("glc_set_gemm_schedule", a.gemm_schedule)
         ctx.call("glc_set_pdl", a.pdl)

@@ -185,6 +185,15 @@ GLC_API int glc_set_attention_split(glc_ctx* ctx, int nsplit);
  * 0 automatic: 3 for the exact gradient, 1 for the reference's simplified one.
  * Variants 2 and 3 take rows of up to 2048 columns; wider rows use 1. */
 GLC_API int glc_set_rmsnorm_variant(glc_ctx* ctx, int variant);
+/* Softmax cross-entropy kernel for vocabularies above 8192 (tuning; no
+ * reference counterpart): 1 one-shot clusters of four CTAs, each row split in
+ * quarters held in registers; 2 (V <= 32768) one persistent CTA per SM that
+ * streams its rows through a ring of bulk-copied chunks and holds the current
+ * row in registers; 0 automatic: 2 for glc_softmax_ce_llama (and the
+ * Llama-mode step) up to V = 32768, else 1.  Both sum each row in a fixed
+ * order of their own, and 2 computes the Llama exponential as ex2.approx of
+ * one FMA: results agree to fp32 rounding, not bit for bit. */
+GLC_API int glc_set_ce_variant(glc_ctx* ctx, int variant);
 /* glc_linear_bwd_dx_q's path (tuning; no reference counterpart): 0 automatic
  * and 1 dequantize W into the workspace, then the CTA-pair GEMM; 2 decode the
  * stored blocks inside the GEMM's operand load (no fp32 copy of W; F16 and
@@ -292,6 +301,13 @@ GLC_API int glc_attention_bwd_noalloc(glc_ctx* ctx, const float* q, const float*
  * logits with the gradient (p - onehot) * scale. row_logp: [rows] scratch. */
 GLC_API int glc_softmax_ce(glc_ctx* ctx, float* logits, const int64_t* targets, int rows, int V, float scale,
                            float* row_logp, float* loss, int write_grad, int round_out);
+/* The same loss and gradient in the Llama semantics of the training step
+ * (glc_trainer_step on a Llama-mode model, which calls this kernel): expf and
+ * logf in place of exp32/log32, p = e * (1 / sum) in place of the division;
+ * round_out=1 also rounds the gradient to TF32 for the GEMM that reads it.
+ * No reference counterpart (the reference trains with exp32). */
+GLC_API int glc_softmax_ce_llama(glc_ctx* ctx, float* logits, const int64_t* targets, int rows, int V, float scale,
+                                 float* row_logp, float* loss, int write_grad, int round_out);
 /* Embedding lookup of TrainableModel.Forward (trainer.go:275-291):
  * out[t] = E[tok[t]] (+ P[t % S] when P != NULL); ids outside [0,V) read row 0. */
 GLC_API int glc_embed_fwd(glc_ctx* ctx, const int64_t* tokens, const float* E, const float* P, float* out, int T,

@@ -97,13 +97,19 @@ def test_swiglu(ctx):
         a.check(name)
 
 
-@pytest.mark.parametrize("rows,V", [(37, 40000), (33, 1000), (5, 8196)])
-def test_softmax_ce_in_place(ctx, rows, V):
+@pytest.mark.parametrize("rows,V", [(37, 40000), (33, 1000), (5, 8196), (37, 32000), (7, 16388)])
+@pytest.mark.parametrize("fn,variant", [("glc_softmax_ce", 0), ("glc_softmax_ce", 2), ("glc_softmax_ce_llama", 0),
+                                        ("glc_softmax_ce_llama", 1)])
+def test_softmax_ce_in_place(ctx, rows, V, fn, variant):
     logits = Guarded(ctx, rows * V, init=rnd((rows, V), 19, 2.0))
     tg = ctx.from_numpy(np.random.default_rng(20).integers(-1, V + 1, rows).astype(np.int64))
     logp, loss = Guarded(ctx, rows), Guarded(ctx, 1)
-    ctx.call("glc_softmax_ce", logits.ptr, tg.ptr, rows, V, C.c_float(1.0 / rows), logp.ptr, loss.ptr, 1, 1)
-    ctx.sync()
+    try:
+        ctx.call("glc_set_ce_variant", variant)
+        ctx.call(fn, logits.ptr, tg.ptr, rows, V, C.c_float(1.0 / rows), logp.ptr, loss.ptr, 1, 1)
+        ctx.sync()
+    finally:
+        ctx.call("glc_set_ce_variant", 0)
     for a, name in ((logits, "ce dlogits"), (logp, "ce row_logp"), (loss, "ce loss")):
         a.check(name)
 

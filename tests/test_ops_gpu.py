@@ -162,9 +162,17 @@ def test_swiglu_bwd_bit_exact(ctx, orc, n):
     assert np.array_equal(bdg.numpy(), dgate)
 
 
-@pytest.mark.parametrize("rows,V", [(7, 256), (512, 32000), (64, 1000), (33, 8196), (16, 40000)])
+@pytest.mark.parametrize("rows,V", [(7, 256), (512, 32000), (64, 1000), (33, 8196), (300, 16384), (7, 16388),
+                                    (16, 40000)])
 @pytest.mark.parametrize("write_grad", [0, 1])
-def test_softmax_ce(ctx, orc, rows, V, write_grad):
+@pytest.mark.parametrize("variant", [0, 2])
+def test_softmax_ce(ctx, orc, rows, V, write_grad, variant):
+    """glc_set_ce_variant: 0 (automatic: one-shot clusters for the reference's
+    arithmetic) and 2 (rows streamed through persistent CTAs, 8192 < V <=
+    32768), both against the oracle; at or below V = 8192, and above 32768,
+    the variants share a kernel."""
+    if variant and not 8192 < V <= 32768:
+        pytest.skip("one kernel for both variants at this vocabulary")
     r = rng(rows + V)
     logits = (r.standard_normal((rows, V)) * 2).astype(np.float32)
     tg = r.integers(0, V, rows).astype(np.int64)
@@ -175,8 +183,12 @@ def test_softmax_ce(ctx, orc, rows, V, write_grad):
     bl, bt = ctx.from_numpy(logits), ctx.from_numpy(tg)
     blogp, bloss = ctx.empty((rows,)), ctx.empty((1,))
     scale = np.float32(1.0) / np.float32(rows)
-    ctx.call("glc_softmax_ce", bl.ptr, bt.ptr, rows, V, C.c_float(scale), blogp.ptr, bloss.ptr, write_grad, 0)
-    ctx.sync()
+    try:
+        ctx.call("glc_set_ce_variant", variant)
+        ctx.call("glc_softmax_ce", bl.ptr, bt.ptr, rows, V, C.c_float(scale), blogp.ptr, bloss.ptr, write_grad, 0)
+        ctx.sync()
+    finally:
+        ctx.call("glc_set_ce_variant", 0)
     loss = float(bloss.numpy()[0])
     assert abs(loss - ref_loss) <= 1e-5 * abs(ref_loss)
     if write_grad:
@@ -184,6 +196,45 @@ def test_softmax_ce(ctx, orc, rows, V, write_grad):
         assert rel_fro(bl.numpy(), ref_g) < 1e-5
         # rows of the CE gradient sum to zero when the target is valid
         assert np.abs(bl.numpy()[2:].sum(1)).max() < 1e-5
+
+
+@pytest.mark.parametrize("rows,V", [(7, 256), (512, 32000), (33, 8196), (7, 16388), (16, 40000)])
+@pytest.mark.parametrize("variant", [0, 1])
+@pytest.mark.parametrize("round_out", [0, 1])
+def test_softmax_ce_llama(ctx, rows, V, variant, round_out):
+    """glc_softmax_ce_llama (expf/logf, reciprocal multiply: the Llama-mode
+    step's loss) against float64 softmax cross-entropy, with an ignored and
+    an out-of-range target; round_out=1 rounds the gradient to TF32."""
+    if variant and not 8192 < V <= 32768:
+        pytest.skip("one kernel for both variants at this vocabulary")
+    r = rng(3 * rows + V)
+    logits = (r.standard_normal((rows, V)) * 2).astype(np.float32)
+    tg = r.integers(0, V, rows).astype(np.int64)
+    tg[0] = -1
+    tg[1] = V + 5
+    x = logits.astype(np.float64)
+    e = np.exp(x - x.max(1, keepdims=True))
+    p = e / e.sum(1, keepdims=True)
+    ok = (tg >= 0) & (tg < V)
+    idx = np.arange(rows)[ok]
+    scale = np.float32(1.0) / np.float32(rows)
+    ref_loss = -np.log(p[idx, tg[ok]] + 1e-10).sum() / rows
+    ref_g = p * float(scale)
+    ref_g[idx, tg[ok]] -= float(scale)
+    bl, bt = ctx.from_numpy(logits), ctx.from_numpy(tg)
+    blogp, bloss = ctx.empty((rows,)), ctx.empty((1,))
+    try:
+        ctx.call("glc_set_ce_variant", variant)
+        ctx.call("glc_softmax_ce_llama", bl.ptr, bt.ptr, rows, V, C.c_float(scale), blogp.ptr, bloss.ptr, 1, round_out)
+        ctx.sync()
+    finally:
+        ctx.call("glc_set_ce_variant", 0)
+    loss = float(bloss.numpy()[0])
+    assert abs(loss - ref_loss) <= 2e-5 * abs(ref_loss), (loss, ref_loss)
+    g = bl.numpy()
+    assert rel_fro(g, ref_g) < (1e-3 if round_out else 1e-5)
+    if round_out:
+        assert not np.any(g.view(np.uint32) & 0x1FFF)
 
 
 def test_rope_matches_oracle_and_inverts(ctx, orc):
