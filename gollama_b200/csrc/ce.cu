@@ -440,26 +440,32 @@ __global__ void __launch_bounds__(CE_ST_THREADS, 1)
 }
 
 // loss = (0 - logp_0 - logp_1 - ...) / rows over valid targets (grad.go:239-246).
-// One block: the threads stage chunks of row_logp in shared memory, thread 0
-// subtracts them in row order (the reference's running float32 total).  The
-// chunk is padded with +0 (x - 0 == x exactly, -0 included), so thread 0
-// reads eight float4 ahead and only the chain of subtractions is serial.
-__global__ void ce_loss_sum_kernel(const float* __restrict__ row_logp, const int64_t* __restrict__ targets, int rows,
-                                   int V, float* __restrict__ loss) {
+// One block: the threads stage chunks of row_logp in shared memory (every
+// thread's loads issued together), thread 0 subtracts them in row order (the
+// reference's running float32 total).  The chunk is padded with +0 (x - 0 ==
+// x exactly, -0 included), so thread 0 reads eight float4 ahead and only the
+// chain of subtractions is serial.
+constexpr int CE_LS_THREADS = 1024;
+__global__ void __launch_bounds__(CE_LS_THREADS) ce_loss_sum_kernel(const float* __restrict__ row_logp,
+                                                                  const int64_t* __restrict__ targets, int rows,
+                                                                  int V, float* __restrict__ loss) {
   GLC_PDL_ENTRY();
-  constexpr int CHUNK = 4096;
+  constexpr int CHUNK = 4096, PER = CHUNK / CE_LS_THREADS;
   __shared__ __align__(16) float buf[CHUNK];
   float total = 0.f;
   for (int base = 0; base < rows; base += CHUNK) {
     const int n = min(CHUNK, rows - base);
-    for (int i = threadIdx.x; i < CHUNK; i += blockDim.x) {
-      float x = 0.f;  // invalid rows and the padding add nothing
-      if (i < n) {
-        const int64_t t = targets[base + i];
-        if (t >= 0 && t < V) x = row_logp[base + i];
-      }
-      buf[i] = x;
+    int64_t tt[PER];
+    float lp[PER];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int i = static_cast<int>(threadIdx.x) + u * CE_LS_THREADS;
+      tt[u] = i < n ? targets[base + i] : -1;
+      lp[u] = i < n ? row_logp[base + i] : 0.f;
     }
+#pragma unroll
+    for (int u = 0; u < PER; ++u)  // invalid rows and the padding add nothing
+      buf[threadIdx.x + u * CE_LS_THREADS] = (tt[u] >= 0 && tt[u] < V) ? lp[u] : 0.f;
     __syncthreads();
     if (threadIdx.x == 0) {
       const float4* b4 = reinterpret_cast<const float4*>(buf);
@@ -525,7 +531,7 @@ int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, in
     glc::launch_pdl(ctx, kern, grid, CE_ST_THREADS, smem, s, logits, targets, rows, V, cf4, nslots, scale, row_logp, wg,
                     ro, ctx->d_err);
     GLC_LAUNCH_CHECK(ctx, "softmax_ce (streamed rows)");
-    glc::launch_pdl(ctx, ce_loss_sum_kernel, 1, 256, 0, s, row_logp, targets, rows, V, loss);
+    glc::launch_pdl(ctx, ce_loss_sum_kernel, 1, CE_LS_THREADS, 0, s, row_logp, targets, rows, V, loss);
     GLC_LAUNCH_CHECK(ctx, "softmax_ce loss");
     return 0;
   }
@@ -548,7 +554,7 @@ int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, in
     else
       return ctx->fail(GLC_ERR_UNSUPPORTED, "softmax_ce: vocab above 65536 is not supported");
     GLC_LAUNCH_CHECK(ctx, "softmax_ce (cluster)");
-    glc::launch_pdl(ctx, ce_loss_sum_kernel, 1, 256, 0, s, row_logp, targets, rows, V, loss);
+    glc::launch_pdl(ctx, ce_loss_sum_kernel, 1, CE_LS_THREADS, 0, s, row_logp, targets, rows, V, loss);
     GLC_LAUNCH_CHECK(ctx, "softmax_ce loss");
     return 0;
   }
@@ -572,7 +578,7 @@ int softmax_ce(Context* ctx, float* logits, const int64_t* targets, int rows, in
   else
     return ctx->fail(GLC_ERR_UNSUPPORTED, "softmax_ce: vocab above 65536 is not supported");
   GLC_LAUNCH_CHECK(ctx, "softmax_ce");
-  glc::launch_pdl(ctx, ce_loss_sum_kernel, 1, 256, 0, s, row_logp, targets, rows, V, loss);
+  glc::launch_pdl(ctx, ce_loss_sum_kernel, 1, CE_LS_THREADS, 0, s, row_logp, targets, rows, V, loss);
   GLC_LAUNCH_CHECK(ctx, "softmax_ce loss");
   return 0;
 }
