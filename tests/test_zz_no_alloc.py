@@ -4,10 +4,12 @@ allocator, or a call must never synchronise the device, as growing the
 library's workspace does).  Its scratch is a fixed device array inside the
 library.  Checked through the C ABI against glc_attention_bwd on two calls in a
 row; this file is collected last so a failure here stops nothing else."""
+import os
+
 import numpy as np
 import pytest
 
-from gollama_b200.device import GlcError
+from gollama_b200.device import Context, GlcError
 from oracle.oracle import Oracle
 from tests.helpers import FP32_RTOL, rel_fro, threads
 from tests.test_ops_gpu import ATTN_TOL, tf32
@@ -48,6 +50,51 @@ def test_noalloc_matches_allocating_entry_point_twice(ctx, round_dv):
         ref, got = _run(ctx, B, S, H, Hkv, hd, seed, round_dv)
         for a, b in zip(got, ref):
             assert rel_fro(a, b) < tol
+
+
+def _buffers(c, B, S, H, Hkv, hd, seed):
+    """Inputs (with the forward's o and lse) and outputs of one attention
+    backward on context c; returns the argument list of the entry points."""
+    T = B * S
+    r = np.random.default_rng(seed)
+    q, dO = (r.standard_normal((T, H * hd), dtype=np.float32) for _ in range(2))
+    k, v = (r.standard_normal((T, Hkv * hd), dtype=np.float32) for _ in range(2))
+    bq, bk, bv, bdo = c.from_numpy(q), c.from_numpy(k), c.from_numpy(v), c.from_numpy(dO)
+    bo, blse = c.empty((T, H * hd)), c.empty((B, H, S))
+    c.call("glc_attention_fwd", bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, B, S, H, Hkv, hd, 0)
+    dq, dk, dv = c.empty(q.shape), c.empty(k.shape), c.empty(v.shape)
+    keep = (bq, bk, bv, bdo, bo, blse, dq, dk, dv)
+    return keep, [bq.ptr, bk.ptr, bv.ptr, bo.ptr, blse.ptr, bdo.ptr, dq.ptr, dk.ptr, dv.ptr, B, S, H, Hkv, hd, 0]
+
+
+def test_noalloc_call_allocates_nothing(ctx):
+    """The entry point's promise: on a fresh context (no workspace yet), after
+    one call, a call with eight times the rows (B*H*S) leaves the device's
+    free memory as it was, where glc_attention_bwd would allocate the
+    context's workspace.  The kernels of both shapes are loaded first, so no
+    lazy module load counts here."""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device visible to torch")
+    dev = int(os.environ.get("GLC_TEST_DEVICE", "0"))
+    small, large = (1, 256, 8, 2, 64), (2, 1024, 8, 2, 64)
+    keep0, args = _buffers(ctx, *large, 7)
+    ctx.call("glc_attention_bwd_noalloc", *args)
+    ctx.call("glc_attention_bwd", *args)
+    ctx.sync()
+    c = Context(dev)
+    try:
+        keep_s, args_s = _buffers(c, *small, 8)
+        keep_l, args_l = _buffers(c, *large, 9)
+        c.call("glc_attention_bwd_noalloc", *args_s)
+        c.sync()
+        free0 = torch.cuda.mem_get_info(dev)[0]
+        c.call("glc_attention_bwd_noalloc", *args_l)
+        c.sync()
+        free1 = torch.cuda.mem_get_info(dev)[0]
+        assert free1 == free0, (free0, free1)
+    finally:
+        c.close()
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch(ctx):
