@@ -1,14 +1,15 @@
 // Fused softmax cross-entropy forward + backward (SoftmaxCrossEntropyGrad,
 // pkg/tensor/grad.go:210-280).
 //
-// One CTA of up to 512 threads per row; the row lives in registers (V <= 65536).  Per row:
+// Up to V = 8192, one CTA of up to 512 threads per row (ce_kernel); in every
+// kernel the row lives in registers (V <= 65536).  Per row:
 //   max (grad.go:220-225), e_v = exp32(l_v - max) and their float32 sum
 //   (:228-232), p_v = e_v / sum (:235-237), the target's log32(p_t + 1e-10)
 //   (:240-243; targets outside [0, V) contribute nothing), and, when the
 //   gradient is wanted, dlogits_v = p_v*scale - [v == t]*scale (:266-276),
 //   written in place over the logits (the row is fully in registers first).
-// The loss (:246) is summed by a second, single-thread kernel in row order,
-// exactly as the reference's running float32 total.
+// The loss (:246) is summed by a second kernel whose thread 0 subtracts the
+// rows' terms in row order, exactly as the reference's running float32 total.
 //
 // Large vocabularies in the Llama arithmetic (8192 < V <= 32768) stream their
 // rows through persistent CTAs (ce_stream_kernel, below): bulk copies fill a
