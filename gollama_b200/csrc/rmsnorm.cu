@@ -339,7 +339,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_full_tma_kernel(
   }
   const float inv_cols = 1.0f / static_cast<float>(cols);
   bool ok = true;
-  for (int row = row0; row < row1; ++row) {
+  int row = row0;  // on abort: the row whose copies the wait gave up on
+  for (; row < row1; ++row) {
     const int k = row - row0, st = k % TMA_STAGES;
     if (!__syncthreads_and(mbar_wait(&full[st], (k / TMA_STAGES) & 1, &abort_flag, err, GLC_DEV_TIMEOUT_EPILOGUE))) {
       ok = false;
@@ -398,9 +399,13 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_full_tma_kernel(
     __syncthreads();  // red is rewritten by the next row
   }
   if (!ok && tid == 0) {
-    // no copy may land after the block exits: wait (bounded) for those in flight
-    for (int row = row0; row < row0 + issued; ++row) {
-      const int k = row - row0;
+    // No copy may land after the block exits: wait (bounded) for those in
+    // flight, the rows from the one whose wait gave up to the last issued,
+    // each in its own stage.  The rows before it were read, and their stages
+    // may since have completed a later phase: a parity wait on them would
+    // name the wrong phase and spin to its limit.
+    for (int r = row; r < row0 + issued; ++r) {
+      const int k = r - row0;
       mbar_drain(&full[k % TMA_STAGES], (k / TMA_STAGES) & 1, err);
     }
   }
