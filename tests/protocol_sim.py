@@ -1,6 +1,7 @@
 """Randomized simulation of the barrier protocols of the persistent attention
-kernels (attn_fwd_persist_kernel, attn_bwd_dq_persist_kernel in
-gollama_b200/csrc/attention_tc.cu).
+kernels (attn_fwd_persist_kernel, attn_bwd_dq_persist_kernel and the dK/dV
+kernel in gollama_b200/csrc/attention_tc.cu) and of the CTA-pair GEMM
+(gemm_tf32_pair_kernel in gollama_b200/csrc/gemm_tf32.cu).
 
 Each role (TMA producer, score-MMA issuer, accumulate-MMA issuer, math warps)
 is a generator transcribing the kernel's loops, the barrier each wait uses and
@@ -411,3 +412,167 @@ def dkdv(n_heads, nq, seed, groups=1):
 
     maths = {f"math{g}": math(g) for g in range(groups)}
     _drive({"tma": tma(), "smma": smma(), "acc": acc(), **maths}, ev, rnd)
+
+
+def pair_gemm(k_blocks, seed, dyn=False, total_tiles=None, stages=6, ring=8, epi_warps=4, skip=0.0, counts=None):
+    """gemm_tf32_pair_kernel (gollama_b200/csrc/gemm_tf32.cu) for one CTA pair.
+
+    k_blocks[i]: the k-blocks of the pair's i-th tile (static order: the tiles
+    the pair owns).  dyn: the dynamic order instead, where the leader's
+    producer takes indices from a counter shared with other pairs (each index
+    taken by another pair with probability `skip`) until total_tiles, and
+    publishes them through a ring of `ring` slots in both CTAs; the peer's
+    producer, the MMA issuer and the epilogue warps of both CTAs read them in
+    order and release each slot on the leader's ring_empty.
+
+    Barriers: full[s] (leader; the leader's producer arrives with expect_tx of
+    both CTAs' copies, and the peer's copy may land before that arrival),
+    empty[s] in each CTA (the MMA issuer's commit), tfull[b] in each CTA (the
+    issuer's commit after a tile), tempty[b] (leader; one arrival per epilogue
+    warp of either CTA).  Checked: every stage the MMAs read holds both CTAs'
+    copies of the right (tile, k-block); no stage is refilled before the MMAs
+    that read it completed; no accumulator is overwritten before every
+    epilogue warp of both CTAs read it; no ring slot is rewritten before its
+    ten readers took it; every tile reaches the epilogue of both CTAs once.
+    counts: arrival counts to override (a planted mistake for the tests)."""
+    rnd = random.Random(seed)
+    bars = {}
+
+    def b(name, i=0, cta=0):
+        key = (name, i, cta)
+        if key not in bars:
+            count = {"tempty": 2 * epi_warps, "ring_empty": 2 + 2 * epi_warps, **(counts or {})}.get(name, 1)
+            bars[key] = Bar(f"{name}{i}.{cta}", count)
+        return bars[key]
+
+    ev = []
+    commits = {"issued": 0, "fired": 0}
+    st = {
+        "stage": [[None, None] for _ in range(stages)],  # (tile, kb) landed per CTA
+        "stage_read": {},                                # stage fill index -> MMAs done
+        "acc": [None, None],                             # tile index complete in accumulator b
+        "drained": {},                                   # local tile -> epilogue warps done
+        "ring": [[None] * ring, [None] * ring],           # published (index, tile) per CTA
+        "ring_reads": {},                                # index -> readers done
+        "seen": [[], []],                                # tiles per CTA's epilogue (warp 0)
+        "counter": 0,
+        "published": [],
+    }
+
+    def take():
+        while st["counter"] < total_tiles and rnd.random() < skip:
+            st["counter"] += 1          # another pair took this index
+        t = st["counter"] if st["counter"] < total_tiles else -1
+        st["counter"] += 1
+        return t
+
+    def consume(cta, i):
+        slot = i % ring
+        yield from _wait(b("ring_full", slot, cta), (i // ring) & 1, i // ring)
+        idx, tile = st["ring"][cta][slot]
+        assert idx == i, ("ring slot holds another index", cta, slot, idx, i)
+        st["ring_reads"][i] = st["ring_reads"].get(i, 0) + 1
+        b("ring_empty", slot).arrive()
+        return tile
+
+    def nkb(tile):
+        return k_blocks[tile % len(k_blocks)]
+
+    def get_tile(cta, i, reader=True):
+        """the i-th tile of a role (-1: no more); in the dynamic order the
+        leader's producer publishes it, every other role reads the ring"""
+        if not dyn:
+            return i if i < len(k_blocks) else -1
+        if reader:
+            return (yield from consume(cta, i))
+        slot = i % ring
+        yield from _wait(b("ring_empty", slot), ((i // ring) & 1) ^ 1, i // ring - 1)
+        assert i < ring or st["ring_reads"].get(i - ring) == 2 + 2 * epi_warps, ("ring slot rewritten early", i)
+        tile = take()
+        for c in (0, 1):
+            st["ring"][c][slot] = (i, tile)
+        st["published"].append(tile)
+        b("ring_full", slot, 0).arrive()
+        b("ring_full", slot, 1).arrive()
+        return tile
+
+    def producer(cta):
+        stage = f = i = 0
+        phase = 0
+        while True:
+            tile = yield from get_tile(cta, i, reader=not (cta == 0))
+            if tile < 0:
+                return
+            for kb in range(nkb(tile)):
+                u = f // stages
+                yield from _wait(b("empty", stage, cta), phase ^ 1, u - 1)
+                assert u == 0 or st["stage_read"].get((cta, f - stages)), ("stage refilled before read", cta, f)
+                if cta == 0:
+                    b("full", stage).expect_tx(2)   # the pair's two copies
+
+                def land(stage=stage, cta=cta, tile=tile, kb=kb):
+                    st["stage"][stage][cta] = (tile, kb)
+                    b("full", stage).complete_tx(1)
+                ev.append(land)
+                f += 1
+                stage += 1
+                if stage == stages:
+                    stage, phase = 0, phase ^ 1
+                yield
+            i += 1
+
+    def mma():
+        stage = f = local = 0
+        phase = 0
+        while True:
+            tile = yield from get_tile(0, local)
+            if tile < 0:
+                return
+            buf, use = local & 1, local >> 1
+            yield from _wait(b("tempty", buf), (use & 1) ^ 1, use - 1)
+            assert local < 2 or st["drained"].get(local - 2) == 2 * epi_warps, ("accumulator overwritten", local)
+            st["acc"][buf] = ("partial", local)
+            for kb in range(nkb(tile)):
+                yield from _wait(b("full", stage), phase, f // stages)
+                assert st["stage"][stage] == [(tile, kb), (tile, kb)], ("stage contents", stage, st["stage"][stage])
+                for c in (0, 1):
+                    def freed(stage=stage, f=f, c=c):
+                        st["stage_read"][(c, f)] = True
+                        b("empty", stage, c).arrive()
+                    ev.append(_in_order(commits, freed, ev))
+                f += 1
+                stage += 1
+                if stage == stages:
+                    stage, phase = 0, phase ^ 1
+                yield
+            for c in (0, 1):
+                def done(buf=buf, local=local, c=c):
+                    st["acc"][buf] = ("done", local)
+                    b("tfull", buf, c).arrive()
+                ev.append(_in_order(commits, done, ev))
+            local += 1
+
+    def epilogue(cta, w):
+        local = 0
+        while True:
+            tile = yield from get_tile(cta, local)
+            if tile < 0:
+                return
+            buf, use = local & 1, local >> 1
+            yield from _wait(b("tfull", buf, cta), use & 1, use)
+            assert st["acc"][buf] == ("done", local), ("accumulator not final", cta, w, local, st["acc"][buf])
+            st["drained"][local] = st["drained"].get(local, 0) + 1
+            b("tempty", buf).arrive()
+            if w == 0:
+                st["seen"][cta].append(tile)
+            local += 1
+            yield
+
+    roles = {"prod0": producer(0), "prod1": producer(1), "mma": mma()}
+    roles.update({f"epi{c}.{w}": epilogue(c, w) for c in (0, 1) for w in range(epi_warps)})
+    _drive(roles, ev, rnd)
+    want = [t for t in st["published"] if t >= 0] if dyn else list(range(len(k_blocks)))
+    assert st["seen"][0] == want and st["seen"][1] == want, (st["seen"], want)
+    if dyn:
+        assert all(st["ring_reads"].get(i) == 2 + 2 * epi_warps for i in range(len(st["published"])))
+    return want
