@@ -1,4 +1,4 @@
-"""Data-parallel host logic on CPU (world_size 2 and 4, gloo).
+"""Data-parallel host logic on CPU (world_size 2, 4 and 8, gloo).
 
 The GPU path sums each gradient bucket with NCCL as soon as the backward has
 written it (glc_dp_bucket_plan gives the buckets).  What that path relies on
@@ -69,7 +69,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank, port, shape_name, out_path, world=WORLD):
+def _rank_main(rank, port, shape_name, out_path, world=WORLD, batch=None):
     import torch
     import torch.distributed as dist
 
@@ -80,6 +80,8 @@ def _rank_main(rank, port, shape_name, out_path, world=WORLD):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
     try:
         shape = syn.SHAPES[shape_name]
+        if batch:
+            shape = shape.with_(batch=batch)
         orc = Oracle(threads=2)
         cfg = oracle_config(shape)
         params = syn.init_params(shape, seed=11)
@@ -99,15 +101,18 @@ def _rank_main(rank, port, shape_name, out_path, world=WORLD):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("shape_name", ["tiny", "tiny-llama"])
 def test_rank_bucket_sum_equals_global_batch(shape_name, world):
+    """world 8 (the largest single-box run) takes the tiny shapes at batch 8,
+    one sequence per rank."""
     import torch.multiprocessing as mp
 
-    assert syn.SHAPES[shape_name].batch >= world
+    batch = max(world, syn.SHAPES[shape_name].batch)
     with tempfile.TemporaryDirectory() as d:
         out = os.path.join(d, "grads.npz")
-        mp.start_processes(_rank_main, args=(_free_port(), shape_name, out, world), nprocs=world, start_method="spawn")
+        mp.start_processes(_rank_main, args=(_free_port(), shape_name, out, world, batch), nprocs=world,
+                           start_method="spawn")
         r = np.load(out)
         # the ranks' shares add in a different fp32 order than the full batch
         assert rel_fro(r["summed"], r["full"]) < 1e-5
