@@ -4,6 +4,7 @@ allocator, or a call must never synchronise the device, as growing the
 library's workspace does).  Its scratch is a fixed device array inside the
 library.  Checked through the C ABI against glc_attention_bwd on two calls in a
 row; this file is collected last so a failure here stops nothing else."""
+import gc
 import os
 
 import numpy as np
@@ -88,10 +89,16 @@ def test_noalloc_call_allocates_nothing(ctx):
         keep_l, args_l = _buffers(c, *large, 9)
         c.call("glc_attention_bwd_noalloc", *args_s)
         c.sync()
-        free0 = torch.cuda.mem_get_info(dev)[0]
-        c.call("glc_attention_bwd_noalloc", *args_l)
-        c.sync()
-        free1 = torch.cuda.mem_get_info(dev)[0]
+        # no buffer of an earlier test may be freed by the collector in between
+        gc.collect()
+        gc.disable()
+        try:
+            free0 = torch.cuda.mem_get_info(dev)[0]
+            c.call("glc_attention_bwd_noalloc", *args_l)
+            c.sync()
+            free1 = torch.cuda.mem_get_info(dev)[0]
+        finally:
+            gc.enable()
         assert free1 == free0, (free0, free1)
     finally:
         c.close()
