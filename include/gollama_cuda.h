@@ -53,15 +53,20 @@ GLC_API int glc_init(int device, glc_ctx** out);
 /* Replaces metal.Cleanup (pkg/metal/metal.go:193-196).  Trainers and models
  * created on the context must be destroyed before it (they use its stream). */
 GLC_API int glc_destroy(glc_ctx* ctx);
-/* Copies the last error message (NUL-terminated, truncated to n).  With
- * ctx == NULL: the message of the calling thread's last failed call that takes
- * no context (the checkpoint file functions). */
+/* Copies the last error message (NUL-terminated, truncated to n): the text a
+ * Go wrapper puts in its error, as the Metal wrappers format a failing status
+ * (pkg/metal/metal.go:185-187).  With ctx == NULL: the message of the calling
+ * thread's last failed call that takes no context (the checkpoint file
+ * functions). */
 GLC_API int glc_last_error(glc_ctx* ctx, char* buf, size_t n);
 /* Replaces metal.DeviceName (pkg/metal/metal.go:204-206). */
 GLC_API int glc_device_name(glc_ctx* ctx, char* buf, size_t n);
-/* Waits for all enqueued work and reports device-side errors. */
+/* Waits for all enqueued work and reports device-side errors.  No reference
+ * counterpart: the Metal calls return when their work is done
+ * (pkg/metal/metal.go:210-226); this library's calls are enqueued. */
 GLC_API int glc_sync(glc_ctx* ctx);
-/* Number of kernels this library has launched on the context. */
+/* Number of kernels this library has launched on the context (diagnostics;
+ * no reference counterpart). */
 GLC_API int glc_launch_count(glc_ctx* ctx, uint64_t* out);
 
 /* ------------------------------------------------------------------ memory
@@ -72,14 +77,15 @@ GLC_API int glc_memcpy_h2d(glc_ctx* ctx, void* dst, const void* src, size_t byte
 GLC_API int glc_memcpy_d2h(glc_ctx* ctx, void* dst, const void* src, size_t bytes);
 GLC_API int glc_memcpy_d2d(glc_ctx* ctx, void* dst, const void* src, size_t bytes);
 GLC_API int glc_memset(glc_ctx* ctx, void* dptr, int value, size_t bytes);
-/* Page-locked host memory for the asynchronous copies below. */
+/* Page-locked host memory for the asynchronous copies below (no reference
+ * counterpart: the Go trainer's host slices are ordinary memory). */
 GLC_API int glc_host_alloc(glc_ctx* ctx, size_t bytes, void** hptr);
 GLC_API int glc_host_free(glc_ctx* ctx, void* hptr);
 GLC_API int glc_memcpy_h2d_async(glc_ctx* ctx, void* dst, const void* src, size_t bytes);
 GLC_API int glc_memcpy_d2h_async(glc_ctx* ctx, void* dst, const void* src, size_t bytes);
 
 /* ------------------------------------------------------------------ timing
- * CUDA events on the context's compute stream. */
+ * CUDA events on the context's compute stream (no reference counterpart). */
 GLC_API int glc_timer_start(glc_ctx* ctx);
 GLC_API int glc_timer_stop(glc_ctx* ctx, float* ms); /* synchronises on the stop event */
 
@@ -87,7 +93,8 @@ GLC_API int glc_timer_stop(glc_ctx* ctx, float* ms); /* synchronises on the stop
  * While enabled, every kernel launch of this library is bracketed by a CUDA
  * event pair on its stream.  glc_profile_end synchronises and returns, per
  * kernel class (GLC_PROF_*), the launch count, the summed device time and the
- * summed algorithmic work (FLOPs for GEMM and attention, bytes otherwise). */
+ * summed algorithmic work (FLOPs for GEMM and attention, bytes otherwise).
+ * No reference counterpart. */
 #define GLC_PROF_GEMM 0
 #define GLC_PROF_ATTN_FWD 1
 #define GLC_PROF_ATTN_BWD 2
@@ -160,7 +167,8 @@ GLC_API int glc_dequantize(glc_ctx* ctx, int type, const void* src, float* dst, 
  * TF32-rounded fp32 copy of W, or none on the fused path (glc_set_quant_path). */
 GLC_API int glc_linear_bwd_dx_q(glc_ctx* ctx, const float* dY, const void* Wq, int type, float* dX, int M, int K,
                                 int N, int accumulate);
-/* General strided form of the three above: C[M,N] (+)= A . B^T (+ R) where
+/* General strided form of the three above (the products of MatMulGrad,
+ * pkg/tensor/grad.go:81-152, on any operand storage): C[M,N] (+)= A . B^T (+ R) where
  * a_mn/b_mn select MN-major storage (element (i,k) at ptr[k*ld+i]) instead of
  * K-major (ptr[i*ld+k]).  round_out rounds the stored values to TF32. */
 GLC_API int glc_gemm_tf32(glc_ctx* ctx, const float* A, int lda, int a_mn, const float* B, int ldb, int b_mn, float* C,
@@ -217,13 +225,15 @@ GLC_API int glc_set_pdl(glc_ctx* ctx, int on);
  * item's loads and score products overlap the current item's last tiles and
  * output).  Results are bit-identical. */
 GLC_API int glc_set_attention_fwd_variant(glc_ctx* ctx, int variant);
-/* The same choice for the attention backward's dQ kernel: 2 walks its
+/* The same choice for the attention backward's dQ kernel (tuning; no
+ * reference counterpart): 2 walks its
  * (query tile, batch, head) items persistently, moving the next item's Q and
  * dO into TMEM while the current item's dQ is written; 0 automatic and 3 the
  * same with sixteen softmax warps in two groups taking alternate steps; 1 one
  * CTA per item.  Bit-identical. */
 GLC_API int glc_set_attention_dq_variant(glc_ctx* ctx, int variant);
-/* The attention backward's dK/dV kernel: 1 eight softmax warps that take
+/* The attention backward's dK/dV kernel (tuning; no reference counterpart):
+ * 1 eight softmax warps that take
  * every 64-query step in turn; 0 automatic and 2 sixteen softmax warps in two
  * groups taking alternate steps, so one group's arithmetic overlaps the
  * other's.  Bit-identical. */
@@ -275,7 +285,10 @@ GLC_API int glc_rope_table(int hd, int max_seq, float theta, float* cos_host, fl
  * k,v: [B*S, Hkv*hd]; lse: [B, H, S]. */
 GLC_API int glc_attention_fwd(glc_ctx* ctx, const float* q, const float* k, const float* v, float* o, float* lse,
                               int B, int S, int H, int Hkv, int hd, int round_out);
-/* Its backward (dq, dk, dv overwritten).  Uses the context workspace. */
+/* Its backward (dq, dk, dv overwritten).  The reference attaches no GradFn to
+ * its attention (trainer.go:335-337): this is the Llama semantics' gradient of
+ * the same causal attention (pkg/model/attention.go:113-206).  Uses the
+ * context workspace. */
 GLC_API int glc_attention_bwd(glc_ctx* ctx, const float* q, const float* k, const float* v, const float* o,
                               const float* lse, const float* dO, float* dq, float* dk, float* dv, int B, int S, int H,
                               int Hkv, int hd, int round_dv);
@@ -313,9 +326,11 @@ GLC_API int glc_softmax_ce_llama(glc_ctx* ctx, float* logits, const int64_t* tar
 GLC_API int glc_embed_fwd(glc_ctx* ctx, const int64_t* tokens, const float* E, const float* P, float* out, int T,
                           int S, int d, int V);
 /* Embedding gradient dE[tok[t]] += dh[t] (t ascending, deterministic);
- * tokens_host are the same ids on the host. */
+ * tokens_host are the same ids on the host.  The reference's lookup has no
+ * GradFn (trainer.go:290-291): this is the Llama semantics' gradient of it. */
 GLC_API int glc_embed_bwd(glc_ctx* ctx, const int64_t* tokens_host, int T, const float* dh, float* dE, int d, int V);
-/* The same scatter with the ids in device memory: the positions are sorted
+/* The same scatter (the gradient of the lookup at trainer.go:275-291) with the
+ * ids in device memory: the positions are sorted
  * by id on the device (stable, so the sums run in ascending t and the result
  * is bit-identical to glc_embed_bwd).  Uses the context workspace. */
 GLC_API int glc_embed_bwd_device(glc_ctx* ctx, const int64_t* tokens_dev, int T, const float* dh, float* dE, int d,
@@ -387,17 +402,21 @@ GLC_API int glc_default_train_config(glc_train_config* cfg);
  * arena in Params() order; matrices N(0, init_std) from `seed` (the Go
  * math/rand Xavier init is not reproducible without Go), RMSNorm weights 1. */
 GLC_API int glc_model_create(glc_ctx* ctx, const glc_train_config* cfg, glc_model** out);
-/* Before its context, and after every trainer created on it. */
+/* Before its context, and after every trainer created on it (no reference
+ * counterpart: Go's collector frees the model). */
 GLC_API int glc_model_destroy(glc_model* m);
 /* Params() (trainer.go:429-431): count, and per parameter its offset/shape in
  * the flat arena and whether it currently has a gradient (Grad != nil). */
 GLC_API int glc_model_num_params(glc_model* m, int* n, int64_t* total_floats);
 GLC_API int glc_model_param_info(glc_model* m, int idx, int64_t* offset, int64_t* rows, int64_t* cols,
                                  int* has_grad);
-/* Host <-> device copies of the whole arena (parameters, gradients, AdamW m/v). */
+/* Host <-> device copies of the whole arena: the Data slices of Params()
+ * (trainer.go:429-431) in order; below, their Grad slices and AdamW's m and v
+ * (pkg/train/optimizer.go:37-76). */
 GLC_API int glc_model_set_params(glc_model* m, const float* host, int64_t n);
 GLC_API int glc_model_get_params(glc_model* m, float* host, int64_t n);
-/* After a TrainStep the gradients are returned as GradientClipping leaves them
+/* After a TrainStep the gradients are returned as GradientClipping
+ * (pkg/train/optimizer.go:169-196) leaves them
  * (scaled by the clip factor); the step itself keeps them unscaled on the
  * device and applies the factor here, in place, on the first read. */
 GLC_API int glc_model_get_grads(glc_model* m, float* host, int64_t n);
@@ -405,7 +424,7 @@ GLC_API int glc_model_get_moments(glc_model* m, float* m_host, float* v_host, in
 /* NewTrainer (trainer.go:447-459): AdamW with the configured hyper-parameters
  * and the warmup + cosine LRScheduler. */
 GLC_API int glc_trainer_create(glc_model* m, glc_trainer** out);
-/* Before its model and context. */
+/* Before its model and context (no reference counterpart). */
 GLC_API int glc_trainer_destroy(glc_trainer* t);
 /* Trainer.TrainStep (trainer.go:462-505): LR, ZeroGrad, forward, loss,
  * backward, (data-parallel gradient allreduce), gradient clipping, AdamW.
@@ -416,9 +435,12 @@ GLC_API int glc_train_step(glc_trainer* t, const int64_t* inputs, const int64_t*
  * synchronisation of a step is the loss readback at its end (trainer.go:488). */
 GLC_API int glc_train_step_device(glc_trainer* t, const int64_t* inputs_dev, const int64_t* targets_dev, int B, int S,
                                   float* loss);
-/* Global gradient norm before clipping and the learning rate of the last step. */
+/* Global gradient norm before clipping (GradientClipping,
+ * pkg/train/optimizer.go:169-196) and the learning rate (LRScheduler.GetLR,
+ * :157-166) of the last step. */
 GLC_API int glc_trainer_last_stats(glc_trainer* t, double* grad_norm, float* lr, int* step);
-/* Kernels launched by the last step (all of them this library's). */
+/* Kernels launched by the last step (all of them this library's;
+ * diagnostics, no reference counterpart). */
 GLC_API int glc_trainer_last_launches(glc_trainer* t, uint64_t* n);
 
 /* ------------------------------------------------------------------ checkpoints
@@ -452,7 +474,8 @@ GLC_API int glc_state_read(const char* path, const glc_train_config* cfg, int* s
  * With data parallelism every rank holds the same parameters and state: call
  * the save functions on one rank; every rank may load the same state file. */
 GLC_API int glc_trainer_save_checkpoint(glc_trainer* t, const char* dir, char* path_out, size_t path_cap);
-/* Binary resume of a trainer: parameters, m, v and both step counters. */
+/* Binary resume of a trainer: parameters, m, v and both step counters (no
+ * reference counterpart: the reference reloads no optimizer state). */
 GLC_API int glc_trainer_save_state(glc_trainer* t, const char* path);
 GLC_API int glc_trainer_load_state(glc_trainer* t, const char* path);
 
@@ -466,6 +489,7 @@ GLC_API int glc_trainer_load_state(glc_trainer* t, const char* path);
  * the reference's maps).  Host-only calls report errors through
  * glc_last_error(NULL). */
 typedef struct glc_gguf glc_gguf;
+/* Open (reader.go:22-49) and Close (:52-61). */
 GLC_API int glc_gguf_open(const char* path, glc_gguf** out);
 GLC_API int glc_gguf_close(glc_gguf* g);
 /* Header (reader.go:299-301) and the data section's offset. */
@@ -493,7 +517,8 @@ GLC_API int glc_gguf_tensor_info(glc_gguf* g, int64_t i, char* name, size_t name
  * glc_gguf_close; GLC_ERR_IO if the data extends beyond the file. */
 GLC_API int glc_gguf_tensor_data(glc_gguf* g, int64_t i, const void** data, uint64_t* nbytes);
 /* The tensor's stored bytes (quantized blocks as they are) to device memory
- * of at least `cap` bytes: the operand glc_linear_bwd_dx_q takes. */
+ * of at least `cap` bytes: the operand glc_linear_bwd_dx_q takes.  No
+ * reference counterpart: the reference dequantizes every tensor at load. */
 GLC_API int glc_gguf_tensor_upload(glc_ctx* ctx, glc_gguf* g, int64_t i, void* dev, uint64_t cap);
 /* loadTensor (pkg/model/transformer.go:285-303) on the device: the stored
  * bytes to the device, then glc_dequantize into dev (n = element count). */
@@ -502,7 +527,8 @@ GLC_API int glc_gguf_tensor_load(glc_ctx* ctx, glc_gguf* g, int64_t i, float* de
 /* ------------------------------------------------------------------ data parallel (NCCL)
  * One process per GPU.  Rank 0 creates the id and shares it (file, store, ...);
  * every rank then calls glc_dp_init.  Gradients are summed with ncclAllReduce
- * (fp32) over NVLink during glc_train_step. */
+ * (fp32) over NVLink during glc_train_step.  No reference counterpart: the
+ * reference trains on one device. */
 GLC_API int glc_dp_unique_id(unsigned char id[128]);
 GLC_API int glc_dp_init(glc_ctx* ctx, int rank, int world, const unsigned char id[128], int timeout_ms);
 GLC_API int glc_dp_allreduce_sum(glc_ctx* ctx, float* buf, size_t n);

@@ -33,6 +33,29 @@ def test_binding_covers_header():
     assert set(_lib.SIGNATURES) == {n for h in HEADERS for n in declared(h)}
 
 
+def test_every_entry_point_cites_the_reference_or_says_it_has_none():
+    """Each declaration's comment (the block above it, or above the group of
+    declarations and #defines it belongs to) cites the reference function it
+    replaces by Go file, or says it has no reference counterpart."""
+    uncited = []
+    for h in HEADERS:
+        lines = h.read_text().split("\n")
+        for i, line in enumerate(lines):
+            if not line.startswith("GLC_API"):
+                continue
+            j = i - 1
+            while j >= 0 and (lines[j].startswith(("GLC_API", "#define")) or
+                              (lines[j].startswith(" ") and not lines[j].lstrip().startswith("*"))):
+                j -= 1
+            block = []
+            while j >= 0 and (lines[j].lstrip().startswith(("/*", "*", "//")) or lines[j].rstrip().endswith("*/")):
+                block.append(lines[j])
+                j -= 1
+            if not re.search(r"\.go\b|counterpart", " ".join(block)):
+                uncited.append(re.search(r"(glc_\w+)\s*\(", line).group(1))
+    assert not uncited, uncited
+
+
 def test_config_struct_layout_matches_header():
     lib = _lib.load()
     cfg = _lib.TrainConfigC()
