@@ -132,12 +132,20 @@ class ClockSampler:
             self.proc.kill()
             self.proc.wait()
         self.f.close()
+        lines = Path(self.path).read_text().splitlines()
+        os.unlink(self.path)
+        return self.summarize(lines)
+
+    @staticmethod
+    def summarize(lines):
+        """The clocks record of the timed region from nvidia-smi's CSV lines
+        (QUERY's columns, no header, no units): median SM clock, the highest
+        max clock, every throttle reason seen active, the sample count."""
         rows = []
-        for line in Path(self.path).read_text().splitlines():
+        for line in lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) >= 9:
                 rows.append(parts)
-        os.unlink(self.path)
         if not rows:
             return None
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
